@@ -1,0 +1,319 @@
+// extern "C" entry points (declared in include/blitzgs_b200.h).
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "blitzgs_b200.h"
+#include "common.cuh"
+#include "kernels.h"
+
+using namespace blitz;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* what) {
+  char buf[512];
+  if (code > 0 && code < 10000)
+    snprintf(buf, sizeof(buf), "%s: %s", what, cudaGetErrorString((cudaError_t)code));
+  else
+    snprintf(buf, sizeof(buf), "%s (status %d)", what, code);
+  g_last_error = buf;
+  return code;
+}
+
+int check(int code, const char* what) { return code == 0 ? 0 : fail(code, what); }
+
+inline cudaStream_t S(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+PreprocessParams make_pp(int64_t P, int D, int M, const float* means3D, const float* scales,
+                         const float* rotations, const float* dc, int64_t dc_stride,
+                         const float* rest, int64_t rest_stride, const float* opacities,
+                         float scale_modifier, const float* viewmatrix, const float* projmatrix,
+                         const float* campos, float tanfovx, float tanfovy, int H, int W) {
+  PreprocessParams p{};
+  p.P = P;
+  p.D = D;
+  p.M = M;
+  p.means3D = means3D;
+  p.scales = scales;
+  p.rotations = rotations;
+  p.opacities = opacities;
+  p.dc = dc;
+  p.dc_stride = dc_stride;
+  p.rest = rest;
+  p.rest_stride = rest_stride;
+  p.sh_packed16 = (M == 15 && dc_stride == 48 && rest_stride == 48 && rest == dc + 3 && aligned16(dc));
+  p.scale_modifier = scale_modifier;
+  p.viewmatrix = viewmatrix;
+  p.projmatrix = projmatrix;
+  p.campos = campos;
+  p.tanfovx = tanfovx;
+  p.tanfovy = tanfovy;
+  // focal lengths exactly as the reference host code computes them
+  p.focal_y = H / (2.0f * tanfovy);
+  p.focal_x = W / (2.0f * tanfovx);
+  p.W = W;
+  p.H = H;
+  p.grid_x = (W + kTileX - 1) / kTileX;
+  p.grid_y = (H + kTileY - 1) / kTileY;
+  return p;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* blitz_version(void) { return "blitzgs_b200 0.1 (sm_100a)"; }
+
+const char* blitz_last_error(void) { return g_last_error.c_str(); }
+
+int blitz_preprocess_forward(int64_t P, int D, int M, const float* means3D, const float* scales,
+                             const float* rotations, const float* sh_dc, int64_t dc_stride,
+                             const float* sh_rest, int64_t rest_stride, const float* opacities,
+                             float scale_modifier, const float* viewmatrix, const float* projmatrix,
+                             const float* campos, float tanfovx, float tanfovy, int image_height,
+                             int image_width, int prefiltered, float* means2D, float* depths,
+                             int32_t* radii, float* cov3D, float* conic_opacity, float* rgb,
+                             uint8_t* clamped, uint32_t* error_word, void* stream) {
+  if (P < 0 || D < 0 || D > 3 || M < 0 || M > 15 || image_height <= 0 || image_width <= 0)
+    return fail(BLITZ_EINVAL, "blitz_preprocess_forward: bad sizes");
+  if (P == 0) return 0;
+  if (!means3D || !scales || !rotations || !sh_dc || !opacities || !viewmatrix || !projmatrix ||
+      !campos || !means2D || !depths || !radii || !conic_opacity || !rgb || (M > 0 && !sh_rest))
+    return fail(BLITZ_EINVAL, "blitz_preprocess_forward: null pointer");
+  if (!aligned16(rotations) || !aligned16(conic_opacity) || (reinterpret_cast<uintptr_t>(means2D) & 7u))
+    return fail(BLITZ_EINVAL, "blitz_preprocess_forward: rotations/conic_opacity need 16-byte, means2D 8-byte alignment");
+  if (prefiltered && !error_word)
+    return fail(BLITZ_EINVAL, "blitz_preprocess_forward: prefiltered=1 needs an error word");
+  PreprocessParams p = make_pp(P, D, M, means3D, scales, rotations, sh_dc, dc_stride, sh_rest,
+                               rest_stride, opacities, scale_modifier, viewmatrix, projmatrix,
+                               campos, tanfovx, tanfovy, image_height, image_width);
+  p.prefiltered = prefiltered != 0;
+  p.out_means2D = means2D;
+  p.out_depths = depths;
+  p.out_radii = radii;
+  p.out_conic_opacity = conic_opacity;
+  p.out_rgb = rgb;
+  p.out_clamped = reinterpret_cast<bool*>(clamped);
+  p.out_cov3D = cov3D;
+  p.error_flag = error_word;
+  return check(launch_preprocess_fwd(p, S(stream)), "blitz_preprocess_forward");
+}
+
+int blitz_preprocess_backward(int64_t P, int D, int M, const int32_t* radii, const float* means3D,
+                              const float* scales, const float* rotations, const float* sh_dc,
+                              int64_t dc_stride, const float* sh_rest, int64_t rest_stride,
+                              float scale_modifier, const float* viewmatrix, const float* projmatrix,
+                              const float* campos, float tanfovx, float tanfovy, int image_height,
+                              int image_width, const float* g_means2D, int64_t g_means2D_stride,
+                              const float* g_conic_opacity, int64_t g_conic_stride,
+                              const float* g_colors, int64_t g_colors_stride, float* dL_dmeans3D,
+                              float* dL_dscales, float* dL_drotations, float* dL_dopacity,
+                              float* g_dc, int64_t g_dc_stride, float* g_rest, int64_t g_rest_stride,
+                              int accumulate, void* stream) {
+  if (P < 0 || D < 0 || D > 3 || M < 0 || M > 15 || image_height <= 0 || image_width <= 0)
+    return fail(BLITZ_EINVAL, "blitz_preprocess_backward: bad sizes");
+  if (P == 0) return 0;
+  if (!radii || !means3D || !scales || !rotations || !sh_dc || !g_means2D || !g_conic_opacity ||
+      !g_colors || !dL_dmeans3D || !dL_dscales || !dL_drotations || !g_dc || (M > 0 && (!sh_rest || !g_rest)))
+    return fail(BLITZ_EINVAL, "blitz_preprocess_backward: null pointer");
+  if (!aligned16(rotations) || !aligned16(dL_drotations) || !aligned16(g_conic_opacity) ||
+      (g_conic_stride & 3))
+    return fail(BLITZ_EINVAL, "blitz_preprocess_backward: 16-byte alignment required");
+  PreprocessBwdParams b{};
+  b.f = make_pp(P, D, M, means3D, scales, rotations, sh_dc, dc_stride, sh_rest, rest_stride, nullptr,
+                scale_modifier, viewmatrix, projmatrix, campos, tanfovx, tanfovy, image_height,
+                image_width);
+  b.radii = radii;
+  b.g_means2D = g_means2D;
+  b.g_means2D_stride = g_means2D_stride;
+  b.g_conic_opacity = g_conic_opacity;
+  b.g_conic_stride = g_conic_stride;
+  b.g_colors = g_colors;
+  b.g_colors_stride = g_colors_stride;
+  b.g_means3D = dL_dmeans3D;
+  b.g_scales = dL_dscales;
+  b.g_rotations = dL_drotations;
+  b.g_opacities = dL_dopacity;
+  b.g_dc = g_dc;
+  b.g_dc_stride = g_dc_stride;
+  b.g_rest = g_rest;
+  b.g_rest_stride = g_rest_stride;
+  return check(launch_preprocess_bwd(b, accumulate != 0, S(stream)), "blitz_preprocess_backward");
+}
+
+int blitz_render_count(int64_t P, int image_height, int image_width, const float* means2D,
+                       const int32_t* radii, const uint8_t* compute_locally, uint32_t* counts,
+                       uint64_t* totals, void* stream) {
+  if (P < 0 || image_height <= 0 || image_width <= 0 || !totals || (P > 0 && (!means2D || !radii || !counts)))
+    return fail(BLITZ_EINVAL, "blitz_render_count: bad arguments");
+  if (P >= (int64_t)0xffffffff) return fail(BLITZ_EINVAL, "blitz_render_count: P must be < 2^32");
+  BinParams b{};
+  b.P = P;
+  b.W = image_width;
+  b.H = image_height;
+  b.grid_x = (image_width + kTileX - 1) / kTileX;
+  b.grid_y = (image_height + kTileY - 1) / kTileY;
+  b.means2D = means2D;
+  b.radii = radii;
+  b.compute_locally = reinterpret_cast<const bool*>(compute_locally);
+  b.counts = counts;
+  b.totals = reinterpret_cast<unsigned long long*>(totals);
+  return check(launch_bin_count(b, S(stream)), "blitz_render_count");
+}
+
+size_t blitz_render_scratch_bytes(int64_t P, int64_t n_vis, int64_t R, int image_height, int image_width) {
+  const int gx = (image_width + kTileX - 1) / kTileX, gy = (image_height + kTileY - 1) / kTileY;
+  return bin_scratch_bytes(P, n_vis, R, gx * gy);
+}
+
+int blitz_render_forward(int64_t P, int64_t n_vis, int64_t R, int image_height, int image_width,
+                         const float* means2D, const float* depths, const int32_t* radii,
+                         const float* conic_opacity, const float* rgb, const float* bg,
+                         const uint8_t* compute_locally, const uint32_t* counts, void* scratch,
+                         size_t scratch_bytes, uint32_t* point_list, uint32_t* ranges,
+                         float* final_T, uint32_t* n_contrib, float* out_color, int32_t* n_render,
+                         int32_t* n_consider, int32_t* n_contrib_tile, int32_t* out_observe,
+                         void* stream) {
+  if (P < 0 || n_vis < 0 || R < 0 || R >= (int64_t)0x7fffffff || n_vis > P || image_height <= 0 ||
+      image_width <= 0)
+    return fail(BLITZ_EINVAL, "blitz_render_forward: bad sizes");
+  if (!bg || !ranges || !final_T || !n_contrib || !out_color || !n_render || !n_consider ||
+      !n_contrib_tile || (P > 0 && (!means2D || !depths || !radii || !conic_opacity || !rgb || !counts ||
+                                     !out_observe)) ||
+      (R > 0 && (!point_list || !scratch)))
+    return fail(BLITZ_EINVAL, "blitz_render_forward: null pointer");
+  if (P > 0 && (!aligned16(conic_opacity) || (reinterpret_cast<uintptr_t>(means2D) & 7u)))
+    return fail(BLITZ_EINVAL, "blitz_render_forward: conic_opacity needs 16-byte, means2D 8-byte alignment");
+  const int gx = (image_width + kTileX - 1) / kTileX, gy = (image_height + kTileY - 1) / kTileY;
+  if (R > 0 && scratch_bytes < bin_scratch_bytes(P, n_vis, R, gx * gy))
+    return fail(BLITZ_ESCRATCH, "blitz_render_forward: scratch too small");
+  cudaStream_t st = S(stream);
+  BinSortParams bs{};
+  bs.b.P = P;
+  bs.b.W = image_width;
+  bs.b.H = image_height;
+  bs.b.grid_x = gx;
+  bs.b.grid_y = gy;
+  bs.b.means2D = means2D;
+  bs.b.depths = depths;
+  bs.b.radii = radii;
+  bs.b.compute_locally = reinterpret_cast<const bool*>(compute_locally);
+  bs.b.counts = const_cast<uint32_t*>(counts);
+  bs.n_vis = n_vis;
+  bs.R = R;
+  bs.scratch = scratch;
+  bs.scratch_bytes = scratch_bytes;
+  bs.point_list = point_list;
+  bs.ranges = reinterpret_cast<uint2*>(ranges);
+  int e = launch_bin_sort(bs, st);
+  if (e) return fail(e, "blitz_render_forward: binning");
+  BlendFwdParams f{};
+  f.W = image_width;
+  f.H = image_height;
+  f.grid_x = gx;
+  f.grid_y = gy;
+  f.P = P;
+  f.ranges = reinterpret_cast<const uint2*>(ranges);
+  f.point_list = point_list;
+  f.means2D = means2D;
+  f.conic_opacity = conic_opacity;
+  f.rgb = rgb;
+  f.bg = bg;
+  f.compute_locally = reinterpret_cast<const bool*>(compute_locally);
+  f.out_color = out_color;
+  f.final_T = final_T;
+  f.n_contrib = n_contrib;
+  f.out_observe = out_observe;
+  f.n_render = n_render;
+  f.n_consider = n_consider;
+  f.n_contrib_tile = n_contrib_tile;
+  return check(launch_blend_fwd(f, st), "blitz_render_forward: blend");
+}
+
+int blitz_render_backward(int64_t P, int image_height, int image_width, const uint32_t* point_list,
+                          const uint32_t* ranges, const float* final_T, const uint32_t* n_contrib,
+                          const float* means2D, const float* conic_opacity, const float* rgb,
+                          const float* bg, const uint8_t* compute_locally, const float* dL_dpix,
+                          float* grad_accum, void* stream) {
+  if (P < 0 || image_height <= 0 || image_width <= 0)
+    return fail(BLITZ_EINVAL, "blitz_render_backward: bad sizes");
+  if (!ranges || !final_T || !n_contrib || !bg || !dL_dpix ||
+      (P > 0 && (!means2D || !conic_opacity || !rgb || !grad_accum)))
+    return fail(BLITZ_EINVAL, "blitz_render_backward: null pointer");
+  if (P > 0 && (!aligned16(conic_opacity) || !aligned16(grad_accum)))
+    return fail(BLITZ_EINVAL, "blitz_render_backward: 16-byte alignment required");
+  BlendBwdParams b{};
+  b.W = image_width;
+  b.H = image_height;
+  b.grid_x = (image_width + kTileX - 1) / kTileX;
+  b.grid_y = (image_height + kTileY - 1) / kTileY;
+  b.P = P;
+  b.ranges = reinterpret_cast<const uint2*>(ranges);
+  b.point_list = point_list;
+  b.means2D = means2D;
+  b.conic_opacity = conic_opacity;
+  b.rgb = rgb;
+  b.bg = bg;
+  b.compute_locally = reinterpret_cast<const bool*>(compute_locally);
+  b.final_T = final_T;
+  b.n_contrib = n_contrib;
+  b.dL_dpix = dL_dpix;
+  b.grad_accum = grad_accum;
+  return check(launch_blend_bwd(b, S(stream)), "blitz_render_backward");
+}
+
+int blitz_loss_forward(int C, int Hb, int W, const float* img, const uint8_t* gt_u8,
+                       const float* gt_f32, const float* window11, float* partials, double* sums,
+                       void* stream) {
+  if (C < 0 || Hb < 0 || W < 0 || !window11 || !sums || ((gt_u8 == nullptr) == (gt_f32 == nullptr)))
+    return fail(BLITZ_EINVAL, "blitz_loss_forward: bad arguments");
+  if ((int64_t)C * Hb * W > 0 && (!img || !partials)) return fail(BLITZ_EINVAL, "blitz_loss_forward: null pointer");
+  LossParams p{C, Hb, W, img, gt_u8, gt_f32, partials};
+  return check(launch_loss_fwd(p, window11, sums, S(stream)), "blitz_loss_forward");
+}
+
+int blitz_loss_backward(int C, int Hb, int W, const float* img, const uint8_t* gt_u8,
+                        const float* gt_f32, const float* window11, const float* partials,
+                        const float* scale, float* dL_dimg, void* stream) {
+  if (C < 0 || Hb < 0 || W < 0 || !window11 || !scale || ((gt_u8 == nullptr) == (gt_f32 == nullptr)))
+    return fail(BLITZ_EINVAL, "blitz_loss_backward: bad arguments");
+  if ((int64_t)C * Hb * W > 0 && (!img || !partials || !dL_dimg))
+    return fail(BLITZ_EINVAL, "blitz_loss_backward: null pointer");
+  LossBwdParams b{};
+  b.f = LossParams{C, Hb, W, img, gt_u8, gt_f32, const_cast<float*>(partials)};
+  b.scale = scale;
+  b.dL_dimg = dL_dimg;
+  return check(launch_loss_bwd(b, window11, S(stream)), "blitz_loss_backward");
+}
+
+int blitz_get_local2j_ids_bool(int image_height, int image_width, int mp_rank, int mp_world_size,
+                               int64_t P, const float* means2D, const int32_t* radii,
+                               const int32_t* dist_global_strategy, int avoid_pixel_all2all,
+                               uint8_t* out, void* stream) {
+  (void)mp_rank;
+  if (P < 0 || mp_world_size <= 0 || image_height <= 0 || image_width <= 0)
+    return fail(BLITZ_EINVAL, "blitz_get_local2j_ids_bool: bad sizes");
+  if (P == 0) return 0;
+  if (!means2D || !radii || !dist_global_strategy || !out)
+    return fail(BLITZ_EINVAL, "blitz_get_local2j_ids_bool: null pointer");
+  RouteParams r{};
+  r.P = P;
+  r.W = image_width;
+  r.H = image_height;
+  r.grid_x = (image_width + kTileX - 1) / kTileX;
+  r.grid_y = (image_height + kTileY - 1) / kTileY;
+  r.world_size = mp_world_size;
+  r.means2D = means2D;
+  r.radii = radii;
+  r.dist_global_strategy = dist_global_strategy;
+  r.avoid_pixel_all2all = avoid_pixel_all2all != 0;
+  r.out_bool = reinterpret_cast<bool*>(out);
+  return check(launch_route_bool(r, S(stream)), "blitz_get_local2j_ids_bool");
+}
+
+}  // extern "C"

@@ -1,0 +1,171 @@
+// Internal launch interface between the C-ABI layer (capi.cu) and the kernels.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace blitz {
+
+enum : unsigned {
+  kErrPrefilteredCulled = 1u << 0,  // a Gaussian failed the near test with prefiltered=true
+  kErrBinOverflow = 1u << 1,        // more tile instances than the caller sized for
+};
+
+struct PreprocessParams {
+  int64_t P;
+  int D;  // active SH degree
+  int M;  // SH coefficients beyond DC held per Gaussian (<= 15)
+  const float* means3D;    // [P,3]
+  const float* scales;     // [P,3] activated
+  const float* rotations;  // [P,4] (r,x,y,z), 16-byte aligned rows
+  const float* opacities;  // [P] activated
+  const float* dc;         // DC triplet of Gaussian i at dc + i*dc_stride
+  int64_t dc_stride;
+  const float* rest;       // M triplets of Gaussian i at rest + i*rest_stride
+  int64_t rest_stride;
+  bool sh_packed16;        // dc/rest are one contiguous 16B-aligned [P,16,3] tensor
+  float scale_modifier;
+  const float* viewmatrix;  // device [16]
+  const float* projmatrix;  // device [16]
+  const float* campos;      // device [3]
+  float tanfovx, tanfovy, focal_x, focal_y;
+  int W, H, grid_x, grid_y;
+  bool prefiltered;
+  float* out_means2D;        // [P,2]
+  float* out_depths;         // [P]
+  int* out_radii;            // [P]
+  float* out_conic_opacity;  // [P,4]
+  float* out_rgb;            // [P,3]
+  bool* out_clamped;         // [P,3] or null
+  float* out_cov3D;          // [P,6] or null
+  unsigned* error_flag;      // device word, OR-ed with kErr* bits
+};
+
+struct PreprocessBwdParams {
+  PreprocessParams f;      // the forward's inputs (outputs unused)
+  const int* radii;        // [P] from the forward
+  const float* g_means2D;  // d/d(means2D) of Gaussian i at g_means2D + i*stride (x, y)
+  int64_t g_means2D_stride;
+  const float* g_conic_opacity;  // float4 at g_conic_opacity + i*stride (conic00, conic01, conic11, opacity)
+  int64_t g_conic_stride;
+  const float* g_colors;  // rgb grad at g_colors + i*stride
+  int64_t g_colors_stride;
+  float* g_means3D;    // [P,3]
+  float* g_scales;     // [P,3]
+  float* g_rotations;  // [P,4]
+  float* g_opacities;  // [P] or null
+  float* g_dc;         // at g_dc + i*g_dc_stride (3 floats)
+  int64_t g_dc_stride;
+  float* g_rest;       // at g_rest + i*g_rest_stride (M*3 floats)
+  int64_t g_rest_stride;
+};
+
+int launch_preprocess_fwd(const PreprocessParams& p, cudaStream_t st);
+int launch_preprocess_bwd(const PreprocessBwdParams& p, bool accumulate, cudaStream_t st);
+
+// ---------------------------------------------------------------------------
+// Binning + blending
+// ---------------------------------------------------------------------------
+struct BinParams {
+  int64_t P;
+  int W, H, grid_x, grid_y;
+  const float* means2D;          // [P,2]
+  const float* depths;           // [P]
+  const int* radii;              // [P]
+  const bool* compute_locally;   // [grid_y*grid_x] or null (= all tiles)
+  uint32_t* counts;              // [P] tiles touched under the mask
+  unsigned long long* totals;    // device [2]: {instances R, visible Gaussians}
+};
+
+int launch_bin_count(const BinParams& p, cudaStream_t st);
+
+// Scratch needed by bin_sort for the given sizes (bytes).
+size_t bin_scratch_bytes(int64_t P, int64_t n_vis, int64_t R, int n_tiles);
+
+struct BinSortParams {
+  BinParams b;
+  int64_t n_vis;   // visible Gaussians (counts > 0), read back by the host
+  int64_t R;       // tile instances, read back by the host
+  void* scratch;
+  size_t scratch_bytes;
+  uint32_t* point_list;  // [R] output: Gaussian index per instance, tile-major, depth order
+  uint2* ranges;         // [n_tiles] output: [start, end) per tile
+};
+
+int launch_bin_sort(const BinSortParams& p, cudaStream_t st);
+
+struct BlendFwdParams {
+  int W, H, grid_x, grid_y;
+  int64_t P;
+  const uint2* ranges;
+  const uint32_t* point_list;
+  const float* means2D;
+  const float* conic_opacity;
+  const float* rgb;
+  const float* bg;             // device [3]
+  const bool* compute_locally; // or null
+  float* out_color;            // [3,H,W]
+  float* final_T;              // [H*W]
+  uint32_t* n_contrib;         // [H*W] last contributor (1-based position in the tile list)
+  int* out_observe;            // [P], zero on entry
+  int* n_render;               // [tiles]
+  int* n_consider;             // [tiles]
+  int* n_contrib_tile;         // [tiles]
+};
+
+int launch_blend_fwd(const BlendFwdParams& p, cudaStream_t st);
+
+struct BlendBwdParams {
+  int W, H, grid_x, grid_y;
+  int64_t P;
+  const uint2* ranges;
+  const uint32_t* point_list;
+  const float* means2D;
+  const float* conic_opacity;
+  const float* rgb;
+  const float* bg;
+  const bool* compute_locally;
+  const float* final_T;
+  const uint32_t* n_contrib;
+  const float* dL_dpix;   // [3,H,W]
+  float* grad_accum;      // [P,16], zero on entry; layout in capi docs
+};
+
+int launch_blend_bwd(const BlendBwdParams& p, cudaStream_t st);
+
+// ---------------------------------------------------------------------------
+// Loss
+// ---------------------------------------------------------------------------
+struct LossParams {
+  int C, Hb, W;
+  const float* img;        // [C,Hb,W]
+  const uint8_t* gt_u8;    // [C,Hb,W] or null
+  const float* gt_f32;     // [C,Hb,W] or null
+  float* partials;         // [C,Hb,W,3] dSSIM/d(mu1, E[x^2], E[xy]) per pixel (fwd output)
+};
+// sums: device double[2] {sum |img-gt|, sum SSIM}, zero on entry.
+int launch_loss_fwd(const LossParams& p, const float* window11, double* sums, cudaStream_t st);
+
+struct LossBwdParams {
+  LossParams f;
+  const float* scale;   // device [2]: dLoss/d(sum L1), dLoss/d(sum SSIM)
+  float* dL_dimg;       // [C,Hb,W]
+};
+int launch_loss_bwd(const LossBwdParams& p, const float* window11, cudaStream_t st);
+
+// ---------------------------------------------------------------------------
+// Routing (which ranks' tile rows a Gaussian overlaps)
+// ---------------------------------------------------------------------------
+struct RouteParams {
+  int64_t P;
+  int W, H, grid_x, grid_y;
+  int world_size;
+  const float* means2D;
+  const int* radii;
+  const int* dist_global_strategy;  // [world_size+1] tile ids (row starts * grid_x)
+  bool avoid_pixel_all2all;
+  bool* out_bool;                   // [P, world_size]
+};
+int launch_route_bool(const RouteParams& p, cudaStream_t st);
+
+}  // namespace blitz

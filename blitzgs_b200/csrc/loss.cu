@@ -1,0 +1,218 @@
+// Fused L1 + SSIM over one image band, forward and backward.
+//
+// Semantics follow the reference loss (utils/loss_utils.py:83-124, called
+// from gaussian_renderer/loss_distribution.py:220-263): per channel, an 11x11
+// Gaussian window (sigma 1.5) applied as a depthwise convolution with zero
+// padding at the band edges to img, gt, img^2, gt^2 and img*gt, then
+//   SSIM = (2 mu1 mu2 + C1)(2 s12 + C2) / ((mu1^2 + mu2^2 + C1)(s11 + s22 + C2)),
+// C1 = 0.01^2, C2 = 0.03^2.  The forward returns sum |img - gt| and sum SSIM
+// over the band (accumulated in double) and keeps, per pixel and channel, the
+// three partial derivatives of the SSIM map with respect to mu1, E[x^2] and
+// E[xy]; the backward applies the (symmetric) window to those partials:
+//   dL/dx = s_l1 sign(x - y) + s_ssim (W*P1 + 2 x W*P2 + y W*P3).
+// The window is separable (the reference's 2D window is the outer product of
+// the 1D one), so each pass costs 2 x 11 taps instead of 121.
+//
+// One CTA computes a 32x32 output tile of one channel; input halos (42x42)
+// and the horizontal pass live in shared memory.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace blitz {
+
+namespace {
+
+constexpr int kLT = 32;              // output tile edge
+constexpr int kHalo = 5;             // window radius
+constexpr int kIn = kLT + 2 * kHalo; // 42
+constexpr float kC1 = 0.01f * 0.01f;
+constexpr float kC2 = 0.03f * 0.03f;
+
+struct Win {
+  float w[11];
+};
+
+__device__ __forceinline__ float load_gt(const LossParams& p, int64_t idx) {
+  if (p.gt_u8) return fminf(fmaxf((float)p.gt_u8[idx] / 255.0f, 0.0f), 1.0f);
+  return p.gt_f32[idx];
+}
+
+__global__ void __launch_bounds__(256) loss_fwd_kernel(LossParams p, Win win, double* sums) {
+  __shared__ float s_x[kIn][kIn + 1];
+  __shared__ float s_y[kIn][kIn + 1];
+  __shared__ float h[5][kIn][kLT + 1];
+  __shared__ double s_red[2][8];
+
+  const int c = blockIdx.z;
+  const int x0 = blockIdx.x * kLT, y0 = blockIdx.y * kLT;
+  const int64_t plane = (int64_t)p.Hb * p.W;
+  const float* img = p.img + c * plane;
+  const int tid = threadIdx.x;
+
+  for (int k = tid; k < kIn * kIn; k += blockDim.x) {
+    const int r = k / kIn, q = k % kIn;
+    const int gy = y0 - kHalo + r, gx = x0 - kHalo + q;
+    float xv = 0.f, yv = 0.f;
+    if (gy >= 0 && gy < p.Hb && gx >= 0 && gx < p.W) {
+      const int64_t idx = (int64_t)gy * p.W + gx;
+      xv = img[idx];
+      yv = load_gt(p, c * plane + idx);
+    }
+    s_x[r][q] = xv;
+    s_y[r][q] = yv;
+  }
+  __syncthreads();
+  // horizontal pass over all 42 input rows, 32 output columns
+  for (int k = tid; k < kIn * kLT; k += blockDim.x) {
+    const int r = k / kLT, q = k % kLT;
+    float a = 0.f, b = 0.f, aa = 0.f, bb = 0.f, ab = 0.f;
+#pragma unroll
+    for (int t = 0; t < 11; ++t) {
+      const float xv = s_x[r][q + t], yv = s_y[r][q + t], w = win.w[t];
+      a += w * xv;
+      b += w * yv;
+      aa += w * (xv * xv);
+      bb += w * (yv * yv);
+      ab += w * (xv * yv);
+    }
+    h[0][r][q] = a;
+    h[1][r][q] = b;
+    h[2][r][q] = aa;
+    h[3][r][q] = bb;
+    h[4][r][q] = ab;
+  }
+  __syncthreads();
+  double l1 = 0.0, ss = 0.0;
+  for (int k = tid; k < kLT * kLT; k += blockDim.x) {
+    const int r = k / kLT, q = k % kLT;
+    const int gy = y0 + r, gx = x0 + q;
+    if (gy >= p.Hb || gx >= p.W) continue;
+    float mu1 = 0.f, mu2 = 0.f, e11 = 0.f, e22 = 0.f, e12 = 0.f;
+#pragma unroll
+    for (int t = 0; t < 11; ++t) {
+      const float w = win.w[t];
+      mu1 += w * h[0][r + t][q];
+      mu2 += w * h[1][r + t][q];
+      e11 += w * h[2][r + t][q];
+      e22 += w * h[3][r + t][q];
+      e12 += w * h[4][r + t][q];
+    }
+    const float mu1_sq = mu1 * mu1, mu2_sq = mu2 * mu2, mu12 = mu1 * mu2;
+    const float s11 = e11 - mu1_sq, s22 = e22 - mu2_sq, s12 = e12 - mu12;
+    const float A1 = 2.f * mu12 + kC1, A2 = 2.f * s12 + kC2;
+    const float B1 = mu1_sq + mu2_sq + kC1, B2 = s11 + s22 + kC2;
+    const float D = B1 * B2;
+    const float S = (A1 * A2) / D;
+    const float dmu1 = (2.f * mu2 * (A2 - A1) - S * 2.f * mu1 * (B2 - B1)) / D;
+    const float de11 = -S / B2;
+    const float de12 = 2.f * A1 / D;
+    const float xv = s_x[r + kHalo][q + kHalo], yv = s_y[r + kHalo][q + kHalo];
+    l1 += fabsf(xv - yv);
+    ss += S;
+    float* pp = p.partials + 3 * (c * plane + (int64_t)gy * p.W + gx);
+    pp[0] = dmu1;
+    pp[1] = de11;
+    pp[2] = de12;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+    ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  }
+  if ((tid & 31) == 0) {
+    s_red[0][tid >> 5] = l1;
+    s_red[1][tid >> 5] = ss;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    double a = 0.0, b = 0.0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+      a += s_red[0][w];
+      b += s_red[1][w];
+    }
+    atomicAdd(sums + 0, a);
+    atomicAdd(sums + 1, b);
+  }
+}
+
+__global__ void __launch_bounds__(256) loss_bwd_kernel(LossBwdParams bp, Win win) {
+  const LossParams& p = bp.f;
+  __shared__ float s_p[3][kIn][kIn + 1];
+  __shared__ float h[3][kLT + 2 * kHalo][kLT + 1];
+  const int c = blockIdx.z;
+  const int x0 = blockIdx.x * kLT, y0 = blockIdx.y * kLT;
+  const int64_t plane = (int64_t)p.Hb * p.W;
+  const int tid = threadIdx.x;
+  for (int k = tid; k < kIn * kIn; k += blockDim.x) {
+    const int r = k / kIn, q = k % kIn;
+    const int gy = y0 - kHalo + r, gx = x0 - kHalo + q;
+    float a = 0.f, b = 0.f, d = 0.f;
+    if (gy >= 0 && gy < p.Hb && gx >= 0 && gx < p.W) {
+      const float* pp = p.partials + 3 * (c * plane + (int64_t)gy * p.W + gx);
+      a = pp[0];
+      b = pp[1];
+      d = pp[2];
+    }
+    s_p[0][r][q] = a;
+    s_p[1][r][q] = b;
+    s_p[2][r][q] = d;
+  }
+  __syncthreads();
+  for (int k = tid; k < kIn * kLT; k += blockDim.x) {
+    const int r = k / kLT, q = k % kLT;
+    float a = 0.f, b = 0.f, d = 0.f;
+#pragma unroll
+    for (int t = 0; t < 11; ++t) {
+      const float w = win.w[t];
+      a += w * s_p[0][r][q + t];
+      b += w * s_p[1][r][q + t];
+      d += w * s_p[2][r][q + t];
+    }
+    h[0][r][q] = a;
+    h[1][r][q] = b;
+    h[2][r][q] = d;
+  }
+  __syncthreads();
+  const float s_l1 = bp.scale[0], s_ss = bp.scale[1];
+  for (int k = tid; k < kLT * kLT; k += blockDim.x) {
+    const int r = k / kLT, q = k % kLT;
+    const int gy = y0 + r, gx = x0 + q;
+    if (gy >= p.Hb || gx >= p.W) continue;
+    float q1 = 0.f, q2 = 0.f, q3 = 0.f;
+#pragma unroll
+    for (int t = 0; t < 11; ++t) {
+      const float w = win.w[t];
+      q1 += w * h[0][r + t][q];
+      q2 += w * h[1][r + t][q];
+      q3 += w * h[2][r + t][q];
+    }
+    const int64_t idx = c * plane + (int64_t)gy * p.W + gx;
+    const float xv = p.img[idx];
+    const float yv = load_gt(p, idx);
+    const float diff = xv - yv;
+    const float sg = diff > 0.f ? 1.f : (diff < 0.f ? -1.f : 0.f);
+    bp.dL_dimg[idx] = s_l1 * sg + s_ss * (q1 + 2.f * xv * q2 + yv * q3);
+  }
+}
+
+}  // namespace
+
+int launch_loss_fwd(const LossParams& p, const float* window11, double* sums, cudaStream_t st) {
+  if (p.C <= 0 || p.Hb <= 0 || p.W <= 0) return 0;
+  Win w;
+  for (int i = 0; i < 11; ++i) w.w[i] = window11[i];
+  dim3 grid((p.W + kLT - 1) / kLT, (p.Hb + kLT - 1) / kLT, p.C);
+  loss_fwd_kernel<<<grid, 256, 0, st>>>(p, w, sums);
+  return (int)cudaGetLastError();
+}
+
+int launch_loss_bwd(const LossBwdParams& p, const float* window11, cudaStream_t st) {
+  if (p.f.C <= 0 || p.f.Hb <= 0 || p.f.W <= 0) return 0;
+  Win w;
+  for (int i = 0; i < 11; ++i) w.w[i] = window11[i];
+  dim3 grid((p.f.W + kLT - 1) / kLT, (p.f.Hb + kLT - 1) / kLT, p.f.C);
+  loss_bwd_kernel<<<grid, 256, 0, st>>>(p, w);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace blitz

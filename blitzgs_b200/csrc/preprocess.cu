@@ -1,0 +1,463 @@
+// EWA preprocess, forward and backward, one thread per Gaussian.
+//
+// Forward follows the reference preprocessCUDA
+// (submodule/diff-gaussian-rasterization_f/cuda_rasterizer/forward.cu:164-284,
+// host side rasterizer_impl.cu:982-1067) with three B200-side differences
+// that do not change any output bit:
+//   * no per-call cudaMalloc/cudaMemset/cudaFree of temporaries;
+//   * every output element is written by the kernel (zeros for culled
+//     Gaussians), so the caller needs no zero-fill pass;
+//   * SH coefficients are read through a (dc, rest) pointer pair with a
+//     per-Gaussian stride, so both the [P,16,3] tensor of the operator API and
+//     the model's separate _features_dc / _features_rest tensors are read in
+//     place (no torch.cat and no .contiguous() split copies); the
+//     contiguous [P,16,3] case is read with 16-byte vector loads.
+// Backward fuses the reference's computeCov2DCUDA and preprocessCUDA
+// (backward.cu:146-400) into one kernel and recomputes cov3D and the
+// clamp flags instead of reading them back from saved buffers.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace blitz {
+
+// Load the SH coefficients of Gaussian i into registers.  16 coefficient
+// triplets at most (degree 3).
+struct ShRegs {
+  float dc[3];
+  float rest[45];
+};
+
+__device__ __forceinline__ void load_sh(const PreprocessParams& p, int64_t i, int nrest,
+                                        ShRegs& s) {
+  const float* dc = p.dc + i * p.dc_stride;
+  const float* rest = p.rest + i * p.rest_stride;
+  if (p.sh_packed16) {
+    // Contiguous [P,16,3]: 48 floats = 12 x float4, dc is the first triplet.
+    const float4* v = reinterpret_cast<const float4*>(dc);
+    float buf[48];
+#pragma unroll
+    for (int k = 0; k < 12; ++k) {
+      float4 q = __ldg(v + k);
+      buf[4 * k + 0] = q.x;
+      buf[4 * k + 1] = q.y;
+      buf[4 * k + 2] = q.z;
+      buf[4 * k + 3] = q.w;
+    }
+    s.dc[0] = buf[0];
+    s.dc[1] = buf[1];
+    s.dc[2] = buf[2];
+#pragma unroll
+    for (int k = 0; k < 45; ++k) s.rest[k] = buf[3 + k];
+  } else {
+    s.dc[0] = __ldg(dc + 0);
+    s.dc[1] = __ldg(dc + 1);
+    s.dc[2] = __ldg(dc + 2);
+#pragma unroll
+    for (int k = 0; k < 45; ++k) s.rest[k] = (k < nrest * 3) ? __ldg(rest + k) : 0.f;
+  }
+}
+
+__global__ void __launch_bounds__(256) preprocess_fwd_kernel(PreprocessParams p) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= p.P) return;
+
+  const float* V = p.viewmatrix;
+  const float* Pm = p.projmatrix;
+  float Vs[16], Ps[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    Vs[k] = __ldg(V + k);
+    Ps[k] = __ldg(Pm + k);
+  }
+
+  const float3 p_orig = make_float3(__ldg(p.means3D + 3 * i + 0), __ldg(p.means3D + 3 * i + 1),
+                                    __ldg(p.means3D + 3 * i + 2));
+
+  bool visible = false;
+  float2 point_image = make_float2(0.f, 0.f);
+  float depth = 0.f;
+  int radius = 0;
+  float4 conic_op = make_float4(0.f, 0.f, 0.f, 0.f);
+  V3 rgb = {0.f, 0.f, 0.f};
+  bool clamp3[3] = {false, false, false};
+  float cov3d[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+
+  do {
+    // near-plane test (reference in_frustum, auxiliary.h:156-185)
+    const float3 p_view = xform_point3(p_orig, Vs);
+    if (p_view.z <= 0.2f) {
+      if (p.prefiltered) atomicOr(p.error_flag, kErrPrefilteredCulled);
+      break;
+    }
+    const float4 p_hom = xform_point4(p_orig, Ps);
+    const float p_w = 1.0f / (p_hom.w + 0.0000001f);
+    const float3 p_proj = make_float3(p_hom.x * p_w, p_hom.y * p_w, p_hom.z * p_w);
+
+    const float4 q = __ldg(reinterpret_cast<const float4*>(p.rotations) + i);
+    cov3d_from_scale_rot(__ldg(p.scales + 3 * i + 0), __ldg(p.scales + 3 * i + 1),
+                         __ldg(p.scales + 3 * i + 2), p.scale_modifier, q, cov3d);
+    const float3 cov = cov2d_ewa(p_orig, p.focal_x, p.focal_y, p.tanfovx, p.tanfovy, cov3d, Vs);
+
+    const float det = (cov.x * cov.z - cov.y * cov.y);
+    if (det == 0.0f) break;
+    const float det_inv = 1.f / det;
+    const float3 conic = make_float3(cov.z * det_inv, -cov.y * det_inv, cov.x * det_inv);
+
+    // Opacity-aware extent: min(3.33, sqrt(2 ln(255 alpha))).  The mixed
+    // double/float min resolves to fmin in double, so a NaN (alpha < 1/255)
+    // yields 3.33 and such Gaussians are not culled by opacity.
+    const float opacity = __ldg(p.opacities + i);
+    constexpr float alpha_threshold = 1.0f / 255.0f;
+    const float opacity_power_threshold = logf(opacity / alpha_threshold);
+    const float extent = fmin(3.33, (double)sqrtf(2.0f * opacity_power_threshold));
+
+    const float mid = 0.5f * (cov.x + cov.z);
+    const float lambda = mid + sqrtf(fmaxf(0.01f, mid * mid - det));
+    const float my_radius = extent * sqrtf(lambda);
+    if (my_radius <= 0.0f) break;
+
+    const float2 pimg = make_float2(ndc_to_pix(p_proj.x, p.W), ndc_to_pix(p_proj.y, p.H));
+    const float extent_x = fminf(extent * sqrtf(cov.x), my_radius);
+    const float extent_y = fminf(extent * sqrtf(cov.z), my_radius);
+    if (tile_rect_f_count(pimg, make_float2(extent_x, extent_y), p.grid_x, p.grid_y) == 0) break;
+
+    ShRegs s;
+    load_sh(p, i, p.M, s);
+    rgb = sh_to_rgb(p.D, p_orig, p.campos, s.dc, s.rest, clamp3);
+
+    visible = true;
+    depth = p_view.z;
+    radius = (int)ceilf(my_radius);
+    point_image = pimg;
+    conic_op = make_float4(conic.x, conic.y, conic.z, opacity);
+  } while (0);
+
+  (void)visible;
+  reinterpret_cast<float2*>(p.out_means2D)[i] = point_image;
+  p.out_depths[i] = depth;
+  p.out_radii[i] = radius;
+  reinterpret_cast<float4*>(p.out_conic_opacity)[i] = conic_op;
+  p.out_rgb[3 * i + 0] = rgb.x;
+  p.out_rgb[3 * i + 1] = rgb.y;
+  p.out_rgb[3 * i + 2] = rgb.z;
+  if (p.out_clamped) {
+    p.out_clamped[3 * i + 0] = clamp3[0];
+    p.out_clamped[3 * i + 1] = clamp3[1];
+    p.out_clamped[3 * i + 2] = clamp3[2];
+  }
+  if (p.out_cov3D) {
+#pragma unroll
+    for (int k = 0; k < 6; ++k) p.out_cov3D[6 * i + k] = cov3d[k];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Backward
+// ---------------------------------------------------------------------------
+
+// d(normalize(v))/dv applied to dv (reference auxiliary.h dnormvdv, float3).
+__device__ __forceinline__ float3 dnorm3(float3 v, float3 dv) {
+  const float sum2 = v.x * v.x + v.y * v.y + v.z * v.z;
+  const float invsum32 = 1.0f / sqrtf(sum2 * sum2 * sum2);
+  float3 r;
+  r.x = ((+sum2 - v.x * v.x) * dv.x - v.y * v.x * dv.y - v.z * v.x * dv.z) * invsum32;
+  r.y = (-v.x * v.y * dv.x + (sum2 - v.y * v.y) * dv.y - v.z * v.y * dv.z) * invsum32;
+  r.z = (-v.x * v.z * dv.x - v.y * v.z * dv.y + (sum2 - v.z * v.z) * dv.z) * invsum32;
+  return r;
+}
+
+template <bool ACC>
+__device__ __forceinline__ void put(float* dst, float v) {
+  if (ACC)
+    *dst += v;
+  else
+    *dst = v;
+}
+
+template <bool ACC>
+__global__ void __launch_bounds__(256) preprocess_bwd_kernel(PreprocessBwdParams p) {
+  const PreprocessParams& f = p.f;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= f.P) return;
+
+  float* g_mean = p.g_means3D + 3 * i;
+  float* g_scale = p.g_scales + 3 * i;
+  float* g_rot = p.g_rotations + 4 * i;
+  float* g_dc = p.g_dc + i * p.g_dc_stride;
+  float* g_rest = p.g_rest + i * p.g_rest_stride;
+
+  const float4 gco = *reinterpret_cast<const float4*>(p.g_conic_opacity + i * p.g_conic_stride);
+  if (p.g_opacities) put<ACC>(p.g_opacities + i, gco.w);
+
+  if (!(__ldg(p.radii + i) > 0)) {
+    if (!ACC) {
+      g_mean[0] = g_mean[1] = g_mean[2] = 0.f;
+      g_scale[0] = g_scale[1] = g_scale[2] = 0.f;
+      *reinterpret_cast<float4*>(g_rot) = make_float4(0.f, 0.f, 0.f, 0.f);
+      g_dc[0] = g_dc[1] = g_dc[2] = 0.f;
+#pragma unroll
+      for (int k = 0; k < 45; ++k)
+        if (k < f.M * 3) g_rest[k] = 0.f;
+    }
+    return;
+  }
+
+  float Vs[16], Ps[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    Vs[k] = __ldg(f.viewmatrix + k);
+    Ps[k] = __ldg(f.projmatrix + k);
+  }
+  const float3 mean = make_float3(__ldg(f.means3D + 3 * i + 0), __ldg(f.means3D + 3 * i + 1),
+                                  __ldg(f.means3D + 3 * i + 2));
+  const float sx = __ldg(f.scales + 3 * i + 0), sy = __ldg(f.scales + 3 * i + 1),
+              sz = __ldg(f.scales + 3 * i + 2);
+  const float4 q = __ldg(reinterpret_cast<const float4*>(f.rotations) + i);
+  float cov3d[6];
+  cov3d_from_scale_rot(sx, sy, sz, f.scale_modifier, q, cov3d);
+
+  // ---- 2D covariance / conic part (reference backward.cu:146-276) ----
+  const float dL_dconic_x = gco.x, dL_dconic_y = gco.y, dL_dconic_z = gco.z;
+  float3 t = xform_point3(mean, Vs);
+  const float h_x = f.focal_x, h_y = f.focal_y;
+  const float limx = 1.3f * f.tanfovx;
+  const float limy = 1.3f * f.tanfovy;
+  const float txtz = t.x / t.z;
+  const float tytz = t.y / t.z;
+  t.x = min(limx, max(-limx, txtz)) * t.z;
+  t.y = min(limy, max(-limy, tytz)) * t.z;
+  const float x_grad_mul = txtz < -limx || txtz > limx ? 0 : 1;
+  const float y_grad_mul = tytz < -limy || tytz > limy ? 0 : 1;
+
+  M3 J = make_m3(h_x / t.z, 0.0f, -(h_x * t.x) / (t.z * t.z), 0.0f, h_y / t.z,
+                 -(h_y * t.y) / (t.z * t.z), 0, 0, 0);
+  M3 W = make_m3(Vs[0], Vs[4], Vs[8], Vs[1], Vs[5], Vs[9], Vs[2], Vs[6], Vs[10]);
+  M3 Vrk = make_m3(cov3d[0], cov3d[1], cov3d[2], cov3d[1], cov3d[3], cov3d[4], cov3d[2],
+                   cov3d[4], cov3d[5]);
+  M3 T = m3_mul(W, J);
+  M3 c2 = m3_mul(m3_mul(m3_t(T), m3_t(Vrk)), T);
+  const float a = c2.m[0][0] += 0.3f;
+  const float b = c2.m[0][1];
+  const float c = c2.m[1][1] += 0.3f;
+
+  const float denom = a * c - b * b;
+  float dL_da = 0, dL_db = 0, dL_dc = 0;
+  const float denom2inv = 1.0f / ((denom * denom) + 0.0000001f);
+  float dcov[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (denom2inv != 0) {
+    dL_da = denom2inv * (-c * c * dL_dconic_x + 2 * b * c * dL_dconic_y + (denom - a * c) * dL_dconic_z);
+    dL_dc = denom2inv * (-a * a * dL_dconic_z + 2 * a * b * dL_dconic_y + (denom - a * c) * dL_dconic_x);
+    dL_db = denom2inv * 2 * (b * c * dL_dconic_x - (denom + 2 * b * b) * dL_dconic_y + a * b * dL_dconic_z);
+    dcov[0] = (T[0][0] * T[0][0] * dL_da + T[0][0] * T[1][0] * dL_db + T[1][0] * T[1][0] * dL_dc);
+    dcov[3] = (T[0][1] * T[0][1] * dL_da + T[0][1] * T[1][1] * dL_db + T[1][1] * T[1][1] * dL_dc);
+    dcov[5] = (T[0][2] * T[0][2] * dL_da + T[0][2] * T[1][2] * dL_db + T[1][2] * T[1][2] * dL_dc);
+    dcov[1] = 2 * T[0][0] * T[0][1] * dL_da + (T[0][0] * T[1][1] + T[0][1] * T[1][0]) * dL_db + 2 * T[1][0] * T[1][1] * dL_dc;
+    dcov[2] = 2 * T[0][0] * T[0][2] * dL_da + (T[0][0] * T[1][2] + T[0][2] * T[1][0]) * dL_db + 2 * T[1][0] * T[1][2] * dL_dc;
+    dcov[4] = 2 * T[0][2] * T[0][1] * dL_da + (T[0][1] * T[1][2] + T[0][2] * T[1][1]) * dL_db + 2 * T[1][1] * T[1][2] * dL_dc;
+  }
+  const float dL_dT00 = 2 * (T[0][0] * Vrk[0][0] + T[0][1] * Vrk[0][1] + T[0][2] * Vrk[0][2]) * dL_da +
+                        (T[1][0] * Vrk[0][0] + T[1][1] * Vrk[0][1] + T[1][2] * Vrk[0][2]) * dL_db;
+  const float dL_dT01 = 2 * (T[0][0] * Vrk[1][0] + T[0][1] * Vrk[1][1] + T[0][2] * Vrk[1][2]) * dL_da +
+                        (T[1][0] * Vrk[1][0] + T[1][1] * Vrk[1][1] + T[1][2] * Vrk[1][2]) * dL_db;
+  const float dL_dT02 = 2 * (T[0][0] * Vrk[2][0] + T[0][1] * Vrk[2][1] + T[0][2] * Vrk[2][2]) * dL_da +
+                        (T[1][0] * Vrk[2][0] + T[1][1] * Vrk[2][1] + T[1][2] * Vrk[2][2]) * dL_db;
+  const float dL_dT10 = 2 * (T[1][0] * Vrk[0][0] + T[1][1] * Vrk[0][1] + T[1][2] * Vrk[0][2]) * dL_dc +
+                        (T[0][0] * Vrk[0][0] + T[0][1] * Vrk[0][1] + T[0][2] * Vrk[0][2]) * dL_db;
+  const float dL_dT11 = 2 * (T[1][0] * Vrk[1][0] + T[1][1] * Vrk[1][1] + T[1][2] * Vrk[1][2]) * dL_dc +
+                        (T[0][0] * Vrk[1][0] + T[0][1] * Vrk[1][1] + T[0][2] * Vrk[1][2]) * dL_db;
+  const float dL_dT12 = 2 * (T[1][0] * Vrk[2][0] + T[1][1] * Vrk[2][1] + T[1][2] * Vrk[2][2]) * dL_dc +
+                        (T[0][0] * Vrk[2][0] + T[0][1] * Vrk[2][1] + T[0][2] * Vrk[2][2]) * dL_db;
+  const float dL_dJ00 = W[0][0] * dL_dT00 + W[0][1] * dL_dT01 + W[0][2] * dL_dT02;
+  const float dL_dJ02 = W[2][0] * dL_dT00 + W[2][1] * dL_dT01 + W[2][2] * dL_dT02;
+  const float dL_dJ11 = W[1][0] * dL_dT10 + W[1][1] * dL_dT11 + W[1][2] * dL_dT12;
+  const float dL_dJ12 = W[2][0] * dL_dT10 + W[2][1] * dL_dT11 + W[2][2] * dL_dT12;
+  const float tz = 1.f / t.z;
+  const float tz2 = tz * tz;
+  const float tz3 = tz2 * tz;
+  const float dL_dtx = x_grad_mul * -h_x * tz2 * dL_dJ02;
+  const float dL_dty = y_grad_mul * -h_y * tz2 * dL_dJ12;
+  const float dL_dtz = -h_x * tz2 * dL_dJ00 - h_y * tz2 * dL_dJ11 + (2 * h_x * t.x) * tz3 * dL_dJ02 +
+                       (2 * h_y * t.y) * tz3 * dL_dJ12;
+  float3 dmean = xform_vec_t(make_float3(dL_dtx, dL_dty, dL_dtz), Vs);
+
+  // ---- screen-space mean part (reference backward.cu:374-391) ----
+  {
+    const float* gm2 = p.g_means2D + i * p.g_means2D_stride;
+    const float gx = gm2[0], gy = gm2[1];
+    const float4 m_hom = xform_point4(mean, Ps);
+    const float m_w = 1.0f / (m_hom.w + 0.0000001f);
+    const float mul1 = (Ps[0] * mean.x + Ps[4] * mean.y + Ps[8] * mean.z + Ps[12]) * m_w * m_w;
+    const float mul2 = (Ps[1] * mean.x + Ps[5] * mean.y + Ps[9] * mean.z + Ps[13]) * m_w * m_w;
+    dmean.x += (Ps[0] * m_w - Ps[3] * mul1) * gx + (Ps[1] * m_w - Ps[3] * mul2) * gy;
+    dmean.y += (Ps[4] * m_w - Ps[7] * mul1) * gx + (Ps[5] * m_w - Ps[7] * mul2) * gy;
+    dmean.z += (Ps[8] * m_w - Ps[11] * mul1) * gx + (Ps[9] * m_w - Ps[11] * mul2) * gy;
+  }
+
+  // ---- SH colour part (reference backward.cu:20-141) ----
+  {
+    ShRegs s;
+    load_sh(f, i, f.M, s);
+    bool clamp3[3];
+    (void)sh_to_rgb(f.D, mean, f.campos, s.dc, s.rest, clamp3);
+    const float* gc = p.g_colors + i * p.g_colors_stride;
+    const float dR[3] = {clamp3[0] ? 0.f : gc[0], clamp3[1] ? 0.f : gc[1], clamp3[2] ? 0.f : gc[2]};
+    const float3 dir_orig = make_float3(mean.x - f.campos[0], mean.y - f.campos[1], mean.z - f.campos[2]);
+    const float len = sqrtf(dir_orig.x * dir_orig.x + dir_orig.y * dir_orig.y + dir_orig.z * dir_orig.z);
+    const float x = dir_orig.x / len, y = dir_orig.y / len, z = dir_orig.z / len;
+    const int D = f.D;
+    float dsh[45];
+#pragma unroll
+    for (int k = 0; k < 45; ++k) dsh[k] = 0.f;
+    float ddx[3] = {0.f, 0.f, 0.f}, ddy[3] = {0.f, 0.f, 0.f}, ddz[3] = {0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ch = 0; ch < 3; ++ch) put<ACC>(g_dc + ch, kSH0 * dR[ch]);
+    if (D > 0) {
+      const float b1 = -kSH1 * y, b2 = kSH1 * z, b3 = -kSH1 * x;
+#pragma unroll
+      for (int ch = 0; ch < 3; ++ch) {
+        const float* sh = s.rest;
+        dsh[0 * 3 + ch] = b1 * dR[ch];
+        dsh[1 * 3 + ch] = b2 * dR[ch];
+        dsh[2 * 3 + ch] = b3 * dR[ch];
+        ddx[ch] = -kSH1 * sh[2 * 3 + ch];
+        ddy[ch] = -kSH1 * sh[0 * 3 + ch];
+        ddz[ch] = kSH1 * sh[1 * 3 + ch];
+      }
+      if (D > 1) {
+        const float xx = x * x, yy = y * y, zz = z * z;
+        const float xy = x * y, yz = y * z, xz = x * z;
+        const float b4 = kSH2[0] * xy, b5 = kSH2[1] * yz, b6 = kSH2[2] * (2.f * zz - xx - yy),
+                    b7 = kSH2[3] * xz, b8 = kSH2[4] * (xx - yy);
+#pragma unroll
+        for (int ch = 0; ch < 3; ++ch) {
+          const float* sh = s.rest;
+          dsh[3 * 3 + ch] = b4 * dR[ch];
+          dsh[4 * 3 + ch] = b5 * dR[ch];
+          dsh[5 * 3 + ch] = b6 * dR[ch];
+          dsh[6 * 3 + ch] = b7 * dR[ch];
+          dsh[7 * 3 + ch] = b8 * dR[ch];
+          ddx[ch] += kSH2[0] * y * sh[3 * 3 + ch] + kSH2[2] * 2.f * -x * sh[5 * 3 + ch] +
+                     kSH2[3] * z * sh[6 * 3 + ch] + kSH2[4] * 2.f * x * sh[7 * 3 + ch];
+          ddy[ch] += kSH2[0] * x * sh[3 * 3 + ch] + kSH2[1] * z * sh[4 * 3 + ch] +
+                     kSH2[2] * 2.f * -y * sh[5 * 3 + ch] + kSH2[4] * 2.f * -y * sh[7 * 3 + ch];
+          ddz[ch] += kSH2[1] * y * sh[4 * 3 + ch] + kSH2[2] * 2.f * 2.f * z * sh[5 * 3 + ch] +
+                     kSH2[3] * x * sh[6 * 3 + ch];
+        }
+        if (D > 2) {
+          const float b9 = kSH3[0] * y * (3.f * xx - yy), b10 = kSH3[1] * xy * z,
+                      b11 = kSH3[2] * y * (4.f * zz - xx - yy),
+                      b12 = kSH3[3] * z * (2.f * zz - 3.f * xx - 3.f * yy),
+                      b13 = kSH3[4] * x * (4.f * zz - xx - yy), b14 = kSH3[5] * z * (xx - yy),
+                      b15 = kSH3[6] * x * (xx - 3.f * yy);
+#pragma unroll
+          for (int ch = 0; ch < 3; ++ch) {
+            const float* sh = s.rest;
+            dsh[8 * 3 + ch] = b9 * dR[ch];
+            dsh[9 * 3 + ch] = b10 * dR[ch];
+            dsh[10 * 3 + ch] = b11 * dR[ch];
+            dsh[11 * 3 + ch] = b12 * dR[ch];
+            dsh[12 * 3 + ch] = b13 * dR[ch];
+            dsh[13 * 3 + ch] = b14 * dR[ch];
+            dsh[14 * 3 + ch] = b15 * dR[ch];
+            ddx[ch] += (kSH3[0] * sh[8 * 3 + ch] * 3.f * 2.f * xy + kSH3[1] * sh[9 * 3 + ch] * yz +
+                        kSH3[2] * sh[10 * 3 + ch] * -2.f * xy + kSH3[3] * sh[11 * 3 + ch] * -3.f * 2.f * xz +
+                        kSH3[4] * sh[12 * 3 + ch] * (-3.f * xx + 4.f * zz - yy) +
+                        kSH3[5] * sh[13 * 3 + ch] * 2.f * xz + kSH3[6] * sh[14 * 3 + ch] * 3.f * (xx - yy));
+            ddy[ch] += (kSH3[0] * sh[8 * 3 + ch] * 3.f * (xx - yy) + kSH3[1] * sh[9 * 3 + ch] * xz +
+                        kSH3[2] * sh[10 * 3 + ch] * (-3.f * yy + 4.f * zz - xx) +
+                        kSH3[3] * sh[11 * 3 + ch] * -3.f * 2.f * yz + kSH3[4] * sh[12 * 3 + ch] * -2.f * xy +
+                        kSH3[5] * sh[13 * 3 + ch] * -2.f * yz + kSH3[6] * sh[14 * 3 + ch] * -3.f * 2.f * xy);
+            ddz[ch] += (kSH3[1] * sh[9 * 3 + ch] * xy + kSH3[2] * sh[10 * 3 + ch] * 4.f * 2.f * yz +
+                        kSH3[3] * sh[11 * 3 + ch] * 3.f * (2.f * zz - xx - yy) +
+                        kSH3[4] * sh[12 * 3 + ch] * 4.f * 2.f * xz + kSH3[5] * sh[13 * 3 + ch] * (xx - yy));
+          }
+        }
+      }
+    }
+    #pragma unroll
+    for (int k = 0; k < 45; ++k)
+      if (k < f.M * 3) put<ACC>(g_rest + k, dsh[k]);
+    const float3 ddir = make_float3(ddx[0] * dR[0] + ddx[1] * dR[1] + ddx[2] * dR[2],
+                                    ddy[0] * dR[0] + ddy[1] * dR[1] + ddy[2] * dR[2],
+                                    ddz[0] * dR[0] + ddz[1] * dR[1] + ddz[2] * dR[2]);
+    const float3 dm = dnorm3(dir_orig, ddir);
+    dmean.x += dm.x;
+    dmean.y += dm.y;
+    dmean.z += dm.z;
+  }
+  put<ACC>(g_mean + 0, dmean.x);
+  put<ACC>(g_mean + 1, dmean.y);
+  put<ACC>(g_mean + 2, dmean.z);
+
+  // ---- scale / rotation part (reference backward.cu:280-343) ----
+  {
+    const float r = q.x, x = q.y, y = q.z, z = q.w;
+    M3 R = make_m3(1.f - 2.f * (y * y + z * z), 2.f * (x * y - r * z), 2.f * (x * z + r * y),
+                   2.f * (x * y + r * z), 1.f - 2.f * (x * x + z * z), 2.f * (y * z - r * x),
+                   2.f * (x * z - r * y), 2.f * (y * z + r * x), 1.f - 2.f * (x * x + y * y));
+    const float s0 = f.scale_modifier * sx, s1 = f.scale_modifier * sy, s2 = f.scale_modifier * sz;
+    M3 S = make_m3(1.f, 0.f, 0.f, 0.f, 1.f, 0.f, 0.f, 0.f, 1.f);
+    S.m[0][0] = s0;
+    S.m[1][1] = s1;
+    S.m[2][2] = s2;
+    M3 Mm = m3_mul(S, R);
+    M3 dSig = make_m3(dcov[0], 0.5f * dcov[1], 0.5f * dcov[2], 0.5f * dcov[1], dcov[3],
+                      0.5f * dcov[4], 0.5f * dcov[2], 0.5f * dcov[4], dcov[5]);
+    M3 twoM;
+#pragma unroll
+    for (int cc = 0; cc < 3; ++cc)
+#pragma unroll
+      for (int rr = 0; rr < 3; ++rr) twoM.m[cc][rr] = 2.0f * Mm.m[cc][rr];
+    M3 dM = m3_mul(twoM, dSig);
+    M3 Rt = m3_t(R);
+    M3 dMt = m3_t(dM);
+    put<ACC>(g_scale + 0, Rt[0][0] * dMt[0][0] + Rt[0][1] * dMt[0][1] + Rt[0][2] * dMt[0][2]);
+    put<ACC>(g_scale + 1, Rt[1][0] * dMt[1][0] + Rt[1][1] * dMt[1][1] + Rt[1][2] * dMt[1][2]);
+    put<ACC>(g_scale + 2, Rt[2][0] * dMt[2][0] + Rt[2][1] * dMt[2][1] + Rt[2][2] * dMt[2][2]);
+#pragma unroll
+    for (int rr = 0; rr < 3; ++rr) {
+      dMt.m[0][rr] *= s0;
+      dMt.m[1][rr] *= s1;
+      dMt.m[2][rr] *= s2;
+    }
+    float4 dq;
+    dq.x = 2 * z * (dMt[0][1] - dMt[1][0]) + 2 * y * (dMt[2][0] - dMt[0][2]) + 2 * x * (dMt[1][2] - dMt[2][1]);
+    dq.y = 2 * y * (dMt[1][0] + dMt[0][1]) + 2 * z * (dMt[2][0] + dMt[0][2]) + 2 * r * (dMt[1][2] - dMt[2][1]) -
+           4 * x * (dMt[2][2] + dMt[1][1]);
+    dq.z = 2 * x * (dMt[1][0] + dMt[0][1]) + 2 * r * (dMt[2][0] - dMt[0][2]) + 2 * z * (dMt[1][2] + dMt[2][1]) -
+           4 * y * (dMt[2][2] + dMt[0][0]);
+    dq.w = 2 * r * (dMt[0][1] - dMt[1][0]) + 2 * x * (dMt[2][0] + dMt[0][2]) + 2 * y * (dMt[1][2] + dMt[2][1]) -
+           4 * z * (dMt[1][1] + dMt[0][0]);
+    if (ACC) {
+      float4 o = *reinterpret_cast<float4*>(g_rot);
+      o.x += dq.x;
+      o.y += dq.y;
+      o.z += dq.z;
+      o.w += dq.w;
+      *reinterpret_cast<float4*>(g_rot) = o;
+    } else {
+      *reinterpret_cast<float4*>(g_rot) = dq;
+    }
+  }
+}
+
+int launch_preprocess_fwd(const PreprocessParams& p, cudaStream_t st) {
+  if (p.P <= 0) return 0;
+  const int threads = 256;
+  const int64_t blocks = (p.P + threads - 1) / threads;
+  preprocess_fwd_kernel<<<(unsigned)blocks, threads, 0, st>>>(p);
+  return (int)cudaGetLastError();
+}
+
+int launch_preprocess_bwd(const PreprocessBwdParams& p, bool accumulate, cudaStream_t st) {
+  if (p.f.P <= 0) return 0;
+  const int threads = 256;
+  const int64_t blocks = (p.f.P + threads - 1) / threads;
+  if (accumulate)
+    preprocess_bwd_kernel<true><<<(unsigned)blocks, threads, 0, st>>>(p);
+  else
+    preprocess_bwd_kernel<false><<<(unsigned)blocks, threads, 0, st>>>(p);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace blitz

@@ -1,0 +1,340 @@
+"""Tensor-level wrappers of the C ABI: allocate outputs, call, return tensors.
+
+These are the building blocks of both the reference-compatible operator API
+(``blitzgs_b200.rasterizer``) and the fused training step
+(``blitzgs_b200.step``).  Every function runs on the current CUDA stream and
+raises if the native library is absent or the tensors are not on a GPU.
+"""
+import ctypes
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from ._lib import ptr
+
+TILE = 16
+
+
+class StageTimer:
+    """Optional CUDA-event timing of each native call, on the launching stream.
+
+    Disabled by default (no events, no overhead).  When enabled, every wrapper
+    below records (stage, start, end) events; ``summary()`` synchronises and
+    returns {stage: (calls, total_ms)}.  Used by bench.py for the live
+    per-kernel roofline numbers."""
+
+    def __init__(self):
+        self.enabled = False
+        self.records = []
+
+    def begin(self, name):
+        if not self.enabled:
+            return None
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        return (name, a, b)
+
+    def end(self, tok, **meta):
+        if tok is None:
+            return
+        tok[2].record()
+        self.records.append((tok[0], tok[1], tok[2], meta))
+
+    def summary(self):
+        out = {}
+        for name, a, b, meta in self.records:
+            b.synchronize()
+            c, t, m = out.get(name, (0, 0.0, []))
+            out[name] = (c + 1, t + a.elapsed_time(b), m + [meta])
+        return out
+
+    def reset(self):
+        self.records = []
+
+
+TIMER = StageTimer()
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("blitzgs_b200 operators need CUDA tensors (there is no CPU path)")
+
+
+def _f32c(t):
+    if t.dtype != torch.float32:
+        raise RuntimeError(f"expected float32 tensor, got {t.dtype}")
+    return t if t.is_contiguous() else t.contiguous()
+
+
+def grid_dims(H, W):
+    return (W + TILE - 1) // TILE, (H + TILE - 1) // TILE
+
+
+class _Scratch:
+    """Grow-only per-device scratch buffer for binning (never shrinks)."""
+
+    def __init__(self):
+        self.bufs = {}
+
+    def get(self, device, nbytes):
+        key = (device.type, device.index)
+        buf = self.bufs.get(key)
+        if buf is None or buf.numel() < nbytes:
+            cap = max(nbytes, int((buf.numel() if buf is not None else 0) * 1.25))
+            cap = (cap + (1 << 20) - 1) // (1 << 20) * (1 << 20)
+            self.bufs[key] = None
+            buf = torch.empty(cap, dtype=torch.uint8, device=device)
+            self.bufs[key] = buf
+        return buf
+
+
+SCRATCH = _Scratch()
+
+
+def sh_layout(shs=None, dc=None, rest=None):
+    """Return (dc, dc_stride, rest, rest_stride, M) for the kernel's SH addressing.
+
+    Either ``shs`` [P,K,3] (K coefficients, DC first, contiguous) or the split
+    ``dc`` [P,1,3] / ``rest`` [P,K-1,3] tensors (each contiguous) are read in
+    place without copies.
+    """
+    if shs is not None:
+        shs = _f32c(shs)
+        if shs.dim() != 3 or shs.shape[2] != 3 or shs.shape[1] < 1:
+            raise RuntimeError("sh must have dimensions (num_points, num_sh_coeffs, 3) with num_sh_coeffs >= 1")
+        K = shs.shape[1]
+        stride = K * 3
+        rest_t = shs.view(-1)[3:] if K > 1 else shs
+        return shs, stride, rest_t, stride, K - 1, (shs,)
+    dc = _f32c(dc)
+    rest = _f32c(rest)
+    M = rest.shape[1] if rest.dim() == 3 else 0
+    return dc, 3, rest, max(M, 1) * 3, M, (dc, rest)
+
+
+def preprocess_forward(means3D, scales, rotations, opacities, sh, raster, *, want_cov3D=False,
+                       want_clamped=False, error_word=None):
+    """EWA preprocess.  ``sh`` is the tuple from :func:`sh_layout`."""
+    _require_cuda(means3D, scales, rotations, opacities)
+    means3D, scales, rotations = _f32c(means3D), _f32c(scales), _f32c(rotations)
+    opacities = _f32c(opacities)
+    dc, dcs, rest, rs, M, _keep = sh
+    P = means3D.shape[0]
+    dev = means3D.device
+    means2D = torch.empty((P, 2), dtype=torch.float32, device=dev)
+    depths = torch.empty((P,), dtype=torch.float32, device=dev)
+    radii = torch.empty((P,), dtype=torch.int32, device=dev)
+    conic = torch.empty((P, 4), dtype=torch.float32, device=dev)
+    rgb = torch.empty((P, 3), dtype=torch.float32, device=dev)
+    cov3D = torch.empty((P, 6), dtype=torch.float32, device=dev) if want_cov3D else None
+    clamped = torch.empty((P, 3), dtype=torch.bool, device=dev) if want_clamped else None
+    if P > 0:
+        tok = TIMER.begin("preprocess_fwd")
+        _lib.call("blitz_preprocess_forward", P, int(raster.sh_degree), M, ptr(means3D), ptr(scales),
+                  ptr(rotations), ptr(dc), dcs, ptr(rest), rs, ptr(opacities),
+                  float(raster.scale_modifier), ptr(_f32c(raster.viewmatrix)),
+                  ptr(_f32c(raster.projmatrix)), ptr(_f32c(raster.campos)), float(raster.tanfovx),
+                  float(raster.tanfovy), int(raster.image_height), int(raster.image_width),
+                  int(bool(raster.prefiltered)), ptr(means2D), ptr(depths), ptr(radii), ptr(cov3D),
+                  ptr(conic), ptr(rgb), ptr(clamped), ptr(error_word), _lib.stream_ptr())
+        TIMER.end(tok, P=P)
+    return means2D, depths, radii, conic, rgb, cov3D, clamped
+
+
+def preprocess_backward(radii, means3D, scales, rotations, sh, raster, g_means2D, g_conic, g_colors,
+                        out=None, accumulate=False):
+    """Backward of :func:`preprocess_forward`.
+
+    ``g_means2D`` / ``g_conic`` / ``g_colors`` may be strided row views (e.g.
+    slices of the [P,16] render-gradient record); rows are addressed with
+    their row stride.  ``out`` = (dmeans3D, dscales, drot, dopacity, ddc, drest)
+    to write into (required when ``accumulate``); ``ddc`` / ``drest`` follow the
+    SH addressing of ``sh``'s layout with their own strides.
+    """
+    dc, dcs, rest, rs, M, _keep = sh
+    P = means3D.shape[0]
+    dev = means3D.device
+    for g, w in ((g_means2D, 2), (g_conic, 4), (g_colors, 3)):
+        if g.dim() != 2 or g.stride(1) != 1 or g.shape[1] < w:
+            raise RuntimeError("gradient rows must be unit-stride")
+    if out is None:
+        dmeans3D = torch.empty((P, 3), dtype=torch.float32, device=dev)
+        dscales = torch.empty((P, 3), dtype=torch.float32, device=dev)
+        drot = torch.empty((P, 4), dtype=torch.float32, device=dev)
+        dop = torch.empty((P, 1), dtype=torch.float32, device=dev)
+        dsh = torch.empty((P, M + 1, 3), dtype=torch.float32, device=dev)
+        ddc, ddcs = dsh, (M + 1) * 3
+        drest, drs = dsh.view(-1)[3:] if M > 0 else dsh, (M + 1) * 3
+        out_t = (dmeans3D, dscales, drot, dop, dsh)
+    else:
+        dmeans3D, dscales, drot, dop, (ddc, ddcs), (drest, drs) = out
+        out_t = None
+    if P > 0:
+        tok = TIMER.begin("preprocess_bwd")
+        _lib.call("blitz_preprocess_backward", P, int(raster.sh_degree), M, ptr(radii), ptr(means3D),
+                  ptr(scales), ptr(rotations), ptr(dc), dcs, ptr(rest), rs,
+                  float(raster.scale_modifier), ptr(raster.viewmatrix), ptr(raster.projmatrix),
+                  ptr(raster.campos), float(raster.tanfovx), float(raster.tanfovy),
+                  int(raster.image_height), int(raster.image_width), ptr(g_means2D), g_means2D.stride(0),
+                  ptr(g_conic), g_conic.stride(0), ptr(g_colors), g_colors.stride(0), ptr(dmeans3D),
+                  ptr(dscales), ptr(drot), ptr(dop), ptr(ddc), ddcs, ptr(drest), drs,
+                  int(bool(accumulate)), _lib.stream_ptr())
+        TIMER.end(tok, P=P, visible=None)
+    elif out is None:
+        for t in out_t:
+            t.zero_()
+    return out_t
+
+
+@dataclass
+class RenderState:
+    """What the render backward needs from its forward (caller-owned buffers)."""
+    H: int
+    W: int
+    R: int
+    n_vis: int
+    point_list: torch.Tensor  # int32 [R]
+    ranges: torch.Tensor      # int32 [T,2]
+    final_T: torch.Tensor     # f32 [H*W]
+    n_contrib: torch.Tensor   # int32 [H*W]
+
+
+_PINNED = {}
+
+
+def _pinned_totals(dev):
+    key = (dev.index,)
+    t = _PINNED.get(key)
+    if t is None:
+        t = torch.empty(2, dtype=torch.int64, pin_memory=True)
+        _PINNED[key] = t
+    return t
+
+
+def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_locally, H, W):
+    """Binning + blending of one camera.  Returns (color, n_render, n_consider,
+    n_contrib_tile, out_observe, state)."""
+    _require_cuda(means2D, depths, radii, conic_opacity, rgb, bg)
+    means2D, depths, conic_opacity, rgb, bg = map(_f32c, (means2D, depths, conic_opacity, rgb, bg))
+    radii = radii.contiguous()
+    if radii.dtype != torch.int32:
+        raise RuntimeError("radii must be int32")
+    P = means2D.shape[0]
+    dev = means2D.device
+    gx, gy = grid_dims(H, W)
+    T = gx * gy
+    cl = None
+    if compute_locally is not None:
+        cl = compute_locally.contiguous().view(-1)
+        if cl.dtype != torch.bool or cl.numel() != T:
+            raise RuntimeError(f"compute_locally must be bool with {T} tiles")
+    counts = torch.empty((max(P, 1),), dtype=torch.int32, device=dev)
+    totals = torch.empty((2,), dtype=torch.int64, device=dev)
+    st = _lib.stream_ptr()
+    tok = TIMER.begin("bin_count")
+    _lib.call("blitz_render_count", P, H, W, ptr(means2D), ptr(radii), ptr(cl), ptr(counts), ptr(totals), st)
+    TIMER.end(tok, P=P)
+    host = _pinned_totals(dev)
+    host.copy_(totals, non_blocking=True)
+    torch.cuda.current_stream().synchronize()
+    R, n_vis = int(host[0]), int(host[1])
+
+    point_list = torch.empty((max(R, 1),), dtype=torch.int32, device=dev)
+    ranges = torch.empty((T, 2), dtype=torch.int32, device=dev)
+    final_T = torch.empty((H * W,), dtype=torch.float32, device=dev)
+    n_contrib = torch.empty((H * W,), dtype=torch.int32, device=dev)
+    color = torch.empty((3, H, W), dtype=torch.float32, device=dev)
+    n_render = torch.empty((T,), dtype=torch.int32, device=dev)
+    n_consider = torch.empty((T,), dtype=torch.int32, device=dev)
+    n_contrib_tile = torch.empty((T,), dtype=torch.int32, device=dev)
+    out_observe = torch.zeros((P,), dtype=torch.int32, device=dev)
+    nbytes = _lib.load().blitz_render_scratch_bytes(P, n_vis, R, H, W)
+    scratch = SCRATCH.get(dev, nbytes)
+    tok = TIMER.begin("render_fwd")
+    _lib.call("blitz_render_forward", P, n_vis, R, H, W, ptr(means2D), ptr(depths), ptr(radii),
+              ptr(conic_opacity), ptr(rgb), ptr(bg), ptr(cl), ptr(counts), ptr(scratch), scratch.numel(),
+              ptr(point_list), ptr(ranges), ptr(final_T), ptr(n_contrib), ptr(color), ptr(n_render),
+              ptr(n_consider), ptr(n_contrib_tile), ptr(out_observe), st)
+    TIMER.end(tok, P=P, R=R, n_vis=n_vis, H=H, W=W)
+    state = RenderState(H, W, R, n_vis, point_list, ranges, final_T, n_contrib)
+    return color, n_render, n_consider, n_contrib_tile, out_observe, state
+
+
+def render_backward(state, means2D, conic_opacity, rgb, bg, compute_locally, dL_dpix, grad_accum=None):
+    """Returns the [P,16] per-Gaussian gradient record (see include/blitzgs_b200.h)."""
+    means2D, conic_opacity, rgb, bg = map(_f32c, (means2D, conic_opacity, rgb, bg))
+    dL_dpix = _f32c(dL_dpix)
+    P = means2D.shape[0]
+    if grad_accum is None:
+        grad_accum = torch.zeros((P, 16), dtype=torch.float32, device=means2D.device)
+    cl = compute_locally.contiguous().view(-1) if compute_locally is not None else None
+    tok = TIMER.begin("render_bwd")
+    _lib.call("blitz_render_backward", P, state.H, state.W, ptr(state.point_list), ptr(state.ranges),
+              ptr(state.final_T), ptr(state.n_contrib), ptr(means2D), ptr(conic_opacity), ptr(rgb), ptr(bg),
+              ptr(cl), ptr(dL_dpix), ptr(grad_accum), _lib.stream_ptr())
+    TIMER.end(tok, P=P, R=state.R)
+    return grad_accum
+
+
+_WINDOW = None
+
+
+def ssim_window():
+    """The reference's normalised 11-tap Gaussian (sigma 1.5) as float32 values
+    (utils/loss_utils.py:21-28: exp() in double, rounded to float32, divided
+    by its float32 sum).  Returns (ctypes float[11], torch tensor)."""
+    global _WINDOW
+    if _WINDOW is None:
+        g = torch.tensor([math.exp(-((x - 5) ** 2) / float(2 * 1.5 ** 2)) for x in range(11)],
+                         dtype=torch.float32)
+        g = g / g.sum()
+        _WINDOW = ((ctypes.c_float * 11)(*g.tolist()), g)
+    return _WINDOW
+
+
+def loss_forward(img, gt):
+    """Fused L1+SSIM sums over a band.  Returns (sums double[2], partials)."""
+    _require_cuda(img, gt)
+    img = _f32c(img)
+    C, Hb, W = img.shape
+    gt = gt.contiguous()
+    win, _ = ssim_window()
+    partials = torch.empty((C, Hb, W, 3), dtype=torch.float32, device=img.device)
+    sums = torch.zeros((2,), dtype=torch.float64, device=img.device)
+    gt_u8 = gt if gt.dtype == torch.uint8 else None
+    gt_f = _f32c(gt) if gt.dtype != torch.uint8 else None
+    tok = TIMER.begin("loss_fwd")
+    _lib.call("blitz_loss_forward", C, Hb, W, ptr(img), ptr(gt_u8), ptr(gt_f), win, ptr(partials),
+              ptr(sums), _lib.stream_ptr())
+    TIMER.end(tok, pixels=C * Hb * W)
+    return sums, partials
+
+
+def loss_backward(img, gt, partials, scale):
+    img = _f32c(img)
+    C, Hb, W = img.shape
+    gt = gt.contiguous()
+    win, _ = ssim_window()
+    out = torch.empty_like(img)
+    gt_u8 = gt if gt.dtype == torch.uint8 else None
+    gt_f = _f32c(gt) if gt.dtype != torch.uint8 else None
+    tok = TIMER.begin("loss_bwd")
+    _lib.call("blitz_loss_backward", C, Hb, W, ptr(img), ptr(gt_u8), ptr(gt_f), win, ptr(partials),
+              ptr(_f32c(scale)), ptr(out), _lib.stream_ptr())
+    TIMER.end(tok, pixels=C * Hb * W)
+    return out
+
+
+def local2j_ids_bool(H, W, mp_rank, mp_world_size, means2D, radii, dist_global_strategy,
+                     avoid_pixel_all2all=False):
+    _require_cuda(means2D, radii, dist_global_strategy)
+    P = means2D.shape[0]
+    out = torch.empty((P, mp_world_size), dtype=torch.bool, device=means2D.device)
+    _lib.call("blitz_get_local2j_ids_bool", int(H), int(W), int(mp_rank), int(mp_world_size), P,
+              ptr(_f32c(means2D)), ptr(radii.contiguous()), ptr(dist_global_strategy.to(torch.int32).contiguous()),
+              int(bool(avoid_pixel_all2all)), ptr(out), _lib.stream_ptr())
+    return out

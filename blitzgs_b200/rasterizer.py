@@ -1,0 +1,354 @@
+"""Drop-in replacement of the ``diff_gaussian_rasterization_f`` operator API.
+
+Mirrors submodule/diff-gaussian-rasterization_f/diff_gaussian_rasterization_f/
+__init__.py of the reference: the ``GaussianRasterizationSettings`` named
+tuple (:647-659), ``GaussianRasterizer`` (:661-829) with
+``preprocess_gaussians`` / ``render_gaussians``, the autograd functions
+``_PreprocessGaussians`` (:75-173) and ``_RenderGaussians`` (:204-318), and a
+``_C`` namespace exposing the native ops the Python layer calls directly
+(``preprocess_gaussians[_backward]``, ``render_gaussians[_backward]``,
+``get_local2j_ids_bool``) with the reference's positional signatures and
+return tuples.  Everything runs on the sm_100a kernels of libblitzgs_b200.so;
+there is no CPU path.
+
+Gradient conventions are the reference's: the means2D gradient is with
+respect to NDC-scaled screen position (dL/dpixel * W/2, H/2), the conic
+off-diagonal gradient is half the derivative with respect to the stored entry,
+and the alpha clamp at 0.99 is ignored in the backward.
+"""
+from types import SimpleNamespace
+from typing import NamedTuple
+
+import torch
+import torch.nn as nn
+
+from . import ops
+
+
+class GaussianRasterizationSettings(NamedTuple):
+    image_height: int
+    image_width: int
+    tanfovx: float
+    tanfovy: float
+    bg: torch.Tensor
+    scale_modifier: float
+    viewmatrix: torch.Tensor
+    projmatrix: torch.Tensor
+    sh_degree: int
+    campos: torch.Tensor
+    prefiltered: bool
+    debug: bool
+
+
+def _settings(scale_modifier, viewmatrix, projmatrix, tanfovx, tanfovy, H, W, degree, campos,
+              prefiltered):
+    return SimpleNamespace(scale_modifier=scale_modifier, viewmatrix=viewmatrix.contiguous(),
+                           projmatrix=projmatrix.contiguous(), tanfovx=tanfovx, tanfovy=tanfovy,
+                           image_height=H, image_width=W, sh_degree=degree,
+                           campos=campos.contiguous(), prefiltered=prefiltered)
+
+
+def _check_error_word(word, debug, prefiltered):
+    if word is None:
+        return
+    if debug or prefiltered:
+        v = int(word.item())
+        if v & 1:
+            raise RuntimeError("Point is filtered although prefiltered is set. This shouldn't happen!")
+
+
+# ---------------------------------------------------------------------------
+# Native-op namespace with the reference's _C signatures
+# ---------------------------------------------------------------------------
+
+def _preprocess_gaussians(means3D, scales, rotations, sh, opacity, scale_modifier, viewmatrix,
+                          projmatrix, tan_fovx, tan_fovy, image_height, image_width, degree, campos,
+                          prefiltered, debug, args=None):
+    """Reference: PreprocessGaussiansCUDA (f/rasterize_points.cu:834-923)."""
+    if means3D.ndimension() != 2 or means3D.size(1) != 3:
+        raise RuntimeError("means3D must have dimensions (num_points, 3)")
+    P = means3D.shape[0]
+    st = _settings(scale_modifier, viewmatrix, projmatrix, tan_fovx, tan_fovy, image_height,
+                   image_width, degree, campos, prefiltered)
+    dev = means3D.device
+    if P == 0 or sh.size(0) == 0:
+        z = lambda *s, dt=torch.float32: torch.zeros(s, dtype=dt, device=dev)
+        return (0, z(P, 2), z(P), z(P, dt=torch.int32), z(P, 6), z(P, 4), z(P, 3), z(P, 3, dt=torch.bool))
+    layout = ops.sh_layout(shs=sh)
+    word = torch.zeros(1, dtype=torch.int32, device=dev) if (prefiltered or debug) else None
+    means2D, depths, radii, conic, rgb, cov3D, clamped = ops.preprocess_forward(
+        means3D, scales, rotations, opacity.reshape(-1), layout, st, want_cov3D=True,
+        want_clamped=True, error_word=word)
+    _check_error_word(word, debug, prefiltered)
+    if debug:
+        torch.cuda.synchronize()
+    return 0, means2D, depths, radii, cov3D, conic, rgb, clamped
+
+
+def _preprocess_gaussians_backward(radii, cov3D, clamped, means3D, scales, rotations, sh,
+                                   scale_modifier, viewmatrix, projmatrix, tan_fovx, tan_fovy,
+                                   image_height, image_width, degree, campos, dL_dmeans2D,
+                                   dL_dconic_opacity, dL_dcolors, R=0, debug=False, args=None):
+    """Reference: PreprocessGaussiansBackwardCUDA (f/rasterize_points.cu:926-1029).
+
+    cov3D and clamped are accepted for signature compatibility; the kernel
+    recomputes both from the parameters (bit-identical to the forward's)."""
+    st = _settings(scale_modifier, viewmatrix, projmatrix, tan_fovx, tan_fovy, image_height,
+                   image_width, degree, campos, False)
+    layout = ops.sh_layout(shs=sh)
+    gm = dL_dmeans2D.contiguous()
+    gc = dL_dconic_opacity.contiguous()
+    gcol = dL_dcolors.contiguous()
+    dmeans3D, dscales, drot, dop, dsh = ops.preprocess_backward(
+        radii.contiguous(), means3D.contiguous(), scales.contiguous(), rotations.contiguous(), layout,
+        st, gm, gc, gcol)
+    if debug:
+        torch.cuda.synchronize()
+    return dmeans3D, dscales, drot, dsh, dop
+
+
+def _pack_img_state(state):
+    """ranges, final_T and n_contrib in one int32 buffer (the reference's imgBuffer role)."""
+    return torch.cat([state.ranges.view(-1), state.final_T.view(torch.int32), state.n_contrib])
+
+
+def _unpack_img_state(buf, H, W, R, point_list):
+    gx, gy = ops.grid_dims(H, W)
+    T = gx * gy
+    HW = H * W
+    ranges = buf[: 2 * T].view(T, 2)
+    final_T = buf[2 * T: 2 * T + HW].view(torch.float32)
+    n_contrib = buf[2 * T + HW: 2 * T + 2 * HW]
+    return ops.RenderState(H, W, R, -1, point_list, ranges, final_T, n_contrib)
+
+
+class _Timer:
+    def __init__(self):
+        self.a = torch.cuda.Event(enable_timing=True)
+        self.b = torch.cuda.Event(enable_timing=True)
+
+    def start(self):
+        self.a.record()
+
+    def stop(self):
+        self.b.record()
+
+    def ms(self):
+        self.b.synchronize()
+        return self.a.elapsed_time(self.b)
+
+
+def _stats(args):
+    if isinstance(args, dict):
+        sc = args.get("stats_collector")
+        if isinstance(sc, dict):
+            return sc
+    return None
+
+
+def _render_gaussians(background, image_height, image_width, means2D, depths, radii, conic_opacity,
+                      rgb, compute_locally, viewmatrix=None, campos=None, tan_fovx=None, tan_fovy=None,
+                      all_map=None, render_geo=False, debug=False, args=None):
+    """Reference: RenderGaussiansCUDA (r/rasterize_points.cu:274-361).
+
+    Returns (num_rendered, color, n_render, n_consider, n_contrib, out_observe,
+    out_all_map, out_plane_depth, geomBuffer, binningBuffer, imgBuffer); the
+    three buffers hold this implementation's backward state."""
+    if render_geo:
+        raise NotImplementedError("render_geo (all-map / plane-depth rendering) is not on the training path")
+    H, W = int(image_height), int(image_width)
+    P = means2D.shape[0]
+    dev = means2D.device
+    sc = _stats(args)
+    tm = _Timer() if sc is not None else None
+    if tm:
+        tm.start()
+    color, n_render, n_consider, n_contrib, out_observe, state = ops.render_forward(
+        means2D, depths, radii, conic_opacity, rgb, background, compute_locally, H, W)
+    if tm:
+        tm.stop()
+        sc["_blitz_fwd_timer"] = tm
+    out_all_map = torch.zeros((5, H, W), dtype=torch.float32, device=dev)
+    out_plane_depth = torch.zeros((1, H, W), dtype=torch.float32, device=dev)
+    geom = torch.empty((0,), dtype=torch.uint8, device=dev)
+    img = _pack_img_state(state)
+    if debug:
+        torch.cuda.synchronize()
+    return (state.R, color, n_render, n_consider, n_contrib, out_observe, out_all_map, out_plane_depth,
+            geom, state.point_list, img)
+
+
+def _render_gaussians_backward_record(background, R, binningBuffer, imageBuffer, compute_locally,
+                                      dL_dout_color, means2D, conic_opacity, rgb, args=None):
+    H, W = int(dL_dout_color.shape[1]), int(dL_dout_color.shape[2])
+    state = _unpack_img_state(imageBuffer, H, W, R, binningBuffer)
+    sc = _stats(args)
+    tm = _Timer() if sc is not None else None
+    if tm:
+        tm.start()
+    rec = ops.render_backward(state, means2D, conic_opacity, rgb, background, compute_locally,
+                              dL_dout_color)
+    if tm:
+        tm.stop()
+        sc["backward_render_time"] = tm.ms()
+        fwd = sc.pop("_blitz_fwd_timer", None)
+        if fwd is not None:
+            sc["forward_render_time"] = fwd.ms()
+    return rec
+
+
+def _render_gaussians_backward(background, tan_fovx, tan_fovy, all_map_pixels, all_maps, R, geomBuffer,
+                               binningBuffer, imageBuffer, compute_locally, dL_dout_color,
+                               dL_dout_all_map, dL_dout_plane_depth, means2D, conic_opacity, rgb,
+                               render_geo=False, debug=False, args=None):
+    """Reference: RenderGaussiansBackwardCUDA (r/rasterize_points.cu:364-436).
+    Returns (dL_dmeans2D [P,3], dL_dmeans2D_abs [P,3], dL_dconic_opacity [P,4],
+    dL_dcolors [P,3], dL_dall_map [P,5])."""
+    if render_geo:
+        raise NotImplementedError("render_geo (all-map / plane-depth rendering) is not on the training path")
+    rec = _render_gaussians_backward_record(background, R, binningBuffer, imageBuffer, compute_locally,
+                                            dL_dout_color.contiguous(), means2D, conic_opacity, rgb, args)
+    P = rec.shape[0]
+    dmeans2D = rec[:, 0:3].contiguous()
+    dmeans2D[:, 2] = 0
+    dabs = rec[:, 4:7].contiguous()
+    dall = torch.zeros((P, 5), dtype=torch.float32, device=rec.device)
+    if debug:
+        torch.cuda.synchronize()
+    return dmeans2D, dabs, rec[:, 8:12].contiguous(), rec[:, 12:15].contiguous(), dall
+
+
+def _get_local2j_ids_bool(image_height, image_width, mp_rank, mp_world_size, means2D, radii,
+                          dist_global_strategy, args=None):
+    """Reference: GetLocal2jIdsBoolCUDA (f/rasterize_points.cu:258-288)."""
+    avoid = bool(args.get("avoid_pixel_all2all", False)) if isinstance(args, dict) else False
+    return ops.local2j_ids_bool(image_height, image_width, mp_rank, mp_world_size, means2D, radii,
+                                dist_global_strategy, avoid)
+
+
+_C = SimpleNamespace(
+    preprocess_gaussians=_preprocess_gaussians,
+    preprocess_gaussians_backward=_preprocess_gaussians_backward,
+    render_gaussians=_render_gaussians,
+    render_gaussians_backward=_render_gaussians_backward,
+    get_local2j_ids_bool=_get_local2j_ids_bool,
+)
+
+
+# ---------------------------------------------------------------------------
+# Autograd functions and module (reference f/__init__.py:55-318, 647-829)
+# ---------------------------------------------------------------------------
+
+def preprocess_gaussians(means3D, scales, rotations, sh, opacities, raster_settings, cuda_args):
+    return _PreprocessGaussians.apply(means3D, scales, rotations, sh, opacities, raster_settings, cuda_args)
+
+
+class _PreprocessGaussians(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, means3D, scales, rotations, sh, opacities, raster_settings, cuda_args):
+        rs = raster_settings
+        num_rendered, means2D, depths, radii, cov3D, conic_opacity, rgb, clamped = _C.preprocess_gaussians(
+            means3D, scales, rotations, sh, opacities, rs.scale_modifier, rs.viewmatrix, rs.projmatrix,
+            rs.tanfovx, rs.tanfovy, rs.image_height, rs.image_width, rs.sh_degree, rs.campos,
+            rs.prefiltered, rs.debug, cuda_args)
+        ctx.raster_settings = rs
+        ctx.cuda_args = cuda_args
+        ctx.num_rendered = num_rendered
+        ctx.save_for_backward(means3D, scales, rotations, sh, radii)
+        ctx.mark_non_differentiable(radii, depths)
+        return means2D, rgb, conic_opacity, radii, depths
+
+    @staticmethod
+    def backward(ctx, grad_means2D, grad_rgb, grad_conic_opacity, grad_radii, grad_depths):
+        rs = ctx.raster_settings
+        means3D, scales, rotations, sh, radii = ctx.saved_tensors
+        P = means3D.shape[0]
+        dev = means3D.device
+        if grad_means2D is None:
+            grad_means2D = torch.zeros((P, 2), dtype=torch.float32, device=dev)
+        if grad_rgb is None:
+            grad_rgb = torch.zeros((P, 3), dtype=torch.float32, device=dev)
+        if grad_conic_opacity is None:
+            grad_conic_opacity = torch.zeros((P, 4), dtype=torch.float32, device=dev)
+        st = _settings(rs.scale_modifier, rs.viewmatrix, rs.projmatrix, rs.tanfovx, rs.tanfovy,
+                       rs.image_height, rs.image_width, rs.sh_degree, rs.campos, False)
+        layout = ops.sh_layout(shs=sh)
+        gm = grad_means2D if grad_means2D.stride(-1) == 1 else grad_means2D.contiguous()
+        gc = grad_conic_opacity if (grad_conic_opacity.stride(-1) == 1 and grad_conic_opacity.stride(0) % 4 == 0
+                                    and grad_conic_opacity.data_ptr() % 16 == 0) else grad_conic_opacity.contiguous()
+        gcol = grad_rgb if grad_rgb.stride(-1) == 1 else grad_rgb.contiguous()
+        dmeans3D, dscales, drot, dop, dsh = ops.preprocess_backward(
+            radii, means3D, scales, rotations, layout, st, gm, gc, gcol)
+        return dmeans3D, dscales, drot, dsh, dop, None, None
+
+
+def render_gaussians(means2D, means2D_abs, conic_opacity, rgb, all_map, depths, radii, compute_locally,
+                     extended_compute_locally, raster_settings, cuda_args):
+    return _RenderGaussians.apply(means2D, means2D_abs, conic_opacity, rgb, all_map, depths, radii,
+                                  compute_locally, extended_compute_locally, raster_settings, cuda_args)
+
+
+class _RenderGaussians(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, means2D, means2D_abs, conic_opacity, rgb, all_maps, depths, radii, compute_locally,
+                extended_compute_locally, raster_settings, cuda_args):
+        rs = raster_settings
+        avoid = bool(cuda_args.get("avoid_pixel_all2all", False)) if isinstance(cuda_args, dict) else False
+        cl = extended_compute_locally if avoid else compute_locally
+        (num_rendered, color, n_render, n_consider, n_contrib, out_observe, out_all_map, out_plane_depth,
+         geom, binning, img) = _C.render_gaussians(
+            rs.bg, rs.image_height, rs.image_width, means2D, depths, radii, conic_opacity, rgb, cl,
+            rs.viewmatrix, rs.campos, rs.tanfovx, rs.tanfovy, all_maps, getattr(rs, "render_geo", False),
+            rs.debug, cuda_args)
+        ctx.raster_settings = rs
+        ctx.cuda_args = cuda_args
+        ctx.num_rendered = num_rendered
+        ctx.means2D_abs_shape = tuple(means2D_abs.shape) if means2D_abs is not None else None
+        ctx.save_for_backward(means2D, conic_opacity, rgb, binning, img, cl if cl is not None else compute_locally)
+        ctx.mark_non_differentiable(n_render, n_consider, n_contrib)
+        return color, n_render, n_consider, n_contrib, out_observe, out_all_map, out_plane_depth
+
+    @staticmethod
+    def backward(ctx, grad_color, grad_n_render, grad_n_consider, grad_n_contrib, grad_out_observe,
+                 grad_out_all_map, grad_out_plane_depth):
+        rs = ctx.raster_settings
+        means2D, conic_opacity, rgb, binning, img, cl = ctx.saved_tensors
+        if grad_color is None:
+            grad_color = torch.zeros((3, rs.image_height, rs.image_width), dtype=torch.float32,
+                                     device=means2D.device)
+        rec = _render_gaussians_backward_record(rs.bg, ctx.num_rendered, binning, img, cl,
+                                                grad_color.contiguous(), means2D, conic_opacity, rgb,
+                                                ctx.cuda_args)
+        g_means2D = rec[:, 0:2]
+        g_abs = None
+        if ctx.needs_input_grad[1] and ctx.means2D_abs_shape is not None:
+            g_abs = rec[:, 4:4 + ctx.means2D_abs_shape[1]]
+        g_conic = rec[:, 8:12]
+        g_rgb = rec[:, 12:15]
+        return g_means2D, g_abs, g_conic, g_rgb, None, None, None, None, None, None, None
+
+
+class GaussianRasterizer(nn.Module):
+    def __init__(self, raster_settings):
+        super().__init__()
+        self.raster_settings = raster_settings
+
+    def preprocess_gaussians(self, means3D, scales, rotations, shs, opacities, cuda_args=None):
+        return preprocess_gaussians(means3D, scales, rotations, shs, opacities, self.raster_settings, cuda_args)
+
+    def render_gaussians(self, means2D, means2D_abs, conic_opacity, rgb, all_map, depths, radii,
+                         compute_locally, extended_compute_locally, cuda_args=None):
+        return render_gaussians(means2D, means2D_abs, conic_opacity, rgb, all_map, depths, radii,
+                                compute_locally, extended_compute_locally, self.raster_settings, cuda_args)
+
+    def markVisible(self, positions):
+        raise NotImplementedError("markVisible belongs to the eval/culling rasterizer (not on the training path)")
+
+    def forward(self, *a, **k):
+        raise NotImplementedError("the full non-distributed rasterizer (eval/culling) is not on the training path")
+
+    def render_simp(self, *a, **k):
+        raise NotImplementedError("render_simp (mini-splatting culling) is not on the training path")
+
+    def render_depth(self, *a, **k):
+        raise NotImplementedError("render_depth (eval) is not on the training path")

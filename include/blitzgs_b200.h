@@ -1,0 +1,184 @@
+/*
+ * blitzgs_b200 -- C ABI of the B200 (sm_100a) Gaussian-splatting training path.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (passed as void*; NULL = legacy default stream), launches asynchronously on
+ * that stream and returns an int status: 0 on success, otherwise a CUDA error
+ * code or one of the BLITZ_E* codes below.  blitz_last_error() returns a
+ * description of the last failure on the calling thread.  The library never
+ * allocates or frees device memory: the caller provides every output and
+ * scratch buffer (sizes are queried with the *_bytes functions).  Nothing
+ * traps: conditions the reference turns into a device __trap() set bits in a
+ * caller-provided device error word instead.
+ *
+ * Tensor layouts are the reference's (row-major, fp32 unless stated):
+ *   means3D [P,3], scales [P,3] (activated), rotations [P,4] (r,x,y,z;
+ *   normalised by the caller; 16-byte aligned rows), opacities [P] (activated),
+ *   SH coefficients addressed as (dc + i*dc_stride, rest + i*rest_stride) in
+ *   floats so both a contiguous [P,16,3] tensor (dc_stride = rest_stride = 48,
+ *   rest = dc + 3) and split [P,1,3] / [P,15,3] tensors are accepted,
+ *   viewmatrix / projmatrix: device float[16] (the transposed world-to-view
+ *   and full projection matrices of the reference Camera), campos float[3].
+ *
+ * Images are [3,H,W]; tiles are 16x16 pixels, grid_x = ceil(W/16),
+ * grid_y = ceil(H/16), tile t = ty*grid_x + tx.
+ */
+#ifndef BLITZGS_B200_H_
+#define BLITZGS_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BLITZ_OK 0
+#define BLITZ_EINVAL 10001      /* bad argument (size, alignment, null pointer) */
+#define BLITZ_ESCRATCH 10002    /* scratch buffer smaller than *_bytes() asked for */
+
+/* Device error-word bits (see blitz_preprocess_forward). */
+#define BLITZ_ERRBIT_PREFILTERED_CULLED 1u /* a Gaussian failed the near test with prefiltered=1 */
+
+const char* blitz_version(void);
+const char* blitz_last_error(void);
+
+/*
+ * EWA preprocess of P Gaussians for one camera.
+ * Replaces _C.preprocess_gaussians / PreprocessGaussiansCUDA
+ * (submodule/diff-gaussian-rasterization_f/rasterize_points.cu:834-923 and
+ * cuda_rasterizer/rasterizer_impl.cu:982-1067).
+ * Outputs (all written, zeros for culled Gaussians): means2D [P,2] (pixels),
+ * depths [P] (view z), radii int32 [P], conic_opacity [P,4], rgb [P,3];
+ * optional (may be NULL): cov3D [P,6], clamped uint8 [P,3].
+ * error_word: device uint32 OR-ed with BLITZ_ERRBIT_* (may be NULL).
+ * M = SH coefficients beyond DC per Gaussian (0..15), D = active degree (0..3).
+ */
+int blitz_preprocess_forward(int64_t P, int D, int M, const float* means3D, const float* scales,
+                             const float* rotations, const float* sh_dc, int64_t dc_stride,
+                             const float* sh_rest, int64_t rest_stride, const float* opacities,
+                             float scale_modifier, const float* viewmatrix, const float* projmatrix,
+                             const float* campos, float tanfovx, float tanfovy, int image_height,
+                             int image_width, int prefiltered, float* means2D, float* depths,
+                             int32_t* radii, float* cov3D, float* conic_opacity, float* rgb,
+                             uint8_t* clamped, uint32_t* error_word, void* stream);
+
+/*
+ * Backward of blitz_preprocess_forward.
+ * Replaces _C.preprocess_gaussians_backward / PreprocessGaussiansBackwardCUDA
+ * (submodule/diff-gaussian-rasterization_f/rasterize_points.cu:926-1029 and
+ * cuda_rasterizer/backward.cu:146-400).
+ * Upstream gradients are addressed with per-Gaussian strides (floats):
+ *   dL_dmeans2D (x,y) at g_means2D + i*g_means2D_stride  (NDC-scaled, as the
+ *     reference's render backward produces),
+ *   dL_dconic_opacity float4 at g_conic_opacity + i*g_conic_stride (16-byte aligned),
+ *   dL_dcolors (r,g,b) at g_colors + i*g_colors_stride.
+ * Outputs: dL_dmeans3D [P,3], dL_dscales [P,3], dL_drotations [P,4]
+ * (w.r.t. the rotation as passed in), dL_dopacity [P] (may be NULL), SH grads
+ * at (g_dc + i*g_dc_stride, g_rest + i*g_rest_stride).
+ * accumulate = 0 overwrites the outputs (zeros for radii <= 0), 1 adds.
+ */
+int blitz_preprocess_backward(int64_t P, int D, int M, const int32_t* radii, const float* means3D,
+                              const float* scales, const float* rotations, const float* sh_dc,
+                              int64_t dc_stride, const float* sh_rest, int64_t rest_stride,
+                              float scale_modifier, const float* viewmatrix, const float* projmatrix,
+                              const float* campos, float tanfovx, float tanfovy, int image_height,
+                              int image_width, const float* g_means2D, int64_t g_means2D_stride,
+                              const float* g_conic_opacity, int64_t g_conic_stride,
+                              const float* g_colors, int64_t g_colors_stride, float* dL_dmeans3D,
+                              float* dL_dscales, float* dL_drotations, float* dL_dopacity,
+                              float* g_dc, int64_t g_dc_stride, float* g_rest, int64_t g_rest_stride,
+                              int accumulate, void* stream);
+
+/*
+ * Render forward, phase 1 of 2: per-Gaussian tile-touch counts under the
+ * compute_locally mask (bool [grid_y*grid_x], NULL = every tile), and the
+ * device totals {R = tile instances, n_vis = Gaussians with count > 0}
+ * (uint64 [2]).  Replaces the updateTileTouched + scan + blocking readback
+ * of renderForward (submodule/diff-gaussian-rasterization_r/cuda_rasterizer/
+ * rasterizer_impl.cu:602-621); the caller reads the two totals back (one
+ * small device-to-host copy) to size phase 2.
+ */
+int blitz_render_count(int64_t P, int image_height, int image_width, const float* means2D,
+                       const int32_t* radii, const uint8_t* compute_locally, uint32_t* counts,
+                       uint64_t* totals, void* stream);
+
+/* Scratch bytes blitz_render_forward needs for the given totals. */
+size_t blitz_render_scratch_bytes(int64_t P, int64_t n_vis, int64_t R, int image_height,
+                                  int image_width);
+
+/*
+ * Render forward, phase 2 of 2: binning (depth sort + stable tile sort) and
+ * front-to-back alpha blending.
+ * Replaces _C.render_gaussians / RenderGaussiansCUDA
+ * (submodule/diff-gaussian-rasterization_r/rasterize_points.cu:274-361,
+ * rasterizer_impl.cu:556-723, forward.cu:263-413).
+ * State kept for the backward (caller-owned): point_list uint32 [R],
+ * ranges uint32 [n_tiles,2], final_T [H*W], n_contrib uint32 [H*W].
+ * Outputs: out_color [3,H,W] (zero outside compute_locally tiles),
+ * n_render / n_consider / n_contrib_tile int32 [n_tiles], out_observe int32 [P]
+ * (must be zero on entry).
+ */
+int blitz_render_forward(int64_t P, int64_t n_vis, int64_t R, int image_height, int image_width,
+                         const float* means2D, const float* depths, const int32_t* radii,
+                         const float* conic_opacity, const float* rgb, const float* bg,
+                         const uint8_t* compute_locally, const uint32_t* counts, void* scratch,
+                         size_t scratch_bytes, uint32_t* point_list, uint32_t* ranges,
+                         float* final_T, uint32_t* n_contrib, float* out_color, int32_t* n_render,
+                         int32_t* n_consider, int32_t* n_contrib_tile, int32_t* out_observe,
+                         void* stream);
+
+/*
+ * Render backward.
+ * Replaces _C.render_gaussians_backward / RenderGaussiansBackwardCUDA
+ * (submodule/diff-gaussian-rasterization_r/rasterize_points.cu:364-436,
+ * rasterizer_impl.cu:727-804, backward.cu:324-530).
+ * grad_accum: float [P,16], zero on entry; per Gaussian the kernel adds
+ *   [0:2]  dL/dmeans2D (x,y)          [4:6]  sum |dL/dmeans2D| (x,y)
+ *   [8:12] dL/dconic_opacity (c00, c01, c11, opacity)
+ *   [12:15] dL/dcolors (r,g,b); other slots stay zero.
+ * (The c01 entry keeps the reference's convention: half the derivative with
+ * respect to the stored off-diagonal conic entry.)
+ */
+int blitz_render_backward(int64_t P, int image_height, int image_width, const uint32_t* point_list,
+                          const uint32_t* ranges, const float* final_T, const uint32_t* n_contrib,
+                          const float* means2D, const float* conic_opacity, const float* rgb,
+                          const float* bg, const uint8_t* compute_locally, const float* dL_dpix,
+                          float* grad_accum, void* stream);
+
+/*
+ * Fused L1 + SSIM over a band [C,Hb,W] (forward).
+ * Replaces pixelwise_l1_with_mask + pixelwise_ssim_with_mask and their sums
+ * (utils/loss_utils.py:83-124, gaussian_renderer/loss_distribution.py:250-257).
+ * gt: uint8 (divided by 255 and clamped, as the reference does) or fp32;
+ * exactly one of gt_u8 / gt_f32 is non-NULL.  window11: HOST float[11], the
+ * normalised 1D Gaussian window.  sums: device double[2] {sum |img-gt|,
+ * sum SSIM}, zero on entry.  partials: device float [C,Hb,W,3] scratch kept
+ * for the backward.
+ */
+int blitz_loss_forward(int C, int Hb, int W, const float* img, const uint8_t* gt_u8,
+                       const float* gt_f32, const float* window11, float* partials, double* sums,
+                       void* stream);
+
+/* Backward: scale = device float[2] {dL/d(sum L1), dL/d(sum SSIM)};
+ * writes dL_dimg [C,Hb,W]. */
+int blitz_loss_backward(int C, int Hb, int W, const float* img, const uint8_t* gt_u8,
+                        const float* gt_f32, const float* window11, const float* partials,
+                        const float* scale, float* dL_dimg, void* stream);
+
+/*
+ * Routing mask bool [P, mp_world_size]: Gaussian i overlaps the tile-id
+ * interval [dist_global_strategy[r], dist_global_strategy[r+1]) of rank r.
+ * Replaces _C.get_local2j_ids_bool / GetLocal2jIdsBoolCUDA
+ * (submodule/diff-gaussian-rasterization_f/rasterize_points.cu:212-288).
+ */
+int blitz_get_local2j_ids_bool(int image_height, int image_width, int mp_rank, int mp_world_size,
+                               int64_t P, const float* means2D, const int32_t* radii,
+                               const int32_t* dist_global_strategy, int avoid_pixel_all2all,
+                               uint8_t* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BLITZGS_B200_H_ */

@@ -1,0 +1,67 @@
+"""CPU-only checks of the native boundary: the C-ABI library loads, exports
+every entry point include/blitzgs_b200.h declares, and rejects bad arguments
+with a status and a message (no GPU needed: validation precedes any CUDA
+call)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from blitzgs_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_functions():
+    src = open(os.path.join(ROOT, "include", "blitzgs_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(blitz_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_declares_expected_entry_points():
+    fns = header_functions()
+    for n in ("blitz_preprocess_forward", "blitz_preprocess_backward", "blitz_render_count",
+              "blitz_render_forward", "blitz_render_backward", "blitz_loss_forward", "blitz_loss_backward",
+              "blitz_get_local2j_ids_bool", "blitz_render_scratch_bytes", "blitz_last_error", "blitz_version"):
+        assert n in fns
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for n in header_functions():
+        assert hasattr(lib, n), f"{n} declared in include/blitzgs_b200.h but not exported"
+    assert set(header_functions()) <= set(_lib.SIGNATURES), "ctypes signatures missing for some entry points"
+
+
+def test_version_string():
+    assert b"sm_100a" in _lib.load().blitz_version()
+
+
+def test_argument_validation_without_gpu():
+    lib = _lib.load()
+    rc = lib.blitz_render_count(-1, 10, 10, None, None, None, None, None, None)
+    assert rc == 10001
+    assert b"bad arguments" in lib.blitz_last_error()
+    rc = lib.blitz_loss_forward(3, 4, 4, None, None, None, None, None, None, None)
+    assert rc == 10001
+    with pytest.raises(RuntimeError, match="blitz_render_count"):
+        _lib.call("blitz_render_count", -1, 10, 10, None, None, None, None, None, None)
+
+
+def test_scratch_size_query_is_host_only():
+    lib = _lib.load()
+    a = lib.blitz_render_scratch_bytes(1000, 100, 500, 64, 64)
+    b = lib.blitz_render_scratch_bytes(1000, 200, 5000, 64, 64)
+    assert 0 < a < b
+
+
+def test_ops_refuse_cpu_tensors():
+    import torch
+    from blitzgs_b200 import ops, scene as S
+    sc = S.tiny(seed=8, P=16, H=32, W=32)
+    rs = S.raster_settings(sc.cameras[0])
+    shs = torch.cat((sc.features_dc, sc.features_rest), 1)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.preprocess_forward(sc.xyz, torch.exp(sc.scaling), sc.rotation, sc.opacity.reshape(-1),
+                               ops.sh_layout(shs=shs), rs)

@@ -1,0 +1,185 @@
+"""The CPU oracle: internal consistency, and pinned against the reference's
+own outputs (golden vectors produced by running BlitzGS's CUDA rasterizer)."""
+import numpy as np
+import pytest
+import torch
+
+from blitzgs_b200 import scene as S
+from oracle import rasterizer_oracle as O
+from tests.conftest import golden_path
+from tests.golden.make_golden import input_checksum, small_scene
+from tests.helpers import activated, frac_close, normwise_rel, scene_params
+
+
+def _pre(sc, cam):
+    xyz, s, q, shs, o = activated(sc)
+    return O.preprocess_forward(xyz, s, q, shs, o, cam.world_view_transform, cam.full_proj_transform,
+                                cam.camera_center, cam.tanfovx, cam.tanfovy, cam.image_height, cam.image_width, 3)
+
+
+def _diff_render(m2, co, rgb, bg, pl, ranges, H, W):
+    """Autograd-able restatement of the blend with the reference's skip/stop
+    decisions frozen from a no-grad pass and the 0.99 clamp ignored in the
+    gradient (as the reference backward does)."""
+    gx = (W + 15) // 16
+    img = torch.zeros(3, H, W)
+    img = img + bg.view(3, 1, 1) * 0
+    out = []
+    for t in range(ranges.shape[0]):
+        s, e = int(ranges[t][0]), int(ranges[t][1])
+        xs, ys = O._tile_pixels(t, gx, H, W)
+        if e == s or len(xs) == 0:
+            continue
+        ids = torch.as_tensor(pl[s:e])
+        with torch.no_grad():
+            _, _, _, _, alpha0, ok, _ = O._pair_terms(ids, m2.detach(), co.detach(), xs, ys)
+            contrib, _, _, _ = O._transmittance(alpha0, ok)
+        xy = m2[ids]
+        c = co[ids]
+        dx = xy[None, :, 0] - xs[:, None].float()
+        dy = xy[None, :, 1] - ys[:, None].float()
+        power = -0.5 * (c[None, :, 0] * dx * dx + c[None, :, 2] * dy * dy) - c[None, :, 1] * dx * dy
+        a_raw = c[None, :, 3] * torch.exp(power)
+        a = a_raw + (torch.clamp(a_raw, max=0.99) - a_raw).detach()
+        a = torch.where(contrib, a, torch.zeros_like(a))
+        Tc = torch.cumprod(1 - a, 1)
+        Tb = torch.cat([torch.ones(len(xs), 1), Tc[:, :-1]], 1)
+        col = (a * Tb) @ rgb[ids] + Tc[:, -1:] * bg.view(1, 3)
+        out.append((ys, xs, col))
+    for ys, xs, col in out:
+        img = img.index_put((torch.arange(3)[:, None], ys[None, :], xs[None, :]), col.t())
+    return img
+
+
+def test_render_backward_closed_form_matches_autograd():
+    sc = S.tiny(seed=21, P=300, H=48, W=64)
+    cam = sc.cameras[0]
+    pre = _pre(sc, cam)
+    H, W = cam.image_height, cam.image_width
+    pl, ranges, _ = O.binning(pre["means2D"].numpy(), pre["depths"].numpy(), pre["radii"].numpy(), H, W)
+    gen = torch.Generator().manual_seed(0)
+    dpix = torch.randn(3, H, W, generator=gen)
+    rec = O.render_backward(pre["means2D"], pre["conic_opacity"], pre["rgb"], torch.zeros(3), pl, ranges, H, W, dpix)
+    m2 = pre["means2D"].clone().requires_grad_(True)
+    co = pre["conic_opacity"].clone().requires_grad_(True)
+    rgb = pre["rgb"].clone().requires_grad_(True)
+    img = _diff_render(m2, co, rgb, torch.zeros(3), pl, ranges, H, W)
+    fwd = O.render_forward(pre["means2D"], pre["conic_opacity"], pre["rgb"], torch.zeros(3), pl, ranges, H, W)
+    assert torch.allclose(img.detach(), fwd["color"], atol=1e-5)
+    (img * dpix).sum().backward()
+    assert normwise_rel(rec[:, 0], m2.grad[:, 0] * (0.5 * W)) < 1e-4
+    assert normwise_rel(rec[:, 1], m2.grad[:, 1] * (0.5 * H)) < 1e-4
+    assert normwise_rel(rec[:, 8], co.grad[:, 0]) < 1e-4
+    assert normwise_rel(rec[:, 9], 0.5 * co.grad[:, 1]) < 1e-4   # half off-diagonal convention
+    assert normwise_rel(rec[:, 10], co.grad[:, 2]) < 1e-4
+    assert normwise_rel(rec[:, 11], co.grad[:, 3]) < 1e-4
+    assert normwise_rel(rec[:, 12:15], rgb.grad) < 1e-4
+
+
+def test_preprocess_backward_matches_finite_differences():
+    sc = S.tiny(seed=22, P=40, H=64, W=64)
+    cam = sc.cameras[0]
+    xyz, s, q, shs, o = activated(sc)
+    xyz, s, q, shs, o = (t.double().float() for t in (xyz, s, q, shs, o))
+    pre = _pre(sc, cam)
+    gen = torch.Generator().manual_seed(1)
+    gm = torch.randn(40, 2, generator=gen)
+    gc = torch.randn(40, 4, generator=gen)
+    gr = torch.randn(40, 3, generator=gen)
+    args = (cam.world_view_transform, cam.full_proj_transform, cam.camera_center, cam.tanfovx, cam.tanfovy, 64, 64, 3)
+    dm, ds, dq, dsh, dop = O.preprocess_backward(xyz, s, q, shs, o, *args, pre["radii"], gm, gc, gr)
+
+    def L(xyz_, s_, q_, shs_, o_):
+        p = O.preprocess_forward(xyz_, s_, q_, shs_, o_, *args)
+        W = 64
+        ndc = (p["means2D"].double() * 2 + 1) / torch.tensor([W, 64.0]) - 1  # inverse ndc2pix
+        vis = (pre["radii"] > 0).double()[:, None]
+        conic = p["conic_opacity"].double()
+        return float(((ndc * gm.double()) * vis).sum() + (conic[:, :3] * gc[:, :3].double() * torch.tensor([1.0, 2.0, 1.0]) * vis).sum()
+                     + (p["rgb"].double() * gr.double() * vis).sum() + (p["conic_opacity"][:, 3].double() * gc[:, 3].double()).sum())
+
+    eps = 1e-3
+    for (name, t, g) in (("scale", s, ds), ("xyz", xyz, dm)):
+        for i in range(0, 40, 7):
+            if pre["radii"][i] == 0:
+                continue
+            for k in range(3):
+                tp = t.clone()
+                tp[i, k] += eps
+                tm = t.clone()
+                tm[i, k] -= eps
+                a = [xyz, s, q, shs, o]
+                idx = 1 if name == "scale" else 0
+                a[idx] = tp
+                lp = L(*a)
+                a[idx] = tm
+                lm = L(*a)
+                fd = (lp - lm) / (2 * eps)
+                assert abs(fd - g[i, k].item()) <= 2e-2 * max(1.0, abs(fd)), (name, i, k, fd, g[i, k].item())
+
+
+def test_route_restatement_semantics():
+    m2 = np.array([[8.0, 8.0], [8.0, 40.0], [100.0, 100.0]], np.float32)
+    r = np.array([3, 3, 0], np.int64)
+    out = O.route_bool(m2, r, 64, 64, [0, 8, 16])   # 4x4 tiles; ranks own 2 rows each
+    assert out[0].tolist() == [True, False]
+    assert out[1].tolist() == [False, True]
+    assert out[2].tolist() == [False, False]
+
+
+# ---- pinned against the reference (golden vectors) ----
+
+def _golden(name):
+    p = golden_path(name)
+    if p is None:
+        pytest.skip(f"{name} not generated yet")
+    return dict(np.load(p))
+
+
+def test_oracle_binning_equals_reference():
+    g = _golden("golden_tiny.npz")
+    pl, ranges, _ = O.binning(g["means2D"], g["depths"], g["radii"], 256, 256)
+    assert np.array_equal(pl, g["point_list"].astype(np.int64))
+    assert np.array_equal(ranges, g["ranges"].astype(np.int64))
+
+
+def test_oracle_routing_equals_reference():
+    g = _golden("golden_tiny.npz")
+    ref = np.unpackbits(g["route_packed"])[: int(np.prod(g["route_shape"]))].reshape(g["route_shape"]).astype(bool)
+    out = O.route_bool(g["means2D"], g["radii"], 256, 256, np.array([0, 4, 8, 12, 16]) * 16)
+    assert np.array_equal(out, ref)
+
+
+def test_oracle_preprocess_close_to_reference():
+    g = _golden("golden_tiny.npz")
+    sc = S.tiny()
+    assert str(g["input_sha256"]) == input_checksum(sc)
+    p = _pre(sc, sc.cameras[0])
+    assert (p["radii"].numpy() != g["radii"]).mean() <= 2e-3
+    both = (p["radii"].numpy() > 0) & (g["radii"] > 0)
+    assert np.abs(p["means2D"].numpy()[both] - g["means2D"][both]).max() < 2e-3
+
+
+def test_oracle_render_close_to_reference():
+    g = _golden("golden_small.npz")
+    sc = small_scene()
+    cam = sc.cameras[0]
+    H, W = cam.image_height, cam.image_width
+    f = O.render_forward(torch.from_numpy(g["means2D"]), torch.from_numpy(g["conic_opacity"]),
+                         torch.from_numpy(g["rgb"]), torch.zeros(3), g["point_list"].astype(np.int64),
+                         g["ranges"].astype(np.int64), H, W)
+    assert frac_close(f["color"].numpy(), g["image"], 1e-5) > 0.999
+    assert frac_close(f["n_contrib"].numpy(), g["n_contrib"], 0) > 0.999
+
+
+def test_oracle_gradients_close_to_reference():
+    g = _golden("golden_small.npz")
+    sc = small_scene()
+    cam = sc.cameras[0]
+    gt = S.target_image(1, cam.image_height, cam.image_width)
+    out = O.train_step(scene_params(sc), cam, gt)
+    assert abs(out["loss"].item() - float(g["loss"])) < 1e-4
+    rec = out["rec"]
+    assert normwise_rel(rec[:, 12:15], g["g_rgb"]) < 5e-3
+    assert normwise_rel(rec[:, 8:12], g["g_conic_opacity"]) < 5e-3
+    assert normwise_rel(rec[:, 0:2], g["g_means2D"]) < 5e-3
