@@ -66,13 +66,17 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.lines = []
+        self.marks = []
         self.thread = None
+
+    def mark(self):
+        self.marks.append(len(self.lines))
 
     def start(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (FileNotFoundError, OSError):
             self.proc = None
             return
@@ -95,7 +99,10 @@ class ClockSampler:
             self.thread.join(timeout=2)
         sms, maxs, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        lines = self.lines
+        if len(self.marks) >= 2 and self.marks[1] > self.marks[0]:
+            lines = self.lines[self.marks[0]:self.marks[1]]
+        for ln in lines:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -157,47 +164,81 @@ def build_workload(args, device, rank=0, ws=1):
 def run_ours(args, ws, rank, local):
     from blitzgs_b200 import ops, step as ST
     from blitzgs_b200 import scene as S
+    from blitzgs_b200 import distributed as D
+    from blitzgs_b200 import dist_step as DS
     dev = torch.device("cuda", local)
     sc, gts_cpu = build_workload(args, dev, rank, ws)
-    model = [t.to(dev).requires_grad_(True) for t in (sc.xyz, sc.scaling, sc.rotation, sc.opacity,
-                                                      sc.features_dc, sc.features_rest)]
     cams = [c.to(dev) for c in sc.cameras]
+    H, W = cams[0].image_height, cams[0].image_width
+    if ws > 1:
+        shard = D.zorder_shards(sc.xyz, ws)[rank]
+        params = [t[shard] for t in (sc.xyz, sc.scaling, sc.rotation, sc.opacity, sc.features_dc, sc.features_rest)]
+        D.init_context(rank, ws, H, W, group=None, bsz=args.bsz * ws)
+    else:
+        params = [sc.xyz, sc.scaling, sc.rotation, sc.opacity, sc.features_dc, sc.features_rest]
+    model = [t.contiguous().to(dev).requires_grad_(True) for t in params]
     rasters = [S.raster_settings(c, device=dev) for c in cams]
     gts_dev = [g.to(dev) for g in gts_cpu]
     gts_pin = [g.pin_memory() for g in gts_cpu]
-    H, W = cams[0].image_height, cams[0].image_width
     bsz = args.bsz
     n_cams = len(cams)
-    offset = rank * bsz
+    history = D.DivisionStrategyHistoryFinal(cams, ws, rank) if ws > 1 else None
+    h2d = [0]
+
+    def batch_ids(it):
+        return [((it * bsz * ws) + k) % n_cams for k in range(bsz * ws)]
 
     def one_step(it, e2e):
         for p in model:
             p.grad = None
-        total = None
-        for k in range(bsz):
-            ci = (offset + (it * bsz * ws) + k) % n_cams
-            if e2e:
-                gt = torch.empty((3, H, W), dtype=torch.uint8, device=dev)
-                gt.copy_(gts_pin[ci], non_blocking=True)
-            else:
-                gt = gts_dev[ci]
-            loss, *_ = ST.view_loss(model, rasters[ci], gt)
-            total = loss if total is None else total + loss
+        if ws == 1:
+            total = None
+            for ci in batch_ids(it):
+                if e2e:
+                    gt = torch.empty((3, H, W), dtype=torch.uint8, device=dev)
+                    gt.copy_(gts_pin[ci], non_blocking=True)
+                    h2d[0] = 3 * H * W * bsz
+                else:
+                    gt = gts_dev[ci]
+                loss, *_ = ST.view_loss(model, rasters[ci], gt)
+                total = loss if total is None else total + loss
+        else:
+            ids = batch_ids(it)
+            bcams = [cams[c] for c in ids]
+            strategies, _ = D.start_strategy_final(bcams, history)
+            gts = []
+            nbytes = 0
+            for k, c in enumerate(ids):
+                rr = strategies[k].row_range(rank)
+                if rr is None:
+                    gts.append(None)
+                    continue
+                y0, y1 = rr[0] * 16, min(H, rr[1] * 16)
+                if e2e:
+                    band = torch.empty((3, y1 - y0, W), dtype=torch.uint8, device=dev)
+                    band.copy_(gts_pin[c][:, y0:y1], non_blocking=True)
+                    nbytes += band.numel()
+                else:
+                    band = gts_dev[c][:, y0:y1]
+                gts.append(band)
+            h2d[0] = max(h2d[0], nbytes)
+            total = DS.batch_loss(model, [rasters[c] for c in ids], gts, strategies)
         total.backward()
         if e2e:
             return total.detach().to("cpu", non_blocking=False)
         return None
 
-    # warm-up (also sizes the binning scratch)
+    clocks = ClockSampler(local)
+    clocks.start()  # started before warm-up so its start-up cost never lands in the timed region
     for it in range(args.warmup):
         one_step(it, False)
     torch.cuda.synchronize()
+    time.sleep(0.2)
 
     # timed: device-resident inputs
-    clocks = ClockSampler(torch.cuda.current_device() if ws == 1 else local)
     barrier(ws)
     torch.cuda.synchronize()
-    clocks.start()
+    clocks.mark()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record()
@@ -205,8 +246,8 @@ def run_ours(args, ws, rank, local):
         one_step(args.warmup + it, False)
     t1.record()
     torch.cuda.synchronize()
+    clocks.mark()
     barrier(ws)
-    clk = clocks.stop()
     ms = max_over_ranks(t0.elapsed_time(t1), ws)
 
     # timed: end to end (GT uploaded from pinned host memory, loss read back)
@@ -220,6 +261,7 @@ def run_ours(args, ws, rank, local):
     e1.record()
     torch.cuda.synchronize()
     barrier(ws)
+    clk = clocks.stop()
     ms_e2e = max_over_ranks(e0.elapsed_time(e1), ws)
 
     # stage timing pass (events around each native call) for the roofline
@@ -230,8 +272,9 @@ def run_ours(args, ws, rank, local):
     torch.cuda.synchronize()
     stages = ops.TIMER.summary()
     ops.TIMER.enabled = False
+    n_stage_steps = min(args.steps, 3)
     return dict(ms=ms, ms_e2e=ms_e2e, clocks=clk, stages=stages, H=H, W=W, P=sc.P, bsz=bsz,
-                h2d=3 * H * W * bsz, d2h=4)
+                h2d=h2d[0], d2h=4, n_stage_steps=n_stage_steps)
 
 
 def roofline_from_stages(stages, peaks, peak_kind):
@@ -388,11 +431,13 @@ def run_reference(args):
         if e2e:
             return total.detach().cpu()
 
+    clocks = ClockSampler(0)
+    clocks.start()
     for it in range(args.warmup):
         one_step(it, False)
     torch.cuda.synchronize()
-    clocks = ClockSampler(0)
-    clocks.start()
+    time.sleep(0.2)
+    clocks.mark()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record()
@@ -400,7 +445,7 @@ def run_reference(args):
         one_step(args.warmup + it, False)
     t1.record()
     torch.cuda.synchronize()
-    clk = clocks.stop()
+    clocks.mark()
     ms = t0.elapsed_time(t1)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
@@ -409,6 +454,7 @@ def run_reference(args):
         one_step(args.warmup + args.steps + it, True)
     e1.record()
     torch.cuda.synchronize()
+    clk = clocks.stop()
     ms_e2e = e0.elapsed_time(e1)
     return dict(ms=ms, ms_e2e=ms_e2e, clocks=clk, H=H, W=W, P=sc.P)
 

@@ -74,6 +74,8 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
       p.out_color[pix] = 0.f;
       p.out_color[HW + pix] = 0.f;
       p.out_color[2 * HW + pix] = 0.f;
+      p.final_T[pix] = 1.f;
+      p.n_contrib[pix] = 0u;
     }
     if (threadIdx.x == 0) {
       p.n_render[tile] = 0;

@@ -73,7 +73,6 @@ __global__ void __launch_bounds__(256) preprocess_fwd_kernel(PreprocessParams p)
   const float3 p_orig = make_float3(__ldg(p.means3D + 3 * i + 0), __ldg(p.means3D + 3 * i + 1),
                                     __ldg(p.means3D + 3 * i + 2));
 
-  bool visible = false;
   float2 point_image = make_float2(0.f, 0.f);
   float depth = 0.f;
   int radius = 0;
@@ -125,14 +124,12 @@ __global__ void __launch_bounds__(256) preprocess_fwd_kernel(PreprocessParams p)
     load_sh(p, i, p.M, s);
     rgb = sh_to_rgb(p.D, p_orig, p.campos, s.dc, s.rest, clamp3);
 
-    visible = true;
     depth = p_view.z;
     radius = (int)ceilf(my_radius);
     point_image = pimg;
     conic_op = make_float4(conic.x, conic.y, conic.z, opacity);
   } while (0);
 
-  (void)visible;
   reinterpret_cast<float2*>(p.out_means2D)[i] = point_image;
   p.out_depths[i] = depth;
   p.out_radii[i] = radius;
@@ -174,33 +171,27 @@ __device__ __forceinline__ void put(float* dst, float v) {
     *dst = v;
 }
 
-template <bool ACC>
-__global__ void __launch_bounds__(256) preprocess_bwd_kernel(PreprocessBwdParams p) {
-  const PreprocessParams& f = p.f;
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= f.P) return;
+// Per-Gaussian backward results, held in registers until the block stores them.
+struct BwdOut {
+  float mean[3];
+  float scale[3];
+  float4 rot;
+  float dc[3];
+  float rest[45];
+};
 
-  float* g_mean = p.g_means3D + 3 * i;
-  float* g_scale = p.g_scales + 3 * i;
-  float* g_rot = p.g_rotations + 4 * i;
-  float* g_dc = p.g_dc + i * p.g_dc_stride;
-  float* g_rest = p.g_rest + i * p.g_rest_stride;
-
-  const float4 gco = *reinterpret_cast<const float4*>(p.g_conic_opacity + i * p.g_conic_stride);
-  if (p.g_opacities) put<ACC>(p.g_opacities + i, gco.w);
-
-  if (!(__ldg(p.radii + i) > 0)) {
-    if (!ACC) {
-      g_mean[0] = g_mean[1] = g_mean[2] = 0.f;
-      g_scale[0] = g_scale[1] = g_scale[2] = 0.f;
-      *reinterpret_cast<float4*>(g_rot) = make_float4(0.f, 0.f, 0.f, 0.f);
-      g_dc[0] = g_dc[1] = g_dc[2] = 0.f;
+__device__ __forceinline__ void bwd_zero(BwdOut& o) {
 #pragma unroll
-      for (int k = 0; k < 45; ++k)
-        if (k < f.M * 3) g_rest[k] = 0.f;
-    }
-    return;
-  }
+  for (int k = 0; k < 3; ++k) o.mean[k] = o.scale[k] = o.dc[k] = 0.f;
+  o.rot = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int k = 0; k < 45; ++k) o.rest[k] = 0.f;
+}
+
+// Gradients of one visible Gaussian (radius > 0) given its upstream
+// gradients gco (conic00, conic01, conic11, opacity).
+__device__ __forceinline__ void bwd_compute(const PreprocessBwdParams& p, int64_t i, float4 gco, BwdOut& out) {
+  const PreprocessParams& f = p.f;
 
   float Vs[16], Ps[16];
 #pragma unroll
@@ -310,7 +301,7 @@ __global__ void __launch_bounds__(256) preprocess_bwd_kernel(PreprocessBwdParams
     for (int k = 0; k < 45; ++k) dsh[k] = 0.f;
     float ddx[3] = {0.f, 0.f, 0.f}, ddy[3] = {0.f, 0.f, 0.f}, ddz[3] = {0.f, 0.f, 0.f};
 #pragma unroll
-    for (int ch = 0; ch < 3; ++ch) put<ACC>(g_dc + ch, kSH0 * dR[ch]);
+    for (int ch = 0; ch < 3; ++ch) out.dc[ch] = kSH0 * dR[ch];
     if (D > 0) {
       const float b1 = -kSH1 * y, b2 = kSH1 * z, b3 = -kSH1 * x;
 #pragma unroll
@@ -375,8 +366,7 @@ __global__ void __launch_bounds__(256) preprocess_bwd_kernel(PreprocessBwdParams
       }
     }
     #pragma unroll
-    for (int k = 0; k < 45; ++k)
-      if (k < f.M * 3) put<ACC>(g_rest + k, dsh[k]);
+    for (int k = 0; k < 45; ++k) out.rest[k] = (k < f.M * 3) ? dsh[k] : 0.f;
     const float3 ddir = make_float3(ddx[0] * dR[0] + ddx[1] * dR[1] + ddx[2] * dR[2],
                                     ddy[0] * dR[0] + ddy[1] * dR[1] + ddy[2] * dR[2],
                                     ddz[0] * dR[0] + ddz[1] * dR[1] + ddz[2] * dR[2]);
@@ -385,9 +375,9 @@ __global__ void __launch_bounds__(256) preprocess_bwd_kernel(PreprocessBwdParams
     dmean.y += dm.y;
     dmean.z += dm.z;
   }
-  put<ACC>(g_mean + 0, dmean.x);
-  put<ACC>(g_mean + 1, dmean.y);
-  put<ACC>(g_mean + 2, dmean.z);
+  out.mean[0] = dmean.x;
+  out.mean[1] = dmean.y;
+  out.mean[2] = dmean.z;
 
   // ---- scale / rotation part (reference backward.cu:280-343) ----
   {
@@ -411,9 +401,9 @@ __global__ void __launch_bounds__(256) preprocess_bwd_kernel(PreprocessBwdParams
     M3 dM = m3_mul(twoM, dSig);
     M3 Rt = m3_t(R);
     M3 dMt = m3_t(dM);
-    put<ACC>(g_scale + 0, Rt[0][0] * dMt[0][0] + Rt[0][1] * dMt[0][1] + Rt[0][2] * dMt[0][2]);
-    put<ACC>(g_scale + 1, Rt[1][0] * dMt[1][0] + Rt[1][1] * dMt[1][1] + Rt[1][2] * dMt[1][2]);
-    put<ACC>(g_scale + 2, Rt[2][0] * dMt[2][0] + Rt[2][1] * dMt[2][1] + Rt[2][2] * dMt[2][2]);
+    out.scale[0] = Rt[0][0] * dMt[0][0] + Rt[0][1] * dMt[0][1] + Rt[0][2] * dMt[0][2];
+    out.scale[1] = Rt[1][0] * dMt[1][0] + Rt[1][1] * dMt[1][1] + Rt[1][2] * dMt[1][2];
+    out.scale[2] = Rt[2][0] * dMt[2][0] + Rt[2][1] * dMt[2][1] + Rt[2][2] * dMt[2][2];
 #pragma unroll
     for (int rr = 0; rr < 3; ++rr) {
       dMt.m[0][rr] *= s0;
@@ -428,16 +418,88 @@ __global__ void __launch_bounds__(256) preprocess_bwd_kernel(PreprocessBwdParams
            4 * y * (dMt[2][2] + dMt[0][0]);
     dq.w = 2 * r * (dMt[0][1] - dMt[1][0]) + 2 * x * (dMt[2][0] + dMt[0][2]) + 2 * y * (dMt[1][2] + dMt[2][1]) -
            4 * z * (dMt[1][1] + dMt[0][0]);
+    out.rot = dq;
+  }
+}
+
+constexpr int kBwdBlock = 128;
+
+// Store one W-float row per thread of the block into the contiguous rows
+// [base, base+n) of dst, staged through shared memory (odd pitch: no bank
+// conflicts) so every warp store covers consecutive addresses.
+template <int W, bool ACC>
+__device__ __forceinline__ void store_rows(float* __restrict__ dst, int n, const float* row, float* stage) {
+  constexpr int PITCH = W | 1;
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < W; ++k) stage[threadIdx.x * PITCH + k] = row[k];
+  __syncthreads();
+  for (int e = threadIdx.x; e < n * W; e += kBwdBlock) {
+    const int r = e / W, c = e - r * W;
+    const float v = stage[r * PITCH + c];
+    if (ACC)
+      dst[e] += v;
+    else
+      dst[e] = v;
+  }
+}
+
+template <bool ACC>
+__global__ void __launch_bounds__(kBwdBlock) preprocess_bwd_kernel(PreprocessBwdParams p) {
+  __shared__ float stage[kBwdBlock * 49];
+  const PreprocessParams& f = p.f;
+  const int64_t base = (int64_t)blockIdx.x * kBwdBlock;
+  const int64_t i = base + threadIdx.x;
+  const int n = (int)((f.P - base) < kBwdBlock ? (f.P - base) : kBwdBlock);
+  const bool valid = i < f.P;
+
+  float4 gco = make_float4(0.f, 0.f, 0.f, 0.f);
+  bool vis = false;
+  if (valid) {
+    gco = *reinterpret_cast<const float4*>(p.g_conic_opacity + i * p.g_conic_stride);
+    if (p.g_opacities) put<ACC>(p.g_opacities + i, gco.w);
+    vis = __ldg(p.radii + i) > 0;
+  }
+  if (ACC && !__syncthreads_or(vis)) return;  // nothing to add in this block
+
+  BwdOut o;
+  bwd_zero(o);
+  if (vis) bwd_compute(p, i, gco, o);
+
+  if (valid) {
+    float4* r = reinterpret_cast<float4*>(p.g_rotations) + i;
     if (ACC) {
-      float4 o = *reinterpret_cast<float4*>(g_rot);
-      o.x += dq.x;
-      o.y += dq.y;
-      o.z += dq.z;
-      o.w += dq.w;
-      *reinterpret_cast<float4*>(g_rot) = o;
+      float4 a = *r;
+      a.x += o.rot.x;
+      a.y += o.rot.y;
+      a.z += o.rot.z;
+      a.w += o.rot.w;
+      *r = a;
     } else {
-      *reinterpret_cast<float4*>(g_rot) = dq;
+      *r = o.rot;
     }
+  }
+  store_rows<3, ACC>(p.g_means3D + 3 * base, n, o.mean, stage);
+  store_rows<3, ACC>(p.g_scales + 3 * base, n, o.scale, stage);
+  const bool packed = p.g_dc_stride == 48 && p.g_rest_stride == 48 && p.g_rest == p.g_dc + 3 && f.M == 15;
+  if (packed) {
+    float row[48];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) row[k] = o.dc[k];
+#pragma unroll
+    for (int k = 0; k < 45; ++k) row[3 + k] = o.rest[k];
+    store_rows<48, ACC>(p.g_dc + 48 * base, n, row, stage);
+  } else if (p.g_dc_stride == 3 && p.g_rest_stride == 45 && f.M == 15) {
+    store_rows<3, ACC>(p.g_dc + 3 * base, n, o.dc, stage);
+    store_rows<45, ACC>(p.g_rest + 45 * base, n, o.rest, stage);
+  } else if (valid) {
+    float* gd = p.g_dc + i * p.g_dc_stride;
+    float* gr = p.g_rest + i * p.g_rest_stride;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) put<ACC>(gd + k, o.dc[k]);
+#pragma unroll
+    for (int k = 0; k < 45; ++k)
+      if (k < f.M * 3) put<ACC>(gr + k, o.rest[k]);
   }
 }
 
@@ -451,7 +513,7 @@ int launch_preprocess_fwd(const PreprocessParams& p, cudaStream_t st) {
 
 int launch_preprocess_bwd(const PreprocessBwdParams& p, bool accumulate, cudaStream_t st) {
   if (p.f.P <= 0) return 0;
-  const int threads = 256;
+  const int threads = kBwdBlock;
   const int64_t blocks = (p.f.P + threads - 1) / threads;
   if (accumulate)
     preprocess_bwd_kernel<true><<<(unsigned)blocks, threads, 0, st>>>(p);

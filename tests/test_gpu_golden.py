@@ -37,7 +37,15 @@ def _run(sc, cam, dev, compute_locally=None):
                 n_consider=nc, n_contrib_tile=nct, out_observe=obs, state=st, rs=rs)
 
 
-def _check_forward(g, o, prefix=""):
+def _local_pixel_mask(H, W, band_rows=None):
+    m = np.ones((H, W), bool)
+    if band_rows is not None:
+        m[:] = False
+        m[band_rows[0] * 16: min(H, band_rows[1] * 16)] = True
+    return m.reshape(-1)
+
+
+def _check_forward(g, o, prefix="", band_rows=None):
     assert np.array_equal(o["radii"].cpu().numpy(), g[prefix + "radii"]), "radii differ from the reference"
     assert np.array_equal(o["means2D"].cpu().numpy().view(np.uint32), g[prefix + "means2D"].view(np.uint32))
     assert np.array_equal(o["depths"].cpu().numpy().view(np.uint32), g[prefix + "depths"].view(np.uint32))
@@ -46,7 +54,11 @@ def _check_forward(g, o, prefix=""):
     assert st.R == R
     assert np.array_equal(st.point_list[:R].cpu().numpy().view(np.uint32), g[prefix + "point_list"])
     assert np.array_equal(st.ranges.cpu().numpy().view(np.uint32), g[prefix + "ranges"])
-    assert np.array_equal(st.n_contrib.cpu().numpy().astype(np.int64), g[prefix + "n_contrib"].astype(np.int64))
+    H, W = o["image"].shape[1], o["image"].shape[2]
+    loc = _local_pixel_mask(H, W, band_rows)
+    assert np.array_equal(st.n_contrib.cpu().numpy().astype(np.int64)[loc], g[prefix + "n_contrib"].astype(np.int64)[loc])
+    if prefix + "final_T" in g:
+        assert np.array_equal(st.final_T.cpu().numpy().view(np.uint32)[loc], g[prefix + "final_T"].view(np.uint32)[loc])
     for k in ("n_render", "n_consider", "n_contrib_tile", "out_observe"):
         assert np.array_equal(o[k].cpu().numpy(), g[prefix + k]), k
     err = np.abs(o["image"].cpu().numpy() - g[prefix + "image"]).max()
@@ -88,7 +100,7 @@ def test_tiny_loss_and_gradient_norms(cuda_device):
     m2, rgb, co, radii, depths = rast.preprocess_gaussians(*acts[:4], acts[4], {"stats_collector": {}})
     H, W = cam.image_height, cam.image_width
     cl = torch.ones((16, 16), dtype=torch.bool, device=cuda_device)
-    color, *_ = rast.render_gaussians(m2, torch.zeros_like(xyz) + 0, co, rgb, torch.zeros((xyz.shape[0], 5),
+    color, *_ = rast.render_gaussians(m2, torch.zeros_like(xyz, requires_grad=True) + 0, co, rgb, torch.zeros((xyz.shape[0], 5),
                                       device=cuda_device), depths, radii, cl, None, {})
     from blitzgs_b200.loss import band_loss
     l1, ss = band_loss(color, gt)
@@ -121,7 +133,7 @@ def test_small_edge_cases_full(cuda_device):
     r0, r1 = g["band_rows"]
     band[r0:r1] = True
     ob = _run(sc, cam, cuda_device, compute_locally=band)
-    _check_forward(g, ob, "band_")
+    _check_forward(g, ob, "band_", band_rows=(r0, r1))
 
 
 def test_small_gradients(cuda_device):
@@ -141,7 +153,7 @@ def test_small_gradients(cuda_device):
     co.retain_grad()
     H, W = cam.image_height, cam.image_width
     cl = torch.ones(((H + 15) // 16, (W + 15) // 16), dtype=torch.bool, device=cuda_device)
-    abs_pts = torch.zeros_like(acts[0]) + 0
+    abs_pts = torch.zeros_like(acts[0], requires_grad=True) + 0
     abs_pts.retain_grad()
     color, *_ = rast.render_gaussians(m2, abs_pts, co, rgb, torch.zeros((xyz.shape[0], 5), device=cuda_device),
                                       depths, radii, cl, None, {})

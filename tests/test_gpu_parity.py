@@ -169,7 +169,8 @@ def test_drop_in_api_autograd_matches_fused(cuda_device):
     m2.retain_grad()
     H, W = cam.image_height, cam.image_width
     cl = torch.ones(((H + 15) // 16, (W + 15) // 16), dtype=torch.bool, device=cuda_device)
-    abs_pts = torch.zeros_like(xyz) + 0
+    abs_pts = torch.zeros_like(xyz, requires_grad=True) + 0
+    abs_pts.retain_grad()
     color, nr, nc, nct, obs, _, _ = rast.render_gaussians(m2, abs_pts, co, rgb, torch.zeros((xyz.shape[0], 5),
                                                           device=cuda_device), depths, radii, cl, None, ca)
     sums, _ = O.band_loss_sums(color.cpu(), gt.cpu())
