@@ -230,9 +230,14 @@ def run_ours(args, ws, rank, local):
 
     clocks = ClockSampler(local)
     clocks.start()  # started before warm-up so its start-up cost never lands in the timed region
-    for it in range(args.warmup):
-        one_step(it, False)
+    # Warm-up visits every camera of the timed sequence (at least W steps), so
+    # buffer growth of the allocator and of the binning scratch never lands in
+    # the timed region.
+    n_warm = max(args.warmup, args.steps)
+    for it in range(n_warm):
+        one_step(args.warmup + (it % args.steps), False)
     torch.cuda.synchronize()
+    args.warmup_done = n_warm
     time.sleep(0.2)
 
     # timed: device-resident inputs
@@ -257,7 +262,7 @@ def run_ours(args, ws, rank, local):
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
     for it in range(args.steps):
-        one_step(args.warmup + args.steps + it, True)
+        one_step(args.warmup + it, True)
     e1.record()
     torch.cuda.synchronize()
     barrier(ws)
@@ -277,32 +282,70 @@ def run_ours(args, ws, rank, local):
                 h2d=h2d[0], d2h=4, n_stage_steps=n_stage_steps)
 
 
-def roofline_from_stages(stages, peaks, peak_kind):
-    """Dominant native stage by time; algorithmic bytes per launch (DESIGN.md
-    lists the per-unit figures) divided by its mean event-timed duration."""
+def stage_bytes(name, metas):
+    """Algorithmic (minimum) DRAM bytes of one native stage, summed over its
+    launches.  P = Gaussians processed, V = Gaussians that touch a rendered
+    tile (n_vis of the same view).
+      preprocess_fwd: every Gaussian reads xyz (12) and writes its 44 output
+        bytes; visible ones also read scale 12, rotation 16, opacity 4, SH 192.
+      preprocess_bwd: every Gaussian reads its radius (4) and writes its 236
+        gradient bytes; visible ones also read their parameters (236) and
+        upstream gradients (36)."""
+    tot = 0.0
+    for m in metas:
+        P, V = m.get("P", 0), m.get("n_vis", 0)
+        if name == "preprocess_fwd":
+            tot += 56.0 * P + 224.0 * V
+        elif name == "preprocess_bwd":
+            tot += 240.0 * P + 272.0 * V
+        else:
+            return None
+    return tot
+
+
+def roofline_from_stages(stages, peaks, peak_kind, n_vis_per_call, fp32_peak=None):
+    """Dominant native stage by time.  HBM-bound stages: algorithmic bytes per
+    launch / mean event-timed duration vs the measured copy bandwidth.  The
+    blend stages are FP32-issue bound: algorithmic FLOPs from the per-pair
+    model (forward 10 FLOP per evaluated pair + 13 per contributing pair,
+    backward 70 FLOP per replayed pair; pairs counted by the kernels' own
+    per-tile counters) vs the FP32 FMA throughput measured in this run."""
     if not stages:
         return None, {}
     per = {k: (v[0], v[1]) for k, v in stages.items()}
     dom = max(per, key=lambda k: per[k][1])
     calls, tot = per[dom]
-    metas = stages[dom][2]
-    hbm = peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"])
-    if dom == "preprocess_fwd":
-        byts = sum(280.0 * m["P"] for m in metas)
-        bound = "hbm"
-    elif dom == "preprocess_bwd":
-        byts = sum(520.0 * m["P"] for m in metas)
-        bound = "hbm"
-    else:
-        byts = None
-        bound = "fp32"
     table = {k: {"calls": v[0], "ms_total": round(v[1], 4)} for k, v in per.items()}
+    metas = [dict(m, n_vis=n_vis_per_call[i % len(n_vis_per_call)]) for i, m in enumerate(stages[dom][2])]
+    hbm = peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"])
+    if dom in ("blend_fwd", "blend_bwd"):
+        flops = 0.0
+        for m in metas:
+            pr = [int(x) for x in m["pairs"]]
+            flops += (10.0 * pr[0] + 13.0 * pr[1]) if dom == "blend_fwd" else 70.0 * pr[0]
+        tf = flops / (tot / 1e3) / 1e12
+        return {"kernel": dom, "bound": "fp32", "achieved": round(tf, 3), "peak": round(fp32_peak, 2) if fp32_peak else None,
+                "unit": "TFLOP/s", "frac": round(tf / fp32_peak, 4) if fp32_peak else None, "traffic": None,
+                "peak_source": "measured in this run (FP32 FMA probe, blitz_fp32_probe)",
+                "flops_per_launch": round(flops / calls), "ms_per_launch": round(tot / calls, 4)}, table
+    byts = stage_bytes(dom, metas)
     if byts is None:
-        return {"kernel": dom, "bound": bound, "achieved": None, "peak": None, "unit": None, "frac": None,
-                "traffic": None, "note": "dominant stage is FP32/MUFU-bound; see profiles/"}, table
+        return {"kernel": dom, "bound": None, "achieved": None, "peak": None, "unit": None, "frac": None,
+                "traffic": None}, table
     gbs = byts / (tot / 1e3) / 1e9
-    return {"kernel": dom, "bound": bound, "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
-            "frac": round(gbs / hbm, 4), "traffic": None, "peak_source": peak_kind}, table
+    return {"kernel": dom, "bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+            "frac": round(gbs / hbm, 4), "traffic": None, "peak_source": peak_kind,
+            "bytes_per_launch": round(byts / calls), "ms_per_launch": round(tot / calls, 4)}, table
+
+
+def hbm_roofline(stages, peaks, peak_kind, n_vis_per_call):
+    """The same arithmetic for the slowest HBM-bound stage (preprocess)."""
+    cands = [k for k in ("preprocess_fwd", "preprocess_bwd") if k in stages]
+    if not cands:
+        return None
+    sub = {k: stages[k] for k in cands}
+    r, _ = roofline_from_stages(sub, peaks, peak_kind, n_vis_per_call)
+    return r
 
 
 def cpu_baseline_sample(budget_s=20.0):
@@ -433,9 +476,11 @@ def run_reference(args):
 
     clocks = ClockSampler(0)
     clocks.start()
-    for it in range(args.warmup):
-        one_step(it, False)
+    n_warm = max(args.warmup, args.steps)
+    for it in range(n_warm):
+        one_step(args.warmup + (it % args.steps), False)
     torch.cuda.synchronize()
+    args.warmup_done = n_warm
     time.sleep(0.2)
     clocks.mark()
     t0 = torch.cuda.Event(enable_timing=True)
@@ -451,10 +496,21 @@ def run_reference(args):
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
     for it in range(args.steps):
-        one_step(args.warmup + args.steps + it, True)
+        one_step(args.warmup + it, True)
     e1.record()
     torch.cuda.synchronize()
     clk = clocks.stop()
+    # per-step device times (diagnostic, stderr)
+    per = []
+    for it in range(args.steps):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        one_step(args.warmup + it, False)
+        b.record()
+        torch.cuda.synchronize()
+        per.append(round(a.elapsed_time(b), 2))
+    log("reference per-step ms:", per)
     ms_e2e = e0.elapsed_time(e1)
     return dict(ms=ms, ms_e2e=ms_e2e, clocks=clk, H=H, W=W, P=sc.P)
 
@@ -496,7 +552,8 @@ def main():
         e2e = views / (r["ms_e2e"] / 1e3)
         cfg.update(gaussians=r["P"], image=f"{r['W']}x{r['H']}")
         line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": 1,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms"] / args.steps, 3),
+                "steps": args.steps, "warmup": getattr(args, "warmup_done", args.warmup),
+                "ms_per_step": round(r["ms"] / args.steps, 3),
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic", "config": cfg, "clocks": r["clocks"],
                 "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": torch.get_num_threads(),
@@ -512,7 +569,11 @@ def main():
     value = views / (r["ms"] / 1e3)
     e2e = views / (r["ms_e2e"] / 1e3)
     peaks, pk = load_peaks()
-    roof, stage_table = roofline_from_stages(r["stages"], peaks, pk)
+    nv = [m.get("n_vis", 0) for m in r["stages"].get("blend_fwd", (0, 0, []))[2]] or [0]
+    from blitzgs_b200 import ops as _ops
+    fp32 = _ops.fp32_peak_tflops()
+    roof, stage_table = roofline_from_stages(r["stages"], peaks, pk, nv, fp32)
+    roof_hbm = hbm_roofline(r["stages"], peaks, pk, nv)
     cb = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         try:
@@ -524,9 +585,10 @@ def main():
     # preprocess bwd 1); the binning figure counts the cub launches seen in the ncu launch list
     launches_per_view = 1 + 1 + KERNELS_RENDER_FWD + 2 + 1 + 1
     line = {"metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(r["ms"] / args.steps, 3), "higher_is_better": True,
+            "warmup": getattr(args, "warmup_done", args.warmup), "ms_per_step": round(r["ms"] / args.steps, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
-            "clocks": r["clocks"], "roofline": roof, "stages_ms": stage_table, "cpu_baseline": cb,
+            "clocks": r["clocks"], "roofline": roof, "roofline_hbm": roof_hbm, "stages_ms": stage_table,
+            "cpu_baseline": cb,
             "e2e": {"value": round(e2e, 4), "unit": UNIT, "h2d_bytes_per_step": r["h2d"],
                     "d2h_bytes_per_step": r["d2h"]},
             "gpu_launches": launches_per_view * args.bsz * args.steps}
@@ -538,9 +600,11 @@ def main():
     return 0
 
 
-# kernels launched by one blitz_render_forward call: cub select (2), depth-key gather (1),
-# 32-bit cub radix sort (6), count gather (1), cub exclusive scan (2), emit (1),
-# 12-bit cub radix sort (4), tile ranges (1), blend (1)
+# kernels launched by the binning + blend calls of one view, as counted in the ncu
+# launch list (profiles/launches_city8M_bench.md): cub select (2), depth-key gather (1),
+# 32-bit cub onesweep sort (histogram + exclusive sum + 4 passes), count gather (1),
+# cub exclusive scan (2), emit (1), 12-bit sort (histogram + exclusive sum + 2 passes),
+# tile ranges (1), blend (1)
 KERNELS_RENDER_FWD = 19
 
 if __name__ == "__main__":

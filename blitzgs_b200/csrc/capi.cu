@@ -146,6 +146,88 @@ int blitz_preprocess_backward(int64_t P, int D, int M, const int32_t* radii, con
   return check(launch_preprocess_bwd(b, accumulate != 0, S(stream)), "blitz_preprocess_backward");
 }
 
+int blitz_preprocess_forward_raw(int64_t P, int D, int M, const float* xyz, const float* scaling_raw,
+                                 const float* rotation_raw, const float* rotation_norm,
+                                 const float* opacity_raw, const float* sh_dc, int64_t dc_stride,
+                                 const float* sh_rest, int64_t rest_stride, float scale_modifier,
+                                 const float* viewmatrix, const float* projmatrix, const float* campos,
+                                 float tanfovx, float tanfovy, int image_height, int image_width,
+                                 float* means2D, float* depths, int32_t* radii, float* conic_opacity,
+                                 float* rgb, double* reg_sums, uint32_t* vis_list, int32_t* vis_count,
+                                 void* stream) {
+  if (P < 0 || D < 0 || D > 3 || M < 0 || M > 15 || image_height <= 0 || image_width <= 0)
+    return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: bad sizes");
+  if (P == 0) return 0;
+  if (!xyz || !scaling_raw || !rotation_raw || !opacity_raw || !sh_dc || !viewmatrix || !projmatrix || !campos ||
+      !means2D || !depths || !radii || !conic_opacity || !rgb || (M > 0 && !sh_rest) || ((vis_list == nullptr) != (vis_count == nullptr)))
+    return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: null pointer");
+  if (!aligned16(rotation_raw) || !aligned16(conic_opacity) || (reinterpret_cast<uintptr_t>(means2D) & 7u))
+    return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: alignment");
+  PreprocessParams p = make_pp(P, D, M, xyz, scaling_raw, rotation_raw, sh_dc, dc_stride, sh_rest, rest_stride,
+                               opacity_raw, scale_modifier, viewmatrix, projmatrix, campos, tanfovx, tanfovy,
+                               image_height, image_width);
+  p.raw = true;
+  p.rot_norm = rotation_norm;
+  p.reg_sums = reg_sums;
+  p.vis_list_out = vis_list;
+  p.vis_count_out = vis_count;
+  p.out_means2D = means2D;
+  p.out_depths = depths;
+  p.out_radii = radii;
+  p.out_conic_opacity = conic_opacity;
+  p.out_rgb = rgb;
+  return check(launch_preprocess_fwd(p, S(stream)), "blitz_preprocess_forward_raw");
+}
+
+int blitz_preprocess_backward_raw(int64_t P, int D, int M, const int32_t* radii, const float* means2D,
+                                  const float* xyz, const float* scaling_raw, const float* rotation_raw,
+                                  const float* rotation_norm, const float* opacity_raw, const float* sh_dc,
+                                  int64_t dc_stride, const float* sh_rest, int64_t rest_stride,
+                                  float scale_modifier, const float* viewmatrix, const float* projmatrix,
+                                  const float* campos, float tanfovx, float tanfovy, int image_height,
+                                  int image_width, const float* g_means2D, int64_t g_means2D_stride,
+                                  const float* g_conic_opacity, int64_t g_conic_stride,
+                                  const float* g_colors, int64_t g_colors_stride, const float* reg_scale,
+                                  const uint32_t* vis_list, const int32_t* vis_count, float* g_xyz,
+                                  float* g_scaling_raw, float* g_rotation_raw, float* g_opacity_raw,
+                                  float* g_dc, int64_t g_dc_stride, float* g_rest, int64_t g_rest_stride,
+                                  int accumulate, void* stream) {
+  if (P < 0 || D < 0 || D > 3 || M < 0 || M > 15 || image_height <= 0 || image_width <= 0)
+    return fail(BLITZ_EINVAL, "blitz_preprocess_backward_raw: bad sizes");
+  if (P == 0) return 0;
+  if (!radii || !means2D || !xyz || !scaling_raw || !rotation_raw || !opacity_raw || !sh_dc || !g_means2D ||
+      !g_conic_opacity || !g_colors || !g_xyz || !g_scaling_raw || !g_rotation_raw || !g_dc ||
+      (M > 0 && (!sh_rest || !g_rest)) || ((vis_list == nullptr) != (vis_count == nullptr)))
+    return fail(BLITZ_EINVAL, "blitz_preprocess_backward_raw: null pointer");
+  if (!aligned16(rotation_raw) || !aligned16(g_rotation_raw) || !aligned16(g_conic_opacity) || (g_conic_stride & 3))
+    return fail(BLITZ_EINVAL, "blitz_preprocess_backward_raw: 16-byte alignment required");
+  PreprocessBwdParams b{};
+  b.f = make_pp(P, D, M, xyz, scaling_raw, rotation_raw, sh_dc, dc_stride, sh_rest, rest_stride, opacity_raw,
+                scale_modifier, viewmatrix, projmatrix, campos, tanfovx, tanfovy, image_height, image_width);
+  b.f.raw = true;
+  b.f.rot_norm = rotation_norm;
+  b.radii = radii;
+  b.means2D = means2D;
+  b.reg_scale = reg_scale;
+  b.vis_list = vis_list;
+  b.vis_count = vis_count;
+  b.g_means2D = g_means2D;
+  b.g_means2D_stride = g_means2D_stride;
+  b.g_conic_opacity = g_conic_opacity;
+  b.g_conic_stride = g_conic_stride;
+  b.g_colors = g_colors;
+  b.g_colors_stride = g_colors_stride;
+  b.g_means3D = g_xyz;
+  b.g_scales = g_scaling_raw;
+  b.g_rotations = g_rotation_raw;
+  b.g_opacities = g_opacity_raw;
+  b.g_dc = g_dc;
+  b.g_dc_stride = g_dc_stride;
+  b.g_rest = g_rest;
+  b.g_rest_stride = g_rest_stride;
+  return check(launch_preprocess_bwd(b, accumulate != 0, S(stream)), "blitz_preprocess_backward_raw");
+}
+
 int blitz_render_count(int64_t P, int image_height, int image_width, const float* means2D,
                        const int32_t* radii, const uint8_t* compute_locally, uint32_t* counts,
                        uint64_t* totals, void* stream) {
@@ -171,28 +253,14 @@ size_t blitz_render_scratch_bytes(int64_t P, int64_t n_vis, int64_t R, int image
   return bin_scratch_bytes(P, n_vis, R, gx * gy);
 }
 
-int blitz_render_forward(int64_t P, int64_t n_vis, int64_t R, int image_height, int image_width,
-                         const float* means2D, const float* depths, const int32_t* radii,
-                         const float* conic_opacity, const float* rgb, const float* bg,
-                         const uint8_t* compute_locally, const uint32_t* counts, void* scratch,
-                         size_t scratch_bytes, uint32_t* point_list, uint32_t* ranges,
-                         float* final_T, uint32_t* n_contrib, float* out_color, int32_t* n_render,
-                         int32_t* n_consider, int32_t* n_contrib_tile, int32_t* out_observe,
-                         void* stream) {
-  if (P < 0 || n_vis < 0 || R < 0 || R >= (int64_t)0x7fffffff || n_vis > P || image_height <= 0 ||
-      image_width <= 0)
-    return fail(BLITZ_EINVAL, "blitz_render_forward: bad sizes");
-  if (!bg || !ranges || !final_T || !n_contrib || !out_color || !n_render || !n_consider ||
-      !n_contrib_tile || (P > 0 && (!means2D || !depths || !radii || !conic_opacity || !rgb || !counts ||
-                                     !out_observe)) ||
-      (R > 0 && (!point_list || !scratch)))
-    return fail(BLITZ_EINVAL, "blitz_render_forward: null pointer");
-  if (P > 0 && (!aligned16(conic_opacity) || (reinterpret_cast<uintptr_t>(means2D) & 7u)))
-    return fail(BLITZ_EINVAL, "blitz_render_forward: conic_opacity needs 16-byte, means2D 8-byte alignment");
+namespace {
+
+int render_bin_impl(int64_t P, int64_t n_vis, int64_t R, int image_height, int image_width, const float* means2D,
+                    const float* depths, const int32_t* radii, const uint8_t* compute_locally, const uint32_t* counts,
+                    void* scratch, size_t scratch_bytes, uint32_t* point_list, uint32_t* ranges, cudaStream_t st) {
   const int gx = (image_width + kTileX - 1) / kTileX, gy = (image_height + kTileY - 1) / kTileY;
   if (R > 0 && scratch_bytes < bin_scratch_bytes(P, n_vis, R, gx * gy))
-    return fail(BLITZ_ESCRATCH, "blitz_render_forward: scratch too small");
-  cudaStream_t st = S(stream);
+    return fail(BLITZ_ESCRATCH, "render binning: scratch too small");
   BinSortParams bs{};
   bs.b.P = P;
   bs.b.W = image_width;
@@ -210,13 +278,19 @@ int blitz_render_forward(int64_t P, int64_t n_vis, int64_t R, int image_height, 
   bs.scratch_bytes = scratch_bytes;
   bs.point_list = point_list;
   bs.ranges = reinterpret_cast<uint2*>(ranges);
-  int e = launch_bin_sort(bs, st);
-  if (e) return fail(e, "blitz_render_forward: binning");
+  return check(launch_bin_sort(bs, st), "render binning");
+}
+
+int render_blend_impl(int64_t P, int image_height, int image_width, const float* means2D, const float* conic_opacity,
+                      const float* rgb, const float* bg, const uint8_t* compute_locally, const uint32_t* point_list,
+                      const uint32_t* ranges, float* final_T, uint32_t* n_contrib, float* out_color,
+                      int32_t* n_render, int32_t* n_consider, int32_t* n_contrib_tile, int32_t* out_observe,
+                      cudaStream_t st) {
   BlendFwdParams f{};
   f.W = image_width;
   f.H = image_height;
-  f.grid_x = gx;
-  f.grid_y = gy;
+  f.grid_x = (image_width + kTileX - 1) / kTileX;
+  f.grid_y = (image_height + kTileY - 1) / kTileY;
   f.P = P;
   f.ranges = reinterpret_cast<const uint2*>(ranges);
   f.point_list = point_list;
@@ -232,7 +306,56 @@ int blitz_render_forward(int64_t P, int64_t n_vis, int64_t R, int image_height, 
   f.n_render = n_render;
   f.n_consider = n_consider;
   f.n_contrib_tile = n_contrib_tile;
-  return check(launch_blend_fwd(f, st), "blitz_render_forward: blend");
+  return check(launch_blend_fwd(f, st), "render blend");
+}
+
+bool render_args_ok(int64_t P, int64_t n_vis, int64_t R, int H, int W) {
+  return !(P < 0 || n_vis < 0 || R < 0 || R >= (int64_t)0x7fffffff || n_vis > P || H <= 0 || W <= 0);
+}
+
+}  // namespace
+
+int blitz_render_forward(int64_t P, int64_t n_vis, int64_t R, int image_height, int image_width,
+                         const float* means2D, const float* depths, const int32_t* radii,
+                         const float* conic_opacity, const float* rgb, const float* bg,
+                         const uint8_t* compute_locally, const uint32_t* counts, void* scratch,
+                         size_t scratch_bytes, uint32_t* point_list, uint32_t* ranges,
+                         float* final_T, uint32_t* n_contrib, float* out_color, int32_t* n_render,
+                         int32_t* n_consider, int32_t* n_contrib_tile, int32_t* out_observe,
+                         void* stream) {
+  int e = blitz_render_bin(P, n_vis, R, image_height, image_width, means2D, depths, radii, compute_locally, counts,
+                           scratch, scratch_bytes, point_list, ranges, stream);
+  if (e) return e;
+  return blitz_render_blend(P, image_height, image_width, means2D, conic_opacity, rgb, bg, compute_locally,
+                            point_list, ranges, final_T, n_contrib, out_color, n_render, n_consider, n_contrib_tile,
+                            out_observe, stream);
+}
+
+int blitz_render_bin(int64_t P, int64_t n_vis, int64_t R, int image_height, int image_width, const float* means2D,
+                     const float* depths, const int32_t* radii, const uint8_t* compute_locally, const uint32_t* counts,
+                     void* scratch, size_t scratch_bytes, uint32_t* point_list, uint32_t* ranges, void* stream) {
+  if (!render_args_ok(P, n_vis, R, image_height, image_width)) return fail(BLITZ_EINVAL, "blitz_render_bin: bad sizes");
+  if (!ranges || (P > 0 && (!means2D || !depths || !radii || !counts)) || (R > 0 && (!point_list || !scratch)))
+    return fail(BLITZ_EINVAL, "blitz_render_bin: null pointer");
+  if (P > 0 && (reinterpret_cast<uintptr_t>(means2D) & 7u)) return fail(BLITZ_EINVAL, "blitz_render_bin: means2D alignment");
+  return render_bin_impl(P, n_vis, R, image_height, image_width, means2D, depths, radii, compute_locally, counts,
+                         scratch, scratch_bytes, point_list, ranges, S(stream));
+}
+
+int blitz_render_blend(int64_t P, int image_height, int image_width, const float* means2D, const float* conic_opacity,
+                       const float* rgb, const float* bg, const uint8_t* compute_locally, const uint32_t* point_list,
+                       const uint32_t* ranges, float* final_T, uint32_t* n_contrib, float* out_color,
+                       int32_t* n_render, int32_t* n_consider, int32_t* n_contrib_tile, int32_t* out_observe,
+                       void* stream) {
+  if (!render_args_ok(P, 0, 0, image_height, image_width)) return fail(BLITZ_EINVAL, "blitz_render_blend: bad sizes");
+  if (!bg || !ranges || !final_T || !n_contrib || !out_color || !n_render || !n_consider || !n_contrib_tile ||
+      (P > 0 && (!means2D || !conic_opacity || !rgb || !out_observe || !point_list)))
+    return fail(BLITZ_EINVAL, "blitz_render_blend: null pointer");
+  if (P > 0 && (!aligned16(conic_opacity) || (reinterpret_cast<uintptr_t>(means2D) & 7u)))
+    return fail(BLITZ_EINVAL, "blitz_render_blend: conic_opacity needs 16-byte, means2D 8-byte alignment");
+  return render_blend_impl(P, image_height, image_width, means2D, conic_opacity, rgb, bg, compute_locally, point_list,
+                           ranges, final_T, n_contrib, out_color, n_render, n_consider, n_contrib_tile, out_observe,
+                           S(stream));
 }
 
 int blitz_render_backward(int64_t P, int image_height, int image_width, const uint32_t* point_list,
@@ -314,6 +437,11 @@ int blitz_get_local2j_ids_bool(int image_height, int image_width, int mp_rank, i
   r.avoid_pixel_all2all = avoid_pixel_all2all != 0;
   r.out_bool = reinterpret_cast<bool*>(out);
   return check(launch_route_bool(r, S(stream)), "blitz_get_local2j_ids_bool");
+}
+
+int blitz_fp32_probe(int blocks, int64_t iters, float* sink, void* stream) {
+  if (blocks <= 0 || iters <= 0 || !sink) return fail(BLITZ_EINVAL, "blitz_fp32_probe: bad arguments");
+  return check(launch_fma_probe(blocks, iters, sink, S(stream)), "blitz_fp32_probe");
 }
 
 }  // extern "C"

@@ -39,6 +39,14 @@ struct PreprocessParams {
   bool* out_clamped;         // [P,3] or null
   float* out_cov3D;          // [P,6] or null
   unsigned* error_flag;      // device word, OR-ed with kErr* bits
+  // Raw-parameter mode: scales/rotations/opacities hold the model's raw
+  // _scaling / _rotation / _opacity; the kernel applies exp, normalize and
+  // sigmoid itself with the same float arithmetic as PyTorch.
+  bool raw;
+  const float* rot_norm;     // raw mode: ||_rotation|| per Gaussian, or null = computed here
+  double* reg_sums;          // raw mode, optional: {sum min-axis scale, count} over regulariser-visible
+  uint32_t* vis_list_out;    // optional [P]: indices of Gaussians with radius > 0 (unordered)
+  int* vis_count_out;        // device counter for vis_list_out, zero on entry
 };
 
 struct PreprocessBwdParams {
@@ -58,6 +66,12 @@ struct PreprocessBwdParams {
   int64_t g_dc_stride;
   float* g_rest;       // at g_rest + i*g_rest_stride (M*3 floats)
   int64_t g_rest_stride;
+  // Raw-parameter mode extras (see PreprocessParams::raw): gradients are with
+  // respect to the raw parameters.
+  const float* means2D;        // forward screen means (regulariser visibility), raw mode
+  const float* reg_scale;      // device float: dLoss/d(sum min-axis scale), or null
+  const uint32_t* vis_list;    // optional: only these Gaussians are processed; outputs pre-zeroed
+  const int* vis_count;        // device count of vis_list
 };
 
 int launch_preprocess_fwd(const PreprocessParams& p, cudaStream_t st);
@@ -167,5 +181,7 @@ struct RouteParams {
   bool* out_bool;                   // [P, world_size]
 };
 int launch_route_bool(const RouteParams& p, cudaStream_t st);
+
+int launch_fma_probe(int blocks, int64_t iters, float* sink, cudaStream_t st);
 
 }  // namespace blitz

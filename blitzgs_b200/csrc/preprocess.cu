@@ -57,9 +57,54 @@ __device__ __forceinline__ void load_sh(const PreprocessParams& p, int64_t i, in
   }
 }
 
+// Activations of the raw model parameters, in the float arithmetic PyTorch's
+// CUDA kernels use for torch.exp, torch.sigmoid and F.normalize
+// (scene/gaussian_model.py:248-276 applies them before the rasterizer), so
+// the activated values are bit-identical to the reference pipeline's.
+__device__ __forceinline__ float act_sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+__device__ __forceinline__ float quat_norm(float4 q) {
+  // squares rounded individually, summed left to right, then sqrt
+  const float a = q.x * q.x, b = q.y * q.y, c = q.z * q.z, d = q.w * q.w;
+  return sqrtf(__fadd_rn(__fadd_rn(__fadd_rn(a, b), c), d));
+}
+
+struct Activated {
+  float sx, sy, sz;
+  float4 q;    // normalised rotation
+  float nrm;   // max(||q_raw||, 1e-12)
+  float o;
+};
+
+__device__ __forceinline__ Activated activate(const PreprocessParams& p, int64_t i) {
+  Activated a;
+  float sx = __ldg(p.scales + 3 * i + 0), sy = __ldg(p.scales + 3 * i + 1), sz = __ldg(p.scales + 3 * i + 2);
+  float4 q = __ldg(reinterpret_cast<const float4*>(p.rotations) + i);
+  // the operator-API backward passes no opacities (it never needs them)
+  float o = p.opacities ? __ldg(p.opacities + i) : 0.f;
+  if (p.raw) {
+    sx = expf(sx);
+    sy = expf(sy);
+    sz = expf(sz);
+    const float n = p.rot_norm ? __ldg(p.rot_norm + i) : quat_norm(q);
+    a.nrm = fmaxf(n, 1e-12f);
+    q = make_float4(q.x / a.nrm, q.y / a.nrm, q.z / a.nrm, q.w / a.nrm);
+    o = act_sigmoid(o);
+  } else {
+    a.nrm = 1.f;
+  }
+  a.sx = sx;
+  a.sy = sy;
+  a.sz = sz;
+  a.q = q;
+  a.o = o;
+  return a;
+}
+
 __global__ void __launch_bounds__(256) preprocess_fwd_kernel(PreprocessParams p) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= p.P) return;
+  const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const bool valid = i0 < p.P;
+  const int64_t i = valid ? i0 : p.P - 1;  // tail threads recompute the last Gaussian, store nothing
 
   const float* V = p.viewmatrix;
   const float* Pm = p.projmatrix;
@@ -80,21 +125,22 @@ __global__ void __launch_bounds__(256) preprocess_fwd_kernel(PreprocessParams p)
   V3 rgb = {0.f, 0.f, 0.f};
   bool clamp3[3] = {false, false, false};
   float cov3d[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  Activated act;
+  act.sx = act.sy = act.sz = 0.f;
 
   do {
     // near-plane test (reference in_frustum, auxiliary.h:156-185)
     const float3 p_view = xform_point3(p_orig, Vs);
     if (p_view.z <= 0.2f) {
-      if (p.prefiltered) atomicOr(p.error_flag, kErrPrefilteredCulled);
+      if (p.prefiltered && valid) atomicOr(p.error_flag, kErrPrefilteredCulled);
       break;
     }
     const float4 p_hom = xform_point4(p_orig, Ps);
     const float p_w = 1.0f / (p_hom.w + 0.0000001f);
     const float3 p_proj = make_float3(p_hom.x * p_w, p_hom.y * p_w, p_hom.z * p_w);
 
-    const float4 q = __ldg(reinterpret_cast<const float4*>(p.rotations) + i);
-    cov3d_from_scale_rot(__ldg(p.scales + 3 * i + 0), __ldg(p.scales + 3 * i + 1),
-                         __ldg(p.scales + 3 * i + 2), p.scale_modifier, q, cov3d);
+    act = activate(p, i);
+    cov3d_from_scale_rot(act.sx, act.sy, act.sz, p.scale_modifier, act.q, cov3d);
     const float3 cov = cov2d_ewa(p_orig, p.focal_x, p.focal_y, p.tanfovx, p.tanfovy, cov3d, Vs);
 
     const float det = (cov.x * cov.z - cov.y * cov.y);
@@ -105,7 +151,7 @@ __global__ void __launch_bounds__(256) preprocess_fwd_kernel(PreprocessParams p)
     // Opacity-aware extent: min(3.33, sqrt(2 ln(255 alpha))).  The mixed
     // double/float min resolves to fmin in double, so a NaN (alpha < 1/255)
     // yields 3.33 and such Gaussians are not culled by opacity.
-    const float opacity = __ldg(p.opacities + i);
+    const float opacity = act.o;
     constexpr float alpha_threshold = 1.0f / 255.0f;
     const float opacity_power_threshold = logf(opacity / alpha_threshold);
     const float extent = fmin(3.33, (double)sqrtf(2.0f * opacity_power_threshold));
@@ -130,6 +176,59 @@ __global__ void __launch_bounds__(256) preprocess_fwd_kernel(PreprocessParams p)
     conic_op = make_float4(conic.x, conic.y, conic.z, opacity);
   } while (0);
 
+  // Block-level aggregation of the optional outputs: one atomic per block on
+  // each counter (a per-warp atomic on one address serialises in L2).
+  if (p.reg_sums || p.vis_list_out) {
+    __shared__ float s_rv[8], s_rc[8];
+    __shared__ int s_wc[8];
+    __shared__ int s_base;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // min-scale regulariser (gaussian_renderer/loss_distribution.py:314-322):
+    // Gaussians the exchange sends (radius > 0 and a non-empty square tile
+    // rect, the get_local2j_ids test) contribute their smallest scale.
+    float v = 0.f, c = 0.f;
+    if (p.reg_sums && valid && radius > 0) {
+      int2 lo, hi;
+      tile_rect_int(point_image, radius, p.grid_x, p.grid_y, lo, hi);
+      if ((hi.y - 1) * p.grid_x + hi.x - 1 >= lo.y * p.grid_x + lo.x) {
+        v = fminf(act.sx, fminf(act.sy, act.sz));
+        c = 1.f;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      v += __shfl_xor_sync(0xffffffffu, v, o);
+      c += __shfl_xor_sync(0xffffffffu, c, o);
+    }
+    const bool listed = valid && radius > 0;
+    const unsigned m = __ballot_sync(0xffffffffu, listed);
+    if (lane == 0) {
+      s_rv[warp] = v;
+      s_rc[warp] = c;
+      s_wc[warp] = __popc(m);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double bv = 0.0, bc = 0.0;
+      int tot = 0;
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+        bv += s_rv[w];
+        bc += s_rc[w];
+        const int n = s_wc[w];
+        s_wc[w] = tot;  // exclusive offset of warp w
+        tot += n;
+      }
+      if (p.reg_sums && bc > 0) {
+        atomicAdd(p.reg_sums + 0, bv);
+        atomicAdd(p.reg_sums + 1, bc);
+      }
+      s_base = (p.vis_list_out && tot) ? atomicAdd(p.vis_count_out, tot) : 0;
+    }
+    __syncthreads();
+    if (p.vis_list_out && listed)
+      p.vis_list_out[s_base + s_wc[warp] + __popc(m & ((1u << lane) - 1u))] = (uint32_t)i;
+  }
+  if (!valid) return;
   reinterpret_cast<float2*>(p.out_means2D)[i] = point_image;
   p.out_depths[i] = depth;
   p.out_radii[i] = radius;
@@ -176,6 +275,7 @@ struct BwdOut {
   float mean[3];
   float scale[3];
   float4 rot;
+  float op;
   float dc[3];
   float rest[45];
 };
@@ -184,6 +284,7 @@ __device__ __forceinline__ void bwd_zero(BwdOut& o) {
 #pragma unroll
   for (int k = 0; k < 3; ++k) o.mean[k] = o.scale[k] = o.dc[k] = 0.f;
   o.rot = make_float4(0.f, 0.f, 0.f, 0.f);
+  o.op = 0.f;
 #pragma unroll
   for (int k = 0; k < 45; ++k) o.rest[k] = 0.f;
 }
@@ -201,9 +302,9 @@ __device__ __forceinline__ void bwd_compute(const PreprocessBwdParams& p, int64_
   }
   const float3 mean = make_float3(__ldg(f.means3D + 3 * i + 0), __ldg(f.means3D + 3 * i + 1),
                                   __ldg(f.means3D + 3 * i + 2));
-  const float sx = __ldg(f.scales + 3 * i + 0), sy = __ldg(f.scales + 3 * i + 1),
-              sz = __ldg(f.scales + 3 * i + 2);
-  const float4 q = __ldg(reinterpret_cast<const float4*>(f.rotations) + i);
+  const Activated act = activate(f, i);
+  const float sx = act.sx, sy = act.sy, sz = act.sz;
+  const float4 q = act.q;
   float cov3d[6];
   cov3d_from_scale_rot(sx, sy, sz, f.scale_modifier, q, cov3d);
 
@@ -420,6 +521,73 @@ __device__ __forceinline__ void bwd_compute(const PreprocessBwdParams& p, int64_
            4 * z * (dMt[1][1] + dMt[0][0]);
     out.rot = dq;
   }
+  out.op = gco.w;
+  if (f.raw) {
+    // min-scale regulariser: d(loss)/d(min-axis scale) for Gaussians the
+    // exchange sends (radius > 0 and a non-empty square tile rect)
+    if (p.reg_scale && p.means2D) {
+      const float2 m2 = reinterpret_cast<const float2*>(p.means2D)[i];
+      int2 lo, hi;
+      tile_rect_int(m2, __ldg(p.radii + i), f.grid_x, f.grid_y, lo, hi);
+      if ((hi.y - 1) * f.grid_x + hi.x - 1 >= lo.y * f.grid_x + lo.x) {
+        const float g = *p.reg_scale;
+        // gradient to the first smallest axis (static indexing keeps `out` in registers)
+        if (sx <= sy && sx <= sz)
+          out.scale[0] += g;
+        else if (sy <= sz)
+          out.scale[1] += g;
+        else
+          out.scale[2] += g;
+      }
+    }
+    // chain through the activations: exp, normalize (with its 1e-12 clamp), sigmoid
+    out.scale[0] *= sx;
+    out.scale[1] *= sy;
+    out.scale[2] *= sz;
+    const float4 g = out.rot;
+    if (act.nrm > 1e-12f) {
+      const float dot = q.x * g.x + q.y * g.y + q.z * g.z + q.w * g.w;
+      out.rot = make_float4((g.x - q.x * dot) / act.nrm, (g.y - q.y * dot) / act.nrm, (g.z - q.z * dot) / act.nrm,
+                            (g.w - q.w * dot) / act.nrm);
+    } else {
+      out.rot = make_float4(g.x / act.nrm, g.y / act.nrm, g.z / act.nrm, g.w / act.nrm);
+    }
+    out.op = gco.w * (1.f - act.o) * act.o;
+  }
+}
+
+// Backward over a compact list of visible Gaussians (raw mode): every lane
+// does useful work; gradients are added into pre-zeroed (or accumulating)
+// outputs.
+__global__ void __launch_bounds__(128) preprocess_bwd_list_kernel(PreprocessBwdParams p) {
+  const PreprocessParams& f = p.f;
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= *p.vis_count) return;
+  const int64_t i = p.vis_list[j];
+  const float4 gco = *reinterpret_cast<const float4*>(p.g_conic_opacity + i * p.g_conic_stride);
+  BwdOut o;
+  bwd_zero(o);
+  bwd_compute(p, i, gco, o);
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    p.g_means3D[3 * i + k] += o.mean[k];
+    p.g_scales[3 * i + k] += o.scale[k];
+  }
+  float4* r = reinterpret_cast<float4*>(p.g_rotations) + i;
+  float4 a = *r;
+  a.x += o.rot.x;
+  a.y += o.rot.y;
+  a.z += o.rot.z;
+  a.w += o.rot.w;
+  *r = a;
+  if (p.g_opacities) p.g_opacities[i] += o.op;
+  float* gd = p.g_dc + i * p.g_dc_stride;
+  float* gr = p.g_rest + i * p.g_rest_stride;
+#pragma unroll
+  for (int k = 0; k < 3; ++k) gd[k] += o.dc[k];
+#pragma unroll
+  for (int k = 0; k < 45; ++k)
+    if (k < f.M * 3) gr[k] += o.rest[k];
 }
 
 constexpr int kBwdBlock = 128;
@@ -456,15 +624,16 @@ __global__ void __launch_bounds__(kBwdBlock) preprocess_bwd_kernel(PreprocessBwd
   float4 gco = make_float4(0.f, 0.f, 0.f, 0.f);
   bool vis = false;
   if (valid) {
-    gco = *reinterpret_cast<const float4*>(p.g_conic_opacity + i * p.g_conic_stride);
-    if (p.g_opacities) put<ACC>(p.g_opacities + i, gco.w);
     vis = __ldg(p.radii + i) > 0;
+    gco = *reinterpret_cast<const float4*>(p.g_conic_opacity + i * p.g_conic_stride);
   }
   if (ACC && !__syncthreads_or(vis)) return;  // nothing to add in this block
 
   BwdOut o;
   bwd_zero(o);
+  o.op = gco.w;  // the reference copies column 3 for every Gaussian
   if (vis) bwd_compute(p, i, gco, o);
+  if (valid && p.g_opacities) put<ACC>(p.g_opacities + i, o.op);
 
   if (valid) {
     float4* r = reinterpret_cast<float4*>(p.g_rotations) + i;
@@ -513,6 +682,11 @@ int launch_preprocess_fwd(const PreprocessParams& p, cudaStream_t st) {
 
 int launch_preprocess_bwd(const PreprocessBwdParams& p, bool accumulate, cudaStream_t st) {
   if (p.f.P <= 0) return 0;
+  if (p.vis_list) {
+    const int64_t blocks = (p.f.P + 127) / 128;
+    preprocess_bwd_list_kernel<<<(unsigned)blocks, 128, 0, st>>>(p);
+    return (int)cudaGetLastError();
+  }
   const int threads = kBwdBlock;
   const int64_t blocks = (p.f.P + threads - 1) / threads;
   if (accumulate)

@@ -190,6 +190,59 @@ def preprocess_backward(radii, means3D, scales, rotations, sh, raster, g_means2D
     return out_t
 
 
+def preprocess_forward_raw(xyz, scaling_raw, rotation_raw, opacity_raw, sh, raster, rot_norm=None, *,
+                           want_reg=True, want_list=True):
+    """Preprocess from the raw model parameters (activations fused into the
+    kernel).  Returns (means2D, depths, radii, conic_opacity, rgb, reg_sums
+    double[2] or None, vis_list or None, vis_count or None)."""
+    _require_cuda(xyz, scaling_raw, rotation_raw, opacity_raw)
+    xyz, scaling_raw, rotation_raw, opacity_raw = map(_f32c, (xyz, scaling_raw, rotation_raw, opacity_raw))
+    dc, dcs, rest, rs, M, _keep = sh
+    P = xyz.shape[0]
+    dev = xyz.device
+    means2D = torch.empty((P, 2), dtype=torch.float32, device=dev)
+    depths = torch.empty((P,), dtype=torch.float32, device=dev)
+    radii = torch.empty((P,), dtype=torch.int32, device=dev)
+    conic = torch.empty((P, 4), dtype=torch.float32, device=dev)
+    rgb = torch.empty((P, 3), dtype=torch.float32, device=dev)
+    reg = torch.zeros((2,), dtype=torch.float64, device=dev) if want_reg else None
+    vlist = torch.empty((max(P, 1),), dtype=torch.int32, device=dev) if want_list else None
+    vcount = torch.zeros((1,), dtype=torch.int32, device=dev) if want_list else None
+    if P > 0:
+        tok = TIMER.begin("preprocess_fwd")
+        _lib.call("blitz_preprocess_forward_raw", P, int(raster.sh_degree), M, ptr(xyz), ptr(scaling_raw),
+                  ptr(rotation_raw), ptr(rot_norm), ptr(opacity_raw), ptr(dc), dcs, ptr(rest), rs,
+                  float(raster.scale_modifier), ptr(_f32c(raster.viewmatrix)), ptr(_f32c(raster.projmatrix)),
+                  ptr(_f32c(raster.campos)), float(raster.tanfovx), float(raster.tanfovy),
+                  int(raster.image_height), int(raster.image_width), ptr(means2D), ptr(depths), ptr(radii),
+                  ptr(conic), ptr(rgb), ptr(reg), ptr(vlist), ptr(vcount), _lib.stream_ptr())
+        TIMER.end(tok, P=P)
+    return means2D, depths, radii, conic, rgb, reg, vlist, vcount
+
+
+def preprocess_backward_raw(radii, means2D, xyz, scaling_raw, rotation_raw, opacity_raw, sh, raster,
+                            g_means2D, g_conic, g_colors, out, rot_norm=None, reg_scale=None, vis_list=None,
+                            vis_count=None, accumulate=False):
+    """Gradients w.r.t. the raw parameters into ``out`` = (g_xyz, g_scaling,
+    g_rotation, g_opacity, (g_dc, stride), (g_rest, stride)).  With a visible
+    list the outputs must be zero-filled (or accumulating)."""
+    dc, dcs, rest, rs, M, _keep = sh
+    P = xyz.shape[0]
+    gx, gs, gq, go, (gdc, gdcs), (grest, grs) = out
+    if P > 0:
+        tok = TIMER.begin("preprocess_bwd")
+        _lib.call("blitz_preprocess_backward_raw", P, int(raster.sh_degree), M, ptr(radii), ptr(means2D),
+                  ptr(xyz), ptr(scaling_raw), ptr(rotation_raw), ptr(rot_norm), ptr(opacity_raw), ptr(dc), dcs,
+                  ptr(rest), rs, float(raster.scale_modifier), ptr(raster.viewmatrix), ptr(raster.projmatrix),
+                  ptr(raster.campos), float(raster.tanfovx), float(raster.tanfovy), int(raster.image_height),
+                  int(raster.image_width), ptr(g_means2D), g_means2D.stride(0), ptr(g_conic), g_conic.stride(0),
+                  ptr(g_colors), g_colors.stride(0), ptr(reg_scale), ptr(vis_list), ptr(vis_count), ptr(gx),
+                  ptr(gs), ptr(gq), ptr(go), ptr(gdc), gdcs, ptr(grest), grs, int(bool(accumulate)),
+                  _lib.stream_ptr())
+        TIMER.end(tok, P=P)
+    return out
+
+
 @dataclass
 class RenderState:
     """What the render backward needs from its forward (caller-owned buffers)."""
@@ -254,12 +307,16 @@ def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_local
     out_observe = torch.zeros((P,), dtype=torch.int32, device=dev)
     nbytes = _lib.load().blitz_render_scratch_bytes(P, n_vis, R, H, W)
     scratch = SCRATCH.get(dev, nbytes)
-    tok = TIMER.begin("render_fwd")
-    _lib.call("blitz_render_forward", P, n_vis, R, H, W, ptr(means2D), ptr(depths), ptr(radii),
-              ptr(conic_opacity), ptr(rgb), ptr(bg), ptr(cl), ptr(counts), ptr(scratch), scratch.numel(),
-              ptr(point_list), ptr(ranges), ptr(final_T), ptr(n_contrib), ptr(color), ptr(n_render),
-              ptr(n_consider), ptr(n_contrib_tile), ptr(out_observe), st)
-    TIMER.end(tok, P=P, R=R, n_vis=n_vis, H=H, W=W)
+    tok = TIMER.begin("binning")
+    _lib.call("blitz_render_bin", P, n_vis, R, H, W, ptr(means2D), ptr(depths), ptr(radii), ptr(cl), ptr(counts),
+              ptr(scratch), scratch.numel(), ptr(point_list), ptr(ranges), st)
+    TIMER.end(tok, P=P, R=R, n_vis=n_vis)
+    tok = TIMER.begin("blend_fwd")
+    _lib.call("blitz_render_blend", P, H, W, ptr(means2D), ptr(conic_opacity), ptr(rgb), ptr(bg), ptr(cl),
+              ptr(point_list), ptr(ranges), ptr(final_T), ptr(n_contrib), ptr(color), ptr(n_render), ptr(n_consider),
+              ptr(n_contrib_tile), ptr(out_observe), st)
+    TIMER.end(tok, P=P, R=R, n_vis=n_vis, H=H, W=W,
+              pairs=(n_consider.sum(dtype=torch.int64), n_contrib_tile.sum(dtype=torch.int64)) if TIMER.enabled else None)
     state = RenderState(H, W, R, n_vis, point_list, ranges, final_T, n_contrib)
     return color, n_render, n_consider, n_contrib_tile, out_observe, state
 
@@ -272,11 +329,11 @@ def render_backward(state, means2D, conic_opacity, rgb, bg, compute_locally, dL_
     if grad_accum is None:
         grad_accum = torch.zeros((P, 16), dtype=torch.float32, device=means2D.device)
     cl = compute_locally.contiguous().view(-1) if compute_locally is not None else None
-    tok = TIMER.begin("render_bwd")
+    tok = TIMER.begin("blend_bwd")
     _lib.call("blitz_render_backward", P, state.H, state.W, ptr(state.point_list), ptr(state.ranges),
               ptr(state.final_T), ptr(state.n_contrib), ptr(means2D), ptr(conic_opacity), ptr(rgb), ptr(bg),
               ptr(cl), ptr(dL_dpix), ptr(grad_accum), _lib.stream_ptr())
-    TIMER.end(tok, P=P, R=state.R)
+    TIMER.end(tok, P=P, R=state.R, pairs=(state.n_contrib.sum(dtype=torch.int64),) if TIMER.enabled else None)
     return grad_accum
 
 
@@ -327,6 +384,31 @@ def loss_backward(img, gt, partials, scale):
               ptr(_f32c(scale)), ptr(out), _lib.stream_ptr())
     TIMER.end(tok, pixels=C * Hb * W)
     return out
+
+
+def fp32_peak_tflops(seconds=0.3):
+    """Measured FP32 FMA throughput of this GPU (TFLOP/s), timed with CUDA events."""
+    dev = torch.device("cuda", torch.cuda.current_device())
+    sink = torch.zeros(1, device=dev)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    blocks = sms * 8
+    st = _lib.stream_ptr()
+    _lib.call("blitz_fp32_probe", blocks, 1000, ptr(sink), st)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    iters = 20000
+    a.record()
+    _lib.call("blitz_fp32_probe", blocks, iters, ptr(sink), st)
+    b.record()
+    b.synchronize()
+    ms = a.elapsed_time(b)
+    if ms < seconds * 1e3:
+        iters = int(iters * seconds * 1e3 / max(ms, 1e-3))
+        a.record()
+        _lib.call("blitz_fp32_probe", blocks, iters, ptr(sink), st)
+        b.record()
+        b.synchronize()
+        ms = a.elapsed_time(b)
+    return blocks * 256 * iters * 16 / (ms * 1e-3) / 1e12
 
 
 def local2j_ids_bool(H, W, mp_rank, mp_world_size, means2D, radii, dist_global_strategy,

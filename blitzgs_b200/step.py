@@ -13,11 +13,11 @@ results identical:
     gradient record [P,16] feeds the preprocess backward directly;
   * the only host synchronisation is the two-number readback that sizes the
     binning buffers.
-Parameter activations (exp, sigmoid, normalize) stay in PyTorch autograd,
-exactly as GaussianModel's getters compute them.
+Parameter activations (exp, sigmoid, normalize) run inside the preprocess
+kernels with PyTorch's float arithmetic, and their backward is chained there
+too, so no activation or regulariser kernel runs in PyTorch.
 """
 import torch
-import torch.nn.functional as F
 
 from . import ops
 
@@ -25,14 +25,18 @@ LAMBDA_DSSIM = 0.2
 
 
 class _ViewLoss(torch.autograd.Function):
-    """(xyz, scales, rots, opac, dc, rest) -> (l1_sum, ssim_sum) for one camera band."""
+    """Raw parameters (xyz, _scaling, _rotation, _opacity, _features_dc,
+    _features_rest) -> (sum L1, sum SSIM, sum of min-axis scales, count) for
+    one camera band; activations are applied inside the kernels."""
 
     @staticmethod
-    def forward(ctx, xyz, scales, rots, opac, dc, rest, raster, gt, compute_locally, band):
+    def forward(ctx, xyz, s_raw, q_raw, o_raw, dc, rest, raster, gt, compute_locally, band, exact_norm):
         H, W = int(raster.image_height), int(raster.image_width)
         sh = ops.sh_layout(dc=dc, rest=rest)
-        means2D, depths, radii, conic, rgb, _, _ = ops.preprocess_forward(
-            xyz, scales, rots, opac.reshape(-1), sh, raster)
+        rot_norm = q_raw.norm(dim=1) if exact_norm else None
+        use_list = compute_locally is None
+        means2D, depths, radii, conic, rgb, reg, vlist, vcount = ops.preprocess_forward_raw(
+            xyz, s_raw, q_raw, o_raw.reshape(-1), sh, raster, rot_norm, want_reg=True, want_list=use_list)
         color, n_render, n_consider, n_contrib, out_observe, state = ops.render_forward(
             means2D, depths, radii, conic, rgb, raster.bg, compute_locally, H, W)
         y0, y1 = band
@@ -43,15 +47,17 @@ class _ViewLoss(torch.autograd.Function):
         ctx.HW = (H, W)
         ctx.state = state
         ctx.cl = compute_locally
-        ctx.save_for_backward(xyz, scales, rots, opac, dc, rest, means2D, conic, rgb, radii, gt, partials, img_band)
-        ctx.mark_non_differentiable(radii, out_observe, n_render, n_consider, n_contrib)
+        ctx.save_for_backward(xyz, s_raw, q_raw, o_raw, dc, rest, means2D, conic, rgb, radii, gt, partials,
+                              img_band, rot_norm, vlist, vcount)
+        ctx.mark_non_differentiable(radii, out_observe, color)
         l1 = sums[0].to(torch.float32)
         ss = sums[1].to(torch.float32)
-        return l1, ss, radii, out_observe, n_render, n_consider, n_contrib, color
+        return l1, ss, reg[0].to(torch.float32), reg[1].to(torch.float32), radii, out_observe, color
 
     @staticmethod
-    def backward(ctx, g_l1, g_ss, *_unused):
-        xyz, scales, rots, opac, dc, rest, means2D, conic, rgb, radii, gt, partials, img_band = ctx.saved_tensors
+    def backward(ctx, g_l1, g_ss, g_reg, _g_cnt, *_unused):
+        (xyz, s_raw, q_raw, o_raw, dc, rest, means2D, conic, rgb, radii, gt, partials, img_band, rot_norm, vlist,
+         vcount) = ctx.saved_tensors
         H, W = ctx.HW
         y0, y1 = ctx.band
         dev = xyz.device
@@ -65,40 +71,36 @@ class _ViewLoss(torch.autograd.Function):
             dL_dpix[:, y0:y1, :] = g_band
         rec = ops.render_backward(ctx.state, means2D, conic, rgb, ctx.raster.bg, ctx.cl, dL_dpix)
         sh = ops.sh_layout(dc=dc, rest=rest)
-        P = xyz.shape[0]
         M = rest.shape[1]
-        g_xyz = torch.empty_like(xyz)
-        g_s = torch.empty_like(scales)
-        g_q = torch.empty_like(rots)
-        g_o = torch.empty((P, 1), dtype=torch.float32, device=dev)
-        g_dc = torch.empty_like(dc)
-        g_rest = torch.empty_like(rest)
-        ops.preprocess_backward(radii, xyz, scales, rots, sh, ctx.raster, rec[:, 0:2], rec[:, 8:12], rec[:, 12:15],
-                                out=(g_xyz, g_s, g_q, g_o, (g_dc, 3), (g_rest, max(M, 1) * 3)))
-        return g_xyz, g_s, g_q, g_o.view_as(opac), g_dc, g_rest, None, None, None, None
+        alloc = torch.zeros_like if vlist is not None else torch.empty_like
+        g_xyz, g_s, g_q, g_dc, g_rest = alloc(xyz), alloc(s_raw), alloc(q_raw), alloc(dc), alloc(rest)
+        g_o = alloc(o_raw)
+        reg_scale = (g_reg if g_reg is not None else zero).float().reshape(1)
+        ops.preprocess_backward_raw(radii, means2D, xyz, s_raw, q_raw, o_raw.reshape(-1), sh, ctx.raster,
+                                    rec[:, 0:2], rec[:, 8:12], rec[:, 12:15],
+                                    (g_xyz, g_s, g_q, g_o, (g_dc, 3), (g_rest, max(M, 1) * 3)), rot_norm=rot_norm,
+                                    reg_scale=reg_scale, vis_list=vlist, vis_count=vcount)
+        return g_xyz, g_s, g_q, g_o, g_dc, g_rest, None, None, None, None, None
 
 
 def view_loss(model, raster, gt_band, compute_locally=None, band=None, lambda_dssim=LAMBDA_DSSIM,
-              scale_reg_weight=10.0):
+              scale_reg_weight=10.0, exact_norm=True):
     """Loss of one camera exactly as batched_loss_computation forms it
     (loss_distribution.py:303-322): (1-l) L1/N3 + l (1 - SSIM/N3) +
-    10 mean(min-axis scale of visible Gaussians), N3 = 3 H W.
+    10 mean(min-axis scale of the Gaussians the exchange sends), N3 = 3 H W.
 
-    ``model`` = (xyz, _scaling, _rotation, _opacity, _features_dc, _features_rest)
-    raw parameters; activations are applied here in PyTorch.
+    ``model`` = raw (xyz, _scaling, _rotation, _opacity, _features_dc,
+    _features_rest); the activations run inside the preprocess kernels.
+    ``exact_norm`` takes ||_rotation|| from PyTorch (bit-identical to the
+    reference's F.normalize); otherwise the kernel computes it.
     Returns (loss, l1_sum, ssim_sum, radii, out_observe, color)."""
     xyz, s_raw, q_raw, o_raw, dc, rest = model
     H, W = int(raster.image_height), int(raster.image_width)
     band = band or (0, H)
-    scales = torch.exp(s_raw)
-    rots = F.normalize(q_raw)
-    opac = torch.sigmoid(o_raw)
-    l1, ss, radii, out_observe, _, _, _, color = _ViewLoss.apply(xyz, scales, rots, opac, dc, rest, raster, gt_band,
-                                                                 compute_locally, band)
+    l1, ss, reg, cnt, radii, out_observe, color = _ViewLoss.apply(xyz, s_raw, q_raw, o_raw, dc, rest, raster,
+                                                                   gt_band, compute_locally, band, exact_norm)
     n3 = H * W * 3
     loss = (1.0 - lambda_dssim) * (l1 / n3) + lambda_dssim * (1.0 - ss / n3)
     if scale_reg_weight:
-        vis = (radii > 0).to(torch.float32)
-        mins = scales.min(dim=1).values
-        loss = loss + scale_reg_weight * (mins * vis).sum() / vis.sum().clamp(min=1.0)
+        loss = loss + scale_reg_weight * reg / cnt.clamp(min=1.0)
     return loss, l1, ss, radii, out_observe, color

@@ -91,6 +91,56 @@ int blitz_preprocess_backward(int64_t P, int D, int M, const int32_t* radii, con
                               int accumulate, void* stream);
 
 /*
+ * Preprocess from the model's RAW parameters (fused training path).
+ * Same outputs as blitz_preprocess_forward, but scaling_raw / rotation_raw /
+ * opacity_raw are GaussianModel's _scaling / _rotation / _opacity and the
+ * kernel applies exp, normalize and sigmoid itself (scene/gaussian_model.py:
+ * 248-276) with PyTorch's float arithmetic; rotation_norm (device [P], may be
+ * NULL = computed in the kernel) is ||_rotation|| per Gaussian.
+ * Optional fused extras (each may be NULL):
+ *   reg_sums  device double[2] += {sum of the smallest activated scale, count}
+ *             over Gaussians with radius > 0 and a non-empty tile rect (the
+ *             min-scale regulariser of gaussian_renderer/loss_distribution.py:314-322);
+ *   vis_list  device uint32 [P] receives the indices of Gaussians with
+ *             radius > 0 (unordered), vis_count (device int32, zero on entry)
+ *             their number -- the work list of blitz_preprocess_backward_raw.
+ * Replaces the activation kernels + preprocess of the reference training step
+ * (gaussian_renderer/__init__.py:260-324); no reference op is a single match.
+ */
+int blitz_preprocess_forward_raw(int64_t P, int D, int M, const float* xyz, const float* scaling_raw,
+                                 const float* rotation_raw, const float* rotation_norm,
+                                 const float* opacity_raw, const float* sh_dc, int64_t dc_stride,
+                                 const float* sh_rest, int64_t rest_stride, float scale_modifier,
+                                 const float* viewmatrix, const float* projmatrix, const float* campos,
+                                 float tanfovx, float tanfovy, int image_height, int image_width,
+                                 float* means2D, float* depths, int32_t* radii, float* conic_opacity,
+                                 float* rgb, double* reg_sums, uint32_t* vis_list, int32_t* vis_count,
+                                 void* stream);
+
+/*
+ * Backward of blitz_preprocess_forward_raw: gradients with respect to the
+ * RAW parameters (xyz, _scaling, _rotation, _opacity, SH), chained through
+ * the activations in the kernel.  reg_scale (device float, may be NULL) is
+ * dLoss/d(reg_sums[0]).  With vis_list/vis_count from the forward only those
+ * Gaussians are processed and their gradients are ADDED to the outputs (which
+ * must be zero-filled or hold gradients to accumulate onto); with NULL every
+ * Gaussian is processed and `accumulate` selects overwrite (0) or add (1).
+ */
+int blitz_preprocess_backward_raw(int64_t P, int D, int M, const int32_t* radii, const float* means2D,
+                                  const float* xyz, const float* scaling_raw, const float* rotation_raw,
+                                  const float* rotation_norm, const float* opacity_raw, const float* sh_dc,
+                                  int64_t dc_stride, const float* sh_rest, int64_t rest_stride,
+                                  float scale_modifier, const float* viewmatrix, const float* projmatrix,
+                                  const float* campos, float tanfovx, float tanfovy, int image_height,
+                                  int image_width, const float* g_means2D, int64_t g_means2D_stride,
+                                  const float* g_conic_opacity, int64_t g_conic_stride,
+                                  const float* g_colors, int64_t g_colors_stride, const float* reg_scale,
+                                  const uint32_t* vis_list, const int32_t* vis_count, float* g_xyz,
+                                  float* g_scaling_raw, float* g_rotation_raw, float* g_opacity_raw,
+                                  float* g_dc, int64_t g_dc_stride, float* g_rest, int64_t g_rest_stride,
+                                  int accumulate, void* stream);
+
+/*
  * Render forward, phase 1 of 2: per-Gaussian tile-touch counts under the
  * compute_locally mask (bool [grid_y*grid_x], NULL = every tile), and the
  * device totals {R = tile instances, n_vis = Gaussians with count > 0}
@@ -127,6 +177,20 @@ int blitz_render_forward(int64_t P, int64_t n_vis, int64_t R, int image_height, 
                          float* final_T, uint32_t* n_contrib, float* out_color, int32_t* n_render,
                          int32_t* n_consider, int32_t* n_contrib_tile, int32_t* out_observe,
                          void* stream);
+
+/*
+ * The two halves of blitz_render_forward, for callers that schedule or time
+ * them separately: binning (point_list, ranges) and blending (everything
+ * else).  Same arguments and contracts as blitz_render_forward.
+ */
+int blitz_render_bin(int64_t P, int64_t n_vis, int64_t R, int image_height, int image_width, const float* means2D,
+                     const float* depths, const int32_t* radii, const uint8_t* compute_locally, const uint32_t* counts,
+                     void* scratch, size_t scratch_bytes, uint32_t* point_list, uint32_t* ranges, void* stream);
+int blitz_render_blend(int64_t P, int image_height, int image_width, const float* means2D, const float* conic_opacity,
+                       const float* rgb, const float* bg, const uint8_t* compute_locally, const uint32_t* point_list,
+                       const uint32_t* ranges, float* final_T, uint32_t* n_contrib, float* out_color,
+                       int32_t* n_render, int32_t* n_consider, int32_t* n_contrib_tile, int32_t* out_observe,
+                       void* stream);
 
 /*
  * Render backward.
@@ -176,6 +240,15 @@ int blitz_get_local2j_ids_bool(int image_height, int image_width, int mp_rank, i
                                int64_t P, const float* means2D, const int32_t* radii,
                                const int32_t* dist_global_strategy, int avoid_pixel_all2all,
                                uint8_t* out, void* stream);
+
+/*
+ * Measurement helper (no reference counterpart): `blocks` CTAs of 256
+ * threads each run 8 independent FMA chains for `iters` iterations
+ * (2*8*iters FLOP per thread); timing it gives the FP32 throughput used as
+ * the blend kernels' roofline denominator.  sink: device float, never written
+ * in practice.
+ */
+int blitz_fp32_probe(int blocks, int64_t iters, float* sink, void* stream);
 
 #ifdef __cplusplus
 }

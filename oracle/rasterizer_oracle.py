@@ -472,9 +472,11 @@ def loss_and_grad(img, gt, num_pixels, lambda_dssim=0.2):
 # Whole step
 # ---------------------------------------------------------------------------
 
-def train_step(scene_params, cam, gt, sh_degree=3, bg=None, lambda_dssim=0.2, compute_locally=None):
+def train_step(scene_params, cam, gt, sh_degree=3, bg=None, lambda_dssim=0.2, compute_locally=None, reg_weight=0.0):
     """One camera: activations -> preprocess -> binning -> blend -> loss ->
-    backward -> gradients w.r.t. the raw parameters."""
+    backward -> gradients w.r.t. the raw parameters.  reg_weight adds the
+    min-scale regulariser of loss_distribution.py:314-322 over the Gaussians
+    the exchange would send (radius > 0, non-empty tile rect)."""
     xyz, scaling, rotation, opacity, fdc, frest = scene_params
     bg = torch.zeros(3) if bg is None else bg
     H, W = cam.image_height, cam.image_width
@@ -496,7 +498,16 @@ def train_step(scene_params, cam, gt, sh_degree=3, bg=None, lambda_dssim=0.2, co
                                                o_act.detach(), cam.world_view_transform, cam.full_proj_transform,
                                                cam.camera_center, cam.tanfovx, cam.tanfovy, H, W, sh_degree,
                                                pre["radii"], rec[:, 0:2], rec[:, 8:12], rec[:, 12:15])
-    torch.autograd.backward([raw[0], s_act, q_act, o_act, shs], [dm, ds, dq, dop.reshape(o_act.shape), dsh])
+    torch.autograd.backward([raw[0], s_act, q_act, o_act, shs], [dm, ds, dq, dop.reshape(o_act.shape), dsh],
+                            retain_graph=True)
+    if reg_weight:
+        gxn, gyn = (W + TILE - 1) // TILE, (H + TILE - 1) // TILE
+        sent = torch.as_tensor(route_bool(pre["means2D"].numpy(), pre["radii"].numpy(), H, W, [0, gxn * gyn])[:, 0])
+        vis = sent & (pre["radii"] > 0)
+        if int(vis.sum()) > 0:
+            reg = reg_weight * torch.sort(s_act[vis], dim=-1)[0][..., 0].mean()
+            reg.backward()
+            loss = loss + reg.detach()
     grads = [t.grad if t.grad is not None else torch.zeros_like(t) for t in raw]
     return dict(pre=pre, point_list=pl, ranges=ranges, counts=counts, fwd=fwd, loss=loss, l1_sum=l1,
                 ssim_sum=ss, dimg=dimg, rec=rec, grads=grads)

@@ -65,3 +65,25 @@ def test_ops_refuse_cpu_tensors():
     with pytest.raises(RuntimeError, match="CUDA"):
         ops.preprocess_forward(sc.xyz, torch.exp(sc.scaling), sc.rotation, sc.opacity.reshape(-1),
                                ops.sh_layout(shs=shs), rs)
+
+
+def test_compat_import_names():
+    import importlib
+    import sys
+    compat = os.path.join(ROOT, "blitzgs_b200", "compat")
+    sys.path.insert(0, compat)
+    try:
+        f = importlib.import_module("diff_gaussian_rasterization_f")
+        r = importlib.import_module("diff_gaussian_rasterization_r")
+        for m in (f, r):
+            assert hasattr(m, "GaussianRasterizationSettings") and hasattr(m, "GaussianRasterizer")
+            for op in ("preprocess_gaussians", "preprocess_gaussians_backward", "render_gaussians",
+                       "render_gaussians_backward", "get_local2j_ids_bool"):
+                assert hasattr(m._C, op)
+        assert list(f.GaussianRasterizationSettings._fields) == [
+            "image_height", "image_width", "tanfovx", "tanfovy", "bg", "scale_modifier", "viewmatrix",
+            "projmatrix", "sh_degree", "campos", "prefiltered", "debug"]
+    finally:
+        sys.path.remove(compat)
+        for n in ("diff_gaussian_rasterization_f", "diff_gaussian_rasterization_r"):
+            sys.modules.pop(n, None)

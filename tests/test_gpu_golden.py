@@ -58,7 +58,11 @@ def _check_forward(g, o, prefix="", band_rows=None):
     loc = _local_pixel_mask(H, W, band_rows)
     assert np.array_equal(st.n_contrib.cpu().numpy().astype(np.int64)[loc], g[prefix + "n_contrib"].astype(np.int64)[loc])
     if prefix + "final_T" in g:
-        assert np.array_equal(st.final_T.cpu().numpy().view(np.uint32)[loc], g[prefix + "final_T"].view(np.uint32)[loc])
+        mine = st.final_T.cpu().numpy()[loc]
+        ref = g[prefix + "final_T"][loc]
+        bad = np.nonzero(mine.view(np.uint32) != ref.view(np.uint32))[0]
+        assert len(bad) == 0, (f"final_T differs at {len(bad)} local pixels; first {bad[:5].tolist()}: "
+                               f"ours {mine[bad[:5]].tolist()} reference {ref[bad[:5]].tolist()}")
     for k in ("n_render", "n_consider", "n_contrib_tile", "out_observe"):
         assert np.array_equal(o[k].cpu().numpy(), g[prefix + k]), k
     err = np.abs(o["image"].cpu().numpy() - g[prefix + "image"]).max()

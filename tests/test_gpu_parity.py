@@ -148,6 +148,33 @@ def test_full_step_gradients_match_oracle(cuda_device):
         assert_grad_close(p.grad.cpu(), r, 2e-3, n)
 
 
+def test_fused_regulariser_matches_oracle(cuda_device):
+    sc = S.tiny(seed=9, P=3000, H=96, W=128)
+    cam = sc.cameras[0]
+    gt = S.target_image(9, cam.image_height, cam.image_width)
+    ref = O.train_step(scene_params(sc), cam, gt, reg_weight=10.0)
+    model = [t.to(cuda_device).requires_grad_(True) for t in scene_params(sc)]
+    rs = _raster(cam.to(cuda_device), cuda_device)
+    loss, *_ = ST.view_loss(model, rs, gt.to(cuda_device), scale_reg_weight=10.0)
+    loss.backward()
+    assert abs(loss.item() - ref["loss"].item()) < 1e-5
+    for n, p, r in zip(["xyz", "scaling", "rotation", "opacity", "features_dc", "features_rest"], model, ref["grads"]):
+        assert_grad_close(p.grad.cpu(), r, 2e-3, n)
+
+
+def test_in_kernel_norm_matches_torch_norm(cuda_device):
+    """The fused step's two ways of normalising the rotation agree bit for bit."""
+    sc = S.tiny(seed=10, P=20000, H=96, W=128)
+    cam = sc.cameras[0].to(cuda_device)
+    rs = _raster(cam, cuda_device)
+    xyz, s, q, o, dc, rest = [t.to(cuda_device) for t in scene_params(sc)]
+    sh = ops.sh_layout(dc=dc, rest=rest)
+    a = ops.preprocess_forward_raw(xyz, s, q, o.reshape(-1), sh, rs, q.norm(dim=1))
+    b = ops.preprocess_forward_raw(xyz, s, q, o.reshape(-1), sh, rs, None)
+    for x, y in zip(a[:5], b[:5]):
+        assert torch.equal(x, y)
+
+
 def test_drop_in_api_autograd_matches_fused(cuda_device):
     """GaussianRasterizer.preprocess_gaussians/render_gaussians (reference API)
     give the same loss and parameter gradients as the fused step."""
@@ -181,7 +208,7 @@ def test_drop_in_api_autograd_matches_fused(cuda_device):
     loss.backward()
     assert abs(loss.item() - loss_f.item()) < 1e-6
     for a, b in zip(model, fused):
-        assert_grad_close(a.grad, b, 1e-6)
+        assert_grad_close(a.grad, b, 1e-5)
     assert "forward_render_time" in ca["stats_collector"] and "backward_render_time" in ca["stats_collector"]
     assert m2.grad is not None and abs_pts.grad is not None
 
