@@ -19,6 +19,7 @@ Python operator API and loss helpers on the same workload; when that build is
 absent it times the CPU oracle port on a bounded sample instead.
 """
 import argparse
+import gc
 import json
 import math
 import os
@@ -238,9 +239,10 @@ def run_ours(args, ws, rank, local):
         one_step(args.warmup + (it % args.steps), False)
     torch.cuda.synchronize()
     args.warmup_done = n_warm
-    time.sleep(0.2)
+    gc.collect()
+    gc.disable()  # no collector pauses inside the timed regions
 
-    # timed: device-resident inputs
+    # timed: device-resident inputs (no idle gap after the warm-up)
     barrier(ws)
     torch.cuda.synchronize()
     clocks.mark()
@@ -269,14 +271,28 @@ def run_ours(args, ws, rank, local):
     clk = clocks.stop()
     ms_e2e = max_over_ranks(e0.elapsed_time(e1), ws)
 
-    # stage timing pass (events around each native call) for the roofline
+    # per-step device times of the same sequence (diagnostic, stderr)
+    per = []
+    for it in range(args.steps):
+        a = torch.cuda.Event(enable_timing=True)
+        b_ = torch.cuda.Event(enable_timing=True)
+        a.record()
+        one_step(args.warmup + it, False)
+        b_.record()
+        torch.cuda.synchronize()
+        per.append(round(a.elapsed_time(b_), 3))
+    if rank == 0:
+        log("per-step ms:", per)
+
+    # stage timing pass (events around each native call) for the roofline, on warmed cameras
     ops.TIMER.enabled = True
     ops.TIMER.reset()
     for it in range(min(args.steps, 3)):
-        one_step(it, False)
+        one_step(args.warmup + it, False)
     torch.cuda.synchronize()
     stages = ops.TIMER.summary()
     ops.TIMER.enabled = False
+    gc.enable()
     n_stage_steps = min(args.steps, 3)
     return dict(ms=ms, ms_e2e=ms_e2e, clocks=clk, stages=stages, H=H, W=W, P=sc.P, bsz=bsz,
                 h2d=h2d[0], d2h=4, n_stage_steps=n_stage_steps)
@@ -481,7 +497,8 @@ def run_reference(args):
         one_step(args.warmup + (it % args.steps), False)
     torch.cuda.synchronize()
     args.warmup_done = n_warm
-    time.sleep(0.2)
+    gc.collect()
+    gc.disable()
     clocks.mark()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
@@ -511,6 +528,7 @@ def run_reference(args):
         torch.cuda.synchronize()
         per.append(round(a.elapsed_time(b), 2))
     log("reference per-step ms:", per)
+    gc.enable()
     ms_e2e = e0.elapsed_time(e1)
     return dict(ms=ms, ms_e2e=ms_e2e, clocks=clk, H=H, W=W, P=sc.P)
 

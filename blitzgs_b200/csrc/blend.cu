@@ -43,6 +43,46 @@ __device__ __forceinline__ float skip_threshold(float o) {
   return __int_as_float(0xff800000);                  // NaN opacity: never pre-skip
 }
 
+// True when no pixel centre of the tile [tx0, tx0+15] x [ty0, ty0+15] can
+// give this Gaussian alpha >= 1/255, i.e. when every (pixel, Gaussian) pair of
+// the tile would be skipped by the per-pixel test.  The alpha >= 1/255 region
+// is the ellipse d^T C d <= 2 ln(255 o) (C = conic); its bounding box is
+// inflated for the float error of the per-pixel power (more for
+// ill-conditioned conics, whose terms cancel).  Degenerate conics and NaN
+// opacities are never culled.
+__device__ __forceinline__ bool tile_cull(float2 xy, float4 co, float tx0, float ty0) {
+  const float o = co.w;
+  if (o < 1.0f / 255.0f) return true;   // o * G <= o < 1/255 for every pixel
+  if (!(o >= 1.0f / 255.0f)) return false;  // NaN
+  const float det = co.x * co.z - co.y * co.y;
+  if (!(co.x > 0.f && co.z > 0.f && det > 0.f)) return false;
+  const float k = co.x * co.z / det;  // >= 1; large when the terms of the quadratic form cancel
+  const float r2 = 2.f * logf(255.f * o) * (1.002f + 1e-5f * k) + 1e-3f;
+  const float hx = sqrtf(r2 * co.z / det) + 0.01f;
+  const float hy = sqrtf(r2 * co.x / det) + 0.01f;
+  if (!(hx < 1e30f && hy < 1e30f)) return false;
+  return (xy.x + hx < tx0) || (xy.x - hx > tx0 + 15.f) || (xy.y + hy < ty0) || (xy.y - hy > ty0 + 15.f);
+}
+
+// Order-preserving compaction of the kept batch slots into s_list; returns
+// the number kept (same value in every thread).  Ends with a barrier.
+__device__ __forceinline__ int compact_batch(bool keep, int* s_wcnt, int* s_list) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const unsigned m = __ballot_sync(0xffffffffu, keep);
+  if (lane == 0) s_wcnt[warp] = __popc(m);
+  __syncthreads();
+  int off = 0, tot = 0;
+#pragma unroll
+  for (int w = 0; w < kTilePix / 32; ++w) {
+    const int c = s_wcnt[w];
+    off += (w < warp) ? c : 0;
+    tot += c;
+  }
+  if (keep) s_list[off + __popc(m & ((1u << lane) - 1u))] = threadIdx.x;
+  __syncthreads();
+  return tot;
+}
+
 __device__ __forceinline__ int block_sum_int(int v, int* s_red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -91,6 +131,9 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
   __shared__ int s_id[kBatch];
   __shared__ int s_obs[kBatch];
   __shared__ int s_red[32];
+  __shared__ int s_list[kBatch];
+  __shared__ int s_wcnt[kTilePix / 32];
+  const float tx0 = (float)(tx * kTileX), ty0 = (float)(ty * kTileY);
 
   const uint2 range = p.ranges[tile];
   const int n = (int)(range.y - range.x);
@@ -107,21 +150,24 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
     const int num_done = __syncthreads_count(done);
     if (num_done == kTilePix) break;
     const int k = r * kBatch + threadIdx.x;
+    bool keep = false;
     if (k < n) {
       const int id = (int)p.point_list[range.x + k];
       s_id[threadIdx.x] = id;
-      s_xy[threadIdx.x] = reinterpret_cast<const float2*>(p.means2D)[id];
+      const float2 xy = reinterpret_cast<const float2*>(p.means2D)[id];
+      s_xy[threadIdx.x] = xy;
       const float4 co = reinterpret_cast<const float4*>(p.conic_opacity)[id];
       s_co[threadIdx.x] = co;
       s_rgb[threadIdx.x] = make_float4(p.rgb[3 * (int64_t)id + 0], p.rgb[3 * (int64_t)id + 1],
                                        p.rgb[3 * (int64_t)id + 2], skip_threshold(co.w));
+      keep = !tile_cull(xy, co, tx0, ty0);
     }
     s_obs[threadIdx.x] = 0;
-    __syncthreads();
+    const int kept = compact_batch(keep, s_wcnt, s_list);
 
-    const int cnt = min(kBatch, toDo);
-    for (int j = 0; !done && j < cnt; ++j) {
-      ++contributor;
+    for (int q = 0; !done && q < kept; ++q) {
+      const int j = s_list[q];
+      contributor = (uint32_t)(r * kBatch + j + 1);  // 1-based list position, as the reference counts it
       const float2 xy = s_xy[j];
       const float2 d = {xy.x - pixf.x, xy.y - pixf.y};
       const float4 con_o = s_co[j];
@@ -145,8 +191,7 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
       last_contributor = contributor;
     }
     __syncthreads();
-    if (threadIdx.x < cnt && s_obs[threadIdx.x] > 0)
-      atomicAdd(&p.out_observe[s_id[threadIdx.x]], s_obs[threadIdx.x]);
+    if (k < n && s_obs[threadIdx.x] > 0) atomicAdd(&p.out_observe[s_id[threadIdx.x]], s_obs[threadIdx.x]);
   }
 
   if (inside) {
@@ -229,6 +274,9 @@ __global__ void __launch_bounds__(kTilePix) blend_bwd_kernel(BlendBwdParams p) {
   __shared__ float4 s_rgb[kBatch];
   __shared__ int s_id[kBatch];
   __shared__ int s_max;
+  __shared__ int s_list[kBatch];
+  __shared__ int s_wcnt[kTilePix / 32];
+  const float tx0 = (float)(tx * kTileX), ty0 = (float)(ty * kTileY);
 
   const uint2 range = p.ranges[tile];
   const float T_final = inside ? p.final_T[pix] : 0.f;
@@ -263,18 +311,21 @@ __global__ void __launch_bounds__(kTilePix) blend_bwd_kernel(BlendBwdParams p) {
   for (int r = 0; r < rounds; ++r) {
     __syncthreads();
     const int k = n_eff - 1 - (r * kBatch + (int)threadIdx.x);  // list position, back to front
+    bool keep = false;
     if (k >= 0) {
       const int id = (int)p.point_list[range.x + k];
       s_id[threadIdx.x] = id;
-      s_xy[threadIdx.x] = reinterpret_cast<const float2*>(p.means2D)[id];
+      const float2 xy = reinterpret_cast<const float2*>(p.means2D)[id];
+      s_xy[threadIdx.x] = xy;
       const float4 co = reinterpret_cast<const float4*>(p.conic_opacity)[id];
       s_co[threadIdx.x] = co;
       s_rgb[threadIdx.x] = make_float4(p.rgb[3 * (int64_t)id + 0], p.rgb[3 * (int64_t)id + 1],
                                        p.rgb[3 * (int64_t)id + 2], skip_threshold(co.w));
+      keep = !tile_cull(xy, co, tx0, ty0);
     }
-    __syncthreads();
-    const int cnt = min(kBatch, n_eff - r * kBatch);
-    for (int j = 0; j < cnt; ++j) {
+    const int kept = compact_batch(keep, s_wcnt, s_list);
+    for (int q = 0; q < kept; ++q) {
+      const int j = s_list[q];
       const int pos = n_eff - 1 - (r * kBatch + j);
       float g[16];
       bool contrib = false;

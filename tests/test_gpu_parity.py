@@ -162,15 +162,19 @@ def test_fused_regulariser_matches_oracle(cuda_device):
         assert_grad_close(p.grad.cpu(), r, 2e-3, n)
 
 
-def test_in_kernel_norm_matches_torch_norm(cuda_device):
-    """The fused step's two ways of normalising the rotation agree bit for bit."""
+def test_raw_preprocess_bit_identical_to_torch_activations(cuda_device):
+    """Activations fused into the kernel (exp, sigmoid, division by PyTorch's
+    rotation norm) give the same bits as the operator API fed with PyTorch's
+    exp / normalize / sigmoid, so the fused step culls and bins exactly as the
+    reference pipeline does."""
     sc = S.tiny(seed=10, P=20000, H=96, W=128)
     cam = sc.cameras[0].to(cuda_device)
     rs = _raster(cam, cuda_device)
     xyz, s, q, o, dc, rest = [t.to(cuda_device) for t in scene_params(sc)]
-    sh = ops.sh_layout(dc=dc, rest=rest)
-    a = ops.preprocess_forward_raw(xyz, s, q, o.reshape(-1), sh, rs, q.norm(dim=1))
-    b = ops.preprocess_forward_raw(xyz, s, q, o.reshape(-1), sh, rs, None)
+    a = ops.preprocess_forward_raw(xyz, s, q, o.reshape(-1), ops.sh_layout(dc=dc, rest=rest), rs, q.norm(dim=1))
+    shs = torch.cat((dc, rest), 1)
+    b = ops.preprocess_forward(xyz, torch.exp(s), torch.nn.functional.normalize(q), torch.sigmoid(o).reshape(-1),
+                               ops.sh_layout(shs=shs), rs)
     for x, y in zip(a[:5], b[:5]):
         assert torch.equal(x, y)
 
