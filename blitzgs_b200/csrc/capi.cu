@@ -65,6 +65,10 @@ PreprocessParams make_pp(int64_t P, int D, int M, const float* means3D, const fl
 
 }  // namespace
 
+namespace blitz {
+void set_last_error(const char* msg) { g_last_error = msg; }
+}  // namespace blitz
+
 extern "C" {
 
 const char* blitz_version(void) { return "blitzgs_b200 0.1 (sm_100a)"; }

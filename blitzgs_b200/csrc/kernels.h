@@ -184,4 +184,7 @@ int launch_route_bool(const RouteParams& p, cudaStream_t st);
 
 int launch_fma_probe(int blocks, int64_t iters, float* sink, cudaStream_t st);
 
+// Records the message blitz_last_error() returns on this thread (capi.cu).
+void set_last_error(const char* msg);
+
 }  // namespace blitz

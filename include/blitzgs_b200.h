@@ -193,6 +193,23 @@ int blitz_render_blend(int64_t P, int image_height, int image_width, const float
                        void* stream);
 
 /*
+ * Binning for callers that cannot allocate device memory at call time (no
+ * counterpart in the reference).  Same arguments and results as
+ * blitz_render_bin minus the scratch buffer: the scratch is a fixed
+ * BLITZ_NOALLOC_SCRATCH_BYTES array inside this library, held by every GPU
+ * that loads it until the process exits.  Requests whose
+ * blitz_render_scratch_bytes() exceed it fail with BLITZ_ESCRATCH.  All calls
+ * on a device share the array: calls that overlap on the GPU race.  The first
+ * call on a device resolves the array's address (make it before any stream
+ * capture).  Allocates nothing.
+ */
+#define BLITZ_NOALLOC_SCRATCH_BYTES (64u << 20)
+int blitz_render_bin_noalloc(int64_t P, int64_t n_vis, int64_t R, int image_height, int image_width,
+                             const float* means2D, const float* depths, const int32_t* radii,
+                             const uint8_t* compute_locally, const uint32_t* counts, uint32_t* point_list,
+                             uint32_t* ranges, void* stream);
+
+/*
  * Render backward.
  * Replaces _C.render_gaussians_backward / RenderGaussiansBackwardCUDA
  * (submodule/diff-gaussian-rasterization_r/rasterize_points.cu:364-436,
