@@ -51,12 +51,35 @@ def load_peaks():
     return PEAKS_FALLBACK, "fallback"
 
 
+_POLLER = r"""
+import sys, time
+import pynvml as nv
+nv.nvmlInit()
+g = sys.argv[1]
+h = nv.nvmlDeviceGetHandleByIndex(int(g)) if g.isdigit() else nv.nvmlDeviceGetHandleByUUID(g)
+mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+rs = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or nv.nvmlDeviceGetCurrentClocksThrottleReasons
+while True:
+    print(time.monotonic_ns(), nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), mx, int(rs(h)), flush=True)
+    time.sleep(0.05)
+"""
+
+
 class ClockSampler:
-    """nvidia-smi samples of SM clock / throttle reasons during the timed region."""
+    """SM clock and throttle reasons during the timed regions.
+
+    A separate process polls NVML (read-only queries) every 50 ms and prints
+    time-stamped samples; samples between pairs of mark() calls count, and a
+    region shorter than the period takes the nearest sample.  Falls back to
+    nvidia-smi at 200 ms when the NVML bindings are missing.  A separate
+    process at a modest rate keeps the queries from competing with this
+    process's kernel launches (for the GIL or the driver)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
 
     def __init__(self, gpu_index):
         vis = os.environ.get("CUDA_VISIBLE_DEVICES")
@@ -66,60 +89,87 @@ class ClockSampler:
                 gpu_index = ids[gpu_index]
         self.gpu = gpu_index
         self.proc = None
-        self.lines = []
-        self.marks = []
+        self.samples = []  # (t_ns, sm_mhz, max_mhz, reason bits)
+        self.windows = []
         self.thread = None
+        self.source = None
 
     def mark(self):
-        self.marks.append(len(self.lines))
+        t = time.monotonic_ns()
+        if self.windows and len(self.windows[-1]) == 1:
+            self.windows[-1].append(t)
+        else:
+            self.windows.append([t])
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except (FileNotFoundError, OSError):
-            self.proc = None
-            return
-        self.thread = threading.Thread(target=self._read, daemon=True)
+            import pynvml  # noqa: F401  (the poller needs it)
+            self.proc = subprocess.Popen([sys.executable, "-c", _POLLER, str(self.gpu)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.source = "nvml"
+            self.thread = threading.Thread(target=self._read_nvml, daemon=True)
+        except Exception:
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                     "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            except (FileNotFoundError, OSError):
+                self.proc = None
+                return
+            self.source = "nvidia-smi"
+            self.thread = threading.Thread(target=self._read_smi, daemon=True)
         self.thread.start()
+        # wait for the first sample, so the poller is up before any timed region
+        t0 = time.time()
+        while not self.samples and time.time() - t0 < 20 and self.proc.poll() is None:
+            time.sleep(0.05)
 
-    def _read(self):
+    def _read_nvml(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            parts = line.split()
+            if len(parts) == 4:
+                self.samples.append((int(parts[0]), float(parts[1]), float(parts[2]), int(parts[3])))
 
-    def stop(self):
-        if self.proc is None:
-            return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        if self.thread:
-            self.thread.join(timeout=2)
-        sms, maxs, reasons = [], [], set()
+    def _read_smi(self):
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        lines = self.lines
-        if len(self.marks) >= 2 and self.marks[1] > self.marks[0]:
-            lines = self.lines[self.marks[0]:self.marks[1]]
-        for ln in lines:
-            parts = [p.strip() for p in ln.split(",")]
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.strip().split(",")]
             if len(parts) < 9:
                 continue
             try:
-                sms.append(float(parts[1]))
-                maxs.append(float(parts[2]))
+                bits = 0
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower() in ("active", "0x1", "1"):
+                        bits |= self.REASONS[n]
+                self.samples.append((time.monotonic_ns(), float(parts[1]), float(parts[2]), bits))
             except ValueError:
                 continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower() in ("active", "0x1", "1"):
-                    reasons.add(n)
-        if not sms:
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        inside = []
+        for w in self.windows:
+            if len(w) != 2 or not self.samples:
+                continue
+            ins = [s for s in self.samples if w[0] <= s[0] <= w[1]]
+            # a region shorter than the sampling period takes its nearest sample
+            inside += ins or [min(self.samples, key=lambda s: abs(s[0] - (w[0] + w[1]) // 2))]
+        if not inside:
             return None
-        sms.sort()
-        return {"sm_mhz": sms[len(sms) // 2], "sm_max_mhz": max(maxs), "reasons": sorted(reasons),
-                "samples": len(sms)}
+        sms = sorted(s[1] for s in inside)
+        bits = 0
+        for s in inside:
+            bits |= s[3]
+        reasons = sorted(n for n, b in self.REASONS.items() if bits & b)
+        return {"sm_mhz": sms[len(sms) // 2], "sm_max_mhz": max(s[2] for s in inside), "reasons": reasons,
+                "samples": len(sms), "source": self.source}
 
 
 def dist_setup(n_gpus):
@@ -260,6 +310,7 @@ def run_ours(args, ws, rank, local):
     # timed: end to end (GT uploaded from pinned host memory, loss read back)
     barrier(ws)
     torch.cuda.synchronize()
+    clocks.mark()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
@@ -267,6 +318,7 @@ def run_ours(args, ws, rank, local):
         one_step(args.warmup + it, True)
     e1.record()
     torch.cuda.synchronize()
+    clocks.mark()
     barrier(ws)
     clk = clocks.stop()
     ms_e2e = max_over_ranks(e0.elapsed_time(e1), ws)
@@ -301,19 +353,28 @@ def run_ours(args, ws, rank, local):
 def stage_bytes(name, metas):
     """Algorithmic (minimum) DRAM bytes of one native stage, summed over its
     launches.  P = Gaussians processed, V = Gaussians that touch a rendered
-    tile (n_vis of the same view).
-      preprocess_fwd: every Gaussian reads xyz (12) and writes its 44 output
-        bytes; visible ones also read scale 12, rotation 16, opacity 4, SH 192.
-      preprocess_bwd: every Gaussian reads its radius (4) and writes its 236
-        gradient bytes; visible ones also read their parameters (236) and
-        upstream gradients (36)."""
+    tile (n_vis of the same view), L = Gaussians with radius > 0 (the visible
+    list, when the launch produced or consumed one).
+      preprocess_fwd with the fused tile count and the list: every Gaussian
+        reads xyz (12) and writes its radius and tile count (8); listed ones
+        also read scale 12, rotation 16, opacity 4, SH 192 and write their
+        40 output bytes and list slot 4.
+      preprocess_fwd, dense: every Gaussian reads xyz (12) and writes its 44
+        output bytes; visible ones also read scale 12, rotation 16, opacity 4,
+        SH 192.
+      preprocess_bwd over the list: listed Gaussians read their parameters
+        (236) and upstream gradients (36) and write their 236 gradient bytes.
+      preprocess_bwd, dense: every Gaussian reads its radius (4) and writes
+        its 236 gradient bytes; visible ones also read parameters and upstream
+        gradients (272)."""
     tot = 0.0
     for m in metas:
         P, V = m.get("P", 0), m.get("n_vis", 0)
+        L = int(m["n_list"]) if "n_list" in m else None
         if name == "preprocess_fwd":
-            tot += 56.0 * P + 224.0 * V
+            tot += (20.0 * P + 268.0 * L) if (L is not None and m.get("fused_count")) else (56.0 * P + 224.0 * V)
         elif name == "preprocess_bwd":
-            tot += 240.0 * P + 272.0 * V
+            tot += 508.0 * L if L is not None else (240.0 * P + 272.0 * V)
         else:
             return None
     return tot

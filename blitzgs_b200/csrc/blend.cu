@@ -17,6 +17,11 @@
 //     whose alpha is provably below 1/255 (margin 1e-3 in the exponent, far
 //     above the few-ulp error of logf/expf), so most pairs cost ~8 FP32
 //     instructions instead of ~30;
+//   * a conservative bounding box of each Gaussian's alpha >= 1/255 region
+//     drops it from the tile's batch when it misses the whole tile (a
+//     per-warp test on two pixel rows was tried and cost more than it saved;
+//     so did two pixels per thread, which cut instructions by a fifth but
+//     lost more in occupancy and early exit than it gained);
 //   * out_observe counts are aggregated per batch in shared memory and
 //     flushed with one atomic per (tile, Gaussian);
 //   * the per-tile statistics (n_render, n_consider, n_contrib) are reduced
@@ -43,30 +48,50 @@ __device__ __forceinline__ float skip_threshold(float o) {
   return __int_as_float(0xff800000);                  // NaN opacity: never pre-skip
 }
 
-// True when no pixel centre of the tile [tx0, tx0+15] x [ty0, ty0+15] can
-// give this Gaussian alpha >= 1/255, i.e. when every (pixel, Gaussian) pair of
-// the tile would be skipped by the per-pixel test.  The alpha >= 1/255 region
-// is the ellipse d^T C d <= 2 ln(255 o) (C = conic); its bounding box is
-// inflated for the float error of the per-pixel power (more for
-// ill-conditioned conics, whose terms cancel).  Degenerate conics and NaN
-// opacities are never culled.
-__device__ __forceinline__ bool tile_cull(float2 xy, float4 co, float tx0, float ty0) {
+// Conservative bounding box of the pixels where this Gaussian can reach
+// alpha >= 1/255: the ellipse d^T C d <= 2 ln(255 o) (C = conic), inflated
+// for the float error of the per-pixel power (more for ill-conditioned
+// conics, whose terms cancel).  An empty box (xmin > xmax) means no pixel
+// can pass; degenerate conics and NaN opacities get an infinite box (never
+// culled).  Every (pixel, Gaussian) pair outside the box is skipped by the
+// per-pixel test too, so skipping them wholesale changes no output.
+__device__ __forceinline__ float4 alpha_box(float2 xy, float4 co) {
+  const float inf = __int_as_float(0x7f800000);
   const float o = co.w;
-  if (o < 1.0f / 255.0f) return true;   // o * G <= o < 1/255 for every pixel
-  if (!(o >= 1.0f / 255.0f)) return false;  // NaN
+  if (o < 1.0f / 255.0f) return make_float4(inf, -inf, inf, -inf);  // o * G <= o < 1/255 everywhere
   const float det = co.x * co.z - co.y * co.y;
-  if (!(co.x > 0.f && co.z > 0.f && det > 0.f)) return false;
+  if (!(o >= 1.0f / 255.0f) || !(co.x > 0.f && co.z > 0.f && det > 0.f)) return make_float4(-inf, inf, -inf, inf);
   const float k = co.x * co.z / det;  // >= 1; large when the terms of the quadratic form cancel
   const float r2 = 2.f * logf(255.f * o) * (1.002f + 1e-5f * k) + 1e-3f;
   const float hx = sqrtf(r2 * co.z / det) + 0.01f;
   const float hy = sqrtf(r2 * co.x / det) + 0.01f;
-  if (!(hx < 1e30f && hy < 1e30f)) return false;
-  return (xy.x + hx < tx0) || (xy.x - hx > tx0 + 15.f) || (xy.y + hy < ty0) || (xy.y - hy > ty0 + 15.f);
+  if (!(hx < 1e30f && hy < 1e30f)) return make_float4(-inf, inf, -inf, inf);
+  return make_float4(xy.x - hx, xy.x + hx, xy.y - hy, xy.y + hy);
 }
 
-// Order-preserving compaction of the kept batch slots into s_list; returns
-// the number kept (same value in every thread).  Ends with a barrier.
-__device__ __forceinline__ int compact_batch(bool keep, int* s_wcnt, int* s_list) {
+// power = -0.5 (c00 dx^2 + c11 dy^2) - c01 dx dy, rounded as the reference
+// kernel rounds it: nvcc fuses the first product of each sum into an FMA when
+// every product has one use,
+//   sum = fma(c00 dx, dx, (c11 dy) dy),  power = fma(-0.5, sum, -(c01 dx) dy).
+// Spelled out so that the rounding cannot change with the code around it (a
+// product shared between two uses would be fused the other way round).  The
+// forward and the backward both call this, so their skip decisions agree bit
+// for bit.
+__device__ __forceinline__ float pair_power(float4 co, float2 d) {
+  const float sum = __fmaf_rn(__fmul_rn(co.x, d.x), d.x, __fmul_rn(__fmul_rn(co.z, d.y), d.y));
+  return __fmaf_rn(-0.5f, sum, -__fmul_rn(__fmul_rn(co.y, d.x), d.y));
+}
+
+// Does the box miss the pixel centres [x0, x1] x [y0, y1]?
+__device__ __forceinline__ bool box_misses(float4 b, float x0, float x1, float y0, float y1) {
+  return b.y < x0 || b.x > x1 || b.w < y0 || b.z > y1;
+}
+
+// Order-preserving compaction: returns this thread's slot among the kept
+// entries of the batch (-1 if not kept) and the number kept.  The caller
+// writes its staged data at that slot, so the blend loops read consecutive
+// slots with no index indirection.  Contains one barrier.
+__device__ __forceinline__ int compact_slot(bool keep, int* s_wcnt, int& kept) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const unsigned m = __ballot_sync(0xffffffffu, keep);
   if (lane == 0) s_wcnt[warp] = __popc(m);
@@ -78,9 +103,8 @@ __device__ __forceinline__ int compact_batch(bool keep, int* s_wcnt, int* s_list
     off += (w < warp) ? c : 0;
     tot += c;
   }
-  if (keep) s_list[off + __popc(m & ((1u << lane) - 1u))] = threadIdx.x;
-  __syncthreads();
-  return tot;
+  kept = tot;
+  return keep ? off + __popc(m & ((1u << lane) - 1u)) : -1;
 }
 
 __device__ __forceinline__ int block_sum_int(int v, int* s_red) {
@@ -151,27 +175,35 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
     if (num_done == kTilePix) break;
     const int k = r * kBatch + threadIdx.x;
     bool keep = false;
+    int id = 0;
+    float2 xy;
+    float4 co, cth;
     if (k < n) {
-      const int id = (int)p.point_list[range.x + k];
-      s_id[threadIdx.x] = id;
-      const float2 xy = reinterpret_cast<const float2*>(p.means2D)[id];
-      s_xy[threadIdx.x] = xy;
-      const float4 co = reinterpret_cast<const float4*>(p.conic_opacity)[id];
-      s_co[threadIdx.x] = co;
-      s_rgb[threadIdx.x] = make_float4(p.rgb[3 * (int64_t)id + 0], p.rgb[3 * (int64_t)id + 1],
-                                       p.rgb[3 * (int64_t)id + 2], skip_threshold(co.w));
-      keep = !tile_cull(xy, co, tx0, ty0);
+      id = (int)p.point_list[range.x + k];
+      xy = reinterpret_cast<const float2*>(p.means2D)[id];
+      co = reinterpret_cast<const float4*>(p.conic_opacity)[id];
+      cth = make_float4(p.rgb[3 * (int64_t)id + 0], p.rgb[3 * (int64_t)id + 1], p.rgb[3 * (int64_t)id + 2],
+                        skip_threshold(co.w));
+      keep = !box_misses(alpha_box(xy, co), tx0, tx0 + 15.f, ty0, ty0 + 15.f);
     }
-    s_obs[threadIdx.x] = 0;
-    const int kept = compact_batch(keep, s_wcnt, s_list);
+    int kept;
+    const int slot = compact_slot(keep, s_wcnt, kept);
+    if (slot >= 0) {
+      s_id[slot] = id;
+      s_xy[slot] = xy;
+      s_co[slot] = co;
+      s_rgb[slot] = cth;
+      s_list[slot] = r * kBatch + threadIdx.x + 1;  // 1-based list position, as the reference counts it
+      s_obs[slot] = 0;
+    }
+    __syncthreads();
 
-    for (int q = 0; !done && q < kept; ++q) {
-      const int j = s_list[q];
-      contributor = (uint32_t)(r * kBatch + j + 1);  // 1-based list position, as the reference counts it
+    for (int j = 0; !done && j < kept; ++j) {
+      contributor = (uint32_t)s_list[j];
       const float2 xy = s_xy[j];
       const float2 d = {xy.x - pixf.x, xy.y - pixf.y};
       const float4 con_o = s_co[j];
-      const float power = -0.5f * (con_o.x * d.x * d.x + con_o.z * d.y * d.y) - con_o.y * d.x * d.y;
+      const float power = pair_power(con_o, d);
       const float4 cth = s_rgb[j];
       if (power < cth.w) continue;  // alpha provably < 1/255
       if (power > 0.0f) continue;
@@ -191,7 +223,7 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
       last_contributor = contributor;
     }
     __syncthreads();
-    if (k < n && s_obs[threadIdx.x] > 0) atomicAdd(&p.out_observe[s_id[threadIdx.x]], s_obs[threadIdx.x]);
+    if (threadIdx.x < kept && s_obs[threadIdx.x] > 0) atomicAdd(&p.out_observe[s_id[threadIdx.x]], s_obs[threadIdx.x]);
   }
 
   if (inside) {
@@ -258,7 +290,7 @@ __device__ __forceinline__ float warp_transpose_reduce16(float v[16]) {
   return g + __shfl_xor_sync(0xffffffffu, g, 1);
 }
 
-__global__ void __launch_bounds__(kTilePix) blend_bwd_kernel(BlendBwdParams p) {
+__global__ void __launch_bounds__(kTilePix, 4) blend_bwd_kernel(BlendBwdParams p) {
   const int tile = blockIdx.x;
   if (p.compute_locally && !p.compute_locally[tile]) return;
   const int tx = tile % p.grid_x, ty = tile / p.grid_x;
@@ -312,28 +344,36 @@ __global__ void __launch_bounds__(kTilePix) blend_bwd_kernel(BlendBwdParams p) {
     __syncthreads();
     const int k = n_eff - 1 - (r * kBatch + (int)threadIdx.x);  // list position, back to front
     bool keep = false;
+    int id = 0;
+    float2 xy;
+    float4 co, cth;
     if (k >= 0) {
-      const int id = (int)p.point_list[range.x + k];
-      s_id[threadIdx.x] = id;
-      const float2 xy = reinterpret_cast<const float2*>(p.means2D)[id];
-      s_xy[threadIdx.x] = xy;
-      const float4 co = reinterpret_cast<const float4*>(p.conic_opacity)[id];
-      s_co[threadIdx.x] = co;
-      s_rgb[threadIdx.x] = make_float4(p.rgb[3 * (int64_t)id + 0], p.rgb[3 * (int64_t)id + 1],
-                                       p.rgb[3 * (int64_t)id + 2], skip_threshold(co.w));
-      keep = !tile_cull(xy, co, tx0, ty0);
+      id = (int)p.point_list[range.x + k];
+      xy = reinterpret_cast<const float2*>(p.means2D)[id];
+      co = reinterpret_cast<const float4*>(p.conic_opacity)[id];
+      cth = make_float4(p.rgb[3 * (int64_t)id + 0], p.rgb[3 * (int64_t)id + 1], p.rgb[3 * (int64_t)id + 2],
+                        skip_threshold(co.w));
+      keep = !box_misses(alpha_box(xy, co), tx0, tx0 + 15.f, ty0, ty0 + 15.f);
     }
-    const int kept = compact_batch(keep, s_wcnt, s_list);
-    for (int q = 0; q < kept; ++q) {
-      const int j = s_list[q];
-      const int pos = n_eff - 1 - (r * kBatch + j);
+    int kept;
+    const int slot = compact_slot(keep, s_wcnt, kept);
+    if (slot >= 0) {
+      s_id[slot] = id;
+      s_xy[slot] = xy;
+      s_co[slot] = co;
+      s_rgb[slot] = cth;
+      s_list[slot] = k;  // list position
+    }
+    __syncthreads();
+    for (int j = 0; j < kept; ++j) {
+      const int pos = s_list[j];
       float g[16];
       bool contrib = false;
       if (pos < last_contributor) {
         const float2 xy = s_xy[j];
         const float2 d = {xy.x - pixf.x, xy.y - pixf.y};
         const float4 con_o = s_co[j];
-        const float power = -0.5f * (con_o.x * d.x * d.x + con_o.z * d.y * d.y) - con_o.y * d.x * d.y;
+        const float power = pair_power(con_o, d);
         const float4 cth = s_rgb[j];
         if (power >= cth.w && !(power > 0.0f)) {
           const float G = expf(power);

@@ -158,13 +158,16 @@ int blitz_preprocess_forward_raw(int64_t P, int D, int M, const float* xyz, cons
                                  float tanfovx, float tanfovy, int image_height, int image_width,
                                  float* means2D, float* depths, int32_t* radii, float* conic_opacity,
                                  float* rgb, double* reg_sums, uint32_t* vis_list, int32_t* vis_count,
-                                 void* stream) {
+                                 const uint8_t* compute_locally, uint32_t* counts, uint64_t* totals,
+                                 void* scratch, size_t scratch_bytes, void* stream) {
   if (P < 0 || D < 0 || D > 3 || M < 0 || M > 15 || image_height <= 0 || image_width <= 0)
     return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: bad sizes");
   if (P == 0) return 0;
   if (!xyz || !scaling_raw || !rotation_raw || !opacity_raw || !sh_dc || !viewmatrix || !projmatrix || !campos ||
-      !means2D || !depths || !radii || !conic_opacity || !rgb || (M > 0 && !sh_rest) || ((vis_list == nullptr) != (vis_count == nullptr)))
+      !means2D || !depths || !radii || !conic_opacity || !rgb || (M > 0 && !sh_rest) || ((vis_list == nullptr) != (vis_count == nullptr)) ||
+      ((counts == nullptr) != (totals == nullptr)))
     return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: null pointer");
+  if (P >= (int64_t)0xffffffff) return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: P must be < 2^32");
   if (!aligned16(rotation_raw) || !aligned16(conic_opacity) || (reinterpret_cast<uintptr_t>(means2D) & 7u))
     return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: alignment");
   PreprocessParams p = make_pp(P, D, M, xyz, scaling_raw, rotation_raw, sh_dc, dc_stride, sh_rest, rest_stride,
@@ -175,13 +178,21 @@ int blitz_preprocess_forward_raw(int64_t P, int D, int M, const float* xyz, cons
   p.reg_sums = reg_sums;
   p.vis_list_out = vis_list;
   p.vis_count_out = vis_count;
+  p.listed_rows_only = vis_list != nullptr;
+  p.counts_out = counts;
+  p.totals_out = reinterpret_cast<unsigned long long*>(totals);
+  p.compute_locally = reinterpret_cast<const bool*>(compute_locally);
   p.out_means2D = means2D;
   p.out_depths = depths;
   p.out_radii = radii;
   p.out_conic_opacity = conic_opacity;
   p.out_rgb = rgb;
-  return check(launch_preprocess_fwd(p, S(stream)), "blitz_preprocess_forward_raw");
+  if (scratch && scratch_bytes < preprocess_scratch_bytes(P))
+    return fail(BLITZ_ESCRATCH, "blitz_preprocess_forward_raw: scratch smaller than blitz_preprocess_scratch_bytes(P)");
+  return check(launch_preprocess_fwd(p, S(stream), scratch, scratch_bytes), "blitz_preprocess_forward_raw");
 }
+
+size_t blitz_preprocess_scratch_bytes(int64_t P) { return preprocess_scratch_bytes(P); }
 
 int blitz_preprocess_backward_raw(int64_t P, int D, int M, const int32_t* radii, const float* means2D,
                                   const float* xyz, const float* scaling_raw, const float* rotation_raw,

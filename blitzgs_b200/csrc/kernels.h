@@ -47,6 +47,15 @@ struct PreprocessParams {
   double* reg_sums;          // raw mode, optional: {sum min-axis scale, count} over regulariser-visible
   uint32_t* vis_list_out;    // optional [P]: indices of Gaussians with radius > 0 (unordered)
   int* vis_count_out;        // device counter for vis_list_out, zero on entry
+  // Optional first pass of the binning, fused: per-Gaussian tile counts under
+  // the compute_locally mask and the totals {tile instances, Gaussians with a
+  // tile} (zeroed by the launcher).
+  uint32_t* counts_out;                // [P] or null
+  unsigned long long* totals_out;      // [2] or null
+  const bool* compute_locally;         // [grid_y*grid_x] or null (all tiles)
+  // Gaussians rejected before the full computation get only radii (and
+  // counts) written; the caller reads other rows through vis_list_out.
+  bool listed_rows_only;
 };
 
 struct PreprocessBwdParams {
@@ -74,7 +83,11 @@ struct PreprocessBwdParams {
   const int* vis_count;        // device count of vis_list
 };
 
-int launch_preprocess_fwd(const PreprocessParams& p, cudaStream_t st);
+// scratch (may be null): preprocess_scratch_bytes(P) bytes select the
+// two-kernel form (cull pass + full pass over the candidates).
+size_t preprocess_scratch_bytes(int64_t P);
+int launch_preprocess_fwd(const PreprocessParams& p, cudaStream_t st, void* scratch = nullptr,
+                          size_t scratch_bytes = 0);
 int launch_preprocess_bwd(const PreprocessBwdParams& p, bool accumulate, cudaStream_t st);
 
 // ---------------------------------------------------------------------------

@@ -15,6 +15,8 @@
 // Backward fuses the reference's computeCov2DCUDA and preprocessCUDA
 // (backward.cu:146-400) into one kernel and recomputes cov3D and the
 // clamp flags instead of reading them back from saved buffers.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -64,9 +66,12 @@ __device__ __forceinline__ void load_sh(const PreprocessParams& p, int64_t i, in
 __device__ __forceinline__ float act_sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
 
 __device__ __forceinline__ float quat_norm(float4 q) {
-  // squares rounded individually, summed left to right, then sqrt
-  const float a = q.x * q.x, b = q.y * q.y, c = q.z * q.z, d = q.w * q.w;
-  return sqrtf(__fadd_rn(__fadd_rn(__fadd_rn(a, b), c), d));
+  // ||q|| as PyTorch's CUDA norm over a contiguous [P,4] row computes it:
+  // squares rounded individually, then (x0^2 + x2^2) + (x1^2 + x3^2), then a
+  // correctly rounded sqrt (bit-identical on 4M random quaternions; checked
+  // by tests/test_gpu_parity.py).
+  const float a = __fmul_rn(q.x, q.x), b = __fmul_rn(q.y, q.y), c = __fmul_rn(q.z, q.z), d = __fmul_rn(q.w, q.w);
+  return __fsqrt_rn(__fadd_rn(__fadd_rn(a, c), __fadd_rn(b, d)));
 }
 
 struct Activated {
@@ -101,47 +106,115 @@ __device__ __forceinline__ Activated activate(const PreprocessParams& p, int64_t
   return a;
 }
 
-__global__ void __launch_bounds__(256) preprocess_fwd_kernel(PreprocessParams p) {
-  const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const bool valid = i0 < p.P;
-  const int64_t i = valid ? i0 : p.P - 1;  // tail threads recompute the last Gaussian, store nothing
+// ---------------------------------------------------------------------------
+// Forward
+// ---------------------------------------------------------------------------
+//
+// Two phases inside one persistent kernel.  In a training view only a few
+// percent of the Gaussians survive the frustum cull, so a thread-per-Gaussian
+// kernel spends its time waiting on one 12-byte xyz load per thread.
+//   Phase A (streaming cull): each block takes chunks of kPreChunk Gaussians;
+//     every thread loads xyz (and the scales of Gaussians in front of the near
+//     plane) of kPreUnroll Gaussians at once and applies a conservative
+//     screen-space bound.  Gaussians it rejects are certain to get radius 0
+//     from the full computation; their rows are written here.
+//   Phase B (full computation): the survivors are queued in shared memory and
+//     processed a full block at a time, so every lane does useful work.
+// Outputs are those of the reference preprocessCUDA bit for bit; phase A only
+// decides who can skip the full computation.
 
-  const float* V = p.viewmatrix;
-  const float* Pm = p.projmatrix;
-  float Vs[16], Ps[16];
-#pragma unroll
-  for (int k = 0; k < 16; ++k) {
-    Vs[k] = __ldg(V + k);
-    Ps[k] = __ldg(Pm + k);
-  }
+constexpr int kPreThreads = 256;
+constexpr int kPreUnroll = 8;
+constexpr int kPreChunk = kPreThreads * kPreUnroll;
+constexpr int kPreQueue = kPreChunk + kPreThreads;  // < kPreThreads carried over + one chunk
+constexpr int kPreMaskSmem = 32 * 1024;             // tiles whose mask is staged in shared memory
 
+// Everything the full computation produces for one Gaussian.
+struct PreResult {
+  float2 pimg;
+  float depth;
+  int radius;
+  float4 conic_op;
+  V3 rgb;
+  bool clamp3[3];
+  float cov3d[6];
+  float smin;  // smallest activated scale (regulariser)
+};
+
+// Squared Frobenius norm of the rotation matrix built from q.
+__device__ __forceinline__ float rot_frob2(float4 q) {
+  const float r00 = 1.f - 2.f * (q.z * q.z + q.w * q.w), r01 = 2.f * (q.y * q.z - q.x * q.w), r02 = 2.f * (q.y * q.w + q.x * q.z);
+  const float r10 = 2.f * (q.y * q.z + q.x * q.w), r11 = 1.f - 2.f * (q.y * q.y + q.w * q.w), r12 = 2.f * (q.z * q.w - q.x * q.y);
+  const float r20 = 2.f * (q.y * q.w - q.x * q.z), r21 = 2.f * (q.z * q.w + q.x * q.y), r22 = 1.f - 2.f * (q.y * q.y + q.z * q.z);
+  return r00 * r00 + r01 * r01 + r02 * r02 + r10 * r10 + r11 * r11 + r12 * r12 + r20 * r20 + r21 * r21 + r22 * r22;
+}
+
+// Conservative screen-space bound.  The tile rect of the full computation uses
+// half-extents <= my_radius = extent * sqrt(lambda) with extent <= 3.33,
+// lambda <= trace(cov2D) + 0.1 and trace(cov2D) <= s_max^2 ||R||_F^2
+// ||J||_F^2 ||W||_F^2 + 0.6 (W the view rotation, R the rotation matrix, S the
+// scales), where |t.x/t.z| is clamped to 1.3 tan(fov) inside J.  If even that
+// radius keeps the rect outside the tile grid, the full computation would cull
+// the Gaussian too.  NaNs never make it return true.
+struct CullBound {
+  float wf;    // ||W||_F^2
+  float jnum;  // ||J||_F^2 * z^2
+  float gw, gh;
+};
+
+__device__ __forceinline__ CullBound make_cull_bound(const PreprocessParams& p, const float* Vs) {
+  CullBound c;
+  c.wf = Vs[0] * Vs[0] + Vs[1] * Vs[1] + Vs[2] * Vs[2] + Vs[4] * Vs[4] + Vs[5] * Vs[5] + Vs[6] * Vs[6] + Vs[8] * Vs[8] +
+         Vs[9] * Vs[9] + Vs[10] * Vs[10];
+  const float cx = 1.3f * p.tanfovx, cy = 1.3f * p.tanfovy;
+  c.jnum = p.focal_x * p.focal_x * (1.f + cx * cx) + p.focal_y * p.focal_y * (1.f + cy * cy);
+  c.gw = (float)(p.grid_x * kTileX);
+  c.gh = (float)(p.grid_y * kTileY);
+  return c;
+}
+
+__device__ __forceinline__ bool off_grid(const CullBound& c, float2 pimg, float z, float smax, float rf) {
+  const float jf = c.jnum / (z * z);
+  const float rb = 3.34f * sqrtf((smax * smax * rf * jf * c.wf + 0.8f) * 1.01f) + 2.f;
+  return pimg.x + rb < -1.f || pimg.x - rb > c.gw + 1.f || pimg.y + rb < -1.f || pimg.y - rb > c.gh + 1.f;
+}
+
+// The reference per-Gaussian computation (forward.cu:164-284) for one
+// Gaussian that passed phase A.
+__device__ __forceinline__ void preprocess_one(const PreprocessParams& p, const float* Vs, const float* Ps,
+                                               const CullBound& cb, int64_t i, PreResult& r) {
   const float3 p_orig = make_float3(__ldg(p.means3D + 3 * i + 0), __ldg(p.means3D + 3 * i + 1),
                                     __ldg(p.means3D + 3 * i + 2));
-
-  float2 point_image = make_float2(0.f, 0.f);
-  float depth = 0.f;
-  int radius = 0;
-  float4 conic_op = make_float4(0.f, 0.f, 0.f, 0.f);
-  V3 rgb = {0.f, 0.f, 0.f};
-  bool clamp3[3] = {false, false, false};
-  float cov3d[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  Activated act;
-  act.sx = act.sy = act.sz = 0.f;
+  r.pimg = make_float2(0.f, 0.f);
+  r.depth = 0.f;
+  r.radius = 0;
+  r.conic_op = make_float4(0.f, 0.f, 0.f, 0.f);
+  r.rgb = {0.f, 0.f, 0.f};
+  r.clamp3[0] = r.clamp3[1] = r.clamp3[2] = false;
+#pragma unroll
+  for (int k = 0; k < 6; ++k) r.cov3d[k] = 0.f;
+  r.smin = 0.f;
 
   do {
     // near-plane test (reference in_frustum, auxiliary.h:156-185)
     const float3 p_view = xform_point3(p_orig, Vs);
     if (p_view.z <= 0.2f) {
-      if (p.prefiltered && valid) atomicOr(p.error_flag, kErrPrefilteredCulled);
+      if (p.prefiltered) atomicOr(p.error_flag, kErrPrefilteredCulled);
       break;
     }
     const float4 p_hom = xform_point4(p_orig, Ps);
     const float p_w = 1.0f / (p_hom.w + 0.0000001f);
     const float3 p_proj = make_float3(p_hom.x * p_w, p_hom.y * p_w, p_hom.z * p_w);
+    const float2 pimg = make_float2(ndc_to_pix(p_proj.x, p.W), ndc_to_pix(p_proj.y, p.H));
 
-    act = activate(p, i);
-    cov3d_from_scale_rot(act.sx, act.sy, act.sz, p.scale_modifier, act.q, cov3d);
-    const float3 cov = cov2d_ewa(p_orig, p.focal_x, p.focal_y, p.tanfovx, p.tanfovy, cov3d, Vs);
+    const Activated act = activate(p, i);
+    r.smin = fminf(act.sx, fminf(act.sy, act.sz));
+    // the bound again, now with the rotation's own ||R||_F^2
+    const float smax = fabsf(p.scale_modifier) * fmaxf(fabsf(act.sx), fmaxf(fabsf(act.sy), fabsf(act.sz)));
+    if (off_grid(cb, pimg, p_view.z, smax, rot_frob2(act.q))) break;
+
+    cov3d_from_scale_rot(act.sx, act.sy, act.sz, p.scale_modifier, act.q, r.cov3d);
+    const float3 cov = cov2d_ewa(p_orig, p.focal_x, p.focal_y, p.tanfovx, p.tanfovy, r.cov3d, Vs);
 
     const float det = (cov.x * cov.z - cov.y * cov.y);
     if (det == 0.0f) break;
@@ -161,90 +234,368 @@ __global__ void __launch_bounds__(256) preprocess_fwd_kernel(PreprocessParams p)
     const float my_radius = extent * sqrtf(lambda);
     if (my_radius <= 0.0f) break;
 
-    const float2 pimg = make_float2(ndc_to_pix(p_proj.x, p.W), ndc_to_pix(p_proj.y, p.H));
     const float extent_x = fminf(extent * sqrtf(cov.x), my_radius);
     const float extent_y = fminf(extent * sqrtf(cov.z), my_radius);
     if (tile_rect_f_count(pimg, make_float2(extent_x, extent_y), p.grid_x, p.grid_y) == 0) break;
 
     ShRegs s;
     load_sh(p, i, p.M, s);
-    rgb = sh_to_rgb(p.D, p_orig, p.campos, s.dc, s.rest, clamp3);
+    r.rgb = sh_to_rgb(p.D, p_orig, p.campos, s.dc, s.rest, r.clamp3);
 
-    depth = p_view.z;
-    radius = (int)ceilf(my_radius);
-    point_image = pimg;
-    conic_op = make_float4(conic.x, conic.y, conic.z, opacity);
+    r.depth = p_view.z;
+    r.radius = (int)ceilf(my_radius);
+    r.pimg = pimg;
+    r.conic_op = make_float4(conic.x, conic.y, conic.z, opacity);
   } while (0);
+}
 
-  // Block-level aggregation of the optional outputs: one atomic per block on
-  // each counter (a per-warp atomic on one address serialises in L2).
-  if (p.reg_sums || p.vis_list_out) {
-    __shared__ float s_rv[8], s_rc[8];
-    __shared__ int s_wc[8];
-    __shared__ int s_base;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    // min-scale regulariser (gaussian_renderer/loss_distribution.py:314-322):
-    // Gaussians the exchange sends (radius > 0 and a non-empty square tile
-    // rect, the get_local2j_ids test) contribute their smallest scale.
-    float v = 0.f, c = 0.f;
-    if (p.reg_sums && valid && radius > 0) {
-      int2 lo, hi;
-      tile_rect_int(point_image, radius, p.grid_x, p.grid_y, lo, hi);
-      if ((hi.y - 1) * p.grid_x + hi.x - 1 >= lo.y * p.grid_x + lo.x) {
-        v = fminf(act.sx, fminf(act.sy, act.sz));
-        c = 1.f;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      v += __shfl_xor_sync(0xffffffffu, v, o);
-      c += __shfl_xor_sync(0xffffffffu, c, o);
-    }
-    const bool listed = valid && radius > 0;
-    const unsigned m = __ballot_sync(0xffffffffu, listed);
-    if (lane == 0) {
-      s_rv[warp] = v;
-      s_rc[warp] = c;
-      s_wc[warp] = __popc(m);
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      double bv = 0.0, bc = 0.0;
-      int tot = 0;
-      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
-        bv += s_rv[w];
-        bc += s_rc[w];
-        const int n = s_wc[w];
-        s_wc[w] = tot;  // exclusive offset of warp w
-        tot += n;
-      }
-      if (p.reg_sums && bc > 0) {
-        atomicAdd(p.reg_sums + 0, bv);
-        atomicAdd(p.reg_sums + 1, bc);
-      }
-      s_base = (p.vis_list_out && tot) ? atomicAdd(p.vis_count_out, tot) : 0;
-    }
-    __syncthreads();
-    if (p.vis_list_out && listed)
-      p.vis_list_out[s_base + s_wc[warp] + __popc(m & ((1u << lane) - 1u))] = (uint32_t)i;
-  }
-  if (!valid) return;
-  reinterpret_cast<float2*>(p.out_means2D)[i] = point_image;
-  p.out_depths[i] = depth;
-  p.out_radii[i] = radius;
-  reinterpret_cast<float4*>(p.out_conic_opacity)[i] = conic_op;
-  p.out_rgb[3 * i + 0] = rgb.x;
-  p.out_rgb[3 * i + 1] = rgb.y;
-  p.out_rgb[3 * i + 2] = rgb.z;
+__device__ __forceinline__ void store_one(const PreprocessParams& p, int64_t i, const PreResult& r) {
+  reinterpret_cast<float2*>(p.out_means2D)[i] = r.pimg;
+  p.out_depths[i] = r.depth;
+  p.out_radii[i] = r.radius;
+  reinterpret_cast<float4*>(p.out_conic_opacity)[i] = r.conic_op;
+  p.out_rgb[3 * i + 0] = r.rgb.x;
+  p.out_rgb[3 * i + 1] = r.rgb.y;
+  p.out_rgb[3 * i + 2] = r.rgb.z;
   if (p.out_clamped) {
-    p.out_clamped[3 * i + 0] = clamp3[0];
-    p.out_clamped[3 * i + 1] = clamp3[1];
-    p.out_clamped[3 * i + 2] = clamp3[2];
+    p.out_clamped[3 * i + 0] = r.clamp3[0];
+    p.out_clamped[3 * i + 1] = r.clamp3[1];
+    p.out_clamped[3 * i + 2] = r.clamp3[2];
   }
   if (p.out_cov3D) {
 #pragma unroll
-    for (int k = 0; k < 6; ++k) p.out_cov3D[6 * i + k] = cov3d[k];
+    for (int k = 0; k < 6; ++k) p.out_cov3D[6 * i + k] = r.cov3d[k];
   }
+}
+
+// Rows of a Gaussian rejected in phase A: zeros, like the reference's
+// zero-initialised outputs.  With listed_rows_only, only radii (and counts)
+// are written: the caller reads the other outputs through the visible list.
+__device__ __forceinline__ void store_culled(const PreprocessParams& p, int64_t i) {
+  p.out_radii[i] = 0;
+  if (p.counts_out) p.counts_out[i] = 0u;
+  if (p.listed_rows_only) return;
+  reinterpret_cast<float2*>(p.out_means2D)[i] = make_float2(0.f, 0.f);
+  p.out_depths[i] = 0.f;
+  reinterpret_cast<float4*>(p.out_conic_opacity)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  p.out_rgb[3 * i + 0] = 0.f;
+  p.out_rgb[3 * i + 1] = 0.f;
+  p.out_rgb[3 * i + 2] = 0.f;
+  if (p.out_clamped) {
+    p.out_clamped[3 * i + 0] = false;
+    p.out_clamped[3 * i + 1] = false;
+    p.out_clamped[3 * i + 2] = false;
+  }
+  if (p.out_cov3D) {
+#pragma unroll
+    for (int k = 0; k < 6; ++k) p.out_cov3D[6 * i + k] = 0.f;
+  }
+}
+
+// Per-thread running sums of one block, reduced once at the end of a kernel.
+struct FwdAcc {
+  double reg_v = 0.0, reg_c = 0.0;      // regulariser: sum of min scales, count
+  unsigned long long r = 0ull, n = 0ull;  // tile instances, Gaussians with a tile
+};
+
+// Phase A for the kPreUnroll Gaussians base + u*kPreThreads of this thread:
+// keep[u] is false only for Gaussians the full computation is certain to cull
+// (their rows are written here).  Every test is conservative, so fast
+// approximate arithmetic is enough: the near plane is tested with a margin
+// and the exact test is repeated in phase B.
+__device__ __forceinline__ void cull_phase(const PreprocessParams& p, const float* Vs, const float* Ps,
+                                           const CullBound& cb, int64_t base, bool (&keep)[kPreUnroll]) {
+  // Without a rotation load, ||R||_F^2 <= 9: every entry of R is bounded by
+  // |q|^2 <= 1 when q was normalised here.  A caller-supplied norm or an
+  // operator-API rotation can have any length, so those load q.
+  const bool load_q = !p.raw || p.rot_norm;
+  const float abs_mod = fabsf(p.scale_modifier);
+  // per-thread base pointers: Gaussian base + u * kPreThreads sits at a
+  // compile-time offset from them
+  const int64_t rem = p.P - base;  // Gaussians from base on
+  const float* xb = p.means3D + 3 * base;
+  const float* sb = p.scales + 3 * base;
+  // xyz and the scales in one round trip (the scales of Gaussians behind the
+  // camera are read for nothing, which costs less than a second round trip)
+  float3 x[kPreUnroll], sc[kPreUnroll];
+#pragma unroll
+  for (int u = 0; u < kPreUnroll; ++u) {
+    x[u] = make_float3(0.f, 0.f, 0.f);
+    sc[u] = make_float3(0.f, 0.f, 0.f);
+    if (u * kPreThreads < rem) {
+      const int o = 3 * u * kPreThreads;
+      x[u] = make_float3(__ldg(xb + o + 0), __ldg(xb + o + 1), __ldg(xb + o + 2));
+      sc[u] = make_float3(__ldg(sb + o + 0), __ldg(sb + o + 1), __ldg(sb + o + 2));
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < kPreUnroll; ++u) {
+    const bool in = u * kPreThreads < rem;
+    const float z = Vs[2] * x[u].x + Vs[6] * x[u].y + Vs[10] * x[u].z + Vs[14];
+    keep[u] = in && z > 0.19999f;
+    // the exact near test (z <= 0.2 culls) runs in phase B; here only what
+    // is clearly behind it is dropped and reported
+    if (in && !keep[u] && p.prefiltered) atomicOr(p.error_flag, kErrPrefilteredCulled);
+    if (keep[u]) {
+      float m = fmaxf(fabsf(sc[u].x), fmaxf(fabsf(sc[u].y), fabsf(sc[u].z)));
+      if (p.raw) m = __expf(fmaxf(sc[u].x, fmaxf(sc[u].y, sc[u].z)));  // exp is increasing: exp(max) = max(exp)
+      const float smax = abs_mod * m * 1.0001f;
+      float rf = 9.001f;
+      if (load_q) {
+        const int64_t i = base + u * kPreThreads;
+        float4 q = __ldg(reinterpret_cast<const float4*>(p.rotations) + i);
+        if (p.raw) {
+          const float inv = 1.f / fmaxf(__ldg(p.rot_norm + i), 1e-12f);
+          q = make_float4(q.x * inv, q.y * inv, q.z * inv, q.w * inv);
+        }
+        rf = rot_frob2(q) * 1.0001f + 1e-6f;
+      }
+      const float hx = Ps[0] * x[u].x + Ps[4] * x[u].y + Ps[8] * x[u].z + Ps[12];
+      const float hy = Ps[1] * x[u].x + Ps[5] * x[u].y + Ps[9] * x[u].z + Ps[13];
+      const float hw = Ps[3] * x[u].x + Ps[7] * x[u].y + Ps[11] * x[u].z + Ps[15];
+      const float pw = __fdividef(1.f, hw + 0.0000001f);
+      const float2 pimg = make_float2(((hx * pw + 1.f) * (float)p.W - 1.f) * 0.5f,
+                                      ((hy * pw + 1.f) * (float)p.H - 1.f) * 0.5f);
+      const float jf = __fdividef(cb.jnum, z * z);
+      const float v = (smax * smax * rf * jf * cb.wf + 0.8f) * 1.01f;
+      const float rb = 3.34f * (v * rsqrtf(v)) * 1.0001f + 2.f;
+      keep[u] = !(pimg.x + rb < -1.f || pimg.x - rb > cb.gw + 1.f || pimg.y + rb < -1.f || pimg.y - rb > cb.gh + 1.f);
+    }
+    if (in && !keep[u]) store_culled(p, base + u * kPreThreads);
+  }
+}
+
+// Phase B for one Gaussian (valid) or a filler lane: full computation, the
+// fused tile count and regulariser, the block-aggregated visible-list slot
+// (three barriers: every thread of the block must call this together), and
+// the row stores.
+__device__ __forceinline__ void full_phase(const PreprocessParams& p, const float* Vs, const float* Ps,
+                                           const CullBound& cb, int64_t i, bool valid, const bool* s_mask,
+                                           bool use_smem, int* s_wc, int* s_base, FwdAcc& acc) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  PreResult res;
+  preprocess_one(p, Vs, Ps, cb, i, res);
+  uint32_t cnt = 0;
+  if (valid && res.radius > 0 && (p.counts_out || p.reg_sums)) {
+    int2 lo, hi;
+    tile_rect_int(res.pimg, res.radius, p.grid_x, p.grid_y, lo, hi);
+    // min-scale regulariser (gaussian_renderer/loss_distribution.py:314-322):
+    // Gaussians the exchange sends (radius > 0 and a non-empty square tile
+    // rect, the get_local2j_ids test) contribute their smallest scale.
+    if (p.reg_sums && (hi.y - 1) * p.grid_x + hi.x - 1 >= lo.y * p.grid_x + lo.x) {
+      acc.reg_v += res.smin;
+      acc.reg_c += 1.0;
+    }
+    // tile count of the binning (the sizing pass before duplicateWithKeys,
+    // rasterizer_impl.cu), restricted to the tiles this rank renders
+    if (p.counts_out) {
+      if (!p.compute_locally) {
+        cnt = (uint32_t)((hi.x - lo.x) * (hi.y - lo.y));
+      } else {
+        for (int y = lo.y; y < hi.y; ++y)
+          for (int xx = lo.x; xx < hi.x; ++xx) {
+            const int t = y * p.grid_x + xx;
+            cnt += (use_smem ? s_mask[t] : p.compute_locally[t]) ? 1u : 0u;
+          }
+      }
+    }
+  }
+  acc.r += cnt;
+  acc.n += cnt > 0u ? 1ull : 0ull;
+  if (p.vis_list_out) {
+    // block-aggregated slots: one atomic per block and round
+    const bool listed = valid && res.radius > 0;
+    const unsigned m = __ballot_sync(0xffffffffu, listed);
+    if (lane == 0) s_wc[warp] = __popc(m);
+    __syncthreads();
+    if (tid == 0) {
+      int tot = 0;
+      for (int w = 0; w < kPreThreads / 32; ++w) {
+        const int n = s_wc[w];
+        s_wc[w] = tot;
+        tot += n;
+      }
+      *s_base = tot ? atomicAdd(p.vis_count_out, tot) : 0;
+    }
+    __syncthreads();
+    if (listed) p.vis_list_out[*s_base + s_wc[warp] + __popc(m & ((1u << lane) - 1u))] = (uint32_t)i;
+    __syncthreads();  // s_wc / s_base are rewritten next round
+  }
+  if (valid) {
+    store_one(p, i, res);
+    if (p.counts_out) p.counts_out[i] = cnt;
+  }
+}
+
+// One atomic per block and counter.
+__device__ __forceinline__ void flush_totals(const PreprocessParams& p, FwdAcc acc) {
+  __shared__ double s_rd[2][kPreThreads / 32];
+  __shared__ unsigned long long s_rt[2][kPreThreads / 32];
+  if (!p.reg_sums && !p.totals_out) return;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    acc.reg_v += __shfl_xor_sync(0xffffffffu, acc.reg_v, o);
+    acc.reg_c += __shfl_xor_sync(0xffffffffu, acc.reg_c, o);
+    acc.r += __shfl_xor_sync(0xffffffffu, acc.r, o);
+    acc.n += __shfl_xor_sync(0xffffffffu, acc.n, o);
+  }
+  if (lane == 0) {
+    s_rd[0][warp] = acc.reg_v;
+    s_rd[1][warp] = acc.reg_c;
+    s_rt[0][warp] = acc.r;
+    s_rt[1][warp] = acc.n;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double bv = 0.0, bc = 0.0;
+    unsigned long long br = 0ull, bn = 0ull;
+    for (int w = 0; w < kPreThreads / 32; ++w) {
+      bv += s_rd[0][w];
+      bc += s_rd[1][w];
+      br += s_rt[0][w];
+      bn += s_rt[1][w];
+    }
+    if (p.reg_sums && bc > 0) {
+      atomicAdd(p.reg_sums + 0, bv);
+      atomicAdd(p.reg_sums + 1, bc);
+    }
+    if (p.totals_out && (br | bn)) {
+      atomicAdd(p.totals_out + 0, br);
+      atomicAdd(p.totals_out + 1, bn);
+    }
+  }
+}
+
+__device__ __forceinline__ void load_camera(const PreprocessParams& p, float* Vs, float* Ps) {
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    Vs[k] = __ldg(p.viewmatrix + k);
+    Ps[k] = __ldg(p.projmatrix + k);
+  }
+}
+
+// Stage the compute_locally tile mask in shared memory when counts are asked
+// for and it fits.  Returns whether it was staged (no barrier here).
+__device__ __forceinline__ bool stage_mask(const PreprocessParams& p, bool* s_mask) {
+  const int n_tiles = p.grid_x * p.grid_y;
+  const bool use_smem = p.counts_out && p.compute_locally && n_tiles <= kPreMaskSmem;
+  if (use_smem)
+    for (int t = threadIdx.x; t < n_tiles; t += kPreThreads) s_mask[t] = p.compute_locally[t];
+  return use_smem;
+}
+
+// Single-kernel form (no scratch): persistent blocks run phase A over chunks
+// and phase B over the survivors queued in shared memory, a full block at a
+// time.
+__global__ void __launch_bounds__(kPreThreads, 2) preprocess_fwd_kernel(PreprocessParams p) {
+  extern __shared__ bool s_mask[];  // n_tiles bytes when the tile mask is staged
+  __shared__ uint32_t s_queue[kPreQueue];
+  __shared__ int s_qn, s_base;
+  __shared__ int s_wc[kPreThreads / 32];
+
+  const int tid = threadIdx.x, lane = tid & 31;
+  const bool use_smem = stage_mask(p, s_mask);
+  if (tid == 0) s_qn = 0;
+  float Vs[16], Ps[16];
+  load_camera(p, Vs, Ps);
+  const CullBound cb = make_cull_bound(p, Vs);
+  FwdAcc acc;
+  const int64_t n_chunks = (p.P + kPreChunk - 1) / kPreChunk;
+  __syncthreads();
+
+  for (int64_t chunk = blockIdx.x; chunk < n_chunks; chunk += gridDim.x) {
+    const bool last = chunk + gridDim.x >= n_chunks;
+    const int64_t base = chunk * kPreChunk + tid;
+    bool keep[kPreUnroll];
+    cull_phase(p, Vs, Ps, cb, base, keep);
+#pragma unroll
+    for (int u = 0; u < kPreUnroll; ++u) {
+      const unsigned m = __ballot_sync(0xffffffffu, keep[u]);
+      int wbase = 0;
+      if (lane == 0 && m) wbase = atomicAdd(&s_qn, __popc(m));
+      wbase = __shfl_sync(0xffffffffu, wbase, 0);
+      if (keep[u]) s_queue[wbase + __popc(m & ((1u << lane) - 1u))] = (uint32_t)(base + u * kPreThreads);
+    }
+    __syncthreads();
+    const int qn = s_qn;
+    __syncthreads();  // everyone has read s_qn before anyone changes it
+    if (qn < kPreThreads && !(last && qn > 0)) continue;
+
+    const int n_proc = last ? qn : (qn / kPreThreads) * kPreThreads;
+    for (int r0 = 0; r0 < n_proc; r0 += kPreThreads) {
+      const bool valid = r0 + tid < n_proc;
+      full_phase(p, Vs, Ps, cb, s_queue[valid ? r0 + tid : r0], valid, s_mask, use_smem, s_wc, &s_base, acc);
+    }
+    // carry the remainder (< kPreThreads entries) to the front of the queue;
+    // sources sit at >= n_proc >= kPreThreads > destinations
+    const int rem = qn - n_proc;
+    const uint32_t carry = tid < rem ? s_queue[n_proc + tid] : 0u;
+    __syncthreads();
+    if (tid < rem) s_queue[tid] = carry;
+    if (tid == 0) s_qn = rem;
+    __syncthreads();
+  }
+  flush_totals(p, acc);
+}
+
+// Two-kernel form (caller scratch).  Phase A alone, at high occupancy: one
+// chunk per block; survivors are appended to a candidate list in ascending
+// index order within the block (one atomic per block).
+__global__ void __launch_bounds__(kPreThreads, 4) preprocess_cull_kernel(PreprocessParams p, uint32_t* cand,
+                                                                          int* cand_count) {
+  __shared__ int s_off[kPreUnroll][kPreThreads / 32];
+  __shared__ int s_base;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float Vs[16], Ps[16];
+  load_camera(p, Vs, Ps);
+  const CullBound cb = make_cull_bound(p, Vs);
+  const int64_t base = (int64_t)blockIdx.x * kPreChunk + tid;
+  bool keep[kPreUnroll];
+  cull_phase(p, Vs, Ps, cb, base, keep);
+  unsigned m[kPreUnroll];
+#pragma unroll
+  for (int u = 0; u < kPreUnroll; ++u) {
+    m[u] = __ballot_sync(0xffffffffu, keep[u]);
+    if (lane == 0) s_off[u][warp] = __popc(m[u]);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int tot = 0;
+    for (int u = 0; u < kPreUnroll; ++u)
+      for (int w = 0; w < kPreThreads / 32; ++w) {
+        const int c = s_off[u][w];
+        s_off[u][w] = tot;
+        tot += c;
+      }
+    s_base = tot ? atomicAdd(cand_count, tot) : 0;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int u = 0; u < kPreUnroll; ++u)
+    if (keep[u]) cand[s_base + s_off[u][warp] + __popc(m[u] & ((1u << lane) - 1u))] = (uint32_t)(base + u * kPreThreads);
+}
+
+// Phase B over the candidate list: persistent blocks take whole rounds of
+// kPreThreads candidates.
+__global__ void __launch_bounds__(kPreThreads, 2) preprocess_full_kernel(PreprocessParams p, const uint32_t* cand,
+                                                                          const int* cand_count) {
+  extern __shared__ bool s_mask[];
+  __shared__ int s_base;
+  __shared__ int s_wc[kPreThreads / 32];
+  const int tid = threadIdx.x;
+  const bool use_smem = stage_mask(p, s_mask);
+  float Vs[16], Ps[16];
+  load_camera(p, Vs, Ps);
+  const CullBound cb = make_cull_bound(p, Vs);
+  FwdAcc acc;
+  const int n = *cand_count;
+  __syncthreads();
+  for (int r0 = blockIdx.x * kPreThreads; r0 < n; r0 += gridDim.x * kPreThreads) {
+    const bool valid = r0 + tid < n;
+    full_phase(p, Vs, Ps, cb, cand[valid ? r0 + tid : r0], valid, s_mask, use_smem, s_wc, &s_base, acc);
+  }
+  flush_totals(p, acc);
 }
 
 // ---------------------------------------------------------------------------
@@ -559,35 +910,45 @@ __device__ __forceinline__ void bwd_compute(const PreprocessBwdParams& p, int64_
 // Backward over a compact list of visible Gaussians (raw mode): every lane
 // does useful work; gradients are added into pre-zeroed (or accumulating)
 // outputs.
-__global__ void __launch_bounds__(128) preprocess_bwd_list_kernel(PreprocessBwdParams p) {
-  const PreprocessParams& f = p.f;
-  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (j >= *p.vis_count) return;
-  const int64_t i = p.vis_list[j];
+template <bool ACC>
+__device__ __forceinline__ void list_one(const PreprocessBwdParams& p, const PreprocessParams& f, int64_t i) {
   const float4 gco = *reinterpret_cast<const float4*>(p.g_conic_opacity + i * p.g_conic_stride);
   BwdOut o;
   bwd_zero(o);
   bwd_compute(p, i, gco, o);
 #pragma unroll
   for (int k = 0; k < 3; ++k) {
-    p.g_means3D[3 * i + k] += o.mean[k];
-    p.g_scales[3 * i + k] += o.scale[k];
+    put<ACC>(p.g_means3D + 3 * i + k, o.mean[k]);
+    put<ACC>(p.g_scales + 3 * i + k, o.scale[k]);
   }
   float4* r = reinterpret_cast<float4*>(p.g_rotations) + i;
-  float4 a = *r;
-  a.x += o.rot.x;
-  a.y += o.rot.y;
-  a.z += o.rot.z;
-  a.w += o.rot.w;
-  *r = a;
-  if (p.g_opacities) p.g_opacities[i] += o.op;
+  if (ACC) {
+    float4 a = *r;
+    a.x += o.rot.x;
+    a.y += o.rot.y;
+    a.z += o.rot.z;
+    a.w += o.rot.w;
+    *r = a;
+  } else {
+    *r = o.rot;
+  }
+  if (p.g_opacities) put<ACC>(p.g_opacities + i, o.op);
   float* gd = p.g_dc + i * p.g_dc_stride;
   float* gr = p.g_rest + i * p.g_rest_stride;
 #pragma unroll
-  for (int k = 0; k < 3; ++k) gd[k] += o.dc[k];
+  for (int k = 0; k < 3; ++k) put<ACC>(gd + k, o.dc[k]);
 #pragma unroll
   for (int k = 0; k < 45; ++k)
-    if (k < f.M * 3) gr[k] += o.rest[k];
+    if (k < f.M * 3) put<ACC>(gr + k, o.rest[k]);
+}
+
+template <bool ACC>
+__global__ void __launch_bounds__(128) preprocess_bwd_list_kernel(PreprocessBwdParams p) {
+  const PreprocessParams& f = p.f;
+  const int64_t n = *p.vis_count;
+  for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n; j += (int64_t)gridDim.x * blockDim.x) {
+    list_one<ACC>(p, f, p.vis_list[j]);
+  }
 }
 
 constexpr int kBwdBlock = 128;
@@ -672,19 +1033,59 @@ __global__ void __launch_bounds__(kBwdBlock) preprocess_bwd_kernel(PreprocessBwd
   }
 }
 
-int launch_preprocess_fwd(const PreprocessParams& p, cudaStream_t st) {
-  if (p.P <= 0) return 0;
-  const int threads = 256;
-  const int64_t blocks = (p.P + threads - 1) / threads;
-  preprocess_fwd_kernel<<<(unsigned)blocks, threads, 0, st>>>(p);
+// Blocks of `kernel` that are resident on the current device at once (SMs x
+// blocks per SM), for persistent grids.  Evaluated once per process: every
+// device of a run is the same model.
+template <typename K>
+int resident_blocks(K kernel, int threads, size_t smem) {
+  int dev = 0, sms = 0, per_sm = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
+  return std::max(sms, 1) * std::max(per_sm, 1);
+}
+
+size_t preprocess_scratch_bytes(int64_t P) { return 256 + sizeof(uint32_t) * (size_t)std::max<int64_t>(P, 1); }
+
+int launch_preprocess_fwd(const PreprocessParams& p, cudaStream_t st, void* scratch, size_t scratch_bytes) {
+  if (p.totals_out) cudaMemsetAsync(p.totals_out, 0, 2 * sizeof(unsigned long long), st);
+  if (p.P <= 0) return (int)cudaGetLastError();
+  const int n_tiles = p.grid_x * p.grid_y;
+  const size_t smem = (p.counts_out && p.compute_locally && n_tiles <= kPreMaskSmem) ? (size_t)n_tiles : 0;
+  const int64_t n_chunks = (p.P + kPreChunk - 1) / kPreChunk;
+  if (scratch && scratch_bytes >= preprocess_scratch_bytes(p.P)) {
+    // cull pass over every Gaussian, then the full computation over the
+    // candidates (persistent grid: the count is only known on the device)
+    int* cand_count = reinterpret_cast<int*>(scratch);
+    uint32_t* cand = reinterpret_cast<uint32_t*>(static_cast<char*>(scratch) + 256);
+    cudaMemsetAsync(cand_count, 0, sizeof(int), st);
+    preprocess_cull_kernel<<<(unsigned)n_chunks, kPreThreads, 0, st>>>(p, cand, cand_count);
+    static const int resident_full = resident_blocks(preprocess_full_kernel, kPreThreads, kPreMaskSmem);
+    const int64_t blocks = std::min<int64_t>((p.P + kPreThreads - 1) / kPreThreads, resident_full);
+    preprocess_full_kernel<<<(unsigned)blocks, kPreThreads, smem, st>>>(p, cand, cand_count);
+    return (int)cudaGetLastError();
+  }
+  // persistent grid: as many blocks as fit on the device at once
+  static const int resident = resident_blocks(preprocess_fwd_kernel, kPreThreads, kPreMaskSmem);
+  const int64_t blocks = std::min<int64_t>(n_chunks, resident);
+  preprocess_fwd_kernel<<<(unsigned)blocks, kPreThreads, smem, st>>>(p);
   return (int)cudaGetLastError();
 }
 
 int launch_preprocess_bwd(const PreprocessBwdParams& p, bool accumulate, cudaStream_t st) {
   if (p.f.P <= 0) return 0;
   if (p.vis_list) {
-    const int64_t blocks = (p.f.P + 127) / 128;
-    preprocess_bwd_list_kernel<<<(unsigned)blocks, 128, 0, st>>>(p);
+    // listed Gaussians only: add onto the outputs when accumulating, else
+    // store (the caller zero-filled every row)
+    // persistent grid-stride launch: the list length is only known on the
+    // device, and one block per possible entry would be mostly empty blocks
+    static const int res_acc = resident_blocks(preprocess_bwd_list_kernel<true>, 128, 0);
+    static const int res_set = resident_blocks(preprocess_bwd_list_kernel<false>, 128, 0);
+    const int64_t need = (p.f.P + 127) / 128;
+    if (accumulate)
+      preprocess_bwd_list_kernel<true><<<(unsigned)std::min<int64_t>(need, res_acc), 128, 0, st>>>(p);
+    else
+      preprocess_bwd_list_kernel<false><<<(unsigned)std::min<int64_t>(need, res_set), 128, 0, st>>>(p);
     return (int)cudaGetLastError();
   }
   const int threads = kBwdBlock;

@@ -37,10 +37,14 @@ class StageTimer:
         a.record()
         return (name, a, b)
 
-    def end(self, tok, **meta):
+    def end(self, tok, lazy=None, **meta):
+        """Record the end event; ``lazy`` (a callable returning a dict) is
+        evaluated only after it, so its kernels stay outside the timed span."""
         if tok is None:
             return
         tok[2].record()
+        if lazy is not None:
+            meta.update(lazy())
         self.records.append((tok[0], tok[1], tok[2], meta))
 
     def summary(self):
@@ -93,6 +97,7 @@ class _Scratch:
 
 
 SCRATCH = _Scratch()
+PRE_SCRATCH = _Scratch()  # candidate list of the two-kernel raw preprocess
 
 
 def sh_layout(shs=None, dc=None, rest=None):
@@ -191,15 +196,25 @@ def preprocess_backward(radii, means3D, scales, rotations, sh, raster, g_means2D
 
 
 def preprocess_forward_raw(xyz, scaling_raw, rotation_raw, opacity_raw, sh, raster, rot_norm=None, *,
-                           want_reg=True, want_list=True):
+                           want_reg=True, want_list=True, want_counts=False, compute_locally=None,
+                           two_pass=True):
     """Preprocess from the raw model parameters (activations fused into the
     kernel).  Returns (means2D, depths, radii, conic_opacity, rgb, reg_sums
-    double[2] or None, vis_list or None, vis_count or None)."""
+    double[2] or None, vis_list or None, vis_count or None, counts or None,
+    totals or None).
+
+    With ``want_list`` only the rows of listed Gaussians (radius > 0) of
+    means2D / depths / conic_opacity / rgb are written; radii is complete.
+    ``want_counts`` fuses the binning's tile count (under ``compute_locally``)
+    into the same kernel; pass counts/totals on to ``render_forward``.
+    ``two_pass`` runs the cull and the full computation as two kernels (with
+    a scratch candidate list); False runs the single persistent kernel."""
     _require_cuda(xyz, scaling_raw, rotation_raw, opacity_raw)
     xyz, scaling_raw, rotation_raw, opacity_raw = map(_f32c, (xyz, scaling_raw, rotation_raw, opacity_raw))
     dc, dcs, rest, rs, M, _keep = sh
     P = xyz.shape[0]
     dev = xyz.device
+    H, W = int(raster.image_height), int(raster.image_width)
     means2D = torch.empty((P, 2), dtype=torch.float32, device=dev)
     depths = torch.empty((P,), dtype=torch.float32, device=dev)
     radii = torch.empty((P,), dtype=torch.int32, device=dev)
@@ -208,16 +223,23 @@ def preprocess_forward_raw(xyz, scaling_raw, rotation_raw, opacity_raw, sh, rast
     reg = torch.zeros((2,), dtype=torch.float64, device=dev) if want_reg else None
     vlist = torch.empty((max(P, 1),), dtype=torch.int32, device=dev) if want_list else None
     vcount = torch.zeros((1,), dtype=torch.int32, device=dev) if want_list else None
+    counts = torch.empty((max(P, 1),), dtype=torch.int32, device=dev) if want_counts else None
+    totals = torch.empty((2,), dtype=torch.int64, device=dev) if want_counts else None
+    cl = _tile_mask(compute_locally, H, W) if want_counts else None
     if P > 0:
+        scratch = PRE_SCRATCH.get(dev, _lib.load().blitz_preprocess_scratch_bytes(P)) if two_pass else None
         tok = TIMER.begin("preprocess_fwd")
         _lib.call("blitz_preprocess_forward_raw", P, int(raster.sh_degree), M, ptr(xyz), ptr(scaling_raw),
                   ptr(rotation_raw), ptr(rot_norm), ptr(opacity_raw), ptr(dc), dcs, ptr(rest), rs,
                   float(raster.scale_modifier), ptr(_f32c(raster.viewmatrix)), ptr(_f32c(raster.projmatrix)),
                   ptr(_f32c(raster.campos)), float(raster.tanfovx), float(raster.tanfovy),
-                  int(raster.image_height), int(raster.image_width), ptr(means2D), ptr(depths), ptr(radii),
-                  ptr(conic), ptr(rgb), ptr(reg), ptr(vlist), ptr(vcount), _lib.stream_ptr())
-        TIMER.end(tok, P=P)
-    return means2D, depths, radii, conic, rgb, reg, vlist, vcount
+                  H, W, ptr(means2D), ptr(depths), ptr(radii),
+                  ptr(conic), ptr(rgb), ptr(reg), ptr(vlist), ptr(vcount), ptr(cl), ptr(counts), ptr(totals),
+                  ptr(scratch), scratch.numel() if two_pass else 0, _lib.stream_ptr())
+        TIMER.end(tok, P=P, fused_count=want_counts, lazy=lambda: {"n_list": vcount} if want_list else {})
+    elif want_counts:
+        totals.zero_()
+    return means2D, depths, radii, conic, rgb, reg, vlist, vcount, counts, totals
 
 
 def preprocess_backward_raw(radii, means2D, xyz, scaling_raw, rotation_raw, opacity_raw, sh, raster,
@@ -239,7 +261,7 @@ def preprocess_backward_raw(radii, means2D, xyz, scaling_raw, rotation_raw, opac
                   ptr(g_colors), g_colors.stride(0), ptr(reg_scale), ptr(vis_list), ptr(vis_count), ptr(gx),
                   ptr(gs), ptr(gq), ptr(go), ptr(gdc), gdcs, ptr(grest), grs, int(bool(accumulate)),
                   _lib.stream_ptr())
-        TIMER.end(tok, P=P)
+        TIMER.end(tok, P=P, lazy=lambda: {"n_list": vis_count} if vis_list is not None else {})
     return out
 
 
@@ -268,9 +290,20 @@ def _pinned_totals(dev):
     return t
 
 
-def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_locally, H, W):
+def _tile_mask(compute_locally, H, W):
+    if compute_locally is None:
+        return None
+    gx, gy = grid_dims(H, W)
+    cl = compute_locally.contiguous().view(-1)
+    if cl.dtype != torch.bool or cl.numel() != gx * gy:
+        raise RuntimeError(f"compute_locally must be bool with {gx * gy} tiles")
+    return cl
+
+
+def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_locally, H, W, counts=None, totals=None):
     """Binning + blending of one camera.  Returns (color, n_render, n_consider,
-    n_contrib_tile, out_observe, state)."""
+    n_contrib_tile, out_observe, state).  ``counts``/``totals`` from
+    ``preprocess_forward_raw(want_counts=True)`` skip the count pass."""
     _require_cuda(means2D, depths, radii, conic_opacity, rgb, bg)
     means2D, depths, conic_opacity, rgb, bg = map(_f32c, (means2D, depths, conic_opacity, rgb, bg))
     radii = radii.contiguous()
@@ -280,17 +313,14 @@ def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_local
     dev = means2D.device
     gx, gy = grid_dims(H, W)
     T = gx * gy
-    cl = None
-    if compute_locally is not None:
-        cl = compute_locally.contiguous().view(-1)
-        if cl.dtype != torch.bool or cl.numel() != T:
-            raise RuntimeError(f"compute_locally must be bool with {T} tiles")
-    counts = torch.empty((max(P, 1),), dtype=torch.int32, device=dev)
-    totals = torch.empty((2,), dtype=torch.int64, device=dev)
+    cl = _tile_mask(compute_locally, H, W)
     st = _lib.stream_ptr()
-    tok = TIMER.begin("bin_count")
-    _lib.call("blitz_render_count", P, H, W, ptr(means2D), ptr(radii), ptr(cl), ptr(counts), ptr(totals), st)
-    TIMER.end(tok, P=P)
+    if counts is None:
+        counts = torch.empty((max(P, 1),), dtype=torch.int32, device=dev)
+        totals = torch.empty((2,), dtype=torch.int64, device=dev)
+        tok = TIMER.begin("bin_count")
+        _lib.call("blitz_render_count", P, H, W, ptr(means2D), ptr(radii), ptr(cl), ptr(counts), ptr(totals), st)
+        TIMER.end(tok, P=P)
     host = _pinned_totals(dev)
     host.copy_(totals, non_blocking=True)
     torch.cuda.current_stream().synchronize()
@@ -316,7 +346,7 @@ def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_local
               ptr(point_list), ptr(ranges), ptr(final_T), ptr(n_contrib), ptr(color), ptr(n_render), ptr(n_consider),
               ptr(n_contrib_tile), ptr(out_observe), st)
     TIMER.end(tok, P=P, R=R, n_vis=n_vis, H=H, W=W,
-              pairs=(n_consider.sum(dtype=torch.int64), n_contrib_tile.sum(dtype=torch.int64)) if TIMER.enabled else None)
+              lazy=lambda: {"pairs": (n_consider.sum(dtype=torch.int64), n_contrib_tile.sum(dtype=torch.int64))})
     state = RenderState(H, W, R, n_vis, point_list, ranges, final_T, n_contrib)
     return color, n_render, n_consider, n_contrib_tile, out_observe, state
 
@@ -333,7 +363,7 @@ def render_backward(state, means2D, conic_opacity, rgb, bg, compute_locally, dL_
     _lib.call("blitz_render_backward", P, state.H, state.W, ptr(state.point_list), ptr(state.ranges),
               ptr(state.final_T), ptr(state.n_contrib), ptr(means2D), ptr(conic_opacity), ptr(rgb), ptr(bg),
               ptr(cl), ptr(dL_dpix), ptr(grad_accum), _lib.stream_ptr())
-    TIMER.end(tok, P=P, R=state.R, pairs=(state.n_contrib.sum(dtype=torch.int64),) if TIMER.enabled else None)
+    TIMER.end(tok, P=P, R=state.R, lazy=lambda: {"pairs": (state.n_contrib.sum(dtype=torch.int64),)})
     return grad_accum
 
 

@@ -35,10 +35,11 @@ class _ViewLoss(torch.autograd.Function):
         sh = ops.sh_layout(dc=dc, rest=rest)
         rot_norm = q_raw.norm(dim=1) if exact_norm else None
         use_list = compute_locally is None
-        means2D, depths, radii, conic, rgb, reg, vlist, vcount = ops.preprocess_forward_raw(
-            xyz, s_raw, q_raw, o_raw.reshape(-1), sh, raster, rot_norm, want_reg=True, want_list=use_list)
+        means2D, depths, radii, conic, rgb, reg, vlist, vcount, counts, totals = ops.preprocess_forward_raw(
+            xyz, s_raw, q_raw, o_raw.reshape(-1), sh, raster, rot_norm, want_reg=True, want_list=use_list,
+            want_counts=True, compute_locally=compute_locally)
         color, n_render, n_consider, n_contrib, out_observe, state = ops.render_forward(
-            means2D, depths, radii, conic, rgb, raster.bg, compute_locally, H, W)
+            means2D, depths, radii, conic, rgb, raster.bg, compute_locally, H, W, counts=counts, totals=totals)
         y0, y1 = band
         img_band = color[:, y0:y1, :]
         sums, partials = ops.loss_forward(img_band, gt)
@@ -84,15 +85,15 @@ class _ViewLoss(torch.autograd.Function):
 
 
 def view_loss(model, raster, gt_band, compute_locally=None, band=None, lambda_dssim=LAMBDA_DSSIM,
-              scale_reg_weight=10.0, exact_norm=True):
+              scale_reg_weight=10.0, exact_norm=False):
     """Loss of one camera exactly as batched_loss_computation forms it
     (loss_distribution.py:303-322): (1-l) L1/N3 + l (1 - SSIM/N3) +
     10 mean(min-axis scale of the Gaussians the exchange sends), N3 = 3 H W.
 
     ``model`` = raw (xyz, _scaling, _rotation, _opacity, _features_dc,
     _features_rest); the activations run inside the preprocess kernels.
-    ``exact_norm`` takes ||_rotation|| from PyTorch (bit-identical to the
-    reference's F.normalize); otherwise the kernel computes it.
+    The kernel computes ||_rotation|| with the summation order of PyTorch's
+    norm (bit-identical); ``exact_norm=True`` takes it from PyTorch instead.
     Returns (loss, l1_sum, ssim_sum, radii, out_observe, color)."""
     xyz, s_raw, q_raw, o_raw, dc, rest = model
     H, W = int(raster.image_height), int(raster.image_width)

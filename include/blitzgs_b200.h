@@ -40,7 +40,10 @@ extern "C" {
 /* Device error-word bits (see blitz_preprocess_forward). */
 #define BLITZ_ERRBIT_PREFILTERED_CULLED 1u /* a Gaussian failed the near test with prefiltered=1 */
 
+/* Library version string (no reference counterpart). */
 const char* blitz_version(void);
+/* Message for the last non-zero status returned on this host thread; the
+ * reference raises these as Python exceptions from its pybind11 modules. */
 const char* blitz_last_error(void);
 
 /*
@@ -104,9 +107,24 @@ int blitz_preprocess_backward(int64_t P, int D, int M, const int32_t* radii, con
  *   vis_list  device uint32 [P] receives the indices of Gaussians with
  *             radius > 0 (unordered), vis_count (device int32, zero on entry)
  *             their number -- the work list of blitz_preprocess_backward_raw.
+ *             With a list, only the rows of listed Gaussians are guaranteed to
+ *             be written in means2D / depths / conic_opacity / rgb (radii is
+ *             always written for every Gaussian): a training view touches a
+ *             few percent of the model, and the other rows are never read;
+ *   counts    device uint32 [P]: tile count of each Gaussian under the
+ *             compute_locally mask (uint8 [tiles], NULL = all tiles), and
+ *             totals (device uint64 [2]) = {tile instances R, Gaussians with
+ *             at least one tile}: the output of blitz_render_count, fused
+ *             (counts and totals must be both given or both NULL);
+ *   scratch   device buffer of blitz_preprocess_scratch_bytes(P) bytes: runs
+ *             the cull and the full computation as two kernels (faster when
+ *             most Gaussians are off-screen); NULL runs one kernel.
  * Replaces the activation kernels + preprocess of the reference training step
  * (gaussian_renderer/__init__.py:260-324); no reference op is a single match.
  */
+/* Size of the optional scratch of blitz_preprocess_forward_raw (no reference
+ * counterpart: the reference allocates its temporaries per call). */
+size_t blitz_preprocess_scratch_bytes(int64_t P);
 int blitz_preprocess_forward_raw(int64_t P, int D, int M, const float* xyz, const float* scaling_raw,
                                  const float* rotation_raw, const float* rotation_norm,
                                  const float* opacity_raw, const float* sh_dc, int64_t dc_stride,
@@ -115,16 +133,18 @@ int blitz_preprocess_forward_raw(int64_t P, int D, int M, const float* xyz, cons
                                  float tanfovx, float tanfovy, int image_height, int image_width,
                                  float* means2D, float* depths, int32_t* radii, float* conic_opacity,
                                  float* rgb, double* reg_sums, uint32_t* vis_list, int32_t* vis_count,
-                                 void* stream);
+                                 const uint8_t* compute_locally, uint32_t* counts, uint64_t* totals,
+                                 void* scratch, size_t scratch_bytes, void* stream);
 
 /*
  * Backward of blitz_preprocess_forward_raw: gradients with respect to the
  * RAW parameters (xyz, _scaling, _rotation, _opacity, SH), chained through
  * the activations in the kernel.  reg_scale (device float, may be NULL) is
  * dLoss/d(reg_sums[0]).  With vis_list/vis_count from the forward only those
- * Gaussians are processed and their gradients are ADDED to the outputs (which
- * must be zero-filled or hold gradients to accumulate onto); with NULL every
- * Gaussian is processed and `accumulate` selects overwrite (0) or add (1).
+ * Gaussians are processed: the caller zero-fills the outputs first, and
+ * `accumulate` selects whether their rows are stored (0) or added onto (1);
+ * with NULL lists every Gaussian is processed and `accumulate` selects
+ * overwrite (0) or add (1).
  */
 int blitz_preprocess_backward_raw(int64_t P, int D, int M, const int32_t* radii, const float* means2D,
                                   const float* xyz, const float* scaling_raw, const float* rotation_raw,

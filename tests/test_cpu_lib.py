@@ -34,6 +34,40 @@ def test_library_exports_every_declared_symbol():
     assert set(header_functions()) <= set(_lib.SIGNATURES), "ctypes signatures missing for some entry points"
 
 
+def header_prototypes():
+    """{name: (return type, [parameter types])} parsed from the header."""
+    src = open(os.path.join(ROOT, "include", "blitzgs_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    protos = {}
+    for ret, name, params in re.findall(r"\b((?:const\s+)?[a-z0-9_]+\s*\*?)\s*(blitz_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", src):
+        ps = [p.strip() for p in params.split(",") if p.strip() and p.strip() != "void"]
+        protos[name] = (ret.strip(), [p.rsplit(" ", 1)[0].replace(" *", "*").strip() if "*" not in p.rsplit(" ", 1)[-1]
+                                      else p.rsplit(" ", 1)[0].strip() + "*" for p in ps])
+    return protos
+
+
+def _ctype_of(c):
+    c = c.replace("const ", "").strip()
+    if c.endswith("*"):
+        return ctypes.c_char_p if c == "char*" else ctypes.c_void_p
+    return {"int": ctypes.c_int, "int64_t": ctypes.c_int64, "float": ctypes.c_float, "size_t": ctypes.c_size_t,
+            "int32_t": ctypes.c_int32, "uint32_t": ctypes.c_uint32}[c]
+
+
+def test_ctypes_signatures_match_the_header():
+    """Every binding in blitzgs_b200._lib has the header's parameter count and
+    types, so a changed prototype cannot silently shift arguments."""
+    protos = header_prototypes()
+    assert set(protos) == set(header_functions())
+    for name, (ret, params) in protos.items():
+        sig_ret, sig_args = _lib.SIGNATURES[name]
+        assert len(sig_args) == len(params), f"{name}: {len(sig_args)} ctypes args, header has {len(params)}"
+        for k, (a, c) in enumerate(zip(sig_args, params)):
+            assert ctypes.sizeof(a) == ctypes.sizeof(_ctype_of(c)) and \
+                (a is ctypes.c_void_p) == c.endswith("*"), f"{name} arg {k}: {a} vs {c}"
+        assert ctypes.sizeof(sig_ret) == ctypes.sizeof(_ctype_of(ret)), f"{name} return: {sig_ret} vs {ret}"
+
+
 def test_version_string():
     assert b"sm_100a" in _lib.load().blitz_version()
 

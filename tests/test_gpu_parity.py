@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 import torch
 
-from blitzgs_b200 import ops, rasterizer as RZ, scene as S, step as ST
+from blitzgs_b200 import _lib, ops, rasterizer as RZ, scene as S, step as ST
 from oracle import rasterizer_oracle as O
 from tests.helpers import (IMG_ATOL, activated, assert_grad_close, frac_close, normwise_rel,
                            scene_params)
@@ -171,12 +171,78 @@ def test_raw_preprocess_bit_identical_to_torch_activations(cuda_device):
     cam = sc.cameras[0].to(cuda_device)
     rs = _raster(cam, cuda_device)
     xyz, s, q, o, dc, rest = [t.to(cuda_device) for t in scene_params(sc)]
-    a = ops.preprocess_forward_raw(xyz, s, q, o.reshape(-1), ops.sh_layout(dc=dc, rest=rest), rs, q.norm(dim=1))
+    a = ops.preprocess_forward_raw(xyz, s, q, o.reshape(-1), ops.sh_layout(dc=dc, rest=rest), rs, q.norm(dim=1),
+                                   want_list=False)
     shs = torch.cat((dc, rest), 1)
     b = ops.preprocess_forward(xyz, torch.exp(s), torch.nn.functional.normalize(q), torch.sigmoid(o).reshape(-1),
                                ops.sh_layout(shs=shs), rs)
     for x, y in zip(a[:5], b[:5]):
         assert torch.equal(x, y)
+
+
+def test_in_kernel_rotation_norm_is_bit_identical_to_torch(cuda_device):
+    """The fused step normalises _rotation in the kernel; its norm must equal
+    PyTorch's norm bit for bit, or radii could differ from the reference's."""
+    g = torch.Generator().manual_seed(77)
+    sc = S.tiny(seed=12, P=200000, H=96, W=128)
+    sc.rotation = torch.randn(200000, 4, generator=g) * torch.rand(200000, 1, generator=g) * 3
+    cam = sc.cameras[0].to(cuda_device)
+    rs = _raster(cam, cuda_device)
+    xyz, s, q, o, dc, rest = [t.to(cuda_device) for t in scene_params(sc)]
+    sh = ops.sh_layout(dc=dc, rest=rest)
+    a = ops.preprocess_forward_raw(xyz, s, q, o.reshape(-1), sh, rs, q.norm(dim=1), want_list=False)
+    b = ops.preprocess_forward_raw(xyz, s, q, o.reshape(-1), sh, rs, None, want_list=False)
+    for x, y in zip(a[:5], b[:5]):
+        assert torch.equal(x, y)
+
+
+def _separate_count(m2, r, cl, H, W):
+    P = m2.shape[0]
+    counts = torch.empty((P,), dtype=torch.int32, device=m2.device)
+    totals = torch.empty((2,), dtype=torch.int64, device=m2.device)
+    mask = None if cl is None else cl.contiguous().view(-1)
+    _lib.call("blitz_render_count", P, H, W, ops.ptr(m2), ops.ptr(r), ops.ptr(mask), ops.ptr(counts), ops.ptr(totals),
+              _lib.stream_ptr())
+    return counts, totals
+
+
+@pytest.mark.parametrize("two_pass", [True, False], ids=["cull+full", "one-kernel"])
+@pytest.mark.parametrize("case", ["mid_full", "mid_masked", "huge_grid_masked"])
+def test_fused_count_and_listed_rows_match_separate_passes(cuda_device, case, two_pass):
+    """The fused step's preprocess writes radii for every Gaussian, full rows
+    only for the listed ones (radius > 0), and the binning's tile counts under
+    the tile mask.  All of it must equal the dense preprocess followed by the
+    separate count pass.  1.5M Gaussians take several chunks per persistent
+    block, so survivors carried from one chunk to the next are covered; the
+    4112x2048 image has more tiles than the kernel stages in shared memory."""
+    if case == "huge_grid_masked":
+        sc = S.tiny(seed=21, P=300000, H=2048, W=4112)
+    else:
+        sc = S.mid(seed=3, P=1_500_000, n_cams=1)
+    cam = sc.cameras[0].to(cuda_device)
+    rs = _raster(cam, cuda_device)
+    H, W = cam.image_height, cam.image_width
+    gx, gy = ops.grid_dims(H, W)
+    cl = None
+    if case != "mid_full":
+        g = torch.Generator().manual_seed(5)
+        cl = (torch.rand(gy, gx, generator=g) < 0.6).to(cuda_device)
+    xyz, s, q, o, dc, rest = [t.to(cuda_device) for t in scene_params(sc)]
+    sh = ops.sh_layout(dc=dc, rest=rest)
+    dense = ops.preprocess_forward_raw(xyz, s, q, o.reshape(-1), sh, rs, None, want_list=False, two_pass=False)
+    fused = ops.preprocess_forward_raw(xyz, s, q, o.reshape(-1), sh, rs, None, want_list=True, want_counts=True,
+                                       compute_locally=cl, two_pass=two_pass)
+    assert torch.equal(dense[2], fused[2])  # radii, every Gaussian
+    n = int(fused[7].item())
+    listed = fused[6][:n].long()
+    assert n > 1000
+    assert torch.equal(torch.sort(listed).values, torch.nonzero(dense[2] > 0).flatten())
+    for a, b in zip(dense[:5], fused[:5]):
+        assert torch.equal(a[listed], b[listed])
+    assert torch.equal(dense[5], fused[5])  or torch.allclose(dense[5], fused[5], rtol=1e-12)  # regulariser sums
+    counts, totals = _separate_count(dense[0], dense[2], cl, H, W)
+    assert torch.equal(counts, fused[8])
+    assert torch.equal(totals, fused[9])
 
 
 def test_drop_in_api_autograd_matches_fused(cuda_device):
