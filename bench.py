@@ -251,7 +251,7 @@ def run_ours(args, ws, rank, local):
                     h2d[0] = 3 * H * W * bsz
                 else:
                     gt = gts_dev[ci]
-                loss, *_ = ST.view_loss(model, rasters[ci], gt)
+                loss, *_ = ST.view_loss(model, rasters[ci], gt, sparse_grad=args.sparse_grad)
                 total = loss if total is None else total + loss
         else:
             ids = batch_ids(it)
@@ -602,6 +602,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="city")
     ap.add_argument("--bsz", type=int, default=1, help="views per GPU per step")
+    ap.add_argument("--sparse-grad", action="store_true",
+                    help="parameter gradients as sparse rows of the visible Gaussians (1 GPU; default dense)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -610,7 +612,8 @@ def main():
     cfg = {"workload": f"{args.config} (BASELINE config 3: 8M clustered Gaussians, 1152x864 aerial views)"
            if args.config == "city" else args.config,
            "gaussians": None, "image": None, "views_per_gpu_per_step": args.bsz,
-           "parallelism": f"dp{ws}" if ws > 1 else "single", "l2": "inputs larger than L2 (8M x 236 B params)"}
+           "parallelism": f"dp{ws}" if ws > 1 else "single", "l2": "inputs larger than L2 (8M x 236 B params)",
+           "grad": "sparse rows (visible Gaussians)" if args.sparse_grad else "dense"}
 
     if args.impl == "reference":
         if rank != 0:

@@ -24,12 +24,12 @@ SIGNATURES = {
         _i32, _i32, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i32, _vp]),
     "blitz_preprocess_forward_raw": (_i32, [
         _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _f32, _vp, _vp, _vp, _f32, _f32,
-        _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+        _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "blitz_preprocess_scratch_bytes": (_sz, [_i64]),
     "blitz_preprocess_backward_raw": (_i32, [
         _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _f32, _vp, _vp, _vp, _f32,
         _f32, _i32, _i32, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64,
-        _vp, _i64, _i32, _vp]),
+        _vp, _i64, _i32, _i32, _vp]),
     "blitz_render_count": (_i32, [_i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp]),
     "blitz_render_scratch_bytes": (_sz, [_i64, _i64, _i64, _i32, _i32]),
     "blitz_render_forward": (_i32, [
@@ -40,7 +40,7 @@ SIGNATURES = {
                                   _vp, _vp]),
     "blitz_render_bin_noalloc": (_i32, [_i64, _i64, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "blitz_render_backward": (_i32, [
-        _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+        _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "blitz_loss_forward": (_i32, [_i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "blitz_loss_backward": (_i32, [_i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "blitz_get_local2j_ids_bool": (_i32, [_i32, _i32, _i32, _i32, _i64, _vp, _vp, _vp, _i32, _vp, _vp]),

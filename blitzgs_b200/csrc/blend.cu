@@ -358,7 +358,7 @@ __global__ void __launch_bounds__(kTilePix, 4) blend_bwd_kernel(BlendBwdParams p
     int kept;
     const int slot = compact_slot(keep, s_wcnt, kept);
     if (slot >= 0) {
-      s_id[slot] = id;
+      s_id[slot] = p.record_rows ? (int)__ldg(p.record_rows + id) : id;  // gradient record row
       s_xy[slot] = xy;
       s_co[slot] = co;
       s_rgb[slot] = cth;

@@ -159,7 +159,7 @@ int blitz_preprocess_forward_raw(int64_t P, int D, int M, const float* xyz, cons
                                  float* means2D, float* depths, int32_t* radii, float* conic_opacity,
                                  float* rgb, double* reg_sums, uint32_t* vis_list, int32_t* vis_count,
                                  const uint8_t* compute_locally, uint32_t* counts, uint64_t* totals,
-                                 void* scratch, size_t scratch_bytes, void* stream) {
+                                 uint32_t* slot_of, void* scratch, size_t scratch_bytes, void* stream) {
   if (P < 0 || D < 0 || D > 3 || M < 0 || M > 15 || image_height <= 0 || image_width <= 0)
     return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: bad sizes");
   if (P == 0) return 0;
@@ -179,6 +179,8 @@ int blitz_preprocess_forward_raw(int64_t P, int D, int M, const float* xyz, cons
   p.vis_list_out = vis_list;
   p.vis_count_out = vis_count;
   p.listed_rows_only = vis_list != nullptr;
+  if (slot_of && !vis_list) return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: slot_of needs vis_list");
+  p.slot_of_out = slot_of;
   p.counts_out = counts;
   p.totals_out = reinterpret_cast<unsigned long long*>(totals);
   p.compute_locally = reinterpret_cast<const bool*>(compute_locally);
@@ -206,7 +208,7 @@ int blitz_preprocess_backward_raw(int64_t P, int D, int M, const int32_t* radii,
                                   const uint32_t* vis_list, const int32_t* vis_count, float* g_xyz,
                                   float* g_scaling_raw, float* g_rotation_raw, float* g_opacity_raw,
                                   float* g_dc, int64_t g_dc_stride, float* g_rest, int64_t g_rest_stride,
-                                  int accumulate, void* stream) {
+                                  int accumulate, int rows, void* stream) {
   if (P < 0 || D < 0 || D > 3 || M < 0 || M > 15 || image_height <= 0 || image_width <= 0)
     return fail(BLITZ_EINVAL, "blitz_preprocess_backward_raw: bad sizes");
   if (P == 0) return 0;
@@ -226,6 +228,10 @@ int blitz_preprocess_backward_raw(int64_t P, int D, int M, const int32_t* radii,
   b.reg_scale = reg_scale;
   b.vis_list = vis_list;
   b.vis_count = vis_count;
+  if ((rows & ~(BLITZ_ROWS_UPSTREAM_BY_SLOT | BLITZ_ROWS_OUTPUT_BY_SLOT)) || (rows && !vis_list))
+    return fail(BLITZ_EINVAL, "blitz_preprocess_backward_raw: bad rows flags (slot rows need vis_list)");
+  b.upstream_by_slot = rows & BLITZ_ROWS_UPSTREAM_BY_SLOT;
+  b.out_by_slot = rows & BLITZ_ROWS_OUTPUT_BY_SLOT;
   b.g_means2D = g_means2D;
   b.g_means2D_stride = g_means2D_stride;
   b.g_conic_opacity = g_conic_opacity;
@@ -377,7 +383,7 @@ int blitz_render_backward(int64_t P, int image_height, int image_width, const ui
                           const uint32_t* ranges, const float* final_T, const uint32_t* n_contrib,
                           const float* means2D, const float* conic_opacity, const float* rgb,
                           const float* bg, const uint8_t* compute_locally, const float* dL_dpix,
-                          float* grad_accum, void* stream) {
+                          const uint32_t* record_rows, float* grad_accum, void* stream) {
   if (P < 0 || image_height <= 0 || image_width <= 0)
     return fail(BLITZ_EINVAL, "blitz_render_backward: bad sizes");
   if (!ranges || !final_T || !n_contrib || !bg || !dL_dpix ||
@@ -402,6 +408,7 @@ int blitz_render_backward(int64_t P, int image_height, int image_width, const ui
   b.n_contrib = n_contrib;
   b.dL_dpix = dL_dpix;
   b.grad_accum = grad_accum;
+  b.record_rows = record_rows;
   return check(launch_blend_bwd(b, S(stream)), "blitz_render_backward");
 }
 

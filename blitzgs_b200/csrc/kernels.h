@@ -56,6 +56,7 @@ struct PreprocessParams {
   // Gaussians rejected before the full computation get only radii (and
   // counts) written; the caller reads other rows through vis_list_out.
   bool listed_rows_only;
+  uint32_t* slot_of_out;  // optional [P]: list position of each listed Gaussian (others untouched)
 };
 
 struct PreprocessBwdParams {
@@ -81,6 +82,10 @@ struct PreprocessBwdParams {
   const float* reg_scale;      // device float: dLoss/d(sum min-axis scale), or null
   const uint32_t* vis_list;    // optional: only these Gaussians are processed; outputs pre-zeroed
   const int* vis_count;        // device count of vis_list
+  // With vis_list: upstream gradients are read at row j (the list position)
+  // instead of row i, and/or the outputs are written at row j (compact rows).
+  bool upstream_by_slot;
+  bool out_by_slot;
 };
 
 // scratch (may be null): preprocess_scratch_bytes(P) bytes select the
@@ -155,7 +160,8 @@ struct BlendBwdParams {
   const float* final_T;
   const uint32_t* n_contrib;
   const float* dL_dpix;   // [3,H,W]
-  float* grad_accum;      // [P,16], zero on entry; layout in capi docs
+  float* grad_accum;      // [rows,16], zero on entry; layout in capi docs
+  const uint32_t* record_rows;  // optional: record row of Gaussian id (else the id itself)
 };
 
 int launch_blend_bwd(const BlendBwdParams& p, cudaStream_t st);

@@ -418,7 +418,11 @@ __device__ __forceinline__ void full_phase(const PreprocessParams& p, const floa
       *s_base = tot ? atomicAdd(p.vis_count_out, tot) : 0;
     }
     __syncthreads();
-    if (listed) p.vis_list_out[*s_base + s_wc[warp] + __popc(m & ((1u << lane) - 1u))] = (uint32_t)i;
+    if (listed) {
+      const uint32_t slot = (uint32_t)(*s_base + s_wc[warp] + __popc(m & ((1u << lane) - 1u)));
+      p.vis_list_out[slot] = (uint32_t)i;
+      if (p.slot_of_out) p.slot_of_out[i] = slot;
+    }
     __syncthreads();  // s_wc / s_base are rewritten next round
   }
   if (valid) {
@@ -642,7 +646,9 @@ __device__ __forceinline__ void bwd_zero(BwdOut& o) {
 
 // Gradients of one visible Gaussian (radius > 0) given its upstream
 // gradients gco (conic00, conic01, conic11, opacity).
-__device__ __forceinline__ void bwd_compute(const PreprocessBwdParams& p, int64_t i, float4 gco, BwdOut& out) {
+// up = row of the upstream gradients (i, or the list position).
+__device__ __forceinline__ void bwd_compute(const PreprocessBwdParams& p, int64_t i, int64_t up, float4 gco,
+                                            BwdOut& out) {
   const PreprocessParams& f = p.f;
 
   float Vs[16], Ps[16];
@@ -725,7 +731,7 @@ __device__ __forceinline__ void bwd_compute(const PreprocessBwdParams& p, int64_
 
   // ---- screen-space mean part (reference backward.cu:374-391) ----
   {
-    const float* gm2 = p.g_means2D + i * p.g_means2D_stride;
+    const float* gm2 = p.g_means2D + up * p.g_means2D_stride;
     const float gx = gm2[0], gy = gm2[1];
     const float4 m_hom = xform_point4(mean, Ps);
     const float m_w = 1.0f / (m_hom.w + 0.0000001f);
@@ -742,7 +748,7 @@ __device__ __forceinline__ void bwd_compute(const PreprocessBwdParams& p, int64_
     load_sh(f, i, f.M, s);
     bool clamp3[3];
     (void)sh_to_rgb(f.D, mean, f.campos, s.dc, s.rest, clamp3);
-    const float* gc = p.g_colors + i * p.g_colors_stride;
+    const float* gc = p.g_colors + up * p.g_colors_stride;
     const float dR[3] = {clamp3[0] ? 0.f : gc[0], clamp3[1] ? 0.f : gc[1], clamp3[2] ? 0.f : gc[2]};
     const float3 dir_orig = make_float3(mean.x - f.campos[0], mean.y - f.campos[1], mean.z - f.campos[2]);
     const float len = sqrtf(dir_orig.x * dir_orig.x + dir_orig.y * dir_orig.y + dir_orig.z * dir_orig.z);
@@ -911,11 +917,14 @@ __device__ __forceinline__ void bwd_compute(const PreprocessBwdParams& p, int64_
 // does useful work; gradients are added into pre-zeroed (or accumulating)
 // outputs.
 template <bool ACC>
-__device__ __forceinline__ void list_one(const PreprocessBwdParams& p, const PreprocessParams& f, int64_t i) {
-  const float4 gco = *reinterpret_cast<const float4*>(p.g_conic_opacity + i * p.g_conic_stride);
+__device__ __forceinline__ void list_one(const PreprocessBwdParams& p, const PreprocessParams& f, int64_t j) {
+  const int64_t g = p.vis_list[j];
+  const int64_t up = p.upstream_by_slot ? j : g;
+  const float4 gco = *reinterpret_cast<const float4*>(p.g_conic_opacity + up * p.g_conic_stride);
   BwdOut o;
   bwd_zero(o);
-  bwd_compute(p, i, gco, o);
+  bwd_compute(p, g, up, gco, o);
+  const int64_t i = p.out_by_slot ? j : g;  // output row
 #pragma unroll
   for (int k = 0; k < 3; ++k) {
     put<ACC>(p.g_means3D + 3 * i + k, o.mean[k]);
@@ -947,7 +956,7 @@ __global__ void __launch_bounds__(128) preprocess_bwd_list_kernel(PreprocessBwdP
   const PreprocessParams& f = p.f;
   const int64_t n = *p.vis_count;
   for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n; j += (int64_t)gridDim.x * blockDim.x) {
-    list_one<ACC>(p, f, p.vis_list[j]);
+    list_one<ACC>(p, f, j);
   }
 }
 
@@ -993,7 +1002,7 @@ __global__ void __launch_bounds__(kBwdBlock) preprocess_bwd_kernel(PreprocessBwd
   BwdOut o;
   bwd_zero(o);
   o.op = gco.w;  // the reference copies column 3 for every Gaussian
-  if (vis) bwd_compute(p, i, gco, o);
+  if (vis) bwd_compute(p, i, i, gco, o);
   if (valid && p.g_opacities) put<ACC>(p.g_opacities + i, o.op);
 
   if (valid) {

@@ -197,18 +197,20 @@ def preprocess_backward(radii, means3D, scales, rotations, sh, raster, g_means2D
 
 def preprocess_forward_raw(xyz, scaling_raw, rotation_raw, opacity_raw, sh, raster, rot_norm=None, *,
                            want_reg=True, want_list=True, want_counts=False, compute_locally=None,
-                           two_pass=True):
+                           two_pass=True, want_slots=False):
     """Preprocess from the raw model parameters (activations fused into the
     kernel).  Returns (means2D, depths, radii, conic_opacity, rgb, reg_sums
     double[2] or None, vis_list or None, vis_count or None, counts or None,
-    totals or None).
+    totals or None, slot_of or None).
 
     With ``want_list`` only the rows of listed Gaussians (radius > 0) of
     means2D / depths / conic_opacity / rgb are written; radii is complete.
     ``want_counts`` fuses the binning's tile count (under ``compute_locally``)
     into the same kernel; pass counts/totals on to ``render_forward``.
     ``two_pass`` runs the cull and the full computation as two kernels (with
-    a scratch candidate list); False runs the single persistent kernel."""
+    a scratch candidate list); False runs the single persistent kernel.
+    ``want_slots`` returns slot_of [P] (list position of each listed
+    Gaussian), which indexes the compact gradient record of the backward."""
     _require_cuda(xyz, scaling_raw, rotation_raw, opacity_raw)
     xyz, scaling_raw, rotation_raw, opacity_raw = map(_f32c, (xyz, scaling_raw, rotation_raw, opacity_raw))
     dc, dcs, rest, rs, M, _keep = sh
@@ -226,6 +228,7 @@ def preprocess_forward_raw(xyz, scaling_raw, rotation_raw, opacity_raw, sh, rast
     counts = torch.empty((max(P, 1),), dtype=torch.int32, device=dev) if want_counts else None
     totals = torch.empty((2,), dtype=torch.int64, device=dev) if want_counts else None
     cl = _tile_mask(compute_locally, H, W) if want_counts else None
+    slot_of = torch.empty((max(P, 1),), dtype=torch.int32, device=dev) if (want_slots and want_list) else None
     if P > 0:
         scratch = PRE_SCRATCH.get(dev, _lib.load().blitz_preprocess_scratch_bytes(P)) if two_pass else None
         tok = TIMER.begin("preprocess_fwd")
@@ -235,19 +238,26 @@ def preprocess_forward_raw(xyz, scaling_raw, rotation_raw, opacity_raw, sh, rast
                   ptr(_f32c(raster.campos)), float(raster.tanfovx), float(raster.tanfovy),
                   H, W, ptr(means2D), ptr(depths), ptr(radii),
                   ptr(conic), ptr(rgb), ptr(reg), ptr(vlist), ptr(vcount), ptr(cl), ptr(counts), ptr(totals),
-                  ptr(scratch), scratch.numel() if two_pass else 0, _lib.stream_ptr())
+                  ptr(slot_of), ptr(scratch), scratch.numel() if two_pass else 0, _lib.stream_ptr())
         TIMER.end(tok, P=P, fused_count=want_counts, lazy=lambda: {"n_list": vcount} if want_list else {})
     elif want_counts:
         totals.zero_()
-    return means2D, depths, radii, conic, rgb, reg, vlist, vcount, counts, totals
+    return means2D, depths, radii, conic, rgb, reg, vlist, vcount, counts, totals, slot_of
+
+
+ROWS_UPSTREAM_BY_SLOT = 1  # BLITZ_ROWS_UPSTREAM_BY_SLOT
+ROWS_OUTPUT_BY_SLOT = 2    # BLITZ_ROWS_OUTPUT_BY_SLOT
 
 
 def preprocess_backward_raw(radii, means2D, xyz, scaling_raw, rotation_raw, opacity_raw, sh, raster,
                             g_means2D, g_conic, g_colors, out, rot_norm=None, reg_scale=None, vis_list=None,
-                            vis_count=None, accumulate=False):
+                            vis_count=None, accumulate=False, rows=0):
     """Gradients w.r.t. the raw parameters into ``out`` = (g_xyz, g_scaling,
     g_rotation, g_opacity, (g_dc, stride), (g_rest, stride)).  With a visible
-    list the outputs must be zero-filled (or accumulating)."""
+    list the outputs must be zero-filled (or accumulating), unless ``rows``
+    has ROWS_OUTPUT_BY_SLOT: then row j of every output is the j-th listed
+    Gaussian's gradient.  ROWS_UPSTREAM_BY_SLOT reads the upstream gradients
+    at row j (the compact record)."""
     dc, dcs, rest, rs, M, _keep = sh
     P = xyz.shape[0]
     gx, gs, gq, go, (gdc, gdcs), (grest, grs) = out
@@ -259,7 +269,7 @@ def preprocess_backward_raw(radii, means2D, xyz, scaling_raw, rotation_raw, opac
                   ptr(raster.campos), float(raster.tanfovx), float(raster.tanfovy), int(raster.image_height),
                   int(raster.image_width), ptr(g_means2D), g_means2D.stride(0), ptr(g_conic), g_conic.stride(0),
                   ptr(g_colors), g_colors.stride(0), ptr(reg_scale), ptr(vis_list), ptr(vis_count), ptr(gx),
-                  ptr(gs), ptr(gq), ptr(go), ptr(gdc), gdcs, ptr(grest), grs, int(bool(accumulate)),
+                  ptr(gs), ptr(gq), ptr(go), ptr(gdc), gdcs, ptr(grest), grs, int(bool(accumulate)), int(rows),
                   _lib.stream_ptr())
         TIMER.end(tok, P=P, lazy=lambda: {"n_list": vis_count} if vis_list is not None else {})
     return out
@@ -276,16 +286,17 @@ class RenderState:
     ranges: torch.Tensor      # int32 [T,2]
     final_T: torch.Tensor     # f32 [H*W]
     n_contrib: torch.Tensor   # int32 [H*W]
+    n_list: int = None        # length of the preprocess's visible list, when read back
 
 
 _PINNED = {}
 
 
-def _pinned_totals(dev):
-    key = (dev.index,)
+def _pinned(dev, n, dtype):
+    key = (dev.index, n, dtype)
     t = _PINNED.get(key)
     if t is None:
-        t = torch.empty(2, dtype=torch.int64, pin_memory=True)
+        t = torch.empty(n, dtype=dtype, pin_memory=True)
         _PINNED[key] = t
     return t
 
@@ -300,10 +311,12 @@ def _tile_mask(compute_locally, H, W):
     return cl
 
 
-def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_locally, H, W, counts=None, totals=None):
+def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_locally, H, W, counts=None, totals=None,
+                   vis_count=None):
     """Binning + blending of one camera.  Returns (color, n_render, n_consider,
     n_contrib_tile, out_observe, state).  ``counts``/``totals`` from
-    ``preprocess_forward_raw(want_counts=True)`` skip the count pass."""
+    ``preprocess_forward_raw(want_counts=True)`` skip the count pass;
+    ``vis_count`` is read back with the totals (state.n_list)."""
     _require_cuda(means2D, depths, radii, conic_opacity, rgb, bg)
     means2D, depths, conic_opacity, rgb, bg = map(_f32c, (means2D, depths, conic_opacity, rgb, bg))
     radii = radii.contiguous()
@@ -321,10 +334,14 @@ def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_local
         tok = TIMER.begin("bin_count")
         _lib.call("blitz_render_count", P, H, W, ptr(means2D), ptr(radii), ptr(cl), ptr(counts), ptr(totals), st)
         TIMER.end(tok, P=P)
-    host = _pinned_totals(dev)
+    host = _pinned(dev, 2, torch.int64)
     host.copy_(totals, non_blocking=True)
+    if vis_count is not None:
+        host_n = _pinned(dev, 1, torch.int32)
+        host_n.copy_(vis_count, non_blocking=True)
     torch.cuda.current_stream().synchronize()
     R, n_vis = int(host[0]), int(host[1])
+    n_list = int(host_n[0]) if vis_count is not None else None
 
     point_list = torch.empty((max(R, 1),), dtype=torch.int32, device=dev)
     ranges = torch.empty((T, 2), dtype=torch.int32, device=dev)
@@ -347,22 +364,25 @@ def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_local
               ptr(n_contrib_tile), ptr(out_observe), st)
     TIMER.end(tok, P=P, R=R, n_vis=n_vis, H=H, W=W,
               lazy=lambda: {"pairs": (n_consider.sum(dtype=torch.int64), n_contrib_tile.sum(dtype=torch.int64))})
-    state = RenderState(H, W, R, n_vis, point_list, ranges, final_T, n_contrib)
+    state = RenderState(H, W, R, n_vis, point_list, ranges, final_T, n_contrib, n_list)
     return color, n_render, n_consider, n_contrib_tile, out_observe, state
 
 
-def render_backward(state, means2D, conic_opacity, rgb, bg, compute_locally, dL_dpix, grad_accum=None):
-    """Returns the [P,16] per-Gaussian gradient record (see include/blitzgs_b200.h)."""
+def render_backward(state, means2D, conic_opacity, rgb, bg, compute_locally, dL_dpix, grad_accum=None,
+                    record_rows=None, n_rows=None):
+    """Returns the per-Gaussian gradient record (see include/blitzgs_b200.h):
+    [P,16], or [n_rows,16] with Gaussian i at row record_rows[i]."""
     means2D, conic_opacity, rgb, bg = map(_f32c, (means2D, conic_opacity, rgb, bg))
     dL_dpix = _f32c(dL_dpix)
     P = means2D.shape[0]
     if grad_accum is None:
-        grad_accum = torch.zeros((P, 16), dtype=torch.float32, device=means2D.device)
+        rows = P if record_rows is None else max(int(n_rows), 1)
+        grad_accum = torch.zeros((rows, 16), dtype=torch.float32, device=means2D.device)
     cl = compute_locally.contiguous().view(-1) if compute_locally is not None else None
     tok = TIMER.begin("blend_bwd")
     _lib.call("blitz_render_backward", P, state.H, state.W, ptr(state.point_list), ptr(state.ranges),
               ptr(state.final_T), ptr(state.n_contrib), ptr(means2D), ptr(conic_opacity), ptr(rgb), ptr(bg),
-              ptr(cl), ptr(dL_dpix), ptr(grad_accum), _lib.stream_ptr())
+              ptr(cl), ptr(dL_dpix), ptr(record_rows), ptr(grad_accum), _lib.stream_ptr())
     TIMER.end(tok, P=P, R=state.R, lazy=lambda: {"pairs": (state.n_contrib.sum(dtype=torch.int64),)})
     return grad_accum
 

@@ -30,16 +30,17 @@ class _ViewLoss(torch.autograd.Function):
     one camera band; activations are applied inside the kernels."""
 
     @staticmethod
-    def forward(ctx, xyz, s_raw, q_raw, o_raw, dc, rest, raster, gt, compute_locally, band, exact_norm):
+    def forward(ctx, xyz, s_raw, q_raw, o_raw, dc, rest, raster, gt, compute_locally, band, exact_norm, sparse_grad):
         H, W = int(raster.image_height), int(raster.image_width)
         sh = ops.sh_layout(dc=dc, rest=rest)
         rot_norm = q_raw.norm(dim=1) if exact_norm else None
-        use_list = compute_locally is None
-        means2D, depths, radii, conic, rgb, reg, vlist, vcount, counts, totals = ops.preprocess_forward_raw(
+        use_list = compute_locally is None or sparse_grad
+        means2D, depths, radii, conic, rgb, reg, vlist, vcount, counts, totals, slot_of = ops.preprocess_forward_raw(
             xyz, s_raw, q_raw, o_raw.reshape(-1), sh, raster, rot_norm, want_reg=True, want_list=use_list,
-            want_counts=True, compute_locally=compute_locally)
+            want_counts=True, compute_locally=compute_locally, want_slots=use_list)
         color, n_render, n_consider, n_contrib, out_observe, state = ops.render_forward(
-            means2D, depths, radii, conic, rgb, raster.bg, compute_locally, H, W, counts=counts, totals=totals)
+            means2D, depths, radii, conic, rgb, raster.bg, compute_locally, H, W, counts=counts, totals=totals,
+            vis_count=vcount)
         y0, y1 = band
         img_band = color[:, y0:y1, :]
         sums, partials = ops.loss_forward(img_band, gt)
@@ -48,8 +49,9 @@ class _ViewLoss(torch.autograd.Function):
         ctx.HW = (H, W)
         ctx.state = state
         ctx.cl = compute_locally
+        ctx.sparse_grad = sparse_grad
         ctx.save_for_backward(xyz, s_raw, q_raw, o_raw, dc, rest, means2D, conic, rgb, radii, gt, partials,
-                              img_band, rot_norm, vlist, vcount)
+                              img_band, rot_norm, vlist, vcount, slot_of)
         ctx.mark_non_differentiable(radii, out_observe, color)
         l1 = sums[0].to(torch.float32)
         ss = sums[1].to(torch.float32)
@@ -58,7 +60,7 @@ class _ViewLoss(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g_l1, g_ss, g_reg, _g_cnt, *_unused):
         (xyz, s_raw, q_raw, o_raw, dc, rest, means2D, conic, rgb, radii, gt, partials, img_band, rot_norm, vlist,
-         vcount) = ctx.saved_tensors
+         vcount, slot_of) = ctx.saved_tensors
         H, W = ctx.HW
         y0, y1 = ctx.band
         dev = xyz.device
@@ -70,22 +72,39 @@ class _ViewLoss(torch.autograd.Function):
         else:
             dL_dpix = torch.zeros((3, H, W), dtype=torch.float32, device=dev)
             dL_dpix[:, y0:y1, :] = g_band
-        rec = ops.render_backward(ctx.state, means2D, conic, rgb, ctx.raster.bg, ctx.cl, dL_dpix)
+        L = ctx.state.n_list
+        # gradient record: one row per listed Gaussian (slot_of) instead of P rows
+        rec = ops.render_backward(ctx.state, means2D, conic, rgb, ctx.raster.bg, ctx.cl, dL_dpix,
+                                  record_rows=slot_of, n_rows=L)
         sh = ops.sh_layout(dc=dc, rest=rest)
         M = rest.shape[1]
-        alloc = torch.zeros_like if vlist is not None else torch.empty_like
-        g_xyz, g_s, g_q, g_dc, g_rest = alloc(xyz), alloc(s_raw), alloc(q_raw), alloc(dc), alloc(rest)
-        g_o = alloc(o_raw)
         reg_scale = (g_reg if g_reg is not None else zero).float().reshape(1)
+        rows = ops.ROWS_UPSTREAM_BY_SLOT if slot_of is not None else 0
+        if ctx.sparse_grad:
+            # row j = the j-th listed Gaussian: every row written, no P-sized buffer
+            rows |= ops.ROWS_OUTPUT_BY_SLOT
+            n = max(L, 1)
+            shapes = [xyz.shape[1:], s_raw.shape[1:], q_raw.shape[1:], o_raw.shape[1:], dc.shape[1:], rest.shape[1:]]
+            g_xyz, g_s, g_q, g_o, g_dc, g_rest = [torch.empty((n,) + tuple(sz), dtype=torch.float32, device=dev)
+                                                  for sz in shapes]
+        else:
+            alloc = torch.zeros_like if vlist is not None else torch.empty_like
+            g_xyz, g_s, g_q, g_dc, g_rest = alloc(xyz), alloc(s_raw), alloc(q_raw), alloc(dc), alloc(rest)
+            g_o = alloc(o_raw)
         ops.preprocess_backward_raw(radii, means2D, xyz, s_raw, q_raw, o_raw.reshape(-1), sh, ctx.raster,
                                     rec[:, 0:2], rec[:, 8:12], rec[:, 12:15],
                                     (g_xyz, g_s, g_q, g_o, (g_dc, 3), (g_rest, max(M, 1) * 3)), rot_norm=rot_norm,
-                                    reg_scale=reg_scale, vis_list=vlist, vis_count=vcount)
-        return g_xyz, g_s, g_q, g_o, g_dc, g_rest, None, None, None, None, None
+                                    reg_scale=reg_scale, vis_list=vlist, vis_count=vcount, rows=rows)
+        grads = [g_xyz, g_s, g_q, g_o, g_dc, g_rest]
+        if ctx.sparse_grad:
+            idx = vlist[:L].to(torch.int64).unsqueeze(0)
+            grads = [torch.sparse_coo_tensor(idx, g[:L], p.shape, check_invariants=False)
+                     for g, p in zip(grads, (xyz, s_raw, q_raw, o_raw, dc, rest))]
+        return (*grads, None, None, None, None, None, None)
 
 
 def view_loss(model, raster, gt_band, compute_locally=None, band=None, lambda_dssim=LAMBDA_DSSIM,
-              scale_reg_weight=10.0, exact_norm=False):
+              scale_reg_weight=10.0, exact_norm=False, sparse_grad=False):
     """Loss of one camera exactly as batched_loss_computation forms it
     (loss_distribution.py:303-322): (1-l) L1/N3 + l (1 - SSIM/N3) +
     10 mean(min-axis scale of the Gaussians the exchange sends), N3 = 3 H W.
@@ -94,12 +113,18 @@ def view_loss(model, raster, gt_band, compute_locally=None, band=None, lambda_ds
     _features_rest); the activations run inside the preprocess kernels.
     The kernel computes ||_rotation|| with the summation order of PyTorch's
     norm (bit-identical); ``exact_norm=True`` takes it from PyTorch instead.
+    ``sparse_grad=True`` makes the parameter gradients sparse COO tensors
+    holding only the rows of the Gaussians with radius > 0 (every other row
+    of the dense gradient is exactly zero), for optimizers that take sparse
+    gradients such as torch.optim.SparseAdam -- the update rule of the
+    reference's SparseGaussianAdam, which only touches visible rows.
     Returns (loss, l1_sum, ssim_sum, radii, out_observe, color)."""
     xyz, s_raw, q_raw, o_raw, dc, rest = model
     H, W = int(raster.image_height), int(raster.image_width)
     band = band or (0, H)
     l1, ss, reg, cnt, radii, out_observe, color = _ViewLoss.apply(xyz, s_raw, q_raw, o_raw, dc, rest, raster,
-                                                                   gt_band, compute_locally, band, exact_norm)
+                                                                   gt_band, compute_locally, band, exact_norm,
+                                                                   sparse_grad)
     n3 = H * W * 3
     loss = (1.0 - lambda_dssim) * (l1 / n3) + lambda_dssim * (1.0 - ss / n3)
     if scale_reg_weight:

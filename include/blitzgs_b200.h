@@ -116,6 +116,8 @@ int blitz_preprocess_backward(int64_t P, int D, int M, const int32_t* radii, con
  *             totals (device uint64 [2]) = {tile instances R, Gaussians with
  *             at least one tile}: the output of blitz_render_count, fused
  *             (counts and totals must be both given or both NULL);
+ *   slot_of   device uint32 [P] (with a list): slot_of[i] = position of
+ *             listed Gaussian i in vis_list (other entries untouched);
  *   scratch   device buffer of blitz_preprocess_scratch_bytes(P) bytes: runs
  *             the cull and the full computation as two kernels (faster when
  *             most Gaussians are off-screen); NULL runs one kernel.
@@ -134,7 +136,7 @@ int blitz_preprocess_forward_raw(int64_t P, int D, int M, const float* xyz, cons
                                  float* means2D, float* depths, int32_t* radii, float* conic_opacity,
                                  float* rgb, double* reg_sums, uint32_t* vis_list, int32_t* vis_count,
                                  const uint8_t* compute_locally, uint32_t* counts, uint64_t* totals,
-                                 void* scratch, size_t scratch_bytes, void* stream);
+                                 uint32_t* slot_of, void* scratch, size_t scratch_bytes, void* stream);
 
 /*
  * Backward of blitz_preprocess_forward_raw: gradients with respect to the
@@ -145,7 +147,14 @@ int blitz_preprocess_forward_raw(int64_t P, int D, int M, const float* xyz, cons
  * `accumulate` selects whether their rows are stored (0) or added onto (1);
  * with NULL lists every Gaussian is processed and `accumulate` selects
  * overwrite (0) or add (1).
+ * rows (with a list only; 0 otherwise): BLITZ_ROWS_UPSTREAM_BY_SLOT reads the
+ * upstream gradients of the j-th listed Gaussian at row j (the compact record
+ * of blitz_render_backward with record_rows), BLITZ_ROWS_OUTPUT_BY_SLOT writes
+ * its gradients at row j of [vis_count, ...] outputs (every row written: no
+ * zero-fill; the gradient as sparse rows, indices = vis_list).
  */
+#define BLITZ_ROWS_UPSTREAM_BY_SLOT 1
+#define BLITZ_ROWS_OUTPUT_BY_SLOT 2
 int blitz_preprocess_backward_raw(int64_t P, int D, int M, const int32_t* radii, const float* means2D,
                                   const float* xyz, const float* scaling_raw, const float* rotation_raw,
                                   const float* rotation_norm, const float* opacity_raw, const float* sh_dc,
@@ -158,7 +167,7 @@ int blitz_preprocess_backward_raw(int64_t P, int D, int M, const int32_t* radii,
                                   const uint32_t* vis_list, const int32_t* vis_count, float* g_xyz,
                                   float* g_scaling_raw, float* g_rotation_raw, float* g_opacity_raw,
                                   float* g_dc, int64_t g_dc_stride, float* g_rest, int64_t g_rest_stride,
-                                  int accumulate, void* stream);
+                                  int accumulate, int rows, void* stream);
 
 /*
  * Render forward, phase 1 of 2: per-Gaussian tile-touch counts under the
@@ -234,18 +243,21 @@ int blitz_render_bin_noalloc(int64_t P, int64_t n_vis, int64_t R, int image_heig
  * Replaces _C.render_gaussians_backward / RenderGaussiansBackwardCUDA
  * (submodule/diff-gaussian-rasterization_r/rasterize_points.cu:364-436,
  * rasterizer_impl.cu:727-804, backward.cu:324-530).
- * grad_accum: float [P,16], zero on entry; per Gaussian the kernel adds
+ * grad_accum: float [rows,16], zero on entry; per Gaussian the kernel adds
  *   [0:2]  dL/dmeans2D (x,y)          [4:6]  sum |dL/dmeans2D| (x,y)
  *   [8:12] dL/dconic_opacity (c00, c01, c11, opacity)
  *   [12:15] dL/dcolors (r,g,b); other slots stay zero.
  * (The c01 entry keeps the reference's convention: half the derivative with
  * respect to the stored off-diagonal conic entry.)
+ * record_rows (may be NULL): row of Gaussian i's record, e.g. the slot_of map
+ * of blitz_preprocess_forward_raw, so the record has one row per listed
+ * Gaussian instead of P rows; NULL uses row i.
  */
 int blitz_render_backward(int64_t P, int image_height, int image_width, const uint32_t* point_list,
                           const uint32_t* ranges, const float* final_T, const uint32_t* n_contrib,
                           const float* means2D, const float* conic_opacity, const float* rgb,
                           const float* bg, const uint8_t* compute_locally, const float* dL_dpix,
-                          float* grad_accum, void* stream);
+                          const uint32_t* record_rows, float* grad_accum, void* stream);
 
 /*
  * Fused L1 + SSIM over a band [C,Hb,W] (forward).

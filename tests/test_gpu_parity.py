@@ -245,6 +245,37 @@ def test_fused_count_and_listed_rows_match_separate_passes(cuda_device, case, tw
     assert torch.equal(totals, fused[9])
 
 
+@pytest.mark.parametrize("scene", ["tiny", "mid"])
+def test_sparse_gradients_equal_dense_rows(cuda_device, scene):
+    """sparse_grad=True returns the same gradient as the dense path: the
+    listed rows hold the values the dense path scatters, and the dense path is
+    zero everywhere else.  (Not bit for bit: the render backward sums each
+    Gaussian's record with float atomics, whose order varies run to run.)
+    torch.optim.SparseAdam accepts it."""
+    sc = S.tiny(seed=9, P=20000, H=128, W=160) if scene == "tiny" else S.mid(seed=2, P=600_000, n_cams=1)
+    cam = sc.cameras[0].to(cuda_device)
+    gt = S.target_image(2, cam.image_height, cam.image_width).to(cuda_device)
+    rs = _raster(cam, cuda_device)
+    grads = []
+    for sparse in (False, True):
+        model = [t.to(cuda_device).requires_grad_(True) for t in scene_params(sc)]
+        loss, *_ = ST.view_loss(model, rs, gt, sparse_grad=sparse)
+        loss.backward()
+        grads.append([p.grad for p in model])
+        if sparse:
+            assert all(p.grad.is_sparse for p in model)
+            opt = torch.optim.SparseAdam(model, lr=1e-3)
+            opt.step()
+    for n, d, sp in zip(["xyz", "scaling", "rotation", "opacity", "dc", "rest"], *grads):
+        sd = sp.to_dense()
+        assert normwise_rel(sd.cpu(), d.cpu()) < 1e-5, n
+        rows = sp.coalesce().indices()[0]
+        assert rows.numel() > 0
+        outside = torch.ones(d.shape[0], dtype=torch.bool, device=d.device)
+        outside[rows] = False
+        assert not d[outside].any(), n  # the dense gradient is zero off the listed rows
+
+
 def test_drop_in_api_autograd_matches_fused(cuda_device):
     """GaussianRasterizer.preprocess_gaussians/render_gaussians (reference API)
     give the same loss and parameter gradients as the fused step."""
