@@ -298,14 +298,26 @@ def run_ours(args, ws, rank, local):
     clocks.mark()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
+    marks, host_t = [], []
     t0.record()
     for it in range(args.steps):
         one_step(args.warmup + it, False)
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()  # no synchronisation: per-step split of the same timed region
+        marks.append(ev)
+        host_t.append(time.perf_counter())
     t1.record()
     torch.cuda.synchronize()
     clocks.mark()
     barrier(ws)
     ms = max_over_ranks(t0.elapsed_time(t1), ws)
+    if rank == 0:
+        prev, split = t0, []
+        for ev in marks:
+            split.append(round(prev.elapsed_time(ev), 3))
+            prev = ev
+        log("timed-region per-step ms:", split,
+            "host ms:", [round((b - a) * 1e3, 3) for a, b in zip(host_t, host_t[1:])])
 
     # timed: end to end (GT uploaded from pinned host memory, loss read back)
     barrier(ws)
@@ -378,6 +390,31 @@ def stage_bytes(name, metas):
         else:
             return None
     return tot
+
+
+TRAFFIC_TABLE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles", "dram_traffic_city8M_bench.md")
+# native stage -> kernels of that stage in the ncu traffic table
+STAGE_KERNELS = {"blend_bwd": ["blend_bwd_kernel"], "blend_fwd": ["blend_fwd_kernel"],
+                 "preprocess_fwd": ["preprocess_cull_kernel", "preprocess_full_kernel"],
+                 "preprocess_bwd": ["preprocess_bwd_list_kernel<0>"]}
+
+
+def measured_traffic(stage, workload):
+    """DRAM bytes per launch of a stage's kernels (read + write, mean over the
+    launches of one ncu capture of this bench's city workload), or None."""
+    if workload != "city" or stage not in STAGE_KERNELS or not os.path.exists(TRAFFIC_TABLE):
+        return None
+    per = {}
+    for line in open(TRAFFIC_TABLE):
+        cells = [c.strip().strip("`") for c in line.strip().strip("|").split("|")]
+        if len(cells) == 6:
+            try:
+                per[cells[0]] = float(cells[4]) * 1e6
+            except ValueError:
+                pass
+    if not all(k in per for k in STAGE_KERNELS[stage]):
+        return None
+    return round(sum(per[k] for k in STAGE_KERNELS[stage]))
 
 
 def roofline_from_stages(stages, peaks, peak_kind, n_vis_per_call, fp32_peak=None):
@@ -656,6 +693,13 @@ def main():
     fp32 = _ops.fp32_peak_tflops()
     roof, stage_table = roofline_from_stages(r["stages"], peaks, pk, nv, fp32)
     roof_hbm = hbm_roofline(r["stages"], peaks, pk, nv)
+    for rf in (roof, roof_hbm):
+        # measured DRAM traffic of the same kernels on this workload (dense 1-GPU step)
+        t = measured_traffic(rf.get("kernel"), args.config) if rf and ws == 1 and not args.sparse_grad else None
+        if t is not None:
+            rf["traffic"] = t
+            rf["traffic_source"] = ("ncu dram__bytes_read.sum + dram__bytes_write.sum, mean per launch: "
+                                    "profiles/dram_traffic_city8M_bench.md")
     cb = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         try:
@@ -663,7 +707,7 @@ def main():
         except Exception as ex:  # the baseline must not sink the bench line
             cb = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "port", "sample": f"failed: {ex}"}
     cfg.update(gaussians=r["P"], image=f"{r['W']}x{r['H']}")
-    # native kernels launched per view (preprocess 1, count 1, binning+blend fwd, loss 2, blend bwd 1,
+    # native kernels launched per view (preprocess cull + full 2, binning+blend fwd, loss 2, blend bwd 1,
     # preprocess bwd 1); the binning figure counts the cub launches seen in the ncu launch list
     launches_per_view = 1 + 1 + KERNELS_RENDER_FWD + 2 + 1 + 1
     line = {"metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
