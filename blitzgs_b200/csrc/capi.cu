@@ -159,7 +159,8 @@ int blitz_preprocess_forward_raw(int64_t P, int D, int M, const float* xyz, cons
                                  float* means2D, float* depths, int32_t* radii, float* conic_opacity,
                                  float* rgb, double* reg_sums, uint32_t* vis_list, int32_t* vis_count,
                                  const uint8_t* compute_locally, uint32_t* counts, uint64_t* totals,
-                                 uint32_t* slot_of, void* scratch, size_t scratch_bytes, void* stream) {
+                                 uint32_t* slot_of, const blitz_exchange_out* exchange, void* scratch,
+                                 size_t scratch_bytes, void* stream) {
   if (P < 0 || D < 0 || D > 3 || M < 0 || M > 15 || image_height <= 0 || image_width <= 0)
     return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: bad sizes");
   if (P == 0) return 0;
@@ -181,6 +182,19 @@ int blitz_preprocess_forward_raw(int64_t P, int D, int M, const float* xyz, cons
   p.listed_rows_only = vis_list != nullptr;
   if (slot_of && !vis_list) return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: slot_of needs vis_list");
   p.slot_of_out = slot_of;
+  if (exchange && exchange->n_ranks > 0) {
+    const blitz_exchange_out& x = *exchange;
+    if (!vis_list || x.n_ranks > 32 || !x.tile_lo || !x.tile_hi || !x.records || !x.dest_mask || !x.dest_counts)
+      return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: exchange outputs need vis_list, n_ranks <= 32 and "
+                                "non-null buffers");
+    if (!aligned16(x.records)) return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: records must be 16-byte aligned");
+    p.x_ranks = x.n_ranks;
+    p.x_tile_lo = x.tile_lo;
+    p.x_tile_hi = x.tile_hi;
+    p.x_records = x.records;
+    p.x_mask = x.dest_mask;
+    p.x_counts = x.dest_counts;
+  }
   p.counts_out = counts;
   p.totals_out = reinterpret_cast<unsigned long long*>(totals);
   p.compute_locally = reinterpret_cast<const bool*>(compute_locally);
@@ -459,6 +473,27 @@ int blitz_get_local2j_ids_bool(int image_height, int image_width, int mp_rank, i
   r.avoid_pixel_all2all = avoid_pixel_all2all != 0;
   r.out_bool = reinterpret_cast<bool*>(out);
   return check(launch_route_bool(r, S(stream)), "blitz_get_local2j_ids_bool");
+}
+
+int blitz_exchange_pack(int64_t n_rows, int n_ranks, const float* records, const uint32_t* dest_mask,
+                        const int64_t* dest_offset, int32_t* cursor, float* send, int32_t* send_row,
+                        int32_t row_base, void* stream) {
+  if (n_rows < 0 || n_ranks <= 0 || n_ranks > 32) return fail(BLITZ_EINVAL, "blitz_exchange_pack: bad sizes");
+  if (n_rows == 0) return 0;
+  if (!records || !dest_mask || !dest_offset || !cursor || !send || !send_row)
+    return fail(BLITZ_EINVAL, "blitz_exchange_pack: null pointer");
+  if (!aligned16(records) || !aligned16(send)) return fail(BLITZ_EINVAL, "blitz_exchange_pack: 16-byte alignment");
+  PackParams k{};
+  k.n_rows = n_rows;
+  k.n_ranks = n_ranks;
+  for (int r = 0; r < n_ranks; ++r) k.dest_offset[r] = dest_offset[r];
+  k.records = records;
+  k.mask = dest_mask;
+  k.cursor = cursor;
+  k.send = send;
+  k.send_row = send_row;
+  k.row_base = row_base;
+  return check(launch_exchange_pack(k, S(stream)), "blitz_exchange_pack");
 }
 
 int blitz_fp32_probe(int blocks, int64_t iters, float* sink, void* stream) {

@@ -57,6 +57,16 @@ struct PreprocessParams {
   // counts) written; the caller reads other rows through vis_list_out.
   bool listed_rows_only;
   uint32_t* slot_of_out;  // optional [P]: list position of each listed Gaussian (others untouched)
+  // Optional exchange outputs of the multi-GPU step (need vis_list_out): row
+  // j = the j-th listed Gaussian's 12-float record and its destination mask
+  // (bit r: its square tile rect overlaps rank r's tile interval
+  // [x_tile_lo[r], x_tile_hi[r])), x_counts[r] += rows for rank r.
+  int x_ranks;              // <= 32; 0 = no exchange outputs
+  const int* x_tile_lo;     // device [x_ranks]
+  const int* x_tile_hi;     // device [x_ranks]
+  float* x_records;         // [P,12]
+  uint32_t* x_mask;         // [P]
+  int* x_counts;            // [x_ranks], zero on entry
 };
 
 struct PreprocessBwdParams {
@@ -200,6 +210,23 @@ struct RouteParams {
   bool* out_bool;                   // [P, world_size]
 };
 int launch_route_bool(const RouteParams& p, cudaStream_t st);
+
+// Pack rows [0, n_rows) of a camera's exchange records into the send buffer:
+// row j goes to every rank r whose bit is set in mask[j], at
+// dest_offset[r] + (its running position among rank r's rows); send_row
+// receives row_base + j there.  cursor: device [n_ranks], zero on entry.
+struct PackParams {
+  int64_t n_rows;
+  int n_ranks;
+  int64_t dest_offset[32];
+  const float* records;  // [n_rows,12]
+  const uint32_t* mask;  // [n_rows]
+  int* cursor;
+  float* send;           // [*,12]
+  int* send_row;         // [*]
+  int row_base;
+};
+int launch_exchange_pack(const PackParams& p, cudaStream_t st);
 
 int launch_fma_probe(int blocks, int64_t iters, float* sink, cudaStream_t st);
 

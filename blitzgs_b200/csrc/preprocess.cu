@@ -418,10 +418,35 @@ __device__ __forceinline__ void full_phase(const PreprocessParams& p, const floa
       *s_base = tot ? atomicAdd(p.vis_count_out, tot) : 0;
     }
     __syncthreads();
+    uint32_t dest = 0u;
     if (listed) {
       const uint32_t slot = (uint32_t)(*s_base + s_wc[warp] + __popc(m & ((1u << lane) - 1u)));
       p.vis_list_out[slot] = (uint32_t)i;
       if (p.slot_of_out) p.slot_of_out[i] = slot;
+      if (p.x_ranks) {
+        // exchange record: conic+opacity | means2D | rgb | depth | radius bits | min scale
+        float4* r4 = reinterpret_cast<float4*>(p.x_records + 12 * (int64_t)slot);
+        r4[0] = res.conic_op;
+        r4[1] = make_float4(res.pimg.x, res.pimg.y, res.rgb.x, res.rgb.y);
+        r4[2] = make_float4(res.rgb.z, res.depth, __int_as_float(res.radius), res.smin);
+        // destinations: the reference getTouchedIdsBool test on the square
+        // tile rect (rasterize_points.cu:212-256) against each rank's rows
+        int2 lo, hi;
+        tile_rect_int(res.pimg, res.radius, p.grid_x, p.grid_y, lo, hi);
+        const int tmin = lo.y * p.grid_x + lo.x;
+        const int tmax = (hi.y - 1) * p.grid_x + hi.x - 1;
+        if (tmax >= tmin)
+          for (int r = 0; r < p.x_ranks; ++r)
+            if (!(tmax < __ldg(p.x_tile_lo + r) || tmin >= __ldg(p.x_tile_hi + r))) dest |= 1u << r;
+        p.x_mask[slot] = dest;
+      }
+    }
+    if (p.x_ranks) {
+      // per-destination row counts: one atomic per warp and rank
+      for (int r = 0; r < p.x_ranks; ++r) {
+        const unsigned b = __ballot_sync(0xffffffffu, (dest >> r) & 1u);
+        if (lane == 0 && b) atomicAdd(p.x_counts + r, __popc(b));
+      }
     }
     __syncthreads();  // s_wc / s_base are rewritten next round
   }

@@ -40,7 +40,47 @@ __global__ void __launch_bounds__(256) route_bool_kernel(RouteParams p) {
   }
 }
 
+// One thread per row; a row sent to k ranks takes k slots.  Positions within
+// a (rank, camera) segment come from warp-aggregated atomics, so their order
+// varies run to run; send_row records where each one came from.
+__global__ void __launch_bounds__(256) exchange_pack_kernel(PackParams p) {
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int lane = threadIdx.x & 31;
+  const bool in = j < p.n_rows;
+  const uint32_t m = in ? __ldg(p.mask + j) : 0u;
+  float4 r0, r1, r2;
+  if (m) {
+    const float4* src = reinterpret_cast<const float4*>(p.records + 12 * j);
+    r0 = src[0];
+    r1 = src[1];
+    r2 = src[2];
+  }
+  for (int r = 0; r < p.n_ranks; ++r) {
+    const bool mine = (m >> r) & 1u;
+    const unsigned b = __ballot_sync(0xffffffffu, mine);
+    if (!b) continue;
+    int base = 0;
+    if (lane == __ffs(b) - 1) base = atomicAdd(p.cursor + r, __popc(b));
+    base = __shfl_sync(0xffffffffu, base, __ffs(b) - 1);
+    if (mine) {
+      const int64_t pos = p.dest_offset[r] + base + __popc(b & ((1u << lane) - 1u));
+      float4* dst = reinterpret_cast<float4*>(p.send + 12 * pos);
+      dst[0] = r0;
+      dst[1] = r1;
+      dst[2] = r2;
+      p.send_row[pos] = p.row_base + (int)j;
+    }
+  }
+}
+
 }  // namespace
+
+int launch_exchange_pack(const PackParams& p, cudaStream_t st) {
+  if (p.n_rows <= 0) return 0;
+  const int threads = 256;
+  exchange_pack_kernel<<<(unsigned)((p.n_rows + threads - 1) / threads), threads, 0, st>>>(p);
+  return (int)cudaGetLastError();
+}
 
 int launch_route_bool(const RouteParams& p, cudaStream_t st) {
   if (p.P <= 0) return 0;

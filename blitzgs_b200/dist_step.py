@@ -3,11 +3,13 @@
 Per step, for a batch of cameras split into tile-row bands by
 ``start_strategy_final``:
   forward   every rank runs the fused raw preprocess (activations in the
-            kernel) of its spatial shard for every camera, routes each
-            listed Gaussian (radius > 0) to the ranks whose bands its tile
-            rect overlaps (the reference's get_local2j_ids semantics), and
-            ONE all_to_all_single moves a 12-float record per (Gaussian,
-            camera, destination); each rank renders its bands and computes
+            kernel) of its spatial shard for every camera; the same kernel
+            writes each listed Gaussian's (radius > 0) 12-float exchange
+            record and the ranks whose bands its tile rect overlaps (the
+            reference's get_local2j_ids semantics); one all-gather of the
+            per-destination counts sizes the exchange, a pack kernel fills
+            the send buffer, and ONE all_to_all_single moves a record per
+            (Gaussian, camera, destination); each rank renders its bands and computes
             the band loss (L1 + SSIM + the min-scale regulariser over the
             received visible Gaussians, loss_distribution.py:303-322);
   backward  band loss / render backward on the receivers, ONE reverse
@@ -18,7 +20,7 @@ Per step, for a batch of cameras split into tile-row bands by
 These two all-to-alls and the tiny size all-gather are the only collectives
 (the reference additionally all-gathers sizes with a blocking .cpu() and
 runs a second all-to-all for radii/depths).  Host synchronisations per step:
-the visible-list lengths, the routed-pair count, and the size all-gather.
+the count all-gather, and one per rendered camera to size its binning.
 """
 import torch
 
@@ -46,54 +48,52 @@ class _DistributedBatch(torch.autograd.Function):
         ws = torch.distributed.get_world_size(group)
         dev = xyz.device
         sh = ops.sh_layout(dc=dc, rest=rest)
-        # 1. preprocess every camera (no host sync in between)
+        # 1. preprocess every camera; the kernel also writes each listed
+        #    Gaussian's exchange record, its destination ranks and the
+        #    per-destination counts (no host synchronisation in between)
+        P = xyz.shape[0]
+        gx = D.CONTEXT.TILE_X
+        table = _pinned_table(n_cams, ws)  # tile interval [lo, hi) of every rank, per camera
+        for k, st in enumerate(strategies):
+            for r_local, g in enumerate(st.gpu_ids):
+                table[k, 0, g] = st.division_pos[r_local] * gx
+                table[k, 1, g] = st.division_pos[r_local + 1] * gx
+        table_dev = table[:n_cams].to(dev, non_blocking=True)
+        cnt = torch.zeros((n_cams, 1 + ws), dtype=torch.int32, device=dev)  # list length | rows per rank
         pre = []
-        for rs in rasters:
+        for k, rs in enumerate(rasters):
+            xrec = torch.empty((max(P, 1), _FWD_C), dtype=torch.float32, device=dev)
+            xmask = torch.empty((max(P, 1),), dtype=torch.int32, device=dev)
             m2, d, r, co, rgb, _, vlist, vcount, _, _, _ = ops.preprocess_forward_raw(
-                xyz, s_raw, q_raw, o_raw.reshape(-1), sh, rs, None, want_reg=False, want_list=True)
-            pre.append((m2, d, r, co, rgb, vlist, vcount))
-        counts = torch.cat([p[6] for p in pre]).cpu().tolist() if n_cams else []
-        # 2. pack the listed Gaussians' records and route them (one nonzero for the batch)
-        recs, masks, ids_all = [], [], []
-        for k, (m2, d, r, co, rgb, vlist, vcount) in enumerate(pre):
-            ids = vlist[:counts[k]].to(torch.int64)
-            ids_all.append(ids)
-            m2c, rc = m2.index_select(0, ids), r.index_select(0, ids)
-            smin = torch.exp(s_raw.index_select(0, ids)).min(dim=1).values
-            recs.append(torch.cat([co.index_select(0, ids), m2c, rgb.index_select(0, ids), d.index_select(0, ids)[:, None],
-                                   rc.view(torch.float32)[:, None], smin[:, None]], 1))
-            st = strategies[k]
-            dist_global = torch.tensor(st.division_pos, dtype=torch.int32, device=dev) * D.CONTEXT.TILE_X
-            mk = ops.local2j_ids_bool(rs_h(rasters[k]), rs_w(rasters[k]), st.rank, st.world_size, m2c, rc,
-                                      dist_global, False)
-            # columns are the camera's renderers; widen to all ranks
-            full = torch.zeros((mk.shape[0], ws), dtype=torch.bool, device=dev)
-            full[:, torch.tensor(st.gpu_ids, device=dev)] = mk
-            masks.append(full)
+                xyz, s_raw, q_raw, o_raw.reshape(-1), sh, rs, None, want_reg=False, want_list=True,
+                vis_count=cnt[k, 0:1], exchange=(table_dev[k, 0], table_dev[k, 1], xrec, xmask, cnt[k, 1:]))
+            pre.append((m2, r, vlist, vcount, xrec, xmask))
+        # 2. one all-gather of every rank's counts: the only host synchronisation
+        #    before the render (it sizes the all-to-all on every rank)
+        gdev = dev if torch.distributed.get_backend(group) == "nccl" else torch.device("cpu")
+        allc = torch.empty((ws * n_cams, 1 + ws), dtype=torch.int32, device=gdev)
+        torch.distributed.all_gather_into_tensor(allc, cnt.to(gdev), group=group)
+        allc = allc.view(ws, n_cams, 1 + ws).cpu().tolist()
+        counts = [allc[rank][k][0] for k in range(n_cams)]
+        size = [[[allc[i][k][1 + j] for k in range(n_cams)] for j in range(ws)] for i in range(ws)]
+        plan = D.plan_from_sizes(size, n_cams, rank, ws)
         offs = [0]
         for c in counts:
             offs.append(offs[-1] + c)
-        records = torch.cat(recs, 0) if recs else torch.zeros((0, _FWD_C), device=dev)
-        mask = torch.cat(masks, 0) if masks else torch.zeros((0, ws), dtype=torch.bool, device=dev)
-        cam_of_row = torch.repeat_interleave(torch.arange(n_cams, device=dev), torch.tensor(counts, device=dev))
-        nz = mask.nonzero()
-        rows, dst = nz[:, 0], nz[:, 1]
-        key = dst * n_cams + cam_of_row.index_select(0, rows)
-        order = torch.sort(key, stable=True).indices
-        send_rows = rows.index_select(0, order)
-        sizes = torch.bincount(key, minlength=ws * n_cams).cpu().tolist()
-        # send_ids[k][j]: compact positions of camera k's records for rank j
-        send_ids = [[None] * ws for _ in range(n_cams)]
-        pos = 0
+        n_send = sum(plan.send_splits)
+        send = torch.empty((max(n_send, 1), _FWD_C), dtype=torch.float32, device=dev)
+        send_row = torch.empty((max(n_send, 1),), dtype=torch.int32, device=dev)
+        cursor = torch.zeros((n_cams, ws), dtype=torch.int32, device=dev)
+        base = [0]
         for j in range(ws):
-            for k in range(n_cams):
-                c = sizes[j * n_cams + k]
-                send_ids[k][j] = send_rows[pos:pos + c] - offs[k]
-                pos += c
-        plan = D.plan_exchange(send_ids, n_cams, group)
-        send = records.index_select(0, send_rows)
+            base.append(base[-1] + plan.send_splits[j])
+        for k in range(n_cams):
+            if counts[k] == 0:
+                continue
+            dest_off = [base[j] + sum(size[rank][j][:k]) for j in range(ws)]
+            ops.exchange_pack(counts[k], pre[k][4], pre[k][5], dest_off, cursor[k], send, send_row, offs[k])
         recv_buf = torch.empty((sum(plan.recv_splits), _FWD_C), dtype=torch.float32, device=dev)
-        torch.distributed.all_to_all_single(recv_buf, send, plan.recv_splits, plan.send_splits, group=group)
+        torch.distributed.all_to_all_single(recv_buf, send[:n_send], plan.recv_splits, plan.send_splits, group=group)
         recv = {}
         for k, parts in plan.recv_offsets.items():
             tot = sum(c for _, _, c in parts)
@@ -134,10 +134,9 @@ class _DistributedBatch(torch.autograd.Function):
         ctx.setup = setup
         ctx.plan = plan
         ctx.saved = saved
-        ctx.pre = [(p[0], p[2], p[5], p[6]) for p in pre]  # means2D, radii, vis_list, vis_count
+        ctx.pre = [(p[0], p[1], p[2], p[3]) for p in pre]  # means2D, radii, vis_list, vis_count
         ctx.counts, ctx.offs = counts, offs
-        ctx.send_rows = send_rows
-        ctx.ids_all = ids_all
+        ctx.send_rows = send_row[:n_send].to(torch.int64)
         ctx.save_for_backward(xyz, s_raw, q_raw, o_raw, dc, rest)
         return loss_sum
 
@@ -184,19 +183,26 @@ class _DistributedBatch(torch.autograd.Function):
                                         vis_list=vlist, vis_count=vcount, accumulate=True,
                                         rows=ops.ROWS_UPSTREAM_BY_SLOT)
             # min-scale regulariser: to the smallest axis of exp(_scaling), chained through exp
-            ids = ctx.ids_all[k]
+            ids = vlist[:ctx.counts[k]].to(torch.int64)
             s_act = torch.exp(s_raw.detach().index_select(0, ids))
             mn, am = s_act.min(dim=1)
             g_s.index_put_((ids, am), a[:, 11] * mn, accumulate=True)
         return g_xyz, g_s, g_q, g_o, g_dc, g_rest, None
 
 
-def rs_h(rs):
-    return int(rs.image_height)
+_TABLE = {}
 
 
-def rs_w(rs):
-    return int(rs.image_width)
+def _pinned_table(n_cams, ws):
+    """Reused pinned host buffer [n_cams, 2, ws] of per-rank tile intervals
+    (zeros: a rank that renders none of a camera).  Reuse is safe: every step
+    synchronises with the host (the count all-gather) after its copy."""
+    t = _TABLE.get(ws)
+    if t is None or t.shape[0] < n_cams:
+        t = torch.zeros((max(n_cams, 8), 2, ws), dtype=torch.int32).pin_memory()
+        _TABLE[ws] = t
+    t[:n_cams].zero_()
+    return t
 
 
 def batch_loss(shard_model, rasters, gts, strategies, group=None, lambda_dssim=0.2, reg_w=10.0):

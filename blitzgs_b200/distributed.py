@@ -318,6 +318,12 @@ def plan_exchange(send_ids, n_cams, group=None):
     allsz = torch.empty((ws * ws, n_cams), dtype=torch.int64, device=gdev)
     dist.all_gather_into_tensor(allsz, local.to(gdev), group=group)
     size = allsz.view(ws, ws, n_cams).cpu().tolist()
+    return plan_from_sizes(size, n_cams, rank, ws, send_ids)
+
+
+def plan_from_sizes(size, n_cams, rank, ws, send_ids=None):
+    """Splits and receive offsets from size[src][dst][cam] (the same matrix on
+    every rank)."""
     my_cams = [k for k in range(n_cams) if any(size[i][rank][k] for i in range(ws))]
     plan = ExchangePlan(send_ids=send_ids, size=size, my_cams=my_cams)
     plan.send_splits = [sum(size[rank][j]) for j in range(ws)]

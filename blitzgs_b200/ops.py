@@ -197,7 +197,7 @@ def preprocess_backward(radii, means3D, scales, rotations, sh, raster, g_means2D
 
 def preprocess_forward_raw(xyz, scaling_raw, rotation_raw, opacity_raw, sh, raster, rot_norm=None, *,
                            want_reg=True, want_list=True, want_counts=False, compute_locally=None,
-                           two_pass=True, want_slots=False):
+                           two_pass=True, want_slots=False, vis_count=None, exchange=None):
     """Preprocess from the raw model parameters (activations fused into the
     kernel).  Returns (means2D, depths, radii, conic_opacity, rgb, reg_sums
     double[2] or None, vis_list or None, vis_count or None, counts or None,
@@ -210,7 +210,10 @@ def preprocess_forward_raw(xyz, scaling_raw, rotation_raw, opacity_raw, sh, rast
     ``two_pass`` runs the cull and the full computation as two kernels (with
     a scratch candidate list); False runs the single persistent kernel.
     ``want_slots`` returns slot_of [P] (list position of each listed
-    Gaussian), which indexes the compact gradient record of the backward."""
+    Gaussian), which indexes the compact gradient record of the backward.
+    ``vis_count``: caller's zeroed int32 [1] counter for the list length.
+    ``exchange`` = (tile_lo, tile_hi, records, dest_mask, dest_counts): the
+    multi-GPU exchange outputs (see blitz_exchange_out in the C header)."""
     _require_cuda(xyz, scaling_raw, rotation_raw, opacity_raw)
     xyz, scaling_raw, rotation_raw, opacity_raw = map(_f32c, (xyz, scaling_raw, rotation_raw, opacity_raw))
     dc, dcs, rest, rs, M, _keep = sh
@@ -224,7 +227,12 @@ def preprocess_forward_raw(xyz, scaling_raw, rotation_raw, opacity_raw, sh, rast
     rgb = torch.empty((P, 3), dtype=torch.float32, device=dev)
     reg = torch.zeros((2,), dtype=torch.float64, device=dev) if want_reg else None
     vlist = torch.empty((max(P, 1),), dtype=torch.int32, device=dev) if want_list else None
-    vcount = torch.zeros((1,), dtype=torch.int32, device=dev) if want_list else None
+    vcount = (vis_count if vis_count is not None else torch.zeros((1,), dtype=torch.int32, device=dev)) \
+        if want_list else None
+    xo = None
+    if exchange is not None:
+        lo, hi, xrec, xmask, xcnt = exchange
+        xo = ExchangeOut(int(lo.numel()), ptr(lo), ptr(hi), ptr(xrec), ptr(xmask), ptr(xcnt))
     counts = torch.empty((max(P, 1),), dtype=torch.int32, device=dev) if want_counts else None
     totals = torch.empty((2,), dtype=torch.int64, device=dev) if want_counts else None
     cl = _tile_mask(compute_locally, H, W) if want_counts else None
@@ -238,11 +246,27 @@ def preprocess_forward_raw(xyz, scaling_raw, rotation_raw, opacity_raw, sh, rast
                   ptr(_f32c(raster.campos)), float(raster.tanfovx), float(raster.tanfovy),
                   H, W, ptr(means2D), ptr(depths), ptr(radii),
                   ptr(conic), ptr(rgb), ptr(reg), ptr(vlist), ptr(vcount), ptr(cl), ptr(counts), ptr(totals),
-                  ptr(slot_of), ptr(scratch), scratch.numel() if two_pass else 0, _lib.stream_ptr())
+                  ptr(slot_of), ctypes.addressof(xo) if xo is not None else None, ptr(scratch),
+                  scratch.numel() if two_pass else 0, _lib.stream_ptr())
         TIMER.end(tok, P=P, fused_count=want_counts, lazy=lambda: {"n_list": vcount} if want_list else {})
     elif want_counts:
         totals.zero_()
     return means2D, depths, radii, conic, rgb, reg, vlist, vcount, counts, totals, slot_of
+
+
+class ExchangeOut(ctypes.Structure):
+    """blitz_exchange_out of include/blitzgs_b200.h."""
+    _fields_ = [("n_ranks", ctypes.c_int), ("tile_lo", ctypes.c_void_p), ("tile_hi", ctypes.c_void_p),
+                ("records", ctypes.c_void_p), ("dest_mask", ctypes.c_void_p), ("dest_counts", ctypes.c_void_p)]
+
+
+def exchange_pack(n_rows, records, dest_mask, dest_offset, cursor, send, send_row, row_base):
+    """Pack n_rows exchange records into the send buffer (blitz_exchange_pack);
+    dest_offset: list of per-rank starting rows."""
+    n_ranks = len(dest_offset)
+    offs = (ctypes.c_int64 * n_ranks)(*[int(x) for x in dest_offset])
+    _lib.call("blitz_exchange_pack", int(n_rows), n_ranks, ptr(records), ptr(dest_mask), ctypes.addressof(offs),
+              ptr(cursor), ptr(send), ptr(send_row), int(row_base), _lib.stream_ptr())
 
 
 ROWS_UPSTREAM_BY_SLOT = 1  # BLITZ_ROWS_UPSTREAM_BY_SLOT

@@ -118,6 +118,7 @@ int blitz_preprocess_backward(int64_t P, int D, int M, const int32_t* radii, con
  *             (counts and totals must be both given or both NULL);
  *   slot_of   device uint32 [P] (with a list): slot_of[i] = position of
  *             listed Gaussian i in vis_list (other entries untouched);
+ *   exchange  host pointer to a blitz_exchange_out (with a list; NULL = none);
  *   scratch   device buffer of blitz_preprocess_scratch_bytes(P) bytes: runs
  *             the cull and the full computation as two kernels (faster when
  *             most Gaussians are off-screen); NULL runs one kernel.
@@ -127,6 +128,33 @@ int blitz_preprocess_backward(int64_t P, int D, int M, const int32_t* radii, con
 /* Size of the optional scratch of blitz_preprocess_forward_raw (no reference
  * counterpart: the reference allocates its temporaries per call). */
 size_t blitz_preprocess_scratch_bytes(int64_t P);
+
+/*
+ * Optional exchange outputs of blitz_preprocess_forward_raw for the
+ * multi-GPU step (they need vis_list).  They replace the record packing and
+ * the getTouchedIdsBool routing of all_to_all_communication_final
+ * (gaussian_renderer/__init__.py:22-189, f/rasterize_points.cu:212-256) for
+ * the listed Gaussians only, inside the preprocess kernel.  Row j belongs to
+ * the j-th listed Gaussian (vis_list[j]):
+ *   records   [P,12] float, 16-byte aligned: conic00 conic01 conic11 opacity |
+ *             means2D x y | r g b | depth | radius (int32 bits) | smallest
+ *             activated scale;
+ *   dest_mask [P] uint32: bit r set when the Gaussian's square tile rect,
+ *             flattened to the tile-id interval [ymin*gx+xmin,
+ *             (ymax-1)*gx+xmax-1], overlaps rank r's interval
+ *             [tile_lo[r], tile_hi[r]) (an empty interval sends nothing);
+ *   dest_counts [n_ranks] int32, zero on entry: rows per destination rank.
+ * tile_lo / tile_hi: device int32 [n_ranks] (n_ranks <= 32); a rank that
+ * renders none of this camera gets lo = hi = 0.
+ */
+typedef struct blitz_exchange_out {
+  int n_ranks;
+  const int32_t* tile_lo;
+  const int32_t* tile_hi;
+  float* records;
+  uint32_t* dest_mask;
+  int32_t* dest_counts;
+} blitz_exchange_out;
 int blitz_preprocess_forward_raw(int64_t P, int D, int M, const float* xyz, const float* scaling_raw,
                                  const float* rotation_raw, const float* rotation_norm,
                                  const float* opacity_raw, const float* sh_dc, int64_t dc_stride,
@@ -136,7 +164,8 @@ int blitz_preprocess_forward_raw(int64_t P, int D, int M, const float* xyz, cons
                                  float* means2D, float* depths, int32_t* radii, float* conic_opacity,
                                  float* rgb, double* reg_sums, uint32_t* vis_list, int32_t* vis_count,
                                  const uint8_t* compute_locally, uint32_t* counts, uint64_t* totals,
-                                 uint32_t* slot_of, void* scratch, size_t scratch_bytes, void* stream);
+                                 uint32_t* slot_of, const blitz_exchange_out* exchange, void* scratch,
+                                 size_t scratch_bytes, void* stream);
 
 /*
  * Backward of blitz_preprocess_forward_raw: gradients with respect to the
@@ -278,6 +307,20 @@ int blitz_loss_forward(int C, int Hb, int W, const float* img, const uint8_t* gt
 int blitz_loss_backward(int C, int Hb, int W, const float* img, const uint8_t* gt_u8,
                         const float* gt_f32, const float* window11, const float* partials,
                         const float* scale, float* dL_dimg, void* stream);
+
+/*
+ * Send-buffer packing of one camera's exchange records (no reference
+ * counterpart: the reference gathers with torch index_select per rank).
+ * Row j < n_rows of records/dest_mask goes to every rank r with bit r set,
+ * at row dest_offset[r] + k of send [*,12] (16-byte aligned), k counting
+ * that rank's rows of this call; send_row receives row_base + j there.
+ * dest_offset: HOST int64 array [n_ranks] (n_ranks <= 32); cursor: device
+ * int32 [n_ranks], zero on entry.  The order of the rows inside one rank's
+ * segment varies from run to run.
+ */
+int blitz_exchange_pack(int64_t n_rows, int n_ranks, const float* records, const uint32_t* dest_mask,
+                        const int64_t* dest_offset, int32_t* cursor, float* send, int32_t* send_row,
+                        int32_t row_base, void* stream);
 
 /*
  * Routing mask bool [P, mp_world_size]: Gaussian i overlaps the tile-id
