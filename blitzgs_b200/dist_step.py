@@ -26,6 +26,7 @@ import torch
 
 from . import distributed as D
 from . import ops
+from .step import _zero_fill_async
 
 # forward record: conic00 conic01 conic11 opacity | x y | r g b | depth radius(bits) minscale
 _FWD_C = 12
@@ -147,6 +148,10 @@ class _DistributedBatch(torch.autograd.Function):
         n_cams = len(rasters)
         dev = xyz.device
         plan = ctx.plan
+        # the shard's dense gradients are zero except at listed rows: fill them on
+        # a side stream while the render backward (issue bound) runs
+        grads = [torch.empty_like(t) for t in (xyz, s_raw, q_raw, o_raw, dc, rest)]
+        fill_done = _zero_fill_async(grads)
         # receiver: render backward of the owned bands -> 12-float gradient records
         send = torch.zeros((sum(plan.recv_splits), _BWD_C), dtype=torch.float32, device=dev)
         for k, (state, m2, conic, rgb, cl, band, gt, partials, vis, nvis, (y0, y1), n3) in ctx.saved.items():
@@ -171,7 +176,8 @@ class _DistributedBatch(torch.autograd.Function):
         acc.index_add_(0, ctx.send_rows, recv)
         sh = ops.sh_layout(dc=dc, rest=rest)
         M = rest.shape[1]
-        g_xyz, g_s, g_q, g_o, g_dc, g_rest = (torch.zeros_like(t) for t in (xyz, s_raw, q_raw, o_raw, dc, rest))
+        g_xyz, g_s, g_q, g_o, g_dc, g_rest = grads
+        torch.cuda.current_stream(dev).wait_event(fill_done)
         for k in range(n_cams):
             m2, r, vlist, vcount = ctx.pre[k]
             a = acc[ctx.offs[k]:ctx.offs[k + 1]]

@@ -73,6 +73,13 @@ class _ViewLoss(torch.autograd.Function):
             dL_dpix = torch.zeros((3, H, W), dtype=torch.float32, device=dev)
             dL_dpix[:, y0:y1, :] = g_band
         L = ctx.state.n_list
+        dense_fill = None
+        if not ctx.sparse_grad and vlist is not None:
+            # The dense gradients are zero except at listed rows.  Their fill is
+            # pure HBM writes (236 B per Gaussian); on a side stream it runs
+            # beside the issue-bound loss and render backward instead of after them.
+            grads_dense = [torch.empty_like(t) for t in (xyz, s_raw, q_raw, o_raw, dc, rest)]
+            dense_fill = _zero_fill_async(grads_dense)
         # gradient record: one row per listed Gaussian (slot_of) instead of P rows
         rec = ops.render_backward(ctx.state, means2D, conic, rgb, ctx.raster.bg, ctx.cl, dL_dpix,
                                   record_rows=slot_of, n_rows=L)
@@ -87,10 +94,12 @@ class _ViewLoss(torch.autograd.Function):
             shapes = [xyz.shape[1:], s_raw.shape[1:], q_raw.shape[1:], o_raw.shape[1:], dc.shape[1:], rest.shape[1:]]
             g_xyz, g_s, g_q, g_o, g_dc, g_rest = [torch.empty((n,) + tuple(sz), dtype=torch.float32, device=dev)
                                                   for sz in shapes]
+        elif dense_fill is not None:
+            g_xyz, g_s, g_q, g_o, g_dc, g_rest = grads_dense
+            torch.cuda.current_stream(dev).wait_event(dense_fill)
         else:
-            alloc = torch.zeros_like if vlist is not None else torch.empty_like
-            g_xyz, g_s, g_q, g_dc, g_rest = alloc(xyz), alloc(s_raw), alloc(q_raw), alloc(dc), alloc(rest)
-            g_o = alloc(o_raw)
+            g_xyz, g_s, g_q, g_dc, g_rest = (torch.empty_like(t) for t in (xyz, s_raw, q_raw, dc, rest))
+            g_o = torch.empty_like(o_raw)
         ops.preprocess_backward_raw(radii, means2D, xyz, s_raw, q_raw, o_raw.reshape(-1), sh, ctx.raster,
                                     rec[:, 0:2], rec[:, 8:12], rec[:, 12:15],
                                     (g_xyz, g_s, g_q, g_o, (g_dc, 3), (g_rest, max(M, 1) * 3)), rot_norm=rot_norm,
@@ -101,6 +110,29 @@ class _ViewLoss(torch.autograd.Function):
             grads = [torch.sparse_coo_tensor(idx, g[:L], p.shape, check_invariants=False)
                      for g, p in zip(grads, (xyz, s_raw, q_raw, o_raw, dc, rest))]
         return (*grads, None, None, None, None, None, None)
+
+
+_SIDE = {}
+
+
+def _zero_fill_async(tensors):
+    """Zero ``tensors`` on a side stream (after the current stream's pending
+    work, which may still use their recycled memory); returns the event that
+    marks the end of the fill."""
+    dev = tensors[0].device
+    main = torch.cuda.current_stream(dev)
+    side = _SIDE.get(dev.index)
+    if side is None:
+        side = _SIDE[dev.index] = torch.cuda.Stream(device=dev)
+    side.wait_stream(main)
+    with torch.cuda.stream(side):
+        for t in tensors:
+            t.zero_()
+        done = torch.cuda.Event()
+        done.record(side)
+    for t in tensors:
+        t.record_stream(side)  # the allocator keeps the memory until the fill is done
+    return done
 
 
 def view_loss(model, raster, gt_band, compute_locally=None, band=None, lambda_dssim=LAMBDA_DSSIM,

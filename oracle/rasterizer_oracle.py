@@ -75,13 +75,27 @@ def _rotmat(q):
     return torch.stack([c0, c1, c2], 2)  # [N, row, col]; column c = glm column c
 
 
+def _mm3(A, B):
+    """Batched 3x3 product [N,3,3] @ [N,3,3] (either may be a single [3,3])
+    summed left to right in float32 elementwise operations.  A BLAS call would
+    round differently on different host CPUs (vector width, FMA), which made
+    the oracle's radii -- and so whole splats -- depend on the machine."""
+    rows = []
+    for r in range(3):
+        cols = []
+        for c in range(3):
+            cols.append(A[..., r, 0] * B[..., 0, c] + A[..., r, 1] * B[..., 1, c] + A[..., r, 2] * B[..., 2, c])
+        rows.append(torch.stack(cols, -1))
+    return torch.stack(rows, -2)
+
+
 def cov3d(scales, q, mod=1.0):
     """Sigma = (S R)^T (S R) in glm semantics -> math Sigma = M_m^T M_m with
     M_m = S_m R_m ... returned as the 6-vector (s00,s01,s02,s11,s12,s22)."""
     R = _rotmat(q)
     S = torch.diag_embed(mod * scales)
-    Mm = S @ R  # glm M = S*R  <->  math S_m @ R_m
-    Sig = Mm.transpose(1, 2) @ Mm
+    Mm = _mm3(S, R)  # glm M = S*R  <->  math S_m @ R_m
+    Sig = _mm3(Mm.transpose(1, 2), Mm)
     return torch.stack([Sig[:, 0, 0], Sig[:, 0, 1], Sig[:, 0, 2], Sig[:, 1, 1], Sig[:, 1, 2], Sig[:, 2, 2]], 1)
 
 
@@ -107,11 +121,11 @@ def _cov2d(mean, V, fx, fy, tanx, tany, c6, clamp_detach=False):
                       torch.stack([-(fx * tx) / (tz * tz), -(fy * ty) / (tz * tz), z0], 1)], 1)
     Wm = torch.stack([torch.stack([V[0], V[1], V[2]]), torch.stack([V[4], V[5], V[6]]),
                       torch.stack([V[8], V[9], V[10]])], 0)
-    Tm = Wm.unsqueeze(0) @ Jm
+    Tm = _mm3(Wm.unsqueeze(0), Jm)
     Vrk = torch.stack([torch.stack([c6[:, 0], c6[:, 1], c6[:, 2]], 1),
                        torch.stack([c6[:, 1], c6[:, 3], c6[:, 4]], 1),
                        torch.stack([c6[:, 2], c6[:, 4], c6[:, 5]], 1)], 1)
-    cov = Tm.transpose(1, 2) @ Vrk @ Tm
+    cov = _mm3(_mm3(Tm.transpose(1, 2), Vrk), Tm)
     return cov[:, 0, 0] + 0.3, cov[:, 1, 0], cov[:, 1, 1] + 0.3
 
 
@@ -363,7 +377,7 @@ def render_forward(means2D, conic_opacity, rgb, bg, point_list, ranges, H, W, co
         dx, dy, power, G, alpha, ok, co = _pair_terms(ids, means2D, conic_opacity, xs, ys)
         contrib, Tb, Tf, last = _transmittance(alpha, ok)
         w = torch.where(contrib, alpha * Tb, torch.zeros_like(alpha))
-        c = w @ rgb[ids]  # [npx,3]
+        c = (w.double() @ rgb[ids].double()).float()  # [npx,3]; float64 sum: the same on every host CPU
         color[:, ys, xs] = (c + Tf[:, None] * bg.view(1, 3)).t()
         final_T[pix] = Tf
         n_contrib[pix] = last
