@@ -253,9 +253,13 @@ def run_ours(args, ws, rank, local):
     def batch_ids(it):
         return [((it * bsz * ws) + k) % n_cams for k in range(bsz * ws)]
 
-    def one_step(it, e2e):
+    def one_step(it, e2e, trace=None):
+        if trace is not None:
+            trace.append(("start", time.perf_counter()))
         for p in model:
             p.grad = None
+        if trace is not None:
+            trace.append(("grads freed", time.perf_counter()))
         if ws == 1:
             total = None
             for ci in batch_ids(it):
@@ -267,6 +271,8 @@ def run_ours(args, ws, rank, local):
                     gt = gts_dev[ci]
                 loss, *_ = ST.view_loss(model, rasters[ci], gt, sparse_grad=args.sparse_grad)
                 total = loss if total is None else total + loss
+                if trace is not None:
+                    trace.append(("forward", time.perf_counter()))
         else:
             ids = batch_ids(it)
             bcams = [cams[c] for c in ids]
@@ -289,6 +295,8 @@ def run_ours(args, ws, rank, local):
             h2d[0] = max(h2d[0], nbytes)
             total = DS.batch_loss(model, [rasters[c] for c in ids], gts, strategies)
         total.backward()
+        if trace is not None:
+            trace.append(("backward", time.perf_counter()))
         if e2e:
             return total.detach().to("cpu", non_blocking=False)
         return None
@@ -315,10 +323,10 @@ def run_ours(args, ws, rank, local):
     clocks.mark()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
-    marks, host_t = [], [time.perf_counter()]
+    marks, host_t, trace = [], [time.perf_counter()], []
     t0.record()
     for it in range(args.steps):
-        one_step(args.warmup + it, False)
+        one_step(args.warmup + it, False, trace if it == 0 else None)
         ev = torch.cuda.Event(enable_timing=True)
         ev.record()  # no synchronisation: per-step split of the same timed region
         marks.append(ev)
@@ -334,7 +342,8 @@ def run_ours(args, ws, rank, local):
             split.append(round(prev.elapsed_time(ev), 3))
             prev = ev
         log("timed-region per-step ms:", split,
-            "host ms:", [round((b - a) * 1e3, 3) for a, b in zip(host_t, host_t[1:])])
+            "host ms:", [round((b - a) * 1e3, 3) for a, b in zip(host_t, host_t[1:])],
+            "first step host phases ms:", [(n, round((t - trace[0][1]) * 1e3, 3)) for n, t in trace])
 
     # timed: end to end (GT uploaded from pinned host memory, loss read back)
     barrier(ws)

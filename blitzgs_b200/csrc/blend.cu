@@ -27,11 +27,16 @@
 //   * the per-tile statistics (n_render, n_consider, n_contrib) are reduced
 //     in the epilogue instead of three extra kernels.
 //
+// Both kernels stage each Gaussian as three float4 in shared memory: the two
+// that every (pixel, Gaussian) pair reads (position, conic, opacity, skip
+// threshold, list position) and the colour, read only by contributing pairs.
+//
 // Backward follows the reference back-to-front replay (backward.cu:324-530)
 // but replaces the 11 global atomics per (pixel, Gaussian) pair with a
 // warp-level transpose reduction (16 shuffles for 11 values) and one
-// 11-lane RED instruction per (warp, Gaussian), and starts the replay at the
-// tile's largest n_contrib instead of the end of the list.
+// 11-lane RED instruction per (warp, Gaussian) -- or, when at most
+// kDirectLanes pixels of the warp contribute, their own REDs -- and starts
+// the replay at the tile's largest n_contrib instead of the end of the list.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -40,6 +45,9 @@ namespace blitz {
 namespace {
 
 constexpr int kBatch = kTilePix;  // 256 Gaussians per staged batch
+// Backward: a (warp, Gaussian) pair with at most this many contributing
+// pixels adds their gradients with per-lane REDs instead of the reduction.
+constexpr int kDirectLanes = 8;
 
 // exp-skip threshold: for power < thr, o*expf(power) < (1/255) * e^-1e-3.
 __device__ __forceinline__ float skip_threshold(float o) {
@@ -149,13 +157,15 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
     return;
   }
 
-  __shared__ float2 s_xy[kBatch];
-  __shared__ float4 s_co[kBatch];
-  __shared__ float4 s_rgb[kBatch];  // rgb + skip threshold in .w
+  // staged Gaussian: A = (x, y, c00, c01), B = (c11, opacity, skip threshold,
+  // list position bits), C = (r, g, b, -); A and B serve every pair, C only
+  // contributing pairs
+  __shared__ float4 s_a[kBatch];
+  __shared__ float4 s_b[kBatch];
+  __shared__ float4 s_c[kBatch];
   __shared__ int s_id[kBatch];
   __shared__ int s_obs[kBatch];
   __shared__ int s_red[32];
-  __shared__ int s_list[kBatch];
   __shared__ int s_wcnt[kTilePix / 32];
   const float tx0 = (float)(tx * kTileX), ty0 = (float)(ty * kTileY);
 
@@ -166,7 +176,7 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
 
   bool done = !inside;
   float T = 1.0f;
-  uint32_t contributor = 0, last_contributor = 0, n2l = 0;
+  uint32_t last_contributor = 0, n2l = 0;
   float C0 = 0.f, C1 = 0.f, C2 = 0.f;
 
   int toDo = n;
@@ -190,22 +200,21 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
     const int slot = compact_slot(keep, s_wcnt, kept);
     if (slot >= 0) {
       s_id[slot] = id;
-      s_xy[slot] = xy;
-      s_co[slot] = co;
-      s_rgb[slot] = cth;
-      s_list[slot] = r * kBatch + threadIdx.x + 1;  // 1-based list position, as the reference counts it
+      s_a[slot] = make_float4(xy.x, xy.y, co.x, co.y);
+      // 1-based list position, as the reference counts it
+      s_b[slot] = make_float4(co.z, co.w, cth.w, __int_as_float(r * kBatch + threadIdx.x + 1));
+      s_c[slot] = cth;
       s_obs[slot] = 0;
     }
     __syncthreads();
 
     for (int j = 0; !done && j < kept; ++j) {
-      contributor = (uint32_t)s_list[j];
-      const float2 xy = s_xy[j];
-      const float2 d = {xy.x - pixf.x, xy.y - pixf.y};
-      const float4 con_o = s_co[j];
+      const float4 ga = s_a[j];
+      const float4 gb = s_b[j];
+      const float2 d = {ga.x - pixf.x, ga.y - pixf.y};
+      const float4 con_o = make_float4(ga.z, ga.w, gb.x, gb.y);
       const float power = pair_power(con_o, d);
-      const float4 cth = s_rgb[j];
-      if (power < cth.w) continue;  // alpha provably < 1/255
+      if (power < gb.z) continue;  // alpha provably < 1/255
       if (power > 0.0f) continue;
       const float alpha = min(0.99f, con_o.w * expf(power));
       if (alpha < 1.0f / 255.0f) continue;
@@ -215,12 +224,13 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
         continue;
       }
       ++n2l;
+      const float4 cth = s_c[j];
       C0 += cth.x * alpha * T;
       C1 += cth.y * alpha * T;
       C2 += cth.z * alpha * T;
       if (T > 0.5) atomicAdd(&s_obs[j], 1);
       T = test_T;
-      last_contributor = contributor;
+      last_contributor = (uint32_t)__float_as_int(gb.w);
     }
     __syncthreads();
     if (threadIdx.x < kept && s_obs[threadIdx.x] > 0) atomicAdd(&p.out_observe[s_id[threadIdx.x]], s_obs[threadIdx.x]);
@@ -301,12 +311,13 @@ __global__ void __launch_bounds__(kTilePix, 4) blend_bwd_kernel(BlendBwdParams p
   const int64_t pix = (int64_t)p.W * py + px;
   const float2 pixf = make_float2((float)px, (float)py);
 
-  __shared__ float2 s_xy[kBatch];
-  __shared__ float4 s_co[kBatch];
-  __shared__ float4 s_rgb[kBatch];
+  // staged Gaussian: A = (x, y, c00, c01), B = (c11, opacity, skip threshold,
+  // list position bits), C = (r, g, b, -)
+  __shared__ float4 s_a[kBatch];
+  __shared__ float4 s_b[kBatch];
+  __shared__ float4 s_c[kBatch];
   __shared__ int s_id[kBatch];
   __shared__ int s_max;
-  __shared__ int s_list[kBatch];
   __shared__ int s_wcnt[kTilePix / 32];
   const float tx0 = (float)(tx * kTileX), ty0 = (float)(ty * kTileY);
 
@@ -359,23 +370,23 @@ __global__ void __launch_bounds__(kTilePix, 4) blend_bwd_kernel(BlendBwdParams p
     const int slot = compact_slot(keep, s_wcnt, kept);
     if (slot >= 0) {
       s_id[slot] = p.record_rows ? (int)__ldg(p.record_rows + id) : id;  // gradient record row
-      s_xy[slot] = xy;
-      s_co[slot] = co;
-      s_rgb[slot] = cth;
-      s_list[slot] = k;  // list position
+      s_a[slot] = make_float4(xy.x, xy.y, co.x, co.y);
+      s_b[slot] = make_float4(co.z, co.w, cth.w, __int_as_float(k));  // list position
+      s_c[slot] = cth;
     }
     __syncthreads();
     for (int j = 0; j < kept; ++j) {
-      const int pos = s_list[j];
+      const float4 gb = s_b[j];
+      const int pos = __float_as_int(gb.w);
       float g[16];
       bool contrib = false;
       if (pos < last_contributor) {
-        const float2 xy = s_xy[j];
-        const float2 d = {xy.x - pixf.x, xy.y - pixf.y};
-        const float4 con_o = s_co[j];
+        const float4 ga = s_a[j];
+        const float2 d = {ga.x - pixf.x, ga.y - pixf.y};
+        const float4 con_o = make_float4(ga.z, ga.w, gb.x, gb.y);
         const float power = pair_power(con_o, d);
-        const float4 cth = s_rgb[j];
-        if (power >= cth.w && !(power > 0.0f)) {
+        if (power >= gb.z && !(power > 0.0f)) {
+          const float4 cth = s_c[j];
           const float G = expf(power);
           const float alpha = min(0.99f, con_o.w * G);
           if (!(alpha < 1.0f / 255.0f)) {
@@ -410,7 +421,27 @@ __global__ void __launch_bounds__(kTilePix, 4) blend_bwd_kernel(BlendBwdParams p
           }
         }
       }
-      if (!__any_sync(0xffffffffu, contrib)) continue;
+      const unsigned cm = __ballot_sync(0xffffffffu, contrib);
+      if (!cm) continue;
+      if (__popc(cm) <= kDirectLanes) {
+        // few contributing pixels: their own REDs cost fewer instructions
+        // than the warp-wide transpose reduction
+        if (contrib) {
+          float* dst = p.grad_accum + 16 * (int64_t)s_id[j];
+          atomicAdd(dst + 0, g[0]);
+          atomicAdd(dst + 1, g[1]);
+          atomicAdd(dst + 4, g[2]);
+          atomicAdd(dst + 5, g[3]);
+          atomicAdd(dst + 8, g[4]);
+          atomicAdd(dst + 9, g[5]);
+          atomicAdd(dst + 10, g[6]);
+          atomicAdd(dst + 11, g[7]);
+          atomicAdd(dst + 12, g[11]);
+          atomicAdd(dst + 13, g[12]);
+          atomicAdd(dst + 14, g[13]);
+        }
+        continue;
+      }
       if (!contrib) {
 #pragma unroll
         for (int m = 0; m < 14; ++m) g[m] = 0.f;

@@ -365,3 +365,56 @@ def test_ops_refuse_cpu_tensors():
     xyz, s, q, shs, o = activated(sc)
     with pytest.raises(RuntimeError):
         ops.preprocess_forward(xyz, s, q, o.reshape(-1), ops.sh_layout(shs=shs), rs)
+
+
+def test_exchange_records_routing_and_pack(cuda_device):
+    """The fused exchange outputs of the raw preprocess (records, destination
+    masks, per-rank counts) equal what the operator API gives: the same
+    per-Gaussian outputs and get_local2j_ids_bool on the reference's tile
+    intervals, here for 4 ranks.  blitz_exchange_pack then puts every routed
+    row exactly once into each destination's segment."""
+    sc = S.mid(seed=4, P=400_000, n_cams=1)
+    cam = sc.cameras[0].to(cuda_device)
+    rs = _raster(cam, cuda_device)
+    H, W = cam.image_height, cam.image_width
+    gx, gy = ops.grid_dims(H, W)
+    division = [0, 11, 23, 40, gy]
+    ranks = len(division) - 1
+    lo = torch.tensor([d * gx for d in division[:-1]], dtype=torch.int32, device=cuda_device)
+    hi = torch.tensor([d * gx for d in division[1:]], dtype=torch.int32, device=cuda_device)
+    xyz, s, q, o, dc, rest = [t.to(cuda_device) for t in scene_params(sc)]
+    sh = ops.sh_layout(dc=dc, rest=rest)
+    P = xyz.shape[0]
+    rec = torch.empty((P, 12), dtype=torch.float32, device=cuda_device)
+    mask = torch.empty((P,), dtype=torch.int32, device=cuda_device)
+    cnt = torch.zeros((ranks,), dtype=torch.int32, device=cuda_device)
+    out = ops.preprocess_forward_raw(xyz, s, q, o.reshape(-1), sh, rs, None, want_list=True,
+                                     exchange=(lo, hi, rec, mask, cnt))
+    dense = ops.preprocess_forward_raw(xyz, s, q, o.reshape(-1), sh, rs, None, want_list=False, two_pass=False)
+    m2, d, r, co, rgb = dense[:5]
+    L = int(out[7].item())
+    ids = out[6][:L].long()
+    assert L > 1000
+    route = ops.local2j_ids_bool(H, W, 0, ranks, m2, r, torch.tensor(division, dtype=torch.int32,
+                                                                       device=cuda_device) * gx)
+    assert not route[r <= 0].any()  # only listed Gaussians are ever sent
+    smin = torch.exp(s).min(dim=1).values
+    want = torch.cat([co[ids], m2[ids], rgb[ids], d[ids, None], r[ids].view(torch.float32)[:, None],
+                      smin[ids, None]], 1)
+    assert torch.equal(rec[:L].view(torch.int32), want.view(torch.int32))
+    bits = torch.stack([(mask[:L] >> k) & 1 for k in range(ranks)], 1).bool()
+    assert torch.equal(bits, route[ids])
+    assert torch.equal(cnt.long(), bits.sum(0))
+    # pack: segment k of the send buffer holds exactly the rows routed to rank k
+    counts = cnt.tolist()
+    offs = [sum(counts[:k]) for k in range(ranks)]
+    n_send = sum(counts)
+    send = torch.empty((n_send, 12), dtype=torch.float32, device=cuda_device)
+    send_row = torch.empty((n_send,), dtype=torch.int32, device=cuda_device)
+    cursor = torch.zeros((ranks,), dtype=torch.int32, device=cuda_device)
+    ops.exchange_pack(L, rec, mask, offs, cursor, send, send_row, 7)
+    assert cursor.tolist() == counts
+    for k in range(ranks):
+        rows = send_row[offs[k]:offs[k] + counts[k]].long() - 7
+        assert torch.equal(torch.sort(rows).values, torch.nonzero(bits[:, k]).flatten())
+        assert torch.equal(send[offs[k]:offs[k] + counts[k]], rec[rows])
