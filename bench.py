@@ -324,6 +324,7 @@ def run_ours(args, ws, rank, local):
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     marks, host_t, trace = [], [time.perf_counter()], []
+    mstat0 = torch.cuda.memory_stats(dev)
     t0.record()
     for it in range(args.steps):
         one_step(args.warmup + it, False, trace if it == 0 else None)
@@ -343,7 +344,9 @@ def run_ours(args, ws, rank, local):
             prev = ev
         log("timed-region per-step ms:", split,
             "host ms:", [round((b - a) * 1e3, 3) for a, b in zip(host_t, host_t[1:])],
-            "first step host phases ms:", [(n, round((t - trace[0][1]) * 1e3, 3)) for n, t in trace])
+            "first step host phases ms:", [(n, round((t - trace[0][1]) * 1e3, 3)) for n, t in trace],
+            "allocator calls in region:", {k: torch.cuda.memory_stats(dev).get(k, 0) - mstat0.get(k, 0)
+                                           for k in ("num_device_alloc", "num_device_free", "num_alloc_retries")})
 
     # timed: end to end (GT uploaded from pinned host memory, loss read back)
     barrier(ws)

@@ -29,8 +29,8 @@ SIGNATURES = {
     "blitz_exchange_pack": (_i32, [_i64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _vp]),
     "blitz_preprocess_backward_raw": (_i32, [
         _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _f32, _vp, _vp, _vp, _f32,
-        _f32, _i32, _i32, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64,
-        _vp, _i64, _i32, _i32, _vp]),
+        _f32, _i32, _i32, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+        _i64, _vp, _i64, _i32, _i32, _vp]),
     "blitz_render_count": (_i32, [_i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp]),
     "blitz_render_scratch_bytes": (_sz, [_i64, _i64, _i64, _i32, _i32]),
     "blitz_render_forward": (_i32, [
@@ -88,13 +88,12 @@ def call(name, *args):
 
 
 def ptr(t):
-    """Device pointer of a tensor (None -> NULL)."""
-    if t is None:
-        return None
-    return ctypes.c_void_p(t.data_ptr())
+    """Device pointer of a tensor as an int (None -> NULL); ctypes converts it
+    for the void* parameters."""
+    return None if t is None else t.data_ptr()
 
 
 def stream_ptr(stream=None):
     import torch
     s = stream if stream is not None else torch.cuda.current_stream()
-    return ctypes.c_void_p(s.cuda_stream)
+    return s.cuda_stream

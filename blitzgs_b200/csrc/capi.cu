@@ -219,6 +219,7 @@ int blitz_preprocess_backward_raw(int64_t P, int D, int M, const int32_t* radii,
                                   int image_width, const float* g_means2D, int64_t g_means2D_stride,
                                   const float* g_conic_opacity, int64_t g_conic_stride,
                                   const float* g_colors, int64_t g_colors_stride, const float* reg_scale,
+                                  const float* g_minscale, int64_t g_minscale_stride,
                                   const uint32_t* vis_list, const int32_t* vis_count, float* g_xyz,
                                   float* g_scaling_raw, float* g_rotation_raw, float* g_opacity_raw,
                                   float* g_dc, int64_t g_dc_stride, float* g_rest, int64_t g_rest_stride,
@@ -244,6 +245,8 @@ int blitz_preprocess_backward_raw(int64_t P, int D, int M, const int32_t* radii,
   b.vis_count = vis_count;
   if ((rows & ~(BLITZ_ROWS_UPSTREAM_BY_SLOT | BLITZ_ROWS_OUTPUT_BY_SLOT)) || (rows && !vis_list))
     return fail(BLITZ_EINVAL, "blitz_preprocess_backward_raw: bad rows flags (slot rows need vis_list)");
+  b.g_minscale = g_minscale;
+  b.g_minscale_stride = g_minscale_stride;
   b.upstream_by_slot = rows & BLITZ_ROWS_UPSTREAM_BY_SLOT;
   b.out_by_slot = rows & BLITZ_ROWS_OUTPUT_BY_SLOT;
   b.g_means2D = g_means2D;

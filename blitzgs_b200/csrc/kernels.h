@@ -96,6 +96,10 @@ struct PreprocessBwdParams {
   // instead of row i, and/or the outputs are written at row j (compact rows).
   bool upstream_by_slot;
   bool out_by_slot;
+  // optional: d(loss)/d(smallest activated scale) at g_minscale + row*stride
+  // (row = the upstream row), added to the first smallest axis (raw mode)
+  const float* g_minscale;
+  int64_t g_minscale_stride;
 };
 
 // scratch (may be null): preprocess_scratch_bytes(P) bytes select the

@@ -907,21 +907,23 @@ __device__ __forceinline__ void bwd_compute(const PreprocessBwdParams& p, int64_
   if (f.raw) {
     // min-scale regulariser: d(loss)/d(min-axis scale) for Gaussians the
     // exchange sends (radius > 0 and a non-empty square tile rect)
+    float gmin = 0.f;
     if (p.reg_scale && p.means2D) {
       const float2 m2 = reinterpret_cast<const float2*>(p.means2D)[i];
       int2 lo, hi;
       tile_rect_int(m2, __ldg(p.radii + i), f.grid_x, f.grid_y, lo, hi);
-      if ((hi.y - 1) * f.grid_x + hi.x - 1 >= lo.y * f.grid_x + lo.x) {
-        const float g = *p.reg_scale;
-        // gradient to the first smallest axis (static indexing keeps `out` in registers)
-        if (sx <= sy && sx <= sz)
-          out.scale[0] += g;
-        else if (sy <= sz)
-          out.scale[1] += g;
-        else
-          out.scale[2] += g;
-      }
+      if ((hi.y - 1) * f.grid_x + hi.x - 1 >= lo.y * f.grid_x + lo.x) gmin += *p.reg_scale;
     }
+    // per-row gradient of the smallest scale (the multi-GPU step: summed over
+    // the ranks that received this Gaussian)
+    if (p.g_minscale) gmin += __ldg(p.g_minscale + up * p.g_minscale_stride);
+    // to the first smallest axis (static indexing keeps `out` in registers)
+    if (sx <= sy && sx <= sz)
+      out.scale[0] += gmin;
+    else if (sy <= sz)
+      out.scale[1] += gmin;
+    else
+      out.scale[2] += gmin;
     // chain through the activations: exp, normalize (with its 1e-12 clamp), sigmoid
     out.scale[0] *= sx;
     out.scale[1] *= sy;

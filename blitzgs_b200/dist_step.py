@@ -61,13 +61,23 @@ class _DistributedBatch(torch.autograd.Function):
                 table[k, 1, g] = st.division_pos[r_local + 1] * gx
         table_dev = table[:n_cams].to(dev, non_blocking=True)
         cnt = torch.zeros((n_cams, 1 + ws), dtype=torch.int32, device=dev)  # list length | rows per rank
+        # one allocation per buffer kind for the whole batch
+        Pc = max(P, 1)
+        b_m2 = torch.empty((n_cams, Pc, 2), dtype=torch.float32, device=dev)
+        b_f1 = torch.empty((n_cams, 2, Pc), dtype=torch.float32, device=dev)  # depths | radii bits
+        b_co = torch.empty((n_cams, Pc, 4), dtype=torch.float32, device=dev)
+        b_rgb = torch.empty((n_cams, Pc, 3), dtype=torch.float32, device=dev)
+        b_list = torch.empty((n_cams, 2, Pc), dtype=torch.int32, device=dev)  # vis list | dest mask
+        b_rec = torch.empty((n_cams, Pc, _FWD_C), dtype=torch.float32, device=dev)
         pre = []
         for k, rs in enumerate(rasters):
-            xrec = torch.empty((max(P, 1), _FWD_C), dtype=torch.float32, device=dev)
-            xmask = torch.empty((max(P, 1),), dtype=torch.int32, device=dev)
+            bufs = (b_m2[k, :P], b_f1[k, 0, :P], b_f1[k, 1, :P].view(torch.int32), b_co[k, :P], b_rgb[k, :P],
+                    b_list[k, 0])
+            xrec, xmask = b_rec[k], b_list[k, 1]
             m2, d, r, co, rgb, _, vlist, vcount, _, _, _ = ops.preprocess_forward_raw(
                 xyz, s_raw, q_raw, o_raw.reshape(-1), sh, rs, None, want_reg=False, want_list=True,
-                vis_count=cnt[k, 0:1], exchange=(table_dev[k, 0], table_dev[k, 1], xrec, xmask, cnt[k, 1:]))
+                vis_count=cnt[k, 0:1], exchange=(table_dev[k, 0], table_dev[k, 1], xrec, xmask, cnt[k, 1:]),
+                out=bufs)
             pre.append((m2, r, vlist, vcount, xrec, xmask))
         # 2. one all-gather of every rank's counts: the only host synchronisation
         #    before the render (it sizes the all-to-all on every rank)
@@ -187,12 +197,7 @@ class _DistributedBatch(torch.autograd.Function):
                                         a[:, 4:6], a[:, 0:4], a[:, 6:9],
                                         (g_xyz, g_s, g_q, g_o, (g_dc, 3), (g_rest, max(M, 1) * 3)),
                                         vis_list=vlist, vis_count=vcount, accumulate=True,
-                                        rows=ops.ROWS_UPSTREAM_BY_SLOT)
-            # min-scale regulariser: to the smallest axis of exp(_scaling), chained through exp
-            ids = vlist[:ctx.counts[k]].to(torch.int64)
-            s_act = torch.exp(s_raw.detach().index_select(0, ids))
-            mn, am = s_act.min(dim=1)
-            g_s.index_put_((ids, am), a[:, 11] * mn, accumulate=True)
+                                        rows=ops.ROWS_UPSTREAM_BY_SLOT, g_minscale=a[:, 11])
         return g_xyz, g_s, g_q, g_o, g_dc, g_rest, None
 
 

@@ -197,7 +197,7 @@ def preprocess_backward(radii, means3D, scales, rotations, sh, raster, g_means2D
 
 def preprocess_forward_raw(xyz, scaling_raw, rotation_raw, opacity_raw, sh, raster, rot_norm=None, *,
                            want_reg=True, want_list=True, want_counts=False, compute_locally=None,
-                           two_pass=True, want_slots=False, vis_count=None, exchange=None):
+                           two_pass=True, want_slots=False, vis_count=None, exchange=None, out=None):
     """Preprocess from the raw model parameters (activations fused into the
     kernel).  Returns (means2D, depths, radii, conic_opacity, rgb, reg_sums
     double[2] or None, vis_list or None, vis_count or None, counts or None,
@@ -213,20 +213,26 @@ def preprocess_forward_raw(xyz, scaling_raw, rotation_raw, opacity_raw, sh, rast
     Gaussian), which indexes the compact gradient record of the backward.
     ``vis_count``: caller's zeroed int32 [1] counter for the list length.
     ``exchange`` = (tile_lo, tile_hi, records, dest_mask, dest_counts): the
-    multi-GPU exchange outputs (see blitz_exchange_out in the C header)."""
+    multi-GPU exchange outputs (see blitz_exchange_out in the C header).
+    ``out`` = (means2D, depths, radii, conic_opacity, rgb, vis_list): caller
+    buffers to write instead of fresh allocations."""
     _require_cuda(xyz, scaling_raw, rotation_raw, opacity_raw)
     xyz, scaling_raw, rotation_raw, opacity_raw = map(_f32c, (xyz, scaling_raw, rotation_raw, opacity_raw))
     dc, dcs, rest, rs, M, _keep = sh
     P = xyz.shape[0]
     dev = xyz.device
     H, W = int(raster.image_height), int(raster.image_width)
-    means2D = torch.empty((P, 2), dtype=torch.float32, device=dev)
-    depths = torch.empty((P,), dtype=torch.float32, device=dev)
-    radii = torch.empty((P,), dtype=torch.int32, device=dev)
-    conic = torch.empty((P, 4), dtype=torch.float32, device=dev)
-    rgb = torch.empty((P, 3), dtype=torch.float32, device=dev)
+    if out is not None:
+        means2D, depths, radii, conic, rgb, vlist = out
+        vlist = vlist if want_list else None
+    else:
+        means2D = torch.empty((P, 2), dtype=torch.float32, device=dev)
+        depths = torch.empty((P,), dtype=torch.float32, device=dev)
+        radii = torch.empty((P,), dtype=torch.int32, device=dev)
+        conic = torch.empty((P, 4), dtype=torch.float32, device=dev)
+        rgb = torch.empty((P, 3), dtype=torch.float32, device=dev)
+        vlist = torch.empty((max(P, 1),), dtype=torch.int32, device=dev) if want_list else None
     reg = torch.zeros((2,), dtype=torch.float64, device=dev) if want_reg else None
-    vlist = torch.empty((max(P, 1),), dtype=torch.int32, device=dev) if want_list else None
     vcount = (vis_count if vis_count is not None else torch.zeros((1,), dtype=torch.int32, device=dev)) \
         if want_list else None
     xo = None
@@ -275,7 +281,7 @@ ROWS_OUTPUT_BY_SLOT = 2    # BLITZ_ROWS_OUTPUT_BY_SLOT
 
 def preprocess_backward_raw(radii, means2D, xyz, scaling_raw, rotation_raw, opacity_raw, sh, raster,
                             g_means2D, g_conic, g_colors, out, rot_norm=None, reg_scale=None, vis_list=None,
-                            vis_count=None, accumulate=False, rows=0):
+                            vis_count=None, accumulate=False, rows=0, g_minscale=None):
     """Gradients w.r.t. the raw parameters into ``out`` = (g_xyz, g_scaling,
     g_rotation, g_opacity, (g_dc, stride), (g_rest, stride)).  With a visible
     list the outputs must be zero-filled (or accumulating), unless ``rows``
@@ -292,7 +298,8 @@ def preprocess_backward_raw(radii, means2D, xyz, scaling_raw, rotation_raw, opac
                   ptr(rest), rs, float(raster.scale_modifier), ptr(raster.viewmatrix), ptr(raster.projmatrix),
                   ptr(raster.campos), float(raster.tanfovx), float(raster.tanfovy), int(raster.image_height),
                   int(raster.image_width), ptr(g_means2D), g_means2D.stride(0), ptr(g_conic), g_conic.stride(0),
-                  ptr(g_colors), g_colors.stride(0), ptr(reg_scale), ptr(vis_list), ptr(vis_count), ptr(gx),
+                  ptr(g_colors), g_colors.stride(0), ptr(reg_scale), ptr(g_minscale),
+                  g_minscale.stride(0) if g_minscale is not None else 0, ptr(vis_list), ptr(vis_count), ptr(gx),
                   ptr(gs), ptr(gq), ptr(go), ptr(gdc), gdcs, ptr(grest), grs, int(bool(accumulate)), int(rows),
                   _lib.stream_ptr())
         TIMER.end(tok, P=P, lazy=lambda: {"n_list": vis_count} if vis_list is not None else {})

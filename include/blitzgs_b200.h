@@ -181,6 +181,9 @@ int blitz_preprocess_forward_raw(int64_t P, int D, int M, const float* xyz, cons
  * of blitz_render_backward with record_rows), BLITZ_ROWS_OUTPUT_BY_SLOT writes
  * its gradients at row j of [vis_count, ...] outputs (every row written: no
  * zero-fill; the gradient as sparse rows, indices = vis_list).
+ * g_minscale (may be NULL): per-row d(loss)/d(smallest activated scale) at
+ * g_minscale + row*g_minscale_stride (row as for the upstream gradients),
+ * added to the first smallest axis -- the multi-GPU regulariser gradient.
  */
 #define BLITZ_ROWS_UPSTREAM_BY_SLOT 1
 #define BLITZ_ROWS_OUTPUT_BY_SLOT 2
@@ -193,6 +196,7 @@ int blitz_preprocess_backward_raw(int64_t P, int D, int M, const int32_t* radii,
                                   int image_width, const float* g_means2D, int64_t g_means2D_stride,
                                   const float* g_conic_opacity, int64_t g_conic_stride,
                                   const float* g_colors, int64_t g_colors_stride, const float* reg_scale,
+                                  const float* g_minscale, int64_t g_minscale_stride,
                                   const uint32_t* vis_list, const int32_t* vis_count, float* g_xyz,
                                   float* g_scaling_raw, float* g_rotation_raw, float* g_opacity_raw,
                                   float* g_dc, int64_t g_dc_stride, float* g_rest, int64_t g_rest_stride,
