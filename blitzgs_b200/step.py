@@ -118,7 +118,10 @@ _SIDE = {}
 def _zero_fill_async(tensors):
     """Zero ``tensors`` on a side stream (after the current stream's pending
     work, which may still use their recycled memory); returns the event that
-    marks the end of the fill."""
+    marks the end of the fill.  The caller makes its stream wait on that
+    event before it touches the tensors, so every later use and free is
+    ordered after the fill on the tensors' own stream (no record_stream:
+    that would hold the memory back from the allocator's reuse)."""
     dev = tensors[0].device
     main = torch.cuda.current_stream(dev)
     side = _SIDE.get(dev.index)
@@ -130,8 +133,6 @@ def _zero_fill_async(tensors):
             t.zero_()
         done = torch.cuda.Event()
         done.record(side)
-    for t in tensors:
-        t.record_stream(side)  # the allocator keeps the memory until the fill is done
     return done
 
 
