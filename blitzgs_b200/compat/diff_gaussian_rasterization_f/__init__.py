@@ -8,6 +8,7 @@ from blitzgs_b200.rasterizer import (  # noqa: F401
     GaussianRasterizer,
     _PreprocessGaussians,
     _RenderGaussians,
+    SparseGaussianAdam,
     preprocess_gaussians,
     render_gaussians,
 )

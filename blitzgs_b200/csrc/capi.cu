@@ -478,6 +478,75 @@ int blitz_get_local2j_ids_bool(int image_height, int image_width, int mp_rank, i
   return check(launch_route_bool(r, S(stream)), "blitz_get_local2j_ids_bool");
 }
 
+int blitz_get_local2j_ids_bool_adjust_mode6(int image_height, int image_width, int mp_rank, int mp_world_size,
+                                            int64_t P, const float* means2D, const int32_t* radii,
+                                            const int32_t* rectangles, int avoid_pixel_all2all, uint8_t* out,
+                                            void* stream) {
+  (void)mp_rank;
+  if (P < 0 || mp_world_size <= 0 || image_height <= 0 || image_width <= 0)
+    return fail(BLITZ_EINVAL, "blitz_get_local2j_ids_bool_adjust_mode6: bad sizes");
+  if (P == 0) return 0;
+  if (!means2D || !radii || !rectangles || !out)
+    return fail(BLITZ_EINVAL, "blitz_get_local2j_ids_bool_adjust_mode6: null pointer");
+  RouteParams r{};
+  r.P = P;
+  r.W = image_width;
+  r.H = image_height;
+  r.grid_x = (image_width + kTileX - 1) / kTileX;
+  r.grid_y = (image_height + kTileY - 1) / kTileY;
+  r.world_size = mp_world_size;
+  r.means2D = means2D;
+  r.radii = radii;
+  r.avoid_pixel_all2all = avoid_pixel_all2all != 0;
+  r.out_bool = reinterpret_cast<bool*>(out);
+  return check(launch_route_bool_rect(r, rectangles, S(stream)), "blitz_get_local2j_ids_bool_adjust_mode6");
+}
+
+int blitz_adam_update(float* param, const float* param_grad, float* exp_avg, float* exp_avg_sq,
+                      const uint8_t* visible, float lr, float b1, float b2, float eps, int64_t N, int64_t M,
+                      void* stream) {
+  if (N < 0 || M <= 0) return fail(BLITZ_EINVAL, "blitz_adam_update: bad sizes");
+  if (N == 0) return 0;
+  if (!param || !param_grad || !exp_avg || !exp_avg_sq || !visible)
+    return fail(BLITZ_EINVAL, "blitz_adam_update: null pointer");
+  AdamParams a{};
+  a.param = param;
+  a.grad = param_grad;
+  a.exp_avg = exp_avg;
+  a.exp_avg_sq = exp_avg_sq;
+  a.visible = reinterpret_cast<const bool*>(visible);
+  a.lr = lr;
+  a.b1 = b1;
+  a.b2 = b2;
+  a.eps = eps;
+  a.N = N;
+  a.M = M;
+  return check(launch_adam(a, S(stream)), "blitz_adam_update");
+}
+
+int blitz_adam_update_rows(float* param, const float* grad_rows, float* exp_avg, float* exp_avg_sq,
+                           const int64_t* rows, int64_t n_rows, float lr, float b1, float b2, float eps, int64_t N,
+                           int64_t M, void* stream) {
+  if (N < 0 || M <= 0 || n_rows < 0) return fail(BLITZ_EINVAL, "blitz_adam_update_rows: bad sizes");
+  if (n_rows == 0) return 0;
+  if (!param || !grad_rows || !exp_avg || !exp_avg_sq || !rows)
+    return fail(BLITZ_EINVAL, "blitz_adam_update_rows: null pointer");
+  AdamParams a{};
+  a.param = param;
+  a.grad = grad_rows;
+  a.exp_avg = exp_avg;
+  a.exp_avg_sq = exp_avg_sq;
+  a.rows = rows;
+  a.n_rows = n_rows;
+  a.lr = lr;
+  a.b1 = b1;
+  a.b2 = b2;
+  a.eps = eps;
+  a.N = N;
+  a.M = M;
+  return check(launch_adam(a, S(stream)), "blitz_adam_update_rows");
+}
+
 int blitz_exchange_pack(int64_t n_rows, int n_ranks, const float* records, const uint32_t* dest_mask,
                         const int64_t* dest_offset, int32_t* cursor, float* send, int32_t* send_row,
                         int32_t row_base, void* stream) {

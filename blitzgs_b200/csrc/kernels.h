@@ -215,6 +215,25 @@ struct RouteParams {
 };
 int launch_route_bool(const RouteParams& p, cudaStream_t st);
 
+// Routing against per-rank tile rectangles [y_l, y_r, x_l, x_r] (the
+// reference's getTouchedIdsBoolAdjustMode6).
+int launch_route_bool_rect(const RouteParams& p, const int* rectangles, cudaStream_t st);
+
+// Sparse Adam (see adam.cu).  rows == null: dense grad [N,M] and visible [N];
+// else grad is [n_rows, M] for Gaussians rows[j].
+struct AdamParams {
+  float* param;
+  const float* grad;
+  float* exp_avg;
+  float* exp_avg_sq;
+  const bool* visible;
+  const int64_t* rows;
+  int64_t n_rows;
+  float lr, b1, b2, eps;
+  int64_t N, M;
+};
+int launch_adam(const AdamParams& p, cudaStream_t st);
+
 // Pack rows [0, n_rows) of a camera's exchange records into the send buffer:
 // row j goes to every rank r whose bit is set in mask[j], at
 // dest_offset[r] + (its running position among rank r's rows); send_row

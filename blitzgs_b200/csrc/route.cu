@@ -73,7 +73,38 @@ __global__ void __launch_bounds__(256) exchange_pack_kernel(PackParams p) {
   }
 }
 
+// Rectangle form: rank rk renders tile rows [y_l, y_r) and columns
+// [x_l, x_r) (rectangles[4*rk..]), optionally widened by one tile (the low
+// bounds only while positive).  The reference tests the square tile rect
+// without first rejecting an empty one, and so does this kernel: a Gaussian
+// whose clamped rect is empty can still be routed.
+__global__ void __launch_bounds__(256) route_bool_rect_kernel(RouteParams p, const int* __restrict__ rects) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= p.P) return;
+  bool* out = p.out_bool + i * p.world_size;
+  const float2 m = reinterpret_cast<const float2*>(p.means2D)[i];
+  int2 lo, hi;
+  tile_rect_int(m, p.radii[i], p.grid_x, p.grid_y, lo, hi);
+  for (int rk = 0; rk < p.world_size; ++rk) {
+    int yl = rects[4 * rk + 0], yr = rects[4 * rk + 1], xl = rects[4 * rk + 2], xr = rects[4 * rk + 3];
+    if (p.avoid_pixel_all2all) {
+      if (yl > 0) yl -= 1;
+      if (xl > 0) xl -= 1;
+      yr += 1;
+      xr += 1;
+    }
+    out[rk] = !(hi.y <= yl || yr <= lo.y || hi.x <= xl || xr <= lo.x);
+  }
+}
+
 }  // namespace
+
+int launch_route_bool_rect(const RouteParams& p, const int* rectangles, cudaStream_t st) {
+  if (p.P <= 0) return 0;
+  const int threads = 256;
+  route_bool_rect_kernel<<<(unsigned)((p.P + threads - 1) / threads), threads, 0, st>>>(p, rectangles);
+  return (int)cudaGetLastError();
+}
 
 int launch_exchange_pack(const PackParams& p, cudaStream_t st) {
   if (p.n_rows <= 0) return 0;

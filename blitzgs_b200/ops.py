@@ -501,3 +501,46 @@ def local2j_ids_bool(H, W, mp_rank, mp_world_size, means2D, radii, dist_global_s
               ptr(_f32c(means2D)), ptr(radii.contiguous()), ptr(dist_global_strategy.to(torch.int32).contiguous()),
               int(bool(avoid_pixel_all2all)), ptr(out), _lib.stream_ptr())
     return out
+
+
+def local2j_ids_bool_adjust_mode6(H, W, mp_rank, mp_world_size, means2D, radii, rectangles,
+                                  avoid_pixel_all2all=False):
+    """Routing mask bool [P, mp_world_size] against per-rank tile rectangles
+    int32 [mp_world_size, 4] = (row begin, row end, column begin, column end)."""
+    _require_cuda(means2D, radii, rectangles)
+    P = means2D.shape[0]
+    out = torch.empty((P, mp_world_size), dtype=torch.bool, device=means2D.device)
+    _lib.call("blitz_get_local2j_ids_bool_adjust_mode6", int(H), int(W), int(mp_rank), int(mp_world_size), P,
+              ptr(_f32c(means2D)), ptr(radii.contiguous()), ptr(rectangles.to(torch.int32).contiguous()),
+              int(bool(avoid_pixel_all2all)), ptr(out), _lib.stream_ptr())
+    return out
+
+
+def adam_update(param, grad, exp_avg, exp_avg_sq, visible, lr, b1, b2, eps, N, M):
+    """In-place sparse Adam step of param [N*M] for the Gaussians with
+    visible[g] (blitz_adam_update; the reference's _C.adamUpdate)."""
+    for t in (param, grad, exp_avg, exp_avg_sq):
+        if t.dtype != torch.float32 or not t.is_contiguous():
+            raise RuntimeError("adam_update needs contiguous float32 tensors")
+    vis = visible.contiguous()
+    if vis.dtype != torch.bool:
+        vis = vis.to(torch.bool)
+    tok = TIMER.begin("adam")
+    _lib.call("blitz_adam_update", ptr(param), ptr(grad), ptr(exp_avg), ptr(exp_avg_sq), ptr(vis), float(lr),
+              float(b1), float(b2), float(eps), int(N), int(M), _lib.stream_ptr())
+    TIMER.end(tok, N=int(N), M=int(M))
+
+
+def adam_update_rows(param, grad_rows, exp_avg, exp_avg_sq, rows, lr, b1, b2, eps, N, M):
+    """In-place sparse Adam step of the Gaussians rows (int64 [n], distinct)
+    whose gradients are the rows of grad_rows [n, M] (blitz_adam_update_rows)."""
+    for t in (param, exp_avg, exp_avg_sq):
+        if t.dtype != torch.float32 or not t.is_contiguous():
+            raise RuntimeError("adam_update_rows needs contiguous float32 tensors")
+    grad_rows = _f32c(grad_rows)
+    rows = rows.to(torch.int64).contiguous()
+    n = rows.numel()
+    tok = TIMER.begin("adam")
+    _lib.call("blitz_adam_update_rows", ptr(param), ptr(grad_rows), ptr(exp_avg), ptr(exp_avg_sq), ptr(rows), n,
+              float(lr), float(b1), float(b2), float(eps), int(N), int(M), _lib.stream_ptr())
+    TIMER.end(tok, N=int(N), M=int(M), n_rows=n)

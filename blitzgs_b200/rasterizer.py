@@ -226,13 +226,71 @@ def _get_local2j_ids_bool(image_height, image_width, mp_rank, mp_world_size, mea
                                 dist_global_strategy, avoid)
 
 
+def _get_local2j_ids_bool_adjust_mode6(image_height, image_width, mp_rank, mp_world_size, means2D, radii,
+                                       rectangles, args=None):
+    """Reference: GetLocal2jIdsBoolAdjustMode6CUDA (f/rasterize_points.cu:337-368)."""
+    avoid = bool(args.get("avoid_pixel_all2all", False)) if isinstance(args, dict) else False
+    return ops.local2j_ids_bool_adjust_mode6(image_height, image_width, mp_rank, mp_world_size, means2D, radii,
+                                             rectangles, avoid)
+
+
+def _adam_update(param, param_grad, exp_avg, exp_avg_sq, visible, lr, b1, b2, eps, N, M):
+    """Reference: adamUpdate (f/rasterize_points.cu:807-833): in place, no return."""
+    ops.adam_update(param, param_grad, exp_avg, exp_avg_sq, visible, lr, b1, b2, eps, N, M)
+
+
 _C = SimpleNamespace(
     preprocess_gaussians=_preprocess_gaussians,
     preprocess_gaussians_backward=_preprocess_gaussians_backward,
     render_gaussians=_render_gaussians,
     render_gaussians_backward=_render_gaussians_backward,
     get_local2j_ids_bool=_get_local2j_ids_bool,
+    get_local2j_ids_bool_adjust_mode6=_get_local2j_ids_bool_adjust_mode6,
+    adamUpdate=_adam_update,
 )
+
+
+class SparseGaussianAdam(torch.optim.Adam):
+    """The reference's SparseGaussianAdam (f/diff_gaussian_rasterization_f/
+    __init__.py:830-863): one parameter tensor per group; ``step(visibility,
+    N)`` updates only the Gaussians marked visible, with the bias corrections
+    folded into the learning rate ``lr * sqrt(1 - 0.999^t) / (1 - 0.9^t)``.
+
+    Also takes the sparse COO gradients of ``step.view_loss(sparse_grad=True)``:
+    their rows are the Gaussians with radius > 0 -- the visibility the
+    reference passes -- and only those rows are read and written."""
+
+    def __init__(self, params, lr, eps):
+        super().__init__(params=params, lr=lr, eps=eps)
+
+    @torch.no_grad()
+    def step(self, visibility=None, N=None):
+        for group in self.param_groups:
+            lr = group["lr"]
+            eps = group["eps"]
+            assert len(group["params"]) == 1, "more than one tensor in group"
+            param = group["params"][0]
+            if param.grad is None or param.grad.numel() == 0:
+                continue
+            state = self.state[param]
+            if len(state) == 0:
+                state["step"] = torch.tensor(0.0, dtype=torch.float32)
+                state["exp_avg"] = torch.zeros_like(param, memory_format=torch.preserve_format)
+                state["exp_avg_sq"] = torch.zeros_like(param, memory_format=torch.preserve_format)
+            exp_avg, exp_avg_sq = state["exp_avg"], state["exp_avg_sq"]
+            state["step"] += 1
+            step = state["step"]
+            lr_t = lr * (1 - 0.999 ** step) ** 0.5 / (1 - 0.9 ** step)
+            n = N if N is not None else param.shape[0]
+            M = param.numel() // n
+            g = param.grad
+            if g.is_sparse:
+                g = g.coalesce()
+                rows = g.indices()[0]
+                ops.adam_update_rows(param, g.values().reshape(rows.numel(), M), exp_avg, exp_avg_sq, rows,
+                                     float(lr_t), 0.9, 0.999, eps, n, M)
+            else:
+                _C.adamUpdate(param, g, exp_avg, exp_avg_sq, visibility, float(lr_t), 0.9, 0.999, eps, n, M)
 
 
 # ---------------------------------------------------------------------------

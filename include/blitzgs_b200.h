@@ -313,6 +313,44 @@ int blitz_loss_backward(int C, int Hb, int W, const float* img, const uint8_t* g
                         const float* scale, float* dL_dimg, void* stream);
 
 /*
+ * Routing mask bool [P, mp_world_size] against per-rank tile rectangles:
+ * rectangles int32 [mp_world_size, 4] = {tile row begin, row end, column
+ * begin, column end} (widened by one tile with avoid_pixel_all2all; the
+ * begin bounds only while positive).  As in the reference, the square tile
+ * rect is tested without first rejecting an empty one.
+ * Replaces _C.get_local2j_ids_bool_adjust_mode6 / GetLocal2jIdsBoolAdjustMode6CUDA
+ * (submodule/diff-gaussian-rasterization_f/rasterize_points.cu:291-368).
+ */
+int blitz_get_local2j_ids_bool_adjust_mode6(int image_height, int image_width, int mp_rank, int mp_world_size,
+                                            int64_t P, const float* means2D, const int32_t* radii,
+                                            const int32_t* rectangles, int avoid_pixel_all2all, uint8_t* out,
+                                            void* stream);
+
+/*
+ * Sparse Adam step of one parameter tensor [N, M] (M floats per Gaussian):
+ * for every element of a Gaussian with visible[g] != 0,
+ *   m = b1 m + (1-b1) g;  v = b2 v + (1-b2) g^2;  param -= lr m / (sqrt(v) + eps)
+ * with the bias corrections folded into lr by the caller; invisible
+ * Gaussians keep their parameter and moments.
+ * Replaces _C.adamUpdate / ADAM::adamUpdate
+ * (submodule/diff-gaussian-rasterization_f/rasterize_points.cu:807-833,
+ * cuda_rasterizer/adam.cu:10-38), bit for bit.
+ */
+int blitz_adam_update(float* param, const float* param_grad, float* exp_avg, float* exp_avg_sq,
+                      const uint8_t* visible, float lr, float b1, float b2, float eps, int64_t N, int64_t M,
+                      void* stream);
+
+/*
+ * The same step for listed Gaussians only (no reference counterpart: the
+ * reference always passes a dense gradient): grad_rows [n_rows, M] holds the
+ * gradient of Gaussian rows[j] (int64, distinct) in row j -- the sparse
+ * gradient of the fused step -- so nothing is read or written for the others.
+ */
+int blitz_adam_update_rows(float* param, const float* grad_rows, float* exp_avg, float* exp_avg_sq,
+                           const int64_t* rows, int64_t n_rows, float lr, float b1, float b2, float eps, int64_t N,
+                           int64_t M, void* stream);
+
+/*
  * Send-buffer packing of one camera's exchange records (no reference
  * counterpart: the reference gathers with torch index_select per rank).
  * Row j < n_rows of records/dest_mask goes to every rank r with bit r set,

@@ -546,3 +546,62 @@ def route_bool(means2D, radii, H, W, dist_global_strategy, avoid_pixel_all2all=F
             lo, hi = lo - (gx + 1), hi + (gx + 1)
         out[:, rk] = (tmax >= tmin) & ~((tmax < lo) | (tmin >= hi))
     return out
+
+
+def route_rect_bool(means2D, radii, H, W, rectangles, avoid_pixel_all2all=False):
+    """Reference getTouchedIdsBoolAdjustMode6 (f/rasterize_points.cu:291-335):
+    rank rk renders tile rows [y_l, y_r) and columns [x_l, x_r)
+    (rectangles[rk]); the square tile rect is tested without rejecting an
+    empty one first.  bool [P, ws]."""
+    gx, gy = (W + TILE - 1) // TILE, (H + TILE - 1) // TILE
+    x0, y0, x1, y1 = tile_rect_int(np.asarray(means2D, np.float32), np.asarray(radii, np.int64), gx, gy)
+    rects = np.asarray(rectangles, np.int64).reshape(-1, 4)
+    out = np.zeros((len(x0), len(rects)), bool)
+    for rk, (yl, yr, xl, xr) in enumerate(rects):
+        if avoid_pixel_all2all:
+            yl = yl - 1 if yl > 0 else yl
+            xl = xl - 1 if xl > 0 else xl
+            yr, xr = yr + 1, xr + 1
+        out[:, rk] = ~((y1 <= yl) | (yr <= y0) | (x1 <= xl) | (xr <= x0))
+    return out
+
+
+def fma32(a, b, c):
+    """Correctly rounded float32 fused multiply-add of float32 tensors.
+    a*b is exact in float64 (2 x 24 significant bits); s + c is formed in
+    float64 with its exact rounding error (Knuth's TwoSum), and a float64 sum
+    that sits exactly halfway between two float32 values is moved one float64
+    step toward the error's sign before the final rounding, so the double
+    rounding cannot go the wrong way.  Exact for results in the float32
+    normal range."""
+    a, b, c = a.double(), b.double(), c.double()
+    s = a * b
+    t = s + c
+    bp = t - s
+    err = (s - (t - bp)) + (c - bp)
+    half = (t.view(torch.int64) & ((1 << 29) - 1)) == (1 << 28)
+    up = torch.nextafter(t, torch.full_like(t, float("inf")))
+    down = torch.nextafter(t, torch.full_like(t, float("-inf")))
+    t = torch.where(half & (err > 0), up, torch.where(half & (err < 0), down, t))
+    return t.float()
+
+
+def adam_update(param, grad, exp_avg, exp_avg_sq, visible, lr, b1, b2, eps):
+    """Reference adamUpdateCUDA (f/cuda_rasterizer/adam.cu:10-38) on [N, M]
+    float32 tensors, in place, for the rows with visible[g].  The moment
+    updates are the fused multiply-adds the reference build makes of
+    f/cuda_rasterizer/adam.cu:30-31 -- fma(1-b1, g, b1*m) and
+    fma((1-b2)*g, g, b2*v) -- so the result is bit-exact."""
+    f = lambda x: torch.tensor(x, dtype=f32)
+    b1, b2, lr, eps = f(b1), f(b2), f(lr), f(eps)
+    v = visible.bool()
+    g = grad[v]
+    m = fma32((f(1.0) - b1).expand_as(g), g, b1 * exp_avg[v])
+    s = fma32((f(1.0) - b2) * g, g, b2 * exp_avg_sq[v])
+    # float32 square root correctly rounded: from float64, where one rounding
+    # to float32 is exact (53 >= 2*24 + 2 bits); torch's vectorised float32
+    # sqrt on the CPU need not be
+    step = (-lr * m) / (torch.sqrt(s.double()).float() + eps)
+    param[v] = param[v] + step
+    exp_avg[v] = m
+    exp_avg_sq[v] = s

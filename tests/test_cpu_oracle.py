@@ -183,3 +183,62 @@ def test_oracle_gradients_close_to_reference():
     assert normwise_rel(rec[:, 12:15], g["g_rgb"]) < 5e-3
     assert normwise_rel(rec[:, 8:12], g["g_conic_opacity"]) < 5e-3
     assert normwise_rel(rec[:, 0:2], g["g_means2D"]) < 5e-3
+
+
+def _golden_optim():
+    import os
+    import sys
+    here = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+    sys.path.insert(0, here)
+    import make_golden_optim as G
+    g = np.load(os.path.join(here, "golden_optim.npz"))
+    adam, route = G.inputs()
+    assert str(g["input_sha256"]) == G.checksum(adam, route)
+    return G, g, adam, route
+
+
+def test_oracle_adam_bit_exact_against_reference():
+    """The reference's _C.adamUpdate, three lazy-Adam steps: parameter and
+    both moments of the visible rows bit for bit; the other rows untouched."""
+    G, g, adam, _ = _golden_optim()
+    for (M, N), (param, grads, vis) in zip(G.ADAM_CASES, adam):
+        p, m, v = param.clone(), torch.zeros_like(param), torch.zeros_like(param)
+        for t, gr in enumerate(grads, start=1):
+            O.adam_update(p, gr, m, v, vis, G.lr_at(t), 0.9, 0.999, G.EPS)
+        assert np.array_equal(p[vis].numpy().view(np.uint32), g[f"adam{M}_param"].view(np.uint32))
+        assert np.array_equal(m[vis].numpy().view(np.uint32), g[f"adam{M}_exp_avg"].view(np.uint32))
+        assert np.array_equal(v[vis].numpy().view(np.uint32), g[f"adam{M}_exp_avg_sq"].view(np.uint32))
+        assert torch.equal(p[~vis], param[~vis]) and not m[~vis].any() and not v[~vis].any()
+
+
+def test_oracle_fma32_is_correctly_rounded():
+    """fma32 against exact rational arithmetic (round to nearest, ties to
+    even) on seeded operands, a quarter of them with c cancelling a*b down to
+    its float32 rounding error."""
+    from fractions import Fraction
+    gen = torch.Generator().manual_seed(3)
+    a = torch.randn(400, generator=gen)
+    b = torch.randn(400, generator=gen)
+    c = torch.randn(400, generator=gen)
+    # c = float32(a*b) - a*b: the exact product minus its own rounding
+    ab32 = (a.double() * b.double()).float()
+    c[:100] = (-(a[:100].double() * b[:100].double()) + ab32[:100].double()).float()
+    got = O.fma32(a, b, c)
+    for i in range(400):
+        exact = Fraction(float(a[i])) * Fraction(float(b[i])) + Fraction(float(c[i]))
+        lo = float(np.float32(float(exact)))  # float64 rounding first: bracket the answer
+        cand = [np.float32(lo), np.nextafter(np.float32(lo), np.float32(np.inf)),
+                np.nextafter(np.float32(lo), np.float32(-np.inf))]
+        best = min(cand, key=lambda x: (abs(Fraction(float(x)) - exact),
+                                        int(np.array(x, np.float32).view(np.uint32)) & 1))
+        assert np.float32(got[i]) == best, i
+
+
+def test_oracle_mode6_routing_equals_reference():
+    """The reference's _C.get_local2j_ids_bool_adjust_mode6 on seeded screen
+    means, radii (zeros included) and four tile rectangles, with and without
+    avoid_pixel_all2all."""
+    G, g, _, (means2D, radii, rects) = _golden_optim()
+    for avoid in (False, True):
+        got = O.route_rect_bool(means2D.numpy(), radii.numpy(), G.H, G.W, rects.numpy(), avoid)
+        assert np.array_equal(got, g[f"mode6_avoid{int(avoid)}"])
