@@ -2,41 +2,49 @@
 //
 // Forward semantics follow the reference renderCUDA
 // (submodule/diff-gaussian-rasterization_r/cuda_rasterizer/forward.cu:263-413):
-// one 16x16 tile per CTA, one pixel per thread, front-to-back over the
-// tile's list in batches of 256 staged in shared memory;
+// one pixel per thread, front-to-back over the tile's depth-sorted list;
 //   power = -0.5 (c00 dx^2 + c11 dy^2) - c01 dx dy   (skip if > 0)
 //   alpha = min(0.99, o exp(power))                   (skip if < 1/255)
 //   stop before the Gaussian that would take T below 1e-4.
 // The per-pair arithmetic is written in the reference's expression order so
 // that skip/stop decisions and n_contrib match bit for bit.
 //
-// B200-side changes (no output bit changes):
-//   * colours are staged in shared memory with the geometry instead of being
-//     re-read from global memory for every (pixel, Gaussian) pair;
+// Work decomposition (B200-side; no output bit changes in the forward):
+//   * the unit of work is a warp strip: 8x4 pixels of a 16x16 tile.  Each
+//     warp walks its tile's list on its own, 32 entries at a time: lane i
+//     loads entry i, tests a conservative bounding box of the Gaussian's
+//     alpha >= 1/255 region against the strip's 32 pixel centres, and the
+//     survivors are compacted (ballot + popc) into the warp's shared-memory
+//     batch.  About half of the (strip, Gaussian) pairs of a tile list miss
+//     the strip and never enter the per-pixel loop, and no warp waits at a
+//     block barrier for the tile's slowest warp;
+//   * the forward stops a warp as soon as its 32 pixels are saturated;
+//     the backward starts each warp at its own largest n_contrib;
 //   * a per-Gaussian log-domain threshold rejects, before the exp, every pair
 //     whose alpha is provably below 1/255 (margin 1e-3 in the exponent, far
 //     above the few-ulp error of logf/expf), so most pairs cost ~8 FP32
 //     instructions instead of ~30;
-//   * a conservative bounding box of each Gaussian's alpha >= 1/255 region
-//     drops it from the tile's batch when it misses the whole tile (a
-//     per-warp test on two pixel rows was tried and cost more than it saved;
-//     so did two pixels per thread, which cut instructions by a fifth but
-//     lost more in occupancy and early exit than it gained);
-//   * out_observe counts are aggregated per batch in shared memory and
-//     flushed with one atomic per (tile, Gaussian);
+//   * colours are staged with the geometry instead of being re-read from
+//     global memory for every (pixel, Gaussian) pair;
+//   * out_observe counts are aggregated per (warp, Gaussian) in shared memory
+//     and flushed with one atomic;
 //   * the per-tile statistics (n_render, n_consider, n_contrib) are reduced
 //     in the epilogue instead of three extra kernels.
-//
-// Both kernels stage each Gaussian as three float4 in shared memory: the two
-// that every (pixel, Gaussian) pair reads (position, conic, opacity, skip
-// threshold, list position) and the colour, read only by contributing pairs.
+// Strip shape: 8x4 pixels overlap ~18% fewer ~12-pixel splats than 16x2.
+// Tried and slower: 16x2 strips (13% slower forward, 19% slower backward);
+// a tile-wide staging round shared by the 8 warps (23% slower forward, 35%
+// slower backward than 8x4 strips); two pixels per
+// thread (fewer instructions, but the occupancy loss cost more), a per-warp
+// box test inside the pair loop, and a guarded __expf in the backward.
 //
 // Backward follows the reference back-to-front replay (backward.cu:324-530)
 // but replaces the 11 global atomics per (pixel, Gaussian) pair with a
 // warp-level transpose reduction (16 shuffles for 11 values) and one
 // 11-lane RED instruction per (warp, Gaussian) -- or, when at most
-// kDirectLanes pixels of the warp contribute, their own REDs -- and starts
-// the replay at the tile's largest n_contrib instead of the end of the list.
+// kDirectLanes pixels of the warp contribute, their own REDs.  T is
+// recovered with one reciprocal of (1 - alpha) (fast division, 1 - alpha in
+// [0.01, 1)) shared by the two divisions of the reference; the gradients
+// differ from IEEE division by ~1e-7 relative.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -44,10 +52,28 @@ namespace blitz {
 
 namespace {
 
-constexpr int kBatch = kTilePix;  // 256 Gaussians per staged batch
 // Backward: a (warp, Gaussian) pair with at most this many contributing
 // pixels adds their gradients with per-lane REDs instead of the reduction.
 constexpr int kDirectLanes = 8;
+// A warp strip: the kStripW x kStripH pixels of one warp (lane l: column
+// l % kStripW, row l / kStripW); kStrips per tile, strip s at column
+// s % kStripsX and row s / kStripsX of the tile's strip grid.
+constexpr int kStripW = 8;
+constexpr int kStripH = 4;
+constexpr int kStripsX = kTileX / kStripW;
+constexpr int kStrips = kStripsX * (kTileY / kStripH);
+static_assert(kStripW * kStripH == 32, "a strip is one warp of pixels");
+
+// Pixel of this lane in strip s of tile (tx, ty).
+__device__ __forceinline__ int2 strip_pixel(int tx, int ty, int s, int lane) {
+  return make_int2(tx * kTileX + (s % kStripsX) * kStripW + lane % kStripW,
+                   ty * kTileY + (s / kStripsX) * kStripH + lane / kStripW);
+}
+
+// Top-left pixel of strip s of tile (tx, ty).
+__device__ __forceinline__ float2 strip_origin(int tx, int ty, int s) {
+  return make_float2((float)(tx * kTileX + (s % kStripsX) * kStripW), (float)(ty * kTileY + (s / kStripsX) * kStripH));
+}
 
 // exp-skip threshold: for power < thr, o*expf(power) < (1/255) * e^-1e-3.
 __device__ __forceinline__ float skip_threshold(float o) {
@@ -95,26 +121,6 @@ __device__ __forceinline__ bool box_misses(float4 b, float x0, float x1, float y
   return b.y < x0 || b.x > x1 || b.w < y0 || b.z > y1;
 }
 
-// Order-preserving compaction: returns this thread's slot among the kept
-// entries of the batch (-1 if not kept) and the number kept.  The caller
-// writes its staged data at that slot, so the blend loops read consecutive
-// slots with no index indirection.  Contains one barrier.
-__device__ __forceinline__ int compact_slot(bool keep, int* s_wcnt, int& kept) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const unsigned m = __ballot_sync(0xffffffffu, keep);
-  if (lane == 0) s_wcnt[warp] = __popc(m);
-  __syncthreads();
-  int off = 0, tot = 0;
-#pragma unroll
-  for (int w = 0; w < kTilePix / 32; ++w) {
-    const int c = s_wcnt[w];
-    off += (w < warp) ? c : 0;
-    tot += c;
-  }
-  kept = tot;
-  return keep ? off + __popc(m & ((1u << lane) - 1u)) : -1;
-}
-
 __device__ __forceinline__ int block_sum_int(int v, int* s_red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -134,8 +140,8 @@ __device__ __forceinline__ int block_sum_int(int v, int* s_red) {
 __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
   const int tile = blockIdx.x;
   const int tx = tile % p.grid_x, ty = tile / p.grid_x;
-  const int lx = threadIdx.x % kTileX, ly = threadIdx.x / kTileX;
-  const int px = tx * kTileX + lx, py = ty * kTileY + ly;
+  const int2 pxy = strip_pixel(tx, ty, threadIdx.x >> 5, threadIdx.x & 31);
+  const int px = pxy.x, py = pxy.y;
   const bool inside = px < p.W && py < p.H;
   const int64_t HW = (int64_t)p.H * p.W;
   const int64_t pix = (int64_t)p.W * py + px;
@@ -157,21 +163,21 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
     return;
   }
 
-  // staged Gaussian: A = (x, y, c00, c01), B = (c11, opacity, skip threshold,
-  // list position bits), C = (r, g, b, -); A and B serve every pair, C only
-  // contributing pairs
-  __shared__ float4 s_a[kBatch];
-  __shared__ float4 s_b[kBatch];
-  __shared__ float4 s_c[kBatch];
-  __shared__ int s_id[kBatch];
-  __shared__ int s_obs[kBatch];
+  // Warp w (strip w of the tile) walks the tile's list on its own, 32
+  // entries at a time, keeps the Gaussians whose alpha box reaches its
+  // pixels, and stops as soon as its 32 pixels are saturated.
+  constexpr int kWarps = kTilePix / 32;
+  __shared__ float4 s_a[kWarps][32];
+  __shared__ float4 s_b[kWarps][32];
+  __shared__ float4 s_c[kWarps][32];
+  __shared__ int s_id[kWarps][32];
+  __shared__ int s_obs[kWarps][32];
   __shared__ int s_red[32];
-  __shared__ int s_wcnt[kTilePix / 32];
-  const float tx0 = (float)(tx * kTileX), ty0 = (float)(ty * kTileY);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float2 so = strip_origin(tx, ty, warp);
 
   const uint2 range = p.ranges[tile];
   const int n = (int)(range.y - range.x);
-  const int rounds = (n + kBatch - 1) / kBatch;
   const float2 pixf = make_float2((float)px, (float)py);
 
   bool done = !inside;
@@ -179,38 +185,36 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
   uint32_t last_contributor = 0, n2l = 0;
   float C0 = 0.f, C1 = 0.f, C2 = 0.f;
 
-  int toDo = n;
-  for (int r = 0; r < rounds; ++r, toDo -= kBatch) {
-    const int num_done = __syncthreads_count(done);
-    if (num_done == kTilePix) break;
-    const int k = r * kBatch + threadIdx.x;
+  for (int base = 0; base < n; base += 32) {
+    if (__all_sync(0xffffffffu, done)) break;
+    const int k = base + lane;
     bool keep = false;
     int id = 0;
     float2 xy;
-    float4 co, cth;
+    float4 co;
     if (k < n) {
       id = (int)p.point_list[range.x + k];
       xy = reinterpret_cast<const float2*>(p.means2D)[id];
       co = reinterpret_cast<const float4*>(p.conic_opacity)[id];
-      cth = make_float4(p.rgb[3 * (int64_t)id + 0], p.rgb[3 * (int64_t)id + 1], p.rgb[3 * (int64_t)id + 2],
-                        skip_threshold(co.w));
-      keep = !box_misses(alpha_box(xy, co), tx0, tx0 + 15.f, ty0, ty0 + 15.f);
+      keep = !box_misses(alpha_box(xy, co), so.x, so.x + (float)(kStripW - 1), so.y, so.y + (float)(kStripH - 1));
     }
-    int kept;
-    const int slot = compact_slot(keep, s_wcnt, kept);
-    if (slot >= 0) {
-      s_id[slot] = id;
-      s_a[slot] = make_float4(xy.x, xy.y, co.x, co.y);
+    const unsigned km = __ballot_sync(0xffffffffu, keep);
+    if (!km) continue;
+    if (keep) {
+      const int slot = __popc(km & ((1u << lane) - 1u));
+      s_id[warp][slot] = id;
+      s_a[warp][slot] = make_float4(xy.x, xy.y, co.x, co.y);
       // 1-based list position, as the reference counts it
-      s_b[slot] = make_float4(co.z, co.w, cth.w, __int_as_float(r * kBatch + threadIdx.x + 1));
-      s_c[slot] = cth;
-      s_obs[slot] = 0;
+      s_b[warp][slot] = make_float4(co.z, co.w, skip_threshold(co.w), __int_as_float(k + 1));
+      s_c[warp][slot] = make_float4(p.rgb[3 * (int64_t)id + 0], p.rgb[3 * (int64_t)id + 1],
+                                    p.rgb[3 * (int64_t)id + 2], 0.f);
+      s_obs[warp][slot] = 0;
     }
-    __syncthreads();
-
+    __syncwarp();
+    const int kept = __popc(km);
     for (int j = 0; !done && j < kept; ++j) {
-      const float4 ga = s_a[j];
-      const float4 gb = s_b[j];
+      const float4 ga = s_a[warp][j];
+      const float4 gb = s_b[warp][j];
       const float2 d = {ga.x - pixf.x, ga.y - pixf.y};
       const float4 con_o = make_float4(ga.z, ga.w, gb.x, gb.y);
       const float power = pair_power(con_o, d);
@@ -224,16 +228,17 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
         continue;
       }
       ++n2l;
-      const float4 cth = s_c[j];
+      const float4 cth = s_c[warp][j];
       C0 += cth.x * alpha * T;
       C1 += cth.y * alpha * T;
       C2 += cth.z * alpha * T;
-      if (T > 0.5) atomicAdd(&s_obs[j], 1);
+      if (T > 0.5) atomicAdd(&s_obs[warp][j], 1);
       T = test_T;
       last_contributor = (uint32_t)__float_as_int(gb.w);
     }
-    __syncthreads();
-    if (threadIdx.x < kept && s_obs[threadIdx.x] > 0) atomicAdd(&p.out_observe[s_id[threadIdx.x]], s_obs[threadIdx.x]);
+    __syncwarp();
+    if (lane < kept && s_obs[warp][lane] > 0) atomicAdd(&p.out_observe[s_id[warp][lane]], s_obs[warp][lane]);
+    __syncwarp();
   }
 
   if (inside) {
@@ -300,26 +305,30 @@ __device__ __forceinline__ float warp_transpose_reduce16(float v[16]) {
   return g + __shfl_xor_sync(0xffffffffu, g, 1);
 }
 
-__global__ void __launch_bounds__(kTilePix, 4) blend_bwd_kernel(BlendBwdParams p) {
-  const int tile = blockIdx.x;
+// Backward, one warp per CTA: CTA tile * kStrips + s replays strip s of the
+// tile.  Each warp walks its tile's list back to front from its own largest
+// n_contrib, 32 list entries at a time: lane i loads entry i, tests the
+// Gaussian's alpha >= 1/255 box against the strip's pixels, and the
+// survivors are compacted into the warp's shared-memory batch.  No block
+// barrier: warps of a tile never wait for one another.
+__global__ void __launch_bounds__(32, 32) blend_bwd_kernel(BlendBwdParams p) {
+  const int tile = blockIdx.x / kStrips;
+  const int strip = blockIdx.x - tile * kStrips;
   if (p.compute_locally && !p.compute_locally[tile]) return;
   const int tx = tile % p.grid_x, ty = tile / p.grid_x;
-  const int lx = threadIdx.x % kTileX, ly = threadIdx.x / kTileX;
-  const int px = tx * kTileX + lx, py = ty * kTileY + ly;
+  const int lane = threadIdx.x;
+  const int2 pxy = strip_pixel(tx, ty, strip, lane);
+  const int px = pxy.x, py = pxy.y;
   const bool inside = px < p.W && py < p.H;
   const int64_t HW = (int64_t)p.H * p.W;
   const int64_t pix = (int64_t)p.W * py + px;
   const float2 pixf = make_float2((float)px, (float)py);
 
-  // staged Gaussian: A = (x, y, c00, c01), B = (c11, opacity, skip threshold,
-  // list position bits), C = (r, g, b, -)
-  __shared__ float4 s_a[kBatch];
-  __shared__ float4 s_b[kBatch];
-  __shared__ float4 s_c[kBatch];
-  __shared__ int s_id[kBatch];
-  __shared__ int s_max;
-  __shared__ int s_wcnt[kTilePix / 32];
-  const float tx0 = (float)(tx * kTileX), ty0 = (float)(ty * kTileY);
+  __shared__ float4 s_a[32];
+  __shared__ float4 s_b[32];
+  __shared__ float4 s_c[32];
+  __shared__ int s_id[32];
+  const float2 so = strip_origin(tx, ty, strip);
 
   const uint2 range = p.ranges[tile];
   const float T_final = inside ? p.final_T[pix] : 0.f;
@@ -333,48 +342,42 @@ __global__ void __launch_bounds__(kTilePix, 4) blend_bwd_kernel(BlendBwdParams p
   }
   const float bg_dot = p.bg[0] * dpx[0] + p.bg[1] * dpx[1] + p.bg[2] * dpx[2];
 
-  // Only list positions below the tile's largest n_contrib can contribute.
-  if (threadIdx.x == 0) s_max = 0;
-  __syncthreads();
-  int wmax = last_contributor;
+  // only list positions below the strip's largest n_contrib can contribute
+  int n_eff = last_contributor;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) wmax = max(wmax, __shfl_xor_sync(0xffffffffu, wmax, o));
-  if ((threadIdx.x & 31) == 0) atomicMax(&s_max, wmax);
-  __syncthreads();
-  const int n_eff = s_max;
-  const int rounds = (n_eff + kBatch - 1) / kBatch;
+  for (int o = 16; o > 0; o >>= 1) n_eff = max(n_eff, __shfl_xor_sync(0xffffffffu, n_eff, o));
 
   const float ddelx_dx = 0.5 * p.W;
   const float ddely_dy = 0.5 * p.H;
   float accum[3] = {0.f, 0.f, 0.f};
   float last_alpha = 0.f;
   float last_color[3] = {0.f, 0.f, 0.f};
-  const int lane = threadIdx.x & 31;
 
-  for (int r = 0; r < rounds; ++r) {
-    __syncthreads();
-    const int k = n_eff - 1 - (r * kBatch + (int)threadIdx.x);  // list position, back to front
+  for (int base = 0; base < n_eff; base += 32) {
+    const int k = n_eff - 1 - (base + lane);  // list position, back to front
     bool keep = false;
     int id = 0;
     float2 xy;
-    float4 co, cth;
+    float4 co;
     if (k >= 0) {
       id = (int)p.point_list[range.x + k];
       xy = reinterpret_cast<const float2*>(p.means2D)[id];
       co = reinterpret_cast<const float4*>(p.conic_opacity)[id];
-      cth = make_float4(p.rgb[3 * (int64_t)id + 0], p.rgb[3 * (int64_t)id + 1], p.rgb[3 * (int64_t)id + 2],
-                        skip_threshold(co.w));
-      keep = !box_misses(alpha_box(xy, co), tx0, tx0 + 15.f, ty0, ty0 + 15.f);
+      keep = !box_misses(alpha_box(xy, co), so.x, so.x + (float)(kStripW - 1), so.y, so.y + (float)(kStripH - 1));
     }
-    int kept;
-    const int slot = compact_slot(keep, s_wcnt, kept);
-    if (slot >= 0) {
+    const unsigned km = __ballot_sync(0xffffffffu, keep);
+    if (!km) continue;
+    __syncwarp();  // the previous batch is no longer read
+    if (keep) {
+      const int slot = __popc(km & ((1u << lane) - 1u));
       s_id[slot] = p.record_rows ? (int)__ldg(p.record_rows + id) : id;  // gradient record row
       s_a[slot] = make_float4(xy.x, xy.y, co.x, co.y);
-      s_b[slot] = make_float4(co.z, co.w, cth.w, __int_as_float(k));  // list position
-      s_c[slot] = cth;
+      s_b[slot] = make_float4(co.z, co.w, skip_threshold(co.w), __int_as_float(k));  // list position
+      s_c[slot] = make_float4(p.rgb[3 * (int64_t)id + 0], p.rgb[3 * (int64_t)id + 1], p.rgb[3 * (int64_t)id + 2],
+                              0.f);
     }
-    __syncthreads();
+    __syncwarp();
+    const int kept = __popc(km);
     for (int j = 0; j < kept; ++j) {
       const float4 gb = s_b[j];
       const int pos = __float_as_int(gb.w);
@@ -391,7 +394,8 @@ __global__ void __launch_bounds__(kTilePix, 4) blend_bwd_kernel(BlendBwdParams p
           const float alpha = min(0.99f, con_o.w * G);
           if (!(alpha < 1.0f / 255.0f)) {
             contrib = true;
-            T = T / (1.f - alpha);
+            const float inv1ma = __fdividef(1.0f, 1.f - alpha);  // 1 - alpha in [0.01, 1)
+            T = T * inv1ma;
             const float dchannel_dcolor = alpha * T;
             float dL_dalpha = 0.0f;
             const float c[3] = {cth.x, cth.y, cth.z};
@@ -404,7 +408,7 @@ __global__ void __launch_bounds__(kTilePix, 4) blend_bwd_kernel(BlendBwdParams p
             }
             dL_dalpha *= T;
             last_alpha = alpha;
-            dL_dalpha += (-T_final / (1.f - alpha)) * bg_dot;
+            dL_dalpha += (-T_final * inv1ma) * bg_dot;
             const float dL_dG = con_o.w * dL_dalpha;
             const float gdx = G * d.x;
             const float gdy = G * d.y;
@@ -460,6 +464,7 @@ __global__ void __launch_bounds__(kTilePix, 4) blend_bwd_kernel(BlendBwdParams p
   }
 }
 
+
 }  // namespace
 
 int launch_blend_fwd(const BlendFwdParams& p, cudaStream_t st) {
@@ -472,7 +477,7 @@ int launch_blend_fwd(const BlendFwdParams& p, cudaStream_t st) {
 int launch_blend_bwd(const BlendBwdParams& p, cudaStream_t st) {
   const int n_tiles = p.grid_x * p.grid_y;
   if (n_tiles <= 0) return 0;
-  blend_bwd_kernel<<<n_tiles, kTilePix, 0, st>>>(p);
+  blend_bwd_kernel<<<n_tiles * kStrips, 32, 0, st>>>(p);
   return (int)cudaGetLastError();
 }
 
