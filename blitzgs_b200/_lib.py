@@ -51,6 +51,11 @@ SIGNATURES = {
     "blitz_loss_backward": (_i32, [_i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "blitz_get_local2j_ids_bool": (_i32, [_i32, _i32, _i32, _i32, _i64, _vp, _vp, _vp, _i32, _vp, _vp]),
     "blitz_fp32_probe": (_i32, [_i32, _i64, _vp, _vp]),
+    "blitz_loss_combine": (_i32, [_vp, _vp, _f32, _f32, _f32, _f32, _vp, _vp]),
+    "blitz_loss_combine_backward": (_i32, [_vp, _vp, _vp, _vp, _f32, _f32, _f32, _f32, _vp, _vp]),
+    "blitz_read_totals": (_i32, [_vp, _vp, _vp, _vp, _vp]),
+    "blitz_zero_fill_async": (_i32, [_i32, _vp, _vp, _vp]),
+    "blitz_zero_fill_wait": (_i32, [_vp]),
 }
 
 _lock = threading.Lock()
@@ -99,6 +104,11 @@ def ptr(t):
 
 
 def stream_ptr(stream=None):
+    """cudaStream_t (as an int) of ``stream``, else of the current device's
+    current stream.  The default path asks torch's C accessors directly:
+    torch.cuda.current_stream() builds a Stream object and re-resolves the
+    device on every call (~15 us, several times per training step)."""
     import torch
-    s = stream if stream is not None else torch.cuda.current_stream()
-    return s.cuda_stream
+    if stream is not None:
+        return stream.cuda_stream
+    return torch._C._cuda_getCurrentRawStream(torch._C._cuda_getDevice())

@@ -1,6 +1,7 @@
 // extern "C" entry points (declared in include/blitzgs_b200.h).
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "blitzgs_b200.h"
@@ -566,6 +567,91 @@ int blitz_exchange_pack(int64_t n_rows, int n_ranks, const float* records, const
   k.send_row = send_row;
   k.row_base = row_base;
   return check(launch_exchange_pack(k, S(stream)), "blitz_exchange_pack");
+}
+
+int blitz_loss_combine(const double* sums, const double* reg, float one_minus_lambda, float lambda, float n3,
+                       float reg_weight, float* out, void* stream) {
+  if (!sums || !out || !(n3 > 0.f)) return fail(BLITZ_EINVAL, "blitz_loss_combine: bad arguments");
+  LossCombineParams p{sums, reg, one_minus_lambda, lambda, n3, reg_weight, out};
+  return check(launch_loss_combine(p, S(stream)), "blitz_loss_combine");
+}
+
+int blitz_loss_combine_backward(const float* g_loss, const float* g_l1, const float* g_ss, const float* fwd_out,
+                                float one_minus_lambda, float lambda, float n3, float reg_weight, float* scales,
+                                void* stream) {
+  if (!fwd_out || !scales || !(n3 > 0.f)) return fail(BLITZ_EINVAL, "blitz_loss_combine_backward: bad arguments");
+  LossCombineParams p{nullptr, nullptr, one_minus_lambda, lambda, n3, reg_weight, const_cast<float*>(fwd_out)};
+  return check(launch_loss_combine_bwd(p, g_loss, g_l1, g_ss, scales, S(stream)), "blitz_loss_combine_backward");
+}
+
+int blitz_read_totals(const int64_t* totals, const int32_t* vis_count, int64_t* host_totals, int32_t* host_vis,
+                      void* stream) {
+  if (!totals || !host_totals || ((vis_count == nullptr) != (host_vis == nullptr)))
+    return fail(BLITZ_EINVAL, "blitz_read_totals: bad arguments");
+  cudaError_t e = cudaMemcpyAsync(host_totals, totals, 2 * sizeof(int64_t), cudaMemcpyDeviceToHost, S(stream));
+  if (e == cudaSuccess && vis_count)
+    e = cudaMemcpyAsync(host_vis, vis_count, sizeof(int32_t), cudaMemcpyDeviceToHost, S(stream));
+  if (e == cudaSuccess) e = cudaStreamSynchronize(S(stream));
+  return check((int)e, "blitz_read_totals");
+}
+
+}  // extern "C"
+
+namespace {
+
+// Side stream and events of the asynchronous zero fill, per device.
+struct FillState {
+  bool ready = false;
+  cudaStream_t side = nullptr;
+  cudaEvent_t queued = nullptr, done = nullptr;
+};
+constexpr int kMaxDevices = 64;
+FillState g_fill[kMaxDevices];
+std::mutex g_fill_mu;
+
+int fill_state(FillState** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev < 0 || dev >= kMaxDevices) return BLITZ_EINVAL;
+  FillState& f = g_fill[dev];
+  if (!f.ready) {
+    std::lock_guard<std::mutex> lock(g_fill_mu);
+    if (!f.ready) {
+      e = cudaStreamCreateWithFlags(&f.side, cudaStreamNonBlocking);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&f.queued, cudaEventDisableTiming);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&f.done, cudaEventDisableTiming);
+      if (e != cudaSuccess) return (int)e;
+      f.ready = true;
+    }
+  }
+  *out = &f;
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int blitz_zero_fill_async(int n, void* const* ptrs, const size_t* bytes, void* stream) {
+  if (n < 0 || (n > 0 && (!ptrs || !bytes))) return fail(BLITZ_EINVAL, "blitz_zero_fill_async: bad arguments");
+  FillState* f = nullptr;
+  int rc = fill_state(&f);
+  if (rc) return fail(rc, "blitz_zero_fill_async: side stream");
+  // the side stream starts after everything already queued on `stream`
+  cudaError_t e = cudaEventRecord(f->queued, S(stream));
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(f->side, f->queued, 0);
+  for (int i = 0; e == cudaSuccess && i < n; ++i)
+    if (bytes[i]) e = cudaMemsetAsync(ptrs[i], 0, bytes[i], f->side);
+  if (e == cudaSuccess) e = cudaEventRecord(f->done, f->side);
+  return check((int)e, "blitz_zero_fill_async");
+}
+
+int blitz_zero_fill_wait(void* stream) {
+  FillState* f = nullptr;
+  int rc = fill_state(&f);
+  if (rc) return fail(rc, "blitz_zero_fill_wait: side stream");
+  return check((int)cudaStreamWaitEvent(S(stream), f->done, 0), "blitz_zero_fill_wait");
 }
 
 int blitz_fp32_probe(int blocks, int64_t iters, float* sink, void* stream) {

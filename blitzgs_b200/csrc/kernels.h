@@ -200,6 +200,16 @@ struct LossBwdParams {
 };
 int launch_loss_bwd(const LossBwdParams& p, const float* window11, cudaStream_t st);
 
+struct LossCombineParams {
+  const double* sums;  // {sum L1, sum SSIM}
+  const double* reg;   // {sum of min-axis scales, count} or null
+  float one_minus_lambda, lambda, n3, reg_weight;
+  float* out;          // {loss, L1, SSIM, reg, cnt}; read back by the backward
+};
+int launch_loss_combine(const LossCombineParams& p, cudaStream_t st);
+int launch_loss_combine_bwd(const LossCombineParams& p, const float* g_loss, const float* g_l1, const float* g_ss,
+                            float* scales, cudaStream_t st);
+
 // ---------------------------------------------------------------------------
 // Routing (which ranks' tile rows a Gaussian overlaps)
 // ---------------------------------------------------------------------------

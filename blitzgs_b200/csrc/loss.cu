@@ -195,7 +195,64 @@ __global__ void __launch_bounds__(256) loss_bwd_kernel(LossBwdParams bp, Win win
   }
 }
 
+// The per-camera loss of the training step
+//   loss = (1 - l) * (L1 / N3) + l * (1 - SSIM / N3) + w * reg / max(cnt, 1)
+// (gaussian_renderer/loss_distribution.py:307-322 with the min-scale term as
+// a sum and a count), evaluated once on the device in float32, rounding step
+// by step as PyTorch's CUDA kernels evaluate the same expression on 0-dim
+// float32 tensors: a Python float enters as float32, and a division by a
+// Python number is a multiplication by its float32 reciprocal (PyTorch's
+// true-division kernel takes that shortcut for a host scalar divisor).
+// out = {loss, L1, SSIM, reg, cnt}.
+__global__ void loss_combine_kernel(LossCombineParams p) {
+  const float inv_n3 = __fdiv_rn(1.0f, p.n3);
+  const float l1 = (float)p.sums[0];
+  const float ss = (float)p.sums[1];
+  float loss = __fadd_rn(__fmul_rn(p.one_minus_lambda, __fmul_rn(l1, inv_n3)),
+                         __fmul_rn(p.lambda, __fsub_rn(1.0f, __fmul_rn(ss, inv_n3))));
+  float reg = 0.f, cnt = 0.f;
+  if (p.reg) {
+    reg = (float)p.reg[0];
+    cnt = (float)p.reg[1];
+    loss = __fadd_rn(loss, __fdiv_rn(__fmul_rn(p.reg_weight, reg), fmaxf(cnt, 1.0f)));
+  }
+  p.out[0] = loss;
+  p.out[1] = l1;
+  p.out[2] = ss;
+  p.out[3] = reg;
+  p.out[4] = cnt;
+}
+
+// Gradients of the sums from the upstream gradients of {loss, L1, SSIM}, as
+// PyTorch's autograd forms them for the expression above:
+//   dsum L1 = (g * (1 - l)) * (1/N3) + g_L1,
+//   dsum SSIM = -(g * l) * (1/N3) + g_SSIM,  dreg = (g / max(cnt, 1)) * w.
+// scales = {dsum L1, dsum SSIM, dreg}; a NULL upstream pointer counts as 0.
+__global__ void loss_combine_bwd_kernel(LossCombineParams p, const float* g_loss, const float* g_l1,
+                                        const float* g_ss, float* scales) {
+  const float inv_n3 = __fdiv_rn(1.0f, p.n3);
+  const float g = g_loss ? *g_loss : 0.f;
+  float s0 = __fmul_rn(__fmul_rn(g, p.one_minus_lambda), inv_n3);
+  float s1 = __fmul_rn(-__fmul_rn(g, p.lambda), inv_n3);
+  if (g_l1) s0 = __fadd_rn(s0, *g_l1);
+  if (g_ss) s1 = __fadd_rn(s1, *g_ss);
+  scales[0] = s0;
+  scales[1] = s1;
+  scales[2] = __fmul_rn(__fdiv_rn(g, fmaxf(p.out[4], 1.0f)), p.reg_weight);
+}
+
 }  // namespace
+
+int launch_loss_combine(const LossCombineParams& p, cudaStream_t st) {
+  loss_combine_kernel<<<1, 1, 0, st>>>(p);
+  return (int)cudaGetLastError();
+}
+
+int launch_loss_combine_bwd(const LossCombineParams& p, const float* g_loss, const float* g_l1, const float* g_ss,
+                            float* scales, cudaStream_t st) {
+  loss_combine_bwd_kernel<<<1, 1, 0, st>>>(p, g_loss, g_l1, g_ss, scales);
+  return (int)cudaGetLastError();
+}
 
 int launch_loss_fwd(const LossParams& p, const float* window11, double* sums, cudaStream_t st) {
   if (p.C <= 0 || p.Hb <= 0 || p.W <= 0) return 0;

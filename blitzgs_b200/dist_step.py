@@ -26,7 +26,7 @@ import torch
 
 from . import distributed as D
 from . import ops
-from .step import _zero_fill_async
+from .step import _zero_fill_async, _zero_fill_wait
 
 # forward record: conic00 conic01 conic11 opacity | x y | r g b | depth radius(bits) minscale
 _FWD_C = 12
@@ -161,33 +161,36 @@ class _DistributedBatch(torch.autograd.Function):
         # the shard's dense gradients are zero except at listed rows: fill them on
         # a side stream while the render backward (issue bound) runs
         grads = [torch.empty_like(t) for t in (xyz, s_raw, q_raw, o_raw, dc, rest)]
-        fill_done = _zero_fill_async(grads)
-        # receiver: render backward of the owned bands -> 12-float gradient records
-        send = torch.zeros((sum(plan.recv_splits), _BWD_C), dtype=torch.float32, device=dev)
-        for k, (state, m2, conic, rgb, cl, band, gt, partials, vis, nvis, (y0, y1), n3) in ctx.saved.items():
-            rs = rasters[k]
-            H, W = int(rs.image_height), int(rs.image_width)
-            scale = torch.stack([g_loss * (1.0 - lambda_dssim) / n3, -g_loss * lambda_dssim / n3]).float()
-            g_band = ops.loss_backward(band, gt, partials, scale)
-            dpix = torch.zeros((3, H, W), dtype=torch.float32, device=dev)
-            dpix[:, y0:y1] = g_band
-            rec16 = ops.render_backward(state, m2, conic, rgb, rs.bg, cl, dpix)
-            g = torch.cat([rec16[:, 8:12], rec16[:, 0:2], rec16[:, 12:15], rec16[:, 4:6],
-                           (g_loss * reg_w * vis / nvis.clamp(min=1.0))[:, None]], 1)
-            pos = 0
-            for _, s, c in plan.recv_offsets[k]:
-                if c:
-                    send[s:s + c] = g[pos:pos + c]
-                    pos += c
-        recv = torch.empty((sum(plan.send_splits), _BWD_C), dtype=torch.float32, device=dev)
-        torch.distributed.all_to_all_single(recv, send, plan.send_splits, plan.recv_splits, group=group)
-        # owner: one scatter-add into compact per-camera rows (aligned with the visible lists)
-        acc = torch.zeros((ctx.offs[-1], _BWD_C), dtype=torch.float32, device=dev)
-        acc.index_add_(0, ctx.send_rows, recv)
-        sh = ops.sh_layout(dc=dc, rest=rest)
-        M = rest.shape[1]
-        g_xyz, g_s, g_q, g_o, g_dc, g_rest = grads
-        torch.cuda.current_stream(dev).wait_event(fill_done)
+        _zero_fill_async(grads)
+        try:
+            # receiver: render backward of the owned bands -> 12-float gradient records
+            send = torch.zeros((sum(plan.recv_splits), _BWD_C), dtype=torch.float32, device=dev)
+            for k, (state, m2, conic, rgb, cl, band, gt, partials, vis, nvis, (y0, y1), n3) in ctx.saved.items():
+                rs = rasters[k]
+                H, W = int(rs.image_height), int(rs.image_width)
+                scale = torch.stack([g_loss * (1.0 - lambda_dssim) / n3, -g_loss * lambda_dssim / n3]).float()
+                g_band = ops.loss_backward(band, gt, partials, scale)
+                dpix = torch.zeros((3, H, W), dtype=torch.float32, device=dev)
+                dpix[:, y0:y1] = g_band
+                rec16 = ops.render_backward(state, m2, conic, rgb, rs.bg, cl, dpix)
+                g = torch.cat([rec16[:, 8:12], rec16[:, 0:2], rec16[:, 12:15], rec16[:, 4:6],
+                               (g_loss * reg_w * vis / nvis.clamp(min=1.0))[:, None]], 1)
+                pos = 0
+                for _, s, c in plan.recv_offsets[k]:
+                    if c:
+                        send[s:s + c] = g[pos:pos + c]
+                        pos += c
+            recv = torch.empty((sum(plan.send_splits), _BWD_C), dtype=torch.float32, device=dev)
+            torch.distributed.all_to_all_single(recv, send, plan.send_splits, plan.recv_splits, group=group)
+            # owner: one scatter-add into compact per-camera rows (aligned with the visible lists)
+            acc = torch.zeros((ctx.offs[-1], _BWD_C), dtype=torch.float32, device=dev)
+            acc.index_add_(0, ctx.send_rows, recv)
+            sh = ops.sh_layout(dc=dc, rest=rest)
+            M = rest.shape[1]
+            g_xyz, g_s, g_q, g_o, g_dc, g_rest = grads
+        finally:
+            # every exit orders this stream after the fill before the grads are used or freed
+            _zero_fill_wait()
         for k in range(n_cams):
             m2, r, vlist, vcount = ctx.pre[k]
             a = acc[ctx.offs[k]:ctx.offs[k + 1]]

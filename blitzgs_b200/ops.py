@@ -232,9 +232,11 @@ def preprocess_forward_raw(xyz, scaling_raw, rotation_raw, opacity_raw, sh, rast
         conic = torch.empty((P, 4), dtype=torch.float32, device=dev)
         rgb = torch.empty((P, 3), dtype=torch.float32, device=dev)
         vlist = torch.empty((max(P, 1),), dtype=torch.int32, device=dev) if want_list else None
-    reg = torch.zeros((2,), dtype=torch.float64, device=dev) if want_reg else None
-    vcount = (vis_count if vis_count is not None else torch.zeros((1,), dtype=torch.int32, device=dev)) \
-        if want_list else None
+    # the regulariser sums and the list counter start at zero: one fill for both
+    zeros = torch.zeros((3,), dtype=torch.int64, device=dev) if (want_reg or (want_list and vis_count is None)) \
+        else None
+    reg = zeros[:2].view(torch.float64) if want_reg else None
+    vcount = (vis_count if vis_count is not None else zeros[2:].view(torch.int32)[:1]) if want_list else None
     xo = None
     if exchange is not None:
         lo, hi, xrec, xmask, xcnt = exchange
@@ -366,11 +368,9 @@ def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_local
         _lib.call("blitz_render_count", P, H, W, ptr(means2D), ptr(radii), ptr(cl), ptr(counts), ptr(totals), st)
         TIMER.end(tok, P=P)
     host = _pinned(dev, 2, torch.int64)
-    host.copy_(totals, non_blocking=True)
-    if vis_count is not None:
-        host_n = _pinned(dev, 1, torch.int32)
-        host_n.copy_(vis_count, non_blocking=True)
-    torch.cuda.current_stream().synchronize()
+    host_n = _pinned(dev, 1, torch.int32) if vis_count is not None else None
+    _lib.call("blitz_read_totals", ptr(totals), ptr(vis_count), host.data_ptr(),
+              host_n.data_ptr() if host_n is not None else None, st)
     R, n_vis = int(host[0]), int(host[1])
     n_list = int(host_n[0]) if vis_count is not None else None
 
@@ -465,6 +465,41 @@ def loss_backward(img, gt, partials, scale):
               ptr(_f32c(scale)), ptr(out), _lib.stream_ptr())
     TIMER.end(tok, pixels=C * Hb * W)
     return out
+
+
+def loss_combine(sums, reg, lambda_dssim, n3, reg_weight):
+    """The per-camera loss on the device: float32 [5] {loss, L1, SSIM, reg,
+    cnt} with loss = (1-l) L1/N3 + l (1 - SSIM/N3) + w reg / max(cnt, 1)
+    (reg = None: no regulariser)."""
+    out = torch.empty((5,), dtype=torch.float32, device=sums.device)
+    _lib.call("blitz_loss_combine", ptr(sums), ptr(reg), 1.0 - lambda_dssim, lambda_dssim, float(n3),
+              float(reg_weight), ptr(out), _lib.stream_ptr())
+    return out
+
+
+def loss_combine_backward(g_loss, g_l1, g_ss, fwd_out, lambda_dssim, n3, reg_weight):
+    """float32 [3] {dLoss/d(sum L1), dLoss/d(sum SSIM), dLoss/d reg} from the
+    upstream gradients of loss, L1 and SSIM (None = 0)."""
+    scales = torch.empty((3,), dtype=torch.float32, device=fwd_out.device)
+    g = [None if t is None else _f32c(t) for t in (g_loss, g_l1, g_ss)]
+    _lib.call("blitz_loss_combine_backward", ptr(g[0]), ptr(g[1]), ptr(g[2]), ptr(fwd_out), 1.0 - lambda_dssim,
+              lambda_dssim, float(n3), float(reg_weight), ptr(scales), _lib.stream_ptr())
+    return scales
+
+
+def zero_fill_async(tensors):
+    """Zero ``tensors`` on the library's side stream after the work already
+    queued on the current stream; ``zero_fill_wait()`` orders the current
+    stream after the fill.  The tensors must not be touched (or freed) by
+    the current stream before that wait."""
+    n = len(tensors)
+    ptrs = (ctypes.c_void_p * n)(*[t.data_ptr() for t in tensors])
+    sizes = (ctypes.c_size_t * n)(*[t.numel() * t.element_size() for t in tensors])
+    _lib.call("blitz_zero_fill_async", n, ptrs, sizes, _lib.stream_ptr())
+
+
+def zero_fill_wait():
+    _lib.call("blitz_zero_fill_wait", _lib.stream_ptr())
 
 
 def fp32_peak_tflops(seconds=0.3):

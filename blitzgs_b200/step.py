@@ -12,7 +12,10 @@ results identical:
     per-Gaussian intermediate is materialised for autograd and the render
     gradient record [P,16] feeds the preprocess backward directly;
   * the only host synchronisation is the two-number readback that sizes the
-    binning buffers.
+    binning buffers;
+  * the loss is combined from the L1/SSIM sums and the regulariser on the
+    device, with the float32 rounding of the same PyTorch expression, so no
+    scalar PyTorch op (or its autograd node) runs per camera.
 Parameter activations (exp, sigmoid, normalize) run inside the preprocess
 kernels with PyTorch's float arithmetic, and their backward is chained there
 too, so no activation or regulariser kernel runs in PyTorch.
@@ -26,11 +29,13 @@ LAMBDA_DSSIM = 0.2
 
 class _ViewLoss(torch.autograd.Function):
     """Raw parameters (xyz, _scaling, _rotation, _opacity, _features_dc,
-    _features_rest) -> (sum L1, sum SSIM, sum of min-axis scales, count) for
-    one camera band; activations are applied inside the kernels."""
+    _features_rest) -> (loss, sum L1, sum SSIM) of one camera band;
+    activations, loss combination and their backward run in the kernels, so
+    the whole camera is one autograd node."""
 
     @staticmethod
-    def forward(ctx, xyz, s_raw, q_raw, o_raw, dc, rest, raster, gt, compute_locally, band, exact_norm, sparse_grad):
+    def forward(ctx, xyz, s_raw, q_raw, o_raw, dc, rest, raster, gt, compute_locally, band, exact_norm, sparse_grad,
+                lambda_dssim, reg_weight):
         H, W = int(raster.image_height), int(raster.image_width)
         sh = ops.sh_layout(dc=dc, rest=rest)
         rot_norm = q_raw.norm(dim=1) if exact_norm else None
@@ -44,48 +49,51 @@ class _ViewLoss(torch.autograd.Function):
         y0, y1 = band
         img_band = color[:, y0:y1, :]
         sums, partials = ops.loss_forward(img_band, gt)
+        consts = (lambda_dssim, H * W * 3, reg_weight)
+        out = ops.loss_combine(sums, reg if reg_weight else None, *consts)
         ctx.raster = raster
         ctx.band = band
         ctx.HW = (H, W)
         ctx.state = state
         ctx.cl = compute_locally
         ctx.sparse_grad = sparse_grad
+        ctx.consts = consts
         ctx.save_for_backward(xyz, s_raw, q_raw, o_raw, dc, rest, means2D, conic, rgb, radii, gt, partials,
-                              img_band, rot_norm, vlist, vcount, slot_of)
+                              img_band, rot_norm, vlist, vcount, slot_of, out)
         ctx.mark_non_differentiable(radii, out_observe, color)
-        l1 = sums[0].to(torch.float32)
-        ss = sums[1].to(torch.float32)
-        return l1, ss, reg[0].to(torch.float32), reg[1].to(torch.float32), radii, out_observe, color
+        return out[0], out[1], out[2], radii, out_observe, color
 
     @staticmethod
-    def backward(ctx, g_l1, g_ss, g_reg, _g_cnt, *_unused):
+    def backward(ctx, g_loss, g_l1, g_ss, *_unused):
         (xyz, s_raw, q_raw, o_raw, dc, rest, means2D, conic, rgb, radii, gt, partials, img_band, rot_norm, vlist,
-         vcount, slot_of) = ctx.saved_tensors
+         vcount, slot_of, out) = ctx.saved_tensors
         H, W = ctx.HW
         y0, y1 = ctx.band
         dev = xyz.device
-        zero = torch.zeros((), device=dev)
-        scale = torch.stack([g_l1 if g_l1 is not None else zero, g_ss if g_ss is not None else zero]).float()
-        g_band = ops.loss_backward(img_band, gt, partials, scale)
+        scales = ops.loss_combine_backward(g_loss, g_l1, g_ss, out, *ctx.consts)
+        g_band = ops.loss_backward(img_band, gt, partials, scales[0:2])
         if y0 == 0 and y1 == H:
             dL_dpix = g_band
         else:
             dL_dpix = torch.zeros((3, H, W), dtype=torch.float32, device=dev)
             dL_dpix[:, y0:y1, :] = g_band
         L = ctx.state.n_list
-        dense_fill = None
+        grads_dense = None
         if not ctx.sparse_grad and vlist is not None:
             # The dense gradients are zero except at listed rows.  Their fill is
             # pure HBM writes (236 B per Gaussian); on a side stream it runs
             # beside the issue-bound loss and render backward instead of after them.
             grads_dense = [torch.empty_like(t) for t in (xyz, s_raw, q_raw, o_raw, dc, rest)]
-            dense_fill = _zero_fill_async(grads_dense)
-        # gradient record: one row per listed Gaussian (slot_of) instead of P rows
-        rec = ops.render_backward(ctx.state, means2D, conic, rgb, ctx.raster.bg, ctx.cl, dL_dpix,
-                                  record_rows=slot_of, n_rows=L)
+            _zero_fill_async(grads_dense)
+        try:
+            # gradient record: one row per listed Gaussian (slot_of) instead of P rows
+            rec = ops.render_backward(ctx.state, means2D, conic, rgb, ctx.raster.bg, ctx.cl, dL_dpix,
+                                      record_rows=slot_of, n_rows=L)
+        finally:
+            if grads_dense is not None:
+                _zero_fill_wait()
         sh = ops.sh_layout(dc=dc, rest=rest)
         M = rest.shape[1]
-        reg_scale = (g_reg if g_reg is not None else zero).float().reshape(1)
         rows = ops.ROWS_UPSTREAM_BY_SLOT if slot_of is not None else 0
         if ctx.sparse_grad:
             # row j = the j-th listed Gaussian: every row written, no P-sized buffer
@@ -94,46 +102,35 @@ class _ViewLoss(torch.autograd.Function):
             shapes = [xyz.shape[1:], s_raw.shape[1:], q_raw.shape[1:], o_raw.shape[1:], dc.shape[1:], rest.shape[1:]]
             g_xyz, g_s, g_q, g_o, g_dc, g_rest = [torch.empty((n,) + tuple(sz), dtype=torch.float32, device=dev)
                                                   for sz in shapes]
-        elif dense_fill is not None:
+        elif grads_dense is not None:
             g_xyz, g_s, g_q, g_o, g_dc, g_rest = grads_dense
-            torch.cuda.current_stream(dev).wait_event(dense_fill)
         else:
             g_xyz, g_s, g_q, g_dc, g_rest = (torch.empty_like(t) for t in (xyz, s_raw, q_raw, dc, rest))
             g_o = torch.empty_like(o_raw)
         ops.preprocess_backward_raw(radii, means2D, xyz, s_raw, q_raw, o_raw.reshape(-1), sh, ctx.raster,
                                     rec[:, 0:2], rec[:, 8:12], rec[:, 12:15],
                                     (g_xyz, g_s, g_q, g_o, (g_dc, 3), (g_rest, max(M, 1) * 3)), rot_norm=rot_norm,
-                                    reg_scale=reg_scale, vis_list=vlist, vis_count=vcount, rows=rows)
+                                    reg_scale=scales[2:3], vis_list=vlist, vis_count=vcount, rows=rows)
         grads = [g_xyz, g_s, g_q, g_o, g_dc, g_rest]
         if ctx.sparse_grad:
             idx = vlist[:L].to(torch.int64).unsqueeze(0)
             grads = [torch.sparse_coo_tensor(idx, g[:L], p.shape, check_invariants=False)
                      for g, p in zip(grads, (xyz, s_raw, q_raw, o_raw, dc, rest))]
-        return (*grads, None, None, None, None, None, None)
-
-
-_SIDE = {}
+        return (*grads, None, None, None, None, None, None, None, None)
 
 
 def _zero_fill_async(tensors):
-    """Zero ``tensors`` on a side stream (after the current stream's pending
-    work, which may still use their recycled memory); returns the event that
-    marks the end of the fill.  The caller makes its stream wait on that
-    event before it touches the tensors, so every later use and free is
-    ordered after the fill on the tensors' own stream (no record_stream:
-    that would hold the memory back from the allocator's reuse)."""
-    dev = tensors[0].device
-    main = torch.cuda.current_stream(dev)
-    side = _SIDE.get(dev.index)
-    if side is None:
-        side = _SIDE[dev.index] = torch.cuda.Stream(device=dev)
-    side.wait_stream(main)
-    with torch.cuda.stream(side):
-        for t in tensors:
-            t.zero_()
-        done = torch.cuda.Event()
-        done.record(side)
-    return done
+    """Zero ``tensors`` on the library's side stream, after the current
+    stream's pending work (which may still use their recycled memory).  The
+    caller runs ``_zero_fill_wait()`` before the current stream touches them,
+    so every later use and free is ordered after the fill on the tensors' own
+    stream (no record_stream: that would hold the memory back from the
+    allocator's reuse)."""
+    ops.zero_fill_async(tensors)
+
+
+def _zero_fill_wait():
+    ops.zero_fill_wait()
 
 
 def view_loss(model, raster, gt_band, compute_locally=None, band=None, lambda_dssim=LAMBDA_DSSIM,
@@ -153,13 +150,7 @@ def view_loss(model, raster, gt_band, compute_locally=None, band=None, lambda_ds
     reference's SparseGaussianAdam, which only touches visible rows.
     Returns (loss, l1_sum, ssim_sum, radii, out_observe, color)."""
     xyz, s_raw, q_raw, o_raw, dc, rest = model
-    H, W = int(raster.image_height), int(raster.image_width)
+    H = int(raster.image_height)
     band = band or (0, H)
-    l1, ss, reg, cnt, radii, out_observe, color = _ViewLoss.apply(xyz, s_raw, q_raw, o_raw, dc, rest, raster,
-                                                                   gt_band, compute_locally, band, exact_norm,
-                                                                   sparse_grad)
-    n3 = H * W * 3
-    loss = (1.0 - lambda_dssim) * (l1 / n3) + lambda_dssim * (1.0 - ss / n3)
-    if scale_reg_weight:
-        loss = loss + scale_reg_weight * reg / cnt.clamp(min=1.0)
-    return loss, l1, ss, radii, out_observe, color
+    return _ViewLoss.apply(xyz, s_raw, q_raw, o_raw, dc, rest, raster, gt_band, compute_locally, band, exact_norm,
+                           sparse_grad, float(lambda_dssim), float(scale_reg_weight))

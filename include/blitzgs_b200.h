@@ -313,6 +313,52 @@ int blitz_loss_backward(int C, int Hb, int W, const float* img, const uint8_t* g
                         const float* scale, float* dL_dimg, void* stream);
 
 /*
+ * Per-camera loss of the training step, on the device (no counterpart in
+ * the reference, which forms it with PyTorch scalar ops in
+ * gaussian_renderer/loss_distribution.py:307-322):
+ *   loss = (1 - l) * (L1 / N3) + l * (1 - SSIM / N3) + w * reg / max(cnt, 1)
+ * sums: device double[2] from blitz_loss_forward; reg: device double[2]
+ * {sum of min-axis scales, count} from blitz_preprocess_forward_raw, or NULL
+ * for no regulariser.  Rounded step by step in float32 as PyTorch's CUDA
+ * kernels evaluate that expression on 0-dim float32 tensors (division by
+ * the number N3 as multiplication by its float32 reciprocal).
+ * out: device float[5] {loss, L1, SSIM, reg, cnt}.
+ */
+int blitz_loss_combine(const double* sums, const double* reg, float one_minus_lambda, float lambda, float n3,
+                       float reg_weight, float* out, void* stream);
+
+/*
+ * Backward of blitz_loss_combine: from the upstream gradients of loss, L1
+ * and SSIM (device floats; NULL counts as 0) and the forward's out, writes
+ * scales = device float[3] {dLoss/d(sum L1), dLoss/d(sum SSIM), dLoss/d reg}
+ * as PyTorch's autograd forms them; scales[0..1] is blitz_loss_backward's
+ * scale, scales[2] the reg_scale of blitz_preprocess_backward_raw.
+ */
+int blitz_loss_combine_backward(const float* g_loss, const float* g_l1, const float* g_ss, const float* fwd_out,
+                                float one_minus_lambda, float lambda, float n3, float reg_weight, float* scales,
+                                void* stream);
+
+/*
+ * Binning totals to the host (no counterpart in the reference, whose
+ * renderForward reads num_rendered back with a blocking cudaMemcpy,
+ * r/cuda_rasterizer/rasterizer_impl.cu:621): copies totals (device int64[2]
+ * {R, V}) and, when both are non-NULL, vis_count (device int32) to the host
+ * and waits for the stream.  host_totals / host_vis should be pinned.
+ */
+int blitz_read_totals(const int64_t* totals, const int32_t* vis_count, int64_t* host_totals, int32_t* host_vis,
+                      void* stream);
+
+/*
+ * Zero n device buffers on a side stream, after the work already queued on
+ * `stream` (no counterpart in the reference).  The library keeps one side
+ * stream and two events per device.  blitz_zero_fill_wait(stream) makes
+ * `stream` wait for the last fill issued on this device; call it before
+ * `stream` touches the buffers.  Not re-entrant across host threads.
+ */
+int blitz_zero_fill_async(int n, void* const* ptrs, const size_t* bytes, void* stream);
+int blitz_zero_fill_wait(void* stream);
+
+/*
  * Routing mask bool [P, mp_world_size] against per-rank tile rectangles:
  * rectangles int32 [mp_world_size, 4] = {tile row begin, row end, column
  * begin, column end} (widened by one tile with avoid_pixel_all2all; the

@@ -162,6 +162,34 @@ def test_fused_regulariser_matches_oracle(cuda_device):
         assert_grad_close(p.grad.cpu(), r, 2e-3, n)
 
 
+@pytest.mark.parametrize("with_reg", [False, True])
+def test_device_loss_combination_bit_identical_to_torch(cuda_device, with_reg):
+    """blitz_loss_combine and its backward against the same expression on
+    0-dim float32 tensors and PyTorch's autograd of it, bit for bit, over
+    seeded sums (the step used to form the loss that way)."""
+    gen = torch.Generator().manual_seed(12)
+    lam, w, n3 = 0.2, 10.0, 864 * 1152 * 3
+    for _ in range(50):
+        sums = (torch.rand(2, generator=gen, dtype=torch.float64) * torch.tensor([n3 * 0.3, n3])).to(cuda_device)
+        reg = torch.tensor([float(torch.rand(1, generator=gen)) * 5e3, float(torch.randint(0, 9, (1,), generator=gen))],
+                           dtype=torch.float64, device=cuda_device)
+        g_up = [torch.randn((), generator=gen).to(cuda_device) for _ in range(3)]
+        out = ops.loss_combine(sums, reg if with_reg else None, lam, n3, w)
+        scales = ops.loss_combine_backward(g_up[0], g_up[1], g_up[2], out, lam, n3, w if with_reg else 0.0)
+        l1 = sums[0].to(torch.float32).requires_grad_(True)
+        ss = sums[1].to(torch.float32).requires_grad_(True)
+        r = reg[0].to(torch.float32).requires_grad_(True)
+        cnt = reg[1].to(torch.float32)
+        loss = (1.0 - lam) * (l1 / n3) + lam * (1.0 - ss / n3)
+        if with_reg:
+            loss = loss + w * r / cnt.clamp(min=1.0)
+        assert torch.equal(out[0], loss.detach()) and torch.equal(out[1], l1.detach()) and torch.equal(out[2], ss.detach())
+        torch.autograd.backward([loss, l1, ss], [g_up[0], g_up[1], g_up[2]])
+        assert torch.equal(scales[0], l1.grad) and torch.equal(scales[1], ss.grad)
+        if with_reg:
+            assert torch.equal(scales[2], r.grad)
+
+
 def test_raw_preprocess_bit_identical_to_torch_activations(cuda_device):
     """Activations fused into the kernel (exp, sigmoid, division by PyTorch's
     rotation norm) give the same bits as the operator API fed with PyTorch's
