@@ -326,11 +326,13 @@ _PINNED = {}
 
 
 def _pinned(dev, n, dtype):
+    """Reused pinned host buffer and a numpy view of it (reading a number
+    through numpy costs far less than indexing the tensor)."""
     key = (dev.index, n, dtype)
     t = _PINNED.get(key)
     if t is None:
-        t = torch.empty(n, dtype=dtype, pin_memory=True)
-        _PINNED[key] = t
+        buf = torch.empty(n, dtype=dtype, pin_memory=True)
+        t = _PINNED[key] = (buf, buf.numpy())
     return t
 
 
@@ -367,14 +369,9 @@ def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_local
         tok = TIMER.begin("bin_count")
         _lib.call("blitz_render_count", P, H, W, ptr(means2D), ptr(radii), ptr(cl), ptr(counts), ptr(totals), st)
         TIMER.end(tok, P=P)
-    host = _pinned(dev, 2, torch.int64)
-    host_n = _pinned(dev, 1, torch.int32) if vis_count is not None else None
-    _lib.call("blitz_read_totals", ptr(totals), ptr(vis_count), host.data_ptr(),
-              host_n.data_ptr() if host_n is not None else None, st)
-    R, n_vis = int(host[0]), int(host[1])
-    n_list = int(host_n[0]) if vis_count is not None else None
-
-    point_list = torch.empty((max(R, 1),), dtype=torch.int32, device=dev)
+    # Everything whose size does not depend on the totals is allocated (and
+    # out_observe zeroed) before the readback: the GPU idles from the end of
+    # the preprocess until the binning is issued, so that window is kept short.
     ranges = torch.empty((T, 2), dtype=torch.int32, device=dev)
     final_T = torch.empty((H * W,), dtype=torch.float32, device=dev)
     n_contrib = torch.empty((H * W,), dtype=torch.int32, device=dev)
@@ -383,6 +380,14 @@ def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_local
     n_consider = torch.empty((T,), dtype=torch.int32, device=dev)
     n_contrib_tile = torch.empty((T,), dtype=torch.int32, device=dev)
     out_observe = torch.zeros((P,), dtype=torch.int32, device=dev)
+    host, host_np = _pinned(dev, 2, torch.int64)
+    host_n, host_n_np = _pinned(dev, 1, torch.int32) if vis_count is not None else (None, None)
+    _lib.call("blitz_read_totals", ptr(totals), ptr(vis_count), host.data_ptr(),
+              host_n.data_ptr() if host_n is not None else None, st)
+    R, n_vis = int(host_np[0]), int(host_np[1])
+    n_list = int(host_n_np[0]) if vis_count is not None else None
+
+    point_list = torch.empty((max(R, 1),), dtype=torch.int32, device=dev)
     nbytes = _lib.load().blitz_render_scratch_bytes(P, n_vis, R, H, W)
     scratch = SCRATCH.get(dev, nbytes)
     tok = TIMER.begin("binning")
