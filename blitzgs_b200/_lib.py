@@ -43,10 +43,10 @@ SIGNATURES = {
         _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "blitz_render_bin": (_i32, [_i64, _i64, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp]),
     "blitz_render_blend": (_i32, [_i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
-                                  _vp, _vp]),
+                                  _vp, _vp, _vp, _vp, _vp]),
     "blitz_render_bin_noalloc": (_i32, [_i64, _i64, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "blitz_render_backward": (_i32, [
-        _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+        _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "blitz_loss_forward": (_i32, [_i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "blitz_loss_backward": (_i32, [_i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "blitz_get_local2j_ids_bool": (_i32, [_i32, _i32, _i32, _i32, _i64, _vp, _vp, _vp, _i32, _vp, _vp]),

@@ -20,6 +20,11 @@
 //     block barrier for the tile's slowest warp;
 //   * the forward stops a warp as soon as its 32 pixels are saturated;
 //     the backward starts each warp at its own largest n_contrib;
+//   * the forward can record, per strip, the Gaussians that contributed to
+//     at least one of its pixels (ids and list positions, in list order);
+//     the backward then replays only those -- the same pairs in the same
+//     order -- instead of walking and box-testing the whole tile list (22%
+//     off the backward for 3% on the forward);
 //   * the list walk is software-pipelined: list entries are loaded two
 //     batches ahead and the Gaussians' position and conic one batch ahead,
 //     so the dependent L2 loads of a batch overlap the previous batch's
@@ -164,6 +169,7 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
       p.n_consider[tile] = 0;
       p.n_contrib_tile[tile] = 0;
     }
+    if (p.strip_counts && threadIdx.x < kStrips) p.strip_counts[(int64_t)tile * kStrips + threadIdx.x] = 0;
     return;
   }
 
@@ -176,6 +182,7 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
   __shared__ float4 s_c[kWarps][32];
   __shared__ int s_id[kWarps][32];
   __shared__ int s_obs[kWarps][32];
+  __shared__ int s_act[kWarps][32];  // did any pixel of the strip take this Gaussian?
   __shared__ int s_red[32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float2 so = strip_origin(tx, ty, warp);
@@ -183,6 +190,15 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
   const uint2 range = p.ranges[tile];
   const int n = (int)(range.y - range.x);
   const float2 pixf = make_float2((float)px, (float)py);
+
+  int* strip_ids = nullptr;
+  int* strip_pos = nullptr;
+  int n_act = 0;
+  if (p.strip_ids) {
+    const int64_t off = (int64_t)kStrips * range.x + (int64_t)warp * n;
+    strip_ids = p.strip_ids + off;
+    strip_pos = p.strip_pos + off;
+  }
 
   bool done = !inside;
   float T = 1.0f;
@@ -224,6 +240,7 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
       s_c[warp][slot] = make_float4(p.rgb[3 * (int64_t)id + 0], p.rgb[3 * (int64_t)id + 1],
                                     p.rgb[3 * (int64_t)id + 2], 0.f);
       s_obs[warp][slot] = 0;
+      s_act[warp][slot] = 0;
     }
     __syncwarp();
     const int kept = __popc(km);
@@ -243,6 +260,7 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
         continue;
       }
       ++n2l;
+      s_act[warp][j] = 1;
       const float4 cth = s_c[warp][j];
       C0 += cth.x * alpha * T;
       C1 += cth.y * alpha * T;
@@ -253,8 +271,20 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
     }
     __syncwarp();
     if (lane < kept && s_obs[warp][lane] > 0) atomicAdd(&p.out_observe[s_id[warp][lane]], s_obs[warp][lane]);
+    if (strip_ids) {
+      // append this batch's contributing Gaussians to the strip's list, in order
+      const bool a = lane < kept && s_act[warp][lane] != 0;
+      const unsigned am = __ballot_sync(0xffffffffu, a);
+      if (a) {
+        const int at = n_act + __popc(am & ((1u << lane) - 1u));
+        strip_ids[at] = s_id[warp][lane];
+        strip_pos[at] = __float_as_int(s_b[warp][lane].w) - 1;  // 0-based list position
+      }
+      n_act += __popc(am);
+    }
     __syncwarp();
   }
+  if (strip_ids && lane == 0) p.strip_counts[(int64_t)tile * kStrips + warp] = n_act;
 
   if (inside) {
     p.final_T[pix] = T;
@@ -326,6 +356,13 @@ __device__ __forceinline__ float warp_transpose_reduce16(float v[16]) {
 // Gaussian's alpha >= 1/255 box against the strip's pixels, and the
 // survivors are compacted into the warp's shared-memory batch.  No block
 // barrier: warps of a tile never wait for one another.
+//
+// With LISTS (the forward recorded, per strip, the Gaussians that contributed
+// to at least one of its pixels: strip_ids / strip_pos, strip_counts) the
+// warp walks only that list, back to front: the same (pixel, Gaussian) pairs
+// in the same order, without the box tests and without the iterations in
+// which no pixel of the strip contributes.
+template <bool LISTS>
 __global__ void __launch_bounds__(32, 28) blend_bwd_kernel(BlendBwdParams p) {
   const int tile = blockIdx.x / kStrips;
   const int strip = blockIdx.x - tile * kStrips;
@@ -368,32 +405,56 @@ __global__ void __launch_bounds__(32, 28) blend_bwd_kernel(BlendBwdParams p) {
   float last_alpha = 0.f;
   float last_color[3] = {0.f, 0.f, 0.f};
 
-  // software pipeline: list ids two batches ahead, Gaussian data one batch ahead
-  int id_n = 0, id_nn = 0;
+  // software pipeline: list entries two batches ahead, Gaussian data one
+  // batch ahead.  Walk mode: entries of the tile list from the strip's
+  // largest n_contrib down; list mode: entries of the strip's recorded list.
+  const int n_tile = (int)(range.y - range.x);
+  const int* lst_id = nullptr;
+  const int* lst_pos = nullptr;
+  int n_walk = n_eff;
+  if constexpr (LISTS) {
+    const int64_t off = (int64_t)kStrips * range.x + (int64_t)strip * n_tile;
+    lst_id = p.strip_ids + off;
+    lst_pos = p.strip_pos + off;
+    n_walk = p.strip_counts[(int64_t)tile * kStrips + strip];
+  }
+  auto entry = [&](int e, int& id, int& pos) {  // e-th entry of the walk, back to front
+    if constexpr (LISTS) {
+      id = __ldg(lst_id + e);
+      pos = __ldg(lst_pos + e);
+    } else {
+      id = (int)p.point_list[range.x + e];
+      pos = e;
+    }
+  };
+  int id_n = 0, id_nn = 0, pos_n = 0, pos_nn = 0;
   float2 xy_n = make_float2(0.f, 0.f);
   float4 co_n = make_float4(0.f, 0.f, 0.f, 0.f);
   {
-    const int k0 = n_eff - 1 - lane, k1 = k0 - 32;
-    if (k0 >= 0) id_n = (int)p.point_list[range.x + k0];
-    if (k1 >= 0) id_nn = (int)p.point_list[range.x + k1];
-    if (k0 >= 0) {
+    const int e0 = n_walk - 1 - lane, e1 = e0 - 32;
+    if (e0 >= 0) entry(e0, id_n, pos_n);
+    if (e1 >= 0) entry(e1, id_nn, pos_nn);
+    if (e0 >= 0) {
       xy_n = reinterpret_cast<const float2*>(p.means2D)[id_n];
       co_n = reinterpret_cast<const float4*>(p.conic_opacity)[id_n];
     }
   }
-  for (int base = 0; base < n_eff; base += 32) {
-    const int k = n_eff - 1 - (base + lane);  // list position, back to front
-    const int id = id_n;
+  for (int base = 0; base < n_walk; base += 32) {
+    const int e = n_walk - 1 - (base + lane);  // walk entry, back to front
+    const int id = id_n, k = pos_n;            // k: list position
     const float2 xy = xy_n;
     const float4 co = co_n;
     id_n = id_nn;
-    if (k - 32 >= 0) {
+    pos_n = pos_nn;
+    if (e - 32 >= 0) {
       xy_n = reinterpret_cast<const float2*>(p.means2D)[id_n];
       co_n = reinterpret_cast<const float4*>(p.conic_opacity)[id_n];
     }
-    if (k - 64 >= 0) id_nn = (int)p.point_list[range.x + k - 64];
-    const bool keep =
-        k >= 0 && !box_misses(alpha_box(xy, co), so.x, so.x + (float)(kStripW - 1), so.y, so.y + (float)(kStripH - 1));
+    if (e - 64 >= 0) entry(e - 64, id_nn, pos_nn);
+    bool keep = e >= 0;
+    if constexpr (!LISTS)
+      keep = keep && !box_misses(alpha_box(xy, co), so.x, so.x + (float)(kStripW - 1), so.y,
+                                 so.y + (float)(kStripH - 1));
     const unsigned km = __ballot_sync(0xffffffffu, keep);
     if (!km) continue;
     __syncwarp();  // the previous batch is no longer read
@@ -506,7 +567,10 @@ int launch_blend_fwd(const BlendFwdParams& p, cudaStream_t st) {
 int launch_blend_bwd(const BlendBwdParams& p, cudaStream_t st) {
   const int n_tiles = p.grid_x * p.grid_y;
   if (n_tiles <= 0) return 0;
-  blend_bwd_kernel<<<n_tiles * kStrips, 32, 0, st>>>(p);
+  if (p.strip_ids)
+    blend_bwd_kernel<true><<<n_tiles * kStrips, 32, 0, st>>>(p);
+  else
+    blend_bwd_kernel<false><<<n_tiles * kStrips, 32, 0, st>>>(p);
   return (int)cudaGetLastError();
 }
 

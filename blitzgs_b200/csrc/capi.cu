@@ -324,7 +324,7 @@ int render_blend_impl(int64_t P, int image_height, int image_width, const float*
                       const float* rgb, const float* bg, const uint8_t* compute_locally, const uint32_t* point_list,
                       const uint32_t* ranges, float* final_T, uint32_t* n_contrib, float* out_color,
                       int32_t* n_render, int32_t* n_consider, int32_t* n_contrib_tile, int32_t* out_observe,
-                      cudaStream_t st) {
+                      int32_t* strip_ids, int32_t* strip_pos, int32_t* strip_counts, cudaStream_t st) {
   BlendFwdParams f{};
   f.W = image_width;
   f.H = image_height;
@@ -345,6 +345,9 @@ int render_blend_impl(int64_t P, int image_height, int image_width, const float*
   f.n_render = n_render;
   f.n_consider = n_consider;
   f.n_contrib_tile = n_contrib_tile;
+  f.strip_ids = strip_ids;
+  f.strip_pos = strip_pos;
+  f.strip_counts = strip_counts;
   return check(launch_blend_fwd(f, st), "render blend");
 }
 
@@ -367,7 +370,7 @@ int blitz_render_forward(int64_t P, int64_t n_vis, int64_t R, int image_height, 
   if (e) return e;
   return blitz_render_blend(P, image_height, image_width, means2D, conic_opacity, rgb, bg, compute_locally,
                             point_list, ranges, final_T, n_contrib, out_color, n_render, n_consider, n_contrib_tile,
-                            out_observe, stream);
+                            out_observe, nullptr, nullptr, nullptr, stream);
 }
 
 int blitz_render_bin(int64_t P, int64_t n_vis, int64_t R, int image_height, int image_width, const float* means2D,
@@ -385,8 +388,10 @@ int blitz_render_blend(int64_t P, int image_height, int image_width, const float
                        const float* rgb, const float* bg, const uint8_t* compute_locally, const uint32_t* point_list,
                        const uint32_t* ranges, float* final_T, uint32_t* n_contrib, float* out_color,
                        int32_t* n_render, int32_t* n_consider, int32_t* n_contrib_tile, int32_t* out_observe,
-                       void* stream) {
+                       int32_t* strip_ids, int32_t* strip_pos, int32_t* strip_counts, void* stream) {
   if (!render_args_ok(P, 0, 0, image_height, image_width)) return fail(BLITZ_EINVAL, "blitz_render_blend: bad sizes");
+  if ((strip_ids == nullptr) != (strip_pos == nullptr) || (strip_ids == nullptr) != (strip_counts == nullptr))
+    return fail(BLITZ_EINVAL, "blitz_render_blend: strip_ids, strip_pos and strip_counts go together");
   if (!bg || !ranges || !final_T || !n_contrib || !out_color || !n_render || !n_consider || !n_contrib_tile ||
       (P > 0 && (!means2D || !conic_opacity || !rgb || !out_observe || !point_list)))
     return fail(BLITZ_EINVAL, "blitz_render_blend: null pointer");
@@ -394,16 +399,19 @@ int blitz_render_blend(int64_t P, int image_height, int image_width, const float
     return fail(BLITZ_EINVAL, "blitz_render_blend: conic_opacity needs 16-byte, means2D 8-byte alignment");
   return render_blend_impl(P, image_height, image_width, means2D, conic_opacity, rgb, bg, compute_locally, point_list,
                            ranges, final_T, n_contrib, out_color, n_render, n_consider, n_contrib_tile, out_observe,
-                           S(stream));
+                           strip_ids, strip_pos, strip_counts, S(stream));
 }
 
 int blitz_render_backward(int64_t P, int image_height, int image_width, const uint32_t* point_list,
                           const uint32_t* ranges, const float* final_T, const uint32_t* n_contrib,
                           const float* means2D, const float* conic_opacity, const float* rgb,
                           const float* bg, const uint8_t* compute_locally, const float* dL_dpix,
-                          const uint32_t* record_rows, float* grad_accum, void* stream) {
+                          const uint32_t* record_rows, const int32_t* strip_ids, const int32_t* strip_pos,
+                          const int32_t* strip_counts, float* grad_accum, void* stream) {
   if (P < 0 || image_height <= 0 || image_width <= 0)
     return fail(BLITZ_EINVAL, "blitz_render_backward: bad sizes");
+  if ((strip_ids == nullptr) != (strip_pos == nullptr) || (strip_ids == nullptr) != (strip_counts == nullptr))
+    return fail(BLITZ_EINVAL, "blitz_render_backward: strip_ids, strip_pos and strip_counts go together");
   if (!ranges || !final_T || !n_contrib || !bg || !dL_dpix ||
       (P > 0 && (!means2D || !conic_opacity || !rgb || !grad_accum)))
     return fail(BLITZ_EINVAL, "blitz_render_backward: null pointer");
@@ -427,6 +435,9 @@ int blitz_render_backward(int64_t P, int image_height, int image_width, const ui
   b.dL_dpix = dL_dpix;
   b.grad_accum = grad_accum;
   b.record_rows = record_rows;
+  b.strip_ids = strip_ids;
+  b.strip_pos = strip_pos;
+  b.strip_counts = strip_counts;
   return check(launch_blend_bwd(b, S(stream)), "blitz_render_backward");
 }
 

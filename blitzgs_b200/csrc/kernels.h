@@ -157,6 +157,13 @@ struct BlendFwdParams {
   int* n_render;               // [tiles]
   int* n_consider;             // [tiles]
   int* n_contrib_tile;         // [tiles]
+  // optional (all or none): per warp strip (8 per tile) the Gaussians that
+  // contributed to any of its pixels, in list order -- Gaussian id and
+  // 0-based list position at [8 * range.x + strip * n_tile + e] -- and their
+  // count at [tile * 8 + strip]; read by the backward
+  int* strip_ids;
+  int* strip_pos;
+  int* strip_counts;
 };
 
 int launch_blend_fwd(const BlendFwdParams& p, cudaStream_t st);
@@ -176,6 +183,9 @@ struct BlendBwdParams {
   const float* dL_dpix;   // [3,H,W]
   float* grad_accum;      // [rows,16], zero on entry; layout in capi docs
   const uint32_t* record_rows;  // optional: record row of Gaussian id (else the id itself)
+  const int* strip_ids;         // optional: the forward's strip lists (see BlendFwdParams)
+  const int* strip_pos;
+  const int* strip_counts;
 };
 
 int launch_blend_bwd(const BlendBwdParams& p, cudaStream_t st);

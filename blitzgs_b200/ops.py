@@ -320,6 +320,9 @@ class RenderState:
     final_T: torch.Tensor     # f32 [H*W]
     n_contrib: torch.Tensor   # int32 [H*W]
     n_list: int = None        # length of the preprocess's visible list, when read back
+    strip_ids: torch.Tensor = None     # int32 [8R]: per warp strip, the Gaussians that contributed
+    strip_pos: torch.Tensor = None     # int32 [8R]: their tile-list positions
+    strip_counts: torch.Tensor = None  # int32 [8T]
 
 
 _PINNED = {}
@@ -347,11 +350,14 @@ def _tile_mask(compute_locally, H, W):
 
 
 def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_locally, H, W, counts=None, totals=None,
-                   vis_count=None):
+                   vis_count=None, strip_lists=True):
     """Binning + blending of one camera.  Returns (color, n_render, n_consider,
     n_contrib_tile, out_observe, state).  ``counts``/``totals`` from
     ``preprocess_forward_raw(want_counts=True)`` skip the count pass;
-    ``vis_count`` is read back with the totals (state.n_list)."""
+    ``vis_count`` is read back with the totals (state.n_list).
+    ``strip_lists`` records, per 8x4-pixel warp strip, the Gaussians that
+    contributed to it (2 x 32 bytes per tile instance of device memory), so
+    the backward replays only those."""
     _require_cuda(means2D, depths, radii, conic_opacity, rgb, bg)
     means2D, depths, conic_opacity, rgb, bg = map(_f32c, (means2D, depths, conic_opacity, rgb, bg))
     radii = radii.contiguous()
@@ -380,6 +386,7 @@ def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_local
     n_consider = torch.empty((T,), dtype=torch.int32, device=dev)
     n_contrib_tile = torch.empty((T,), dtype=torch.int32, device=dev)
     out_observe = torch.zeros((P,), dtype=torch.int32, device=dev)
+    strip_counts = torch.empty((T * 8,), dtype=torch.int32, device=dev) if strip_lists else None
     host, host_np = _pinned(dev, 2, torch.int64)
     host_n, host_n_np = _pinned(dev, 1, torch.int32) if vis_count is not None else (None, None)
     _lib.call("blitz_read_totals", ptr(totals), ptr(vis_count), host.data_ptr(),
@@ -388,6 +395,8 @@ def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_local
     n_list = int(host_n_np[0]) if vis_count is not None else None
 
     point_list = torch.empty((max(R, 1),), dtype=torch.int32, device=dev)
+    strip_ids = torch.empty((8 * max(R, 1),), dtype=torch.int32, device=dev) if strip_lists else None
+    strip_pos = torch.empty((8 * max(R, 1),), dtype=torch.int32, device=dev) if strip_lists else None
     nbytes = _lib.load().blitz_render_scratch_bytes(P, n_vis, R, H, W)
     scratch = SCRATCH.get(dev, nbytes)
     tok = TIMER.begin("binning")
@@ -397,10 +406,11 @@ def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_local
     tok = TIMER.begin("blend_fwd")
     _lib.call("blitz_render_blend", P, H, W, ptr(means2D), ptr(conic_opacity), ptr(rgb), ptr(bg), ptr(cl),
               ptr(point_list), ptr(ranges), ptr(final_T), ptr(n_contrib), ptr(color), ptr(n_render), ptr(n_consider),
-              ptr(n_contrib_tile), ptr(out_observe), st)
+              ptr(n_contrib_tile), ptr(out_observe), ptr(strip_ids), ptr(strip_pos), ptr(strip_counts), st)
     TIMER.end(tok, P=P, R=R, n_vis=n_vis, H=H, W=W,
               lazy=lambda: {"pairs": (n_consider.sum(dtype=torch.int64), n_contrib_tile.sum(dtype=torch.int64))})
-    state = RenderState(H, W, R, n_vis, point_list, ranges, final_T, n_contrib, n_list)
+    state = RenderState(H, W, R, n_vis, point_list, ranges, final_T, n_contrib, n_list, strip_ids, strip_pos,
+                        strip_counts)
     return color, n_render, n_consider, n_contrib_tile, out_observe, state
 
 
@@ -418,7 +428,8 @@ def render_backward(state, means2D, conic_opacity, rgb, bg, compute_locally, dL_
     tok = TIMER.begin("blend_bwd")
     _lib.call("blitz_render_backward", P, state.H, state.W, ptr(state.point_list), ptr(state.ranges),
               ptr(state.final_T), ptr(state.n_contrib), ptr(means2D), ptr(conic_opacity), ptr(rgb), ptr(bg),
-              ptr(cl), ptr(dL_dpix), ptr(record_rows), ptr(grad_accum), _lib.stream_ptr())
+              ptr(cl), ptr(dL_dpix), ptr(record_rows), ptr(state.strip_ids), ptr(state.strip_pos),
+              ptr(state.strip_counts), ptr(grad_accum), _lib.stream_ptr())
     TIMER.end(tok, P=P, R=state.R, lazy=lambda: {"pairs": (state.n_contrib.sum(dtype=torch.int64),)})
     return grad_accum
 

@@ -244,6 +244,12 @@ int blitz_render_forward(int64_t P, int64_t n_vis, int64_t R, int image_height, 
  * The two halves of blitz_render_forward, for callers that schedule or time
  * them separately: binning (point_list, ranges) and blending (everything
  * else).  Same arguments and contracts as blitz_render_forward.
+ * blitz_render_blend may also record, for blitz_render_backward, the
+ * Gaussians that contributed to each warp strip (8 strips of 8x4 pixels per
+ * tile): strip_ids / strip_pos int32 [8*R] (Gaussian id and 0-based tile-list
+ * position, strip s of tile t at [8*ranges[t].begin + s*n_t + e], n_t the
+ * tile's list length) and strip_counts int32 [n_tiles*8].  All three or none
+ * (NULL); no counterpart in the reference.
  */
 int blitz_render_bin(int64_t P, int64_t n_vis, int64_t R, int image_height, int image_width, const float* means2D,
                      const float* depths, const int32_t* radii, const uint8_t* compute_locally, const uint32_t* counts,
@@ -252,7 +258,7 @@ int blitz_render_blend(int64_t P, int image_height, int image_width, const float
                        const float* rgb, const float* bg, const uint8_t* compute_locally, const uint32_t* point_list,
                        const uint32_t* ranges, float* final_T, uint32_t* n_contrib, float* out_color,
                        int32_t* n_render, int32_t* n_consider, int32_t* n_contrib_tile, int32_t* out_observe,
-                       void* stream);
+                       int32_t* strip_ids, int32_t* strip_pos, int32_t* strip_counts, void* stream);
 
 /*
  * Binning for callers that cannot allocate device memory at call time (no
@@ -285,12 +291,16 @@ int blitz_render_bin_noalloc(int64_t P, int64_t n_vis, int64_t R, int image_heig
  * record_rows (may be NULL): row of Gaussian i's record, e.g. the slot_of map
  * of blitz_preprocess_forward_raw, so the record has one row per listed
  * Gaussian instead of P rows; NULL uses row i.
+ * strip_ids / strip_pos / strip_counts (all three or NULL): the strip lists
+ * blitz_render_blend recorded for this render; with them each strip replays
+ * only the Gaussians that contributed to it (same result, less work).
  */
 int blitz_render_backward(int64_t P, int image_height, int image_width, const uint32_t* point_list,
                           const uint32_t* ranges, const float* final_T, const uint32_t* n_contrib,
                           const float* means2D, const float* conic_opacity, const float* rgb,
                           const float* bg, const uint8_t* compute_locally, const float* dL_dpix,
-                          const uint32_t* record_rows, float* grad_accum, void* stream);
+                          const uint32_t* record_rows, const int32_t* strip_ids, const int32_t* strip_pos,
+                          const int32_t* strip_counts, float* grad_accum, void* stream);
 
 /*
  * Fused L1 + SSIM over a band [C,Hb,W] (forward).

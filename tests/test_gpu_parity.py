@@ -364,6 +364,51 @@ def test_band_compute_locally(cuda_device):
     assert frac_close(c, f["color"], IMG_ATOL) > 0.999
 
 
+@pytest.mark.parametrize("banded", [False, True])
+def test_strip_lists_replay_the_same_pairs(cuda_device, banded):
+    """The forward's per-strip contributor lists (strip_lists=True) leave the
+    forward outputs bit-identical, list every Gaussian that contributed to a
+    pixel of the strip exactly once in list order, and give the backward the
+    same gradient record as the full list walk (up to atomic ordering)."""
+    sc = S.mid(seed=3, P=200_000, n_cams=1, H=216, W=296)
+    cam = sc.cameras[0]
+    g, rs = _gpu_preprocess(sc, cam, cuda_device)
+    H, W = cam.image_height, cam.image_width
+    gx, gy = (W + 15) // 16, (H + 15) // 16
+    cl = None
+    if banded:
+        band = torch.zeros((gy, gx), dtype=torch.bool)
+        band[3:9] = True
+        cl = band.to(cuda_device)
+    args = (g["means2D"], g["depths"], g["radii"], g["conic_opacity"], g["rgb"], rs.bg, cl, H, W)
+    out_w = ops.render_forward(*args, strip_lists=False)
+    out_l = ops.render_forward(*args, strip_lists=True)
+    for a, b in zip(out_w[:5], out_l[:5]):
+        assert torch.equal(a, b)
+    st = out_l[5]
+    assert st.strip_ids is not None and out_w[5].strip_ids is None
+    # lists are increasing positions of the tile list, each entry the Gaussian at that position
+    cnt = st.strip_counts.cpu().view(-1, 8)
+    ranges = st.ranges.cpu().numpy().astype(np.int64)
+    ids, pos, pl = st.strip_ids.cpu().numpy(), st.strip_pos.cpu().numpy(), st.point_list.cpu().numpy()
+    tiles = range(gx * gy) if cl is None else np.nonzero(band.view(-1).numpy())[0]
+    checked = 0
+    for t in list(tiles)[:: max(1, len(tiles) // 40)]:
+        lo, hi = ranges[t]
+        for s in range(8):
+            n = int(cnt[t, s])
+            off = 8 * lo + s * (hi - lo)
+            p_ = pos[off:off + n]
+            assert n <= hi - lo and np.all(np.diff(p_) > 0) and np.all(p_ < hi - lo)
+            assert np.array_equal(ids[off:off + n], pl[lo + p_])
+            checked += n
+    assert checked > 0
+    dL = torch.randn(3, H, W, generator=torch.Generator().manual_seed(4)).to(cuda_device)
+    rec_w = ops.render_backward(out_w[5], g["means2D"], g["conic_opacity"], g["rgb"], rs.bg, cl, dL)
+    rec_l = ops.render_backward(st, g["means2D"], g["conic_opacity"], g["rgb"], rs.bg, cl, dL)
+    assert normwise_rel(rec_l.cpu(), rec_w.cpu()) < 1e-5
+
+
 def test_edge_cases(cuda_device):
     dev = cuda_device
     sc = S.tiny(seed=7, P=64, H=40, W=56)
