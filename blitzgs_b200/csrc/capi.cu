@@ -580,6 +580,66 @@ int blitz_exchange_pack(int64_t n_rows, int n_ranks, const float* records, const
   return check(launch_exchange_pack(k, S(stream)), "blitz_exchange_pack");
 }
 
+}  // extern "C"
+
+namespace {
+
+int fill_segments(int n_segments, const int64_t* seg_start, const int64_t* seg_count, Segments& sg, int64_t& n) {
+  if (n_segments < 0 || n_segments > kMaxSegments || (n_segments > 0 && (!seg_start || !seg_count))) return 1;
+  sg.n = n_segments;
+  n = 0;
+  for (int s = 0; s < n_segments; ++s) {
+    if (seg_start[s] < 0 || seg_count[s] < 0) return 1;
+    sg.start[s] = seg_start[s];
+    sg.count[s] = seg_count[s];
+    n += seg_count[s];
+  }
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int blitz_exchange_unpack(int n_segments, const int64_t* seg_start, const int64_t* seg_count, const float* records,
+                          float* conic, float* means2D, float* rgb, float* depths, int32_t* radii, double* reg,
+                          void* stream) {
+  UnpackParams p{};
+  int64_t n = 0;
+  if (fill_segments(n_segments, seg_start, seg_count, p.seg, n))
+    return fail(BLITZ_EINVAL, "blitz_exchange_unpack: bad segments");
+  if (n == 0) return 0;
+  if (!records || !conic || !means2D || !rgb || !depths || !radii)
+    return fail(BLITZ_EINVAL, "blitz_exchange_unpack: null pointer");
+  if (!aligned16(records) || !aligned16(conic) || (reinterpret_cast<uintptr_t>(means2D) & 7u))
+    return fail(BLITZ_EINVAL, "blitz_exchange_unpack: records/conic need 16-byte, means2D 8-byte alignment");
+  p.records = records;
+  p.conic = conic;
+  p.means2D = means2D;
+  p.rgb = rgb;
+  p.depths = depths;
+  p.radii = radii;
+  p.reg = reg;
+  return check(launch_exchange_unpack(p, n, S(stream)), "blitz_exchange_unpack");
+}
+
+int blitz_grad_records_pack(int n_segments, const int64_t* seg_start, const int64_t* seg_count, const float* rec16,
+                            const int32_t* radii, const float* reg_scale, float* send, void* stream) {
+  GradPackParams p{};
+  int64_t n = 0;
+  if (fill_segments(n_segments, seg_start, seg_count, p.seg, n))
+    return fail(BLITZ_EINVAL, "blitz_grad_records_pack: bad segments");
+  if (n == 0) return 0;
+  if (!rec16 || !radii || !send) return fail(BLITZ_EINVAL, "blitz_grad_records_pack: null pointer");
+  if (!aligned16(rec16) || !aligned16(send))
+    return fail(BLITZ_EINVAL, "blitz_grad_records_pack: rec16 and send need 16-byte alignment");
+  p.rec16 = rec16;
+  p.radii = radii;
+  p.reg_scale = reg_scale;
+  p.send = send;
+  return check(launch_grad_records_pack(p, n, S(stream)), "blitz_grad_records_pack");
+}
+
 int blitz_loss_combine(const double* sums, const double* reg, float one_minus_lambda, float lambda, float n3,
                        float reg_weight, float* out, void* stream) {
   if (!sums || !out || !(n3 > 0.f)) return fail(BLITZ_EINVAL, "blitz_loss_combine: bad arguments");

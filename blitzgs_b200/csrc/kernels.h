@@ -271,6 +271,37 @@ struct PackParams {
 };
 int launch_exchange_pack(const PackParams& p, cudaStream_t st);
 
+// Received exchange records of one camera: up to kMaxSegments runs of rows
+// [seg_start[s], seg_start[s] + seg_count[s]) of a [*,12] buffer, taken in
+// order as rows 0..n-1 of the camera.
+constexpr int kMaxSegments = 32;
+struct Segments {
+  int n;
+  int64_t start[kMaxSegments];
+  int64_t count[kMaxSegments];
+};
+
+struct UnpackParams {
+  Segments seg;
+  const float* records;  // [*,12]
+  float* conic;          // [n,4]
+  float* means2D;        // [n,2]
+  float* rgb;            // [n,3]
+  float* depths;         // [n]
+  int* radii;            // [n]
+  double* reg;           // [2] += {sum of min-axis scales of rows with radius > 0, their count}, or null
+};
+int launch_exchange_unpack(const UnpackParams& p, int64_t n, cudaStream_t st);
+
+struct GradPackParams {
+  Segments seg;          // destination runs in send, in the order of the camera's rows
+  const float* rec16;    // [n,16] render-backward record
+  const int* radii;      // [n]
+  const float* reg_scale;  // device float: dLoss/d(sum of min-axis scales), or null
+  float* send;           // [*,12]
+};
+int launch_grad_records_pack(const GradPackParams& p, int64_t n, cudaStream_t st);
+
 int launch_fma_probe(int blocks, int64_t iters, float* sink, cudaStream_t st);
 
 // Records the message blitz_last_error() returns on this thread (capi.cu).

@@ -106,6 +106,99 @@ int launch_route_bool_rect(const RouteParams& p, const int* rectangles, cudaStre
   return (int)cudaGetLastError();
 }
 
+namespace {
+
+// Segment s and offset inside it of camera row r (segments are few: a
+// linear scan over the run lengths).
+__device__ __forceinline__ int64_t segment_row(const Segments& sg, int64_t r) {
+  for (int s = 0; s < sg.n; ++s) {
+    if (r < sg.count[s]) return sg.start[s] + r;
+    r -= sg.count[s];
+  }
+  return -1;
+}
+
+// Received record [c00 c01 c11 op | x y | r g b | depth radius-bits minscale]
+// -> the render's arrays; the min-scale regulariser's sum and count over the
+// rows with radius > 0 are reduced per block and added in double.
+__global__ void __launch_bounds__(256) exchange_unpack_kernel(UnpackParams p, int64_t n) {
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  double ms = 0.0, cnt = 0.0;
+  if (r < n) {
+    const int64_t src = segment_row(p.seg, r);
+    if (src >= 0) {
+      const float4* v = reinterpret_cast<const float4*>(p.records + 12 * src);
+      const float4 a = v[0], b = v[1], c = v[2];
+      reinterpret_cast<float4*>(p.conic)[r] = a;
+      reinterpret_cast<float2*>(p.means2D)[r] = make_float2(b.x, b.y);
+      p.rgb[3 * r + 0] = b.z;
+      p.rgb[3 * r + 1] = b.w;
+      p.rgb[3 * r + 2] = c.x;
+      p.depths[r] = c.y;
+      const int rad = __float_as_int(c.z);
+      p.radii[r] = rad;
+      if (rad > 0) {
+        ms = c.w;
+        cnt = 1.0;
+      }
+    }
+  }
+  if (!p.reg) return;
+  __shared__ double s_red[2][8];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    ms += __shfl_xor_sync(0xffffffffu, ms, o);
+    cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    s_red[0][threadIdx.x >> 5] = ms;
+    s_red[1][threadIdx.x >> 5] = cnt;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double a = 0.0, c = 0.0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+      a += s_red[0][w];
+      c += s_red[1][w];
+    }
+    if (c > 0.0) {
+      atomicAdd(p.reg + 0, a);
+      atomicAdd(p.reg + 1, c);
+    }
+  }
+}
+
+// Render-backward record [m.x m.y 0 0 | a.x a.y 0 0 | c00 c01 c11 op | r g b 0]
+// of camera row r -> gradient record [c00 c01 c11 op | x y | r g b | |x| |y|
+// dminscale] at its send row (dminscale = reg_scale for rows with radius > 0).
+__global__ void __launch_bounds__(256) grad_records_pack_kernel(GradPackParams p, int64_t n) {
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= n) return;
+  const int64_t dst = segment_row(p.seg, r);
+  if (dst < 0) return;
+  const float4* v = reinterpret_cast<const float4*>(p.rec16 + 16 * r);
+  const float4 m = v[0], a = v[1], c = v[2], col = v[3];
+  const float g_min = (p.reg_scale && __ldg(p.radii + r) > 0) ? *p.reg_scale : 0.f;
+  float4* o = reinterpret_cast<float4*>(p.send + 12 * dst);
+  o[0] = c;
+  o[1] = make_float4(m.x, m.y, col.x, col.y);
+  o[2] = make_float4(col.z, a.x, a.y, g_min);
+}
+
+}  // namespace
+
+int launch_exchange_unpack(const UnpackParams& p, int64_t n, cudaStream_t st) {
+  if (n <= 0) return 0;
+  exchange_unpack_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(p, n);
+  return (int)cudaGetLastError();
+}
+
+int launch_grad_records_pack(const GradPackParams& p, int64_t n, cudaStream_t st) {
+  if (n <= 0) return 0;
+  grad_records_pack_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(p, n);
+  return (int)cudaGetLastError();
+}
+
 int launch_exchange_pack(const PackParams& p, cudaStream_t st) {
   if (p.n_rows <= 0) return 0;
   const int threads = 256;

@@ -105,43 +105,45 @@ class _DistributedBatch(torch.autograd.Function):
             ops.exchange_pack(counts[k], pre[k][4], pre[k][5], dest_off, cursor[k], send, send_row, offs[k])
         recv_buf = torch.empty((sum(plan.recv_splits), _FWD_C), dtype=torch.float32, device=dev)
         torch.distributed.all_to_all_single(recv_buf, send[:n_send], plan.recv_splits, plan.send_splits, group=group)
-        recv = {}
-        for k, parts in plan.recv_offsets.items():
-            tot = sum(c for _, _, c in parts)
-            if tot:
-                recv[k] = torch.cat([recv_buf[s:s + c] for _, s, c in parts if c], 0)
-
-        # 3. render and score the bands this rank owns
-        loss_sum = torch.zeros((), dtype=torch.float32, device=dev)
-        saved = {}
-        for k in range(n_cams):
-            st = strategies[k]
-            if rank not in st.gpu_ids:
-                continue
+        # 3. render and score the bands this rank owns.  Per camera: unpack
+        #    the received records (and the regulariser sums) in one kernel,
+        #    count tile instances; then one readback of every camera's totals
+        #    sizes all the binning buffers at once.
+        mine = [k for k in range(n_cams) if rank in strategies[k].gpu_ids]
+        nm = len(mine)
+        totals = torch.zeros((max(nm, 1), 2), dtype=torch.int64, device=dev)
+        regs = torch.zeros((max(nm, 1), 2), dtype=torch.float64, device=dev)
+        staged = []
+        for i, k in enumerate(mine):
             rs = rasters[k]
             H, W = int(rs.image_height), int(rs.image_width)
-            rec = recv.get(k)
-            if rec is None:
-                rec = torch.zeros((0, _FWD_C), dtype=torch.float32, device=dev)
-            conic = rec[:, 0:4].contiguous()
-            m2 = rec[:, 4:6].contiguous()
-            rgb = rec[:, 6:9].contiguous()
-            depth = rec[:, 9].contiguous()
-            radii = rec[:, 10].contiguous().view(torch.int32)
-            mins = rec[:, 11]
-            y0t, y1t = st.row_range(rank)
-            cl = st.get_compute_locally(device=dev)
-            color, _, _, _, _, state = ops.render_forward(m2, depth, radii, conic, rgb, rs.bg, cl, H, W)
+            segs = [(s, c) for _, s, c in plan.recv_offsets.get(k, []) if c]
+            conic, m2, rgb, depth, radii = ops.exchange_unpack(recv_buf, segs, regs[i])
+            cl = strategies[k].get_compute_locally(device=dev)
+            counts_k = torch.empty((max(m2.shape[0], 1),), dtype=torch.int32, device=dev)
+            ops.render_count(m2, radii, cl, H, W, counts_k, totals[i])
+            staged.append((k, segs, conic, m2, rgb, depth, radii, cl, counts_k))
+        tot_host = totals.cpu().tolist() if nm else []
+        losses = []
+        saved = {}
+        for i, (k, segs, conic, m2, rgb, depth, radii, cl, counts_k) in enumerate(staged):
+            rs = rasters[k]
+            H, W = int(rs.image_height), int(rs.image_width)
+            color, _, _, _, _, state = ops.render_forward(m2, depth, radii, conic, rgb, rs.bg, cl, H, W,
+                                                          counts=counts_k, totals=totals[i],
+                                                          totals_host=tot_host[i])
+            y0t, y1t = strategies[k].row_range(rank)
             y0, y1 = y0t * D.TILE, min(H, y1t * D.TILE)
             band = color[:, y0:y1, :]
             sums, partials = ops.loss_forward(band, gts[k])
             n3 = H * W * 3
-            vis = (radii > 0).to(torch.float32)
-            nvis = vis.sum()
-            reg = (mins * vis).sum() / nvis.clamp(min=1.0)
-            lk = ((1.0 - lambda_dssim) * (sums[0] / n3) + lambda_dssim * (1.0 - sums[1] / n3)).to(torch.float32)
-            loss_sum = loss_sum + lk + reg_w * reg
-            saved[k] = (state, m2, conic, rgb, cl, band, gts[k], partials, vis, nvis, (y0, y1), n3)
+            out = ops.loss_combine(sums, regs[i], lambda_dssim, n3, reg_w)
+            losses.append(out[0])
+            saved[k] = (state, m2, conic, rgb, cl, band, gts[k], partials, radii, out, (y0, y1), n3, segs)
+        if losses:
+            loss_sum = losses[0] if len(losses) == 1 else torch.stack(losses).sum()
+        else:
+            loss_sum = torch.zeros((), dtype=torch.float32, device=dev)
         ctx.setup = setup
         ctx.plan = plan
         ctx.saved = saved
@@ -165,21 +167,19 @@ class _DistributedBatch(torch.autograd.Function):
         try:
             # receiver: render backward of the owned bands -> 12-float gradient records
             send = torch.zeros((sum(plan.recv_splits), _BWD_C), dtype=torch.float32, device=dev)
-            for k, (state, m2, conic, rgb, cl, band, gt, partials, vis, nvis, (y0, y1), n3) in ctx.saved.items():
+            for k, (state, m2, conic, rgb, cl, band, gt, partials, radii, out, (y0, y1), n3, segs) in \
+                    ctx.saved.items():
                 rs = rasters[k]
                 H, W = int(rs.image_height), int(rs.image_width)
-                scale = torch.stack([g_loss * (1.0 - lambda_dssim) / n3, -g_loss * lambda_dssim / n3]).float()
-                g_band = ops.loss_backward(band, gt, partials, scale)
-                dpix = torch.zeros((3, H, W), dtype=torch.float32, device=dev)
-                dpix[:, y0:y1] = g_band
+                scales = ops.loss_combine_backward(g_loss, None, None, out, lambda_dssim, n3, reg_w)
+                g_band = ops.loss_backward(band, gt, partials, scales[0:2])
+                if y0 == 0 and y1 == H:
+                    dpix = g_band
+                else:
+                    dpix = torch.zeros((3, H, W), dtype=torch.float32, device=dev)
+                    dpix[:, y0:y1] = g_band
                 rec16 = ops.render_backward(state, m2, conic, rgb, rs.bg, cl, dpix)
-                g = torch.cat([rec16[:, 8:12], rec16[:, 0:2], rec16[:, 12:15], rec16[:, 4:6],
-                               (g_loss * reg_w * vis / nvis.clamp(min=1.0))[:, None]], 1)
-                pos = 0
-                for _, s, c in plan.recv_offsets[k]:
-                    if c:
-                        send[s:s + c] = g[pos:pos + c]
-                        pos += c
+                ops.grad_records_pack(rec16, radii, scales[2:3], segs, send)
             recv = torch.empty((sum(plan.send_splits), _BWD_C), dtype=torch.float32, device=dev)
             torch.distributed.all_to_all_single(recv, send, plan.send_splits, plan.recv_splits, group=group)
             # owner: one scatter-add into compact per-camera rows (aligned with the visible lists)

@@ -277,6 +277,39 @@ def exchange_pack(n_rows, records, dest_mask, dest_offset, cursor, send, send_ro
               ptr(cursor), ptr(send), ptr(send_row), int(row_base), _lib.stream_ptr())
 
 
+def _segments(segs):
+    n = len(segs)
+    start = (ctypes.c_int64 * max(n, 1))(*[int(a) for a, _ in segs])
+    count = (ctypes.c_int64 * max(n, 1))(*[int(c) for _, c in segs])
+    return n, start, count
+
+
+def exchange_unpack(records, segs, reg=None):
+    """Rows of one camera = the runs ``segs`` [(start, count), ...] of the
+    received [*,12] records, unpacked into (conic [n,4], means2D [n,2],
+    rgb [n,3], depths [n], radii int32 [n]); ``reg`` (double [2], zeroed)
+    accumulates the min-scale sum and count over rows with radius > 0."""
+    n = sum(int(c) for _, c in segs)
+    dev = records.device
+    conic = torch.empty((n, 4), dtype=torch.float32, device=dev)
+    m2 = torch.empty((n, 2), dtype=torch.float32, device=dev)
+    rgb = torch.empty((n, 3), dtype=torch.float32, device=dev)
+    depth = torch.empty((n,), dtype=torch.float32, device=dev)
+    radii = torch.empty((n,), dtype=torch.int32, device=dev)
+    k, start, count = _segments(segs)
+    _lib.call("blitz_exchange_unpack", k, start, count, ptr(records), ptr(conic), ptr(m2), ptr(rgb), ptr(depth),
+              ptr(radii), ptr(reg), _lib.stream_ptr())
+    return conic, m2, rgb, depth, radii
+
+
+def grad_records_pack(rec16, radii, reg_scale, segs, send):
+    """Render-backward records of one camera's rows -> 12-float gradient
+    records at the send rows of the runs ``segs``."""
+    k, start, count = _segments(segs)
+    _lib.call("blitz_grad_records_pack", k, start, count, ptr(rec16), ptr(radii), ptr(reg_scale), ptr(send),
+              _lib.stream_ptr())
+
+
 ROWS_UPSTREAM_BY_SLOT = 1  # BLITZ_ROWS_UPSTREAM_BY_SLOT
 ROWS_OUTPUT_BY_SLOT = 2    # BLITZ_ROWS_OUTPUT_BY_SLOT
 
@@ -349,15 +382,25 @@ def _tile_mask(compute_locally, H, W):
     return cl
 
 
+def render_count(means2D, radii, compute_locally, H, W, counts, totals):
+    """Per-Gaussian tile counts under ``compute_locally`` into ``counts``
+    int32 [P] and the device totals {R, n_vis} into ``totals`` int64 [2]."""
+    P = means2D.shape[0]
+    cl = _tile_mask(compute_locally, H, W)
+    _lib.call("blitz_render_count", P, H, W, ptr(_f32c(means2D)), ptr(radii), ptr(cl), ptr(counts), ptr(totals),
+              _lib.stream_ptr())
+
+
 def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_locally, H, W, counts=None, totals=None,
-                   vis_count=None, strip_lists=True):
+                   vis_count=None, strip_lists=True, totals_host=None):
     """Binning + blending of one camera.  Returns (color, n_render, n_consider,
     n_contrib_tile, out_observe, state).  ``counts``/``totals`` from
     ``preprocess_forward_raw(want_counts=True)`` skip the count pass;
     ``vis_count`` is read back with the totals (state.n_list).
     ``strip_lists`` records, per 8x4-pixel warp strip, the Gaussians that
     contributed to it (2 x 32 bytes per tile instance of device memory), so
-    the backward replays only those."""
+    the backward replays only those.  ``totals_host`` = (R, n_vis) already
+    read back by the caller (with ``counts``): no readback here."""
     _require_cuda(means2D, depths, radii, conic_opacity, rgb, bg)
     means2D, depths, conic_opacity, rgb, bg = map(_f32c, (means2D, depths, conic_opacity, rgb, bg))
     radii = radii.contiguous()
@@ -387,12 +430,16 @@ def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_local
     n_contrib_tile = torch.empty((T,), dtype=torch.int32, device=dev)
     out_observe = torch.zeros((P,), dtype=torch.int32, device=dev)
     strip_counts = torch.empty((T * 8,), dtype=torch.int32, device=dev) if strip_lists else None
-    host, host_np = _pinned(dev, 2, torch.int64)
-    host_n, host_n_np = _pinned(dev, 1, torch.int32) if vis_count is not None else (None, None)
-    _lib.call("blitz_read_totals", ptr(totals), ptr(vis_count), host.data_ptr(),
-              host_n.data_ptr() if host_n is not None else None, st)
-    R, n_vis = int(host_np[0]), int(host_np[1])
-    n_list = int(host_n_np[0]) if vis_count is not None else None
+    if totals_host is not None:
+        R, n_vis = int(totals_host[0]), int(totals_host[1])
+        n_list = None
+    else:
+        host, host_np = _pinned(dev, 2, torch.int64)
+        host_n, host_n_np = _pinned(dev, 1, torch.int32) if vis_count is not None else (None, None)
+        _lib.call("blitz_read_totals", ptr(totals), ptr(vis_count), host.data_ptr(),
+                  host_n.data_ptr() if host_n is not None else None, st)
+        R, n_vis = int(host_np[0]), int(host_np[1])
+        n_list = int(host_n_np[0]) if vis_count is not None else None
 
     point_list = torch.empty((max(R, 1),), dtype=torch.int32, device=dev)
     strip_ids = torch.empty((8 * max(R, 1),), dtype=torch.int32, device=dev) if strip_lists else None

@@ -323,6 +323,33 @@ int blitz_loss_backward(int C, int Hb, int W, const float* img, const uint8_t* g
                         const float* scale, float* dL_dimg, void* stream);
 
 /*
+ * Multi-GPU exchange, receiving side (no counterpart in the reference, whose
+ * all_to_all_communication_final splits the received tensors with PyTorch,
+ * gaussian_renderer/__init__.py:22-189): the rows of one camera are the
+ * n_segments runs [seg_start[s], seg_start[s] + seg_count[s]) of records
+ * ([*,12] floats: c00 c01 c11 opacity | x y | r g b | depth radius-bits
+ * min-axis-scale; 16-byte aligned), in order.  Writes conic [n,4] (16-byte
+ * aligned), means2D [n,2], rgb [n,3], depths [n], radii int32 [n]; with reg
+ * (device double[2], caller-zeroed) adds the sum of the min-axis scales of
+ * the rows with radius > 0 and their count.  n_segments <= 32.
+ */
+int blitz_exchange_unpack(int n_segments, const int64_t* seg_start, const int64_t* seg_count, const float* records,
+                          float* conic, float* means2D, float* rgb, float* depths, int32_t* radii, double* reg,
+                          void* stream);
+
+/*
+ * Multi-GPU exchange, backward send side (no counterpart in the reference):
+ * row r of the camera's render-backward record rec16 [n,16] (see
+ * blitz_render_backward) becomes the 12-float gradient record
+ * {dconic c00 c01 c11, dopacity | dx dy | dr dg db | |dx| |dy| | dmin-scale}
+ * at send row seg_start[s] + (r - rows before run s); dmin-scale =
+ * *reg_scale for rows with radius > 0 (reg_scale may be NULL: 0).
+ * n = sum of seg_count; n_segments <= 32.
+ */
+int blitz_grad_records_pack(int n_segments, const int64_t* seg_start, const int64_t* seg_count, const float* rec16,
+                            const int32_t* radii, const float* reg_scale, float* send, void* stream);
+
+/*
  * Per-camera loss of the training step, on the device (no counterpart in
  * the reference, which forms it with PyTorch scalar ops in
  * gaussian_renderer/loss_distribution.py:307-322):

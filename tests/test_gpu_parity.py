@@ -491,3 +491,38 @@ def test_exchange_records_routing_and_pack(cuda_device):
         rows = send_row[offs[k]:offs[k] + counts[k]].long() - 7
         assert torch.equal(torch.sort(rows).values, torch.nonzero(bits[:, k]).flatten())
         assert torch.equal(send[offs[k]:offs[k] + counts[k]], rec[rows])
+
+
+def test_exchange_unpack_and_gradient_pack(cuda_device):
+    """blitz_exchange_unpack splits received records (several runs, in order)
+    exactly like slicing them, with the min-scale sum/count over rows of
+    radius > 0; blitz_grad_records_pack writes the 12-float gradient records
+    at the runs' rows."""
+    gen = torch.Generator().manual_seed(21)
+    rows = torch.randn(500, 12, generator=gen)
+    rad = torch.randint(-2, 30, (500,), generator=gen).to(torch.int32)
+    rows[:, 10] = rad.view(torch.float32)
+    recs = rows.to(cuda_device)
+    segs = [(7, 40), (100, 0), (200, 123), (400, 61)]
+    sel = torch.cat([rows[s:s + c] for s, c in segs if c])
+    reg = torch.zeros(2, dtype=torch.float64, device=cuda_device)
+    conic, m2, rgb, depth, radii = ops.exchange_unpack(recs, segs, reg)
+    assert torch.equal(conic.cpu(), sel[:, 0:4]) and torch.equal(m2.cpu(), sel[:, 4:6])
+    assert torch.equal(rgb.cpu(), sel[:, 6:9]) and torch.equal(depth.cpu(), sel[:, 9])
+    assert torch.equal(radii.cpu(), sel[:, 10].contiguous().view(torch.int32))
+    vis = radii.cpu() > 0
+    assert reg[1].item() == vis.sum().item()
+    assert abs(reg[0].item() - sel[vis, 11].double().sum().item()) < 1e-9
+    n = sel.shape[0]
+    rec16 = torch.randn(n, 16, generator=gen).to(cuda_device)
+    scale = torch.tensor([0.37], device=cuda_device)
+    send = torch.full((700, 12), -7.0, device=cuda_device)
+    dst = [(0, 40), (300, 123), (600, 61)]
+    ops.grad_records_pack(rec16, radii, scale, dst, send)
+    r = rec16.cpu()
+    want = torch.cat([r[:, 8:12], r[:, 0:2], r[:, 12:15], r[:, 4:6],
+                      torch.where(vis, torch.tensor(0.37), torch.tensor(0.0))[:, None]], 1)
+    got = send.cpu()
+    assert torch.equal(got[0:40], want[0:40]) and torch.equal(got[300:423], want[40:163])
+    assert torch.equal(got[600:661], want[163:224])
+    assert torch.all(got[40:300] == -7.0) and torch.all(got[423:600] == -7.0)
