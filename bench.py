@@ -443,12 +443,22 @@ def measured_traffic(stage, workload):
         cells = [c.strip().strip("`") for c in line.strip().strip("|").split("|")]
         if len(cells) == 6:
             try:
-                per[cells[0]] = float(cells[4]) * 1e6
+                per[cells[0].split("::")[-1]] = float(cells[4]) * 1e6
             except ValueError:
                 pass
-    if not all(k in per for k in STAGE_KERNELS[stage]):
+
+    def lookup(name):
+        # exact name, else the same kernel under another template argument
+        if name in per:
+            return per[name]
+        base = name.split("<")[0]
+        hits = [v for k, v in per.items() if k.split("<")[0] == base]
+        return hits[0] if hits else None
+
+    vals = [lookup(k) for k in STAGE_KERNELS[stage]]
+    if any(v is None for v in vals):
         return None
-    return round(sum(per[k] for k in STAGE_KERNELS[stage]))
+    return round(sum(vals))
 
 
 def roofline_from_stages(stages, peaks, peak_kind, n_vis_per_call, fp32_peak=None):
