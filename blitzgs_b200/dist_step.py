@@ -9,18 +9,23 @@ Per step, for a batch of cameras split into tile-row bands by
             reference's get_local2j_ids semantics); one all-gather of the
             per-destination counts sizes the exchange, a pack kernel fills
             the send buffer, and ONE all_to_all_single moves a record per
-            (Gaussian, camera, destination); each rank renders its bands and computes
-            the band loss (L1 + SSIM + the min-scale regulariser over the
+            (Gaussian, camera, destination); each rank unpacks every
+            camera's received records with one kernel (which also sums the
+            min-scale regulariser), renders its bands and forms the band
+            loss on the device (L1 + SSIM + the regulariser over the
             received visible Gaussians, loss_distribution.py:303-322);
-  backward  band loss / render backward on the receivers, ONE reverse
-            all_to_all_single of 12-float gradient records, one scatter-add
-            into compact per-camera rows on the owners (aligned with each
-            camera's visible list), and the listed preprocess backward
-            accumulated into the shard's raw-parameter gradients.
+  backward  band loss / render backward on the receivers, the gradient
+            records written straight into the send buffer by one kernel per
+            camera, ONE reverse all_to_all_single of 12-float gradient
+            records, one scatter-add into compact per-camera rows on the
+            owners (aligned with each camera's visible list), and the listed
+            preprocess backward accumulated into the shard's raw-parameter
+            gradients.
 These two all-to-alls and the tiny size all-gather are the only collectives
 (the reference additionally all-gathers sizes with a blocking .cpu() and
 runs a second all-to-all for radii/depths).  Host synchronisations per step:
-the count all-gather, and one per rendered camera to size its binning.
+the count all-gather, and one readback of every rendered camera's binning
+totals.
 """
 import torch
 

@@ -4,7 +4,7 @@
 This is the body of the reference's distributed_preprocess3dgs_and_all2all_final
 + render_final + batched_loss_computation + loss.backward() for the Gaussians
 and tile rows a rank owns (gaussian_renderer/__init__.py:220-413, 664-854,
-gaussian_renderer/loss_distribution.py:220-329), with three changes that keep
+gaussian_renderer/loss_distribution.py:220-329), with these changes, which keep
 results identical:
   * SH coefficients are read from _features_dc / _features_rest in place (the
     reference concatenates them with torch.cat and splits them again in C++);
@@ -15,7 +15,9 @@ results identical:
     binning buffers;
   * the loss is combined from the L1/SSIM sums and the regulariser on the
     device, with the float32 rounding of the same PyTorch expression, so no
-    scalar PyTorch op (or its autograd node) runs per camera.
+    scalar PyTorch op (or its autograd node) runs per camera;
+  * the blend forward records each 8x4-pixel strip's contributing Gaussians
+    and the blend backward replays only those (same pairs, same order).
 Parameter activations (exp, sigmoid, normalize) run inside the preprocess
 kernels with PyTorch's float arithmetic, and their backward is chained there
 too, so no activation or regulariser kernel runs in PyTorch.
