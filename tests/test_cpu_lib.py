@@ -83,6 +83,53 @@ def test_argument_validation_without_gpu():
         _lib.call("blitz_render_count", -1, 10, 10, None, None, None, None, None, None)
 
 
+def test_step_and_exchange_entries_validate_arguments_without_gpu():
+    """The loss combination, totals readback, zero fill, exchange unpack /
+    gradient pack and the strip-list arguments of the blend entries reject
+    bad arguments with BLITZ_EINVAL and a message before any CUDA call."""
+    lib = _lib.load()
+    EINVAL = 10001
+
+    def rejects(name, *args, msg=None):
+        rc = getattr(lib, name)(*args)
+        assert rc == EINVAL, (name, rc)
+        text = lib.blitz_last_error().decode()
+        assert name in text and (msg is None or msg in text), text
+
+    # loss combination: the sums pointer and a positive N3 are required
+    rejects("blitz_loss_combine", None, None, 0.8, 0.2, 100.0, 10.0, 1, None)
+    rejects("blitz_loss_combine", 8, None, 0.8, 0.2, 0.0, 10.0, 8, None)
+    rejects("blitz_loss_combine_backward", None, None, None, None, 0.8, 0.2, 100.0, 10.0, 8, None)
+    # totals readback: vis_count and host_vis go together
+    rejects("blitz_read_totals", None, None, 8, None, None)
+    rejects("blitz_read_totals", 8, 8, 8, None, None)
+    # zero fill: negative count, or a non-empty list without arrays
+    rejects("blitz_zero_fill_async", -1, None, None, None)
+    rejects("blitz_zero_fill_async", 2, None, None, None)
+    # exchange unpack / gradient pack: at most 32 runs, non-negative runs, pointers when rows exist
+    n = 33
+    starts = (ctypes.c_int64 * n)(*range(n))
+    counts = (ctypes.c_int64 * n)(*([1] * n))
+    rejects("blitz_exchange_unpack", n, starts, counts, None, None, None, None, None, None, None, None,
+            msg="segments")
+    neg = (ctypes.c_int64 * 1)(-5)
+    one = (ctypes.c_int64 * 1)(1)
+    rejects("blitz_exchange_unpack", 1, neg, one, None, None, None, None, None, None, None, None, msg="segments")
+    rejects("blitz_exchange_unpack", 1, one, one, None, None, None, None, None, None, None, None,
+            msg="null pointer")
+    rejects("blitz_grad_records_pack", n, starts, counts, None, None, None, None, None, msg="segments")
+    rejects("blitz_grad_records_pack", 1, one, one, None, None, None, None, None, msg="null pointer")
+    # empty runs are a no-op, not an error
+    zero = (ctypes.c_int64 * 1)(0)
+    assert lib.blitz_exchange_unpack(1, one, zero, None, None, None, None, None, None, None, None) == 0
+    assert lib.blitz_grad_records_pack(0, None, None, None, None, None, None, None) == 0
+    # strip lists: all three pointers or none
+    rejects("blitz_render_blend", 10, 16, 16, 8, 16, 8, 8, None, 8, 8, 8, 8, 8, 8, 8, 8, 8, 8, None, None, None,
+            msg="go together")
+    rejects("blitz_render_backward", 10, 16, 16, 8, 8, 8, 8, 8, 16, 8, 8, None, 8, None, 8, None, 8, 16, None,
+            msg="go together")
+
+
 def test_scratch_size_query_is_host_only():
     lib = _lib.load()
     a = lib.blitz_render_scratch_bytes(1000, 100, 500, 64, 64)
