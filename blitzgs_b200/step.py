@@ -116,8 +116,10 @@ class _ViewLoss(torch.autograd.Function):
         grads = [g_xyz, g_s, g_q, g_o, g_dc, g_rest]
         if ctx.sparse_grad:
             idx = vlist[:L].to(torch.int64).unsqueeze(0)
-            grads = [torch.sparse_coo_tensor(idx, g[:L], p.shape, check_invariants=False)
-                     for g, p in zip(grads, (xyz, s_raw, q_raw, o_raw, dc, rest))]
+            # the rows are the visible list: unique and in range by construction
+            with torch.sparse.check_sparse_tensor_invariants(enable=False):
+                grads = [torch.sparse_coo_tensor(idx, g[:L], p.shape, check_invariants=False)
+                         for g, p in zip(grads, (xyz, s_raw, q_raw, o_raw, dc, rest))]
         return (*grads, None, None, None, None, None, None, None, None)
 
 
