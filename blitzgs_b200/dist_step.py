@@ -29,6 +29,7 @@ totals.
 """
 import torch
 
+from . import densify as DZ
 from . import distributed as D
 from . import ops
 from .step import _zero_fill_async, _zero_fill_wait
@@ -48,7 +49,7 @@ class _DistributedBatch(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, xyz, s_raw, q_raw, o_raw, dc, rest, setup):
-        rasters, gts, strategies, group, lambda_dssim, reg_w = setup
+        rasters, gts, strategies, group, lambda_dssim, reg_w, densify = setup
         n_cams = len(rasters)
         rank = torch.distributed.get_rank(group)
         ws = torch.distributed.get_world_size(group)
@@ -84,6 +85,8 @@ class _DistributedBatch(torch.autograd.Function):
                 vis_count=cnt[k, 0:1], exchange=(table_dev[k, 0], table_dev[k, 1], xrec, xmask, cnt[k, 1:]),
                 out=bufs)
             pre.append((m2, r, vlist, vcount, xrec, xmask))
+            if densify is not None:
+                DZ.update_max_radii(densify, r)
         # 2. one all-gather of every rank's counts: the only host synchronisation
         #    before the render (it sizes the all-to-all on every rank)
         gdev = dev if torch.distributed.get_backend(group) == "nccl" else torch.device("cpu")
@@ -160,7 +163,7 @@ class _DistributedBatch(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, g_loss):
-        rasters, gts, strategies, group, lambda_dssim, reg_w = ctx.setup
+        rasters, gts, strategies, group, lambda_dssim, reg_w, densify = ctx.setup
         xyz, s_raw, q_raw, o_raw, dc, rest = ctx.saved_tensors
         n_cams = len(rasters)
         dev = xyz.device
@@ -201,6 +204,9 @@ class _DistributedBatch(torch.autograd.Function):
             a = acc[ctx.offs[k]:ctx.offs[k + 1]]
             if ctx.counts[k] == 0:
                 continue
+            if densify is not None:
+                # viewspace gradient of the owner's screen means: summed over the receivers
+                DZ.accumulate_grad(densify, vlist[:ctx.counts[k]].to(torch.int64), a[:, 4:6])
             ops.preprocess_backward_raw(r, m2, xyz, s_raw, q_raw, o_raw.reshape(-1), sh, rasters[k],
                                         a[:, 4:6], a[:, 0:4], a[:, 6:9],
                                         (g_xyz, g_s, g_q, g_o, (g_dc, 3), (g_rest, max(M, 1) * 3)),
@@ -224,13 +230,15 @@ def _pinned_table(n_cams, ws):
     return t
 
 
-def batch_loss(shard_model, rasters, gts, strategies, group=None, lambda_dssim=0.2, reg_w=10.0):
+def batch_loss(shard_model, rasters, gts, strategies, group=None, lambda_dssim=0.2, reg_w=10.0, densify=None):
     """Sum over the cameras this rank renders of the reference's per-camera
     loss.  Every rank must call ``.backward()`` on the result (the backward
     exchange is a collective), also when it renders nothing.
     ``shard_model`` = raw (xyz, _scaling, _rotation, _opacity, _features_dc,
     _features_rest) of this rank's shard; ``gts[k]`` is this rank's uint8
-    ground-truth band of camera k (rows of its tile band) or None."""
+    ground-truth band of camera k (rows of its tile band) or None.
+    ``densify`` (a densify.DensificationStats over the shard) receives the
+    densification statistics of every camera of the batch."""
     xyz, s_raw, q_raw, o_raw, dc, rest = shard_model
     return _DistributedBatch.apply(xyz, s_raw, q_raw, o_raw, dc, rest,
-                                   (rasters, gts, strategies, group, lambda_dssim, reg_w))
+                                   (rasters, gts, strategies, group, lambda_dssim, reg_w, densify))

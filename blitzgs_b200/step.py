@@ -24,6 +24,7 @@ too, so no activation or regulariser kernel runs in PyTorch.
 """
 import torch
 
+from . import densify as D
 from . import ops
 
 LAMBDA_DSSIM = 0.2
@@ -37,7 +38,7 @@ class _ViewLoss(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, xyz, s_raw, q_raw, o_raw, dc, rest, raster, gt, compute_locally, band, exact_norm, sparse_grad,
-                lambda_dssim, reg_weight):
+                lambda_dssim, reg_weight, densify):
         H, W = int(raster.image_height), int(raster.image_width)
         sh = ops.sh_layout(dc=dc, rest=rest)
         rot_norm = q_raw.norm(dim=1) if exact_norm else None
@@ -60,6 +61,9 @@ class _ViewLoss(torch.autograd.Function):
         ctx.cl = compute_locally
         ctx.sparse_grad = sparse_grad
         ctx.consts = consts
+        ctx.densify = densify
+        if densify is not None:
+            D.update_max_radii(densify, radii)
         ctx.save_for_backward(xyz, s_raw, q_raw, o_raw, dc, rest, means2D, conic, rgb, radii, gt, partials,
                               img_band, rot_norm, vlist, vcount, slot_of, out)
         ctx.mark_non_differentiable(radii, out_observe, color)
@@ -94,6 +98,14 @@ class _ViewLoss(torch.autograd.Function):
         finally:
             if grads_dense is not None:
                 _zero_fill_wait()
+        if ctx.densify is not None:
+            # the viewspace gradient of the visible Gaussians: record rows
+            # are list slots (slot_of) or, without a list, Gaussian ids
+            if slot_of is not None:
+                D.accumulate_grad(ctx.densify, vlist[:L].to(torch.int64), rec[:L, 0:2])
+            else:
+                vis = torch.nonzero(radii > 0).flatten()
+                D.accumulate_grad(ctx.densify, vis, rec[vis, 0:2])
         sh = ops.sh_layout(dc=dc, rest=rest)
         M = rest.shape[1]
         rows = ops.ROWS_UPSTREAM_BY_SLOT if slot_of is not None else 0
@@ -120,7 +132,7 @@ class _ViewLoss(torch.autograd.Function):
             with torch.sparse.check_sparse_tensor_invariants(enable=False):
                 grads = [torch.sparse_coo_tensor(idx, g[:L], p.shape, check_invariants=False)
                          for g, p in zip(grads, (xyz, s_raw, q_raw, o_raw, dc, rest))]
-        return (*grads, None, None, None, None, None, None, None, None)
+        return (*grads, None, None, None, None, None, None, None, None, None)
 
 
 def _zero_fill_async(tensors):
@@ -138,7 +150,7 @@ def _zero_fill_wait():
 
 
 def view_loss(model, raster, gt_band, compute_locally=None, band=None, lambda_dssim=LAMBDA_DSSIM,
-              scale_reg_weight=10.0, exact_norm=False, sparse_grad=False):
+              scale_reg_weight=10.0, exact_norm=False, sparse_grad=False, densify=None):
     """Loss of one camera exactly as batched_loss_computation forms it
     (loss_distribution.py:303-322): (1-l) L1/N3 + l (1 - SSIM/N3) +
     10 mean(min-axis scale of the Gaussians the exchange sends), N3 = 3 H W.
@@ -152,9 +164,12 @@ def view_loss(model, raster, gt_band, compute_locally=None, band=None, lambda_ds
     of the dense gradient is exactly zero), for optimizers that take sparse
     gradients such as torch.optim.SparseAdam -- the update rule of the
     reference's SparseGaussianAdam, which only touches visible rows.
+    ``densify`` (a densify.DensificationStats) receives this camera's
+    densification statistics: max_radii2D in the forward, the viewspace
+    gradient norm and count of every visible Gaussian in the backward.
     Returns (loss, l1_sum, ssim_sum, radii, out_observe, color)."""
     xyz, s_raw, q_raw, o_raw, dc, rest = model
     H = int(raster.image_height)
     band = band or (0, H)
     return _ViewLoss.apply(xyz, s_raw, q_raw, o_raw, dc, rest, raster, gt_band, compute_locally, band, exact_norm,
-                           sparse_grad, float(lambda_dssim), float(scale_reg_weight))
+                           sparse_grad, float(lambda_dssim), float(scale_reg_weight), densify)

@@ -605,3 +605,15 @@ def adam_update(param, grad, exp_avg, exp_avg_sq, visible, lr, b1, b2, eps):
     param[v] = param[v] + step
     exp_avg[v] = m
     exp_avg_sq[v] = s
+
+
+def densification_stats(max_radii2D, xyz_gradient_accum, denom, radii, grad_means2D):
+    """One camera's densification statistics, in place, as the reference
+    updates them (train_internal.py:365-367 max_radii2D over the visibility
+    filter; scene/gaussian_model.py:792-794 add_densification_stats): vis =
+    radii > 0, grad_means2D [P, >=2] the viewspace gradient of every
+    Gaussian."""
+    vis = radii > 0
+    max_radii2D[vis] = torch.max(max_radii2D[vis], radii[vis].to(max_radii2D.dtype))
+    xyz_gradient_accum[vis] += torch.norm(grad_means2D[vis, :2], dim=-1, keepdim=True)
+    denom[vis] += 1
