@@ -2,12 +2,14 @@
 
 The reference (scene/gaussian_model.py:1044-1133) checks after densification
 whether the ranks' Gaussian counts drifted apart (min * threshold < max, or
-a forced round; need_redistribute_gaussians) and then moves every row of
-every parameter *and* its Adam moments (exp_avg, exp_avg_sq) to its
-destination rank with one all-to-all per tensor (all2all_gaussian_state,
-all2all_tensors_in_optimizer), rebuilds the optimizer's parameters and
-resets the densification statistics.  Its destination is round-robin:
-local row i goes to rank i % world_size (get_destination_1).
+a forced round; need_redistribute_gaussians, :1078-1088) and then moves
+every row of every parameter *and* its Adam moments (exp_avg, exp_avg_sq)
+to its destination rank with one all-to-all per tensor
+(all2all_gaussian_state :1044-1052, all2all_tensors_in_optimizer
+:1054-1073), rebuilds the optimizer's parameters and resets the
+densification statistics (redistribute_gaussians :1090-1133).  Its
+destination is round-robin: local row i goes to rank i % world_size
+(get_destination_1, :1075-1076).
 
 Here the same machinery serves the spatial sharding the fused distributed
 step uses (each rank owns a contiguous z-order range of the scene, which

@@ -1,7 +1,7 @@
 """Redistribution of the shards after densification (blitzgs_b200.redistribute)
 on gloo CPU ranks: the round-robin mode against a restatement of the
-reference's all2all_gaussian_state (scene/gaussian_model.py:1044-1053,
-1085-1086), the z-order mode's invariants, Adam moments travelling with their
+reference's all2all_gaussian_state (scene/gaussian_model.py:1044-1052,
+1075-1076), the z-order mode's invariants, Adam moments travelling with their
 rows, and the redistribution trigger."""
 import os
 import socket
