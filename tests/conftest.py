@@ -7,7 +7,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-GOLDEN_DIRS = [os.path.join(ROOT, "tests", "golden"), os.path.join(ROOT, "gpurun_out", "golden")]
+GOLDEN_DIRS = [os.path.join(ROOT, "tests", "golden")]
 
 
 def pytest_configure(config):

@@ -4,8 +4,8 @@ from the reference sources by oracle/build_ref.py into oracle/_ref/) on a
 GPU, through the reference's own Python autograd wrappers, and the reference
 loss helpers (utils/loss_utils.py).
 
-Run on a B200 box:  python tests/golden/make_golden.py --out gpurun_out/golden
-then copy the .npz files here.  Inputs are NOT stored: the tests regenerate
+Run on a B200:  python tests/golden/make_golden.py --out <dir>
+(default: this directory) and commit the .npz files here.  Inputs are NOT stored: the tests regenerate
 them from the same seeds with blitzgs_b200.scene (CPU torch.Generator, bit
 identical everywhere); an input checksum is stored to detect drift.
 
@@ -157,7 +157,7 @@ def route_reference(means2D, radii, H, W, division_rows):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--out", default=os.path.join(ROOT, "gpurun_out", "golden"))
+    ap.add_argument("--out", default=os.path.dirname(os.path.abspath(__file__)))
     a = ap.parse_args()
     os.makedirs(a.out, exist_ok=True)
     torch.backends.cudnn.deterministic = True
