@@ -754,9 +754,10 @@ def main():
         except Exception as ex:  # the baseline must not sink the bench line
             cb = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "port", "sample": f"failed: {ex}"}
     cfg.update(gaussians=r["P"], image=f"{r['W']}x{r['H']}")
-    # native kernels launched per view (preprocess cull + full 2, binning+blend fwd, loss 2, blend bwd 1,
-    # preprocess bwd 1); the binning figure counts the cub launches seen in the ncu launch list
-    launches_per_view = 1 + 1 + KERNELS_RENDER_FWD + 2 + 1 + 1
+    # native kernels launched per view (preprocess cull + full 2, binning+blend fwd, loss forward /
+    # combination / combination backward / backward 4, blend bwd 1, preprocess bwd 1); the binning
+    # figure counts the cub launches seen in the ncu launch list (27 per view there)
+    launches_per_view = 2 + KERNELS_RENDER_FWD + 4 + 1 + 1
     line = {"metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
             "warmup": getattr(args, "warmup_done", args.warmup), "ms_per_step": round(r["ms"] / args.steps, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
