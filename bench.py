@@ -249,6 +249,7 @@ def run_ours(args, ws, rank, local):
     n_cams = len(cams)
     history = D.DivisionStrategyHistoryFinal(cams, ws, rank) if ws > 1 else None
     h2d = [0]
+    n_launch = [0]  # native kernels of the whole job issued by one_step (see LAUNCHES_PER_VIEW)
 
     def batch_ids(it):
         return [((it * bsz * ws) + k) % n_cams for k in range(bsz * ws)]
@@ -271,6 +272,7 @@ def run_ours(args, ws, rank, local):
                     gt = gts_dev[ci]
                 loss, *_ = ST.view_loss(model, rasters[ci], gt, sparse_grad=args.sparse_grad)
                 total = loss if total is None else total + loss
+                n_launch[0] += LAUNCHES_PER_VIEW
                 if trace is not None:
                     trace.append(("forward", time.perf_counter()))
         else:
@@ -294,6 +296,10 @@ def run_ours(args, ws, rank, local):
                 gts.append(band)
             h2d[0] = max(h2d[0], nbytes)
             total = DS.batch_loss(model, [rasters[c] for c in ids], gts, strategies)
+            # every rank preprocesses (cull + full), packs and back-propagates every camera of
+            # the batch; every rendered band adds unpack, count, binning, blend, loss and pack
+            n_launch[0] += ws * DIST_LAUNCHES_PER_CAMERA * len(ids) + \
+                DIST_LAUNCHES_PER_BAND * sum(len(st.gpu_ids) for st in strategies)
         total.backward()
         if trace is not None:
             trace.append(("backward", time.perf_counter()))
@@ -330,6 +336,7 @@ def run_ours(args, ws, rank, local):
     t1 = torch.cuda.Event(enable_timing=True)
     marks, host_t, trace = [], [time.perf_counter()], []
     mstat0 = torch.cuda.memory_stats(dev)
+    n_launch[0] = 0
     t0.record()
     for it in range(args.steps):
         one_step(args.warmup + it, False, trace if it == 0 else None)
@@ -338,6 +345,7 @@ def run_ours(args, ws, rank, local):
         marks.append(ev)
         host_t.append(time.perf_counter())
     t1.record()
+    launches = n_launch[0]
     torch.cuda.synchronize()
     clocks.mark()
     barrier(ws)
@@ -393,7 +401,7 @@ def run_ours(args, ws, rank, local):
     gc.enable()
     n_stage_steps = min(args.steps, 3)
     return dict(ms=ms, ms_e2e=ms_e2e, clocks=clk, stages=stages, H=H, W=W, P=sc.P, bsz=bsz,
-                h2d=h2d[0], d2h=4, n_stage_steps=n_stage_steps)
+                h2d=h2d[0], d2h=4, n_stage_steps=n_stage_steps, launches=launches)
 
 
 def stage_bytes(name, metas):
@@ -754,10 +762,6 @@ def main():
         except Exception as ex:  # the baseline must not sink the bench line
             cb = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "port", "sample": f"failed: {ex}"}
     cfg.update(gaussians=r["P"], image=f"{r['W']}x{r['H']}")
-    # native kernels launched per view (preprocess cull + full 2, binning+blend fwd, loss forward /
-    # combination / combination backward / backward 4, blend bwd 1, preprocess bwd 1); the binning
-    # figure counts the cub launches seen in the ncu launch list (27 per view there)
-    launches_per_view = 2 + KERNELS_RENDER_FWD + 4 + 1 + 1
     line = {"metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
             "warmup": getattr(args, "warmup_done", args.warmup), "ms_per_step": round(r["ms"] / args.steps, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
@@ -765,7 +769,7 @@ def main():
             "cpu_baseline": cb,
             "e2e": {"value": round(e2e, 4), "unit": UNIT, "h2d_bytes_per_step": r["h2d"],
                     "d2h_bytes_per_step": r["d2h"]},
-            "gpu_launches": launches_per_view * args.bsz * args.steps}
+            "gpu_launches": r["launches"]}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if ws > 1:
@@ -780,6 +784,15 @@ def main():
 # cub exclusive scan (2), emit (1), 12-bit sort (histogram + exclusive sum + 2 passes),
 # tile ranges (1), blend (1)
 KERNELS_RENDER_FWD = 19
+# native kernels of one single-GPU view: preprocess cull + full (2), binning + blend forward,
+# loss forward / combination / combination backward / backward (4), blend backward (1),
+# preprocess backward (1) -- 27, as the ncu launch list shows
+LAUNCHES_PER_VIEW = 2 + KERNELS_RENDER_FWD + 4 + 1 + 1
+# multi-GPU: per rank and camera of the batch (preprocess cull + full, exchange pack, preprocess
+# backward), and per rendered band (unpack, tile count, binning + blend, loss forward /
+# combination / combination backward / backward, blend backward, gradient-record pack)
+DIST_LAUNCHES_PER_CAMERA = 4
+DIST_LAUNCHES_PER_BAND = 1 + 1 + KERNELS_RENDER_FWD + 4 + 1 + 1
 
 if __name__ == "__main__":
     sys.exit(main())
