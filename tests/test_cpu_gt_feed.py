@@ -18,6 +18,8 @@ H, W, WS = 64, 24, 3
 # rank g renders tile rows [t_l, t_r) of camera c for (c, t_l, t_r) in TASKS[g]
 TASKS = [[(0, 0, 4), (1, 0, 1)], [(1, 1, 4), (2, 0, 2)], [(2, 2, 4)]]
 LOCAL_TASKS = [[(0, 0, 4)], [(1, 0, 4)], [(2, 0, 4)]]
+# the rank holding the images renders nothing itself
+IDLE_HOLDER_TASKS = [[], [(0, 0, 4), (1, 0, 3)], [(1, 3, 4), (2, 0, 4)]]
 
 
 class _Cam:
@@ -58,9 +60,9 @@ def _worker(rank, port, mode, q):
                 assert torch.equal(c.original_image, c.full)
             q.put((rank, "ok"))
             return
-        tasks = LOCAL_TASKS if mode == "local" else TASKS
+        tasks = {"local": LOCAL_TASKS, "dist_idle_holder": IDLE_HOLDER_TASKS}.get(mode, TASKS)
         # distributed storage: only the first rank of the node holds the images
-        cams = [_Cam(k, mode != "dist" or rank == 0) for k in range(3)]
+        cams = [_Cam(k, not mode.startswith("dist") or rank == 0) for k in range(3)]
         G.load_camera_from_cpu_to_all_gpu(cams, None, tasks, device="cpu", distributed_storage=(mode != "default"),
                                           local_sampling=(mode == "local"))
         for c, tl, tr in tasks[rank]:
@@ -75,7 +77,7 @@ def _worker(rank, port, mode, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["default", "dist", "local", "eval_dist", "eval_local"])
+@pytest.mark.parametrize("mode", ["default", "dist", "dist_idle_holder", "local", "eval_dist", "eval_local"])
 def test_gt_bands_reach_their_ranks(mode):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()

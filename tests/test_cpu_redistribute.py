@@ -24,10 +24,13 @@ def _free_port():
     return p
 
 
+_SIZES = [300, 90, 170]
+
+
 def _shard(rank):
     """Rank-local rows: positions, and a feature row whose column 0 is the
     row's global id; sizes differ per rank (a densified, unbalanced state)."""
-    n = [300, 90, 170][rank]
+    n = _SIZES[rank]
     g = torch.Generator().manual_seed(40 + rank)
     xyz = torch.rand(n, 3, generator=g) * torch.tensor([100.0, 60.0, 8.0])
     feat = torch.rand(n, 4, generator=g)
@@ -44,10 +47,12 @@ def _model(rank):
     return params, opt
 
 
-def _worker(rank, ws, port, mode, q):
+def _worker(rank, ws, port, mode, q, sizes=None):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=ws)
+    if sizes is not None:
+        _SIZES[:] = sizes
     try:
         params, opt = _model(rank)
         stats = DZ.DensificationStats(params[0].shape[0], "cpu")
@@ -83,11 +88,11 @@ def _worker(rank, ws, port, mode, q):
         dist.destroy_process_group()
 
 
-def _run(ws, mode):
+def _run(ws, mode, sizes=None):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, ws, port, mode, q)) for r in range(ws)]
+    procs = [ctx.Process(target=_worker, args=(r, ws, port, mode, q, sizes)) for r in range(ws)]
     for p in procs:
         p.start()
     res = sorted([q.get(timeout=180) for _ in procs], key=lambda r: r[0])
@@ -103,9 +108,11 @@ def test_round_robin_matches_reference_all2all(ws):
     _run(ws, "round_robin")
 
 
-@pytest.mark.parametrize("ws", [2, 3])
-def test_zorder_keeps_rows_orders_ranges_and_balances(ws):
-    res = _run(ws, "zorder")
+@pytest.mark.parametrize("ws,sizes", [(2, None), (3, None), (3, [300, 0, 170])])
+def test_zorder_keeps_rows_orders_ranges_and_balances(ws, sizes):
+    res = _run(ws, "zorder", sizes)
+    if sizes is not None:
+        _SIZES[:] = sizes
     ids = sorted(i for _, _, (_, _, rows) in res for i in rows)
     expected = sorted(int(i) for r in range(ws) for i in _shard(r)[1][:, 0].long().tolist())
     assert ids == expected  # every row arrives exactly once
