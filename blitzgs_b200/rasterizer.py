@@ -402,8 +402,44 @@ class GaussianRasterizer(nn.Module):
     def markVisible(self, positions):
         raise NotImplementedError("markVisible belongs to the eval/culling rasterizer (not on the training path)")
 
-    def forward(self, *a, **k):
-        raise NotImplementedError("the full non-distributed rasterizer (eval/culling) is not on the training path")
+    def forward(self, means3D, means2D, opacities, culling=None, dc=None, shs=None, colors_precomp=None,
+                scales=None, rotations=None, cov3D_precomp=None, flag_max_count=False):
+        """The reference's full (non-distributed) rasterizer forward
+        (f/diff_gaussian_rasterization_f/__init__.py:691-729 -> _RasterizeGaussians
+        :412-474): one camera, the whole image.  Composed from the training
+        path's two operators: preprocess (SH colour from ``dc`` and ``shs``,
+        scales and rotations), the radii of the Gaussians ``culling`` marks set
+        to 0 so they are never binned (cuda_rasterizer/forward.cu:191-206),
+        then the render over every tile.  The caller's ``means2D`` (zeros
+        [P, >=2]) receives the screen-space gradient in its first two columns,
+        as in the reference.  Returns (color [3,H,W], radii int32 [P],
+        accum_max_count [P] zeros).
+
+        Not provided: ``colors_precomp``, ``cov3D_precomp`` and
+        ``flag_max_count`` (the per-pixel maximum-weight count of the
+        mini-splatting pruning), which raise NotImplementedError."""
+        if (shs is None and colors_precomp is None) or (shs is not None and colors_precomp is not None):
+            raise Exception('Please provide excatly one of either SHs or precomputed colors!')
+        if ((scales is None or rotations is None) and cov3D_precomp is None) or \
+                ((scales is not None or rotations is not None) and cov3D_precomp is not None):
+            raise Exception('Please provide exactly one of either scale/rotation pair or precomputed 3D covariance!')
+        if colors_precomp is not None:
+            raise NotImplementedError("precomputed colours are not supported (SH colour only)")
+        if cov3D_precomp is not None:
+            raise NotImplementedError("precomputed 3D covariances are not supported (scales and rotations only)")
+        if flag_max_count:
+            raise NotImplementedError("flag_max_count (mini-splatting max-weight counts) is not supported")
+        rs = self.raster_settings
+        sh = shs if dc is None or dc.numel() == 0 else torch.cat((dc, shs), 1)
+        m2, rgb, conic, radii, depths = preprocess_gaussians(means3D, scales, rotations, sh, opacities, rs, None)
+        if culling is not None and culling.numel():
+            radii = radii.masked_fill(culling.reshape(-1).to(torch.bool), 0)
+        m2 = m2 + means2D[:, :2]
+        P = means3D.shape[0]
+        all_map = torch.zeros((P, 5), dtype=torch.float32, device=means3D.device)
+        color, *_ = render_gaussians(m2, None, conic, rgb, all_map, depths, radii, None, None, rs, None)
+        accum_max_count = torch.zeros((P,), dtype=torch.float32, device=means3D.device)
+        return color, radii, accum_max_count
 
     def render_simp(self, *a, **k):
         raise NotImplementedError("render_simp (mini-splatting culling) is not on the training path")
