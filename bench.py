@@ -589,6 +589,7 @@ def run_reference(args):
     gx, gy = (W + 15) // 16, (H + 15) // 16
     bg = torch.zeros(3, device=dev)
     n3 = H * W * 3
+    strategy = torch.tensor([0, gx * gy], dtype=torch.int32, device=dev)  # division_pos * TILE_X, one rank
 
     def cuda_args():
         return {"mode": "train", "world_size": "1", "global_rank": "0", "local_rank": "0", "mp_world_size": "1",
@@ -618,7 +619,10 @@ def run_reference(args):
         Ll1 = LU.pixelwise_l1_with_mask(color, gt, ones).sum() / n3
         ss = LU.pixelwise_ssim_with_mask(color, gt, ones).sum() / n3
         loss = 0.8 * Ll1 + 0.2 * (1.0 - ss)
-        vis = radii > 0
+        # render_final's visibility_filter: radius > 0 among the Gaussians
+        # get_local2j_ids_bool routes to this rank (all tiles at world size 1)
+        routed = ref._C.get_local2j_ids_bool(H, W, 0, 1, means2D.detach(), radii, strategy, ca)[:, 0]
+        vis = (radii > 0) & routed
         if vis.sum() > 0:
             loss = loss + 10.0 * torch.sort(scales[vis], dim=-1)[0][..., 0].mean()
         return loss

@@ -160,9 +160,20 @@ struct CullBound {
   float wf;    // ||W||_F^2
   float jnum;  // ||J||_F^2 * z^2
   float gw, gh;
+  // Magnitude bounds of the affine rows phase A evaluates: for a point with
+  // max(|x|,|y|,|z|) = m, the terms of each row sum in absolute value to at
+  // most lin * m + off (zw: view z and clip w; xy: clip x and clip y).
+  float zw_lin, zw_off, xy_lin, xy_off;
 };
 
-__device__ __forceinline__ CullBound make_cull_bound(const PreprocessParams& p, const float* Vs) {
+// Rounding bound for a 4-term affine row a*x + b*y + c*z + d evaluated in
+// float32, with or without FMA contraction: each of its at most six
+// operations rounds a partial result bounded by S = |a x| + |b y| + |c z| + |d|
+// by at most u = 2^-24 relative, so two evaluations of the same row in
+// different orders differ by at most 12 u S.  16 u S leaves room.
+constexpr float kAffineErr = 16.0f / 16777216.0f;
+
+__device__ __forceinline__ CullBound make_cull_bound(const PreprocessParams& p, const float* Vs, const float* Ps) {
   CullBound c;
   c.wf = Vs[0] * Vs[0] + Vs[1] * Vs[1] + Vs[2] * Vs[2] + Vs[4] * Vs[4] + Vs[5] * Vs[5] + Vs[6] * Vs[6] + Vs[8] * Vs[8] +
          Vs[9] * Vs[9] + Vs[10] * Vs[10];
@@ -170,6 +181,10 @@ __device__ __forceinline__ CullBound make_cull_bound(const PreprocessParams& p, 
   c.jnum = p.focal_x * p.focal_x * (1.f + cx * cx) + p.focal_y * p.focal_y * (1.f + cy * cy);
   c.gw = (float)(p.grid_x * kTileX);
   c.gh = (float)(p.grid_y * kTileY);
+  c.zw_lin = fmaxf(fabsf(Vs[2]) + fabsf(Vs[6]) + fabsf(Vs[10]), fabsf(Ps[3]) + fabsf(Ps[7]) + fabsf(Ps[11]));
+  c.zw_off = fmaxf(fabsf(Vs[14]), fabsf(Ps[15]));
+  c.xy_lin = fmaxf(fabsf(Ps[0]) + fabsf(Ps[4]) + fabsf(Ps[8]), fabsf(Ps[1]) + fabsf(Ps[5]) + fabsf(Ps[9]));
+  c.xy_off = fmaxf(fabsf(Ps[12]), fabsf(Ps[13]));
   return c;
 }
 
@@ -301,8 +316,11 @@ struct FwdAcc {
 // Phase A for the kPreUnroll Gaussians base + u*kPreThreads of this thread:
 // keep[u] is false only for Gaussians the full computation is certain to cull
 // (their rows are written here).  Every test is conservative, so fast
-// approximate arithmetic is enough: the near plane is tested with a margin
-// and the exact test is repeated in phase B.
+// approximate arithmetic is enough: the view depth and the clip coordinates
+// are evaluated here in an order of our own, so each test widens its
+// threshold by the rounding bound kAffineErr of the affine rows (at city
+// coordinates, |x| ~ 1000, that is ~1e-3 in depth); the exact tests are
+// repeated in phase B with the reference's expressions.
 __device__ __forceinline__ void cull_phase(const PreprocessParams& p, const float* Vs, const float* Ps,
                                            const CullBound& cb, int64_t base, bool (&keep)[kPreUnroll]) {
   // Without a rotation load, ||R||_F^2 <= 9: every entry of R is bounded by
@@ -331,10 +349,11 @@ __device__ __forceinline__ void cull_phase(const PreprocessParams& p, const floa
 #pragma unroll
   for (int u = 0; u < kPreUnroll; ++u) {
     const bool in = u * kPreThreads < rem;
+    const float m = fmaxf(fabsf(x[u].x), fmaxf(fabsf(x[u].y), fabsf(x[u].z)));
     const float z = Vs[2] * x[u].x + Vs[6] * x[u].y + Vs[10] * x[u].z + Vs[14];
-    keep[u] = in && z > 0.19999f;
     // the exact near test (z <= 0.2 culls) runs in phase B; here only what
-    // is clearly behind it is dropped and reported
+    // is behind it by more than the rounding bound is dropped and reported
+    keep[u] = in && z > 0.2f - kAffineErr * fmaf(cb.zw_lin, m, cb.zw_off);
     if (in && !keep[u] && p.prefiltered) atomicOr(p.error_flag, kErrPrefilteredCulled);
     if (keep[u]) {
       float m = fmaxf(fabsf(sc[u].x), fmaxf(fabsf(sc[u].y), fabsf(sc[u].z)));
@@ -354,12 +373,20 @@ __device__ __forceinline__ void cull_phase(const PreprocessParams& p, const floa
       const float hy = Ps[1] * x[u].x + Ps[5] * x[u].y + Ps[9] * x[u].z + Ps[13];
       const float hw = Ps[3] * x[u].x + Ps[7] * x[u].y + Ps[11] * x[u].z + Ps[15];
       const float pw = __fdividef(1.f, hw + 0.0000001f);
-      const float2 pimg = make_float2(((hx * pw + 1.f) * (float)p.W - 1.f) * 0.5f,
-                                      ((hy * pw + 1.f) * (float)p.H - 1.f) * 0.5f);
+      const float nx = hx * pw, ny = hy * pw;
+      const float2 pimg = make_float2(((nx + 1.f) * (float)p.W - 1.f) * 0.5f, ((ny + 1.f) * (float)p.H - 1.f) * 0.5f);
+      // pixel distance between this pimg and the reference's: the rounding
+      // bounds of hx, hy and hw carried through x / w (a vanishing or
+      // negative w gives an infinite or NaN margin, which keeps the Gaussian)
+      const float ew = kAffineErr * fmaf(cb.zw_lin, m, cb.zw_off);
+      const float exy = kAffineErr * fmaf(cb.xy_lin, m, cb.xy_off);
+      const float ex = 0.5f * (float)p.W * fabsf(pw) * (exy + fabsf(nx) * ew);
+      const float ey = 0.5f * (float)p.H * fabsf(pw) * (exy + fabsf(ny) * ew);
       const float jf = __fdividef(cb.jnum, z * z);
       const float v = (smax * smax * rf * jf * cb.wf + 0.8f) * 1.01f;
       const float rb = 3.34f * (v * rsqrtf(v)) * 1.0001f + 2.f;
-      keep[u] = !(pimg.x + rb < -1.f || pimg.x - rb > cb.gw + 1.f || pimg.y + rb < -1.f || pimg.y - rb > cb.gh + 1.f);
+      const float rx = rb + ex, ry = rb + ey;
+      keep[u] = !(pimg.x + rx < -1.f || pimg.x - rx > cb.gw + 1.f || pimg.y + ry < -1.f || pimg.y - ry > cb.gh + 1.f);
     }
     if (in && !keep[u]) store_culled(p, base + u * kPreThreads);
   }
@@ -528,7 +555,7 @@ __global__ void __launch_bounds__(kPreThreads, 2) preprocess_fwd_kernel(Preproce
   if (tid == 0) s_qn = 0;
   float Vs[16], Ps[16];
   load_camera(p, Vs, Ps);
-  const CullBound cb = make_cull_bound(p, Vs);
+  const CullBound cb = make_cull_bound(p, Vs, Ps);
   FwdAcc acc;
   const int64_t n_chunks = (p.P + kPreChunk - 1) / kPreChunk;
   __syncthreads();
@@ -578,7 +605,7 @@ __global__ void __launch_bounds__(kPreThreads, 4) preprocess_cull_kernel(Preproc
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float Vs[16], Ps[16];
   load_camera(p, Vs, Ps);
-  const CullBound cb = make_cull_bound(p, Vs);
+  const CullBound cb = make_cull_bound(p, Vs, Ps);
   const int64_t base = (int64_t)blockIdx.x * kPreChunk + tid;
   bool keep[kPreUnroll];
   cull_phase(p, Vs, Ps, cb, base, keep);
@@ -616,7 +643,7 @@ __global__ void __launch_bounds__(kPreThreads, 2) preprocess_full_kernel(Preproc
   const bool use_smem = stage_mask(p, s_mask);
   float Vs[16], Ps[16];
   load_camera(p, Vs, Ps);
-  const CullBound cb = make_cull_bound(p, Vs);
+  const CullBound cb = make_cull_bound(p, Vs, Ps);
   FwdAcc acc;
   const int n = *cand_count;
   __syncthreads();

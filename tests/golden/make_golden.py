@@ -13,7 +13,9 @@ Cases
   tiny   BASELINE config 1: 16,384 Gaussians, one 256x256 camera.  Stores the
          bit-exact outputs (radii, means2D, depths, per-tile sorted lists and
          ranges, n_contrib), the image, tile statistics, observation counts,
-         the routing mask for a 4-way row split, loss sums and gradient norms.
+         the routing mask for a 4-way row split, loss sums, and every
+         gradient row (rasterizer intermediates and activated parameters,
+         float32) with its norm and sum.
   small  2,048 Gaussians, ragged 184x120 image, with edge cases planted: 5 %
          opacity below 1/255 (extent falls back to 3.33), points behind the
          near plane, points beyond the 1.3 tan(fov) clamp.  Stores every
@@ -158,10 +160,18 @@ def route_reference(means2D, radii, H, W, division_rows):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", default=os.path.dirname(os.path.abspath(__file__)))
+    ap.add_argument("--only", choices=["tiny", "small"], default=None)
     a = ap.parse_args()
     os.makedirs(a.out, exist_ok=True)
     torch.backends.cudnn.deterministic = True
 
+    if a.only != "small":
+        make_tiny(a.out)
+    if a.only != "tiny":
+        make_small(a.out)
+
+
+def make_tiny(out):
     # --- tiny (config 1) ---
     sc = S.tiny()
     cam = sc.cameras[0]
@@ -179,10 +189,13 @@ def main():
         g = o[k].astype(np.float64)
         d[k + "_l2"] = np.sqrt((g * g).sum())
         d[k + "_sum"] = g.sum()
+        d[k] = o[k].astype(np.float32)
     d["input_sha256"] = np.array(input_checksum(sc))
-    np.savez_compressed(os.path.join(a.out, "golden_tiny.npz"), **d)
+    np.savez_compressed(os.path.join(out, "golden_tiny.npz"), **d)
     print("tiny: R", len(o["point_list"]), "visible", int((o["radii"] > 0).sum()), "loss", o["loss"])
 
+
+def make_small(out):
     # --- small with edge cases, full outputs + band render ---
     sc = small_scene()
     cam = sc.cameras[0]
@@ -198,7 +211,7 @@ def main():
         d["band_" + k] = v
     d["band_rows"] = np.array([2, 5])
     d["input_sha256"] = np.array(input_checksum(sc))
-    np.savez_compressed(os.path.join(a.out, "golden_small.npz"), **d)
+    np.savez_compressed(os.path.join(out, "golden_small.npz"), **d)
     print("small: R", len(o["point_list"]), "visible", int((o["radii"] > 0).sum()), "loss", o["loss"])
 
 

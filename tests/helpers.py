@@ -21,12 +21,6 @@ def assert_grad_close(a, b, rtol=GRAD_RTOL, name=""):
     assert r <= rtol, f"{name}: normwise relative error {r:.3e} > {rtol:.1e}"
 
 
-def frac_close(a, b, atol):
-    a = np.asarray(a, np.float64)
-    b = np.asarray(b, np.float64)
-    return float((np.abs(a - b) <= atol).mean())
-
-
 def scene_params(sc, device=None):
     ts = (sc.xyz, sc.scaling, sc.rotation, sc.opacity, sc.features_dc, sc.features_rest)
     return tuple(t.to(device) if device is not None else t for t in ts)
