@@ -209,7 +209,8 @@ def load_scene(args):
     sharding gives each rank, so 1-GPU and N-GPU runs (and the reference arm)
     see the same memory layout; --layout given keeps the generator's order."""
     from blitzgs_b200 import scene as S, distributed as D
-    sc = S.CONFIGS[args.config](seed=0)
+    kw = {"P": args.gaussians} if getattr(args, "gaussians", None) else {}
+    sc = S.CONFIGS[args.config](seed=0, **kw)
     if getattr(args, "layout", "zorder") == "zorder":
         order = D.zorder_shards(sc.xyz, 1)[0]
         for name in ("xyz", "scaling", "rotation", "opacity", "features_dc", "features_rest"):
@@ -434,39 +435,12 @@ def stage_bytes(name, metas):
     return tot
 
 
-TRAFFIC_TABLE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles", "dram_traffic_city8M_bench.md")
-# native stage -> kernels of that stage in the ncu traffic table
-STAGE_KERNELS = {"blend_bwd": ["blend_bwd_kernel"], "blend_fwd": ["blend_fwd_kernel"],
-                 "preprocess_fwd": ["preprocess_cull_kernel", "preprocess_full_kernel"],
-                 "preprocess_bwd": ["preprocess_bwd_list_kernel<0>"]}
-
-
-def measured_traffic(stage, workload):
-    """DRAM bytes per launch of a stage's kernels (read + write, mean over the
-    launches of one ncu capture of this bench's city workload), or None."""
-    if workload != "city" or stage not in STAGE_KERNELS or not os.path.exists(TRAFFIC_TABLE):
-        return None
-    per = {}
-    for line in open(TRAFFIC_TABLE):
-        cells = [c.strip().strip("`") for c in line.strip().strip("|").split("|")]
-        if len(cells) == 6:
-            try:
-                per[cells[0].split("::")[-1]] = float(cells[4]) * 1e6
-            except ValueError:
-                pass
-
-    def lookup(name):
-        # exact name, else the same kernel under another template argument
-        if name in per:
-            return per[name]
-        base = name.split("<")[0]
-        hits = [v for k, v in per.items() if k.split("<")[0] == base]
-        return hits[0] if hits else None
-
-    vals = [lookup(k) for k in STAGE_KERNELS[stage]]
-    if any(v is None for v in vals):
-        return None
-    return round(sum(vals))
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of each
+# stage's kernels, summed over the stage's kernels, measured by ncu on this
+# bench's city workload; see profiles/ for the capture and its command.
+# Fill in again whenever the kernels change.
+NCU_TRAFFIC = {}
+NCU_TRAFFIC_SOURCE = "ncu capture of bench.py (city, 1 GPU), mean per launch"
 
 
 def roofline_from_stages(stages, peaks, peak_kind, n_vis_per_call, fp32_peak=None):
@@ -700,6 +674,9 @@ def main():
     ap.add_argument("--sparse-grad", action="store_true",
                     help="parameter gradients as sparse rows of the visible Gaussians (1 GPU; default dense)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gaussians", type=int, default=None,
+                    help="Gaussian count of the scene (default: the config's); a smaller scene of the same "
+                         "distribution is the profiling case")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -753,12 +730,13 @@ def main():
     roof, stage_table = roofline_from_stages(r["stages"], peaks, pk, nv, fp32)
     roof_hbm = hbm_roofline(r["stages"], peaks, pk, nv)
     for rf in (roof, roof_hbm):
-        # measured DRAM traffic of the same kernels on this workload (dense 1-GPU step)
-        t = measured_traffic(rf.get("kernel"), args.config) if rf and ws == 1 and not args.sparse_grad else None
+        # DRAM traffic of the same kernel per launch, from the ncu capture of
+        # this workload (city, 1 GPU, dense gradients) recorded in NCU_TRAFFIC
+        t = NCU_TRAFFIC.get(rf.get("kernel")) if rf and ws == 1 and args.config == "city" and \
+            not args.gaussians and not args.sparse_grad else None
         if t is not None:
             rf["traffic"] = t
-            rf["traffic_source"] = ("ncu dram__bytes_read.sum + dram__bytes_write.sum, mean per launch: "
-                                    "profiles/dram_traffic_city8M_bench.md")
+            rf["traffic_source"] = NCU_TRAFFIC_SOURCE
     cb = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         try:

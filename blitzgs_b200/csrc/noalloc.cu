@@ -26,7 +26,11 @@
 //     threads without ordering) race on the array: order them;
 //   * the first call on each device looks up the array's device address
 //     (cudaGetSymbolAddress with that device current) and caches it; make
-//     that first call before any stream capture on the device.
+//     that first call before any stream capture on the device;
+//   * the cached address belongs to the device's primary context (the one
+//     the CUDA runtime, and PyTorch, use): a host that drives the device
+//     through a context of its own, or resets the device within the
+//     process, must not call this entry point.
 #include <cstdio>
 #include <mutex>
 
@@ -44,6 +48,7 @@ constexpr size_t kNoAllocScratch = BLITZ_NOALLOC_SCRATCH_BYTES;
 static __device__ __align__(256) unsigned char g_bin_scratch[kNoAllocScratch];
 
 constexpr int kMaxDevices = 64;
+constexpr int kErrDeviceOrdinal = -1;  // internal: the current device's ordinal is >= kMaxDevices
 std::mutex g_mu;
 void* g_scratch_ptr[kMaxDevices] = {};
 
@@ -53,7 +58,7 @@ int noalloc_scratch(void** out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return (int)e;
-  if (dev < 0 || dev >= kMaxDevices) return BLITZ_EINVAL;
+  if (dev < 0 || dev >= kMaxDevices) return kErrDeviceOrdinal;
   std::lock_guard<std::mutex> lk(g_mu);
   if (!g_scratch_ptr[dev]) {
     void* p = nullptr;
@@ -87,6 +92,12 @@ extern "C" int blitz_render_bin_noalloc(int64_t P, int64_t n_vis, int64_t R, int
   }
   void* scratch = nullptr;
   int e = noalloc_scratch(&scratch);
+  if (e == kErrDeviceOrdinal) {
+    snprintf(g_msg, sizeof(g_msg), "blitz_render_bin_noalloc: the current device's ordinal is beyond the %d devices "
+             "this entry point supports", kMaxDevices);
+    set_last_error(g_msg);
+    return BLITZ_EINVAL;
+  }
   if (e) {
     snprintf(g_msg, sizeof(g_msg), "blitz_render_bin_noalloc: cudaGetSymbolAddress of the static scratch failed (%d)", e);
     set_last_error(g_msg);

@@ -12,9 +12,11 @@
 //     the model's separate _features_dc / _features_rest tensors are read in
 //     place (no torch.cat and no .contiguous() split copies); the
 //     contiguous [P,16,3] case is read with 16-byte vector loads.
-// Backward fuses the reference's computeCov2DCUDA and preprocessCUDA
-// (backward.cu:146-400) into one kernel and recomputes cov3D and the
-// clamp flags instead of reading them back from saved buffers.
+// Backward computes, in one kernel, the gradients the reference's
+// computeCov2DCUDA and preprocessCUDA backward produce (backward.cu:146-400),
+// from a matrix-form derivation of its own (written out above bwd_compute),
+// and recomputes the 3D covariance and the clamp flags instead of reading
+// them back from saved buffers.
 #include <algorithm>
 
 #include "common.cuh"
@@ -657,16 +659,50 @@ __global__ void __launch_bounds__(kPreThreads, 2) preprocess_full_kernel(Preproc
 // ---------------------------------------------------------------------------
 // Backward
 // ---------------------------------------------------------------------------
+//
+// Derived in matrix form, math convention (column vectors; R(q) the rotation
+// of the quaternion q = (r, x, y, z); S = diag(mod * s)).  The forward chain of
+// one Gaussian with centre m is
+//   t = W m + w                      view-space centre (W the view rotation)
+//   J = [ fx/tz  0      -fx cx/tz^2 ]   EWA Jacobian at the clamped centre,
+//       [ 0      fy/tz  -fy cy/tz^2 ]   cx, cy = t.x, t.y clamped to +-1.3 tan(fov) tz
+//   L = R(q) S,  Sigma = L L^T         3D covariance
+//   T = J W,     A = T Sigma T^T + 0.3 I     2D covariance
+//   Q = A^-1 (the conic),  p = ndc(P [m; 1]) the screen centre
+//   c = max(0, sum_k B_k(d / |d|) f_k + 0.5),  d = m - campos  (SH colour)
+// and reverse mode through it gives, for an upstream G_Q that is symmetric
+// (its off-diagonal entry is the gradient of each of the two symmetric
+// entries of Q),
+//   G_A = -adj(A) G_Q adj(A) / (det(A)^2 + 1e-7)
+//   G_Sigma = T^T G_A T,   G_T = 2 G_A T Sigma,   G_J = G_T W^T
+//   dL/dt through the four non-zero entries of J,  dL/dm += W^T dL/dt
+//   G_L = 2 G_Sigma L,  dL/ds_j = sum_i R_ij (G_L)_ij,  G_R = G_L S,
+//   dL/dq = sum_ij (G_R)_ij dR_ij/dq
+// The gradient conventions are the operator contract of the reference
+// rasterizer (submodule/diff-gaussian-rasterization_f/cuda_rasterizer/
+// backward.cu:146-400): the clamped cx, cy carry gradient to t.x, t.y only
+// where the clamp is inactive and are held constant in tz; the scale gradient
+// is the gradient with respect to mod * s (equal to the true one at mod = 1,
+// the training value); the quaternion gradient is with respect to the
+// quaternion the kernel was given; a clamped colour channel passes nothing.
 
-// d(normalize(v))/dv applied to dv (reference auxiliary.h dnormvdv, float3).
-__device__ __forceinline__ float3 dnorm3(float3 v, float3 dv) {
-  const float sum2 = v.x * v.x + v.y * v.y + v.z * v.z;
-  const float invsum32 = 1.0f / sqrtf(sum2 * sum2 * sum2);
-  float3 r;
-  r.x = ((+sum2 - v.x * v.x) * dv.x - v.y * v.x * dv.y - v.z * v.x * dv.z) * invsum32;
-  r.y = (-v.x * v.y * dv.x + (sum2 - v.y * v.y) * dv.y - v.z * v.y * dv.z) * invsum32;
-  r.z = (-v.x * v.z * dv.x - v.y * v.z * dv.y + (sum2 - v.z * v.z) * dv.z) * invsum32;
-  return r;
+// Row k of the 3x3 part of a column-major 4x4 M (math convention).
+__device__ __forceinline__ float3 mat_row(const float* M, int k) { return make_float3(M[k], M[4 + k], M[8 + k]); }
+
+__device__ __forceinline__ float dot3(float3 a, float3 b) { return a.x * b.x + a.y * b.y + a.z * b.z; }
+
+__device__ __forceinline__ float3 lin2(float a, float3 u, float b, float3 v) {
+  return make_float3(a * u.x + b * v.x, a * u.y + b * v.y, a * u.z + b * v.z);
+}
+
+// Symmetric 3x3 matrix.
+struct Sym3 {
+  float xx, xy, xz, yy, yz, zz;
+};
+
+__device__ __forceinline__ float3 sym_mul(const Sym3& S, float3 v) {
+  return make_float3(S.xx * v.x + S.xy * v.y + S.xz * v.z, S.xy * v.x + S.yy * v.y + S.yz * v.z,
+                     S.xz * v.x + S.yz * v.y + S.zz * v.z);
 }
 
 template <bool ACC>
@@ -696,239 +732,195 @@ __device__ __forceinline__ void bwd_zero(BwdOut& o) {
   for (int k = 0; k < 45; ++k) o.rest[k] = 0.f;
 }
 
+// SH colour part: dL/d(coefficients) into out.dc / out.rest, and the
+// gradient with respect to the unit view direction (returned).  Each basis
+// function B_k of degree <= 3 enters with its value and its Cartesian
+// gradient in (x, y, z); the coefficient gradient is B_k dL/dc and the
+// direction gradient sums grad(B_k) (f_k . dL/dc).
+__device__ __forceinline__ float3 sh_backward(int D, float3 u, const ShRegs& s, const float dR[3], BwdOut& out) {
+  const float x = u.x, y = u.y, z = u.z;
+  float3 g = make_float3(0.f, 0.f, 0.f);
+#pragma unroll
+  for (int ch = 0; ch < 3; ++ch) out.dc[ch] = kSH0 * dR[ch];
+  // coefficient k (1-based past DC) with basis value b and gradient (bx, by, bz)
+  auto term = [&](int k, float b, float bx, float by, float bz) {
+    const float* f = s.rest + 3 * (k - 1);
+    float* o = out.rest + 3 * (k - 1);
+    o[0] = b * dR[0];
+    o[1] = b * dR[1];
+    o[2] = b * dR[2];
+    const float w = f[0] * dR[0] + f[1] * dR[1] + f[2] * dR[2];
+    g.x += w * bx;
+    g.y += w * by;
+    g.z += w * bz;
+  };
+  if (D > 0) {
+    term(1, -kSH1 * y, 0.f, -kSH1, 0.f);
+    term(2, kSH1 * z, 0.f, 0.f, kSH1);
+    term(3, -kSH1 * x, -kSH1, 0.f, 0.f);
+    if (D > 1) {
+      const float xx = x * x, yy = y * y, zz = z * z;
+      term(4, kSH2[0] * x * y, kSH2[0] * y, kSH2[0] * x, 0.f);
+      term(5, kSH2[1] * y * z, 0.f, kSH2[1] * z, kSH2[1] * y);
+      term(6, kSH2[2] * (2.f * zz - xx - yy), -2.f * kSH2[2] * x, -2.f * kSH2[2] * y, 4.f * kSH2[2] * z);
+      term(7, kSH2[3] * x * z, kSH2[3] * z, 0.f, kSH2[3] * x);
+      term(8, kSH2[4] * (xx - yy), 2.f * kSH2[4] * x, -2.f * kSH2[4] * y, 0.f);
+      if (D > 2) {
+        term(9, kSH3[0] * y * (3.f * xx - yy), 6.f * kSH3[0] * x * y, 3.f * kSH3[0] * (xx - yy), 0.f);
+        term(10, kSH3[1] * x * y * z, kSH3[1] * y * z, kSH3[1] * x * z, kSH3[1] * x * y);
+        term(11, kSH3[2] * y * (4.f * zz - xx - yy), -2.f * kSH3[2] * x * y, kSH3[2] * (4.f * zz - xx - 3.f * yy),
+             8.f * kSH3[2] * y * z);
+        term(12, kSH3[3] * z * (2.f * zz - 3.f * xx - 3.f * yy), -6.f * kSH3[3] * x * z, -6.f * kSH3[3] * y * z,
+             kSH3[3] * (6.f * zz - 3.f * xx - 3.f * yy));
+        term(13, kSH3[4] * x * (4.f * zz - xx - yy), kSH3[4] * (4.f * zz - 3.f * xx - yy), -2.f * kSH3[4] * x * y,
+             8.f * kSH3[4] * x * z);
+        term(14, kSH3[5] * z * (xx - yy), 2.f * kSH3[5] * x * z, -2.f * kSH3[5] * y * z, kSH3[5] * (xx - yy));
+        term(15, kSH3[6] * x * (xx - 3.f * yy), 3.f * kSH3[6] * (xx - yy), -6.f * kSH3[6] * x * y, 0.f);
+      }
+    }
+  }
+  return g;
+}
+
 // Gradients of one visible Gaussian (radius > 0) given its upstream
 // gradients gco (conic00, conic01, conic11, opacity).
 // up = row of the upstream gradients (i, or the list position).
 __device__ __forceinline__ void bwd_compute(const PreprocessBwdParams& p, int64_t i, int64_t up, float4 gco,
                                             BwdOut& out) {
   const PreprocessParams& f = p.f;
-
-  float Vs[16], Ps[16];
+  float V[16], Pm[16];
 #pragma unroll
   for (int k = 0; k < 16; ++k) {
-    Vs[k] = __ldg(f.viewmatrix + k);
-    Ps[k] = __ldg(f.projmatrix + k);
+    V[k] = __ldg(f.viewmatrix + k);
+    Pm[k] = __ldg(f.projmatrix + k);
   }
-  const float3 mean = make_float3(__ldg(f.means3D + 3 * i + 0), __ldg(f.means3D + 3 * i + 1),
-                                  __ldg(f.means3D + 3 * i + 2));
+  const float3 m = make_float3(__ldg(f.means3D + 3 * i + 0), __ldg(f.means3D + 3 * i + 1),
+                               __ldg(f.means3D + 3 * i + 2));
   const Activated act = activate(f, i);
   const float sx = act.sx, sy = act.sy, sz = act.sz;
-  const float4 q = act.q;
-  float cov3d[6];
-  cov3d_from_scale_rot(sx, sy, sz, f.scale_modifier, q, cov3d);
+  const float qr = act.q.x, qx = act.q.y, qy = act.q.z, qz = act.q.w;
 
-  // ---- 2D covariance / conic part (reference backward.cu:146-276) ----
-  const float dL_dconic_x = gco.x, dL_dconic_y = gco.y, dL_dconic_z = gco.z;
-  float3 t = xform_point3(mean, Vs);
-  const float h_x = f.focal_x, h_y = f.focal_y;
-  const float limx = 1.3f * f.tanfovx;
-  const float limy = 1.3f * f.tanfovy;
-  const float txtz = t.x / t.z;
-  const float tytz = t.y / t.z;
-  t.x = min(limx, max(-limx, txtz)) * t.z;
-  t.y = min(limy, max(-limy, tytz)) * t.z;
-  const float x_grad_mul = txtz < -limx || txtz > limx ? 0 : 1;
-  const float y_grad_mul = tytz < -limy || tytz > limy ? 0 : 1;
+  // L = R(q) S; Sigma = L L^T
+  const float Rm[3][3] = {{1.f - 2.f * (qy * qy + qz * qz), 2.f * (qx * qy - qr * qz), 2.f * (qx * qz + qr * qy)},
+                          {2.f * (qx * qy + qr * qz), 1.f - 2.f * (qx * qx + qz * qz), 2.f * (qy * qz - qr * qx)},
+                          {2.f * (qx * qz - qr * qy), 2.f * (qy * qz + qr * qx), 1.f - 2.f * (qx * qx + qy * qy)}};
+  const float sm[3] = {f.scale_modifier * sx, f.scale_modifier * sy, f.scale_modifier * sz};
+  float Lm[3][3];
+#pragma unroll
+  for (int a = 0; a < 3; ++a)
+#pragma unroll
+    for (int j = 0; j < 3; ++j) Lm[a][j] = Rm[a][j] * sm[j];
+  Sym3 Sg;
+  Sg.xx = Lm[0][0] * Lm[0][0] + Lm[0][1] * Lm[0][1] + Lm[0][2] * Lm[0][2];
+  Sg.xy = Lm[0][0] * Lm[1][0] + Lm[0][1] * Lm[1][1] + Lm[0][2] * Lm[1][2];
+  Sg.xz = Lm[0][0] * Lm[2][0] + Lm[0][1] * Lm[2][1] + Lm[0][2] * Lm[2][2];
+  Sg.yy = Lm[1][0] * Lm[1][0] + Lm[1][1] * Lm[1][1] + Lm[1][2] * Lm[1][2];
+  Sg.yz = Lm[1][0] * Lm[2][0] + Lm[1][1] * Lm[2][1] + Lm[1][2] * Lm[2][2];
+  Sg.zz = Lm[2][0] * Lm[2][0] + Lm[2][1] * Lm[2][1] + Lm[2][2] * Lm[2][2];
 
-  M3 J = make_m3(h_x / t.z, 0.0f, -(h_x * t.x) / (t.z * t.z), 0.0f, h_y / t.z,
-                 -(h_y * t.y) / (t.z * t.z), 0, 0, 0);
-  M3 W = make_m3(Vs[0], Vs[4], Vs[8], Vs[1], Vs[5], Vs[9], Vs[2], Vs[6], Vs[10]);
-  M3 Vrk = make_m3(cov3d[0], cov3d[1], cov3d[2], cov3d[1], cov3d[3], cov3d[4], cov3d[2],
-                   cov3d[4], cov3d[5]);
-  M3 T = m3_mul(W, J);
-  M3 c2 = m3_mul(m3_mul(m3_t(T), m3_t(Vrk)), T);
-  const float a = c2.m[0][0] += 0.3f;
-  const float b = c2.m[0][1];
-  const float c = c2.m[1][1] += 0.3f;
+  // view-space centre, clamp masks, Jacobian entries, T = J W
+  const float3 t = xform_point3(m, V);
+  const float limx = 1.3f * f.tanfovx, limy = 1.3f * f.tanfovy;
+  const float ux = t.x / t.z, uy = t.y / t.z;
+  const float free_x = (ux < -limx || ux > limx) ? 0.f : 1.f;
+  const float free_y = (uy < -limy || uy > limy) ? 0.f : 1.f;
+  const float cx = fminf(limx, fmaxf(-limx, ux)) * t.z;
+  const float cy = fminf(limy, fmaxf(-limy, uy)) * t.z;
+  const float iz = 1.f / t.z, iz2 = iz * iz;
+  const float fx = f.focal_x, fy = f.focal_y;
+  const float3 w0 = mat_row(V, 0), w1 = mat_row(V, 1), w2 = mat_row(V, 2);
+  const float3 T0 = lin2(fx * iz, w0, -fx * cx * iz2, w2);
+  const float3 T1 = lin2(fy * iz, w1, -fy * cy * iz2, w2);
 
-  const float denom = a * c - b * b;
-  float dL_da = 0, dL_db = 0, dL_dc = 0;
-  const float denom2inv = 1.0f / ((denom * denom) + 0.0000001f);
-  float dcov[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  if (denom2inv != 0) {
-    dL_da = denom2inv * (-c * c * dL_dconic_x + 2 * b * c * dL_dconic_y + (denom - a * c) * dL_dconic_z);
-    dL_dc = denom2inv * (-a * a * dL_dconic_z + 2 * a * b * dL_dconic_y + (denom - a * c) * dL_dconic_x);
-    dL_db = denom2inv * 2 * (b * c * dL_dconic_x - (denom + 2 * b * b) * dL_dconic_y + a * b * dL_dconic_z);
-    dcov[0] = (T[0][0] * T[0][0] * dL_da + T[0][0] * T[1][0] * dL_db + T[1][0] * T[1][0] * dL_dc);
-    dcov[3] = (T[0][1] * T[0][1] * dL_da + T[0][1] * T[1][1] * dL_db + T[1][1] * T[1][1] * dL_dc);
-    dcov[5] = (T[0][2] * T[0][2] * dL_da + T[0][2] * T[1][2] * dL_db + T[1][2] * T[1][2] * dL_dc);
-    dcov[1] = 2 * T[0][0] * T[0][1] * dL_da + (T[0][0] * T[1][1] + T[0][1] * T[1][0]) * dL_db + 2 * T[1][0] * T[1][1] * dL_dc;
-    dcov[2] = 2 * T[0][0] * T[0][2] * dL_da + (T[0][0] * T[1][2] + T[0][2] * T[1][0]) * dL_db + 2 * T[1][0] * T[1][2] * dL_dc;
-    dcov[4] = 2 * T[0][2] * T[0][1] * dL_da + (T[0][1] * T[1][2] + T[0][2] * T[1][1]) * dL_db + 2 * T[1][1] * T[1][2] * dL_dc;
+  // A = T Sigma T^T + 0.3 I, with U = T Sigma
+  const float3 U0 = sym_mul(Sg, T0), U1 = sym_mul(Sg, T1);
+  const float a00 = dot3(U0, T0) + 0.3f, a01 = dot3(U0, T1), a11 = dot3(U1, T1) + 0.3f;
+
+  // G_A = -adj(A) G_Q adj(A) / (det^2 + 1e-7); adj(A) = [a11 -a01; -a01 a00]
+  const float q00 = gco.x, q01 = gco.y, q11 = gco.z;
+  const float det = a00 * a11 - a01 * a01;
+  const float inv = 1.f / (det * det + 1e-7f);
+  float g00 = 0.f, g01 = 0.f, g11 = 0.f;
+  if (inv != 0.f) {
+    const float k00 = a11 * q00 - a01 * q01, k01 = a11 * q01 - a01 * q11;  // row 0 of adj(A) G_Q
+    const float k10 = a00 * q01 - a01 * q00, k11 = a00 * q11 - a01 * q01;  // row 1
+    g00 = -(k00 * a11 - k01 * a01) * inv;
+    g01 = -(k01 * a00 - k00 * a01) * inv;
+    g11 = -(k11 * a00 - k10 * a01) * inv;
   }
-  const float dL_dT00 = 2 * (T[0][0] * Vrk[0][0] + T[0][1] * Vrk[0][1] + T[0][2] * Vrk[0][2]) * dL_da +
-                        (T[1][0] * Vrk[0][0] + T[1][1] * Vrk[0][1] + T[1][2] * Vrk[0][2]) * dL_db;
-  const float dL_dT01 = 2 * (T[0][0] * Vrk[1][0] + T[0][1] * Vrk[1][1] + T[0][2] * Vrk[1][2]) * dL_da +
-                        (T[1][0] * Vrk[1][0] + T[1][1] * Vrk[1][1] + T[1][2] * Vrk[1][2]) * dL_db;
-  const float dL_dT02 = 2 * (T[0][0] * Vrk[2][0] + T[0][1] * Vrk[2][1] + T[0][2] * Vrk[2][2]) * dL_da +
-                        (T[1][0] * Vrk[2][0] + T[1][1] * Vrk[2][1] + T[1][2] * Vrk[2][2]) * dL_db;
-  const float dL_dT10 = 2 * (T[1][0] * Vrk[0][0] + T[1][1] * Vrk[0][1] + T[1][2] * Vrk[0][2]) * dL_dc +
-                        (T[0][0] * Vrk[0][0] + T[0][1] * Vrk[0][1] + T[0][2] * Vrk[0][2]) * dL_db;
-  const float dL_dT11 = 2 * (T[1][0] * Vrk[1][0] + T[1][1] * Vrk[1][1] + T[1][2] * Vrk[1][2]) * dL_dc +
-                        (T[0][0] * Vrk[1][0] + T[0][1] * Vrk[1][1] + T[0][2] * Vrk[1][2]) * dL_db;
-  const float dL_dT12 = 2 * (T[1][0] * Vrk[2][0] + T[1][1] * Vrk[2][1] + T[1][2] * Vrk[2][2]) * dL_dc +
-                        (T[0][0] * Vrk[2][0] + T[0][1] * Vrk[2][1] + T[0][2] * Vrk[2][2]) * dL_db;
-  const float dL_dJ00 = W[0][0] * dL_dT00 + W[0][1] * dL_dT01 + W[0][2] * dL_dT02;
-  const float dL_dJ02 = W[2][0] * dL_dT00 + W[2][1] * dL_dT01 + W[2][2] * dL_dT02;
-  const float dL_dJ11 = W[1][0] * dL_dT10 + W[1][1] * dL_dT11 + W[1][2] * dL_dT12;
-  const float dL_dJ12 = W[2][0] * dL_dT10 + W[2][1] * dL_dT11 + W[2][2] * dL_dT12;
-  const float tz = 1.f / t.z;
-  const float tz2 = tz * tz;
-  const float tz3 = tz2 * tz;
-  const float dL_dtx = x_grad_mul * -h_x * tz2 * dL_dJ02;
-  const float dL_dty = y_grad_mul * -h_y * tz2 * dL_dJ12;
-  const float dL_dtz = -h_x * tz2 * dL_dJ00 - h_y * tz2 * dL_dJ11 + (2 * h_x * t.x) * tz3 * dL_dJ02 +
-                       (2 * h_y * t.y) * tz3 * dL_dJ12;
-  float3 dmean = xform_vec_t(make_float3(dL_dtx, dL_dty, dL_dtz), Vs);
 
-  // ---- screen-space mean part (reference backward.cu:374-391) ----
+  // Y = G_A T (2x3); G_Sigma = T^T Y; G_T = 2 Y Sigma
+  const float3 Y0 = lin2(g00, T0, g01, T1), Y1 = lin2(g01, T0, g11, T1);
+  Sym3 GS;
+  GS.xx = T0.x * Y0.x + T1.x * Y1.x;
+  GS.xy = T0.x * Y0.y + T1.x * Y1.y;
+  GS.xz = T0.x * Y0.z + T1.x * Y1.z;
+  GS.yy = T0.y * Y0.y + T1.y * Y1.y;
+  GS.yz = T0.y * Y0.z + T1.y * Y1.z;
+  GS.zz = T0.z * Y0.z + T1.z * Y1.z;
+  const float3 GT0 = sym_mul(Sg, Y0), GT1 = sym_mul(Sg, Y1);  // halves of the rows of G_T
+  // the four live entries of G_J = G_T W^T
+  const float gj00 = 2.f * dot3(GT0, w0), gj02 = 2.f * dot3(GT0, w2);
+  const float gj11 = 2.f * dot3(GT1, w1), gj12 = 2.f * dot3(GT1, w2);
+  const float dtx = free_x * -fx * iz2 * gj02;
+  const float dty = free_y * -fy * iz2 * gj12;
+  const float dtz = -iz2 * (fx * gj00 + fy * gj11) + 2.f * iz2 * iz * (fx * cx * gj02 + fy * cy * gj12);
+  float3 dm = make_float3(dtx * w0.x + dty * w1.x + dtz * w2.x, dtx * w0.y + dty * w1.y + dtz * w2.y,
+                          dtx * w0.z + dty * w1.z + dtz * w2.z);
+
+  // screen centre: p = (h.x, h.y) / (h.w + 1e-7), upstream already in NDC units
   {
     const float* gm2 = p.g_means2D + up * p.g_means2D_stride;
     const float gx = gm2[0], gy = gm2[1];
-    const float4 m_hom = xform_point4(mean, Ps);
-    const float m_w = 1.0f / (m_hom.w + 0.0000001f);
-    const float mul1 = (Ps[0] * mean.x + Ps[4] * mean.y + Ps[8] * mean.z + Ps[12]) * m_w * m_w;
-    const float mul2 = (Ps[1] * mean.x + Ps[5] * mean.y + Ps[9] * mean.z + Ps[13]) * m_w * m_w;
-    dmean.x += (Ps[0] * m_w - Ps[3] * mul1) * gx + (Ps[1] * m_w - Ps[3] * mul2) * gy;
-    dmean.y += (Ps[4] * m_w - Ps[7] * mul1) * gx + (Ps[5] * m_w - Ps[7] * mul2) * gy;
-    dmean.z += (Ps[8] * m_w - Ps[11] * mul1) * gx + (Ps[9] * m_w - Ps[11] * mul2) * gy;
+    const float4 h = xform_point4(m, Pm);
+    const float u = 1.0f / (h.w + 0.0000001f);
+    const float v = (gx * h.x + gy * h.y) * u * u;
+    const float3 px = mat_row(Pm, 0), py = mat_row(Pm, 1), pw = mat_row(Pm, 3);
+    dm.x += u * (gx * px.x + gy * py.x) - v * pw.x;
+    dm.y += u * (gx * px.y + gy * py.y) - v * pw.y;
+    dm.z += u * (gx * px.z + gy * py.z) - v * pw.z;
   }
 
-  // ---- SH colour part (reference backward.cu:20-141) ----
+  // SH colour through the unit direction d / |d|
   {
     ShRegs s;
     load_sh(f, i, f.M, s);
     bool clamp3[3];
-    (void)sh_to_rgb(f.D, mean, f.campos, s.dc, s.rest, clamp3);
+    (void)sh_to_rgb(f.D, m, f.campos, s.dc, s.rest, clamp3);
     const float* gc = p.g_colors + up * p.g_colors_stride;
     const float dR[3] = {clamp3[0] ? 0.f : gc[0], clamp3[1] ? 0.f : gc[1], clamp3[2] ? 0.f : gc[2]};
-    const float3 dir_orig = make_float3(mean.x - f.campos[0], mean.y - f.campos[1], mean.z - f.campos[2]);
-    const float len = sqrtf(dir_orig.x * dir_orig.x + dir_orig.y * dir_orig.y + dir_orig.z * dir_orig.z);
-    const float x = dir_orig.x / len, y = dir_orig.y / len, z = dir_orig.z / len;
-    const int D = f.D;
-    float dsh[45];
-#pragma unroll
-    for (int k = 0; k < 45; ++k) dsh[k] = 0.f;
-    float ddx[3] = {0.f, 0.f, 0.f}, ddy[3] = {0.f, 0.f, 0.f}, ddz[3] = {0.f, 0.f, 0.f};
-#pragma unroll
-    for (int ch = 0; ch < 3; ++ch) out.dc[ch] = kSH0 * dR[ch];
-    if (D > 0) {
-      const float b1 = -kSH1 * y, b2 = kSH1 * z, b3 = -kSH1 * x;
-#pragma unroll
-      for (int ch = 0; ch < 3; ++ch) {
-        const float* sh = s.rest;
-        dsh[0 * 3 + ch] = b1 * dR[ch];
-        dsh[1 * 3 + ch] = b2 * dR[ch];
-        dsh[2 * 3 + ch] = b3 * dR[ch];
-        ddx[ch] = -kSH1 * sh[2 * 3 + ch];
-        ddy[ch] = -kSH1 * sh[0 * 3 + ch];
-        ddz[ch] = kSH1 * sh[1 * 3 + ch];
-      }
-      if (D > 1) {
-        const float xx = x * x, yy = y * y, zz = z * z;
-        const float xy = x * y, yz = y * z, xz = x * z;
-        const float b4 = kSH2[0] * xy, b5 = kSH2[1] * yz, b6 = kSH2[2] * (2.f * zz - xx - yy),
-                    b7 = kSH2[3] * xz, b8 = kSH2[4] * (xx - yy);
-#pragma unroll
-        for (int ch = 0; ch < 3; ++ch) {
-          const float* sh = s.rest;
-          dsh[3 * 3 + ch] = b4 * dR[ch];
-          dsh[4 * 3 + ch] = b5 * dR[ch];
-          dsh[5 * 3 + ch] = b6 * dR[ch];
-          dsh[6 * 3 + ch] = b7 * dR[ch];
-          dsh[7 * 3 + ch] = b8 * dR[ch];
-          ddx[ch] += kSH2[0] * y * sh[3 * 3 + ch] + kSH2[2] * 2.f * -x * sh[5 * 3 + ch] +
-                     kSH2[3] * z * sh[6 * 3 + ch] + kSH2[4] * 2.f * x * sh[7 * 3 + ch];
-          ddy[ch] += kSH2[0] * x * sh[3 * 3 + ch] + kSH2[1] * z * sh[4 * 3 + ch] +
-                     kSH2[2] * 2.f * -y * sh[5 * 3 + ch] + kSH2[4] * 2.f * -y * sh[7 * 3 + ch];
-          ddz[ch] += kSH2[1] * y * sh[4 * 3 + ch] + kSH2[2] * 2.f * 2.f * z * sh[5 * 3 + ch] +
-                     kSH2[3] * x * sh[6 * 3 + ch];
-        }
-        if (D > 2) {
-          const float b9 = kSH3[0] * y * (3.f * xx - yy), b10 = kSH3[1] * xy * z,
-                      b11 = kSH3[2] * y * (4.f * zz - xx - yy),
-                      b12 = kSH3[3] * z * (2.f * zz - 3.f * xx - 3.f * yy),
-                      b13 = kSH3[4] * x * (4.f * zz - xx - yy), b14 = kSH3[5] * z * (xx - yy),
-                      b15 = kSH3[6] * x * (xx - 3.f * yy);
-#pragma unroll
-          for (int ch = 0; ch < 3; ++ch) {
-            const float* sh = s.rest;
-            dsh[8 * 3 + ch] = b9 * dR[ch];
-            dsh[9 * 3 + ch] = b10 * dR[ch];
-            dsh[10 * 3 + ch] = b11 * dR[ch];
-            dsh[11 * 3 + ch] = b12 * dR[ch];
-            dsh[12 * 3 + ch] = b13 * dR[ch];
-            dsh[13 * 3 + ch] = b14 * dR[ch];
-            dsh[14 * 3 + ch] = b15 * dR[ch];
-            ddx[ch] += (kSH3[0] * sh[8 * 3 + ch] * 3.f * 2.f * xy + kSH3[1] * sh[9 * 3 + ch] * yz +
-                        kSH3[2] * sh[10 * 3 + ch] * -2.f * xy + kSH3[3] * sh[11 * 3 + ch] * -3.f * 2.f * xz +
-                        kSH3[4] * sh[12 * 3 + ch] * (-3.f * xx + 4.f * zz - yy) +
-                        kSH3[5] * sh[13 * 3 + ch] * 2.f * xz + kSH3[6] * sh[14 * 3 + ch] * 3.f * (xx - yy));
-            ddy[ch] += (kSH3[0] * sh[8 * 3 + ch] * 3.f * (xx - yy) + kSH3[1] * sh[9 * 3 + ch] * xz +
-                        kSH3[2] * sh[10 * 3 + ch] * (-3.f * yy + 4.f * zz - xx) +
-                        kSH3[3] * sh[11 * 3 + ch] * -3.f * 2.f * yz + kSH3[4] * sh[12 * 3 + ch] * -2.f * xy +
-                        kSH3[5] * sh[13 * 3 + ch] * -2.f * yz + kSH3[6] * sh[14 * 3 + ch] * -3.f * 2.f * xy);
-            ddz[ch] += (kSH3[1] * sh[9 * 3 + ch] * xy + kSH3[2] * sh[10 * 3 + ch] * 4.f * 2.f * yz +
-                        kSH3[3] * sh[11 * 3 + ch] * 3.f * (2.f * zz - xx - yy) +
-                        kSH3[4] * sh[12 * 3 + ch] * 4.f * 2.f * xz + kSH3[5] * sh[13 * 3 + ch] * (xx - yy));
-          }
-        }
-      }
-    }
-    #pragma unroll
-    for (int k = 0; k < 45; ++k) out.rest[k] = (k < f.M * 3) ? dsh[k] : 0.f;
-    const float3 ddir = make_float3(ddx[0] * dR[0] + ddx[1] * dR[1] + ddx[2] * dR[2],
-                                    ddy[0] * dR[0] + ddy[1] * dR[1] + ddy[2] * dR[2],
-                                    ddz[0] * dR[0] + ddz[1] * dR[1] + ddz[2] * dR[2]);
-    const float3 dm = dnorm3(dir_orig, ddir);
-    dmean.x += dm.x;
-    dmean.y += dm.y;
-    dmean.z += dm.z;
+    const float3 d = make_float3(m.x - f.campos[0], m.y - f.campos[1], m.z - f.campos[2]);
+    const float len = sqrtf(d.x * d.x + d.y * d.y + d.z * d.z);
+    const float3 dir = make_float3(d.x / len, d.y / len, d.z / len);
+    const float3 gu = sh_backward(f.D, dir, s, dR, out);
+    // d(d/|d|)/dd = (I - dir dir^T) / |d|
+    const float proj = dot3(dir, gu);
+    dm.x += (gu.x - dir.x * proj) / len;
+    dm.y += (gu.y - dir.y * proj) / len;
+    dm.z += (gu.z - dir.z * proj) / len;
   }
-  out.mean[0] = dmean.x;
-  out.mean[1] = dmean.y;
-  out.mean[2] = dmean.z;
+  out.mean[0] = dm.x;
+  out.mean[1] = dm.y;
+  out.mean[2] = dm.z;
 
-  // ---- scale / rotation part (reference backward.cu:280-343) ----
+  // scale and quaternion: G_L = 2 G_Sigma L, G_R = G_L S
   {
-    const float r = q.x, x = q.y, y = q.z, z = q.w;
-    M3 R = make_m3(1.f - 2.f * (y * y + z * z), 2.f * (x * y - r * z), 2.f * (x * z + r * y),
-                   2.f * (x * y + r * z), 1.f - 2.f * (x * x + z * z), 2.f * (y * z - r * x),
-                   2.f * (x * z - r * y), 2.f * (y * z + r * x), 1.f - 2.f * (x * x + y * y));
-    const float s0 = f.scale_modifier * sx, s1 = f.scale_modifier * sy, s2 = f.scale_modifier * sz;
-    M3 S = make_m3(1.f, 0.f, 0.f, 0.f, 1.f, 0.f, 0.f, 0.f, 1.f);
-    S.m[0][0] = s0;
-    S.m[1][1] = s1;
-    S.m[2][2] = s2;
-    M3 Mm = m3_mul(S, R);
-    M3 dSig = make_m3(dcov[0], 0.5f * dcov[1], 0.5f * dcov[2], 0.5f * dcov[1], dcov[3],
-                      0.5f * dcov[4], 0.5f * dcov[2], 0.5f * dcov[4], dcov[5]);
-    M3 twoM;
+    float GR[3][3];
 #pragma unroll
-    for (int cc = 0; cc < 3; ++cc)
-#pragma unroll
-      for (int rr = 0; rr < 3; ++rr) twoM.m[cc][rr] = 2.0f * Mm.m[cc][rr];
-    M3 dM = m3_mul(twoM, dSig);
-    M3 Rt = m3_t(R);
-    M3 dMt = m3_t(dM);
-    out.scale[0] = Rt[0][0] * dMt[0][0] + Rt[0][1] * dMt[0][1] + Rt[0][2] * dMt[0][2];
-    out.scale[1] = Rt[1][0] * dMt[1][0] + Rt[1][1] * dMt[1][1] + Rt[1][2] * dMt[1][2];
-    out.scale[2] = Rt[2][0] * dMt[2][0] + Rt[2][1] * dMt[2][1] + Rt[2][2] * dMt[2][2];
-#pragma unroll
-    for (int rr = 0; rr < 3; ++rr) {
-      dMt.m[0][rr] *= s0;
-      dMt.m[1][rr] *= s1;
-      dMt.m[2][rr] *= s2;
+    for (int j = 0; j < 3; ++j) {
+      const float3 gl = sym_mul(GS, make_float3(Lm[0][j], Lm[1][j], Lm[2][j]));  // column j of G_Sigma L
+      out.scale[j] = 2.f * (Rm[0][j] * gl.x + Rm[1][j] * gl.y + Rm[2][j] * gl.z);
+      GR[0][j] = 2.f * gl.x * sm[j];
+      GR[1][j] = 2.f * gl.y * sm[j];
+      GR[2][j] = 2.f * gl.z * sm[j];
     }
-    float4 dq;
-    dq.x = 2 * z * (dMt[0][1] - dMt[1][0]) + 2 * y * (dMt[2][0] - dMt[0][2]) + 2 * x * (dMt[1][2] - dMt[2][1]);
-    dq.y = 2 * y * (dMt[1][0] + dMt[0][1]) + 2 * z * (dMt[2][0] + dMt[0][2]) + 2 * r * (dMt[1][2] - dMt[2][1]) -
-           4 * x * (dMt[2][2] + dMt[1][1]);
-    dq.z = 2 * x * (dMt[1][0] + dMt[0][1]) + 2 * r * (dMt[2][0] - dMt[0][2]) + 2 * z * (dMt[1][2] + dMt[2][1]) -
-           4 * y * (dMt[2][2] + dMt[0][0]);
-    dq.w = 2 * r * (dMt[0][1] - dMt[1][0]) + 2 * x * (dMt[2][0] + dMt[0][2]) + 2 * y * (dMt[1][2] + dMt[2][1]) -
-           4 * z * (dMt[1][1] + dMt[0][0]);
-    out.rot = dq;
+    // dR/dq for R(q) above, contracted with G_R
+    const float s01 = GR[0][1] + GR[1][0], s02 = GR[0][2] + GR[2][0], s12 = GR[1][2] + GR[2][1];
+    const float d10 = GR[1][0] - GR[0][1], d02 = GR[0][2] - GR[2][0], d21 = GR[2][1] - GR[1][2];
+    out.rot.x = 2.f * (qz * d10 + qy * d02 + qx * d21);
+    out.rot.y = 2.f * (qy * s01 + qz * s02 + qr * d21) - 4.f * qx * (GR[1][1] + GR[2][2]);
+    out.rot.z = 2.f * (qx * s01 + qr * d02 + qz * s12) - 4.f * qy * (GR[0][0] + GR[2][2]);
+    out.rot.w = 2.f * (qr * d10 + qx * s02 + qy * s12) - 4.f * qz * (GR[0][0] + GR[1][1]);
   }
   out.op = gco.w;
   if (f.raw) {
@@ -955,7 +947,7 @@ __device__ __forceinline__ void bwd_compute(const PreprocessBwdParams& p, int64_
     out.scale[0] *= sx;
     out.scale[1] *= sy;
     out.scale[2] *= sz;
-    const float4 g = out.rot;
+    const float4 g = out.rot, q = act.q;
     if (act.nrm > 1e-12f) {
       const float dot = q.x * g.x + q.y * g.y + q.z * g.z + q.w * g.w;
       out.rot = make_float4((g.x - q.x * dot) / act.nrm, (g.y - q.y * dot) / act.nrm, (g.z - q.z * dot) / act.nrm,

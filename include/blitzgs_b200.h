@@ -269,7 +269,10 @@ int blitz_render_blend(int64_t P, int image_height, int image_width, const float
  * blitz_render_scratch_bytes() exceed it fail with BLITZ_ESCRATCH.  All calls
  * on a device share the array: calls that overlap on the GPU race.  The first
  * call on a device resolves the array's address (make it before any stream
- * capture).  Allocates nothing.
+ * capture) and caches it for the process: it is the address in the device's
+ * primary context (the CUDA runtime's and PyTorch's), so callers that use a
+ * context of their own, or reset the device within the process, must not use
+ * this entry point.  Allocates nothing.
  */
 #define BLITZ_NOALLOC_SCRATCH_BYTES (64u << 20)
 int blitz_render_bin_noalloc(int64_t P, int64_t n_vis, int64_t R, int image_height, int image_width,

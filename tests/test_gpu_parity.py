@@ -522,3 +522,67 @@ def test_exchange_unpack_and_gradient_pack(cuda_device):
     assert torch.equal(got[0:40], want[0:40]) and torch.equal(got[300:423], want[40:163])
     assert torch.equal(got[600:661], want[163:224])
     assert torch.all(got[40:300] == -7.0) and torch.all(got[423:600] == -7.0)
+
+
+def test_preprocess_backward_matches_finite_differences(cuda_device):
+    """The preprocess backward against central differences of the preprocess
+    forward kernel itself.  Every Gaussian is independent, so one parameter
+    component of all Gaussians is perturbed at once and each Gaussian's own
+    scalar L_i = <means2D_i, g_m> + <conic_i, g_c (x2 off-diagonal)> +
+    <rgb_i, g_rgb> is differenced.  Float32 forward outputs and a step of
+    1e-3 (relative for scales) bound the agreement at ~1e-3 normwise."""
+    dev = cuda_device
+    sc = S.tiny(seed=4, P=600, H=96, W=128)
+    cam = sc.cameras[0]
+    rs = _raster(cam.to(dev), dev)
+    xyz, s, q, shs, o = [t.to(dev) for t in activated(sc)]
+    o = o.reshape(-1)
+    P = xyz.shape[0]
+    gen = torch.Generator().manual_seed(8)
+    gm = torch.randn(P, 2, generator=gen).to(dev)
+    gc = torch.randn(P, 4, generator=gen).to(dev)
+    gr = torch.randn(P, 3, generator=gen).to(dev)
+    w3 = torch.tensor([1.0, 2.0, 1.0], dtype=torch.float64, device=dev)
+
+    def fwd(xyz_, s_, q_, shs_):
+        m2, d, r, co, rgb, _, cl = ops.preprocess_forward(xyz_, s_, q_, o, ops.sh_layout(shs=shs_), rs,
+                                                          want_clamped=True)
+        L = ((m2.double() * gm.double()).sum(1) + (co[:, :3].double() * gc[:, :3].double() * w3).sum(1) +
+             (rgb.double() * gr.double()).sum(1))
+        return L, r, cl
+
+    L0, r0, cl0 = fwd(xyz, s, q, shs)
+    dm, ds, dq, _, dsh = ops.preprocess_backward(r0, xyz, s, q, ops.sh_layout(shs=shs), rs, gm, gc, gr)
+    keep = r0 > 0
+    # outside +-1.3 tan(fov) the operator contract holds the clamped centre
+    # constant (not the derivative of the clamp): leave those out
+    t = torch.cat([xyz, torch.ones(P, 1, device=dev)], 1) @ rs.viewmatrix
+    keep &= ((t[:, 0] / t[:, 2]).abs() < 0.99 * 1.3 * rs.tanfovx) & ((t[:, 1] / t[:, 2]).abs() < 0.99 * 1.3 * rs.tanfovy)
+    analytic, numeric = [], []
+    for which, base, grad, rel in (("xyz", xyz, dm, False), ("scale", s, ds, True), ("rot", q, dq, False),
+                                   ("sh", shs.reshape(P, -1), dsh.reshape(P, -1), False)):
+        for c in range(base.shape[1]):
+            step = (1e-3 * base[:, c].abs()) if rel else torch.full((P,), 1e-3, device=dev)
+            outs = []
+            for sign in (1.0, -1.0):
+                pert = base.clone()
+                pert[:, c] += sign * step
+                if which == "xyz":
+                    args = (pert, s, q, shs)
+                elif which == "scale":
+                    args = (xyz, pert, q, shs)
+                elif which == "rot":
+                    args = (xyz, s, pert, shs)
+                else:
+                    args = (xyz, s, q, pert.reshape(shs.shape))
+                L, r, cl = fwd(*args)
+                outs.append(L)
+                # a Gaussian that crosses the cull or a colour clamp is not differentiable there
+                keep &= (r > 0) & (cl == cl0).all(1)
+            numeric.append((outs[0] - outs[1]) / (2.0 * step.double()))
+            analytic.append(grad[:, c].double())
+    A = torch.stack(analytic, 1)[keep]
+    N = torch.stack(numeric, 1)[keep]
+    assert keep.sum() > 100
+    err = normwise_rel(A.cpu(), N.cpu())
+    assert err <= 2e-3, f"finite differences: normwise relative error {err:.3e}"

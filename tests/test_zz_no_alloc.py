@@ -69,6 +69,31 @@ def test_noalloc_binning_matches_caller_scratch_twice(cuda_device):
         assert np.array_equal(a_rg, b_rg)
 
 
+@pytest.mark.gpu
+def test_noalloc_call_allocates_no_device_memory(cuda_device):
+    """The promise itself: once the library is loaded, a call takes no device
+    memory from the driver (free memory unchanged) and none from PyTorch's
+    allocator."""
+    x = _binning_inputs(S.tiny(seed=43, P=8000, H=160, W=208), cuda_device)
+    gx, gy = (x["W"] + 15) // 16, (x["H"] + 15) // 16
+    pl = torch.empty((max(x["R"], 1),), dtype=torch.int32, device=cuda_device)
+    ranges = torch.empty((gx * gy, 2), dtype=torch.int32, device=cuda_device)
+    args = (x["P"], x["n_vis"], x["R"], x["H"], x["W"], ptr(x["m2"]), ptr(x["d"]), ptr(x["r"]), None,
+            ptr(x["counts"]), ptr(pl), ptr(ranges), _lib.stream_ptr())
+    _lib.call("blitz_render_bin_noalloc", *args)  # first call on the device: resolves the array's address
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info(cuda_device)
+    stats0 = torch.cuda.memory_stats(cuda_device)
+    for _ in range(3):
+        _lib.call("blitz_render_bin_noalloc", *args)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info(cuda_device)
+    stats1 = torch.cuda.memory_stats(cuda_device)
+    assert free1 == free0, f"device free memory changed by {free0 - free1} bytes"
+    for k in ("allocated_bytes.all.current", "num_alloc_retries", "num_device_alloc"):
+        assert stats1.get(k, 0) == stats0.get(k, 0), k
+
+
 def test_noalloc_rejects_requests_beyond_its_fixed_scratch():
     """Checked on the host before any launch, so no GPU is needed."""
     lib = _lib.load()
