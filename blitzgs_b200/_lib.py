@@ -26,7 +26,15 @@ SIGNATURES = {
         _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _f32, _vp, _vp, _vp, _f32, _f32,
         _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "blitz_preprocess_scratch_bytes": (_sz, [_i64]),
-    "blitz_exchange_pack": (_i32, [_i64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _vp]),
+    "blitz_exchange_pack_scratch_bytes": (_sz, [_i64, _i32]),
+    "blitz_exchange_pack": (_i32, [_i64, _i32, _vp, _vp, _vp, _vp, _vp, _i32, _vp, _sz, _vp]),
+    "blitz_exchange_pack_batch": (_i32, [_i32, _i32, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "blitz_preprocess_forward_raw_batch": (_i32, [
+        _i32, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _f32, _vp, _vp, _vp, _vp, _i32, _i32,
+        _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "blitz_preprocess_backward_raw_batch": (_i32, [
+        _i32, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _i32, _i64, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _f32,
+        _vp, _vp, _vp, _vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _vp]),
     "blitz_get_local2j_ids_bool_adjust_mode6": (_i32, [_i32, _i32, _i32, _i32, _i64, _vp, _vp, _vp, _i32, _vp,
                                                         _vp]),
     "blitz_adam_update": (_i32, [_vp, _vp, _vp, _vp, _vp, _f32, _f32, _f32, _f32, _i64, _i64, _vp]),
@@ -53,7 +61,7 @@ SIGNATURES = {
     "blitz_fp32_probe": (_i32, [_i32, _i64, _vp, _vp]),
     "blitz_loss_combine": (_i32, [_vp, _vp, _f32, _f32, _f32, _f32, _vp, _vp]),
     "blitz_loss_combine_backward": (_i32, [_vp, _vp, _vp, _vp, _f32, _f32, _f32, _f32, _vp, _vp]),
-    "blitz_read_totals": (_i32, [_vp, _vp, _vp, _vp, _vp]),
+    "blitz_read_totals": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "blitz_zero_fill_async": (_i32, [_i32, _vp, _vp, _vp]),
     "blitz_zero_fill_wait": (_i32, [_vp]),
     "blitz_exchange_unpack": (_i32, [_i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),

@@ -189,6 +189,9 @@ int blitz_preprocess_forward_raw(int64_t P, int D, int M, const float* xyz, cons
       return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: exchange outputs need vis_list, n_ranks <= 32 and "
                                 "non-null buffers");
     if (!aligned16(x.records)) return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: records must be 16-byte aligned");
+    // the exchange must keep one order on every run: list in index order
+    if (!scratch) return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: exchange outputs need the scratch");
+    p.ordered_list = true;
     p.x_ranks = x.n_ranks;
     p.x_tile_lo = x.tile_lo;
     p.x_tile_hi = x.tile_hi;
@@ -559,25 +562,124 @@ int blitz_adam_update_rows(float* param, const float* grad_rows, float* exp_avg,
   return check(launch_adam(a, S(stream)), "blitz_adam_update_rows");
 }
 
+size_t blitz_exchange_pack_scratch_bytes(int64_t n_rows, int n_ranks) {
+  return exchange_pack_scratch_bytes(n_rows, n_ranks);
+}
+
 int blitz_exchange_pack(int64_t n_rows, int n_ranks, const float* records, const uint32_t* dest_mask,
-                        const int64_t* dest_offset, int32_t* cursor, float* send, int32_t* send_row,
-                        int32_t row_base, void* stream) {
+                        const int64_t* dest_offset, float* send, int32_t* send_row, int32_t row_base, void* scratch,
+                        size_t scratch_bytes, void* stream) {
   if (n_rows < 0 || n_ranks <= 0 || n_ranks > 32) return fail(BLITZ_EINVAL, "blitz_exchange_pack: bad sizes");
   if (n_rows == 0) return 0;
-  if (!records || !dest_mask || !dest_offset || !cursor || !send || !send_row)
+  if (!records || !dest_mask || !dest_offset || !send || !send_row || !scratch)
     return fail(BLITZ_EINVAL, "blitz_exchange_pack: null pointer");
   if (!aligned16(records) || !aligned16(send)) return fail(BLITZ_EINVAL, "blitz_exchange_pack: 16-byte alignment");
+  if (scratch_bytes < exchange_pack_scratch_bytes(n_rows, n_ranks))
+    return fail(BLITZ_ESCRATCH, "blitz_exchange_pack: scratch smaller than blitz_exchange_pack_scratch_bytes");
   PackParams k{};
   k.n_rows = n_rows;
   k.n_ranks = n_ranks;
   for (int r = 0; r < n_ranks; ++r) k.dest_offset[r] = dest_offset[r];
   k.records = records;
   k.mask = dest_mask;
-  k.cursor = cursor;
   k.send = send;
   k.send_row = send_row;
   k.row_base = row_base;
-  return check(launch_exchange_pack(k, S(stream)), "blitz_exchange_pack");
+  return check(launch_exchange_pack(k, scratch, S(stream)), "blitz_exchange_pack");
+}
+
+int blitz_exchange_pack_batch(int n_cams, int n_ranks, const int64_t* n_rows, int64_t cam_stride,
+                              const float* records, const uint32_t* dest_mask, const int64_t* dest_offset,
+                              const int64_t* row_base, float* send, int32_t* send_row, void* scratch,
+                              size_t scratch_bytes, void* stream) {
+  if (n_cams < 0 || n_ranks <= 0 || n_ranks > 32 || cam_stride < 0)
+    return fail(BLITZ_EINVAL, "blitz_exchange_pack_batch: bad sizes");
+  if (n_cams == 0) return 0;
+  if (!n_rows || !dest_offset || !row_base) return fail(BLITZ_EINVAL, "blitz_exchange_pack_batch: null pointer");
+  for (int c = 0; c < n_cams; ++c) {
+    if (n_rows[c] < 0 || n_rows[c] > cam_stride || row_base[c] < 0 || row_base[c] > 0x7fffffff)
+      return fail(BLITZ_EINVAL, "blitz_exchange_pack_batch: bad rows");
+    const int rc = blitz_exchange_pack(n_rows[c], n_ranks, records ? records + 12 * c * cam_stride : nullptr,
+                                       dest_mask ? dest_mask + c * cam_stride : nullptr, dest_offset + c * n_ranks,
+                                       send, send_row, (int32_t)row_base[c], scratch, scratch_bytes, stream);
+    if (rc) return rc;
+  }
+  return 0;
+}
+
+int blitz_preprocess_forward_raw_batch(int n_cams, int64_t P, int D, int M, const float* xyz,
+                                       const float* scaling_raw, const float* rotation_raw, const float* opacity_raw,
+                                       const float* sh_dc, int64_t dc_stride, const float* sh_rest,
+                                       int64_t rest_stride, float scale_modifier, const float* viewmatrices,
+                                       const float* projmatrices, const float* campos, const float* tanfov,
+                                       int image_height, int image_width, int64_t cam_stride, float* means2D,
+                                       float* depths, int32_t* radii, float* conic_opacity, float* rgb,
+                                       uint32_t* vis_list, int32_t* counts, int n_ranks, const int32_t* tile_bounds,
+                                       float* records, uint32_t* dest_mask, void* scratch, size_t scratch_bytes,
+                                       void* stream) {
+  if (n_cams < 0 || n_ranks < 0 || n_ranks > 32 || cam_stride < P)
+    return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw_batch: bad sizes");
+  if (n_cams == 0 || P == 0) return 0;
+  if (!viewmatrices || !projmatrices || !campos || !tanfov || !vis_list || !counts || !scratch)
+    return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw_batch: null pointer");
+  if (n_ranks > 0 && (!tile_bounds || !records || !dest_mask))
+    return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw_batch: exchange outputs need tile_bounds, records, "
+                              "dest_mask");
+  if ((cam_stride & 3) != 0) return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw_batch: cam_stride % 4");
+  const int cs = 1 + n_ranks;
+  for (int c = 0; c < n_cams; ++c) {
+    blitz_exchange_out x{};
+    x.n_ranks = n_ranks;
+    if (n_ranks > 0) {
+      x.tile_lo = tile_bounds + (int64_t)c * 2 * n_ranks;
+      x.tile_hi = tile_bounds + (int64_t)c * 2 * n_ranks + n_ranks;
+      x.records = records + 12 * c * cam_stride;
+      x.dest_mask = dest_mask + c * cam_stride;
+      x.dest_counts = counts + (int64_t)c * cs + 1;
+    }
+    const int64_t o = c * cam_stride;
+    const int rc = blitz_preprocess_forward_raw(
+        P, D, M, xyz, scaling_raw, rotation_raw, nullptr, opacity_raw, sh_dc, dc_stride, sh_rest, rest_stride,
+        scale_modifier, viewmatrices + 16 * c, projmatrices + 16 * c, campos + 3 * c, tanfov[2 * c],
+        tanfov[2 * c + 1], image_height, image_width, means2D + 2 * o, depths + o, radii + o, conic_opacity + 4 * o,
+        rgb + 3 * o, nullptr, vis_list + o, counts + (int64_t)c * cs, nullptr, nullptr, nullptr, nullptr,
+        n_ranks > 0 ? &x : nullptr, scratch, scratch_bytes, stream);
+    if (rc) return rc;
+  }
+  return 0;
+}
+
+int blitz_preprocess_backward_raw_batch(int n_cams, int64_t P, int D, int M, const int32_t* radii,
+                                        const float* means2D, const uint32_t* vis_list, const int32_t* counts,
+                                        int counts_stride, int64_t cam_stride, const float* xyz,
+                                        const float* scaling_raw, const float* rotation_raw,
+                                        const float* opacity_raw, const float* sh_dc, int64_t dc_stride,
+                                        const float* sh_rest, int64_t rest_stride, float scale_modifier,
+                                        const float* viewmatrices, const float* projmatrices, const float* campos,
+                                        const float* tanfov, int image_height, int image_width,
+                                        const float* upstream, const int64_t* upstream_row0, float* g_xyz,
+                                        float* g_scaling_raw, float* g_rotation_raw, float* g_opacity_raw,
+                                        float* g_dc, int64_t g_dc_stride, float* g_rest, int64_t g_rest_stride,
+                                        void* stream) {
+  if (n_cams < 0 || counts_stride < 1 || cam_stride < P)
+    return fail(BLITZ_EINVAL, "blitz_preprocess_backward_raw_batch: bad sizes");
+  if (n_cams == 0 || P == 0) return 0;
+  if (!viewmatrices || !projmatrices || !campos || !tanfov || !vis_list || !counts || !upstream || !upstream_row0)
+    return fail(BLITZ_EINVAL, "blitz_preprocess_backward_raw_batch: null pointer");
+  if (!aligned16(upstream)) return fail(BLITZ_EINVAL, "blitz_preprocess_backward_raw_batch: upstream alignment");
+  for (int c = 0; c < n_cams; ++c) {
+    if (upstream_row0[c] < 0) return fail(BLITZ_EINVAL, "blitz_preprocess_backward_raw_batch: bad upstream row");
+    const int64_t o = c * cam_stride;
+    const float* u = upstream + 12 * upstream_row0[c];
+    const int rc = blitz_preprocess_backward_raw(
+        P, D, M, radii + o, means2D + 2 * o, xyz, scaling_raw, rotation_raw, nullptr, opacity_raw, sh_dc, dc_stride,
+        sh_rest, rest_stride, scale_modifier, viewmatrices + 16 * c, projmatrices + 16 * c, campos + 3 * c,
+        tanfov[2 * c], tanfov[2 * c + 1], image_height, image_width, u + 4, 12, u + 0, 12, u + 6, 12, nullptr,
+        u + 11, 12, vis_list + o, counts + (int64_t)c * counts_stride, g_xyz, g_scaling_raw, g_rotation_raw,
+        g_opacity_raw, g_dc, g_dc_stride, g_rest, g_rest_stride, 1, BLITZ_ROWS_UPSTREAM_BY_SLOT, stream);
+    if (rc) return rc;
+  }
+  return 0;
 }
 
 }  // extern "C"
@@ -655,14 +757,26 @@ int blitz_loss_combine_backward(const float* g_loss, const float* g_l1, const fl
   return check(launch_loss_combine_bwd(p, g_loss, g_l1, g_ss, scales, S(stream)), "blitz_loss_combine_backward");
 }
 
-int blitz_read_totals(const int64_t* totals, const int32_t* vis_count, int64_t* host_totals, int32_t* host_vis,
-                      void* stream) {
-  if (!totals || !host_totals || ((vis_count == nullptr) != (host_vis == nullptr)))
+int blitz_read_totals(const int64_t* totals, const int32_t* vis_count, const uint32_t* status, int64_t* host_totals,
+                      int32_t* host_vis, uint32_t* host_status, void* stream) {
+  if (!totals || !host_totals || ((vis_count == nullptr) != (host_vis == nullptr)) ||
+      ((status == nullptr) != (host_status == nullptr)))
     return fail(BLITZ_EINVAL, "blitz_read_totals: bad arguments");
   cudaError_t e = cudaMemcpyAsync(host_totals, totals, 2 * sizeof(int64_t), cudaMemcpyDeviceToHost, S(stream));
   if (e == cudaSuccess && vis_count)
     e = cudaMemcpyAsync(host_vis, vis_count, sizeof(int32_t), cudaMemcpyDeviceToHost, S(stream));
+  if (e == cudaSuccess && status)
+    e = cudaMemcpyAsync(host_status, status, sizeof(uint32_t), cudaMemcpyDeviceToHost, S(stream));
   if (e == cudaSuccess) e = cudaStreamSynchronize(S(stream));
+  if (e == cudaSuccess && status && *host_status) {
+    const unsigned bits = *host_status;
+    e = cudaMemsetAsync(const_cast<uint32_t*>(status), 0, sizeof(uint32_t), S(stream));
+    if (e == cudaSuccess) {
+      char msg[160];
+      snprintf(msg, sizeof(msg), "blitz_read_totals: an ordered scan gave up waiting (status 0x%x)", bits);
+      return fail(BLITZ_ESCAN, msg);
+    }
+  }
   return check((int)e, "blitz_read_totals");
 }
 

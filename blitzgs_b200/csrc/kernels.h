@@ -45,7 +45,8 @@ struct PreprocessParams {
   bool raw;
   const float* rot_norm;     // raw mode: ||_rotation|| per Gaussian, or null = computed here
   double* reg_sums;          // raw mode, optional: {sum min-axis scale, count} over regulariser-visible
-  uint32_t* vis_list_out;    // optional [P]: indices of Gaussians with radius > 0 (unordered)
+  uint32_t* vis_list_out;    // optional [P]: indices of Gaussians with radius > 0
+  bool ordered_list;         // two-kernel form: vis_list_out in ascending index order (ordered scans)
   int* vis_count_out;        // device counter for vis_list_out, zero on entry
   // Optional first pass of the binning, fused: per-Gaussian tile counts under
   // the compute_locally mask and the totals {tile instances, Gaussians with a
@@ -103,7 +104,11 @@ struct PreprocessBwdParams {
 };
 
 // scratch (may be null): preprocess_scratch_bytes(P) bytes select the
-// two-kernel form (cull pass + full pass over the candidates).
+// two-kernel form (cull pass + full pass over the candidates), whose visible
+// list is in ascending index order when p.ordered_list is set.  The uint32 at byte kPreStatusOffset of
+// the scratch collects scan.cuh status bits; the launcher never clears it
+// (the caller zeroes a new buffer and reads / clears the word).
+constexpr size_t kPreStatusOffset = 0;
 size_t preprocess_scratch_bytes(int64_t P);
 int launch_preprocess_fwd(const PreprocessParams& p, cudaStream_t st, void* scratch = nullptr,
                           size_t scratch_bytes = 0);
@@ -264,12 +269,18 @@ struct PackParams {
   int64_t dest_offset[32];
   const float* records;  // [n_rows,12]
   const uint32_t* mask;  // [n_rows]
-  int* cursor;
   float* send;           // [*,12]
   int* send_row;         // [*]
   int row_base;
+  // set by the launcher from its scratch
+  int* ticket;
+  unsigned long long* scan_state;
+  unsigned* status;
 };
-int launch_exchange_pack(const PackParams& p, cudaStream_t st);
+// Scratch of one pack launch: a status word (bytes [0,4), never cleared by
+// the launcher), a ticket and the ordered-scan state (cleared per launch).
+size_t exchange_pack_scratch_bytes(int64_t n_rows, int n_ranks);
+int launch_exchange_pack(PackParams p, void* scratch, cudaStream_t st);
 
 // Received exchange records of one camera: up to kMaxSegments runs of rows
 // [seg_start[s], seg_start[s] + seg_count[s]) of a [*,12] buffer, taken in

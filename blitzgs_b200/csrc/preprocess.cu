@@ -21,6 +21,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "scan.cuh"
 
 namespace blitz {
 
@@ -397,10 +398,14 @@ __device__ __forceinline__ void cull_phase(const PreprocessParams& p, const floa
 // Phase B for one Gaussian (valid) or a filler lane: full computation, the
 // fused tile count and regulariser, the block-aggregated visible-list slot
 // (three barriers: every thread of the block must call this together), and
-// the row stores.
+// the row stores.  With scan_state the block's slots follow the ordered
+// prefix of the listed counts of the rounds before `round` (the list keeps
+// the candidates' order); without it they come from one atomic per block.
 __device__ __forceinline__ void full_phase(const PreprocessParams& p, const float* Vs, const float* Ps,
                                            const CullBound& cb, int64_t i, bool valid, const bool* s_mask,
-                                           bool use_smem, int* s_wc, int* s_base, FwdAcc& acc) {
+                                           bool use_smem, int* s_wc, int* s_base, FwdAcc& acc,
+                                           int64_t round = -1, unsigned long long* scan_state = nullptr,
+                                           unsigned* status = nullptr) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   PreResult res;
   preprocess_one(p, Vs, Ps, cb, i, res);
@@ -437,14 +442,25 @@ __device__ __forceinline__ void full_phase(const PreprocessParams& p, const floa
     const unsigned m = __ballot_sync(0xffffffffu, listed);
     if (lane == 0) s_wc[warp] = __popc(m);
     __syncthreads();
-    if (tid == 0) {
-      int tot = 0;
-      for (int w = 0; w < kPreThreads / 32; ++w) {
-        const int n = s_wc[w];
-        s_wc[w] = tot;
-        tot += n;
+    if (warp == 0) {
+      // exclusive prefix of the warps' counts, the block total, the block's base
+      const int c = lane < kPreThreads / 32 ? s_wc[lane] : 0;
+      int incl = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
       }
-      *s_base = tot ? atomicAdd(p.vis_count_out, tot) : 0;
+      const int tot = __shfl_sync(0xffffffffu, incl, 31);
+      if (lane < kPreThreads / 32) s_wc[lane] = incl - c;
+      int b = 0;
+      if (scan_state) {
+        b = (int)scan_exclusive(scan_state, round, 1, 0, (unsigned long long)tot, status);
+        if (lane == 0 && tot) atomicAdd(p.vis_count_out, tot);
+      } else if (lane == 0 && tot) {
+        b = atomicAdd(p.vis_count_out, tot);
+      }
+      if (lane == 0) *s_base = b;
     }
     __syncthreads();
     uint32_t dest = 0u;
@@ -598,17 +614,24 @@ __global__ void __launch_bounds__(kPreThreads, 2) preprocess_fwd_kernel(Preproce
 }
 
 // Two-kernel form (caller scratch).  Phase A alone, at high occupancy: one
-// chunk per block; survivors are appended to a candidate list in ascending
-// index order within the block (one atomic per block).
+// chunk per block, chunks taken in ticket order; survivors are appended to
+// the candidate list at the ordered prefix of the survivor counts of the
+// chunks before (scan.cuh), so the list is in ascending index order.
+template <bool ORDERED>
 __global__ void __launch_bounds__(kPreThreads, 4) preprocess_cull_kernel(PreprocessParams p, uint32_t* cand,
-                                                                          int* cand_count) {
+                                                                          int* cand_count, int* ticket,
+                                                                          unsigned long long* chunk_state,
+                                                                          unsigned* status) {
   __shared__ int s_off[kPreUnroll][kPreThreads / 32];
-  __shared__ int s_base;
+  __shared__ int s_base, s_chunk;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (ORDERED && tid == 0) s_chunk = atomicAdd(ticket, 1);
   float Vs[16], Ps[16];
   load_camera(p, Vs, Ps);
   const CullBound cb = make_cull_bound(p, Vs, Ps);
-  const int64_t base = (int64_t)blockIdx.x * kPreChunk + tid;
+  if (ORDERED) __syncthreads();
+  const int64_t chunk = ORDERED ? s_chunk : blockIdx.x;
+  const int64_t base = chunk * kPreChunk + tid;
   bool keep[kPreUnroll];
   cull_phase(p, Vs, Ps, cb, base, keep);
   unsigned m[kPreUnroll];
@@ -618,15 +641,29 @@ __global__ void __launch_bounds__(kPreThreads, 4) preprocess_cull_kernel(Preproc
     if (lane == 0) s_off[u][warp] = __popc(m[u]);
   }
   __syncthreads();
-  if (tid == 0) {
-    int tot = 0;
-    for (int u = 0; u < kPreUnroll; ++u)
-      for (int w = 0; w < kPreThreads / 32; ++w) {
-        const int c = s_off[u][w];
-        s_off[u][w] = tot;
-        tot += c;
+  if (warp == 0) {
+    // exclusive prefix over the (u, warp) counts in index order, two per lane
+    static_assert(kPreUnroll * (kPreThreads / 32) == 64, "two (u, warp) counts per lane");
+    int* flat = &s_off[0][0];
+    const int c0 = flat[2 * lane], c1 = flat[2 * lane + 1];
+    int incl = c0 + c1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    const int tot = __shfl_sync(0xffffffffu, incl, 31);
+    flat[2 * lane] = incl - c0 - c1;
+    flat[2 * lane + 1] = incl - c1;
+    if (ORDERED) {
+      const int b = (int)scan_exclusive(chunk_state, chunk, 1, 0, (unsigned long long)tot, status);
+      if (lane == 0) {
+        s_base = b;
+        if (tot) atomicAdd(cand_count, tot);
       }
-    s_base = tot ? atomicAdd(cand_count, tot) : 0;
+    } else if (lane == 0) {
+      s_base = tot ? atomicAdd(cand_count, tot) : 0;
+    }
   }
   __syncthreads();
 #pragma unroll
@@ -634,12 +671,16 @@ __global__ void __launch_bounds__(kPreThreads, 4) preprocess_cull_kernel(Preproc
     if (keep[u]) cand[s_base + s_off[u][warp] + __popc(m[u] & ((1u << lane) - 1u))] = (uint32_t)(base + u * kPreThreads);
 }
 
-// Phase B over the candidate list: persistent blocks take whole rounds of
-// kPreThreads candidates.
+// Phase B over the candidate list: persistent blocks take rounds of
+// kPreThreads candidates in ticket order; the visible list is written in
+// candidate order (ordered prefix over the rounds, scan.cuh).
+template <bool ORDERED>
 __global__ void __launch_bounds__(kPreThreads, 2) preprocess_full_kernel(PreprocessParams p, const uint32_t* cand,
-                                                                          const int* cand_count) {
+                                                                          const int* cand_count, int* ticket,
+                                                                          unsigned long long* round_state,
+                                                                          unsigned* status) {
   extern __shared__ bool s_mask[];
-  __shared__ int s_base;
+  __shared__ int s_base, s_round;
   __shared__ int s_wc[kPreThreads / 32];
   const int tid = threadIdx.x;
   const bool use_smem = stage_mask(p, s_mask);
@@ -648,10 +689,23 @@ __global__ void __launch_bounds__(kPreThreads, 2) preprocess_full_kernel(Preproc
   const CullBound cb = make_cull_bound(p, Vs, Ps);
   FwdAcc acc;
   const int n = *cand_count;
-  __syncthreads();
-  for (int r0 = blockIdx.x * kPreThreads; r0 < n; r0 += gridDim.x * kPreThreads) {
+  const int n_rounds = (n + kPreThreads - 1) / kPreThreads;
+  if (!ORDERED) __syncthreads();
+  for (int k = 0;; ++k) {
+    int round;
+    if (ORDERED) {
+      if (tid == 0) s_round = atomicAdd(ticket, 1);
+      __syncthreads();
+      round = s_round;
+      __syncthreads();  // everyone has read s_round before it is rewritten
+    } else {
+      round = blockIdx.x + k * gridDim.x;
+    }
+    if (round >= n_rounds) break;
+    const int r0 = round * kPreThreads;
     const bool valid = r0 + tid < n;
-    full_phase(p, Vs, Ps, cb, cand[valid ? r0 + tid : r0], valid, s_mask, use_smem, s_wc, &s_base, acc);
+    full_phase(p, Vs, Ps, cb, cand[valid ? r0 + tid : r0], valid, s_mask, use_smem, s_wc, &s_base, acc, round,
+               ORDERED ? round_state : nullptr, status);
   }
   flush_totals(p, acc);
 }
@@ -1100,24 +1154,69 @@ int resident_blocks(K kernel, int threads, size_t smem) {
   return std::max(sms, 1) * std::max(per_sm, 1);
 }
 
-size_t preprocess_scratch_bytes(int64_t P) { return 256 + sizeof(uint32_t) * (size_t)std::max<int64_t>(P, 1); }
+// Scratch of the two-kernel form: counters, the ordered-scan state of the
+// cull chunks and of the full kernel's rounds, and the candidate list.
+struct PreScratch {
+  int* cand_count;
+  int* cull_ticket;
+  int* round_ticket;
+  unsigned* status;  // scan.cuh status bits
+  unsigned long long* chunk_state;
+  unsigned long long* round_state;
+  uint32_t* cand;
+  size_t zero_bytes;  // bytes [256, zero_bytes) must be zero before the launch
+};
+
+static int64_t pre_chunks(int64_t P) { return (P + kPreChunk - 1) / kPreChunk; }
+static int64_t pre_rounds(int64_t P) { return (P + kPreThreads - 1) / kPreThreads; }
+
+static PreScratch pre_scratch_layout(void* base, int64_t P) {
+  char* b = static_cast<char*>(base);
+  PreScratch s;
+  s.status = reinterpret_cast<unsigned*>(b + kPreStatusOffset);  // bytes [0, 256): never cleared here
+  s.cand_count = reinterpret_cast<int*>(b + 256);
+  s.cull_ticket = reinterpret_cast<int*>(b + 260);
+  s.round_ticket = reinterpret_cast<int*>(b + 264);
+  size_t off = 384;
+  s.chunk_state = reinterpret_cast<unsigned long long*>(b + off);
+  off += 8 * (size_t)std::max<int64_t>(pre_chunks(P), 1);
+  s.round_state = reinterpret_cast<unsigned long long*>(b + off);
+  off += 8 * (size_t)std::max<int64_t>(pre_rounds(P), 1);
+  s.zero_bytes = off;
+  s.cand = reinterpret_cast<uint32_t*>(b + off);
+  return s;
+}
+
+size_t preprocess_scratch_bytes(int64_t P) {
+  return pre_scratch_layout(nullptr, P).zero_bytes + sizeof(uint32_t) * (size_t)std::max<int64_t>(P, 1);
+}
 
 int launch_preprocess_fwd(const PreprocessParams& p, cudaStream_t st, void* scratch, size_t scratch_bytes) {
   if (p.totals_out) cudaMemsetAsync(p.totals_out, 0, 2 * sizeof(unsigned long long), st);
   if (p.P <= 0) return (int)cudaGetLastError();
   const int n_tiles = p.grid_x * p.grid_y;
   const size_t smem = (p.counts_out && p.compute_locally && n_tiles <= kPreMaskSmem) ? (size_t)n_tiles : 0;
-  const int64_t n_chunks = (p.P + kPreChunk - 1) / kPreChunk;
+  const int64_t n_chunks = pre_chunks(p.P);
   if (scratch && scratch_bytes >= preprocess_scratch_bytes(p.P)) {
     // cull pass over every Gaussian, then the full computation over the
     // candidates (persistent grid: the count is only known on the device)
-    int* cand_count = reinterpret_cast<int*>(scratch);
-    uint32_t* cand = reinterpret_cast<uint32_t*>(static_cast<char*>(scratch) + 256);
-    cudaMemsetAsync(cand_count, 0, sizeof(int), st);
-    preprocess_cull_kernel<<<(unsigned)n_chunks, kPreThreads, 0, st>>>(p, cand, cand_count);
-    static const int resident_full = resident_blocks(preprocess_full_kernel, kPreThreads, kPreMaskSmem);
+    const PreScratch s = pre_scratch_layout(scratch, p.P);
+    static const int resident_full = resident_blocks(preprocess_full_kernel<false>, kPreThreads, kPreMaskSmem);
     const int64_t blocks = std::min<int64_t>((p.P + kPreThreads - 1) / kPreThreads, resident_full);
-    preprocess_full_kernel<<<(unsigned)blocks, kPreThreads, smem, st>>>(p, cand, cand_count);
+    if (p.ordered_list) {
+      cudaMemsetAsync(static_cast<char*>(scratch) + 256, 0, s.zero_bytes - 256, st);
+      preprocess_cull_kernel<true><<<(unsigned)n_chunks, kPreThreads, 0, st>>>(p, s.cand, s.cand_count, s.cull_ticket,
+                                                                               s.chunk_state, s.status);
+      preprocess_full_kernel<true><<<(unsigned)blocks, kPreThreads, smem, st>>>(p, s.cand, s.cand_count,
+                                                                                s.round_ticket, s.round_state,
+                                                                                s.status);
+    } else {
+      cudaMemsetAsync(s.cand_count, 0, sizeof(int), st);
+      preprocess_cull_kernel<false><<<(unsigned)n_chunks, kPreThreads, 0, st>>>(p, s.cand, s.cand_count, nullptr,
+                                                                                nullptr, s.status);
+      preprocess_full_kernel<false><<<(unsigned)blocks, kPreThreads, smem, st>>>(p, s.cand, s.cand_count, nullptr,
+                                                                                 nullptr, s.status);
+    }
     return (int)cudaGetLastError();
   }
   // persistent grid: as many blocks as fit on the device at once

@@ -9,8 +9,11 @@
 // against each rank's [dist[r], dist[r+1]) interval of tile ids (optionally
 // widened by gx+1 on both sides).  An empty interval sends nothing.  The
 // output is the dense bool [P, world_size] matrix the reference returns.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
+#include "scan.cuh"
 
 namespace blitz {
 
@@ -40,12 +43,24 @@ __global__ void __launch_bounds__(256) route_bool_kernel(RouteParams p) {
   }
 }
 
-// One thread per row; a row sent to k ranks takes k slots.  Positions within
-// a (rank, camera) segment come from warp-aggregated atomics, so their order
-// varies run to run; send_row records where each one came from.
-__global__ void __launch_bounds__(256) exchange_pack_kernel(PackParams p) {
-  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int lane = threadIdx.x & 31;
+// One thread per row, 256-row tiles taken in ticket order; a row sent to k
+// ranks takes k slots.  Its position in a destination's segment is the
+// ordered count of the rows before it that go there: per-warp ballots, a
+// block prefix over the warps, and the ordered prefix over the tiles before
+// (scan.cuh, one counter per rank).  Rows keep their list order in every
+// segment, so with an index-ordered list (the two-kernel preprocess) each
+// segment is in ascending index order and the receivers see the same order
+// on every run.  send_row records where each slot came from.
+constexpr int kPackThreads = 256;
+__global__ void __launch_bounds__(kPackThreads) exchange_pack_kernel(PackParams p) {
+  __shared__ int s_tile;
+  __shared__ int s_wcnt[kPackThreads / 32][32];  // rows per (warp, rank), then their exclusive prefix
+  __shared__ int s_base[32];                      // tile's exclusive prefix per rank
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) s_tile = atomicAdd(p.ticket, 1);
+  __syncthreads();
+  const int64_t tile = s_tile;
+  const int64_t j = tile * kPackThreads + tid;
   const bool in = j < p.n_rows;
   const uint32_t m = in ? __ldg(p.mask + j) : 0u;
   float4 r0, r1, r2;
@@ -56,14 +71,31 @@ __global__ void __launch_bounds__(256) exchange_pack_kernel(PackParams p) {
     r2 = src[2];
   }
   for (int r = 0; r < p.n_ranks; ++r) {
+    const unsigned b = __ballot_sync(0xffffffffu, (m >> r) & 1u);
+    if (lane == 0) s_wcnt[warp][r] = __popc(b);
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int tot = 0;
+    if (lane < p.n_ranks)
+      for (int w = 0; w < kPackThreads / 32; ++w) {
+        const int c = s_wcnt[w][lane];
+        s_wcnt[w][lane] = tot;
+        tot += c;
+      }
+    // one warp-wide look-back per rank
+    for (int r = 0; r < p.n_ranks; ++r) {
+      const int t_r = __shfl_sync(0xffffffffu, tot, r);
+      const int b = (int)scan_exclusive(p.scan_state, tile, p.n_ranks, r, (unsigned long long)t_r, p.status);
+      if (lane == 0) s_base[r] = b;
+    }
+  }
+  __syncthreads();
+  for (int r = 0; r < p.n_ranks; ++r) {
     const bool mine = (m >> r) & 1u;
     const unsigned b = __ballot_sync(0xffffffffu, mine);
-    if (!b) continue;
-    int base = 0;
-    if (lane == __ffs(b) - 1) base = atomicAdd(p.cursor + r, __popc(b));
-    base = __shfl_sync(0xffffffffu, base, __ffs(b) - 1);
     if (mine) {
-      const int64_t pos = p.dest_offset[r] + base + __popc(b & ((1u << lane) - 1u));
+      const int64_t pos = p.dest_offset[r] + s_base[r] + s_wcnt[warp][r] + __popc(b & ((1u << lane) - 1u));
       float4* dst = reinterpret_cast<float4*>(p.send + 12 * pos);
       dst[0] = r0;
       dst[1] = r1;
@@ -199,10 +231,19 @@ int launch_grad_records_pack(const GradPackParams& p, int64_t n, cudaStream_t st
   return (int)cudaGetLastError();
 }
 
-int launch_exchange_pack(const PackParams& p, cudaStream_t st) {
+size_t exchange_pack_scratch_bytes(int64_t n_rows, int n_ranks) {
+  const int64_t tiles = std::max<int64_t>((n_rows + kPackThreads - 1) / kPackThreads, 1);
+  return 384 + 8 * (size_t)tiles * (size_t)std::max(n_ranks, 1);
+}
+
+int launch_exchange_pack(PackParams p, void* scratch, cudaStream_t st) {
   if (p.n_rows <= 0) return 0;
-  const int threads = 256;
-  exchange_pack_kernel<<<(unsigned)((p.n_rows + threads - 1) / threads), threads, 0, st>>>(p);
+  char* b = static_cast<char*>(scratch);
+  p.status = reinterpret_cast<unsigned*>(b);  // bytes [0, 256): never cleared here
+  p.ticket = reinterpret_cast<int*>(b + 256);
+  p.scan_state = reinterpret_cast<unsigned long long*>(b + 384);
+  cudaMemsetAsync(b + 256, 0, exchange_pack_scratch_bytes(p.n_rows, p.n_ranks) - 256, st);
+  exchange_pack_kernel<<<(unsigned)((p.n_rows + kPackThreads - 1) / kPackThreads), kPackThreads, 0, st>>>(p);
   return (int)cudaGetLastError();
 }
 

@@ -55,9 +55,10 @@ class _DistributedBatch(torch.autograd.Function):
         ws = torch.distributed.get_world_size(group)
         dev = xyz.device
         sh = ops.sh_layout(dc=dc, rest=rest)
-        # 1. preprocess every camera; the kernel also writes each listed
-        #    Gaussian's exchange record, its destination ranks and the
-        #    per-destination counts (no host synchronisation in between)
+        # 1. preprocess every camera in one call; the kernels also write each
+        #    listed Gaussian's exchange record, its destination ranks and the
+        #    per-destination counts (no host synchronisation in between).  The
+        #    visible lists are in ascending index order.
         P = xyz.shape[0]
         gx = D.CONTEXT.TILE_X
         table = _pinned_table(n_cams, ws)  # tile interval [lo, hi) of every rank, per camera
@@ -67,50 +68,34 @@ class _DistributedBatch(torch.autograd.Function):
                 table[k, 1, g] = st.division_pos[r_local + 1] * gx
         table_dev = table[:n_cams].to(dev, non_blocking=True)
         cnt = torch.zeros((n_cams, 1 + ws), dtype=torch.int32, device=dev)  # list length | rows per rank
-        # one allocation per buffer kind for the whole batch
-        Pc = max(P, 1)
+        # one allocation per buffer kind for the whole batch; camera k's rows start at k*Pc
+        Pc = (max(P, 1) + 3) // 4 * 4
         b_m2 = torch.empty((n_cams, Pc, 2), dtype=torch.float32, device=dev)
-        b_f1 = torch.empty((n_cams, 2, Pc), dtype=torch.float32, device=dev)  # depths | radii bits
+        b_depth = torch.empty((n_cams, Pc), dtype=torch.float32, device=dev)
+        b_radii = torch.empty((n_cams, Pc), dtype=torch.int32, device=dev)
         b_co = torch.empty((n_cams, Pc, 4), dtype=torch.float32, device=dev)
         b_rgb = torch.empty((n_cams, Pc, 3), dtype=torch.float32, device=dev)
-        b_list = torch.empty((n_cams, 2, Pc), dtype=torch.int32, device=dev)  # vis list | dest mask
+        b_list = torch.empty((n_cams, Pc), dtype=torch.int32, device=dev)
+        b_mask = torch.empty((n_cams, Pc), dtype=torch.int32, device=dev)
         b_rec = torch.empty((n_cams, Pc, _FWD_C), dtype=torch.float32, device=dev)
-        pre = []
-        for k, rs in enumerate(rasters):
-            bufs = (b_m2[k, :P], b_f1[k, 0, :P], b_f1[k, 1, :P].view(torch.int32), b_co[k, :P], b_rgb[k, :P],
-                    b_list[k, 0])
-            xrec, xmask = b_rec[k], b_list[k, 1]
-            m2, d, r, co, rgb, _, vlist, vcount, _, _, _ = ops.preprocess_forward_raw(
-                xyz, s_raw, q_raw, o_raw.reshape(-1), sh, rs, None, want_reg=False, want_list=True,
-                vis_count=cnt[k, 0:1], exchange=(table_dev[k, 0], table_dev[k, 1], xrec, xmask, cnt[k, 1:]),
-                out=bufs)
-            pre.append((m2, r, vlist, vcount, xrec, xmask))
-            if densify is not None:
-                DZ.update_max_radii(densify, r)
+        cams = _camera_arrays(rasters)
+        ops.preprocess_forward_raw_batch(xyz, s_raw, q_raw, o_raw.reshape(-1), sh, rasters, cams, Pc,
+                                         (b_m2, b_depth, b_radii, b_co, b_rgb, b_list), cnt,
+                                         exchange=(table_dev, b_rec, b_mask))
+        if densify is not None:
+            for k in range(n_cams):
+                DZ.update_max_radii(densify, b_radii[k, :P])
         # 2. one all-gather of every rank's counts: the only host synchronisation
         #    before the render (it sizes the all-to-all on every rank)
         gdev = dev if torch.distributed.get_backend(group) == "nccl" else torch.device("cpu")
         allc = torch.empty((ws * n_cams, 1 + ws), dtype=torch.int32, device=gdev)
         torch.distributed.all_gather_into_tensor(allc, cnt.to(gdev), group=group)
         allc = allc.view(ws, n_cams, 1 + ws).cpu().tolist()
-        counts = [allc[rank][k][0] for k in range(n_cams)]
-        size = [[[allc[i][k][1 + j] for k in range(n_cams)] for j in range(ws)] for i in range(ws)]
-        plan = D.plan_from_sizes(size, n_cams, rank, ws)
-        offs = [0]
-        for c in counts:
-            offs.append(offs[-1] + c)
+        counts, plan, offs, dest_off = D.exchange_layout(allc, rank, ws, n_cams)
         n_send = sum(plan.send_splits)
         send = torch.empty((max(n_send, 1), _FWD_C), dtype=torch.float32, device=dev)
         send_row = torch.empty((max(n_send, 1),), dtype=torch.int32, device=dev)
-        cursor = torch.zeros((n_cams, ws), dtype=torch.int32, device=dev)
-        base = [0]
-        for j in range(ws):
-            base.append(base[-1] + plan.send_splits[j])
-        for k in range(n_cams):
-            if counts[k] == 0:
-                continue
-            dest_off = [base[j] + sum(size[rank][j][:k]) for j in range(ws)]
-            ops.exchange_pack(counts[k], pre[k][4], pre[k][5], dest_off, cursor[k], send, send_row, offs[k])
+        ops.exchange_pack_batch(counts, Pc, b_rec, b_mask, dest_off, offs[:-1], send, send_row)
         recv_buf = torch.empty((sum(plan.recv_splits), _FWD_C), dtype=torch.float32, device=dev)
         torch.distributed.all_to_all_single(recv_buf, send[:n_send], plan.recv_splits, plan.send_splits, group=group)
         # 3. render and score the bands this rank owns.  Per camera: unpack
@@ -132,6 +117,7 @@ class _DistributedBatch(torch.autograd.Function):
             ops.render_count(m2, radii, cl, H, W, counts_k, totals[i])
             staged.append((k, segs, conic, m2, rgb, depth, radii, cl, counts_k))
         tot_host = totals.cpu().tolist() if nm else []
+        ops.check_scan_status(dev)
         losses = []
         saved = {}
         for i, (k, segs, conic, m2, rgb, depth, radii, cl, counts_k) in enumerate(staged):
@@ -155,7 +141,7 @@ class _DistributedBatch(torch.autograd.Function):
         ctx.setup = setup
         ctx.plan = plan
         ctx.saved = saved
-        ctx.pre = [(p[0], p[1], p[2], p[3]) for p in pre]  # means2D, radii, vis_list, vis_count
+        ctx.pre = (b_m2, b_radii, b_list, cnt, Pc, cams)
         ctx.counts, ctx.offs = counts, offs
         ctx.send_rows = send_row[:n_send].to(torch.int64)
         ctx.save_for_backward(xyz, s_raw, q_raw, o_raw, dc, rest)
@@ -191,7 +177,7 @@ class _DistributedBatch(torch.autograd.Function):
             recv = torch.empty((sum(plan.send_splits), _BWD_C), dtype=torch.float32, device=dev)
             torch.distributed.all_to_all_single(recv, send, plan.send_splits, plan.recv_splits, group=group)
             # owner: one scatter-add into compact per-camera rows (aligned with the visible lists)
-            acc = torch.zeros((ctx.offs[-1], _BWD_C), dtype=torch.float32, device=dev)
+            acc = torch.zeros((max(ctx.offs[-1], 1), _BWD_C), dtype=torch.float32, device=dev)
             acc.index_add_(0, ctx.send_rows, recv)
             sh = ops.sh_layout(dc=dc, rest=rest)
             M = rest.shape[1]
@@ -199,23 +185,28 @@ class _DistributedBatch(torch.autograd.Function):
         finally:
             # every exit orders this stream after the fill before the grads are used or freed
             _zero_fill_wait()
-        for k in range(n_cams):
-            m2, r, vlist, vcount = ctx.pre[k]
-            a = acc[ctx.offs[k]:ctx.offs[k + 1]]
-            if ctx.counts[k] == 0:
-                continue
-            if densify is not None:
-                # viewspace gradient of the owner's screen means: summed over the receivers
-                DZ.accumulate_grad(densify, vlist[:ctx.counts[k]].to(torch.int64), a[:, 4:6])
-            ops.preprocess_backward_raw(r, m2, xyz, s_raw, q_raw, o_raw.reshape(-1), sh, rasters[k],
-                                        a[:, 4:6], a[:, 0:4], a[:, 6:9],
-                                        (g_xyz, g_s, g_q, g_o, (g_dc, 3), (g_rest, max(M, 1) * 3)),
-                                        vis_list=vlist, vis_count=vcount, accumulate=True,
-                                        rows=ops.ROWS_UPSTREAM_BY_SLOT, g_minscale=a[:, 11])
+        b_m2, b_radii, b_list, cnt, Pc, cams = ctx.pre
+        if densify is not None:
+            for k in range(n_cams):
+                if ctx.counts[k]:
+                    # viewspace gradient of the owner's screen means: summed over the receivers
+                    DZ.accumulate_grad(densify, b_list[k, :ctx.counts[k]].to(torch.int64),
+                                       acc[ctx.offs[k]:ctx.offs[k + 1], 4:6])
+        ops.preprocess_backward_raw_batch(b_radii, b_m2, b_list, cnt, Pc, xyz, s_raw, q_raw, o_raw.reshape(-1), sh,
+                                          rasters, cams, acc, ctx.offs[:-1],
+                                          (g_xyz, g_s, g_q, g_o, (g_dc, 3), (g_rest, max(M, 1) * 3)))
         return g_xyz, g_s, g_q, g_o, g_dc, g_rest, None
 
 
 _TABLE = {}
+
+
+def _camera_arrays(rasters):
+    """(viewmatrices [n,16], projmatrices [n,16], campos [n,3]) of the batch."""
+    views = torch.stack([r.viewmatrix.reshape(16) for r in rasters])
+    projs = torch.stack([r.projmatrix.reshape(16) for r in rasters])
+    campos = torch.stack([r.campos.reshape(3) for r in rasters])
+    return views.float().contiguous(), projs.float().contiguous(), campos.float().contiguous()
 
 
 def _pinned_table(n_cams, ws):

@@ -292,7 +292,6 @@ def zorder_shards(xyz, world_size):
 @dataclass
 class ExchangePlan:
     """Send/receive bookkeeping of one step (kept for the backward exchange)."""
-    send_ids: list            # [n_cams][ws] local index tensors (empty where nothing is sent)
     size: list                # size[src][dst][cam] record counts, identical on every rank
     my_cams: list             # cameras this rank renders, in batch order
     recv_offsets: dict = field(default_factory=dict)  # cam -> [(src, start, count) in recv buffer]
@@ -300,32 +299,13 @@ class ExchangePlan:
     recv_splits: list = field(default_factory=list)
 
 
-def plan_exchange(send_ids, n_cams, group=None):
-    """All-gather the [ws, ws, n_cams] size matrix (one small collective, one
-    device-to-host copy) and derive the all-to-all splits."""
-    ws = dist.get_world_size(group)
-    rank = dist.get_rank(group)
-    dev = None
-    for per in send_ids:
-        for t in per:
-            dev = t.device
-            break
-        if dev is not None:
-            break
-    local = torch.tensor([[len(send_ids[k][j]) for k in range(n_cams)] for j in range(ws)], dtype=torch.int64)
-    backend = dist.get_backend(group)
-    gdev = torch.device("cuda", torch.cuda.current_device()) if backend == "nccl" else torch.device("cpu")
-    allsz = torch.empty((ws * ws, n_cams), dtype=torch.int64, device=gdev)
-    dist.all_gather_into_tensor(allsz, local.to(gdev), group=group)
-    size = allsz.view(ws, ws, n_cams).cpu().tolist()
-    return plan_from_sizes(size, n_cams, rank, ws, send_ids)
-
-
-def plan_from_sizes(size, n_cams, rank, ws, send_ids=None):
+def plan_from_sizes(size, n_cams, rank, ws):
     """Splits and receive offsets from size[src][dst][cam] (the same matrix on
-    every rank)."""
+    every rank).  The send buffer holds, per destination in rank order, that
+    destination's rows camera by camera; the receive buffer holds, per
+    source in rank order, the rows that source sent, camera by camera."""
     my_cams = [k for k in range(n_cams) if any(size[i][rank][k] for i in range(ws))]
-    plan = ExchangePlan(send_ids=send_ids, size=size, my_cams=my_cams)
+    plan = ExchangePlan(size=size, my_cams=my_cams)
     plan.send_splits = [sum(size[rank][j]) for j in range(ws)]
     plan.recv_splits = [sum(size[i][rank]) for i in range(ws)]
     off = 0
@@ -339,59 +319,30 @@ def plan_from_sizes(size, n_cams, rank, ws, send_ids=None):
     return plan
 
 
-def exchange_forward(records, plan, group=None):
-    """records[k]: [P_local, C] per camera.  Returns {cam: [P'_k, C]} of the
-    records this rank receives, ordered by source rank then source index."""
-    ws = dist.get_world_size(group)
-    n_cams = len(records)
-    C = records[0].shape[1]
-    dev = records[0].device
-    chunks = []
+def send_offsets(size, rank, ws, n_cams):
+    """dest_off[k][j]: first send-buffer row of camera k's records for rank j
+    (the layout plan_from_sizes describes)."""
+    base = [0]
     for j in range(ws):
-        for k in range(n_cams):
-            ids = plan.send_ids[k][j]
-            if len(ids):
-                chunks.append(records[k].index_select(0, ids))
-    send = torch.cat(chunks, 0) if chunks else torch.empty((0, C), dtype=records[0].dtype, device=dev)
-    recv = torch.empty((sum(plan.recv_splits), C), dtype=records[0].dtype, device=dev)
-    dist.all_to_all_single(recv, send.contiguous(), plan.recv_splits, plan.send_splits, group=group)
-    out = {}
-    for k, parts in plan.recv_offsets.items():
-        tot = sum(c for _, _, c in parts)
-        if tot == 0:
-            continue
-        out[k] = torch.cat([recv[s:s + c] for _, s, c in parts if c], 0) if len(parts) > 1 else recv[parts[0][1]:parts[0][1] + tot]
+        base.append(base[-1] + sum(size[rank][j]))
+    out = []
+    for k in range(n_cams):
+        out.append([base[j] + sum(size[rank][j][:k]) for j in range(ws)])
     return out
 
 
-def exchange_backward(grads, plan, P_local, n_cams, C, group=None, dtype=torch.float32, device=None):
-    """grads: {cam: [P'_k, C]} aligned with exchange_forward's output.  Sends
-    each gradient row back to the Gaussian's owner and scatter-adds it:
-    returns [n_cams][P_local, C] accumulators (rows of Gaussians not sent
-    for a camera stay zero)."""
-    ws = dist.get_world_size(group)
-    rank = dist.get_rank(group)
-    dev = device
-    if dev is None:
-        dev = next(iter(grads.values())).device if grads else torch.device("cpu")
-    send = torch.zeros((sum(plan.recv_splits), C), dtype=dtype, device=dev)
-    for k, parts in plan.recv_offsets.items():
-        if k not in grads:
-            continue
-        g = grads[k]
-        pos = 0
-        for _, s, c in parts:
-            if c:
-                send[s:s + c] = g[pos:pos + c]
-                pos += c
-    recv = torch.empty((sum(plan.send_splits), C), dtype=dtype, device=dev)
-    dist.all_to_all_single(recv, send, plan.send_splits, plan.recv_splits, group=group)
-    acc = [torch.zeros((P_local, C), dtype=dtype, device=dev) for _ in range(n_cams)]
-    off = 0
-    for j in range(ws):
-        for k in range(n_cams):
-            c = plan.size[rank][j][k]
-            if c:
-                acc[k].index_add_(0, plan.send_ids[k][j], recv[off:off + c])
-                off += c
-    return acc
+def exchange_layout(allc, rank, ws, n_cams):
+    """Everything one step's exchange needs, from the all-gathered counts
+    ``allc[src][cam] = [list length, rows for rank 0, ..., rows for rank
+    ws-1]`` (identical on every rank): (counts, plan, offs, dest_off) with
+    counts[k] this rank's list length of camera k, offs the compact-row
+    offsets of the cameras' lists (offs[k] + slot is the row of camera k's
+    slot-th listed Gaussian in the backward's accumulator), and dest_off the
+    send offsets of send_offsets()."""
+    counts = [int(allc[rank][k][0]) for k in range(n_cams)]
+    size = [[[int(allc[i][k][1 + j]) for k in range(n_cams)] for j in range(ws)] for i in range(ws)]
+    plan = plan_from_sizes(size, n_cams, rank, ws)
+    offs = [0]
+    for c in counts:
+        offs.append(offs[-1] + c)
+    return counts, plan, offs, send_offsets(size, rank, ws, n_cams)

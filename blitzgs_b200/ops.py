@@ -79,10 +79,12 @@ def grid_dims(H, W):
 
 
 class _Scratch:
-    """Grow-only per-device scratch buffer for binning (never shrinks)."""
+    """Grow-only per-device scratch buffer (never shrinks).  ``zeroed``
+    buffers start at zero when (re)allocated."""
 
-    def __init__(self):
+    def __init__(self, zeroed=False):
         self.bufs = {}
+        self.zeroed = zeroed
 
     def get(self, device, nbytes):
         key = (device.type, device.index)
@@ -91,13 +93,18 @@ class _Scratch:
             cap = max(nbytes, int((buf.numel() if buf is not None else 0) * 1.25))
             cap = (cap + (1 << 20) - 1) // (1 << 20) * (1 << 20)
             self.bufs[key] = None
-            buf = torch.empty(cap, dtype=torch.uint8, device=device)
+            buf = (torch.zeros if self.zeroed else torch.empty)(cap, dtype=torch.uint8, device=device)
             self.bufs[key] = buf
         return buf
 
+    def peek(self, device):
+        return self.bufs.get((device.type, device.index))
+
 
 SCRATCH = _Scratch()
-PRE_SCRATCH = _Scratch()  # candidate list of the two-kernel raw preprocess
+# candidate list and ordered-scan state of the two-kernel raw preprocess; its
+# first 4 bytes are the scans' status word (checked at the totals readback)
+PRE_SCRATCH = _Scratch(zeroed=True)
 
 
 def sh_layout(shs=None, dc=None, rest=None):
@@ -268,13 +275,109 @@ class ExchangeOut(ctypes.Structure):
                 ("records", ctypes.c_void_p), ("dest_mask", ctypes.c_void_p), ("dest_counts", ctypes.c_void_p)]
 
 
-def exchange_pack(n_rows, records, dest_mask, dest_offset, cursor, send, send_row, row_base):
+PACK_SCRATCH = _Scratch(zeroed=True)  # ordered-scan state of the exchange pack; first 4 bytes: status word
+
+
+def check_scan_status(device):
+    """Raise if an ordered scan of the preprocess or the exchange pack on
+    ``device`` gave up waiting (one small readback of their status words)."""
+    bufs = [b for b in (PRE_SCRATCH.peek(device), PACK_SCRATCH.peek(device)) if b is not None]
+    if not bufs:
+        return
+    words = torch.stack([b[:4].view(torch.int32)[0] for b in bufs]).cpu().tolist()
+    if any(words):
+        for b in bufs:
+            b[:4].zero_()
+        raise RuntimeError(f"blitzgs_b200: an ordered scan gave up waiting (status words {words})")
+
+
+def exchange_pack(n_rows, records, dest_mask, dest_offset, send, send_row, row_base):
     """Pack n_rows exchange records into the send buffer (blitz_exchange_pack);
-    dest_offset: list of per-rank starting rows."""
+    dest_offset: list of per-rank starting rows.  Each rank's segment keeps
+    the rows' order."""
     n_ranks = len(dest_offset)
     offs = (ctypes.c_int64 * n_ranks)(*[int(x) for x in dest_offset])
+    lib = _lib.load()
+    scratch = PACK_SCRATCH.get(records.device, lib.blitz_exchange_pack_scratch_bytes(int(n_rows), n_ranks))
     _lib.call("blitz_exchange_pack", int(n_rows), n_ranks, ptr(records), ptr(dest_mask), ctypes.addressof(offs),
-              ptr(cursor), ptr(send), ptr(send_row), int(row_base), _lib.stream_ptr())
+              ptr(send), ptr(send_row), int(row_base), ptr(scratch), scratch.numel(), _lib.stream_ptr())
+
+
+def exchange_pack_batch(n_rows, cam_stride, records, dest_mask, dest_offset, row_base, send, send_row):
+    """blitz_exchange_pack_batch: camera k's n_rows[k] rows (records /
+    dest_mask rows from k*cam_stride) to send, rank r's segment of camera k
+    starting at dest_offset[k][r]; send_row gets row_base[k] + j."""
+    n_cams = len(n_rows)
+    if n_cams == 0:
+        return
+    n_ranks = len(dest_offset[0])
+    nr = (ctypes.c_int64 * n_cams)(*[int(x) for x in n_rows])
+    rb = (ctypes.c_int64 * n_cams)(*[int(x) for x in row_base])
+    do = (ctypes.c_int64 * (n_cams * n_ranks))(*[int(x) for row in dest_offset for x in row])
+    lib = _lib.load()
+    scratch = PACK_SCRATCH.get(records.device, lib.blitz_exchange_pack_scratch_bytes(max(int(x) for x in n_rows),
+                                                                                     n_ranks))
+    _lib.call("blitz_exchange_pack_batch", n_cams, n_ranks, nr, int(cam_stride), ptr(records), ptr(dest_mask), do, rb,
+              ptr(send), ptr(send_row), ptr(scratch), scratch.numel(), _lib.stream_ptr())
+
+
+def _tanfov(rasters):
+    n = len(rasters)
+    return (ctypes.c_float * (2 * n))(*[float(v) for r in rasters for v in (r.tanfovx, r.tanfovy)])
+
+
+def preprocess_forward_raw_batch(xyz, scaling_raw, rotation_raw, opacity_raw, sh, rasters, cams, cam_stride, out,
+                                 counts, exchange=None):
+    """blitz_preprocess_forward_raw_batch over the cameras of ``rasters``.
+    ``cams`` = (viewmatrices [n,16], projmatrices [n,16], campos [n,3])
+    device tensors; ``out`` = (means2D, depths, radii, conic_opacity, rgb,
+    vis_list) with camera k's rows from k*cam_stride; ``counts`` int32
+    [n, 1+ranks] zeroed; ``exchange`` = (tile_bounds int32 [n,2,ranks],
+    records, dest_mask) or None."""
+    _require_cuda(xyz, scaling_raw, rotation_raw, opacity_raw)
+    dc, dcs, rest, rs, M, _keep = sh
+    P = xyz.shape[0]
+    n = len(rasters)
+    if n == 0 or P == 0:
+        return
+    r0 = rasters[0]
+    H, W = int(r0.image_height), int(r0.image_width)
+    views, projs, campos = cams
+    means2D, depths, radii, conic, rgb, vlist = out
+    n_ranks = 0 if exchange is None else int(exchange[0].shape[-1])
+    tb, rec, mask = exchange if exchange is not None else (None, None, None)
+    scratch = PRE_SCRATCH.get(xyz.device, _lib.load().blitz_preprocess_scratch_bytes(P))
+    tok = TIMER.begin("preprocess_fwd")
+    _lib.call("blitz_preprocess_forward_raw_batch", n, P, int(r0.sh_degree), M, ptr(xyz), ptr(scaling_raw),
+              ptr(rotation_raw), ptr(opacity_raw), ptr(dc), dcs, ptr(rest), rs, float(r0.scale_modifier), ptr(views),
+              ptr(projs), ptr(campos), _tanfov(rasters), H, W, int(cam_stride), ptr(means2D), ptr(depths),
+              ptr(radii), ptr(conic), ptr(rgb), ptr(vlist), ptr(counts), n_ranks, ptr(tb), ptr(rec), ptr(mask),
+              ptr(scratch), scratch.numel(), _lib.stream_ptr())
+    TIMER.end(tok, P=P * n)
+
+
+def preprocess_backward_raw_batch(radii, means2D, vis_list, counts, cam_stride, xyz, scaling_raw, rotation_raw,
+                                  opacity_raw, sh, rasters, cams, upstream, upstream_row0, out):
+    """blitz_preprocess_backward_raw_batch: every camera's listed backward
+    added into ``out`` = (g_xyz, g_scaling, g_rotation, g_opacity, (g_dc,
+    stride), (g_rest, stride))."""
+    dc, dcs, rest, rs, M, _keep = sh
+    P = xyz.shape[0]
+    n = len(rasters)
+    if n == 0 or P == 0:
+        return
+    r0 = rasters[0]
+    H, W = int(r0.image_height), int(r0.image_width)
+    views, projs, campos = cams
+    gx, gs, gq, go, (gdc, gdcs), (grest, grs) = out
+    rows0 = (ctypes.c_int64 * n)(*[int(v) for v in upstream_row0])
+    tok = TIMER.begin("preprocess_bwd")
+    _lib.call("blitz_preprocess_backward_raw_batch", n, P, int(r0.sh_degree), M, ptr(radii), ptr(means2D),
+              ptr(vis_list), ptr(counts), int(counts.stride(0)), int(cam_stride), ptr(xyz), ptr(scaling_raw),
+              ptr(rotation_raw), ptr(opacity_raw), ptr(dc), dcs, ptr(rest), rs, float(r0.scale_modifier), ptr(views),
+              ptr(projs), ptr(campos), _tanfov(rasters), H, W, ptr(upstream), rows0, ptr(gx), ptr(gs), ptr(gq),
+              ptr(go), ptr(gdc), gdcs, ptr(grest), grs, _lib.stream_ptr())
+    TIMER.end(tok, P=P * n)
 
 
 def _segments(segs):
@@ -361,10 +464,10 @@ class RenderState:
 _PINNED = {}
 
 
-def _pinned(dev, n, dtype):
+def _pinned(dev, n, dtype, tag=""):
     """Reused pinned host buffer and a numpy view of it (reading a number
     through numpy costs far less than indexing the tensor)."""
-    key = (dev.index, n, dtype)
+    key = (dev.index, n, dtype, tag)
     t = _PINNED.get(key)
     if t is None:
         buf = torch.empty(n, dtype=dtype, pin_memory=True)
@@ -436,8 +539,11 @@ def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_local
     else:
         host, host_np = _pinned(dev, 2, torch.int64)
         host_n, host_n_np = _pinned(dev, 1, torch.int32) if vis_count is not None else (None, None)
-        _lib.call("blitz_read_totals", ptr(totals), ptr(vis_count), host.data_ptr(),
-                  host_n.data_ptr() if host_n is not None else None, st)
+        pre = PRE_SCRATCH.peek(dev)
+        host_s = _pinned(dev, 1, torch.int32, "status")[0] if pre is not None else None
+        _lib.call("blitz_read_totals", ptr(totals), ptr(vis_count), ptr(pre), host.data_ptr(),
+                  host_n.data_ptr() if host_n is not None else None,
+                  host_s.data_ptr() if host_s is not None else None, st)
         R, n_vis = int(host_np[0]), int(host_np[1])
         n_list = int(host_n_np[0]) if vis_count is not None else None
 

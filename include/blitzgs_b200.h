@@ -36,6 +36,7 @@ extern "C" {
 #define BLITZ_OK 0
 #define BLITZ_EINVAL 10001      /* bad argument (size, alignment, null pointer) */
 #define BLITZ_ESCRATCH 10002    /* scratch buffer smaller than *_bytes() asked for */
+#define BLITZ_ESCAN 10003       /* an ordered list scan gave up waiting (results of that launch are unordered) */
 
 /* Device error-word bits (see blitz_preprocess_forward). */
 #define BLITZ_ERRBIT_PREFILTERED_CULLED 1u /* a Gaussian failed the near test with prefiltered=1 */
@@ -118,7 +119,10 @@ int blitz_preprocess_backward(int64_t P, int D, int M, const int32_t* radii, con
  *             (counts and totals must be both given or both NULL);
  *   slot_of   device uint32 [P] (with a list): slot_of[i] = position of
  *             listed Gaussian i in vis_list (other entries untouched);
- *   exchange  host pointer to a blitz_exchange_out (with a list; NULL = none);
+ *   exchange  host pointer to a blitz_exchange_out (with a list and the
+ *             scratch; NULL = none).  With it the visible list is in
+ *             ascending index order (the exchange keeps one order on every
+ *             run); without it the list's order is unspecified;
  *   scratch   device buffer of blitz_preprocess_scratch_bytes(P) bytes: runs
  *             the cull and the full computation as two kernels (faster when
  *             most Gaussians are off-screen); NULL runs one kernel.
@@ -126,7 +130,9 @@ int blitz_preprocess_backward(int64_t P, int D, int M, const int32_t* radii, con
  * (gaussian_renderer/__init__.py:260-324); no reference op is a single match.
  */
 /* Size of the optional scratch of blitz_preprocess_forward_raw (no reference
- * counterpart: the reference allocates its temporaries per call). */
+ * counterpart: the reference allocates its temporaries per call).  Its first
+ * 4 bytes are a status word of the ordered list scans: zero a new buffer
+ * once, then check it with blitz_read_totals; the launches never clear it. */
 size_t blitz_preprocess_scratch_bytes(int64_t P);
 
 /*
@@ -384,9 +390,13 @@ int blitz_loss_combine_backward(const float* g_loss, const float* g_l1, const fl
  * r/cuda_rasterizer/rasterizer_impl.cu:621): copies totals (device int64[2]
  * {R, V}) and, when both are non-NULL, vis_count (device int32) to the host
  * and waits for the stream.  host_totals / host_vis should be pinned.
+ * status / host_status (both NULL, or both given): a device status word of
+ * the ordered scans (the first 4 bytes of a blitz_preprocess_forward_raw
+ * scratch, or of a blitz_exchange_pack scratch) read in the same wait; when
+ * it is non-zero it is cleared and the call returns BLITZ_ESCAN.
  */
-int blitz_read_totals(const int64_t* totals, const int32_t* vis_count, int64_t* host_totals, int32_t* host_vis,
-                      void* stream);
+int blitz_read_totals(const int64_t* totals, const int32_t* vis_count, const uint32_t* status, int64_t* host_totals,
+                      int32_t* host_vis, uint32_t* host_status, void* stream);
 
 /*
  * Zero n device buffers on a side stream, after the work already queued on
@@ -441,14 +451,84 @@ int blitz_adam_update_rows(float* param, const float* grad_rows, float* exp_avg,
  * counterpart: the reference gathers with torch index_select per rank).
  * Row j < n_rows of records/dest_mask goes to every rank r with bit r set,
  * at row dest_offset[r] + k of send [*,12] (16-byte aligned), k counting
- * that rank's rows of this call; send_row receives row_base + j there.
- * dest_offset: HOST int64 array [n_ranks] (n_ranks <= 32); cursor: device
- * int32 [n_ranks], zero on entry.  The order of the rows inside one rank's
- * segment varies from run to run.
+ * that rank's rows of this call in row order: each rank's segment keeps the
+ * order of the rows (with the index-ordered list of the two-kernel
+ * preprocess, ascending index order, the same on every run).  send_row
+ * receives row_base + j there.  dest_offset: HOST int64 array [n_ranks]
+ * (n_ranks <= 32).  scratch: device buffer of
+ * blitz_exchange_pack_scratch_bytes(n_rows, n_ranks) bytes whose first 4
+ * bytes are a status word (zero it once when allocated; check it with
+ * blitz_read_totals); calls on one stream may share it.
  */
+size_t blitz_exchange_pack_scratch_bytes(int64_t n_rows, int n_ranks);
 int blitz_exchange_pack(int64_t n_rows, int n_ranks, const float* records, const uint32_t* dest_mask,
-                        const int64_t* dest_offset, int32_t* cursor, float* send, int32_t* send_row,
-                        int32_t row_base, void* stream);
+                        const int64_t* dest_offset, float* send, int32_t* send_row, int32_t row_base, void* scratch,
+                        size_t scratch_bytes, void* stream);
+
+/*
+ * Batched forms for the multi-GPU step, which preprocesses, packs and
+ * back-propagates every camera of a batch on every rank (no reference
+ * counterpart: the reference calls its preprocess once per camera from
+ * Python, gaussian_renderer/__init__.py:260-324).  Each call loops over the
+ * cameras inside the library, so a batch costs one call instead of one per
+ * camera.  Camera k's output rows start at row k*cam_stride of every output
+ * (means2D + 2*k*cam_stride, records + 12*k*cam_stride, ...).
+ *
+ * blitz_preprocess_forward_raw_batch: blitz_preprocess_forward_raw with a
+ * visible list (ascending index order) and the exchange outputs, for
+ * n_cams cameras.  viewmatrices / projmatrices: device [n_cams][16];
+ * campos: device [n_cams][3]; tanfov: HOST float [n_cams][2] (x, y).
+ * counts: device int32 [n_cams][1 + n_ranks], zero on entry: [k][0] = list
+ * length, [k][1 + r] = rows for rank r.  tile_bounds: device int32
+ * [n_cams][2][n_ranks] (tile_lo row, then tile_hi row); n_ranks = 0 skips
+ * the exchange outputs (records / dest_mask / tile_bounds may be NULL).
+ * scratch: blitz_preprocess_scratch_bytes(P) bytes, shared by the cameras.
+ */
+int blitz_preprocess_forward_raw_batch(int n_cams, int64_t P, int D, int M, const float* xyz,
+                                       const float* scaling_raw, const float* rotation_raw, const float* opacity_raw,
+                                       const float* sh_dc, int64_t dc_stride, const float* sh_rest,
+                                       int64_t rest_stride, float scale_modifier, const float* viewmatrices,
+                                       const float* projmatrices, const float* campos, const float* tanfov,
+                                       int image_height, int image_width, int64_t cam_stride, float* means2D,
+                                       float* depths, int32_t* radii, float* conic_opacity, float* rgb,
+                                       uint32_t* vis_list, int32_t* counts, int n_ranks, const int32_t* tile_bounds,
+                                       float* records, uint32_t* dest_mask, void* scratch, size_t scratch_bytes,
+                                       void* stream);
+
+/*
+ * blitz_exchange_pack_batch: blitz_exchange_pack for n_cams cameras.
+ * n_rows, row_base: HOST int64 [n_cams]; dest_offset: HOST int64
+ * [n_cams][n_ranks]; records / dest_mask rows of camera k start at row
+ * k*cam_stride.  scratch: blitz_exchange_pack_scratch_bytes(max n_rows,
+ * n_ranks) bytes.
+ */
+int blitz_exchange_pack_batch(int n_cams, int n_ranks, const int64_t* n_rows, int64_t cam_stride,
+                              const float* records, const uint32_t* dest_mask, const int64_t* dest_offset,
+                              const int64_t* row_base, float* send, int32_t* send_row, void* scratch,
+                              size_t scratch_bytes, void* stream);
+
+/*
+ * blitz_preprocess_backward_raw_batch: the listed backward of every camera,
+ * accumulated into the raw-parameter gradients (which the caller has
+ * zero-filled or holds earlier contributions).  radii / means2D / vis_list
+ * rows of camera k start at row k*cam_stride; counts as in the forward
+ * batch (only [k][0] is read, with row stride counts_stride).  upstream:
+ * the received 12-float gradient records [c00 c01 c11 op | x y | r g b |
+ * |x| |y| d(min scale)], camera k's j-th listed Gaussian at row
+ * upstream_row0[k] + j (upstream_row0: HOST int64 [n_cams]).
+ */
+int blitz_preprocess_backward_raw_batch(int n_cams, int64_t P, int D, int M, const int32_t* radii,
+                                        const float* means2D, const uint32_t* vis_list, const int32_t* counts,
+                                        int counts_stride, int64_t cam_stride, const float* xyz,
+                                        const float* scaling_raw, const float* rotation_raw,
+                                        const float* opacity_raw, const float* sh_dc, int64_t dc_stride,
+                                        const float* sh_rest, int64_t rest_stride, float scale_modifier,
+                                        const float* viewmatrices, const float* projmatrices, const float* campos,
+                                        const float* tanfov, int image_height, int image_width,
+                                        const float* upstream, const int64_t* upstream_row0, float* g_xyz,
+                                        float* g_scaling_raw, float* g_rotation_raw, float* g_opacity_raw,
+                                        float* g_dc, int64_t g_dc_stride, float* g_rest, int64_t g_rest_stride,
+                                        void* stream);
 
 /*
  * Routing mask bool [P, mp_world_size]: Gaussian i overlaps the tile-id
@@ -462,7 +542,8 @@ int blitz_get_local2j_ids_bool(int image_height, int image_width, int mp_rank, i
                                uint8_t* out, void* stream);
 
 /*
- * Measurement helper (no reference counterpart): `blocks` CTAs of 256
+ * MEASUREMENT-ONLY entry (no reference counterpart; not part of the
+ * rasterizer's operator surface, and no operator calls it): `blocks` CTAs of 256
  * threads each run 8 independent FMA chains for `iters` iterations
  * (2*8*iters FLOP per thread); timing it gives the FP32 throughput used as
  * the blend kernels' roofline denominator.  sink: device float, never written

@@ -1,4 +1,7 @@
-"""Multi-rank host logic on CPU: the packed exchange (gloo, world_size 2) and the
+"""Multi-rank host logic on CPU: the exchange layout of the multi-GPU step
+(blitzgs_b200.distributed.exchange_layout with the count all-gather, the
+all-to-alls and the scatter-back, on gloo ranks; the GPU pack kernel is
+restated on the CPU and checked against the same rule on a GPU) and the
 workload-division policy (pure host code, checked against a restatement of
 gaussian_renderer/workload_division.py:785-873)."""
 import os
@@ -21,27 +24,51 @@ def _free_port():
 
 
 N_CAMS = 3
+SHARD = [40, 47, 33]  # Gaussians per rank (contiguous z-order shards: global id = shard offset + local index)
 
 
 def _rank_data(rank, ws):
-    """Deterministic shard records and routes of one rank."""
-    P = 40 + 7 * rank
+    """One rank's output of the batched preprocess, restated on the CPU: per
+    camera its visible list (ascending local index), each listed Gaussian's
+    12-float record (global id, camera, source rank, ...) and destination
+    mask, and the count row [list length, rows per rank]."""
+    P = SHARD[rank]
+    base = sum(SHARD[:rank])
     g = torch.Generator().manual_seed(100 + rank)
-    recs = []
+    cams = []
     for k in range(N_CAMS):
-        gid = torch.arange(P, dtype=torch.float32) + 1000 * rank
-        recs.append(torch.stack([gid, torch.full((P,), float(k)), torch.full((P,), float(rank)),
-                                 torch.rand(P, generator=g)], 1))
-    send = []
-    for k in range(N_CAMS):
-        per = []
+        listed = (torch.rand(P, generator=g) < 0.7).nonzero(as_tuple=True)[0]
+        L = len(listed)
+        rec = torch.zeros(L, 12)
+        rec[:, 0] = (base + listed).float()
+        rec[:, 1] = float(k)
+        rec[:, 2] = float(rank)
+        rec[:, 3:] = torch.rand(L, 9, generator=g)
+        mask = torch.zeros(L, dtype=torch.int64)
         for j in range(ws):
-            m = torch.rand(P, generator=g) < (0.3 + 0.2 * j)
+            m = torch.rand(L, generator=g) < (0.3 + 0.2 * j)
             if k == 2 and j == 1:
                 m[:] = False  # a camera sends nothing to rank 1
-            per.append(m.nonzero(as_tuple=True)[0])
-        send.append(per)
-    return P, recs, send
+            mask |= m.to(torch.int64) << j
+        cnt = [L] + [int(((mask >> j) & 1).sum()) for j in range(ws)]
+        cams.append((listed, rec, mask, cnt))
+    return cams
+
+
+def _pack(cams, dest_off, n_send, ws):
+    """CPU statement of blitz_exchange_pack_batch: camera k's rows routed to
+    rank j, in list order, from dest_off[k][j]; send_row = offs[k] + slot."""
+    send = torch.zeros(n_send, 12)
+    send_row = torch.full((n_send,), -1, dtype=torch.int64)
+    row0 = 0
+    for k, (listed, rec, mask, cnt) in enumerate(cams):
+        for j in range(ws):
+            rows = ((mask >> j) & 1).nonzero(as_tuple=True)[0]
+            o = dest_off[k][j]
+            send[o:o + len(rows)] = rec[rows]
+            send_row[o:o + len(rows)] = row0 + rows
+        row0 += len(listed)
+    return send, send_row
 
 
 def _worker(rank, ws, port, q):
@@ -49,47 +76,67 @@ def _worker(rank, ws, port, q):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=ws)
     try:
-        P, recs, send = _rank_data(rank, ws)
-        plan = D.plan_exchange(send, N_CAMS)
-        out = D.exchange_forward(recs, plan)
-        # expected: concatenation over source ranks (in order) of their rows routed here
+        cams = _rank_data(rank, ws)
+        # the count all-gather and layout of dist_step, on gloo
+        cnt = torch.tensor([c[3] for c in cams], dtype=torch.int32)
+        allc = torch.empty((ws * N_CAMS, 1 + ws), dtype=torch.int32)
+        dist.all_gather_into_tensor(allc, cnt)
+        allc = allc.view(ws, N_CAMS, 1 + ws).tolist()
+        counts, plan, offs, dest_off = D.exchange_layout(allc, rank, ws, N_CAMS)
+        assert counts == [c[3][0] for c in cams]
+        n_send = sum(plan.send_splits)
+        send, send_row = _pack(cams, dest_off, n_send, ws)
+        assert bool((send_row >= 0).all()), "every send row is written exactly once"
+        recv = torch.empty((sum(plan.recv_splits), 12))
+        dist.all_to_all_single(recv, send, plan.recv_splits, plan.send_splits)
+        # receiver: camera k = its runs in recv_offsets order; the rows are exactly the
+        # Gaussians routed here, in ascending global id (source rank, then local index)
+        everyone = [_rank_data(i, ws) for i in range(ws)]
         for k in range(N_CAMS):
+            segs = [(s_, c) for _, s_, c in plan.recv_offsets[k] if c]
+            got = torch.cat([recv[s_:s_ + c] for s_, c in segs]) if segs else torch.zeros(0, 12)
             exp = []
             for i in range(ws):
-                Pi, ri, si = _rank_data(i, ws)
-                if len(si[k][rank]):
-                    exp.append(ri[k][si[k][rank]])
-            if exp:
-                assert torch.equal(out[k], torch.cat(exp, 0)), (rank, k)
-            else:
-                assert k not in out
-        # backward: gradient = f(record); owner accumulates over destinations
-        grads = {k: v[:, :3] * 2 + 1 for k, v in out.items()}
-        acc = D.exchange_backward(grads, plan, P, N_CAMS, 3)
-        for k in range(N_CAMS):
-            e = torch.zeros(P, 3)
+                listed, rec, mask, _ = everyone[i][k]
+                exp.append(rec[((mask >> rank) & 1).bool()])
+            exp = torch.cat(exp)
+            assert torch.equal(got, exp), (rank, k)
+            ids = got[:, 0]
+            assert bool((ids[1:] > ids[:-1]).all()), "receive order is ascending global id"
+            assert (k in plan.my_cams) == (len(got) > 0)
+        # backward: the gradient rows go back along the same layout and are summed
+        # into the owner's compact per-camera rows (offs[k] + slot) through send_row
+        g_send = recv[:, :3] * 2 + 1 + rank
+        g_recv = torch.empty((n_send, 3))
+        dist.all_to_all_single(g_recv, g_send, plan.send_splits, plan.recv_splits)
+        acc = torch.zeros((offs[-1], 3))
+        acc.index_add_(0, send_row, g_recv)
+        for k, (listed, rec, mask, _) in enumerate(cams):
+            e = torch.zeros(len(listed), 3)
             for j in range(ws):
-                ids = send[k][j]
-                e.index_add_(0, ids, recs[k][ids][:, :3] * 2 + 1)
-            assert torch.allclose(acc[k], e), (rank, k)
+                sel = ((mask >> j) & 1).bool()
+                e[sel] += rec[sel, :3] * 2 + 1 + j
+            assert torch.allclose(acc[offs[k]:offs[k + 1]], e), (rank, k)
         q.put((rank, "ok"))
     except BaseException as ex:  # report to the parent
-        q.put((rank, repr(ex)))
+        import traceback
+        q.put((rank, repr(ex) + traceback.format_exc()))
     finally:
         dist.destroy_process_group()
 
 
-def test_exchange_round_trip_gloo_ws2():
+@pytest.mark.parametrize("ws", [2, 3])
+def test_exchange_layout_round_trip_gloo(ws):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, ws, port, q)) for r in range(ws)]
     for p in procs:
         p.start()
     res = [q.get(timeout=120) for _ in procs]
     for p in procs:
         p.join(timeout=60)
-    assert sorted(res) == [(0, "ok"), (1, "ok")], res
+    assert sorted(res) == [(r, "ok") for r in range(ws)], res
 
 
 def _ref_division(heur, n_rows, ws, coeff):

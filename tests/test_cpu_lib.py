@@ -100,9 +100,10 @@ def test_step_and_exchange_entries_validate_arguments_without_gpu():
     rejects("blitz_loss_combine", None, None, 0.8, 0.2, 100.0, 10.0, 1, None)
     rejects("blitz_loss_combine", 8, None, 0.8, 0.2, 0.0, 10.0, 8, None)
     rejects("blitz_loss_combine_backward", None, None, None, None, 0.8, 0.2, 100.0, 10.0, 8, None)
-    # totals readback: vis_count and host_vis go together
-    rejects("blitz_read_totals", None, None, 8, None, None)
-    rejects("blitz_read_totals", 8, 8, 8, None, None)
+    # totals readback: vis_count and host_vis go together, and so do status and host_status
+    rejects("blitz_read_totals", None, None, None, 8, None, None, None)
+    rejects("blitz_read_totals", 8, 8, None, 8, None, None, None)
+    rejects("blitz_read_totals", 8, None, 8, 8, None, None, None)
     # zero fill: negative count, or a non-empty list without arrays
     rejects("blitz_zero_fill_async", -1, None, None, None)
     rejects("blitz_zero_fill_async", 2, None, None, None)
@@ -119,6 +120,24 @@ def test_step_and_exchange_entries_validate_arguments_without_gpu():
             msg="null pointer")
     rejects("blitz_grad_records_pack", n, starts, counts, None, None, None, None, None, msg="segments")
     rejects("blitz_grad_records_pack", 1, one, one, None, None, None, None, None, msg="null pointer")
+    # ordered pack: needs its scratch; the batched forms check sizes and host arrays
+    offs = (ctypes.c_int64 * 2)(0, 0)
+    rejects("blitz_exchange_pack", 10, 2, 16, 16, offs, 16, 16, 0, None, 0, None, msg="null pointer")
+    rejects("blitz_exchange_pack", 10, 33, 16, 16, offs, 16, 16, 0, 16, 0, None, msg="bad sizes")
+    rejects("blitz_exchange_pack_batch", 2, 0, None, 8, None, None, None, None, None, None, None, 0, None,
+            msg="bad sizes")
+    rejects("blitz_exchange_pack_batch", 2, 2, None, 8, None, None, None, None, None, None, None, 0, None,
+            msg="null pointer")
+    tan = (ctypes.c_float * 4)(0.5, 0.5, 0.5, 0.5)
+    params = [None] * 5 + [0, None, 0, 1.0]  # xyz, _scaling, _rotation, _opacity, dc, dc_stride, rest, stride, mod
+    cams = [None, None, None, tan, 8, 8]      # views, projections, centres, tan(fov), H, W
+    rejects("blitz_preprocess_forward_raw_batch", 2, 100, 3, 15, *params, *cams, 50, *([None] * 7), 0, None, None,
+            None, None, 0, None, msg="bad sizes")
+    rejects("blitz_preprocess_forward_raw_batch", 2, 100, 3, 15, *params, *cams, 100, *([None] * 7), 0, None, None,
+            None, None, 0, None, msg="null pointer")
+    rows0 = (ctypes.c_int64 * 2)(0, 0)
+    rejects("blitz_preprocess_backward_raw_batch", 2, 100, 3, 15, None, None, None, None, 0, 100, *params[:4],
+            *params[4:], *cams, None, rows0, None, None, None, None, None, 0, None, 0, None, msg="bad sizes")
     # empty runs are a no-op, not an error
     zero = (ctypes.c_int64 * 1)(0)
     assert lib.blitz_exchange_unpack(1, one, zero, None, None, None, None, None, None, None, None) == 0

@@ -441,7 +441,7 @@ def test_exchange_records_routing_and_pack(cuda_device):
     masks, per-rank counts) equal what the operator API gives: the same
     per-Gaussian outputs and get_local2j_ids_bool on the reference's tile
     intervals, here for 4 ranks.  blitz_exchange_pack then puts every routed
-    row exactly once into each destination's segment."""
+    row exactly once into each destination's segment, in list order."""
     sc = S.mid(seed=4, P=400_000, n_cams=1)
     cam = sc.cameras[0].to(cuda_device)
     rs = _raster(cam, cuda_device)
@@ -464,6 +464,9 @@ def test_exchange_records_routing_and_pack(cuda_device):
     L = int(out[7].item())
     ids = out[6][:L].long()
     assert L > 1000
+    # the two-kernel preprocess lists the visible Gaussians in ascending index order
+    assert bool((ids[1:] > ids[:-1]).all())
+    assert torch.equal(ids, torch.nonzero(dense[2] > 0).flatten())
     route = ops.local2j_ids_bool(H, W, 0, ranks, m2, r, torch.tensor(division, dtype=torch.int32,
                                                                        device=cuda_device) * gx)
     assert not route[r <= 0].any()  # only listed Gaussians are ever sent
@@ -480,13 +483,13 @@ def test_exchange_records_routing_and_pack(cuda_device):
     n_send = sum(counts)
     send = torch.empty((n_send, 12), dtype=torch.float32, device=cuda_device)
     send_row = torch.empty((n_send,), dtype=torch.int32, device=cuda_device)
-    cursor = torch.zeros((ranks,), dtype=torch.int32, device=cuda_device)
-    ops.exchange_pack(L, rec, mask, offs, cursor, send, send_row, 7)
-    assert cursor.tolist() == counts
+    ops.exchange_pack(L, rec, mask, offs, send, send_row, 7)
     for k in range(ranks):
+        # each segment keeps the list order: the routed rows in ascending order
         rows = send_row[offs[k]:offs[k] + counts[k]].long() - 7
-        assert torch.equal(torch.sort(rows).values, torch.nonzero(bits[:, k]).flatten())
+        assert torch.equal(rows, torch.nonzero(bits[:, k]).flatten())
         assert torch.equal(send[offs[k]:offs[k] + counts[k]], rec[rows])
+    ops.check_scan_status(cuda_device)
 
 
 def test_exchange_unpack_and_gradient_pack(cuda_device):
@@ -528,7 +531,7 @@ def test_preprocess_backward_matches_finite_differences(cuda_device):
     """The preprocess backward against central differences of the preprocess
     forward kernel itself.  Every Gaussian is independent, so one parameter
     component of all Gaussians is perturbed at once and each Gaussian's own
-    scalar L_i = <means2D_i, g_m> + <conic_i, g_c (x2 off-diagonal)> +
+    scalar L_i = <ndc_i, g_m> + <conic_i, g_c (x2 off-diagonal)> +
     <rgb_i, g_rgb> is differenced.  Float32 forward outputs and a step of
     1e-3 (relative for scales) bound the agreement at ~1e-3 normwise."""
     dev = cuda_device
@@ -543,11 +546,14 @@ def test_preprocess_backward_matches_finite_differences(cuda_device):
     gc = torch.randn(P, 4, generator=gen).to(dev)
     gr = torch.randn(P, 3, generator=gen).to(dev)
     w3 = torch.tensor([1.0, 2.0, 1.0], dtype=torch.float64, device=dev)
+    # the screen-mean gradient of the operator contract is per NDC unit
+    # (pixel = (ndc + 1) W / 2 - 1/2): weight pixels by 2/W and 2/H
+    w2 = torch.tensor([2.0 / cam.image_width, 2.0 / cam.image_height], dtype=torch.float64, device=dev)
 
     def fwd(xyz_, s_, q_, shs_):
         m2, d, r, co, rgb, _, cl = ops.preprocess_forward(xyz_, s_, q_, o, ops.sh_layout(shs=shs_), rs,
                                                           want_clamped=True)
-        L = ((m2.double() * gm.double()).sum(1) + (co[:, :3].double() * gc[:, :3].double() * w3).sum(1) +
+        L = ((m2.double() * gm.double() * w2).sum(1) + (co[:, :3].double() * gc[:, :3].double() * w3).sum(1) +
              (rgb.double() * gr.double()).sum(1))
         return L, r, cl
 
