@@ -27,6 +27,7 @@ SIGNATURES = {
         _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "blitz_preprocess_scratch_bytes": (_sz, [_i64]),
     "blitz_exchange_pack_scratch_bytes": (_sz, [_i64, _i32]),
+    "blitz_preprocess_batch_scratch_bytes": (_sz, [_i32, _i64]),
     "blitz_exchange_pack": (_i32, [_i64, _i32, _vp, _vp, _vp, _vp, _vp, _i32, _vp, _sz, _vp]),
     "blitz_exchange_pack_batch": (_i32, [_i32, _i32, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "blitz_preprocess_forward_raw_batch": (_i32, [

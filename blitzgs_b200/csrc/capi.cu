@@ -64,6 +64,69 @@ PreprocessParams make_pp(int64_t P, int D, int M, const float* means3D, const fl
   return p;
 }
 
+static int preprocess_forward_raw_impl(int64_t P, int D, int M, const float* xyz, const float* scaling_raw,
+                                 const float* rotation_raw, const float* rotation_norm,
+                                 const float* opacity_raw, const float* sh_dc, int64_t dc_stride,
+                                 const float* sh_rest, int64_t rest_stride, float scale_modifier,
+                                 const float* viewmatrix, const float* projmatrix, const float* campos,
+                                 float tanfovx, float tanfovy, int image_height, int image_width,
+                                 float* means2D, float* depths, int32_t* radii, float* conic_opacity,
+                                 float* rgb, double* reg_sums, uint32_t* vis_list, int32_t* vis_count,
+                                 const uint8_t* compute_locally, uint32_t* counts, uint64_t* totals,
+                                 uint32_t* slot_of, const blitz_exchange_out* exchange, void* scratch,
+                                 size_t scratch_bytes, void* stream, int grid_share,
+                                       unsigned* status) {
+  if (P < 0 || D < 0 || D > 3 || M < 0 || M > 15 || image_height <= 0 || image_width <= 0)
+    return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: bad sizes");
+  if (P == 0) return 0;
+  if (!xyz || !scaling_raw || !rotation_raw || !opacity_raw || !sh_dc || !viewmatrix || !projmatrix || !campos ||
+      !means2D || !depths || !radii || !conic_opacity || !rgb || (M > 0 && !sh_rest) || ((vis_list == nullptr) != (vis_count == nullptr)) ||
+      ((counts == nullptr) != (totals == nullptr)))
+    return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: null pointer");
+  if (P >= (int64_t)0xffffffff) return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: P must be < 2^32");
+  if (!aligned16(rotation_raw) || !aligned16(conic_opacity) || (reinterpret_cast<uintptr_t>(means2D) & 7u))
+    return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: alignment");
+  PreprocessParams p = make_pp(P, D, M, xyz, scaling_raw, rotation_raw, sh_dc, dc_stride, sh_rest, rest_stride,
+                               opacity_raw, scale_modifier, viewmatrix, projmatrix, campos, tanfovx, tanfovy,
+                               image_height, image_width);
+  p.raw = true;
+  p.rot_norm = rotation_norm;
+  p.reg_sums = reg_sums;
+  p.vis_list_out = vis_list;
+  p.vis_count_out = vis_count;
+  p.listed_rows_only = vis_list != nullptr;
+  if (slot_of && !vis_list) return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: slot_of needs vis_list");
+  p.slot_of_out = slot_of;
+  if (exchange && exchange->n_ranks > 0) {
+    const blitz_exchange_out& x = *exchange;
+    if (!vis_list || x.n_ranks > 32 || !x.tile_lo || !x.tile_hi || !x.records || !x.dest_mask || !x.dest_counts)
+      return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: exchange outputs need vis_list, n_ranks <= 32 and "
+                                "non-null buffers");
+    if (!aligned16(x.records)) return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: records must be 16-byte aligned");
+    // the exchange must keep one order on every run: list in index order
+    if (!scratch) return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: exchange outputs need the scratch");
+    p.ordered_list = true;
+    p.x_ranks = x.n_ranks;
+    p.x_tile_lo = x.tile_lo;
+    p.x_tile_hi = x.tile_hi;
+    p.x_records = x.records;
+    p.x_mask = x.dest_mask;
+    p.x_counts = x.dest_counts;
+  }
+  p.counts_out = counts;
+  p.totals_out = reinterpret_cast<unsigned long long*>(totals);
+  p.compute_locally = reinterpret_cast<const bool*>(compute_locally);
+  p.out_means2D = means2D;
+  p.out_depths = depths;
+  p.out_radii = radii;
+  p.out_conic_opacity = conic_opacity;
+  p.out_rgb = rgb;
+  if (scratch && scratch_bytes < preprocess_scratch_bytes(P))
+    return fail(BLITZ_ESCRATCH, "blitz_preprocess_forward_raw: scratch smaller than blitz_preprocess_scratch_bytes(P)");
+  return check(launch_preprocess_fwd(p, S(stream), scratch, scratch_bytes, grid_share, status),
+               "blitz_preprocess_forward_raw");
+}
+
 }  // namespace
 
 namespace blitz {
@@ -162,54 +225,11 @@ int blitz_preprocess_forward_raw(int64_t P, int D, int M, const float* xyz, cons
                                  const uint8_t* compute_locally, uint32_t* counts, uint64_t* totals,
                                  uint32_t* slot_of, const blitz_exchange_out* exchange, void* scratch,
                                  size_t scratch_bytes, void* stream) {
-  if (P < 0 || D < 0 || D > 3 || M < 0 || M > 15 || image_height <= 0 || image_width <= 0)
-    return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: bad sizes");
-  if (P == 0) return 0;
-  if (!xyz || !scaling_raw || !rotation_raw || !opacity_raw || !sh_dc || !viewmatrix || !projmatrix || !campos ||
-      !means2D || !depths || !radii || !conic_opacity || !rgb || (M > 0 && !sh_rest) || ((vis_list == nullptr) != (vis_count == nullptr)) ||
-      ((counts == nullptr) != (totals == nullptr)))
-    return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: null pointer");
-  if (P >= (int64_t)0xffffffff) return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: P must be < 2^32");
-  if (!aligned16(rotation_raw) || !aligned16(conic_opacity) || (reinterpret_cast<uintptr_t>(means2D) & 7u))
-    return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: alignment");
-  PreprocessParams p = make_pp(P, D, M, xyz, scaling_raw, rotation_raw, sh_dc, dc_stride, sh_rest, rest_stride,
-                               opacity_raw, scale_modifier, viewmatrix, projmatrix, campos, tanfovx, tanfovy,
-                               image_height, image_width);
-  p.raw = true;
-  p.rot_norm = rotation_norm;
-  p.reg_sums = reg_sums;
-  p.vis_list_out = vis_list;
-  p.vis_count_out = vis_count;
-  p.listed_rows_only = vis_list != nullptr;
-  if (slot_of && !vis_list) return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: slot_of needs vis_list");
-  p.slot_of_out = slot_of;
-  if (exchange && exchange->n_ranks > 0) {
-    const blitz_exchange_out& x = *exchange;
-    if (!vis_list || x.n_ranks > 32 || !x.tile_lo || !x.tile_hi || !x.records || !x.dest_mask || !x.dest_counts)
-      return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: exchange outputs need vis_list, n_ranks <= 32 and "
-                                "non-null buffers");
-    if (!aligned16(x.records)) return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: records must be 16-byte aligned");
-    // the exchange must keep one order on every run: list in index order
-    if (!scratch) return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw: exchange outputs need the scratch");
-    p.ordered_list = true;
-    p.x_ranks = x.n_ranks;
-    p.x_tile_lo = x.tile_lo;
-    p.x_tile_hi = x.tile_hi;
-    p.x_records = x.records;
-    p.x_mask = x.dest_mask;
-    p.x_counts = x.dest_counts;
-  }
-  p.counts_out = counts;
-  p.totals_out = reinterpret_cast<unsigned long long*>(totals);
-  p.compute_locally = reinterpret_cast<const bool*>(compute_locally);
-  p.out_means2D = means2D;
-  p.out_depths = depths;
-  p.out_radii = radii;
-  p.out_conic_opacity = conic_opacity;
-  p.out_rgb = rgb;
-  if (scratch && scratch_bytes < preprocess_scratch_bytes(P))
-    return fail(BLITZ_ESCRATCH, "blitz_preprocess_forward_raw: scratch smaller than blitz_preprocess_scratch_bytes(P)");
-  return check(launch_preprocess_fwd(p, S(stream), scratch, scratch_bytes), "blitz_preprocess_forward_raw");
+  return preprocess_forward_raw_impl(P, D, M, xyz, scaling_raw, rotation_raw, rotation_norm, opacity_raw, sh_dc,
+                                     dc_stride, sh_rest, rest_stride, scale_modifier, viewmatrix, projmatrix, campos,
+                                     tanfovx, tanfovy, image_height, image_width, means2D, depths, radii,
+                                     conic_opacity, rgb, reg_sums, vis_list, vis_count, compute_locally, counts,
+                                     totals, slot_of, exchange, scratch, scratch_bytes, stream, 1, nullptr);
 }
 
 size_t blitz_preprocess_scratch_bytes(int64_t P) { return preprocess_scratch_bytes(P); }
@@ -607,6 +627,54 @@ int blitz_exchange_pack_batch(int n_cams, int n_ranks, const int64_t* n_rows, in
   return 0;
 }
 
+}  // extern "C"
+
+namespace {
+
+// Side streams on which the batched preprocess runs its cameras side by
+// side, per device (created on first use; the library's only other
+// resources are the zero fill's stream and events).
+constexpr int kBatchStreams = 8;
+struct BatchStreams {
+  bool ready = false;
+  cudaStream_t s[kBatchStreams] = {};
+  cudaEvent_t fork = nullptr, join[kBatchStreams] = {};
+};
+BatchStreams g_batch[64];
+std::mutex g_batch_mu;
+
+int batch_streams(BatchStreams** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev < 0 || dev >= 64) return BLITZ_EINVAL;
+  BatchStreams& b = g_batch[dev];
+  if (!b.ready) {
+    std::lock_guard<std::mutex> lock(g_batch_mu);
+    if (!b.ready) {
+      e = cudaEventCreateWithFlags(&b.fork, cudaEventDisableTiming);
+      for (int i = 0; i < kBatchStreams && e == cudaSuccess; ++i) {
+        e = cudaStreamCreateWithFlags(&b.s[i], cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&b.join[i], cudaEventDisableTiming);
+      }
+      if (e != cudaSuccess) return (int)e;
+      b.ready = true;
+    }
+  }
+  *out = &b;
+  return 0;
+}
+
+size_t batch_slice_bytes(int64_t P) { return (preprocess_scratch_bytes(P) + 255) / 256 * 256; }
+
+}  // namespace
+
+extern "C" {
+
+size_t blitz_preprocess_batch_scratch_bytes(int n_cams, int64_t P) {
+  return (size_t)std::max(n_cams, 1) * batch_slice_bytes(P);
+}
+
 int blitz_preprocess_forward_raw_batch(int n_cams, int64_t P, int D, int M, const float* xyz,
                                        const float* scaling_raw, const float* rotation_raw, const float* opacity_raw,
                                        const float* sh_dc, int64_t dc_stride, const float* sh_rest,
@@ -626,8 +694,23 @@ int blitz_preprocess_forward_raw_batch(int n_cams, int64_t P, int D, int M, cons
     return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw_batch: exchange outputs need tile_bounds, records, "
                               "dest_mask");
   if ((cam_stride & 3) != 0) return fail(BLITZ_EINVAL, "blitz_preprocess_forward_raw_batch: cam_stride % 4");
+  const size_t slice = batch_slice_bytes(P);
+  if (scratch_bytes < (size_t)n_cams * slice)
+    return fail(BLITZ_ESCRATCH, "blitz_preprocess_forward_raw_batch: scratch smaller than "
+                                "blitz_preprocess_batch_scratch_bytes(n_cams, P)");
+  BatchStreams* bs = nullptr;
+  int rc0 = batch_streams(&bs);
+  if (rc0) return fail(rc0, "blitz_preprocess_forward_raw_batch: side streams");
+  // cameras run side by side on the side streams, each on its own scratch
+  // slice; all report into the first slice's status word
+  const int ns = std::min(n_cams, kBatchStreams);
+  cudaError_t e = cudaEventRecord(bs->fork, S(stream));
+  for (int i = 0; i < ns && e == cudaSuccess; ++i) e = cudaStreamWaitEvent(bs->s[i], bs->fork, 0);
+  if (e != cudaSuccess) return check((int)e, "blitz_preprocess_forward_raw_batch: fork");
+  unsigned* status = reinterpret_cast<unsigned*>(static_cast<char*>(scratch) + kPreStatusOffset);
   const int cs = 1 + n_ranks;
-  for (int c = 0; c < n_cams; ++c) {
+  int rc_all = 0;
+  for (int c = 0; c < n_cams && !rc_all; ++c) {
     blitz_exchange_out x{};
     x.n_ranks = n_ranks;
     if (n_ranks > 0) {
@@ -638,15 +721,20 @@ int blitz_preprocess_forward_raw_batch(int n_cams, int64_t P, int D, int M, cons
       x.dest_counts = counts + (int64_t)c * cs + 1;
     }
     const int64_t o = c * cam_stride;
-    const int rc = blitz_preprocess_forward_raw(
+    rc_all = preprocess_forward_raw_impl(
         P, D, M, xyz, scaling_raw, rotation_raw, nullptr, opacity_raw, sh_dc, dc_stride, sh_rest, rest_stride,
         scale_modifier, viewmatrices + 16 * c, projmatrices + 16 * c, campos + 3 * c, tanfov[2 * c],
         tanfov[2 * c + 1], image_height, image_width, means2D + 2 * o, depths + o, radii + o, conic_opacity + 4 * o,
         rgb + 3 * o, nullptr, vis_list + o, counts + (int64_t)c * cs, nullptr, nullptr, nullptr, nullptr,
-        n_ranks > 0 ? &x : nullptr, scratch, scratch_bytes, stream);
-    if (rc) return rc;
+        n_ranks > 0 ? &x : nullptr, static_cast<char*>(scratch) + (size_t)c * slice, slice, bs->s[c % ns], 1,
+        status);
   }
-  return 0;
+  // join: the caller's stream waits for every side stream (also after an error)
+  for (int i = 0; i < ns; ++i) {
+    cudaEventRecord(bs->join[i], bs->s[i]);
+    cudaStreamWaitEvent(S(stream), bs->join[i], 0);
+  }
+  return rc_all;
 }
 
 int blitz_preprocess_backward_raw_batch(int n_cams, int64_t P, int D, int M, const int32_t* radii,

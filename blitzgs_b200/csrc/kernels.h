@@ -110,8 +110,11 @@ struct PreprocessBwdParams {
 // (the caller zeroes a new buffer and reads / clears the word).
 constexpr size_t kPreStatusOffset = 0;
 size_t preprocess_scratch_bytes(int64_t P);
+// grid_share: number of such launches running side by side (each takes that
+// share of the device's resident blocks); status: overrides the scratch's
+// own status word.
 int launch_preprocess_fwd(const PreprocessParams& p, cudaStream_t st, void* scratch = nullptr,
-                          size_t scratch_bytes = 0);
+                          size_t scratch_bytes = 0, int grid_share = 1, unsigned* status = nullptr);
 int launch_preprocess_bwd(const PreprocessBwdParams& p, bool accumulate, cudaStream_t st);
 
 // ---------------------------------------------------------------------------

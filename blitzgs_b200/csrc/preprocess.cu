@@ -1191,7 +1191,8 @@ size_t preprocess_scratch_bytes(int64_t P) {
   return pre_scratch_layout(nullptr, P).zero_bytes + sizeof(uint32_t) * (size_t)std::max<int64_t>(P, 1);
 }
 
-int launch_preprocess_fwd(const PreprocessParams& p, cudaStream_t st, void* scratch, size_t scratch_bytes) {
+int launch_preprocess_fwd(const PreprocessParams& p, cudaStream_t st, void* scratch, size_t scratch_bytes,
+                          int grid_share, unsigned* status) {
   if (p.totals_out) cudaMemsetAsync(p.totals_out, 0, 2 * sizeof(unsigned long long), st);
   if (p.P <= 0) return (int)cudaGetLastError();
   const int n_tiles = p.grid_x * p.grid_y;
@@ -1200,9 +1201,12 @@ int launch_preprocess_fwd(const PreprocessParams& p, cudaStream_t st, void* scra
   if (scratch && scratch_bytes >= preprocess_scratch_bytes(p.P)) {
     // cull pass over every Gaussian, then the full computation over the
     // candidates (persistent grid: the count is only known on the device)
-    const PreScratch s = pre_scratch_layout(scratch, p.P);
+    PreScratch s = pre_scratch_layout(scratch, p.P);
+    if (status) s.status = status;
     static const int resident_full = resident_blocks(preprocess_full_kernel<false>, kPreThreads, kPreMaskSmem);
-    const int64_t blocks = std::min<int64_t>((p.P + kPreThreads - 1) / kPreThreads, resident_full);
+    // launches that run side by side (grid_share of them) split the device
+    const int64_t blocks = std::min<int64_t>((p.P + kPreThreads - 1) / kPreThreads,
+                                             std::max(resident_full / std::max(grid_share, 1), 1));
     if (p.ordered_list) {
       cudaMemsetAsync(static_cast<char*>(scratch) + 256, 0, s.zero_bytes - 256, st);
       preprocess_cull_kernel<true><<<(unsigned)n_chunks, kPreThreads, 0, st>>>(p, s.cand, s.cand_count, s.cull_ticket,

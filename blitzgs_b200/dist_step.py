@@ -61,11 +61,11 @@ class _DistributedBatch(torch.autograd.Function):
         #    visible lists are in ascending index order.
         P = xyz.shape[0]
         gx = D.CONTEXT.TILE_X
-        table = _pinned_table(n_cams, ws)  # tile interval [lo, hi) of every rank, per camera
+        table, tnp = _pinned_table(n_cams, ws)  # tile interval [lo, hi) of every rank, per camera
         for k, st in enumerate(strategies):
             for r_local, g in enumerate(st.gpu_ids):
-                table[k, 0, g] = st.division_pos[r_local] * gx
-                table[k, 1, g] = st.division_pos[r_local + 1] * gx
+                tnp[k, 0, g] = st.division_pos[r_local] * gx
+                tnp[k, 1, g] = st.division_pos[r_local + 1] * gx
         table_dev = table[:n_cams].to(dev, non_blocking=True)
         cnt = torch.zeros((n_cams, 1 + ws), dtype=torch.int32, device=dev)  # list length | rows per rank
         # one allocation per buffer kind for the whole batch; camera k's rows start at k*Pc
@@ -214,10 +214,10 @@ def _pinned_table(n_cams, ws):
     (zeros: a rank that renders none of a camera).  Reuse is safe: every step
     synchronises with the host (the count all-gather) after its copy."""
     t = _TABLE.get(ws)
-    if t is None or t.shape[0] < n_cams:
-        t = torch.zeros((max(n_cams, 8), 2, ws), dtype=torch.int32).pin_memory()
-        _TABLE[ws] = t
-    t[:n_cams].zero_()
+    if t is None or t[0].shape[0] < n_cams:
+        buf = torch.zeros((max(n_cams, 8), 2, ws), dtype=torch.int32).pin_memory()
+        t = _TABLE[ws] = (buf, buf.numpy())  # numpy view: element writes cost far less than tensor indexing
+    t[1][:n_cams] = 0
     return t
 
 

@@ -346,7 +346,7 @@ def preprocess_forward_raw_batch(xyz, scaling_raw, rotation_raw, opacity_raw, sh
     means2D, depths, radii, conic, rgb, vlist = out
     n_ranks = 0 if exchange is None else int(exchange[0].shape[-1])
     tb, rec, mask = exchange if exchange is not None else (None, None, None)
-    scratch = PRE_SCRATCH.get(xyz.device, _lib.load().blitz_preprocess_scratch_bytes(P))
+    scratch = PRE_SCRATCH.get(xyz.device, _lib.load().blitz_preprocess_batch_scratch_bytes(n, P))
     tok = TIMER.begin("preprocess_fwd")
     _lib.call("blitz_preprocess_forward_raw_batch", n, P, int(r0.sh_degree), M, ptr(xyz), ptr(scaling_raw),
               ptr(rotation_raw), ptr(opacity_raw), ptr(dc), dcs, ptr(rest), rs, float(r0.scale_modifier), ptr(views),

@@ -482,8 +482,13 @@ int blitz_exchange_pack(int64_t n_rows, int n_ranks, const float* records, const
  * length, [k][1 + r] = rows for rank r.  tile_bounds: device int32
  * [n_cams][2][n_ranks] (tile_lo row, then tile_hi row); n_ranks = 0 skips
  * the exchange outputs (records / dest_mask / tile_bounds may be NULL).
- * scratch: blitz_preprocess_scratch_bytes(P) bytes, shared by the cameras.
+ * The cameras run side by side on up to 8 side streams the library keeps
+ * per device, ordered after the work already on `stream`; `stream` waits for
+ * all of them before the call returns.  scratch:
+ * blitz_preprocess_batch_scratch_bytes(n_cams, P) bytes (a slice per
+ * camera); its first 4 bytes are the status word of blitz_read_totals.
  */
+size_t blitz_preprocess_batch_scratch_bytes(int n_cams, int64_t P);
 int blitz_preprocess_forward_raw_batch(int n_cams, int64_t P, int D, int M, const float* xyz,
                                        const float* scaling_raw, const float* rotation_raw, const float* opacity_raw,
                                        const float* sh_dc, int64_t dc_stride, const float* sh_rest,
