@@ -255,6 +255,31 @@ def run_ours(args, ws, rank, local):
     def batch_ids(it):
         return [((it * bsz * ws) + k) % n_cams for k in range(bsz * ws)]
 
+    gx_, gy_ = (W + 15) // 16, (H + 15) // 16
+    all_tiles = torch.ones((gy_, gx_), dtype=torch.bool, device=dev)
+
+    def operator_view_loss(raster, gt):
+        """One camera through the reference-compatible operator API, as a
+        trainer that keeps the reference's renderer calls runs it: torch
+        activations, GaussianRasterizer.preprocess_gaussians /
+        render_gaussians, the fused L1+SSIM loss and the min-scale
+        regulariser over the visible Gaussians."""
+        from blitzgs_b200 import rasterizer as RZ
+        from blitzgs_b200.loss import band_loss
+        xyz, s_raw, q_raw, o_raw, dc, rest = model
+        scales = torch.exp(s_raw)
+        rast = RZ.GaussianRasterizer(raster)
+        ca = {"stats_collector": {}}
+        m2, rgb, co, radii, depths = rast.preprocess_gaussians(xyz, scales, torch.nn.functional.normalize(q_raw),
+                                                               torch.cat((dc, rest), 1), torch.sigmoid(o_raw), ca)
+        abs_pts = torch.zeros_like(xyz) + 0
+        color, *_ = rast.render_gaussians(m2, abs_pts, co, rgb, None, depths, radii, all_tiles, None, ca)
+        l1, ss = band_loss(color, gt)
+        n3 = H * W * 3
+        loss = 0.8 * (l1 / n3) + 0.2 * (1.0 - ss / n3)
+        vis = radii > 0
+        return loss + 10.0 * torch.sort(scales[vis], dim=-1)[0][..., 0].mean()
+
     def one_step(it, e2e, trace=None):
         if trace is not None:
             trace.append(("start", time.perf_counter()))
@@ -271,7 +296,10 @@ def run_ours(args, ws, rank, local):
                     h2d[0] = 3 * H * W * bsz
                 else:
                     gt = gts_dev[ci]
-                loss, *_ = ST.view_loss(model, rasters[ci], gt, sparse_grad=args.sparse_grad)
+                if args.api == "operator":
+                    loss = operator_view_loss(rasters[ci], gt)
+                else:
+                    loss, *_ = ST.view_loss(model, rasters[ci], gt, sparse_grad=args.sparse_grad)
                 total = loss if total is None else total + loss
                 n_launch[0] += LAUNCHES_PER_VIEW
                 if trace is not None:
@@ -674,6 +702,9 @@ def main():
     ap.add_argument("--sparse-grad", action="store_true",
                     help="parameter gradients as sparse rows of the visible Gaussians (1 GPU; default dense)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--api", choices=["fused", "operator"], default="fused",
+                    help="fused: blitzgs_b200.step.view_loss; operator: the reference-compatible operator API "
+                         "(GaussianRasterizer per camera with torch activations), 1 GPU")
     ap.add_argument("--gaussians", type=int, default=None,
                     help="Gaussian count of the scene (default: the config's); a smaller scene of the same "
                          "distribution is the profiling case")
@@ -686,7 +717,9 @@ def main():
            "gaussians": None, "image": None, "views_per_gpu_per_step": args.bsz,
            "parallelism": f"dp{ws}" if ws > 1 else "single", "l2": "inputs larger than L2 (8M x 236 B params)",
            "grad": "sparse rows (visible Gaussians)" if args.sparse_grad else "dense",
-           "layout": "Gaussians in z-order of their means" if args.layout == "zorder" else "generator order"}
+           "layout": "Gaussians in z-order of their means" if args.layout == "zorder" else "generator order",
+           "api": "fused training step (blitzgs_b200.step.view_loss)" if args.api == "fused" else
+           "operator API (GaussianRasterizer.preprocess_gaussians / render_gaussians per camera, torch activations)"}
 
     if args.impl == "reference":
         if rank != 0:

@@ -16,6 +16,9 @@ The reference's Python autograd wrappers
 and its loss helpers (utils/loss_utils.py) are installed beside the built
 modules, as ``pip install --target`` would, so the reference arm of
 ``bench.py`` and the golden-vector generator can run the stock code path.
+The renderer glue (gaussian_renderer/*.py and the utils modules it imports)
+goes to ``oracle/_ref/refsrc`` for the drop-in test, which runs it on top of
+either rasterizer.
 
 Usage:  python oracle/build_ref.py [--ref /path/to/reference] [--force]
 """
@@ -43,6 +46,14 @@ MODULES = {
          "cuda_rasterizer/backward.cu", "cuda_rasterizer/adam.cu",
          "rasterize_points.cu", "conv.cu", "ext.cpp"],
     ),
+}
+
+# reference Python modules the renderer-glue test imports (installed under
+# oracle/_ref/refsrc; scene.*, pytorch3d, plyfile and simple_knn are stubbed
+# by the test itself)
+GLUE = {
+    "gaussian_renderer": ["__init__.py", "workload_division.py", "loss_distribution.py"],
+    "utils": ["general_utils.py", "loss_utils.py", "sh_utils.py", "graphics_utils.py", "system_utils.py"],
 }
 
 _CHILD = r"""
@@ -95,6 +106,19 @@ def build(ref, force=False):
     lu = os.path.join(ref, "utils", "loss_utils.py")
     if os.path.exists(lu):
         shutil.copyfile(lu, os.path.join(OUT, "ref_loss_utils.py"))
+    # the reference's renderer glue and the utils modules it imports, as
+    # installed packages, so a GPU test can run the stock
+    # distributed_preprocess3dgs_and_all2all_final -> render_final ->
+    # batched_loss_computation path on either rasterizer
+    glue = os.path.join(OUT, "refsrc")
+    for pkg, files in GLUE.items():
+        dst = os.path.join(glue, pkg)
+        os.makedirs(dst, exist_ok=True)
+        for f in files:
+            src = os.path.join(ref, pkg, f)
+            if os.path.exists(src):
+                shutil.copyfile(src, os.path.join(dst, f))
+    open(os.path.join(glue, "utils", "__init__.py"), "a").close()
     return ok
 
 
