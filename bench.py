@@ -439,9 +439,10 @@ def stage_bytes(name, metas):
     tile (n_vis of the same view), L = Gaussians with radius > 0 (the visible
     list, when the launch produced or consumed one).
       preprocess_fwd with the fused tile count and the list: every Gaussian
-        reads xyz (12) and writes its radius and tile count (8); listed ones
-        also read scale 12, rotation 16, opacity 4, SH 192 and write their
-        40 output bytes and list slot 4.
+        reads xyz and its log-scales (24: the cull's bound needs the largest
+        scale) and writes its radius and tile count (8); listed ones also
+        read rotation 16, opacity 4, SH 192 (and xyz, scale again: 24) and
+        write their 40 output bytes and list slot 4.
       preprocess_fwd, dense: every Gaussian reads xyz (12) and writes its 44
         output bytes; visible ones also read scale 12, rotation 16, opacity 4,
         SH 192.
@@ -455,7 +456,7 @@ def stage_bytes(name, metas):
         P, V = m.get("P", 0), m.get("n_vis", 0)
         L = int(m["n_list"]) if "n_list" in m else None
         if name == "preprocess_fwd":
-            tot += (20.0 * P + 268.0 * L) if (L is not None and m.get("fused_count")) else (56.0 * P + 224.0 * V)
+            tot += (32.0 * P + 280.0 * L) if (L is not None and m.get("fused_count")) else (56.0 * P + 224.0 * V)
         elif name == "preprocess_bwd":
             tot += 508.0 * L if L is not None else (240.0 * P + 272.0 * V)
         else:
@@ -465,10 +466,12 @@ def stage_bytes(name, metas):
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of each
 # stage's kernels, summed over the stage's kernels, measured by ncu on this
-# bench's city workload; see profiles/ for the capture and its command.
+# bench's city workload (one-pass capture of the full workload).
 # Fill in again whenever the kernels change.
-NCU_TRAFFIC = {}
-NCU_TRAFFIC_SOURCE = "ncu capture of bench.py (city, 1 GPU), mean per launch"
+NCU_TRAFFIC = {"preprocess_fwd": 341_700_000, "blend_fwd": 19_800_000, "blend_bwd": 69_700_000,
+               "preprocess_bwd": 165_200_000}
+NCU_TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of bench.py (city, 1 GPU), mean over two "
+                      "launches of the full workload")
 
 
 def roofline_from_stages(stages, peaks, peak_kind, n_vis_per_call, fp32_peak=None):
@@ -794,7 +797,7 @@ def main():
 
 
 # kernels launched by the binning + blend calls of one view, as counted in the ncu
-# launch list (profiles/launches_city8M_bench.md): cub select (2), depth-key gather (1),
+# ncu launch list of the bench: cub select (2), depth-key gather (1),
 # 32-bit cub onesweep sort (histogram + exclusive sum + 4 passes), count gather (1),
 # cub exclusive scan (2), emit (1), 12-bit sort (histogram + exclusive sum + 2 passes),
 # tile ranges (1), blend (1)

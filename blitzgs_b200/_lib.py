@@ -39,7 +39,7 @@ SIGNATURES = {
     "blitz_get_local2j_ids_bool_adjust_mode6": (_i32, [_i32, _i32, _i32, _i32, _i64, _vp, _vp, _vp, _i32, _vp,
                                                         _vp]),
     "blitz_adam_update": (_i32, [_vp, _vp, _vp, _vp, _vp, _f32, _f32, _f32, _f32, _i64, _i64, _vp]),
-    "blitz_adam_update_rows": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _f32, _f32, _f32, _f32, _i64, _i64,
+    "blitz_adam_update_rows": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _f32, _f32, _f32, _f32, _f32, _i64, _i64,
                                       _vp]),
     "blitz_preprocess_backward_raw": (_i32, [
         _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _f32, _vp, _vp, _vp, _f32,

@@ -11,7 +11,8 @@
 //     per-element expressions, so the same FMA contractions);
 //   * rows: only the listed rows, with the gradient given as compact rows
 //     (the sparse gradient of view_loss(sparse_grad=True)): no pass over the
-//     invisible Gaussians at all.
+//     invisible Gaussians at all.  It also folds in the trainer's gradient
+//     scaling by 1/bsz (train_internal.py:504-515), bit for bit.
 // Both are HBM bound: per updated element, read param, grad, two moments
 // (16 B) and write param and moments (12 B).
 #include "kernels.h"
@@ -54,7 +55,9 @@ __global__ void __launch_bounds__(256) adam_rows_kernel(AdamParams p) {
   if (g < 0 || g >= p.N) return;
   const int64_t k = g * p.M + c;
   float param = p.param[k], m = p.exp_avg[k], v = p.exp_avg_sq[k];
-  adam_element(param, p.grad[e], m, v, p.lr, p.b1, p.b2, p.eps);
+  // the trainer's grad /= bsz, fused: PyTorch divides a float tensor by a host
+  // scalar as a multiplication by the scalar's float reciprocal
+  adam_element(param, __fmul_rn(p.grad[e], p.grad_scale), m, v, p.lr, p.b1, p.b2, p.eps);
   p.param[k] = param;
   p.exp_avg[k] = m;
   p.exp_avg_sq[k] = v;

@@ -54,6 +54,8 @@
 // recovered with one reciprocal of (1 - alpha) (fast division, 1 - alpha in
 // [0.01, 1)) shared by the two divisions of the reference; the gradients
 // differ from IEEE division by ~1e-7 relative.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -363,9 +365,10 @@ __device__ __forceinline__ float warp_transpose_reduce16(float v[16]) {
 // in the same order, without the box tests and without the iterations in
 // which no pixel of the strip contributes.
 template <bool LISTS>
-__global__ void __launch_bounds__(32, 28) blend_bwd_kernel(BlendBwdParams p) {
-  const int tile = blockIdx.x / kStrips;
-  const int strip = blockIdx.x - tile * kStrips;
+__device__ __forceinline__ void blend_bwd_strip(const BlendBwdParams& p, int gstrip, float4* s_a, float4* s_b,
+                                                float4* s_c, int* s_id) {
+  const int tile = gstrip / kStrips;
+  const int strip = gstrip - tile * kStrips;
   if (p.compute_locally && !p.compute_locally[tile]) return;
   const int tx = tile % p.grid_x, ty = tile / p.grid_x;
   const int lane = threadIdx.x;
@@ -376,10 +379,6 @@ __global__ void __launch_bounds__(32, 28) blend_bwd_kernel(BlendBwdParams p) {
   const int64_t pix = (int64_t)p.W * py + px;
   const float2 pixf = make_float2((float)px, (float)py);
 
-  __shared__ float4 s_a[32];
-  __shared__ float4 s_b[32];
-  __shared__ float4 s_c[32];
-  __shared__ int s_id[32];
   const float2 so = strip_origin(tx, ty, strip);
 
   const uint2 range = p.ranges[tile];
@@ -554,6 +553,19 @@ __global__ void __launch_bounds__(32, 28) blend_bwd_kernel(BlendBwdParams p) {
   }
 }
 
+// One warp per CTA, CTA g replays strip g (tile g / kStrips).  (Persistent
+// one-warp CTAs looping over the strips, with static or ticketed strip
+// assignment, measured 45-55% slower on the city workload.)
+template <bool LISTS>
+__global__ void __launch_bounds__(32, 28) blend_bwd_kernel(BlendBwdParams p, int n_strips) {
+  __shared__ float4 s_a[32];
+  __shared__ float4 s_b[32];
+  __shared__ float4 s_c[32];
+  __shared__ int s_id[32];
+  (void)n_strips;
+  blend_bwd_strip<LISTS>(p, blockIdx.x, s_a, s_b, s_c, s_id);
+}
+
 
 }  // namespace
 
@@ -567,10 +579,11 @@ int launch_blend_fwd(const BlendFwdParams& p, cudaStream_t st) {
 int launch_blend_bwd(const BlendBwdParams& p, cudaStream_t st) {
   const int n_tiles = p.grid_x * p.grid_y;
   if (n_tiles <= 0) return 0;
+  const int n_strips = n_tiles * kStrips;
   if (p.strip_ids)
-    blend_bwd_kernel<true><<<n_tiles * kStrips, 32, 0, st>>>(p);
+    blend_bwd_kernel<true><<<n_strips, 32, 0, st>>>(p, n_strips);
   else
-    blend_bwd_kernel<false><<<n_tiles * kStrips, 32, 0, st>>>(p);
+    blend_bwd_kernel<false><<<n_strips, 32, 0, st>>>(p, n_strips);
   return (int)cudaGetLastError();
 }
 

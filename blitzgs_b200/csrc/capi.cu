@@ -560,8 +560,8 @@ int blitz_adam_update(float* param, const float* param_grad, float* exp_avg, flo
 }
 
 int blitz_adam_update_rows(float* param, const float* grad_rows, float* exp_avg, float* exp_avg_sq,
-                           const int64_t* rows, int64_t n_rows, float lr, float b1, float b2, float eps, int64_t N,
-                           int64_t M, void* stream) {
+                           const int64_t* rows, int64_t n_rows, float grad_scale, float lr, float b1, float b2,
+                           float eps, int64_t N, int64_t M, void* stream) {
   if (N < 0 || M <= 0 || n_rows < 0) return fail(BLITZ_EINVAL, "blitz_adam_update_rows: bad sizes");
   if (n_rows == 0) return 0;
   if (!param || !grad_rows || !exp_avg || !exp_avg_sq || !rows)
@@ -573,6 +573,7 @@ int blitz_adam_update_rows(float* param, const float* grad_rows, float* exp_avg,
   a.exp_avg_sq = exp_avg_sq;
   a.rows = rows;
   a.n_rows = n_rows;
+  a.grad_scale = grad_scale;
   a.lr = lr;
   a.b1 = b1;
   a.b2 = b2;

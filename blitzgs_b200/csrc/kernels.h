@@ -259,6 +259,7 @@ struct AdamParams {
   int64_t n_rows;
   float lr, b1, b2, eps;
   int64_t N, M;
+  float grad_scale;  // rows form: the gradient is multiplied by this first (1 = as given)
 };
 int launch_adam(const AdamParams& p, cudaStream_t st);
 

@@ -735,9 +735,10 @@ def adam_update(param, grad, exp_avg, exp_avg_sq, visible, lr, b1, b2, eps, N, M
     TIMER.end(tok, N=int(N), M=int(M))
 
 
-def adam_update_rows(param, grad_rows, exp_avg, exp_avg_sq, rows, lr, b1, b2, eps, N, M):
+def adam_update_rows(param, grad_rows, exp_avg, exp_avg_sq, rows, lr, b1, b2, eps, N, M, grad_scale=1.0):
     """In-place sparse Adam step of the Gaussians rows (int64 [n], distinct)
-    whose gradients are the rows of grad_rows [n, M] (blitz_adam_update_rows)."""
+    whose gradients are the rows of grad_rows [n, M] (blitz_adam_update_rows),
+    each gradient element first multiplied by grad_scale (float32)."""
     for t in (param, exp_avg, exp_avg_sq):
         if t.dtype != torch.float32 or not t.is_contiguous():
             raise RuntimeError("adam_update_rows needs contiguous float32 tensors")
@@ -746,5 +747,5 @@ def adam_update_rows(param, grad_rows, exp_avg, exp_avg_sq, rows, lr, b1, b2, ep
     n = rows.numel()
     tok = TIMER.begin("adam")
     _lib.call("blitz_adam_update_rows", ptr(param), ptr(grad_rows), ptr(exp_avg), ptr(exp_avg_sq), ptr(rows), n,
-              float(lr), float(b1), float(b2), float(eps), int(N), int(M), _lib.stream_ptr())
+              float(grad_scale), float(lr), float(b1), float(b2), float(eps), int(N), int(M), _lib.stream_ptr())
     TIMER.end(tok, N=int(N), M=int(M), n_rows=n)

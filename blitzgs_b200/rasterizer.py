@@ -264,7 +264,14 @@ class SparseGaussianAdam(torch.optim.Adam):
         super().__init__(params=params, lr=lr, eps=eps)
 
     @torch.no_grad()
-    def step(self, visibility=None, N=None):
+    def step(self, visibility=None, N=None, bsz=None):
+        """``bsz``: divide the gradients by the batch size inside the update
+        (the trainer's ``param.grad /= bsz``, train_internal.py:504-515,
+        fused; the same float32 result) instead of beforehand."""
+        scale = None
+        if bsz is not None:
+            import numpy as np
+            scale = float(np.float32(1.0) / np.float32(bsz))  # PyTorch divides by a host scalar this way
         for group in self.param_groups:
             lr = group["lr"]
             eps = group["eps"]
@@ -288,8 +295,10 @@ class SparseGaussianAdam(torch.optim.Adam):
                 g = g.coalesce()
                 rows = g.indices()[0]
                 ops.adam_update_rows(param, g.values().reshape(rows.numel(), M), exp_avg, exp_avg_sq, rows,
-                                     float(lr_t), 0.9, 0.999, eps, n, M)
+                                     float(lr_t), 0.9, 0.999, eps, n, M, grad_scale=1.0 if scale is None else scale)
             else:
+                if scale is not None:
+                    g = g * scale
                 _C.adamUpdate(param, g, exp_avg, exp_avg_sq, visibility, float(lr_t), 0.9, 0.999, eps, n, M)
 
 

@@ -441,10 +441,14 @@ int blitz_adam_update(float* param, const float* param_grad, float* exp_avg, flo
  * reference always passes a dense gradient): grad_rows [n_rows, M] holds the
  * gradient of Gaussian rows[j] (int64, distinct) in row j -- the sparse
  * gradient of the fused step -- so nothing is read or written for the others.
+ * grad_scale multiplies each gradient element first: the trainer's
+ * `param.grad /= bsz` (train_internal.py:504-515) fused into the step, bit
+ * for bit when grad_scale is the float32 reciprocal of bsz (how PyTorch
+ * divides a float tensor by a host scalar); 1 leaves the gradient as given.
  */
 int blitz_adam_update_rows(float* param, const float* grad_rows, float* exp_avg, float* exp_avg_sq,
-                           const int64_t* rows, int64_t n_rows, float lr, float b1, float b2, float eps, int64_t N,
-                           int64_t M, void* stream);
+                           const int64_t* rows, int64_t n_rows, float grad_scale, float lr, float b1, float b2,
+                           float eps, int64_t N, int64_t M, void* stream);
 
 /*
  * Send-buffer packing of one camera's exchange records (no reference

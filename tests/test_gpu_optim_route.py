@@ -115,3 +115,66 @@ def test_sparse_gaussian_adam_sparse_and_dense_gradients_agree(cuda_device):
         assert torch.equal(a, b)
     changed = (results[0][0] != model[0].detach().cpu()).any(dim=1)
     assert changed.any() and not changed.all()
+
+
+@pytest.mark.parametrize("bsz", [3, 4, 7])
+def test_adam_rows_fuse_the_batch_gradient_scaling(golden, cuda_device, bsz):
+    """The trainer's `param.grad /= bsz` before the step (train_internal.py:
+    504-515), fused into the rows update, gives the same bits as dividing
+    with PyTorch first."""
+    _, adam, _ = golden
+    for param, grads, vis in adam:
+        N, M = param.shape
+        rows = torch.nonzero(vis).flatten().to(cuda_device)
+        outs = []
+        for fused in (False, True):
+            p = param.clone().to(cuda_device)
+            m = torch.zeros_like(p)
+            v = torch.zeros_like(p)
+            for t, gr in enumerate(grads, start=1):
+                g = gr.to(cuda_device)
+                if not fused:
+                    g /= bsz
+                scale = float(np.float32(1.0) / np.float32(bsz)) if fused else 1.0
+                ops.adam_update_rows(p, g[rows].contiguous(), m, v, rows, G.lr_at(t), 0.9, 0.999, G.EPS, N, M,
+                                     grad_scale=scale)
+            outs.append((p.cpu(), m.cpu(), v.cpu()))
+        for a, b in zip(*outs):
+            assert torch.equal(a.view(torch.int32), b.view(torch.int32))
+
+
+def test_densification_stats_from_the_fused_step_match_reference(cuda_device):
+    """view_loss(densify=...) accumulates max_radii2D, the viewspace gradient
+    norm and the count of the visible Gaussians (train_internal.py:340-371,
+    gaussian_model.py:792-794) from its render-backward record; compared with
+    the same updates applied to the reference's own radii and means2D
+    gradient of config 1 (golden_tiny.npz)."""
+    from blitzgs_b200 import densify as DZ
+    from tests.conftest import golden_path
+    gp = golden_path("golden_tiny.npz")
+    g = np.load(gp)
+    if "g_means2D" not in g:
+        pytest.skip("golden_tiny.npz predates the full gradient rows")
+    sc = S.tiny()
+    cam = sc.cameras[0].to(cuda_device)
+    gt = S.target_image(0, cam.image_height, cam.image_width).to(cuda_device)
+    model = [t.to(cuda_device).requires_grad_(True) for t in scene_params(sc)]
+    rs = S.raster_settings(cam, device=cuda_device)
+    stats = DZ.DensificationStats(sc.P, cuda_device)
+    for sparse in (False, True):  # two steps: the statistics accumulate
+        for p in model:
+            p.grad = None
+        loss, *_ = ST.view_loss(model, rs, gt, scale_reg_weight=0.0, sparse_grad=sparse, densify=stats)
+        loss.backward()
+    torch.cuda.synchronize()
+    radii = torch.from_numpy(g["radii"])
+    vis = radii > 0
+    gm = torch.from_numpy(g["g_means2D"]).reshape(-1, 2)
+    mr, acc, den = torch.zeros(sc.P), torch.zeros(sc.P, 1), torch.zeros(sc.P, 1)
+    for _ in range(2):
+        O.densification_stats(mr, acc, den, radii, gm)
+    assert torch.equal(stats.max_radii2D.cpu(), mr)
+    assert torch.equal(stats.denom.cpu(), den)
+    assert not stats.xyz_gradient_accum.cpu()[~vis].any()
+    from tests.helpers import normwise_rel
+    assert normwise_rel(stats.xyz_gradient_accum.cpu(), acc) <= 1e-4
