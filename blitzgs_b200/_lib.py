@@ -18,7 +18,14 @@ SIGNATURES = {
     "blitz_last_error": (ctypes.c_char_p, []),
     "blitz_preprocess_forward": (_i32, [
         _i64, _i32, _i32, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _f32, _vp, _vp, _vp, _f32, _f32,
-        _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+        _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "blitz_rasterize_count": (_i32, [_i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "blitz_rasterize_bin": (_i32, [_i64, _i64, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp,
+                                   _vp]),
+    "blitz_rasterize_blend": (_i32, [_i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                     _vp]),
+    "blitz_rasterize_depth": (_i32, [_i64, _i32, _i32] + [_vp] * 18),
+    "blitz_mark_visible": (_i32, [_i64, _vp, _vp, _vp, _vp, _vp]),
     "blitz_preprocess_backward": (_i32, [
         _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _f32, _vp, _vp, _vp, _f32, _f32,
         _i32, _i32, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i32, _vp]),

@@ -7,8 +7,12 @@ from blitzgs_b200.rasterizer import (  # noqa: F401
     GaussianRasterizationSettings,
     GaussianRasterizer,
     _PreprocessGaussians,
+    _RasterizeGaussians,
     _RenderGaussians,
     SparseGaussianAdam,
     preprocess_gaussians,
+    rasterize_gaussians,
+    rasterize_gaussians_depth,
+    rasterize_gaussians_simp,
     render_gaussians,
 )

@@ -114,19 +114,6 @@ __device__ __forceinline__ float4 alpha_box(float2 xy, float4 co) {
   return make_float4(xy.x - hx, xy.x + hx, xy.y - hy, xy.y + hy);
 }
 
-// power = -0.5 (c00 dx^2 + c11 dy^2) - c01 dx dy, rounded as the reference
-// kernel rounds it: nvcc fuses the first product of each sum into an FMA when
-// every product has one use,
-//   sum = fma(c00 dx, dx, (c11 dy) dy),  power = fma(-0.5, sum, -(c01 dx) dy).
-// Spelled out so that the rounding cannot change with the code around it (a
-// product shared between two uses would be fused the other way round).  The
-// forward and the backward both call this, so their skip decisions agree bit
-// for bit.
-__device__ __forceinline__ float pair_power(float4 co, float2 d) {
-  const float sum = __fmaf_rn(__fmul_rn(co.x, d.x), d.x, __fmul_rn(__fmul_rn(co.z, d.y), d.y));
-  return __fmaf_rn(-0.5f, sum, -__fmul_rn(__fmul_rn(co.y, d.x), d.y));
-}
-
 // Does the box miss the pixel centres [x0, x1] x [y0, y1]?
 __device__ __forceinline__ bool box_misses(float4 b, float x0, float x1, float y0, float y1) {
   return b.y < x0 || b.x > x1 || b.w < y0 || b.z > y1;
@@ -148,6 +135,7 @@ __device__ __forceinline__ int block_sum_int(int v, int* s_red) {
   return t;  // valid in thread 0
 }
 
+template <bool STATS>
 __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
   const int tile = blockIdx.x;
   const int tx = tile % p.grid_x, ty = tile / p.grid_x;
@@ -166,7 +154,7 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
       p.final_T[pix] = 1.f;
       p.n_contrib[pix] = 0u;
     }
-    if (threadIdx.x == 0) {
+    if (threadIdx.x == 0 && p.n_render) {
       p.n_render[tile] = 0;
       p.n_consider[tile] = 0;
       p.n_contrib_tile[tile] = 0;
@@ -186,6 +174,8 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
   __shared__ int s_obs[kWarps][32];
   __shared__ int s_act[kWarps][32];  // did any pixel of the strip take this Gaussian?
   __shared__ int s_red[32];
+  __shared__ float s_w[STATS ? kWarps : 1][32];  // STATS: blend weights and counts per batch entry
+  __shared__ int s_n[STATS ? kWarps : 1][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float2 so = strip_origin(tx, ty, warp);
 
@@ -206,6 +196,8 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
   float T = 1.0f;
   uint32_t last_contributor = 0, n2l = 0;
   float C0 = 0.f, C1 = 0.f, C2 = 0.f;
+  float w_max = 0.f;  // STATS: largest blending weight so far and its Gaussian
+  int id_max = -1;
 
   // software pipeline: list ids two batches ahead, Gaussian data one batch ahead
   int id_n = 0, id_nn = 0;
@@ -243,6 +235,10 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
                                     p.rgb[3 * (int64_t)id + 2], 0.f);
       s_obs[warp][slot] = 0;
       s_act[warp][slot] = 0;
+      if (STATS) {
+        s_w[warp][slot] = 0.f;
+        s_n[warp][slot] = 0;
+      }
     }
     __syncwarp();
     const int kept = __popc(km);
@@ -267,12 +263,31 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
       C0 += cth.x * alpha * T;
       C1 += cth.y * alpha * T;
       C2 += cth.z * alpha * T;
-      if (T > 0.5) atomicAdd(&s_obs[warp][j], 1);
+      if (STATS) {
+        const float w = alpha * T;
+        if (w_max < w) {
+          w_max = w;
+          id_max = s_id[warp][j];
+        }
+        if (p.accum_w) {
+          atomicAdd(&s_w[warp][j], w);
+          atomicAdd(&s_n[warp][j], 1);
+        }
+      } else if (T > 0.5) {
+        atomicAdd(&s_obs[warp][j], 1);
+      }
       T = test_T;
       last_contributor = (uint32_t)__float_as_int(gb.w);
     }
     __syncwarp();
-    if (lane < kept && s_obs[warp][lane] > 0) atomicAdd(&p.out_observe[s_id[warp][lane]], s_obs[warp][lane]);
+    if (STATS) {
+      if (p.accum_w && lane < kept && s_n[warp][lane] > 0) {
+        atomicAdd(&p.accum_w[s_id[warp][lane]], s_w[warp][lane]);
+        atomicAdd(&p.accum_n[s_id[warp][lane]], s_n[warp][lane]);
+      }
+    } else if (lane < kept && s_obs[warp][lane] > 0) {
+      atomicAdd(&p.out_observe[s_id[warp][lane]], s_obs[warp][lane]);
+    }
     if (strip_ids) {
       // append this batch's contributing Gaussians to the strip's list, in order
       const bool a = lane < kept && s_act[warp][lane] != 0;
@@ -294,6 +309,10 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
     p.out_color[pix] = C0 + T * p.bg[0];
     p.out_color[HW + pix] = C1 + T * p.bg[1];
     p.out_color[2 * HW + pix] = C2 + T * p.bg[2];
+  }
+  if (STATS) {
+    if (p.max_count && id_max >= 0) atomicAdd(&p.max_count[id_max], 1.f);
+    if (!p.n_render) return;  // (uniform across the block)
   }
   const int s1 = block_sum_int(inside ? (int)last_contributor : 0, s_red);
   if (threadIdx.x == 0) p.n_consider[tile] = s1;
@@ -572,7 +591,10 @@ __global__ void __launch_bounds__(32, 28) blend_bwd_kernel(BlendBwdParams p, int
 int launch_blend_fwd(const BlendFwdParams& p, cudaStream_t st) {
   const int n_tiles = p.grid_x * p.grid_y;
   if (n_tiles <= 0) return 0;
-  blend_fwd_kernel<<<n_tiles, kTilePix, 0, st>>>(p);
+  if (p.max_count || p.accum_w)
+    blend_fwd_kernel<true><<<n_tiles, kTilePix, 0, st>>>(p);
+  else
+    blend_fwd_kernel<false><<<n_tiles, kTilePix, 0, st>>>(p);
   return (int)cudaGetLastError();
 }
 

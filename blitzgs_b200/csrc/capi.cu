@@ -146,15 +146,18 @@ int blitz_preprocess_forward(int64_t P, int D, int M, const float* means3D, cons
                              const float* campos, float tanfovx, float tanfovy, int image_height,
                              int image_width, int prefiltered, float* means2D, float* depths,
                              int32_t* radii, float* cov3D, float* conic_opacity, float* rgb,
-                             uint8_t* clamped, uint32_t* error_word, void* stream) {
+                             uint8_t* clamped, const uint8_t* culling, float* rects, uint32_t* error_word,
+                             void* stream) {
   if (P < 0 || D < 0 || D > 3 || M < 0 || M > 15 || image_height <= 0 || image_width <= 0)
     return fail(BLITZ_EINVAL, "blitz_preprocess_forward: bad sizes");
   if (P == 0) return 0;
   if (!means3D || !scales || !rotations || !sh_dc || !opacities || !viewmatrix || !projmatrix ||
       !campos || !means2D || !depths || !radii || !conic_opacity || !rgb || (M > 0 && !sh_rest))
     return fail(BLITZ_EINVAL, "blitz_preprocess_forward: null pointer");
-  if (!aligned16(rotations) || !aligned16(conic_opacity) || (reinterpret_cast<uintptr_t>(means2D) & 7u))
-    return fail(BLITZ_EINVAL, "blitz_preprocess_forward: rotations/conic_opacity need 16-byte, means2D 8-byte alignment");
+  if (!aligned16(rotations) || !aligned16(conic_opacity) || (reinterpret_cast<uintptr_t>(means2D) & 7u) ||
+      (reinterpret_cast<uintptr_t>(rects) & 7u))
+    return fail(BLITZ_EINVAL,
+                "blitz_preprocess_forward: rotations/conic_opacity need 16-byte, means2D/rects 8-byte alignment");
   if (prefiltered && !error_word)
     return fail(BLITZ_EINVAL, "blitz_preprocess_forward: prefiltered=1 needs an error word");
   PreprocessParams p = make_pp(P, D, M, means3D, scales, rotations, sh_dc, dc_stride, sh_rest,
@@ -168,6 +171,8 @@ int blitz_preprocess_forward(int64_t P, int D, int M, const float* means3D, cons
   p.out_rgb = rgb;
   p.out_clamped = reinterpret_cast<bool*>(clamped);
   p.out_cov3D = cov3D;
+  p.culling = reinterpret_cast<const bool*>(culling);
+  p.out_rects = rects;
   p.error_flag = error_word;
   return check(launch_preprocess_fwd(p, S(stream)), "blitz_preprocess_forward");
 }
@@ -319,7 +324,8 @@ namespace {
 
 int render_bin_impl(int64_t P, int64_t n_vis, int64_t R, int image_height, int image_width, const float* means2D,
                     const float* depths, const int32_t* radii, const uint8_t* compute_locally, const uint32_t* counts,
-                    void* scratch, size_t scratch_bytes, uint32_t* point_list, uint32_t* ranges, cudaStream_t st) {
+                    void* scratch, size_t scratch_bytes, uint32_t* point_list, uint32_t* ranges, cudaStream_t st,
+                    const float* rects = nullptr, const float* conic_opacity = nullptr) {
   const int gx = (image_width + kTileX - 1) / kTileX, gy = (image_height + kTileY - 1) / kTileY;
   if (R > 0 && scratch_bytes < bin_scratch_bytes(P, n_vis, R, gx * gy))
     return fail(BLITZ_ESCRATCH, "render binning: scratch too small");
@@ -334,6 +340,8 @@ int render_bin_impl(int64_t P, int64_t n_vis, int64_t R, int image_height, int i
   bs.b.radii = radii;
   bs.b.compute_locally = reinterpret_cast<const bool*>(compute_locally);
   bs.b.counts = const_cast<uint32_t*>(counts);
+  bs.b.rects = rects;
+  bs.b.conic_opacity = conic_opacity;
   bs.n_vis = n_vis;
   bs.R = R;
   bs.scratch = scratch;
@@ -931,6 +939,136 @@ int blitz_zero_fill_wait(void* stream) {
 int blitz_fp32_probe(int blocks, int64_t iters, float* sink, void* stream) {
   if (blocks <= 0 || iters <= 0 || !sink) return fail(BLITZ_EINVAL, "blitz_fp32_probe: bad arguments");
   return check(launch_fma_probe(blocks, iters, sink, S(stream)), "blitz_fp32_probe");
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Full (non-distributed) rasterizer: rasterize_gaussians, _simp, _depth and
+// mark_visible.
+
+extern "C" {
+
+int blitz_rasterize_count(int64_t P, int image_height, int image_width, const float* means2D, const int32_t* radii,
+                          const float* rects, const float* conic_opacity, uint32_t* counts, uint64_t* totals,
+                          void* stream) {
+  if (P < 0 || P >= (int64_t)0xffffffff || image_height <= 0 || image_width <= 0)
+    return fail(BLITZ_EINVAL, "blitz_rasterize_count: bad sizes");
+  if (!totals || (P > 0 && (!means2D || !radii || !rects || !conic_opacity || !counts)))
+    return fail(BLITZ_EINVAL, "blitz_rasterize_count: null pointer");
+  if (P > 0 && ((reinterpret_cast<uintptr_t>(means2D) & 7u) || (reinterpret_cast<uintptr_t>(rects) & 7u) ||
+                !aligned16(conic_opacity)))
+    return fail(BLITZ_EINVAL, "blitz_rasterize_count: means2D/rects need 8-byte, conic_opacity 16-byte alignment");
+  BinParams b{};
+  b.P = P;
+  b.W = image_width;
+  b.H = image_height;
+  b.grid_x = (image_width + kTileX - 1) / kTileX;
+  b.grid_y = (image_height + kTileY - 1) / kTileY;
+  b.means2D = means2D;
+  b.radii = radii;
+  b.counts = counts;
+  b.totals = reinterpret_cast<unsigned long long*>(totals);
+  b.rects = rects;
+  b.conic_opacity = conic_opacity;
+  return check(launch_bin_count(b, S(stream)), "blitz_rasterize_count");
+}
+
+int blitz_rasterize_bin(int64_t P, int64_t n_vis, int64_t R, int image_height, int image_width, const float* means2D,
+                        const float* depths, const int32_t* radii, const float* rects, const float* conic_opacity,
+                        const uint32_t* counts, void* scratch, size_t scratch_bytes, uint32_t* point_list,
+                        uint32_t* ranges, void* stream) {
+  if (!render_args_ok(P, n_vis, R, image_height, image_width))
+    return fail(BLITZ_EINVAL, "blitz_rasterize_bin: bad sizes");
+  if (!ranges || (P > 0 && (!means2D || !depths || !radii || !rects || !conic_opacity || !counts)) ||
+      (R > 0 && (!point_list || !scratch)))
+    return fail(BLITZ_EINVAL, "blitz_rasterize_bin: null pointer");
+  if (P > 0 && ((reinterpret_cast<uintptr_t>(means2D) & 7u) || (reinterpret_cast<uintptr_t>(rects) & 7u) ||
+                !aligned16(conic_opacity)))
+    return fail(BLITZ_EINVAL, "blitz_rasterize_bin: means2D/rects need 8-byte, conic_opacity 16-byte alignment");
+  return render_bin_impl(P, n_vis, R, image_height, image_width, means2D, depths, radii, nullptr, counts, scratch,
+                         scratch_bytes, point_list, ranges, S(stream), rects, conic_opacity);
+}
+
+int blitz_rasterize_blend(int64_t P, int image_height, int image_width, const float* means2D,
+                          const float* conic_opacity, const float* rgb, const float* bg, const uint32_t* point_list,
+                          const uint32_t* ranges, float* final_T, uint32_t* n_contrib, float* out_color,
+                          float* max_count, float* accum_w, int32_t* accum_n, void* stream) {
+  if (!render_args_ok(P, 0, 0, image_height, image_width))
+    return fail(BLITZ_EINVAL, "blitz_rasterize_blend: bad sizes");
+  if ((accum_w == nullptr) != (accum_n == nullptr))
+    return fail(BLITZ_EINVAL, "blitz_rasterize_blend: accum_w and accum_n go together");
+  if (!bg || !ranges || !final_T || !n_contrib || !out_color ||
+      (P > 0 && (!means2D || !conic_opacity || !rgb || !point_list)))
+    return fail(BLITZ_EINVAL, "blitz_rasterize_blend: null pointer");
+  BlendFwdParams f{};
+  f.W = image_width;
+  f.H = image_height;
+  f.grid_x = (image_width + kTileX - 1) / kTileX;
+  f.grid_y = (image_height + kTileY - 1) / kTileY;
+  f.P = P;
+  f.ranges = reinterpret_cast<const uint2*>(ranges);
+  f.point_list = point_list;
+  f.means2D = means2D;
+  f.conic_opacity = conic_opacity;
+  f.rgb = rgb;
+  f.bg = bg;
+  f.out_color = out_color;
+  f.final_T = final_T;
+  f.n_contrib = n_contrib;
+  f.max_count = max_count;
+  f.accum_w = accum_w;
+  f.accum_n = accum_n;
+  if (!max_count && !accum_w) {
+    // plain colour forward: the training blend needs its per-tile outputs
+    return fail(BLITZ_EINVAL, "blitz_rasterize_blend: no statistics requested (use blitz_render_blend)");
+  }
+  return check(launch_blend_fwd(f, S(stream)), "blitz_rasterize_blend");
+}
+
+int blitz_rasterize_depth(int64_t P, int image_height, int image_width, const float* means2D,
+                          const float* conic_opacity, const float* rgb, const float* bg, const uint32_t* point_list,
+                          const uint32_t* ranges, const float* means3D, const float* scales, const float* rotations,
+                          const float* projmatrix, const float* campos, float* out_color, float* out_pts,
+                          float* out_depth, float* accum_alpha, int32_t* gidx, float* discriminants, void* stream) {
+  if (!render_args_ok(P, 0, 0, image_height, image_width))
+    return fail(BLITZ_EINVAL, "blitz_rasterize_depth: bad sizes");
+  if (!bg || !ranges || !projmatrix || !campos || !out_color || !out_pts || !out_depth || !accum_alpha || !gidx ||
+      !discriminants || (P > 0 && (!means2D || !conic_opacity || !rgb || !point_list || !means3D || !scales ||
+                                   !rotations)))
+    return fail(BLITZ_EINVAL, "blitz_rasterize_depth: null pointer");
+  DepthParams d{};
+  d.W = image_width;
+  d.H = image_height;
+  d.grid_x = (image_width + kTileX - 1) / kTileX;
+  d.grid_y = (image_height + kTileY - 1) / kTileY;
+  d.ranges = reinterpret_cast<const uint2*>(ranges);
+  d.point_list = point_list;
+  d.means2D = means2D;
+  d.conic_opacity = conic_opacity;
+  d.rgb = rgb;
+  d.bg = bg;
+  d.means3D = means3D;
+  d.scales = scales;
+  d.rotations = rotations;
+  d.projmatrix = projmatrix;
+  d.campos = campos;
+  d.out_color = out_color;
+  d.out_pts = out_pts;
+  d.out_depth = out_depth;
+  d.accum_alpha = accum_alpha;
+  d.gidx = gidx;
+  d.discriminants = discriminants;
+  return check(launch_depth_render(d, S(stream)), "blitz_rasterize_depth");
+}
+
+int blitz_mark_visible(int64_t P, const float* means3D, const float* viewmatrix, const float* projmatrix,
+                       uint8_t* present, void* stream) {
+  (void)projmatrix;  // the frustum test reads only the view depth
+  if (P < 0) return fail(BLITZ_EINVAL, "blitz_mark_visible: bad sizes");
+  if (P > 0 && (!means3D || !viewmatrix || !present)) return fail(BLITZ_EINVAL, "blitz_mark_visible: null pointer");
+  return check(launch_mark_visible(P, means3D, viewmatrix, reinterpret_cast<bool*>(present), S(stream)),
+               "blitz_mark_visible");
 }
 
 }  // extern "C"

@@ -120,6 +120,65 @@ __device__ __forceinline__ int tile_rect_f_count(float2 p, float2 e, int gx, int
   return (x1 - x0) * (y1 - y0);
 }
 
+// power = -0.5 (c00 dx^2 + c11 dy^2) - c01 dx dy, rounded as the reference
+// kernel rounds it: nvcc fuses the first product of each sum into an FMA when
+// every product has one use,
+//   sum = fma(c00 dx, dx, (c11 dy) dy),  power = fma(-0.5, sum, -(c01 dx) dy).
+// Spelled out so that the rounding cannot change with the code around it (a
+// product shared between two uses would be fused the other way round).  The
+// forward and the backward both call this, so their skip decisions agree bit
+// for bit.
+__device__ __forceinline__ float pair_power(float4 co, float2 d) {
+  const float sum = __fmaf_rn(__fmul_rn(co.x, d.x), d.x, __fmul_rn(__fmul_rn(co.z, d.y), d.y));
+  return __fmaf_rn(-0.5f, sum, -__fmul_rn(__fmul_rn(co.y, d.x), d.y));
+}
+
+// The same rectangle as tile bounds [rmin, rmax).
+__device__ __forceinline__ void tile_rect_f(float2 p, float2 e, int gx, int gy, int2& rmin, int2& rmax) {
+  rmin.x = min(gx, max(0, (int)floorf((p.x - e.x) / kTileX)));
+  rmin.y = min(gy, max(0, (int)floorf((p.y - e.y) / kTileY)));
+  rmax.x = min(gx, max(0, (int)ceilf((p.x + e.x) / kTileX)));
+  rmax.y = min(gy, max(0, (int)ceilf((p.y + e.y) / kTileY)));
+}
+
+// Exact tile test of the full rasterizer: does Gaussian (mean m, conic and
+// opacity co) reach alpha >= 1/255 anywhere on tile (tx, ty)?  thr is
+// ln(255 * opacity).  The exponent factor 0.5 d^T conic d is evaluated at
+// one point of the tile's pixel-centre rectangle: the mean itself when it
+// lies inside (factor 0), else the corner on the mean's side moved along the
+// rectangle's edges towards the minimiser of the factor on each edge line,
+// clamped to the edge (the method of rasterizer_impl.cu:52-97; the same
+// float operations in the same order, with the products fused into FMAs the
+// way nvcc fuses that expression, so the emitted tile set is bit-identical).
+__device__ __forceinline__ bool tile_reached(float4 co, float2 m, float thr, int tx, int ty) {
+  constexpr float kSpanX = (float)(kTileX - 1), kSpanY = (float)(kTileY - 1);
+  const float x0 = (float)(tx * kTileX), x1 = (float)((tx + 1) * kTileX - 1);
+  const float y0 = (float)(ty * kTileY), y1 = (float)((ty + 1) * kTileY - 1);
+  const float gap_x = x0 - m.x, gap_y = y0 - m.y;  // > 0: the mean lies before the tile
+  const bool before_x = gap_x > 0.f, before_y = gap_y > 0.f;
+  const bool out_x = before_x || m.x > x1, out_y = before_y || m.y > y1;
+  if (!out_x && !out_y) return 0.f <= thr;
+  const float cx = before_x ? x0 : x1, cy = before_y ? y0 : y1;  // starting corner
+  const float sx = copysignf(kSpanX, gap_x), sy = copysignf(kSpanY, gap_y);  // edge vectors from it
+  const float ex = m.x - cx, ey = m.y - cy;
+  // position along each edge (0..1) of the factor's minimum on that edge line
+  const float rx = __frcp_rn(__fmul_rn(kSpanX * kSpanX, co.x));
+  const float ry = __frcp_rn(__fmul_rn(kSpanY * kSpanY, co.z));
+  const float ux = __saturatef(__fmul_rn(__fmaf_rn(__fmul_rn(sx, co.x), ex, __fmul_rn(__fmul_rn(sx, co.y), ey)), rx));
+  const float uy = __saturatef(__fmul_rn(__fmaf_rn(__fmul_rn(sy, co.y), ex, __fmul_rn(__fmul_rn(sy, co.z), ey)), ry));
+  const float qx = __fmaf_rn(out_y ? ux : 0.f, sx, cx);
+  const float qy = __fmaf_rn(out_x ? uy : 0.f, sy, cy);
+  const float dx = m.x - qx, dy = m.y - qy;
+  const float f = __fmaf_rn(0.5f, __fmaf_rn(__fmul_rn(co.x, dx), dx, __fmul_rn(__fmul_rn(co.z, dy), dy)),
+                            __fmul_rn(__fmul_rn(co.y, dx), dy));
+  return f <= thr;
+}
+
+// ln(255 * opacity) as the full rasterizer's binning computes it.
+__device__ __forceinline__ float tile_reach_threshold(float opacity) {
+  return logf(__fdiv_rn(opacity, 1.0f / 255.0f));
+}
+
 // 3D covariance (upper triangle) from scale and an (unnormalised) quaternion
 // (r, x, y, z): Sigma = (S R)^T (S R).  The reference normalises the
 // quaternion in PyTorch before the kernel, not inside it (forward.cu:136).

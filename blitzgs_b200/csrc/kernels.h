@@ -38,6 +38,11 @@ struct PreprocessParams {
   float* out_rgb;            // [P,3]
   bool* out_clamped;         // [P,3] or null
   float* out_cov3D;          // [P,6] or null
+  // Full-rasterizer extras (both optional): Gaussians with culling[i] set are
+  // skipped (radius 0, zero rows), and out_rects receives the float
+  // half-extents of each Gaussian's screen rectangle (zeros when culled).
+  const bool* culling;       // [P] or null
+  float* out_rects;          // [P,2] or null
   unsigned* error_flag;      // device word, OR-ed with kErr* bits
   // Raw-parameter mode: scales/rotations/opacities hold the model's raw
   // _scaling / _rotation / _opacity; the kernel applies exp, normalize and
@@ -129,6 +134,11 @@ struct BinParams {
   const bool* compute_locally;   // [grid_y*grid_x] or null (= all tiles)
   uint32_t* counts;              // [P] tiles touched under the mask
   unsigned long long* totals;    // device [2]: {instances R, visible Gaussians}
+  // Full rasterizer (rasterize_gaussians): with rects, a Gaussian's tiles are
+  // those of its float half-extent rectangle that pass the exact tile test on
+  // conic_opacity, instead of the square radius rectangle (no mask then).
+  const float* rects;            // [P,2] or null
+  const float* conic_opacity;    // [P,4], with rects
 };
 
 int launch_bin_count(const BinParams& p, cudaStream_t st);
@@ -172,6 +182,15 @@ struct BlendFwdParams {
   int* strip_ids;
   int* strip_pos;
   int* strip_counts;
+  // Full-rasterizer statistics (rasterize_gaussians with flag_max_count, and
+  // rasterize_gaussians_simp), each optional: per pixel, the Gaussian of
+  // largest blending weight alpha*T (the first in list order on ties) gets
+  // +1 in max_count; every (pixel, Gaussian) blend adds alpha*T to
+  // accum_w[id] and 1 to accum_n[id].  With any of them set, n_render /
+  // n_consider / n_contrib_tile / out_observe may be null.
+  float* max_count;  // [P] or null
+  float* accum_w;    // [P] or null
+  int* accum_n;      // [P] or null (with accum_w)
 };
 
 int launch_blend_fwd(const BlendFwdParams& p, cudaStream_t st);
@@ -316,6 +335,36 @@ struct GradPackParams {
   float* send;           // [*,12]
 };
 int launch_grad_records_pack(const GradPackParams& p, int64_t n, cudaStream_t st);
+
+// Full rasterizer, eval outputs (rasterize_gaussians_depth, forward.cu:614-845):
+// the colour blend of the tile lists, plus per pixel the Gaussian of largest
+// blending weight among those whose ray-ellipsoid depth is >= 0, with that
+// depth, the discriminant of the intersection and the 3D point.
+struct DepthParams {
+  int W, H, grid_x, grid_y;
+  const uint2* ranges;
+  const uint32_t* point_list;
+  const float* means2D;        // [P,2]
+  const float* conic_opacity;  // [P,4]
+  const float* rgb;            // [P,3]
+  const float* bg;             // device [3]
+  const float* means3D;        // [P,3]
+  const float* scales;         // [P,3] activated
+  const float* rotations;      // [P,4] (r,x,y,z), as given
+  const float* projmatrix;     // device [16]
+  const float* campos;         // device [3]
+  float* out_color;            // [3,H,W]
+  float* out_pts;              // [3,H,W]
+  float* out_depth;            // [H,W]
+  float* accum_alpha;          // [H,W] final transmittance
+  int* gidx;                   // [H,W]
+  float* discriminants;        // [H,W]
+};
+
+int launch_depth_render(const DepthParams& p, cudaStream_t st);
+
+// Frustum mark of markVisible (rasterizer_impl.cu:100-114): view depth > 0.2.
+int launch_mark_visible(int64_t P, const float* means3D, const float* viewmatrix, bool* present, cudaStream_t st);
 
 int launch_fma_probe(int blocks, int64_t iters, float* sink, cudaStream_t st);
 

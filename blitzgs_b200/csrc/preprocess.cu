@@ -141,7 +141,8 @@ struct PreResult {
   V3 rgb;
   bool clamp3[3];
   float cov3d[6];
-  float smin;  // smallest activated scale (regulariser)
+  float smin;   // smallest activated scale (regulariser)
+  float2 rect;  // half-extents of the screen rectangle (full rasterizer)
 };
 
 // Squared Frobenius norm of the rotation matrix built from q.
@@ -212,6 +213,7 @@ __device__ __forceinline__ void preprocess_one(const PreprocessParams& p, const 
 #pragma unroll
   for (int k = 0; k < 6; ++k) r.cov3d[k] = 0.f;
   r.smin = 0.f;
+  r.rect = make_float2(0.f, 0.f);
 
   do {
     // near-plane test (reference in_frustum, auxiliary.h:156-185)
@@ -264,6 +266,7 @@ __device__ __forceinline__ void preprocess_one(const PreprocessParams& p, const 
     r.radius = (int)ceilf(my_radius);
     r.pimg = pimg;
     r.conic_op = make_float4(conic.x, conic.y, conic.z, opacity);
+    r.rect = make_float2(extent_x, extent_y);
   } while (0);
 }
 
@@ -284,6 +287,7 @@ __device__ __forceinline__ void store_one(const PreprocessParams& p, int64_t i, 
 #pragma unroll
     for (int k = 0; k < 6; ++k) p.out_cov3D[6 * i + k] = r.cov3d[k];
   }
+  if (p.out_rects) reinterpret_cast<float2*>(p.out_rects)[i] = r.rect;
 }
 
 // Rows of a Gaussian rejected in phase A: zeros, like the reference's
@@ -308,6 +312,7 @@ __device__ __forceinline__ void store_culled(const PreprocessParams& p, int64_t 
 #pragma unroll
     for (int k = 0; k < 6; ++k) p.out_cov3D[6 * i + k] = 0.f;
   }
+  if (p.out_rects) reinterpret_cast<float2*>(p.out_rects)[i] = make_float2(0.f, 0.f);
 }
 
 // Per-thread running sums of one block, reduced once at the end of a kernel.
@@ -354,10 +359,12 @@ __device__ __forceinline__ void cull_phase(const PreprocessParams& p, const floa
     const bool in = u * kPreThreads < rem;
     const float m = fmaxf(fabsf(x[u].x), fmaxf(fabsf(x[u].y), fabsf(x[u].z)));
     const float z = Vs[2] * x[u].x + Vs[6] * x[u].y + Vs[10] * x[u].z + Vs[14];
+    // a Gaussian the caller culls is skipped before any test (forward.cu:196-203)
+    const bool culled = in && p.culling && p.culling[base + u * kPreThreads];
     // the exact near test (z <= 0.2 culls) runs in phase B; here only what
     // is behind it by more than the rounding bound is dropped and reported
-    keep[u] = in && z > 0.2f - kAffineErr * fmaf(cb.zw_lin, m, cb.zw_off);
-    if (in && !keep[u] && p.prefiltered) atomicOr(p.error_flag, kErrPrefilteredCulled);
+    keep[u] = in && !culled && z > 0.2f - kAffineErr * fmaf(cb.zw_lin, m, cb.zw_off);
+    if (in && !culled && !keep[u] && p.prefiltered) atomicOr(p.error_flag, kErrPrefilteredCulled);
     if (keep[u]) {
       float m = fmaxf(fabsf(sc[u].x), fmaxf(fabsf(sc[u].y), fabsf(sc[u].z)));
       if (p.raw) m = __expf(fmaxf(sc[u].x, fmaxf(sc[u].y, sc[u].z)));  // exp is increasing: exp(max) = max(exp)

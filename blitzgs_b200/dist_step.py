@@ -112,12 +112,15 @@ class _DistributedBatch(torch.autograd.Function):
             H, W = int(rs.image_height), int(rs.image_width)
             segs = [(s, c) for _, s, c in plan.recv_offsets.get(k, []) if c]
             conic, m2, rgb, depth, radii = ops.exchange_unpack(recv_buf, segs, regs[i])
-            cl = strategies[k].get_compute_locally(device=dev)
+            cl = _band_mask(strategies[k], rank, dev)
             counts_k = torch.empty((max(m2.shape[0], 1),), dtype=torch.int32, device=dev)
             ops.render_count(m2, radii, cl, H, W, counts_k, totals[i])
             staged.append((k, segs, conic, m2, rgb, depth, radii, cl, counts_k))
+        status = ops.queue_scan_status(dev)
         tot_host = totals.cpu().tolist() if nm else []
-        ops.check_scan_status(dev)
+        if not nm:
+            torch.cuda.current_stream(dev).synchronize()
+        ops.check_scan_status(status)
         losses = []
         saved = {}
         for i, (k, segs, conic, m2, rgb, depth, radii, cl, counts_k) in enumerate(staged):
@@ -199,6 +202,20 @@ class _DistributedBatch(torch.autograd.Function):
 
 
 _TABLE = {}
+_MASKS = {}
+
+
+def _band_mask(strategy, rank, dev):
+    """The rank's compute_locally tile mask of a camera (rows of its band),
+    cached per (device, band): bands repeat from step to step."""
+    y0, y1 = strategy.row_range(rank)
+    key = (dev.index, y0, y1, D.CONTEXT.TILE_Y, D.CONTEXT.TILE_X)
+    m = _MASKS.get(key)
+    if m is None:
+        if len(_MASKS) > 4096:
+            _MASKS.clear()
+        m = _MASKS[key] = strategy.get_compute_locally(device=dev)
+    return m
 
 
 def _camera_arrays(rasters):

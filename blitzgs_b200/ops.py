@@ -129,8 +129,11 @@ def sh_layout(shs=None, dc=None, rest=None):
 
 
 def preprocess_forward(means3D, scales, rotations, opacities, sh, raster, *, want_cov3D=False,
-                       want_clamped=False, error_word=None):
-    """EWA preprocess.  ``sh`` is the tuple from :func:`sh_layout`."""
+                       want_clamped=False, error_word=None, culling=None, want_rects=False):
+    """EWA preprocess.  ``sh`` is the tuple from :func:`sh_layout`.
+    ``culling`` (bool [P]) skips the Gaussians it marks; ``want_rects`` also
+    returns the float half-extents [P,2] of each screen rectangle (the full
+    rasterizer's binning input) as an eighth value."""
     _require_cuda(means3D, scales, rotations, opacities)
     means3D, scales, rotations = _f32c(means3D), _f32c(scales), _f32c(rotations)
     opacities = _f32c(opacities)
@@ -144,6 +147,11 @@ def preprocess_forward(means3D, scales, rotations, opacities, sh, raster, *, wan
     rgb = torch.empty((P, 3), dtype=torch.float32, device=dev)
     cov3D = torch.empty((P, 6), dtype=torch.float32, device=dev) if want_cov3D else None
     clamped = torch.empty((P, 3), dtype=torch.bool, device=dev) if want_clamped else None
+    rects = torch.empty((P, 2), dtype=torch.float32, device=dev) if want_rects else None
+    if culling is not None:
+        culling = culling.reshape(-1).to(device=dev, dtype=torch.bool).contiguous()
+        if culling.numel() != P:
+            raise RuntimeError(f"culling must have {P} entries, got {culling.numel()}")
     if P > 0:
         tok = TIMER.begin("preprocess_fwd")
         _lib.call("blitz_preprocess_forward", P, int(raster.sh_degree), M, ptr(means3D), ptr(scales),
@@ -152,8 +160,11 @@ def preprocess_forward(means3D, scales, rotations, opacities, sh, raster, *, wan
                   ptr(_f32c(raster.projmatrix)), ptr(_f32c(raster.campos)), float(raster.tanfovx),
                   float(raster.tanfovy), int(raster.image_height), int(raster.image_width),
                   int(bool(raster.prefiltered)), ptr(means2D), ptr(depths), ptr(radii), ptr(cov3D),
-                  ptr(conic), ptr(rgb), ptr(clamped), ptr(error_word), _lib.stream_ptr())
+                  ptr(conic), ptr(rgb), ptr(clamped), ptr(culling), ptr(rects), ptr(error_word),
+                  _lib.stream_ptr())
         TIMER.end(tok, P=P)
+    if want_rects:
+        return means2D, depths, radii, conic, rgb, cov3D, clamped, rects
     return means2D, depths, radii, conic, rgb, cov3D, clamped
 
 
@@ -278,13 +289,24 @@ class ExchangeOut(ctypes.Structure):
 PACK_SCRATCH = _Scratch(zeroed=True)  # ordered-scan state of the exchange pack; first 4 bytes: status word
 
 
-def check_scan_status(device):
-    """Raise if an ordered scan of the preprocess or the exchange pack on
-    ``device`` gave up waiting (one small readback of their status words)."""
+def queue_scan_status(device):
+    """Queue, on the current stream, copies of the status words of the
+    ordered scans of the preprocess and the exchange pack on ``device`` into
+    pinned host memory; call check_scan_status(handle) after the stream has
+    been synchronised (e.g. by a readback that follows).  No extra sync."""
     bufs = [b for b in (PRE_SCRATCH.peek(device), PACK_SCRATCH.peek(device)) if b is not None]
-    if not bufs:
-        return
-    words = torch.stack([b[:4].view(torch.int32)[0] for b in bufs]).cpu().tolist()
+    host, host_np = _pinned(device, 2, torch.int32, "scan-status")
+    host_np[:] = 0
+    for i, b in enumerate(bufs):
+        host[i:i + 1].copy_(b[:4].view(torch.int32), non_blocking=True)
+    return host_np, bufs
+
+
+def check_scan_status(handle):
+    """Raise if a status word read by queue_scan_status shows that an
+    ordered scan gave up waiting (and clear the words)."""
+    host_np, bufs = handle
+    words = [int(x) for x in host_np[:len(bufs)]]
     if any(words):
         for b in bufs:
             b[:4].zero_()
@@ -565,6 +587,103 @@ def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_local
     state = RenderState(H, W, R, n_vis, point_list, ranges, final_T, n_contrib, n_list, strip_ids, strip_pos,
                         strip_counts)
     return color, n_render, n_consider, n_contrib_tile, out_observe, state
+
+
+def rasterize_forward(means2D, depths, radii, rects, conic_opacity, rgb, bg, H, W, *, max_count=False,
+                      simp=False, strip_lists=True, blend=True):
+    """Binning and blending of the full (non-distributed) rasterizer
+    (_C.rasterize_gaussians / _simp): each Gaussian's float rectangle
+    ``rects`` restricted to the tiles that pass the exact tile test.
+    Returns (color, state, stats) with stats a dict of the requested
+    per-Gaussian statistics: "max_count" float [P] (``max_count`` or
+    ``simp``), "accum_weights" float [P] and "accum_count" int32 [P]
+    (``simp``).  ``blend=False`` stops after the binning (color None; the
+    state holds the lists only)."""
+    _require_cuda(means2D, depths, radii, rects, conic_opacity, rgb, bg)
+    means2D, depths, rects, conic_opacity, rgb, bg = map(_f32c, (means2D, depths, rects, conic_opacity, rgb, bg))
+    radii = radii.contiguous()
+    if radii.dtype != torch.int32:
+        raise RuntimeError("radii must be int32")
+    P = means2D.shape[0]
+    dev = means2D.device
+    gx, gy = grid_dims(H, W)
+    T = gx * gy
+    st = _lib.stream_ptr()
+    counts = torch.empty((max(P, 1),), dtype=torch.int32, device=dev)
+    totals = torch.empty((2,), dtype=torch.int64, device=dev)
+    tok = TIMER.begin("bin_count")
+    _lib.call("blitz_rasterize_count", P, H, W, ptr(means2D), ptr(radii), ptr(rects), ptr(conic_opacity), ptr(counts),
+              ptr(totals), st)
+    TIMER.end(tok, P=P)
+    ranges = torch.empty((T, 2), dtype=torch.int32, device=dev)
+    final_T = torch.empty((H * W,), dtype=torch.float32, device=dev)
+    n_contrib = torch.empty((H * W,), dtype=torch.int32, device=dev)
+    color = torch.empty((3, H, W), dtype=torch.float32, device=dev)
+    stats = {}
+    if max_count or simp:
+        stats["max_count"] = torch.zeros((P,), dtype=torch.float32, device=dev)
+    if simp:
+        stats["accum_weights"] = torch.zeros((P,), dtype=torch.float32, device=dev)
+        stats["accum_count"] = torch.zeros((P,), dtype=torch.int32, device=dev)
+    host, host_np = _pinned(dev, 2, torch.int64)
+    _lib.call("blitz_read_totals", ptr(totals), None, None, host.data_ptr(), None, None, st)
+    R, n_vis = int(host_np[0]), int(host_np[1])
+    point_list = torch.empty((max(R, 1),), dtype=torch.int32, device=dev)
+    scratch = SCRATCH.get(dev, _lib.load().blitz_render_scratch_bytes(P, n_vis, R, H, W))
+    tok = TIMER.begin("binning")
+    _lib.call("blitz_rasterize_bin", P, n_vis, R, H, W, ptr(means2D), ptr(depths), ptr(radii), ptr(rects),
+              ptr(conic_opacity), ptr(counts), ptr(scratch), scratch.numel(), ptr(point_list), ptr(ranges), st)
+    TIMER.end(tok, P=P, R=R, n_vis=n_vis)
+    if not blend:
+        return None, RenderState(H, W, R, n_vis, point_list, ranges, final_T, n_contrib), stats
+    strip = strip_lists and not stats
+    strip_ids = torch.empty((8 * max(R, 1),), dtype=torch.int32, device=dev) if strip else None
+    strip_pos = torch.empty((8 * max(R, 1),), dtype=torch.int32, device=dev) if strip else None
+    strip_counts = torch.empty((T * 8,), dtype=torch.int32, device=dev) if strip else None
+    tok = TIMER.begin("blend_fwd")
+    if stats:
+        _lib.call("blitz_rasterize_blend", P, H, W, ptr(means2D), ptr(conic_opacity), ptr(rgb), ptr(bg),
+                  ptr(point_list), ptr(ranges), ptr(final_T), ptr(n_contrib), ptr(color), ptr(stats.get("max_count")),
+                  ptr(stats.get("accum_weights")), ptr(stats.get("accum_count")), st)
+    else:
+        tile_i = torch.empty((3, T), dtype=torch.int32, device=dev)
+        observe = torch.zeros((max(P, 1),), dtype=torch.int32, device=dev)
+        _lib.call("blitz_render_blend", P, H, W, ptr(means2D), ptr(conic_opacity), ptr(rgb), ptr(bg), None,
+                  ptr(point_list), ptr(ranges), ptr(final_T), ptr(n_contrib), ptr(color), ptr(tile_i[0]),
+                  ptr(tile_i[1]), ptr(tile_i[2]), ptr(observe), ptr(strip_ids), ptr(strip_pos), ptr(strip_counts), st)
+    TIMER.end(tok, P=P, R=R, n_vis=n_vis, H=H, W=W)
+    state = RenderState(H, W, R, n_vis, point_list, ranges, final_T, n_contrib, None, strip_ids, strip_pos,
+                        strip_counts)
+    return color, state, stats
+
+
+def rasterize_depth(means2D, conic_opacity, rgb, bg, state, means3D, scales, rotations, raster):
+    """rasterize_gaussians_depth's blend over the lists of
+    :func:`rasterize_forward`: (color [3,H,W], out_pts [3,H,W], depth
+    [1,H,W], accum_alpha [1,H,W], gidx int32 [1,H,W], discriminants [1,H,W])."""
+    means2D, conic_opacity, rgb, bg, means3D, scales, rotations = map(
+        _f32c, (means2D, conic_opacity, rgb, bg, means3D, scales, rotations))
+    H, W = state.H, state.W
+    dev = means2D.device
+    f = lambda c=1: torch.empty((c, H, W), dtype=torch.float32, device=dev)  # noqa: E731
+    color, pts, depth, alpha, disc = f(3), f(3), f(), f(), f()
+    gidx = torch.empty((1, H, W), dtype=torch.int32, device=dev)
+    _lib.call("blitz_rasterize_depth", means2D.shape[0], H, W, ptr(means2D), ptr(conic_opacity), ptr(rgb), ptr(bg),
+              ptr(state.point_list), ptr(state.ranges), ptr(means3D), ptr(scales), ptr(rotations),
+              ptr(_f32c(raster.projmatrix)), ptr(_f32c(raster.campos)), ptr(color), ptr(pts), ptr(depth), ptr(alpha),
+              ptr(gidx), ptr(disc), _lib.stream_ptr())
+    return color, pts, depth, alpha, gidx, disc
+
+
+def mark_visible(means3D, viewmatrix, projmatrix):
+    """bool [P]: view depth > 0.2 (the frustum test of markVisible)."""
+    _require_cuda(means3D)
+    means3D = _f32c(means3D)
+    P = means3D.shape[0]
+    present = torch.zeros((P,), dtype=torch.bool, device=means3D.device)
+    _lib.call("blitz_mark_visible", P, ptr(means3D), ptr(_f32c(viewmatrix)), ptr(_f32c(projmatrix)), ptr(present),
+              _lib.stream_ptr())
+    return present
 
 
 def render_backward(state, means2D, conic_opacity, rgb, bg, compute_locally, dL_dpix, grad_accum=None,

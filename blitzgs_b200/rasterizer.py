@@ -239,7 +239,92 @@ def _adam_update(param, param_grad, exp_avg, exp_avg_sq, visible, lr, b1, b2, ep
     ops.adam_update(param, param_grad, exp_avg, exp_avg_sq, visible, lr, b1, b2, eps, N, M)
 
 
+def _full_sh(dc, sh, colors_precomp, P, dev):
+    """SH layout of the full rasterizer's inputs: ``dc`` [P,1,3] and ``sh``
+    [P,M,3] (the coefficients beyond DC), or ``sh`` alone holding all of
+    them; with precomputed colours a zero DC stands in (its colour is not
+    used)."""
+    if colors_precomp is not None and colors_precomp.numel():
+        return ops.sh_layout(shs=torch.zeros((P, 1, 3), dtype=torch.float32, device=dev)), 0
+    if dc is None or dc.numel() == 0:
+        return ops.sh_layout(shs=sh), None
+    rest = sh if sh is not None and sh.numel() else torch.zeros((P, 0, 3), dtype=torch.float32, device=dev)
+    return ops.sh_layout(dc=dc, rest=rest), None
+
+
+def _full_forward(background, means3D, colors, opacity, scales, rotations, scale_modifier, cov3D_precomp,
+                  viewmatrix, projmatrix, tan_fovx, tan_fovy, image_height, image_width, dc, sh, degree, campos,
+                  prefiltered, culling, debug, *, max_count=False, simp=False, blend=True):
+    """Preprocess + exact-test binning + blend of the full rasterizer.
+    Returns (color, radii, stats, state, ctx) with ``state`` the render state
+    (tile lists, final T, contributor counts) and ``ctx`` = (settings, SH
+    layout, means2D, conic_opacity, rgb, bg) for a backward or a depth pass."""
+    if means3D.ndimension() != 2 or means3D.size(1) != 3:
+        raise RuntimeError("means3D must have dimensions (num_points, 3)")
+    if cov3D_precomp is not None and cov3D_precomp.numel():
+        raise NotImplementedError("precomputed 3D covariances are not supported (scales and rotations only)")
+    P = means3D.shape[0]
+    dev = means3D.device
+    H, W = int(image_height), int(image_width)
+    layout, deg = _full_sh(dc, sh, colors, P, dev)
+    st = _settings(scale_modifier, viewmatrix, projmatrix, tan_fovx, tan_fovy, H, W,
+                   degree if deg is None else deg, campos, prefiltered)
+    word = torch.zeros(1, dtype=torch.int32, device=dev) if (prefiltered or debug) else None
+    cull = culling if culling is not None and culling.numel() else None
+    m2, depths, radii, conic, rgb, _, _, rects = ops.preprocess_forward(
+        means3D, scales, rotations, opacity.reshape(-1), layout, st, error_word=word, culling=cull, want_rects=True)
+    _check_error_word(word, debug, prefiltered)
+    if colors is not None and colors.numel():
+        rgb = colors.reshape(P, 3).float().contiguous()
+    bg = background.float().contiguous()
+    color, state, stats = ops.rasterize_forward(m2, depths, radii, rects, conic, rgb, bg, H, W, max_count=max_count,
+                                                simp=simp, blend=blend)
+    if debug:
+        torch.cuda.synchronize()
+    return color, radii, stats, state, (st, layout, m2, conic, rgb, bg)
+
+
+def _rasterize_gaussians_simp(background, means3D, colors, opacity, scales, rotations, scale_modifier,
+                              cov3D_precomp, viewmatrix, projmatrix, tan_fovx, tan_fovy, image_height, image_width,
+                              dc, sh, degree, campos, prefiltered, culling, debug):
+    """Reference: RasterizeGaussiansSimpCUDA (f/rasterize_points.cu:479-585).
+    Returns (num_rendered, color, accum_weights_ptr, accum_weights_count,
+    accum_max_count, radii, geomBuffer, binningBuffer, imgBuffer); the three
+    buffers are empty (no backward follows)."""
+    color, radii, stats, state, _ = _full_forward(
+        background, means3D, colors, opacity, scales, rotations, scale_modifier, cov3D_precomp, viewmatrix,
+        projmatrix, tan_fovx, tan_fovy, image_height, image_width, dc, sh, degree, campos, prefiltered, culling,
+        debug, simp=True)
+    e = torch.empty((0,), dtype=torch.uint8, device=means3D.device)
+    return (state.R, color, stats["accum_weights"], stats["accum_count"], stats["max_count"], radii, e, e, e)
+
+
+def _rasterize_gaussians_depth(background, means3D, colors, opacity, scales, rotations, scale_modifier,
+                               cov3D_precomp, viewmatrix, projmatrix, tan_fovx, tan_fovy, image_height, image_width,
+                               dc, sh, degree, campos, prefiltered, culling, debug):
+    """Reference: RasterizeGaussiansDepthCUDA (f/rasterize_points.cu:588-700).
+    Returns (num_rendered, color, out_pts, depth, accum_alpha, gidx,
+    discriminants, radii, geomBuffer, binningBuffer, imgBuffer); the buffers
+    are empty."""
+    _, radii, _, state, (st, _, m2, conic, rgb, bg) = _full_forward(
+        background, means3D, colors, opacity, scales, rotations, scale_modifier, cov3D_precomp, viewmatrix,
+        projmatrix, tan_fovx, tan_fovy, image_height, image_width, dc, sh, degree, campos, prefiltered, culling,
+        debug, blend=False)
+    color, pts, depth, alpha, gidx, disc = ops.rasterize_depth(m2, conic, rgb, bg, state, means3D, scales,
+                                                               rotations, st)
+    e = torch.empty((0,), dtype=torch.uint8, device=means3D.device)
+    return (state.R, color, pts, depth, alpha, gidx, disc, radii, e, e, e)
+
+
+def _mark_visible(means3D, viewmatrix, projmatrix):
+    """Reference: markVisible (f/rasterize_points.cu:785-804)."""
+    return ops.mark_visible(means3D, viewmatrix, projmatrix)
+
+
 _C = SimpleNamespace(
+    rasterize_gaussians_simp=_rasterize_gaussians_simp,
+    rasterize_gaussians_depth=_rasterize_gaussians_depth,
+    mark_visible=_mark_visible,
     preprocess_gaussians=_preprocess_gaussians,
     preprocess_gaussians_backward=_preprocess_gaussians_backward,
     render_gaussians=_render_gaussians,
@@ -395,6 +480,104 @@ class _RenderGaussians(torch.autograd.Function):
         return g_means2D, g_abs, g_conic, g_rgb, None, None, None, None, None, None, None
 
 
+def _empty(t):
+    return torch.Tensor([]) if t is None else t
+
+
+def rasterize_gaussians(means3D, means2D, dc, sh, colors_precomp, opacities, scales, rotations, cov3Ds_precomp,
+                        flag_max_count, culling, raster_settings):
+    return _RasterizeGaussians.apply(means3D, means2D, _empty(dc), _empty(sh), _empty(colors_precomp), opacities,
+                                     _empty(scales), _empty(rotations), _empty(cov3Ds_precomp), flag_max_count,
+                                     culling, raster_settings)
+
+
+def _simp_or_depth_args(means3D, dc, sh, colors_precomp, opacities, scales, rotations, cov3Ds_precomp, culling,
+                        rs):
+    return (rs.bg, means3D, _empty(colors_precomp), opacities, _empty(scales), _empty(rotations), rs.scale_modifier,
+            _empty(cov3Ds_precomp), rs.viewmatrix, rs.projmatrix, rs.tanfovx, rs.tanfovy, rs.image_height,
+            rs.image_width, _empty(dc), _empty(sh), rs.sh_degree, rs.campos, rs.prefiltered, culling, rs.debug)
+
+
+@torch.no_grad()
+def rasterize_gaussians_simp(means3D, means2D, dc, sh, colors_precomp, opacities, scales, rotations,
+                             cov3Ds_precomp, culling, raster_settings):
+    """Reference: _RasterizeGaussians.render_simp (f/__init__.py:477-521)."""
+    out = _C.rasterize_gaussians_simp(*_simp_or_depth_args(means3D, dc, sh, colors_precomp, opacities, scales,
+                                                           rotations, cov3Ds_precomp, culling, raster_settings))
+    _, color, accum_w, accum_n, accum_max, radii = out[:6]
+    return color, radii, accum_w, accum_n, accum_max
+
+
+@torch.no_grad()
+def rasterize_gaussians_depth(means3D, means2D, dc, sh, colors_precomp, opacities, scales, rotations,
+                              cov3Ds_precomp, culling, raster_settings):
+    """Reference: _RasterizeGaussians.render_depth (f/__init__.py:525-579)."""
+    out = _C.rasterize_gaussians_depth(*_simp_or_depth_args(means3D, dc, sh, colors_precomp, opacities, scales,
+                                                            rotations, cov3Ds_precomp, culling, raster_settings))
+    _, color, pts, depth, alpha, gidx, disc = out[:7]
+    return {"render": color, "out_pts": pts, "rendered_depth": depth, "discriminants": disc, "gidx": gidx,
+            "accum_alpha": alpha}
+
+
+class _RasterizeGaussians(torch.autograd.Function):
+    """Reference: _RasterizeGaussians (f/diff_gaussian_rasterization_f/
+    __init__.py:412-644).  The backward replays the blend over the same tile
+    lists (csrc/blend.cu) and runs the preprocess backward; the means2D
+    gradient keeps the reference's NDC scaling."""
+
+    @staticmethod
+    def forward(ctx, means3D, means2D, dc, sh, colors_precomp, opacities, scales, rotations, cov3Ds_precomp,
+                flag_max_count, culling, raster_settings):
+        rs = raster_settings
+        color, radii, stats, state, (st, layout, m2, conic, rgb, bg) = _full_forward(
+            rs.bg, means3D, colors_precomp, opacities, scales, rotations, rs.scale_modifier, cov3Ds_precomp,
+            rs.viewmatrix, rs.projmatrix, rs.tanfovx, rs.tanfovy, rs.image_height, rs.image_width, dc, sh,
+            rs.sh_degree, rs.campos, rs.prefiltered, culling, rs.debug, max_count=bool(flag_max_count))
+        accum_max_count = stats.get("max_count")
+        if accum_max_count is None:
+            accum_max_count = torch.zeros((means3D.shape[0],), dtype=torch.float32, device=means3D.device)
+        ctx.st, ctx.layout, ctx.state = st, layout, state
+        ctx.precomp = colors_precomp.numel() > 0
+        ctx.shapes = (means2D.shape, dc.shape, sh.shape, opacities.shape)
+        ctx.save_for_backward(means3D, scales, rotations, radii, m2, conic, rgb, bg)
+        ctx.mark_non_differentiable(radii, accum_max_count)
+        return color, radii, accum_max_count
+
+    @staticmethod
+    def backward(ctx, grad_color, *_):
+        means3D, scales, rotations, radii, m2, conic, rgb, bg = ctx.saved_tensors
+        st, layout, state = ctx.st, ctx.layout, ctx.state
+        P = means3D.shape[0]
+        dev = means3D.device
+        m2_shape, dc_shape, sh_shape, op_shape = ctx.shapes
+        rec = ops.render_backward(state, m2, conic, rgb, bg, None, grad_color.contiguous())
+        g_colors = rec[:, 12:15]
+        g_precomp = None
+        if ctx.precomp:
+            g_precomp = g_colors.contiguous()
+            g_colors = torch.zeros((P, 3), dtype=torch.float32, device=dev)
+        dmeans3D = torch.empty((P, 3), dtype=torch.float32, device=dev)
+        dscales = torch.empty((P, 3), dtype=torch.float32, device=dev)
+        drot = torch.empty((P, 4), dtype=torch.float32, device=dev)
+        dop = torch.empty((P, 1), dtype=torch.float32, device=dev)
+        dc_t, _dcs, rest_t, _rs, M, _keep = layout
+        dsh = torch.empty((P, M + 1, 3), dtype=torch.float32, device=dev)
+        ops.preprocess_backward(radii, means3D, scales, rotations, layout, st, rec[:, 0:2], rec[:, 8:12], g_colors,
+                                out=(dmeans3D, dscales, drot, dop, (dsh, (M + 1) * 3),
+                                     (dsh.view(-1)[3:] if M > 0 else dsh, (M + 1) * 3)))
+        g_means2D = torch.zeros(m2_shape, dtype=torch.float32, device=dev)
+        g_means2D[:, :2] = rec[:, 0:2]
+        g_dc = g_sh = None
+        if not ctx.precomp:
+            if len(dc_shape) and dc_shape[0] == P:
+                g_dc = dsh[:, :1].reshape(dc_shape)
+                g_sh = dsh[:, 1:].reshape(sh_shape) if len(sh_shape) and sh_shape[0] == P else None
+            else:
+                g_sh = dsh.reshape(sh_shape)
+        return (dmeans3D, g_means2D, g_dc, g_sh, g_precomp, dop.reshape(op_shape), dscales, drot, None, None, None,
+                None)
+
+
 class GaussianRasterizer(nn.Module):
     def __init__(self, raster_settings):
         super().__init__()
@@ -409,49 +592,52 @@ class GaussianRasterizer(nn.Module):
                                 compute_locally, extended_compute_locally, self.raster_settings, cuda_args)
 
     def markVisible(self, positions):
-        raise NotImplementedError("markVisible belongs to the eval/culling rasterizer (not on the training path)")
+        """bool [P]: Gaussians in front of the camera (view depth > 0.2;
+        f/__init__.py:666-675)."""
+        with torch.no_grad():
+            rs = self.raster_settings
+            return _C.mark_visible(positions, rs.viewmatrix, rs.projmatrix)
 
-    def forward(self, means3D, means2D, opacities, culling=None, dc=None, shs=None, colors_precomp=None,
-                scales=None, rotations=None, cov3D_precomp=None, flag_max_count=False):
-        """The reference's full (non-distributed) rasterizer forward
-        (f/diff_gaussian_rasterization_f/__init__.py:691-729 -> _RasterizeGaussians
-        :412-474): one camera, the whole image.  Composed from the training
-        path's two operators: preprocess (SH colour from ``dc`` and ``shs``,
-        scales and rotations), the radii of the Gaussians ``culling`` marks set
-        to 0 so they are never binned (cuda_rasterizer/forward.cu:191-206),
-        then the render over every tile.  The caller's ``means2D`` (zeros
-        [P, >=2]) receives the screen-space gradient in its first two columns,
-        as in the reference.  Returns (color [3,H,W], radii int32 [P],
-        accum_max_count [P] zeros).
-
-        Not provided: ``colors_precomp``, ``cov3D_precomp`` and
-        ``flag_max_count`` (the per-pixel maximum-weight count of the
-        mini-splatting pruning), which raise NotImplementedError."""
+    def _inputs(self, shs, colors_precomp, scales, rotations, cov3D_precomp):
+        """The reference's argument checks (f/__init__.py:695-720)."""
         if (shs is None and colors_precomp is None) or (shs is not None and colors_precomp is not None):
             raise Exception('Please provide excatly one of either SHs or precomputed colors!')
         if ((scales is None or rotations is None) and cov3D_precomp is None) or \
                 ((scales is not None or rotations is not None) and cov3D_precomp is not None):
             raise Exception('Please provide exactly one of either scale/rotation pair or precomputed 3D covariance!')
-        if colors_precomp is not None:
-            raise NotImplementedError("precomputed colours are not supported (SH colour only)")
-        if cov3D_precomp is not None:
-            raise NotImplementedError("precomputed 3D covariances are not supported (scales and rotations only)")
-        if flag_max_count:
-            raise NotImplementedError("flag_max_count (mini-splatting max-weight counts) is not supported")
-        rs = self.raster_settings
-        sh = shs if dc is None or dc.numel() == 0 else torch.cat((dc, shs), 1)
-        m2, rgb, conic, radii, depths = preprocess_gaussians(means3D, scales, rotations, sh, opacities, rs, None)
-        if culling is not None and culling.numel():
-            radii = radii.masked_fill(culling.reshape(-1).to(torch.bool), 0)
-        m2 = m2 + means2D[:, :2]
-        P = means3D.shape[0]
-        all_map = torch.zeros((P, 5), dtype=torch.float32, device=means3D.device)
-        color, *_ = render_gaussians(m2, None, conic, rgb, all_map, depths, radii, None, None, rs, None)
-        accum_max_count = torch.zeros((P,), dtype=torch.float32, device=means3D.device)
-        return color, radii, accum_max_count
 
-    def render_simp(self, *a, **k):
-        raise NotImplementedError("render_simp (mini-splatting culling) is not on the training path")
+    def forward(self, means3D, means2D, opacities, culling=None, dc=None, shs=None, colors_precomp=None,
+                scales=None, rotations=None, cov3D_precomp=None, flag_max_count=False):
+        """The reference's full (non-distributed) rasterizer
+        (f/diff_gaussian_rasterization_f/__init__.py:691-729 ->
+        _RasterizeGaussians :412-474): one camera, the whole image, each
+        Gaussian binned over its float screen rectangle restricted to the
+        tiles that pass the exact tile test.  Returns (color [3,H,W], radii
+        int32 [P], accum_max_count float [P]); with ``flag_max_count`` every
+        pixel adds 1 to the count of its Gaussian of largest blending weight.
+        Gradients reach means3D, means2D (its first two columns: the
+        NDC-scaled screen gradient), dc, shs or colors_precomp, opacities,
+        scales and rotations.  ``cov3D_precomp`` is not supported."""
+        self._inputs(shs, colors_precomp, scales, rotations, cov3D_precomp)
+        return rasterize_gaussians(means3D, means2D, dc, shs, colors_precomp, opacities, scales, rotations,
+                                   cov3D_precomp, flag_max_count, culling, self.raster_settings)
 
-    def render_depth(self, *a, **k):
-        raise NotImplementedError("render_depth (eval) is not on the training path")
+    def render_simp(self, means3D, means2D, opacities, culling=None, dc=None, shs=None, colors_precomp=None,
+                    scales=None, rotations=None, cov3D_precomp=None):
+        """Mini-splatting statistics pass (f/__init__.py:732-770, forward.cu:
+        466-607): (color, radii, accum_weights_ptr float [P] = sum of alpha*T
+        over the pixels each Gaussian blends into, accum_weights_count int32
+        [P] = their number, accum_max_count float [P]).  No gradients."""
+        self._inputs(shs, colors_precomp, scales, rotations, cov3D_precomp)
+        return rasterize_gaussians_simp(means3D, means2D, dc, shs, colors_precomp, opacities, scales, rotations,
+                                        cov3D_precomp, culling, self.raster_settings)
+
+    def render_depth(self, means3D, means2D, opacities, culling=None, dc=None, shs=None, colors_precomp=None,
+                     scales=None, rotations=None, cov3D_precomp=None):
+        """Depth pass (f/__init__.py:773-810, forward.cu:614-845): a dict with
+        "render" [3,H,W], "out_pts" [3,H,W], "rendered_depth" [1,H,W],
+        "discriminants" [1,H,W], "gidx" int32 [1,H,W], "accum_alpha"
+        [1,H,W].  No gradients."""
+        self._inputs(shs, colors_precomp, scales, rotations, cov3D_precomp)
+        return rasterize_gaussians_depth(means3D, means2D, dc, shs, colors_precomp, opacities, scales, rotations,
+                                         cov3D_precomp, culling, self.raster_settings)

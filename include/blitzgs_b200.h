@@ -54,7 +54,11 @@ const char* blitz_last_error(void);
  * cuda_rasterizer/rasterizer_impl.cu:982-1067).
  * Outputs (all written, zeros for culled Gaussians): means2D [P,2] (pixels),
  * depths [P] (view z), radii int32 [P], conic_opacity [P,4], rgb [P,3];
- * optional (may be NULL): cov3D [P,6], clamped uint8 [P,3].
+ * optional (may be NULL): cov3D [P,6], clamped uint8 [P,3], rects [P,2] (the
+ * float half-extents of each Gaussian's screen rectangle, which the full
+ * rasterizer bins over: forward.cu:253-262).
+ * culling (uint8 [P], may be NULL): Gaussians with a non-zero entry are
+ * skipped, as _C.rasterize_gaussians skips them (forward.cu:196-203).
  * error_word: device uint32 OR-ed with BLITZ_ERRBIT_* (may be NULL).
  * M = SH coefficients beyond DC per Gaussian (0..15), D = active degree (0..3).
  */
@@ -65,7 +69,8 @@ int blitz_preprocess_forward(int64_t P, int D, int M, const float* means3D, cons
                              const float* campos, float tanfovx, float tanfovy, int image_height,
                              int image_width, int prefiltered, float* means2D, float* depths,
                              int32_t* radii, float* cov3D, float* conic_opacity, float* rgb,
-                             uint8_t* clamped, uint32_t* error_word, void* stream);
+                             uint8_t* clamped, const uint8_t* culling, float* rects, uint32_t* error_word,
+                             void* stream);
 
 /*
  * Backward of blitz_preprocess_forward.
@@ -310,6 +315,59 @@ int blitz_render_backward(int64_t P, int image_height, int image_width, const ui
                           const float* bg, const uint8_t* compute_locally, const float* dL_dpix,
                           const uint32_t* record_rows, const int32_t* strip_ids, const int32_t* strip_pos,
                           const int32_t* strip_counts, float* grad_accum, void* stream);
+
+/*
+ * Full (non-distributed) rasterizer.  Replaces _C.rasterize_gaussians,
+ * _C.rasterize_gaussians_simp, _C.rasterize_gaussians_depth and
+ * _C.mark_visible (submodule/diff-gaussian-rasterization_f/rasterize_points.cu:
+ * 372-784, cuda_rasterizer/rasterizer_impl.cu:100-114, 119-191, 336-853,
+ * forward.cu:292-845).  A forward is: blitz_preprocess_forward with culling
+ * and rects -> blitz_rasterize_count -> (read the totals) ->
+ * blitz_rasterize_bin -> blitz_render_blend (colour, no mask) or
+ * blitz_rasterize_blend (with flag_max_count / simp statistics) or
+ * blitz_rasterize_depth; its backward is blitz_render_backward over the same
+ * lists, then blitz_preprocess_backward.
+ *
+ * blitz_rasterize_count: per-Gaussian tile counts over each Gaussian's float
+ * half-extent rectangle (rects [P,2]) keeping only the tiles that pass the
+ * exact tile test on conic_opacity (the Gaussian reaches alpha >= 1/255 at
+ * the point of the tile's pixel-centre rectangle the test picks), and the
+ * device totals {R, n_vis} (uint64 [2]).
+ * blitz_rasterize_bin: the per-tile lists of those instances in (depth,
+ * index) order -- point_list uint32 [R], ranges uint32 [n_tiles,2]; scratch
+ * of blitz_render_scratch_bytes bytes.
+ * blitz_rasterize_blend: the colour blend (as blitz_render_blend without a
+ * tile mask) plus, each optional: max_count float [P] += 1 for the Gaussian
+ * of largest weight alpha*T of every pixel (flag_max_count, and simp);
+ * accum_w float [P] += alpha*T and accum_n int32 [P] += 1 over every
+ * (pixel, Gaussian) blend (simp; together).  At least one must be given;
+ * the arrays accumulate (zero them first).
+ * blitz_rasterize_depth: the colour blend of rasterize_gaussians_depth with,
+ * per pixel, the Gaussian of largest weight among those whose ray-ellipsoid
+ * depth (3-sigma ellipsoid, rotations and scales as given) is >= 0: out_pts
+ * [3,H,W] its closest ray point, out_depth [H,W], discriminants [H,W], gidx
+ * int32 [H,W] (0 where none), accum_alpha [H,W] the final transmittance.
+ * blitz_mark_visible: present uint8 [P] = view depth > 0.2 (projmatrix is
+ * accepted for the reference's signature and not read).
+ */
+int blitz_rasterize_count(int64_t P, int image_height, int image_width, const float* means2D, const int32_t* radii,
+                          const float* rects, const float* conic_opacity, uint32_t* counts, uint64_t* totals,
+                          void* stream);
+int blitz_rasterize_bin(int64_t P, int64_t n_vis, int64_t R, int image_height, int image_width, const float* means2D,
+                        const float* depths, const int32_t* radii, const float* rects, const float* conic_opacity,
+                        const uint32_t* counts, void* scratch, size_t scratch_bytes, uint32_t* point_list,
+                        uint32_t* ranges, void* stream);
+int blitz_rasterize_blend(int64_t P, int image_height, int image_width, const float* means2D,
+                          const float* conic_opacity, const float* rgb, const float* bg, const uint32_t* point_list,
+                          const uint32_t* ranges, float* final_T, uint32_t* n_contrib, float* out_color,
+                          float* max_count, float* accum_w, int32_t* accum_n, void* stream);
+int blitz_rasterize_depth(int64_t P, int image_height, int image_width, const float* means2D,
+                          const float* conic_opacity, const float* rgb, const float* bg, const uint32_t* point_list,
+                          const uint32_t* ranges, const float* means3D, const float* scales, const float* rotations,
+                          const float* projmatrix, const float* campos, float* out_color, float* out_pts,
+                          float* out_depth, float* accum_alpha, int32_t* gidx, float* discriminants, void* stream);
+int blitz_mark_visible(int64_t P, const float* means3D, const float* viewmatrix, const float* projmatrix,
+                       uint8_t* present, void* stream);
 
 /*
  * Fused L1 + SSIM over a band [C,Hb,W] (forward).

@@ -17,6 +17,11 @@ stage, each function citing the reference lines it follows:
                        rasterizer_impl.cu:213-256, 696-717)
   render_backward      r/cuda_rasterizer/backward.cu:324-530, written out in
                        closed form per tile
+  full_binning         the full rasterizer's binning with the exact tile test,
+                       f/cuda_rasterizer/rasterizer_impl.cu:52-97, 119-191
+  render_stats         flag_max_count / render_simp statistics,
+                       f/cuda_rasterizer/forward.cu:402-440, 566-590
+  mark_visible         f/cuda_rasterizer/rasterizer_impl.cu:100-114
   loss                 utils/loss_utils.py:31-37, 83-124 and
                        gaussian_renderer/loss_distribution.py:220-263, 307-309
 
@@ -564,6 +569,133 @@ def route_rect_bool(means2D, radii, H, W, rectangles, avoid_pixel_all2all=False)
             yr, xr = yr + 1, xr + 1
         out[:, rk] = ~((y1 <= yl) | (yr <= y0) | (x1 <= xl) | (xr <= x0))
     return out
+
+
+# ---------------------------------------------------------------------------
+# Full (non-distributed) rasterizer: rasterize_gaussians / _simp / mark_visible
+# ---------------------------------------------------------------------------
+
+def tile_rect_float(means2D, rects, gx, gy):
+    """Reference getRect with float half-extents (f/cuda_rasterizer/
+    auxiliary.h:63-73): floor / ceil of (mean -+ extent) / 16, clamped."""
+    m = torch.as_tensor(np.asarray(means2D, np.float32))
+    e = torch.as_tensor(np.asarray(rects, np.float32))
+    T = torch.tensor(float(TILE), dtype=f32)
+    clip = lambda v, g: v.to(torch.int64).clamp(0, g).numpy()  # noqa: E731
+    return (clip(torch.floor((m[:, 0] - e[:, 0]) / T), gx), clip(torch.floor((m[:, 1] - e[:, 1]) / T), gy),
+            clip(torch.ceil((m[:, 0] + e[:, 0]) / T), gx), clip(torch.ceil((m[:, 1] + e[:, 1]) / T), gy))
+
+
+def tile_reached(conic_opacity, means2D, tx, ty):
+    """Reference exact tile test (f/cuda_rasterizer/rasterizer_impl.cu:52-97,
+    153-170), float32, vectorised over (Gaussian, tile) pairs: the exponent
+    factor 0.5 d^T conic d at the point of the tile's pixel-centre rectangle
+    the test picks, compared with ln(opacity * 255).  The FMAs are the ones
+    nvcc forms from the reference expressions (first product of each sum
+    fused), evaluated with fma32."""
+    co = torch.as_tensor(conic_opacity, dtype=f32)
+    m = torch.as_tensor(means2D, dtype=f32)
+    tx = torch.as_tensor(tx, dtype=torch.int64)
+    ty = torch.as_tensor(ty, dtype=torch.int64)
+    span = torch.tensor(float(TILE - 1), dtype=f32)
+    x0, x1 = (tx * TILE).to(f32), ((tx + 1) * TILE - 1).to(f32)
+    y0, y1 = (ty * TILE).to(f32), ((ty + 1) * TILE - 1).to(f32)
+    mx, my = m[:, 0], m[:, 1]
+    gap_x, gap_y = x0 - mx, y0 - my
+    before_x, before_y = gap_x > 0, gap_y > 0
+    out_x, out_y = before_x | (mx > x1), before_y | (my > y1)
+    cx, cy = torch.where(before_x, x0, x1), torch.where(before_y, y0, y1)
+    sx, sy = torch.copysign(span.expand_as(gap_x), gap_x), torch.copysign(span.expand_as(gap_y), gap_y)
+    ex, ey = mx - cx, my - cy
+    rx = 1.0 / ((span * span) * co[:, 0])
+    ry = 1.0 / ((span * span) * co[:, 2])
+    sat = lambda v: torch.where(torch.isnan(v), torch.zeros_like(v), v.clamp(0.0, 1.0))  # noqa: E731
+    ux = sat(fma32(sx * co[:, 0], ex, (sx * co[:, 1]) * ey) * rx)
+    uy = sat(fma32(sy * co[:, 1], ex, (sy * co[:, 2]) * ey) * ry)
+    zero = torch.zeros_like(ux)
+    qx = fma32(torch.where(out_y, ux, zero), sx, cx)
+    qy = fma32(torch.where(out_x, uy, zero), sy, cy)
+    dx, dy = mx - qx, my - qy
+    half = torch.full_like(dx, 0.5)
+    f = fma32(half, fma32(co[:, 0] * dx, dx, (co[:, 2] * dy) * dy), (co[:, 1] * dx) * dy)
+    f = torch.where(out_x | out_y, f, zero)
+    thr = torch.log(co[:, 3] / torch.tensor(1.0 / 255.0, dtype=f32))
+    return (f <= thr).numpy()
+
+
+def full_binning(means2D, depths, radii, rects, conic_opacity, H, W):
+    """Per-tile lists of the full rasterizer (rasterizer_impl.cu:119-191,
+    336-430): each Gaussian with radius > 0 over its float rectangle, only
+    the tiles that pass the exact tile test, in (depth bits, index) order.
+    Returns (point_list int64 [R], ranges int64 [T,2], counts int64 [P])."""
+    m = np.asarray(means2D, np.float32)
+    d = np.asarray(depths, np.float32)
+    r = np.asarray(radii, np.int64)
+    co = np.asarray(conic_opacity, np.float32)
+    gx, gy = (W + TILE - 1) // TILE, (H + TILE - 1) // TILE
+    T = gx * gy
+    x0, y0, x1, y1 = tile_rect_float(m, rects, gx, gy)
+    idx_l, tx_l, ty_l = [], [], []
+    for i in np.nonzero(r > 0)[0]:
+        for ty in range(y0[i], y1[i]):
+            for tx in range(x0[i], x1[i]):
+                idx_l.append(i)
+                tx_l.append(tx)
+                ty_l.append(ty)
+    idx = np.asarray(idx_l, np.int64)
+    if len(idx):
+        keep = tile_reached(co[idx], m[idx], np.asarray(tx_l), np.asarray(ty_l))
+        idx = idx[keep]
+        tile = (np.asarray(ty_l) * gx + np.asarray(tx_l))[keep]
+    counts = np.bincount(idx, minlength=len(r)) if len(idx) else np.zeros(len(r), np.int64)
+    if len(idx) == 0:
+        return idx, np.zeros((T, 2), np.int64), counts
+    order = np.lexsort((idx, d.view(np.uint32)[idx].astype(np.int64), tile))
+    pl, ts = idx[order], tile[order]
+    ranges = np.zeros((T, 2), np.int64)
+    starts = np.searchsorted(ts, np.arange(T), side="left")
+    ends = np.searchsorted(ts, np.arange(T), side="right")
+    ranges[:, 0] = np.where(ends > starts, starts, 0)
+    ranges[:, 1] = np.where(ends > starts, ends, 0)
+    return pl, ranges, counts
+
+
+def render_stats(means2D, conic_opacity, point_list, ranges, H, W, P):
+    """Statistics of rasterize_gaussians (flag_max_count) and
+    rasterize_gaussians_simp (f/cuda_rasterizer/forward.cu:402-440, 566-590):
+    per pixel, +1 for the contributing Gaussian of largest alpha*T (the first
+    in list order on ties); over every (pixel, Gaussian) blend, the sum of
+    alpha*T and the count.  Returns (max_count, accum_w, accum_n), float64 /
+    int64 [P]."""
+    gx, gy = (W + TILE - 1) // TILE, (H + TILE - 1) // TILE
+    mx = torch.zeros(P, dtype=torch.float64)
+    aw = torch.zeros(P, dtype=torch.float64)
+    an = torch.zeros(P, dtype=torch.int64)
+    pl = torch.as_tensor(point_list, dtype=torch.int64)
+    m2 = torch.as_tensor(means2D, dtype=f32)
+    co = torch.as_tensor(conic_opacity, dtype=f32)
+    for t in range(gx * gy):
+        s, e = int(ranges[t][0]), int(ranges[t][1])
+        if e == s:
+            continue
+        xs, ys = _tile_pixels(t, gx, H, W)
+        ids = pl[s:e]
+        _, _, _, _, alpha, ok, _ = _pair_terms(ids, m2, co, xs, ys)
+        contrib, Tb, _, _ = _transmittance(alpha, ok)
+        w = torch.where(contrib, alpha * Tb, torch.zeros_like(alpha))
+        aw.index_add_(0, ids, w.double().sum(0))
+        an.index_add_(0, ids, contrib.sum(0))
+        has = contrib.any(1)
+        best = torch.where(contrib, w, torch.full_like(w, -1.0)).argmax(1)
+        mx.index_add_(0, ids[best[has]], torch.ones(int(has.sum()), dtype=torch.float64))
+    return mx, aw, an
+
+
+def mark_visible(means3D, viewmatrix):
+    """Reference checkFrustum / in_frustum (f/cuda_rasterizer/
+    rasterizer_impl.cu:100-114, auxiliary.h:158-185): view depth > 0.2."""
+    p = torch.as_tensor(means3D, dtype=f32)
+    return (_xform3(p, torch.as_tensor(viewmatrix, dtype=f32).reshape(-1))[:, 2] > 0.2).numpy()
 
 
 def fma32(a, b, c):

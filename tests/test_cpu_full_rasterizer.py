@@ -1,9 +1,8 @@
-"""GaussianRasterizer.forward (the reference's full rasterizer) is composed
-from the two training-path operators; on the CPU the composition is checked
-with stand-ins for those operators (the operators themselves are checked on
-the GPU): argument validation with the reference's messages, SH assembly
-from dc + rest, culled Gaussians dropped through their radii, and the
-screen-space gradient routed to the caller's means2D."""
+"""GaussianRasterizer.forward / render_simp / render_depth / markVisible (the
+reference's full rasterizer, f/__init__.py:666-810) on the CPU: the argument
+checks with the reference's messages, the SH layouts the three entry points
+accept, and the refusal of CPU tensors (the kernels themselves are checked
+against the reference on the GPU in tests/test_gpu_full_rasterizer.py)."""
 import pytest
 import torch
 
@@ -12,71 +11,67 @@ from blitzgs_b200 import rasterizer as RZ
 
 class _Settings:
     image_height, image_width = 8, 8
+    tanfovx = tanfovy = 0.5
+    bg = torch.zeros(3)
+    scale_modifier = 1.0
+    viewmatrix = torch.eye(4)
+    projmatrix = torch.eye(4)
+    sh_degree = 3
+    campos = torch.zeros(3)
+    prefiltered = False
+    debug = False
 
 
-def _fakes(monkeypatch, seen):
-    def pre(means3D, scales, rotations, sh, opacities, rs, cuda_args):
-        seen["sh"] = sh
-        m2 = means3D[:, :2] * 2.0
-        rgb = sh[:, 0, :] * 1.0
-        conic = torch.cat([scales, opacities], 1)
-        radii = torch.full((means3D.shape[0],), 5, dtype=torch.int32)
-        return m2, rgb, conic, radii, means3D[:, 2].detach()
-
-    def render(m2, m2_abs, conic, rgb, all_map, depths, radii, cl, ecl, rs, cuda_args):
-        seen["radii"] = radii.clone()
-        w = (radii > 0).float()[:, None]
-        v = (m2 * w).sum() + 3.0 * (rgb * w).sum()
-        color = v * torch.ones((3, rs.image_height, rs.image_width))
-        return color, None, None, None, None, None, None
-
-    monkeypatch.setattr(RZ, "preprocess_gaussians", pre)
-    monkeypatch.setattr(RZ, "render_gaussians", render)
+def _args(P=3):
+    return torch.zeros(P, 3), torch.zeros(P, 3), torch.ones(P, 1), torch.ones(P, 3), torch.ones(P, 4)
 
 
-def test_forward_composes_preprocess_culling_and_render(monkeypatch):
-    seen = {}
-    _fakes(monkeypatch, seen)
-    P = 6
-    g = torch.Generator().manual_seed(1)
-    means3D = torch.randn(P, 3, generator=g, requires_grad=True)
-    dc = torch.randn(P, 1, 3, generator=g, requires_grad=True)
-    rest = torch.randn(P, 15, 3, generator=g, requires_grad=True)
-    screen = torch.zeros(P, 3, requires_grad=True)
-    culling = torch.tensor([False, True, False, False, True, False])
+@pytest.mark.parametrize("method", ["forward", "render_simp", "render_depth"])
+def test_argument_checks_use_the_reference_messages(method):
     rast = RZ.GaussianRasterizer(_Settings())
-    color, radii, accum = rast(means3D, screen, torch.rand(P, 1, generator=g), culling, dc=dc, shs=rest,
-                               scales=torch.rand(P, 3, generator=g), rotations=torch.randn(P, 4, generator=g))
-    assert seen["sh"].shape == (P, 16, 3) and torch.equal(seen["sh"][:, 0], dc[:, 0]) and torch.equal(seen["sh"][:, 1:], rest)
-    assert torch.equal(radii, torch.tensor([5, 0, 5, 5, 0, 5], dtype=torch.int32))
-    assert torch.equal(seen["radii"], radii)
-    assert accum.shape == (P,) and not accum.any()
-    color.sum().backward()
-    keep = (~culling).float()[:, None]
-    n = color.numel()
-    # d color.sum / d screen[:, :2] = n * w; the third column gets nothing
-    assert torch.equal(screen.grad[:, :2], n * keep.expand(P, 2))
-    assert not screen.grad[:, 2].any()
-    assert torch.equal(dc.grad[:, 0], 3.0 * n * keep.expand(P, 3))
-    assert not rest.grad.any()
-
-
-def test_forward_argument_validation(monkeypatch):
-    _fakes(monkeypatch, {})
-    rast = RZ.GaussianRasterizer(_Settings())
-    P = 3
-    x, s, q, o = torch.zeros(P, 3), torch.ones(P, 3), torch.ones(P, 4), torch.ones(P, 1)
-    sh = torch.zeros(P, 16, 3)
+    fn = getattr(rast, method)
+    x, m2, o, s, q = _args()
+    sh = torch.zeros(3, 15, 3)
     with pytest.raises(Exception, match="excatly one of either SHs or precomputed colors"):
-        rast(x, torch.zeros(P, 3), o, None, scales=s, rotations=q)
+        fn(x, m2, o, None, scales=s, rotations=q)
+    with pytest.raises(Exception, match="excatly one of either SHs or precomputed colors"):
+        fn(x, m2, o, None, shs=sh, colors_precomp=torch.zeros(3, 3), scales=s, rotations=q)
     with pytest.raises(Exception, match="exactly one of either scale/rotation pair"):
-        rast(x, torch.zeros(P, 3), o, None, shs=sh, scales=s)
-    with pytest.raises(NotImplementedError, match="precomputed colours"):
-        rast(x, torch.zeros(P, 3), o, None, colors_precomp=torch.zeros(P, 3), scales=s, rotations=q)
+        fn(x, m2, o, None, shs=sh, scales=s)
+    with pytest.raises(Exception, match="exactly one of either scale/rotation pair"):
+        fn(x, m2, o, None, shs=sh, scales=s, rotations=q, cov3D_precomp=torch.zeros(3, 6))
+
+
+def test_precomputed_covariances_are_refused():
+    rast = RZ.GaussianRasterizer(_Settings())
+    x, m2, o, _, _ = _args()
     with pytest.raises(NotImplementedError, match="precomputed 3D covariances"):
-        rast(x, torch.zeros(P, 3), o, None, shs=sh, cov3D_precomp=torch.zeros(P, 6))
-    with pytest.raises(NotImplementedError, match="flag_max_count"):
-        rast(x, torch.zeros(P, 3), o, None, shs=sh, scales=s, rotations=q, flag_max_count=True)
+        rast(x, m2, o, None, shs=torch.zeros(3, 15, 3), cov3D_precomp=torch.zeros(3, 6))
+
+
+def test_cpu_tensors_are_refused():
+    rast = RZ.GaussianRasterizer(_Settings())
+    x, m2, o, s, q = _args()
+    dc, rest = torch.zeros(3, 1, 3), torch.zeros(3, 15, 3)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        rast(x, m2, o, None, dc=dc, shs=rest, scales=s, rotations=q, flag_max_count=True)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        rast.render_simp(x, m2, o, None, dc=dc, shs=rest, scales=s, rotations=q)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        rast.markVisible(x)
+
+
+def test_sh_layouts():
+    P = 4
+    dc = torch.arange(P * 3, dtype=torch.float32).reshape(P, 1, 3)
+    rest = torch.arange(P * 45, dtype=torch.float32).reshape(P, 15, 3)
+    # dc + rest read in place, rest = the coefficients beyond DC
+    (d, ds, r, rs, M, _), deg = RZ._full_sh(dc, rest, None, P, "cpu")
+    assert d is dc and r is rest and (ds, rs, M, deg) == (3, 45, 15, None)
     # without dc, shs carries every coefficient
-    color, radii, _ = rast(x, torch.zeros(P, 3), o, None, shs=sh, scales=s, rotations=q)
-    assert color.shape == (3, 8, 8) and torch.all(radii == 5)
+    full = torch.cat((dc, rest), 1)
+    (d, ds, r, rs, M, _), deg = RZ._full_sh(None, full, None, P, "cpu")
+    assert d is full and (ds, rs, M, deg) == (48, 48, 15, None)
+    # precomputed colours: a zero DC at degree 0 stands in
+    (d, ds, r, rs, M, _), deg = RZ._full_sh(torch.Tensor([]), torch.Tensor([]), torch.ones(P, 3), P, "cpu")
+    assert d.shape == (P, 1, 3) and not d.any() and M == 0 and deg == 0

@@ -204,3 +204,53 @@ def test_small_gradients(cuda_device):
              ("g_shs", acts[3].grad), ("g_opacities", acts[4].grad)]
     for name, t in pairs:
         assert_grad_close(t.cpu(), torch.from_numpy(g[name]), GRAD_RTOL, name)
+
+
+# ---- the full rasterizer (golden_full.npz, tests/golden/make_golden_full.py) ----
+
+def test_full_rasterizer_matches_reference_golden(cuda_device):
+    """GaussianRasterizer.forward (flag_max_count), render_simp and
+    markVisible against the reference's outputs: lists, ranges, n_contrib,
+    final T, radii and the counts bit-exact; images within 1e-5; with
+    precomputed colours, the gradients within 1e-4 (normwise)."""
+    from tests.golden.make_golden_full import activated_inputs, full_scene, input_checksum, settings
+    g = _load("golden_full.npz")
+    dev = cuda_device
+    sc, cam, culling, weight, colors = full_scene()
+    assert str(g["checksum"]) == input_checksum(sc, cam, culling, weight, colors)
+    inp = activated_inputs(sc, dev)
+    cull = culling.to(dev)
+    rast = RZ.GaussianRasterizer(settings(RZ, cam, dev))
+    x = {k: v.clone().requires_grad_(True) for k, v in inp.items()}
+    color, radii, amc = rast(x["means3D"], torch.zeros_like(inp["means3D"], requires_grad=True), x["opacities"],
+                             cull, dc=x["dc"], shs=x["shs"], scales=x["scales"], rotations=x["rotations"],
+                             flag_max_count=True)
+    st = color.grad_fn.state
+    R = len(g["point_list"])
+    assert np.array_equal(radii.cpu().numpy(), g["radii"])
+    assert np.array_equal(st.ranges.cpu().numpy(), g["ranges"])
+    assert np.array_equal(st.point_list[:R].cpu().numpy(), g["point_list"])
+    assert np.array_equal(st.n_contrib.cpu().numpy(), g["n_contrib"])
+    assert np.array_equal(st.final_T.cpu().numpy().view(np.uint32), g["final_T"].view(np.uint32))
+    assert np.abs(color.detach().cpu().numpy() - g["image"]).max() <= IMG_ATOL
+    assert np.array_equal(amc.cpu().numpy(), g["accum_max_count"])
+    with torch.no_grad():
+        _, _, acc_w, acc_n, acc_m = rast.render_simp(inp["means3D"], torch.zeros_like(inp["means3D"]),
+                                                     inp["opacities"], cull, dc=inp["dc"], shs=inp["shs"],
+                                                     scales=inp["scales"], rotations=inp["rotations"])
+        vis = rast.markVisible(inp["means3D"] * 3.0)
+    assert np.array_equal(acc_n.cpu().numpy(), g["accum_weights_count"])
+    assert np.array_equal(acc_m.cpu().numpy(), g["accum_max_count"])
+    w = g["accum_weights_ptr"]
+    assert np.abs(acc_w.cpu().numpy() - w).max() <= 1e-5 * max(1.0, float(np.abs(w).max()))
+    assert np.array_equal(vis.cpu().numpy(), g["mark_visible"])
+    # precomputed colours: image and gradients
+    y = {k: inp[k].clone().requires_grad_(True) for k in ("means3D", "opacities", "scales", "rotations")}
+    y["means2D"] = torch.zeros_like(inp["means3D"], requires_grad=True)
+    y["colors_precomp"] = colors.to(dev).requires_grad_(True)
+    color_pc, _, _ = rast(y["means3D"], y["means2D"], y["opacities"], cull, colors_precomp=y["colors_precomp"],
+                          scales=y["scales"], rotations=y["rotations"])
+    assert np.abs(color_pc.detach().cpu().numpy() - g["image_precomp"]).max() <= IMG_ATOL
+    (color_pc * weight.to(dev)).sum().backward()
+    for k in ("means3D", "means2D", "opacities", "scales", "rotations", "colors_precomp"):
+        assert_grad_close(y[k].grad.cpu(), torch.from_numpy(g["grad_" + k]), GRAD_RTOL, k)

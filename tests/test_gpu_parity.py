@@ -489,7 +489,9 @@ def test_exchange_records_routing_and_pack(cuda_device):
         rows = send_row[offs[k]:offs[k] + counts[k]].long() - 7
         assert torch.equal(rows, torch.nonzero(bits[:, k]).flatten())
         assert torch.equal(send[offs[k]:offs[k] + counts[k]], rec[rows])
-    ops.check_scan_status(cuda_device)
+    st = ops.queue_scan_status(cuda_device)
+    torch.cuda.synchronize()
+    ops.check_scan_status(st)
 
 
 def test_exchange_unpack_and_gradient_pack(cuda_device):
