@@ -211,7 +211,8 @@ __global__ void __launch_bounds__(256) tile_hist_kernel(BinParams p, unsigned* _
     const bool vis = i < p.P && p.counts[i] != 0u;
     const unsigned vm = __ballot_sync(0xffffffffu, vis);
     unsigned wb = 0u;
-    if (lane == 0 && vm) wb = atomicAdd(n_vis, (unsigned)__popc(vm));
+    if (!vm) continue;  // (warp-uniform) most of a view's Gaussians are off-screen
+    if (lane == 0) wb = atomicAdd(n_vis, (unsigned)__popc(vm));
     wb = __shfl_sync(0xffffffffu, wb, 0);
     if (vis) {
       const int64_t slot = (int64_t)wb + __popc(vm & ((1u << lane) - 1u));

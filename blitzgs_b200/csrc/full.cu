@@ -25,9 +25,12 @@ __global__ void __launch_bounds__(256) mark_visible_kernel(int64_t P, const floa
 }
 
 // Inverse of a column-major 4x4 matrix by cofactors (2x2 minors of the two
-// column pairs); a singular matrix yields non-finite entries, as any inverse.
-__device__ void invert4(const float* m, float* inv) {
-  auto at = [&](int r, int c) { return m[c * 4 + r]; };
+// row pairs), in float as the reference computes its inverse: the matrix is
+// ill-conditioned in its depth row (znear 0.01), so a more accurate inverse
+// would move every ray away from the reference's by ~7e-4 relative.  A
+// singular matrix yields non-finite entries, as any inverse.
+__device__ void invert4(const float* mf, float* inv) {
+  auto at = [&](int r, int c) { return mf[c * 4 + r]; };
   // minors of rows (0,1) and rows (2,3), columns (i,j)
   const float s0 = at(0, 0) * at(1, 1) - at(1, 0) * at(0, 1);
   const float s1 = at(0, 0) * at(1, 2) - at(1, 0) * at(0, 2);

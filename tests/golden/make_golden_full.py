@@ -140,9 +140,9 @@ def main():
         vis = rast.markVisible(inp["means3D"] * 3.0)
     torch.cuda.synchronize()
     keep = (radii > 0).cpu()
-    out = {"checksum": np.array(input_checksum(sc, cam, culling, weight, colors)), "radii": radii.cpu().numpy(),
+    out = {"checksum": np.array(input_checksum(sc, cam, culling, weight, colors)), "radii": radii.detach().cpu().numpy(),
            "image": color.cpu().numpy(), "image_precomp": color_pc.detach().cpu().numpy(),
-           "accum_max_count": amc.cpu().numpy(),
+           "accum_max_count": amc.detach().cpu().numpy(),
            "accum_weights_ptr": acc_w.cpu().numpy(), "accum_weights_count": acc_n.cpu().numpy(),
            "mark_visible": vis.cpu().numpy()}
     for k in ("depths", "rects", "means2D", "conic_opacity", "rgb"):
