@@ -206,25 +206,41 @@ __global__ void __launch_bounds__(256) tile_hist_kernel(BinParams p, unsigned* _
   __syncthreads();
   const int lane = threadIdx.x & 31;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t base = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31); base < p.P; base += stride) {
-    const int64_t i = base + lane;
-    const bool vis = i < p.P && p.counts[i] != 0u;
-    const unsigned vm = __ballot_sync(0xffffffffu, vis);
-    unsigned wb = 0u;
-    if (!vm) continue;  // (warp-uniform) most of a view's Gaussians are off-screen
-    if (lane == 0) wb = atomicAdd(n_vis, (unsigned)__popc(vm));
-    wb = __shfl_sync(0xffffffffu, wb, 0);
-    if (vis) {
-      const int64_t slot = (int64_t)wb + __popc(vm & ((1u << lane) - 1u));
-      if (slot < vis_cap)
-        vis_list[slot] = (uint32_t)i;
-      else
-        atomicOr(err, kErrBinOverflow);
+  // kHistUnroll chunks of 32 counts per warp and round, loaded together: most
+  // of a view's Gaussians are off-screen, so the walk is bound by the latency
+  // of these loads, not by the work behind them
+  constexpr int kHistUnroll = 8;
+  for (int64_t base0 = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31); base0 < p.P;
+       base0 += stride * kHistUnroll) {
+    unsigned bits = 0u;  // bit u: this lane's Gaussian of chunk u is visible
+#pragma unroll
+    for (int u = 0; u < kHistUnroll; ++u) {
+      const int64_t i = base0 + u * stride + lane;
+      bits |= (i < p.P && __ldcs(p.counts + i) != 0u ? 1u : 0u) << u;
     }
-    warp_expand<RECTS>(p, vis ? i : -1, s_mask, use_smem, [&](bool valid, int64_t, int t) {
-      const unsigned peers = tile_peers(valid, t);
-      if (valid && lane == __ffs(peers) - 1) atomicAdd(hist_smem ? &s_hist[t] : &tile_count[t], (unsigned)__popc(peers));
-    });
+    if (!__any_sync(0xffffffffu, bits)) continue;
+#pragma unroll 1
+    for (int u = 0; u < kHistUnroll; ++u) {
+      const int64_t i = base0 + u * stride + lane;
+      const bool vis = (bits >> u) & 1u;
+      const unsigned vm = __ballot_sync(0xffffffffu, vis);
+      if (!vm) continue;  // (warp-uniform)
+      unsigned wb = 0u;
+      if (lane == 0) wb = atomicAdd(n_vis, (unsigned)__popc(vm));
+      wb = __shfl_sync(0xffffffffu, wb, 0);
+      if (vis) {
+        const int64_t slot = (int64_t)wb + __popc(vm & ((1u << lane) - 1u));
+        if (slot < vis_cap)
+          vis_list[slot] = (uint32_t)i;
+        else
+          atomicOr(err, kErrBinOverflow);
+      }
+      warp_expand<RECTS>(p, vis ? i : -1, s_mask, use_smem, [&](bool valid, int64_t, int t) {
+        const unsigned peers = tile_peers(valid, t);
+        if (valid && lane == __ffs(peers) - 1)
+          atomicAdd(hist_smem ? &s_hist[t] : &tile_count[t], (unsigned)__popc(peers));
+      });
+    }
   }
   if (!hist_smem) return;
   __syncthreads();

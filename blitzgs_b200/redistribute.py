@@ -172,6 +172,16 @@ def redistribute(params, optimizer=None, group=None, mode="zorder", threshold=1.
         for p in params:
             st = optimizer.state.get(p, {})
             states.append([k for k in ("exp_avg", "exp_avg_sq") if k in st])
+        # every rank must move the same moments, or the exchanges below pair
+        # different tensors (or wait for ever): agree first, fail together
+        have = torch.tensor([[k in keys for k in ("exp_avg", "exp_avg_sq")] for keys in states],
+                            dtype=torch.int32, device=dev).reshape(-1)
+        lo_have, hi_have = have.clone(), have.clone()
+        dist.all_reduce(lo_have, op=dist.ReduceOp.MIN, group=group)
+        dist.all_reduce(hi_have, op=dist.ReduceOp.MAX, group=group)
+        if not torch.equal(lo_have, hi_have):
+            raise RuntimeError("redistribute: the ranks hold different Adam moments (a rank has not stepped "
+                               "its optimizer yet); step every rank, or redistribute before any step")
     moving = list(params)
     for p, keys in zip(params, states):
         moving += [optimizer.state[p][k] for k in keys]

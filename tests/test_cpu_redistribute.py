@@ -148,3 +148,36 @@ def test_trigger_is_the_reference_threshold():
         p.join(timeout=60)
     for _, out in res:
         assert out == (False, True, True)
+
+
+def _missing_moment_worker(rank, ws, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=ws)
+    try:
+        params, opt = _model(rank)
+        if rank == 1:  # this rank has not stepped its optimizer: no moments yet
+            for p in params:
+                opt.state.pop(p)
+        try:
+            RD.redistribute(params, opt, mode="round_robin", force=True)
+            q.put((rank, "no error"))
+        except RuntimeError as e:
+            q.put((rank, "raised" if "different Adam moments" in str(e) else repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ranks_with_different_moments_fail_together():
+    """A rank without Adam moments (not stepped yet) would make fewer
+    exchanges than the others; every rank raises before the first one."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_missing_moment_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    assert sorted(res) == [(0, "raised"), (1, "raised")]
