@@ -22,12 +22,108 @@ Parameter activations (exp, sigmoid, normalize) run inside the preprocess
 kernels with PyTorch's float arithmetic, and their backward is chained there
 too, so no activation or regulariser kernel runs in PyTorch.
 """
+import sys
+
 import torch
+from torch.autograd.graph import get_gradient_edge
 
 from . import densify as D
 from . import ops
 
 LAMBDA_DSSIM = 0.2
+
+
+class _GradBuffers:
+    """Dense parameter gradients written in place.
+
+    A camera's dense gradient is zero except at the rows of the Gaussians it
+    sees (a few percent of the model), yet a fresh dense tensor has to be
+    zero-filled in full (236 B per Gaussian, 1.9 GB per view at 8M).  When
+    ``loss.backward()`` would accumulate into the parameters' ``.grad``, the
+    fused step writes those rows straight into ``.grad`` instead: into the
+    existing gradient (accumulating over the views of a batch), or, when
+    ``.grad`` is None, into a buffer kept here whose rows written earlier are
+    zeroed again -- only those rows -- before it is handed out.  A buffer is
+    reused only when nothing else references its memory and its version
+    counter shows no in-place change since this class last wrote it;
+    otherwise it is zero-filled in full.  Not used under
+    ``torch.autograd.grad`` or with gradient hooks on the parameters (the
+    gradients are then returned the usual way)."""
+
+    def __init__(self):
+        self._entries = []  # dicts: t (buffer), dirty (row index tensors), version
+
+    @staticmethod
+    def _unshared(t):
+        # references: the entry, the caller's local and this call's argument
+        return sys.getrefcount(t) <= 4 and torch._C._storage_Use_Count(t.untyped_storage()._cdata) <= 2
+
+    def _clean(self, e):
+        t = e["t"]
+        if e["dirty"] is None or e["version"] != t._version:
+            t.zero_()
+        else:
+            for idx in e["dirty"]:
+                t.index_fill_(0, idx, 0)
+        e["dirty"] = []
+        e["version"] = t._version
+
+    def _take(self, like):
+        for e in self._entries:
+            t = e["t"]
+            if (t.shape == like.shape and t.dtype == like.dtype and t.device == like.device
+                    and self._unshared(t)):
+                self._clean(e)
+                return e
+        e = {"t": torch.empty_like(like, memory_format=torch.contiguous_format), "dirty": None, "version": -1}
+        self._entries.append(e)
+        self._clean(e)
+        return e
+
+    def _owned(self, g):
+        for e in self._entries:
+            if e["t"] is g:
+                return e
+        return None
+
+    def targets(self, params, nodes):
+        """(entries, accumulate) to write this view's gradient rows into, or
+        None to return the gradients the usual way."""
+        try:
+            if not all(torch._C._will_engine_execute_node(n) for n in nodes):
+                return None
+        except RuntimeError:  # torch.autograd.grad: no accumulation into .grad
+            return None
+        for p in params:
+            if p._backward_hooks or getattr(p, "_post_accumulate_grad_hooks", None):
+                return None
+        gs = [p.grad for p in params]
+        if all(g is None for g in gs):
+            return [self._take(p) for p in params], False
+        if any(g is None for g in gs):
+            return None
+        out = []
+        for p, g in zip(params, gs):
+            e = self._owned(g)
+            if e is not None and e["version"] == g._version:
+                out.append(e)
+            elif (g.layout == torch.strided and g.is_contiguous() and g.dtype == torch.float32
+                  and g.device == p.device and g.shape == p.shape and not g.requires_grad):
+                out.append({"t": g, "foreign": True})  # a gradient we do not track: add to it
+            else:
+                return None
+        return out, True
+
+    def written(self, params, entries, rows, fresh):
+        for p, e in zip(params, entries):
+            if fresh:
+                p.grad = e["t"]
+            if not e.get("foreign"):
+                e["dirty"].append(rows)
+                e["version"] = e["t"]._version
+
+
+_GRADS = _GradBuffers()
 
 
 class _ViewLoss(torch.autograd.Function):
@@ -62,6 +158,12 @@ class _ViewLoss(torch.autograd.Function):
         ctx.sparse_grad = sparse_grad
         ctx.consts = consts
         ctx.densify = densify
+        ctx.params = None
+        if not sparse_grad and vlist is not None:
+            params = (xyz, s_raw, q_raw, o_raw, dc, rest)
+            if all(t.is_leaf and t.requires_grad for t in params):
+                ctx.params = params
+                ctx.nodes = [get_gradient_edge(t).node for t in params]
         if densify is not None:
             D.update_max_radii(densify, radii)
         ctx.save_for_backward(xyz, s_raw, q_raw, o_raw, dc, rest, means2D, conic, rgb, radii, gt, partials,
@@ -85,7 +187,8 @@ class _ViewLoss(torch.autograd.Function):
             dL_dpix[:, y0:y1, :] = g_band
         L = ctx.state.n_list
         grads_dense = None
-        if not ctx.sparse_grad and vlist is not None:
+        inplace = _GRADS.targets(ctx.params, ctx.nodes) if ctx.params is not None else None
+        if inplace is None and not ctx.sparse_grad and vlist is not None:
             # The dense gradients are zero except at listed rows.  Their fill is
             # pure HBM writes (236 B per Gaussian); on a side stream it runs
             # beside the issue-bound loss and render backward instead of after them.
@@ -116,6 +219,8 @@ class _ViewLoss(torch.autograd.Function):
             shapes = [xyz.shape[1:], s_raw.shape[1:], q_raw.shape[1:], o_raw.shape[1:], dc.shape[1:], rest.shape[1:]]
             g_xyz, g_s, g_q, g_o, g_dc, g_rest = [torch.empty((n,) + tuple(sz), dtype=torch.float32, device=dev)
                                                   for sz in shapes]
+        elif inplace is not None:
+            g_xyz, g_s, g_q, g_o, g_dc, g_rest = [e["t"] for e in inplace[0]]
         elif grads_dense is not None:
             g_xyz, g_s, g_q, g_o, g_dc, g_rest = grads_dense
         else:
@@ -124,7 +229,12 @@ class _ViewLoss(torch.autograd.Function):
         ops.preprocess_backward_raw(radii, means2D, xyz, s_raw, q_raw, o_raw.reshape(-1), sh, ctx.raster,
                                     rec[:, 0:2], rec[:, 8:12], rec[:, 12:15],
                                     (g_xyz, g_s, g_q, g_o, (g_dc, 3), (g_rest, max(M, 1) * 3)), rot_norm=rot_norm,
-                                    reg_scale=scales[2:3], vis_list=vlist, vis_count=vcount, rows=rows)
+                                    reg_scale=scales[2:3], vis_list=vlist, vis_count=vcount, rows=rows,
+                                    accumulate=inplace is not None and inplace[1])
+        if inplace is not None:
+            # written straight into .grad: nothing left for autograd to accumulate
+            _GRADS.written(ctx.params, inplace[0], vlist[:L].to(torch.int64), fresh=not inplace[1])
+            return (None,) * 15
         grads = [g_xyz, g_s, g_q, g_o, g_dc, g_rest]
         if ctx.sparse_grad:
             idx = vlist[:L].to(torch.int64).unsqueeze(0)
