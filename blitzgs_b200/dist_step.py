@@ -32,7 +32,9 @@ import torch
 from . import densify as DZ
 from . import distributed as D
 from . import ops
-from .step import _zero_fill_async, _zero_fill_wait
+from torch.autograd.graph import get_gradient_edge
+
+from .step import _GRADS, _zero_fill_async, _zero_fill_wait
 
 # forward record: conic00 conic01 conic11 opacity | x y | r g b | depth radius(bits) minscale
 _FWD_C = 12
@@ -147,6 +149,9 @@ class _DistributedBatch(torch.autograd.Function):
         ctx.pre = (b_m2, b_radii, b_list, cnt, Pc, cams)
         ctx.counts, ctx.offs = counts, offs
         ctx.send_rows = send_row[:n_send].to(torch.int64)
+        params = (xyz, s_raw, q_raw, o_raw, dc, rest)
+        ctx.params = params if all(t.is_leaf and t.requires_grad for t in params) else None
+        ctx.nodes = [get_gradient_edge(t).node for t in params] if ctx.params is not None else None
         ctx.save_for_backward(xyz, s_raw, q_raw, o_raw, dc, rest)
         return loss_sum
 
@@ -157,10 +162,16 @@ class _DistributedBatch(torch.autograd.Function):
         n_cams = len(rasters)
         dev = xyz.device
         plan = ctx.plan
-        # the shard's dense gradients are zero except at listed rows: fill them on
-        # a side stream while the render backward (issue bound) runs
-        grads = [torch.empty_like(t) for t in (xyz, s_raw, q_raw, o_raw, dc, rest)]
-        _zero_fill_async(grads)
+        # the shard's dense gradients are zero except at listed rows: written in
+        # place into .grad (only the rows written before are zeroed again), or
+        # zero-filled on a side stream while the render backward (issue
+        # bound) runs
+        inplace = _GRADS.targets(ctx.params, ctx.nodes) if ctx.params is not None else None
+        if inplace is not None:
+            grads = [e["t"] for e in inplace[0]]
+        else:
+            grads = [torch.empty_like(t) for t in (xyz, s_raw, q_raw, o_raw, dc, rest)]
+            _zero_fill_async(grads)
         try:
             # receiver: render backward of the owned bands -> 12-float gradient records
             send = torch.zeros((sum(plan.recv_splits), _BWD_C), dtype=torch.float32, device=dev)
@@ -187,7 +198,8 @@ class _DistributedBatch(torch.autograd.Function):
             g_xyz, g_s, g_q, g_o, g_dc, g_rest = grads
         finally:
             # every exit orders this stream after the fill before the grads are used or freed
-            _zero_fill_wait()
+            if inplace is None:
+                _zero_fill_wait()
         b_m2, b_radii, b_list, cnt, Pc, cams = ctx.pre
         if densify is not None:
             for k in range(n_cams):
@@ -198,6 +210,11 @@ class _DistributedBatch(torch.autograd.Function):
         ops.preprocess_backward_raw_batch(b_radii, b_m2, b_list, cnt, Pc, xyz, s_raw, q_raw, o_raw.reshape(-1), sh,
                                           rasters, cams, acc, ctx.offs[:-1],
                                           (g_xyz, g_s, g_q, g_o, (g_dc, 3), (g_rest, max(M, 1) * 3)))
+        if inplace is not None:
+            rows = [b_list[k, :ctx.counts[k]].to(torch.int64) for k in range(n_cams) if ctx.counts[k]]
+            rows = torch.cat(rows) if rows else torch.zeros((0,), dtype=torch.int64, device=dev)
+            _GRADS.written(ctx.params, inplace[0], rows, fresh=not inplace[1])
+            return None, None, None, None, None, None, None
         return g_xyz, g_s, g_q, g_o, g_dc, g_rest, None
 
 
