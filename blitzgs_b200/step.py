@@ -68,11 +68,11 @@ class _GradBuffers:
         e["dirty"] = []
         e["version"] = t._version
 
-    def _take(self, like):
+    def _take(self, like, taken):
         for e in self._entries:
             t = e["t"]
             if (t.shape == like.shape and t.dtype == like.dtype and t.device == like.device
-                    and self._unshared(t)):
+                    and not any(e is x for x in taken) and self._unshared(t)):
                 self._clean(e)
                 return e
         e = {"t": torch.empty_like(like, memory_format=torch.contiguous_format), "dirty": None, "version": -1}
@@ -99,7 +99,10 @@ class _GradBuffers:
                 return None
         gs = [p.grad for p in params]
         if all(g is None for g in gs):
-            return [self._take(p) for p in params], False
+            taken = []
+            for p in params:  # parameters of one shape get one buffer each
+                taken.append(self._take(p, taken))
+            return taken, False
         if any(g is None for g in gs):
             return None
         out = []

@@ -2,14 +2,16 @@
 (blitzgs_b200.step._GradBuffers): only the rows of the Gaussians a view sees
 are written, into the existing gradient or into a reused buffer whose rows
 from earlier views are zeroed again.  Checked against the gradients the same
-step returns through ``torch.autograd.grad`` (which never writes in place),
-bit for bit: one view, two views accumulated in one backward, a reused buffer
+step returns through ``torch.autograd.grad`` (which never writes in place), up
+to the order of the render backward's float atomics (normwise 1e-6; a row
+left over from an earlier view would be off by its whole value): one view, two views accumulated in one backward, a reused buffer
 after ``.grad = None`` with a different view, after an in-place change of the
 gradient, and while another reference to the old gradient is alive."""
 import pytest
 import torch
 
 from blitzgs_b200 import scene as S, step as ST
+from tests.helpers import normwise_rel
 
 pytestmark = pytest.mark.gpu
 
@@ -38,10 +40,14 @@ def _expected(model, rasters, gts, views):
     return torch.autograd.grad(_loss(model, rasters, gts, views), model)
 
 
+def _close(a, e):
+    return normwise_rel(a, e) <= 1e-6
+
+
 def _check(model, expected):
     for p, e in zip(model, expected):
         assert p.grad is not None and p.grad.shape == p.shape
-        assert torch.equal(p.grad, e)
+        assert _close(p.grad, e), normwise_rel(p.grad, e)
 
 
 def test_in_place_gradients_equal_the_returned_ones(case):
@@ -85,4 +91,4 @@ def test_in_place_gradients_equal_the_returned_ones(case):
     _loss(model, rasters, gts, [0]).backward()
     exp = _expected(model, rasters, gts, [0])
     for p, e in zip(model, exp):
-        assert torch.equal(p.grad, e + 0.5)
+        assert _close(p.grad, e + 0.5)
