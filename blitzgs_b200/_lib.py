@@ -72,6 +72,7 @@ SIGNATURES = {
     "blitz_read_totals": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "blitz_zero_fill_async": (_i32, [_i32, _vp, _vp, _vp]),
     "blitz_zero_fill_wait": (_i32, [_vp]),
+    "blitz_zero_rows": (_i32, [_i32, _vp, _vp, _vp, _i64, _vp]),
     "blitz_exchange_unpack": (_i32, [_i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "blitz_grad_records_pack": (_i32, [_i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
 }

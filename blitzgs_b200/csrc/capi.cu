@@ -936,6 +936,24 @@ int blitz_zero_fill_wait(void* stream) {
   return check((int)cudaStreamWaitEvent(S(stream), f->done, 0), "blitz_zero_fill_wait");
 }
 
+int blitz_zero_rows(int n_arrays, void* const* arrays, const size_t* row_bytes, const uint32_t* rows, int64_t n_rows,
+                    void* stream) {
+  if (n_arrays < 0 || n_arrays > kZeroRowsMax || n_rows < 0 || (n_arrays > 0 && (!arrays || !row_bytes)) ||
+      (n_rows > 0 && !rows))
+    return fail(BLITZ_EINVAL, "blitz_zero_rows: bad arguments");
+  ZeroRowsParams p{};
+  p.n_arrays = n_arrays;
+  p.rows = rows;
+  p.n_rows = n_rows;
+  for (int a = 0; a < n_arrays; ++a) {
+    if (!arrays[a] || row_bytes[a] == 0 || (row_bytes[a] & 3u) || (reinterpret_cast<uintptr_t>(arrays[a]) & 3u))
+      return fail(BLITZ_EINVAL, "blitz_zero_rows: arrays need 4-byte aligned rows of whole 32-bit words");
+    p.arrays[a] = arrays[a];
+    p.row_words[a] = (int64_t)(row_bytes[a] / 4);
+  }
+  return check(launch_zero_rows(p, S(stream)), "blitz_zero_rows");
+}
+
 int blitz_fp32_probe(int blocks, int64_t iters, float* sink, void* stream) {
   if (blocks <= 0 || iters <= 0 || !sink) return fail(BLITZ_EINVAL, "blitz_fp32_probe: bad arguments");
   return check(launch_fma_probe(blocks, iters, sink, S(stream)), "blitz_fp32_probe");

@@ -366,6 +366,19 @@ int launch_depth_render(const DepthParams& p, cudaStream_t st);
 // Frustum mark of markVisible (rasterizer_impl.cu:100-114): view depth > 0.2.
 int launch_mark_visible(int64_t P, const float* means3D, const float* viewmatrix, bool* present, cudaStream_t st);
 
+// Zero rows[0..n_rows) of up to kZeroRowsMax dense row-major arrays (row i
+// of array a: row_words[a] 32-bit words at arrays[a] + i * row_words[a]).
+constexpr int kZeroRowsMax = 8;
+struct ZeroRowsParams {
+  int n_arrays;
+  void* arrays[kZeroRowsMax];
+  int64_t row_words[kZeroRowsMax];
+  const uint32_t* rows;  // device [n_rows]
+  int64_t n_rows;
+};
+
+int launch_zero_rows(const ZeroRowsParams& p, cudaStream_t st);
+
 int launch_fma_probe(int blocks, int64_t iters, float* sink, cudaStream_t st);
 
 // Records the message blitz_last_error() returns on this thread (capi.cu).

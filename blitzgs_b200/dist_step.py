@@ -211,9 +211,9 @@ class _DistributedBatch(torch.autograd.Function):
                                           rasters, cams, acc, ctx.offs[:-1],
                                           (g_xyz, g_s, g_q, g_o, (g_dc, 3), (g_rest, max(M, 1) * 3)))
         if inplace is not None:
-            rows = [b_list[k, :ctx.counts[k]].to(torch.int64) for k in range(n_cams) if ctx.counts[k]]
-            rows = torch.cat(rows) if rows else torch.zeros((0,), dtype=torch.int64, device=dev)
-            _GRADS.written(ctx.params, inplace[0], rows, fresh=not inplace[1])
+            rows = [b_list[k, :ctx.counts[k]] for k in range(n_cams) if ctx.counts[k]]
+            rows = torch.cat(rows) if rows else torch.zeros((0,), dtype=torch.int32, device=dev)
+            _GRADS.written(ctx.params, inplace[0], (rows, rows.numel()), fresh=not inplace[1])
             return None, None, None, None, None, None, None
         return g_xyz, g_s, g_q, g_o, g_dc, g_rest, None
 

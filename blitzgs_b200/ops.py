@@ -786,6 +786,21 @@ def zero_fill_async(tensors):
     _lib.call("blitz_zero_fill_async", n, ptrs, sizes, _lib.stream_ptr())
 
 
+def zero_rows(tensors, rows, n_rows):
+    """Zero rows ``rows[:n_rows]`` (device uint32/int32 indices) of each
+    contiguous tensor in ``tensors`` (at most 8, rows along dim 0), in one
+    launch on the current stream."""
+    n = len(tensors)
+    if n == 0 or n_rows <= 0:
+        return
+    for t in tensors:
+        if not t.is_contiguous() or t.dtype != torch.float32:
+            raise RuntimeError("zero_rows: contiguous float32 tensors only")
+    ptrs = (ctypes.c_void_p * n)(*[t.data_ptr() for t in tensors])
+    sizes = (ctypes.c_size_t * n)(*[t[0].numel() * 4 for t in tensors])
+    _lib.call("blitz_zero_rows", n, ptrs, sizes, ptr(rows), int(n_rows), _lib.stream_ptr())
+
+
 def zero_fill_wait():
     _lib.call("blitz_zero_fill_wait", _lib.stream_ptr())
 

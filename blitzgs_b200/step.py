@@ -58,26 +58,34 @@ class _GradBuffers:
         # references: the entry, the caller's local and this call's argument
         return sys.getrefcount(t) <= 4 and torch._C._storage_Use_Count(t.untyped_storage()._cdata) <= 2
 
-    def _clean(self, e):
-        t = e["t"]
-        if e["dirty"] is None or e["version"] != t._version:
-            t.zero_()
-        else:
-            for idx in e["dirty"]:
-                t.index_fill_(0, idx, 0)
-        e["dirty"] = []
-        e["version"] = t._version
+    @staticmethod
+    def _clean(entries):
+        """Zero what earlier views wrote into the buffers: the listed rows,
+        in one launch per row list for every buffer that shares it, or the
+        whole buffer when its contents are unknown."""
+        lists = {}
+        for e in entries:
+            t = e["t"]
+            if e["dirty"] is None or e["version"] != t._version:
+                t.zero_()
+            else:
+                for rows, n in e["dirty"]:
+                    lists.setdefault(id(rows), (rows, n, []))[2].append(t)
+            e["dirty"] = []
+        for rows, n, ts in lists.values():
+            for k in range(0, len(ts), 8):
+                ops.zero_rows(ts[k:k + 8], rows, n)
+        for e in entries:
+            e["version"] = e["t"]._version
 
     def _take(self, like, taken):
         for e in self._entries:
             t = e["t"]
             if (t.shape == like.shape and t.dtype == like.dtype and t.device == like.device
                     and not any(e is x for x in taken) and self._unshared(t)):
-                self._clean(e)
                 return e
         e = {"t": torch.empty_like(like, memory_format=torch.contiguous_format), "dirty": None, "version": -1}
         self._entries.append(e)
-        self._clean(e)
         return e
 
     def _owned(self, g):
@@ -102,6 +110,7 @@ class _GradBuffers:
             taken = []
             for p in params:  # parameters of one shape get one buffer each
                 taken.append(self._take(p, taken))
+            self._clean(taken)
             return taken, False
         if any(g is None for g in gs):
             return None
@@ -118,6 +127,7 @@ class _GradBuffers:
         return out, True
 
     def written(self, params, entries, rows, fresh):
+        """``rows`` = (device index tensor, count): the rows this view wrote."""
         for p, e in zip(params, entries):
             if fresh:
                 p.grad = e["t"]
@@ -236,7 +246,7 @@ class _ViewLoss(torch.autograd.Function):
                                     accumulate=inplace is not None and inplace[1])
         if inplace is not None:
             # written straight into .grad: nothing left for autograd to accumulate
-            _GRADS.written(ctx.params, inplace[0], vlist[:L].to(torch.int64), fresh=not inplace[1])
+            _GRADS.written(ctx.params, inplace[0], (vlist, L), fresh=not inplace[1])
             return (None,) * 15
         grads = [g_xyz, g_s, g_q, g_o, g_dc, g_rest]
         if ctx.sparse_grad:

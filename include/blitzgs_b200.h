@@ -464,6 +464,16 @@ int blitz_read_totals(const int64_t* totals, const int32_t* vis_count, const uin
  * `stream` touches the buffers.  Not re-entrant across host threads.
  */
 int blitz_zero_fill_async(int n, void* const* ptrs, const size_t* bytes, void* stream);
+
+/*
+ * Zero the listed rows of up to 8 dense row-major arrays in one launch on
+ * `stream` (no counterpart in the reference): row rows[i] of array a, i.e.
+ * row_bytes[a] bytes (a multiple of 4) at arrays[a] + rows[i] * row_bytes[a].
+ * rows: device uint32 [n_rows].  Used to reset the rows of a reused dense
+ * gradient buffer that an earlier view wrote, instead of the whole buffer.
+ */
+int blitz_zero_rows(int n_arrays, void* const* arrays, const size_t* row_bytes, const uint32_t* rows, int64_t n_rows,
+                    void* stream);
 int blitz_zero_fill_wait(void* stream);
 
 /*

@@ -44,6 +44,6 @@ def test_ncu_traffic_table_is_per_stage_bytes(bench):
 
 
 def test_launch_accounting(bench):
-    # one single-GPU view: the 27 native kernels of the ncu launch list
-    assert bench.LAUNCHES_PER_VIEW == 27
-    assert bench.DIST_LAUNCHES_PER_BAND == 27 and bench.DIST_LAUNCHES_PER_CAMERA == 4
+    # one single-GPU view: the 14 native kernels of the ncu launch list
+    assert bench.LAUNCHES_PER_VIEW == 14
+    assert bench.DIST_LAUNCHES_PER_BAND == 14 and bench.DIST_LAUNCHES_PER_CAMERA == 4
