@@ -43,6 +43,11 @@ constexpr int kMaskSmem = 32 * 1024;  // tiles whose mask is staged in shared me
 constexpr int kHistSmem = 8192;       // tiles counted in a shared-memory histogram
 constexpr int kSortSmem = 4096;       // keys a tile_sort CTA sorts in shared memory
 constexpr int kSortThreads = 256;
+// A merge round of the long lists is split into output slices of
+// kMergeSlice keys, kMergeUnits per chunk: four times the CTAs of one slice
+// per chunk, so a round over a few very long lists still fills the GPU.
+constexpr int kMergeSlice = 1024;
+constexpr int kMergeUnits = kSortSmem / kMergeSlice;
 
 __device__ __forceinline__ bool tile_on(const bool* s_mask, const bool* g_mask, int t, bool use_smem) {
   if (!g_mask) return true;
@@ -523,7 +528,7 @@ __device__ __forceinline__ int tile_of_chunk(const unsigned* chunk_start, int n_
 // every chunk of kSortSmem keys is sorted in shared memory by some CTA, then
 // runs of width w = kSortSmem, 2 kSortSmem, ... are merged pairwise until
 // the longest list is one run, with a grid-wide barrier between steps.  In a
-// merge step a CTA produces one kSortSmem-key output slice: a warp-wide
+// merge step a CTA produces one kMergeSlice-key output slice: a warp-wide
 // co-rank search finds the input ranges of both runs in global memory, the
 // block stages them in shared memory with coalesced loads, merges there and
 // stores the slice coalesced -- as indices, in the last step.
@@ -557,14 +562,17 @@ __global__ void __launch_bounds__(kSortThreads) big_tile_sort_kernel(const uint2
   for (int64_t w = kSortSmem; w < (int64_t)longest; w <<= 1) {
     const bool last = 2 * w >= (int64_t)longest;
     grid.sync();
-    for (unsigned b = blockIdx.x; b < n_chunks; b += gridDim.x) {
+    for (unsigned u = blockIdx.x; u < n_chunks * kMergeUnits; u += gridDim.x) {
+      const unsigned b = u / kMergeUnits;
       const int t = tile_of_chunk(chunk_start, n_tiles, b);
       const uint2 r = ranges[t];
       const int64_t n = (int64_t)(r.y - r.x);
-      const int64_t k0 = (int64_t)(b - chunk_start[t]) * kSortSmem;  // this output slice of the tile
-      const int64_t a0 = (k0 / (2 * w)) * (2 * w);                    // its pair of runs
+      // this output slice of the tile: kSortSmem / kMergeUnits outputs
+      const int64_t k0 = (int64_t)(b - chunk_start[t]) * kSortSmem + (int64_t)(u % kMergeUnits) * kMergeSlice;
+      if (k0 >= n) continue;  // (uniform over the CTA) the tail of the tile's last chunk
+      const int64_t a0 = (k0 / (2 * w)) * (2 * w);  // its pair of runs
       const int64_t na = std::min<int64_t>(w, n - a0), nb = std::max<int64_t>(0, std::min<int64_t>(w, n - a0 - w));
-      const int len = (int)std::min<int64_t>(kSortSmem, n - k0);
+      const int len = (int)std::min<int64_t>(kMergeSlice, n - k0);
       const unsigned long long* ga = src + r.x + a0;
       const unsigned long long* gb = ga + na;
       if (warp < 2) {
