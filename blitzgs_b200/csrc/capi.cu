@@ -1055,6 +1055,8 @@ int blitz_rasterize_depth(int64_t P, int image_height, int image_width, const fl
       !discriminants || (P > 0 && (!means2D || !conic_opacity || !rgb || !point_list || !means3D || !scales ||
                                    !rotations)))
     return fail(BLITZ_EINVAL, "blitz_rasterize_depth: null pointer");
+  if (P > 0 && (!aligned16(rotations) || !aligned16(conic_opacity)))
+    return fail(BLITZ_EINVAL, "blitz_rasterize_depth: rotations and conic_opacity need 16-byte aligned rows");
   DepthParams d{};
   d.W = image_width;
   d.H = image_height;

@@ -87,7 +87,11 @@ __global__ void __launch_bounds__(kTilePix) depth_render_kernel(DepthParams p) {
   __shared__ int s_id[kDepthBatch];
   __shared__ float4 s_co[kDepthBatch];
   __shared__ float2 s_xy[kDepthBatch];
-  __shared__ float s_g[kDepthBatch][10];  // mean xyz, scale xyz, quaternion r,x,y,z
+  // per Gaussian, for the ray-ellipsoid test: the world -> Gaussian rotation
+  // (9), 1/(3 s)^2 per axis (3), the camera centre in the Gaussian frame
+  // scaled by 1/(3 s)^2 (3) and the constant term c of the quadratic (1).
+  // All of it depends on the Gaussian and the camera only, not the pixel.
+  __shared__ float s_g[kDepthBatch][16];
   const int tile = blockIdx.x;
   const int tx = tile % p.grid_x, ty = tile / p.grid_x;
   const int px = tx * kTileX + (threadIdx.x % kTileX), py = ty * kTileY + (threadIdx.x / kTileX);
@@ -124,11 +128,28 @@ __global__ void __launch_bounds__(kTilePix) depth_render_kernel(DepthParams p) {
       s_xy[threadIdx.x] = reinterpret_cast<const float2*>(p.means2D)[id];
       s_co[threadIdx.x] = reinterpret_cast<const float4*>(p.conic_opacity)[id];
       float* g = s_g[threadIdx.x];
-      for (int c = 0; c < 3; ++c) {
-        g[c] = p.means3D[3 * (int64_t)id + c];
-        g[3 + c] = p.scales[3 * (int64_t)id + c];
+      const float4 q = reinterpret_cast<const float4*>(p.rotations)[id];
+      const float qr = q.x, qx = q.y, qy = q.z, qz = q.w;
+      // the transpose of the rotation built from q (quaternion as given)
+      const float R[9] = {1.f - 2.f * (qy * qy + qz * qz), 2.f * (qx * qy + qr * qz), 2.f * (qx * qz - qr * qy),
+                          2.f * (qx * qy - qr * qz), 1.f - 2.f * (qx * qx + qz * qz), 2.f * (qy * qz + qr * qx),
+                          2.f * (qx * qz + qr * qy), 2.f * (qy * qz - qr * qx), 1.f - 2.f * (qx * qx + qy * qy)};
+      const float v[3] = {o.x - p.means3D[3 * (int64_t)id + 0], o.y - p.means3D[3 * (int64_t)id + 1],
+                          o.z - p.means3D[3 * (int64_t)id + 2]};
+      float c = -1.f;
+#pragma unroll
+      for (int r = 0; r < 3; ++r) {
+        const float s3 = p.scales[3 * (int64_t)id + r] * 3.0f;
+        const float is2 = 1.0f / (s3 * s3);
+        const float ro = R[3 * r] * v[0] + R[3 * r + 1] * v[1] + R[3 * r + 2] * v[2];  // rotated origin
+        g[r * 3 + 0] = R[3 * r];
+        g[r * 3 + 1] = R[3 * r + 1];
+        g[r * 3 + 2] = R[3 * r + 2];
+        g[9 + r] = is2;
+        g[12 + r] = ro * is2;
+        c += ro * ro * is2;
       }
-      for (int c = 0; c < 4; ++c) g[6 + c] = p.rotations[4 * (int64_t)id + c];
+      g[15] = c;
     }
     __syncthreads();
     const int cnt = min(kDepthBatch, n - base);
@@ -150,27 +171,15 @@ __global__ void __launch_bounds__(kTilePix) depth_render_kernel(DepthParams p) {
       C1 += p.rgb[3 * (int64_t)id + 1] * alpha * T;
       C2 += p.rgb[3 * (int64_t)id + 2] * alpha * T;
       const float* g = s_g[j];
-      const float qr = g[6], qx = g[7], qy = g[8], qz = g[9];
-      // world -> Gaussian frame: the transpose of the rotation built from q
-      const float R[3][3] = {
-          {1.f - 2.f * (qy * qy + qz * qz), 2.f * (qx * qy + qr * qz), 2.f * (qx * qz - qr * qy)},
-          {2.f * (qx * qy - qr * qz), 1.f - 2.f * (qx * qx + qz * qz), 2.f * (qy * qz + qr * qx)},
-          {2.f * (qx * qz + qr * qy), 2.f * (qy * qz - qr * qx), 1.f - 2.f * (qx * qx + qy * qy)}};
-      const float v[3] = {o.x - g[0], o.y - g[1], o.z - g[2]};
       const float w[3] = {u.x, u.y, u.z};
-      float ta[3], tb[3], tc[3];  // per axis: (d/3s) d/3s, (d/3s) o/3s, (o/3s) o/3s
+      float a = 0.f, bh = 0.f;  // a t^2 + 2 bh t + c: the ray in the Gaussian's 3-sigma frame
 #pragma unroll
       for (int r = 0; r < 3; ++r) {
-        const float ro = R[r][0] * v[0] + R[r][1] * v[1] + R[r][2] * v[2];  // rotated origin
-        const float rd = R[r][0] * w[0] + R[r][1] * w[1] + R[r][2] * w[2];  // rotated direction
-        const float s3 = g[3 + r] * 3.0f;
-        ta[r] = rd / s3 * rd / s3;
-        tb[r] = rd / s3 * ro / s3;
-        tc[r] = ro / s3 * ro / s3;
+        const float rd = g[3 * r] * w[0] + g[3 * r + 1] * w[1] + g[3 * r + 2] * w[2];  // rotated direction
+        a += rd * rd * g[9 + r];
+        bh += rd * g[12 + r];
       }
-      const float a = ta[0] + ta[1] + ta[2];
-      const float b = 2 * (tb[0] + tb[1] + tb[2]);
-      const float c = tc[0] + tc[1] + tc[2] - 1;
+      const float b = 2 * bh, c = g[15];
       const float t_star = -b / 2 / a;
       const float depth = t_star / ray_len;
       if (depth < 0) continue;
