@@ -762,6 +762,87 @@ def run_reference(args):
     return dict(ms=ms, ms_e2e=ms_e2e, clocks=clk, H=H, W=W, P=sc.P)
 
 
+def run_ops_case(args):
+    """Profiling case for the kernels the fused step does not run (no timing,
+    no bench line): on one GPU, a mid-scene camera through the operator API
+    (forward and backward), the full rasterizer (forward with
+    flag_max_count and its backward, render_simp, render_depth,
+    markVisible), SparseGaussianAdam (dense mask and compact rows) and a
+    one-rank exchange batch.  Runs it three times, the third between
+    cudaProfilerStart / cudaProfilerStop (for ncu --profile-from-start off)."""
+    import datetime
+
+    import torch.distributed as dist
+
+    from blitzgs_b200 import scene as S, rasterizer as RZ, dist_step as DS, distributed as D, step as ST
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29561")
+    dist.init_process_group("nccl", rank=0, world_size=1, timeout=datetime.timedelta(seconds=60), device_id=dev)
+    sc = S.mid(seed=1, P=args.gaussians or 300_000, n_cams=2)
+    raw = [t.to(dev).contiguous().requires_grad_(True) for t in
+           (sc.xyz, sc.scaling, sc.rotation, sc.opacity, sc.features_dc, sc.features_rest)]
+    xyz, s_raw, q_raw, o_raw, dc, rest = raw
+    cams = [c.to(dev) for c in sc.cameras]
+    rs = S.raster_settings(cams[0], device=dev)
+    H, W = cams[0].image_height, cams[0].image_width
+    D.init_context(0, 1, H, W, group=None, bsz=1)
+    history = D.DivisionStrategyHistoryFinal(cams, 1, 0)
+    gt = S.target_image(0, H, W).to(dev)
+    opt = RZ.SparseGaussianAdam([{"params": [p], "lr": 1e-3} for p in raw], lr=1e-3, eps=1e-15)
+    ca = {"mode": "train", "world_size": "1", "global_rank": "0", "local_rank": "0", "mp_world_size": "1",
+          "mp_rank": "0", "log_folder": "/tmp", "log_interval": "1000000", "iteration": "1",
+          "avoid_pixel_all2all": False, "stats_collector": {}}
+
+    def activated():
+        return torch.exp(s_raw), torch.nn.functional.normalize(q_raw), torch.sigmoid(o_raw)
+
+    def once():
+        rast = RZ.GaussianRasterizer(rs)
+        scales, rots, opac = activated()
+        m2, rgb, co, radii, depths = rast.preprocess_gaussians(xyz, scales, rots, torch.cat((dc, rest), 1), opac, ca)
+        cl = torch.ones(((H + 15) // 16, (W + 15) // 16), dtype=torch.bool, device=dev)
+        color, *_ = rast.render_gaussians(m2, torch.zeros((xyz.shape[0], 3), device=dev), co, rgb, None, depths,
+                                          radii, cl, None, ca)
+        color.sum().backward()
+        scales, rots, opac = activated()
+        screen = torch.zeros_like(xyz, requires_grad=True)
+        cull = torch.zeros(xyz.shape[0], dtype=torch.bool, device=dev)
+        c2, _, _ = rast(xyz, screen, opac, cull, dc=dc, shs=rest, scales=scales, rotations=rots,
+                        flag_max_count=True)
+        c2.sum().backward()
+        with torch.no_grad():
+            rast.render_simp(xyz, screen, opac, cull, dc=dc, shs=rest, scales=scales, rotations=rots)
+            rast.render_depth(xyz, screen, opac, cull, dc=dc, shs=rest, scales=scales, rotations=rots)
+            rast.markVisible(xyz)
+        opt.step(radii > 0, xyz.shape[0])
+        for p in raw:
+            p.grad = None
+        ST.view_loss(raw, rs, gt, sparse_grad=True)[0].backward()
+        opt.step()
+        for p in raw:
+            p.grad = None
+        strategies, _ = D.start_strategy_final(cams, history)
+        gts = []
+        for k in range(len(cams)):
+            y0, y1 = strategies[k].row_range(0)
+            gts.append(S.target_image(k, H, W).to(dev)[:, y0 * 16:min(H, y1 * 16)])
+        DS.batch_loss(raw, [S.raster_settings(c, device=dev) for c in cams], gts, strategies).backward()
+        for p in raw:
+            p.grad = None
+        torch.cuda.synchronize()
+
+    once()
+    once()
+    torch.cuda.cudart().cudaProfilerStart()
+    once()
+    torch.cuda.cudart().cudaProfilerStop()
+    dist.destroy_process_group()
+    print(json.dumps({"ops_case": "ok", "gaussians": xyz.shape[0]}), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -781,8 +862,12 @@ def main():
     ap.add_argument("--gaussians", type=int, default=None,
                     help="Gaussian count of the scene (default: the config's); a smaller scene of the same "
                          "distribution is the profiling case")
+    ap.add_argument("--ops-case", action="store_true",
+                    help="profiling case of the kernels outside the fused step (no bench line; see run_ops_case)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.ops_case:
+        return run_ops_case(args)
 
     ws, rank, local = dist_setup(args.gpus)
     cfg = {"workload": f"{args.config} (BASELINE config 3: 8M clustered Gaussians, 1152x864 aerial views)"
