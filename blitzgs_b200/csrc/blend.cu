@@ -171,8 +171,6 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
   __shared__ float4 s_b[kWarps][32];
   __shared__ float4 s_c[kWarps][32];
   __shared__ int s_id[kWarps][32];
-  __shared__ int s_obs[kWarps][32];
-  __shared__ int s_act[kWarps][32];  // did any pixel of the strip take this Gaussian?
   __shared__ int s_red[32];
   __shared__ float s_w[STATS ? kWarps : 1][32];  // STATS: blend weights and counts per batch entry
   __shared__ int s_n[STATS ? kWarps : 1][32];
@@ -233,8 +231,6 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
       s_b[warp][slot] = make_float4(co.z, co.w, skip_threshold(co.w), __int_as_float(k + 1));
       s_c[warp][slot] = make_float4(p.rgb[3 * (int64_t)id + 0], p.rgb[3 * (int64_t)id + 1],
                                     p.rgb[3 * (int64_t)id + 2], 0.f);
-      s_obs[warp][slot] = 0;
-      s_act[warp][slot] = 0;
       if (STATS) {
         s_w[warp][slot] = 0.f;
         s_n[warp][slot] = 0;
@@ -242,6 +238,10 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
     }
     __syncwarp();
     const int kept = __popc(km);
+    // per lane, bit j: this pixel blended batch entry j (act) while T > 0.5 (obs);
+    // reduced over the warp after the loop instead of shared-memory atomics
+    // that all lanes would aim at the same word
+    unsigned act_bits = 0u, obs_bits = 0u;
     for (int j = 0; !done && j < kept; ++j) {
       const float4 ga = s_a[warp][j];
       const float4 gb = s_b[warp][j];
@@ -258,7 +258,7 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
         continue;
       }
       ++n2l;
-      s_act[warp][j] = 1;
+      act_bits |= 1u << j;
       const float4 cth = s_c[warp][j];
       C0 += cth.x * alpha * T;
       C1 += cth.y * alpha * T;
@@ -274,7 +274,7 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
           atomicAdd(&s_n[warp][j], 1);
         }
       } else if (T > 0.5) {
-        atomicAdd(&s_obs[warp][j], 1);
+        obs_bits |= 1u << j;
       }
       T = test_T;
       last_contributor = (uint32_t)__float_as_int(gb.w);
@@ -285,12 +285,21 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
         atomicAdd(&p.accum_w[s_id[warp][lane]], s_w[warp][lane]);
         atomicAdd(&p.accum_n[s_id[warp][lane]], s_n[warp][lane]);
       }
-    } else if (lane < kept && s_obs[warp][lane] > 0) {
-      atomicAdd(&p.out_observe[s_id[warp][lane]], s_obs[warp][lane]);
+    } else {
+      // observation count of entry j = lanes with bit j; lane j flushes it
+      unsigned todo = __reduce_or_sync(0xffffffffu, obs_bits);
+      int my_obs = 0;
+      while (todo) {
+        const int j = __ffs(todo) - 1;
+        todo &= todo - 1u;
+        const int c = __popc(__ballot_sync(0xffffffffu, (obs_bits >> j) & 1u));
+        if (lane == j) my_obs = c;
+      }
+      if (my_obs) atomicAdd(&p.out_observe[s_id[warp][lane]], my_obs);
     }
     if (strip_ids) {
       // append this batch's contributing Gaussians to the strip's list, in order
-      const bool a = lane < kept && s_act[warp][lane] != 0;
+      const bool a = ((__reduce_or_sync(0xffffffffu, act_bits) >> lane) & 1u) != 0;
       const unsigned am = __ballot_sync(0xffffffffu, a);
       if (a) {
         const int at = n_act + __popc(am & ((1u << lane) - 1u));

@@ -3,8 +3,8 @@
 // The fused step hands out dense parameter gradients whose only non-zero
 // rows are the ones an earlier view wrote; before a buffer is reused, those
 // rows -- a few percent of the model -- are zeroed instead of the whole
-// buffer.  blockIdx.y picks the array; each warp clears one listed row at a
-// time, its lanes on consecutive words of the row.
+// buffer.  blockIdx.y picks the array; the words of the listed rows are
+// spread over the threads of a grid-stride loop.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -15,13 +15,14 @@ namespace {
 __global__ void __launch_bounds__(256) zero_rows_kernel(ZeroRowsParams p) {
   const int a = blockIdx.y;
   uint32_t* base = reinterpret_cast<uint32_t*>(p.arrays[a]);
-  const int64_t words = p.row_words[a];
-  const int lane = threadIdx.x & 31;
-  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  // one warp per listed row: its lanes clear the row's words (no division)
-  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < p.n_rows; r += warps) {
-    uint32_t* row = base + (int64_t)p.rows[r] * words;
-    for (int64_t c = lane; c < words; c += 32) row[c] = 0u;
+  const uint32_t words = (uint32_t)p.row_words[a];
+  // flat (listed row, word) index: consecutive threads write consecutive words
+  // of a row and then of the next listed row, so narrow rows (3-4 words)
+  // still keep every lane busy; 32-bit arithmetic (the launcher checks the range)
+  const uint32_t total = words * (uint32_t)p.n_rows;
+  for (uint32_t f = blockIdx.x * blockDim.x + threadIdx.x; f < total; f += gridDim.x * blockDim.x) {
+    const uint32_t r = f / words;
+    base[(int64_t)p.rows[r] * words + (f - r * words)] = 0u;
   }
 }
 
@@ -29,8 +30,11 @@ __global__ void __launch_bounds__(256) zero_rows_kernel(ZeroRowsParams p) {
 
 int launch_zero_rows(const ZeroRowsParams& p, cudaStream_t st) {
   if (p.n_arrays <= 0 || p.n_rows <= 0) return 0;
-  const int64_t need = (p.n_rows + 7) / 8;  // 8 warps (rows) per block and round
-  const unsigned blocks = (unsigned)(need < 1184 ? need : 1184);
+  int64_t most = 0;
+  for (int a = 0; a < p.n_arrays; ++a) most = p.row_words[a] > most ? p.row_words[a] : most;
+  if (most * p.n_rows >= (int64_t)1 << 31) return (int)cudaErrorInvalidValue;  // (2^31 words: 8 GB of rows)
+  const int64_t need = (most * p.n_rows + 255) / 256;
+  const unsigned blocks = (unsigned)(need < 2368 ? need : 2368);
   zero_rows_kernel<<<dim3(blocks, (unsigned)p.n_arrays), 256, 0, st>>>(p);
   return (int)cudaGetLastError();
 }
