@@ -35,8 +35,9 @@
 //     instructions instead of ~30;
 //   * colours are staged with the geometry instead of being re-read from
 //     global memory for every (pixel, Gaussian) pair;
-//   * out_observe counts are aggregated per (warp, Gaussian) in shared memory
-//     and flushed with one atomic;
+//   * out_observe counts are kept per lane as a bitmask over the batch and
+//     reduced over the warp once per batch, then flushed with one atomic per
+//     (warp, Gaussian);
 //   * the per-tile statistics (n_render, n_consider, n_contrib) are reduced
 //     in the epilogue instead of three extra kernels.
 // Strip shape: 8x4 pixels overlap ~18% fewer ~12-pixel splats than 16x2.
