@@ -233,14 +233,16 @@ __global__ void __launch_bounds__(256) tile_hist_kernel(BinParams p, unsigned* _
       unsigned wb = 0u;
       if (lane == 0) wb = atomicAdd(n_vis, (unsigned)__popc(vm));
       wb = __shfl_sync(0xffffffffu, wb, 0);
+      bool listed = false;  // only Gaussians with a list slot are counted: the scatter walks the list
       if (vis) {
         const int64_t slot = (int64_t)wb + __popc(vm & ((1u << lane) - 1u));
-        if (slot < vis_cap)
+        listed = slot < vis_cap;
+        if (listed)
           vis_list[slot] = (uint32_t)i;
         else
           atomicOr(err, kErrBinOverflow);
       }
-      warp_expand<RECTS>(p, vis ? i : -1, s_mask, use_smem, [&](bool valid, int64_t, int t) {
+      warp_expand<RECTS>(p, listed ? i : -1, s_mask, use_smem, [&](bool valid, int64_t, int t) {
         const unsigned peers = tile_peers(valid, t);
         if (valid && lane == __ffs(peers) - 1)
           atomicAdd(hist_smem ? &s_hist[t] : &tile_count[t], (unsigned)__popc(peers));
@@ -289,32 +291,42 @@ __device__ __forceinline__ unsigned big_chunks(unsigned c) {
 // same scan over the big tiles' chunk counts -> chunk_start, and
 // big[0] = all chunks, big[1] = the longest big list.
 __global__ void __launch_bounds__(1024) tile_offsets_kernel(const unsigned* __restrict__ tile_count, int n_tiles,
-                                                            uint2* __restrict__ ranges, unsigned* __restrict__ cursor,
+                                                            unsigned cap, uint2* __restrict__ ranges,
+                                                            unsigned* __restrict__ cursor,
                                                             unsigned* __restrict__ chunk_start,
                                                             unsigned* __restrict__ big) {
   __shared__ unsigned s_part[32];
   const int per = (n_tiles + blockDim.x - 1) / blockDim.x;  // consecutive tiles of this thread
   const int t0 = threadIdx.x * per;
-  unsigned sum = 0u, chunks = 0u, longest = 0u;
+  unsigned sum = 0u;
+  for (int k = 0; k < per; ++k)
+    if (t0 + k < n_tiles) sum += tile_count[t0 + k];
+  const unsigned start0 = block_exclusive_scan(sum, s_part);
+  // Ranges are clipped to the `cap` instances the buffers hold: a caller that
+  // sized them from an estimate gets truncated lists (and re-bins), never an
+  // access beyond them.  The scatter drops the instances past the cap.
+  auto clipped = [&](unsigned start, unsigned c) { return min(start + c, cap) - min(start, cap); };
+  unsigned chunks = 0u, longest = 0u, start = start0;
   for (int k = 0; k < per; ++k)
     if (t0 + k < n_tiles) {
-      const unsigned c = tile_count[t0 + k];
-      sum += c;
-      chunks += big_chunks(c);
-      if (big_chunks(c)) longest = max(longest, c);
+      const unsigned c = tile_count[t0 + k], ce = clipped(start, c);
+      chunks += big_chunks(ce);
+      if (big_chunks(ce)) longest = max(longest, ce);
+      start += c;
     }
-  unsigned start = block_exclusive_scan(sum, s_part);
-  unsigned cstart = block_exclusive_scan(chunks, s_part);
+  const unsigned cstart0 = block_exclusive_scan(chunks, s_part);
   if (longest) atomicMax(&big[1], longest);
+  start = start0;
+  unsigned cstart = cstart0;
   for (int k = 0; k < per; ++k) {
     const int t = t0 + k;
     if (t >= n_tiles) break;
-    const unsigned c = tile_count[t];
-    ranges[t] = c ? make_uint2(start, start + c) : make_uint2(0u, 0u);
+    const unsigned c = tile_count[t], ce = clipped(start, c);
+    ranges[t] = ce ? make_uint2(start, start + ce) : make_uint2(0u, 0u);
     cursor[t] = start;
     chunk_start[t] = cstart;
     start += c;
-    cstart += big_chunks(c);
+    cstart += big_chunks(ce);
   }
   if (threadIdx.x == blockDim.x - 1) big[0] = cstart;
 }
@@ -666,12 +678,12 @@ int launch_bin_sort(const BinSortParams& p, cudaStream_t st) {
       1, std::min<int64_t>((p.n_vis + 255) / 256, 4 * (int64_t)sms));
   if (p.b.rects) {
     tile_hist_kernel<true><<<blocks, 256, 0, st>>>(p.b, tile_count, vis_list, misc + 3, p.n_vis, misc + 2);
-    tile_offsets_kernel<<<1, 1024, 0, st>>>(tile_count, n_tiles, p.ranges, cursor, chunk_start, misc);
+    tile_offsets_kernel<<<1, 1024, 0, st>>>(tile_count, n_tiles, (unsigned)p.R, p.ranges, cursor, chunk_start, misc);
     tile_scatter_kernel<true><<<vblocks, 256, 0, st>>>(p.b, vis_list, p.n_vis, misc + 3, cursor, keys, p.R,
                                                         misc + 2);
   } else {
     tile_hist_kernel<false><<<blocks, 256, 0, st>>>(p.b, tile_count, vis_list, misc + 3, p.n_vis, misc + 2);
-    tile_offsets_kernel<<<1, 1024, 0, st>>>(tile_count, n_tiles, p.ranges, cursor, chunk_start, misc);
+    tile_offsets_kernel<<<1, 1024, 0, st>>>(tile_count, n_tiles, (unsigned)p.R, p.ranges, cursor, chunk_start, misc);
     tile_scatter_kernel<false><<<vblocks, 256, 0, st>>>(p.b, vis_list, p.n_vis, misc + 3, cursor, keys, p.R,
                                                          misc + 2);
   }

@@ -516,6 +516,11 @@ def render_count(means2D, radii, compute_locally, H, W, counts, totals):
               _lib.stream_ptr())
 
 
+# per (device, tile count): capacities (instances, visible Gaussians) of the
+# render buffers, 25% above the largest totals seen
+_RENDER_CAPS = {}
+
+
 def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_locally, H, W, counts=None, totals=None,
                    vis_count=None, strip_lists=True, totals_host=None):
     """Binning + blending of one camera.  Returns (color, n_render, n_consider,
@@ -544,8 +549,7 @@ def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_local
         _lib.call("blitz_render_count", P, H, W, ptr(means2D), ptr(radii), ptr(cl), ptr(counts), ptr(totals), st)
         TIMER.end(tok, P=P)
     # Everything whose size does not depend on the totals is allocated (and
-    # out_observe zeroed) before the readback: the GPU idles from the end of
-    # the preprocess until the binning is issued, so that window is kept short.
+    # out_observe zeroed) before the binning is issued.
     ranges = torch.empty((T, 2), dtype=torch.int32, device=dev)
     final_T = torch.empty((H * W,), dtype=torch.float32, device=dev)
     n_contrib = torch.empty((H * W,), dtype=torch.int32, device=dev)
@@ -555,10 +559,7 @@ def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_local
     n_contrib_tile = torch.empty((T,), dtype=torch.int32, device=dev)
     out_observe = torch.zeros((P,), dtype=torch.int32, device=dev)
     strip_counts = torch.empty((T * 8,), dtype=torch.int32, device=dev) if strip_lists else None
-    if totals_host is not None:
-        R, n_vis = int(totals_host[0]), int(totals_host[1])
-        n_list = None
-    else:
+    def read_totals():
         host, host_np = _pinned(dev, 2, torch.int64)
         host_n, host_n_np = _pinned(dev, 1, torch.int32) if vis_count is not None else (None, None)
         pre = PRE_SCRATCH.peek(dev)
@@ -566,24 +567,65 @@ def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_local
         _lib.call("blitz_read_totals", ptr(totals), ptr(vis_count), ptr(pre), host.data_ptr(),
                   host_n.data_ptr() if host_n is not None else None,
                   host_s.data_ptr() if host_s is not None else None, st)
+        return int(host_np[0]), int(host_np[1]), (int(host_n_np[0]) if vis_count is not None else None)
+
+    def issue(R, n_vis):
+        """Binning + blend with buffers for up to R instances and n_vis
+        visible Gaussians (the kernels read the exact totals on the device)."""
+        point_list = torch.empty((max(R, 1),), dtype=torch.int32, device=dev)
+        strip_ids = torch.empty((8 * max(R, 1),), dtype=torch.int32, device=dev) if strip_lists else None
+        strip_pos = torch.empty((8 * max(R, 1),), dtype=torch.int32, device=dev) if strip_lists else None
+        scratch = SCRATCH.get(dev, _lib.load().blitz_render_scratch_bytes(P, n_vis, R, H, W))
+        tok = TIMER.begin("binning")
+        _lib.call("blitz_render_bin", P, n_vis, R, H, W, ptr(means2D), ptr(depths), ptr(radii), ptr(cl), ptr(counts),
+                  ptr(scratch), scratch.numel(), ptr(point_list), ptr(ranges), st)
+        TIMER.end(tok, P=P, R=R, n_vis=n_vis)
+        tok = TIMER.begin("blend_fwd")
+        _lib.call("blitz_render_blend", P, H, W, ptr(means2D), ptr(conic_opacity), ptr(rgb), ptr(bg), ptr(cl),
+                  ptr(point_list), ptr(ranges), ptr(final_T), ptr(n_contrib), ptr(color), ptr(n_render),
+                  ptr(n_consider), ptr(n_contrib_tile), ptr(out_observe), ptr(strip_ids), ptr(strip_pos),
+                  ptr(strip_counts), st)
+        TIMER.end(tok, P=P, R=R, n_vis=n_vis, H=H, W=W,
+                  lazy=lambda: {"pairs": (n_consider.sum(dtype=torch.int64), n_contrib_tile.sum(dtype=torch.int64))})
+        return point_list, strip_ids, strip_pos
+
+    key = (dev.index, T)
+    caps = _RENDER_CAPS.get(key) if totals_host is None else None
+    if totals_host is not None:
+        R, n_vis = int(totals_host[0]), int(totals_host[1])
+        n_list = None
+        point_list, strip_ids, strip_pos = issue(R, n_vis)
+    elif caps is not None:
+        # Issue the binning and blend with buffers sized from earlier views,
+        # then read the totals: the host waits while the GPU already runs
+        # them instead of the GPU waiting for the host.  A view that needs
+        # more is binned and blended again with exact sizes (nothing
+        # downstream has read the outputs yet).
+        R_cap, V_cap = caps[0], min(caps[1], P)
+        # the totals (and the scan status words) are copied before the
+        # binning in stream order; the host waits for that copy only
+        host, host_np = _pinned(dev, 2, torch.int64, "spec")
+        host.copy_(totals.view(-1)[:2], non_blocking=True)
+        host_n, host_n_np = _pinned(dev, 1, torch.int32, "spec") if vis_count is not None else (None, None)
+        if vis_count is not None:
+            host_n.copy_(vis_count.view(-1)[:1], non_blocking=True)
+        status = queue_scan_status(dev)
+        copied = torch.cuda.Event()
+        copied.record()
+        point_list, strip_ids, strip_pos = issue(R_cap, V_cap)
+        copied.synchronize()
+        check_scan_status(status)
         R, n_vis = int(host_np[0]), int(host_np[1])
         n_list = int(host_n_np[0]) if vis_count is not None else None
-
-    point_list = torch.empty((max(R, 1),), dtype=torch.int32, device=dev)
-    strip_ids = torch.empty((8 * max(R, 1),), dtype=torch.int32, device=dev) if strip_lists else None
-    strip_pos = torch.empty((8 * max(R, 1),), dtype=torch.int32, device=dev) if strip_lists else None
-    nbytes = _lib.load().blitz_render_scratch_bytes(P, n_vis, R, H, W)
-    scratch = SCRATCH.get(dev, nbytes)
-    tok = TIMER.begin("binning")
-    _lib.call("blitz_render_bin", P, n_vis, R, H, W, ptr(means2D), ptr(depths), ptr(radii), ptr(cl), ptr(counts),
-              ptr(scratch), scratch.numel(), ptr(point_list), ptr(ranges), st)
-    TIMER.end(tok, P=P, R=R, n_vis=n_vis)
-    tok = TIMER.begin("blend_fwd")
-    _lib.call("blitz_render_blend", P, H, W, ptr(means2D), ptr(conic_opacity), ptr(rgb), ptr(bg), ptr(cl),
-              ptr(point_list), ptr(ranges), ptr(final_T), ptr(n_contrib), ptr(color), ptr(n_render), ptr(n_consider),
-              ptr(n_contrib_tile), ptr(out_observe), ptr(strip_ids), ptr(strip_pos), ptr(strip_counts), st)
-    TIMER.end(tok, P=P, R=R, n_vis=n_vis, H=H, W=W,
-              lazy=lambda: {"pairs": (n_consider.sum(dtype=torch.int64), n_contrib_tile.sum(dtype=torch.int64))})
+        if R > R_cap or n_vis > V_cap:
+            out_observe.zero_()
+            point_list, strip_ids, strip_pos = issue(R, n_vis)
+    else:
+        R, n_vis, n_list = read_totals()
+        point_list, strip_ids, strip_pos = issue(R, n_vis)
+    if totals_host is None:
+        old = caps or (0, 0)
+        _RENDER_CAPS[key] = (max(old[0], (R * 5 + 3) // 4), max(old[1], (n_vis * 5 + 3) // 4))
     state = RenderState(H, W, R, n_vis, point_list, ranges, final_T, n_contrib, n_list, strip_ids, strip_pos,
                         strip_counts)
     return color, n_render, n_consider, n_contrib_tile, out_observe, state

@@ -255,6 +255,11 @@ int blitz_render_forward(int64_t P, int64_t n_vis, int64_t R, int image_height, 
  * The two halves of blitz_render_forward, for callers that schedule or time
  * them separately: binning (point_list, ranges) and blending (everything
  * else).  Same arguments and contracts as blitz_render_forward.
+ * n_vis and R may also be capacities above the totals (the kernels read the
+ * exact counts on the device), so the binning can be issued before the
+ * totals are read back; if the true totals exceed them, the tile lists are
+ * clipped to the R instances the buffers hold -- no access goes beyond them
+ * -- and the caller bins again with the exact totals.
  * blitz_render_blend may also record, for blitz_render_backward, the
  * Gaussians that contributed to each warp strip (8 strips of 8x4 pixels per
  * tile): strip_ids / strip_pos int32 [8*R] (Gaussian id and 0-based tile-list
