@@ -118,11 +118,19 @@ class _DistributedBatch(torch.autograd.Function):
             counts_k = torch.empty((max(m2.shape[0], 1),), dtype=torch.int32, device=dev)
             ops.render_count(m2, radii, cl, H, W, counts_k, totals[i])
             staged.append((k, segs, conic, m2, rgb, depth, radii, cl, counts_k))
-        status = ops.queue_scan_status(dev)
-        tot_host = totals.cpu().tolist() if nm else []
-        if not nm:
-            torch.cuda.current_stream(dev).synchronize()
-        ops.check_scan_status(status)
+        # one camera with known buffer sizes (the usual case at one view per
+        # GPU): render_forward issues its binning before it reads the totals
+        # back (and checks the scan status words); otherwise one readback of
+        # every camera's totals first
+        spec = nm == 1 and ops.render_caps_known(dev, int(rasters[mine[0]].image_height),
+                                                 int(rasters[mine[0]].image_width))
+        tot_host = [None] * nm
+        if not spec:
+            status = ops.queue_scan_status(dev)
+            tot_host = totals.cpu().tolist() if nm else []
+            if not nm:
+                torch.cuda.current_stream(dev).synchronize()
+            ops.check_scan_status(status)
         losses = []
         saved = {}
         for i, (k, segs, conic, m2, rgb, depth, radii, cl, counts_k) in enumerate(staged):
@@ -130,7 +138,7 @@ class _DistributedBatch(torch.autograd.Function):
             H, W = int(rs.image_height), int(rs.image_width)
             color, _, _, _, _, state = ops.render_forward(m2, depth, radii, conic, rgb, rs.bg, cl, H, W,
                                                           counts=counts_k, totals=totals[i],
-                                                          totals_host=tot_host[i])
+                                                          totals_host=tot_host[i], caps_update=True)
             y0t, y1t = strategies[k].row_range(rank)
             y0, y1 = y0t * D.TILE, min(H, y1t * D.TILE)
             band = color[:, y0:y1, :]

@@ -521,8 +521,15 @@ def render_count(means2D, radii, compute_locally, H, W, counts, totals):
 _RENDER_CAPS = {}
 
 
+def render_caps_known(dev, H, W):
+    """Whether render_forward would issue this size's binning before its
+    totals readback (buffer capacities are known from an earlier view)."""
+    gx, gy = grid_dims(H, W)
+    return (dev.index, gx * gy) in _RENDER_CAPS
+
+
 def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_locally, H, W, counts=None, totals=None,
-                   vis_count=None, strip_lists=True, totals_host=None):
+                   vis_count=None, strip_lists=True, totals_host=None, caps_update=False):
     """Binning + blending of one camera.  Returns (color, n_render, n_consider,
     n_contrib_tile, out_observe, state).  ``counts``/``totals`` from
     ``preprocess_forward_raw(want_counts=True)`` skip the count pass;
@@ -530,7 +537,11 @@ def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_local
     ``strip_lists`` records, per 8x4-pixel warp strip, the Gaussians that
     contributed to it (2 x 32 bytes per tile instance of device memory), so
     the backward replays only those.  ``totals_host`` = (R, n_vis) already
-    read back by the caller (with ``counts``): no readback here."""
+    read back by the caller (with ``counts``): no readback here;
+    ``caps_update`` then still records them for later views' capacities.
+    Without ``totals_host``, once a view of this size has been rendered, the
+    binning and blend are issued with capacities before the totals are
+    read back (see blitz_render_bin)."""
     _require_cuda(means2D, depths, radii, conic_opacity, rgb, bg)
     means2D, depths, conic_opacity, rgb, bg = map(_f32c, (means2D, depths, conic_opacity, rgb, bg))
     radii = radii.contiguous()
@@ -623,8 +634,8 @@ def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_local
     else:
         R, n_vis, n_list = read_totals()
         point_list, strip_ids, strip_pos = issue(R, n_vis)
-    if totals_host is None:
-        old = caps or (0, 0)
+    if totals_host is None or caps_update:
+        old = _RENDER_CAPS.get(key, (0, 0))
         _RENDER_CAPS[key] = (max(old[0], (R * 5 + 3) // 4), max(old[1], (n_vis * 5 + 3) // 4))
     state = RenderState(H, W, R, n_vis, point_list, ranges, final_T, n_contrib, n_list, strip_ids, strip_pos,
                         strip_counts)
