@@ -243,12 +243,26 @@ def _band_mask(strategy, rank, dev):
     return m
 
 
+_CAMS = {}
+
+
 def _camera_arrays(rasters):
-    """(viewmatrices [n,16], projmatrices [n,16], campos [n,3]) of the batch."""
+    """(viewmatrices [n,16], projmatrices [n,16], campos [n,3]) of the batch,
+    cached per batch of camera tensors: the key holds the tensors themselves
+    (so their ids cannot be reused while cached) and their version counters
+    (an in-place change of a matrix misses the cache)."""
+    key = tuple((id(t), t._version) for r in rasters for t in (r.viewmatrix, r.projmatrix, r.campos))
+    hit = _CAMS.get(key)
+    if hit is not None:
+        return hit[1]
     views = torch.stack([r.viewmatrix.reshape(16) for r in rasters])
     projs = torch.stack([r.projmatrix.reshape(16) for r in rasters])
     campos = torch.stack([r.campos.reshape(3) for r in rasters])
-    return views.float().contiguous(), projs.float().contiguous(), campos.float().contiguous()
+    out = (views.float().contiguous(), projs.float().contiguous(), campos.float().contiguous())
+    if len(_CAMS) > 256:
+        _CAMS.clear()
+    _CAMS[key] = ([t for r in rasters for t in (r.viewmatrix, r.projmatrix, r.campos)], out)
+    return out
 
 
 def _pinned_table(n_cams, ws):

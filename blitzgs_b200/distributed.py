@@ -28,6 +28,7 @@ gloo on CPU in the tests).
 from dataclasses import dataclass, field
 from types import SimpleNamespace
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -69,14 +70,27 @@ def _group_size():
 
 def division_pos_heuristic(heuristic, tile_num, world_size, right=False):
     """Split the prefix sum of per-tile-row costs into world_size equal parts
-    (workload_division.py:66-82).  Runs on the host copy of the heuristic."""
+    (workload_division.py:66-82).  Runs on the host copy of the heuristic,
+    in numpy with PyTorch's float32 rounding: torch.cumsum of float32 on the
+    CPU accumulates in double and rounds each prefix to float32, which
+    cumsum in float64 followed by one cast reproduces; the share and the
+    thresholds are float32 operations as in torch (a few torch calls cost
+    ~0.1 ms per step, this ~0.01)."""
     assert heuristic.shape[0] == tile_num, "the length of heuristics should be the same as the number of tiles."
-    h = heuristic.detach().to("cpu")
-    prefix = torch.cumsum(h, dim=0)
-    per = prefix[-1] / world_size
-    thresholds = torch.arange(1, world_size, dtype=prefix.dtype) * per
-    idx = torch.searchsorted(prefix, thresholds, right=right)
-    return [0] + idx.tolist() + [tile_num]
+    h = heuristic.detach().to("cpu").numpy() if isinstance(heuristic, torch.Tensor) else np.asarray(heuristic)
+    if h.dtype != np.float32:
+        # other dtypes: the torch formulation itself
+        t = torch.from_numpy(np.ascontiguousarray(h))
+        prefix = torch.cumsum(t, dim=0)
+        per = prefix[-1] / world_size
+        thresholds = torch.arange(1, world_size, dtype=prefix.dtype) * per
+        idx = torch.searchsorted(prefix, thresholds, right=right)
+        return [0] + idx.tolist() + [tile_num]
+    prefix = np.cumsum(h, dtype=np.float64).astype(np.float32)
+    per = np.float32(prefix[-1]) / np.float32(world_size)
+    thresholds = np.arange(1, world_size, dtype=np.float32) * per
+    idx = np.searchsorted(prefix, thresholds, side="right" if right else "left")
+    return [0] + [int(i) for i in idx] + [tile_num]
 
 
 class DivisionStrategyFinal:
@@ -179,7 +193,8 @@ def start_strategy_final(batched_cameras, strategy_history):
             tasks[g].append((idx, 0, n_rows))
             strategies.append(DivisionStrategyFinal(camera, 1, [g], [0, n_rows], [(0, n_rows)]))
         return strategies, tasks
-    catted = torch.cat([strategy_history.accum_heuristic[c.uid].to("cpu") for c in batched_cameras], 0)
+    catted = np.concatenate([strategy_history.accum_heuristic[c.uid].detach().to("cpu").numpy()
+                             for c in batched_cameras])
     pos = division_pos_heuristic(catted, total, ws, right=True)
     coeff = args.border_divpos_coeff
     for i in range(1, len(pos) - 1):

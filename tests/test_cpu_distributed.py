@@ -210,3 +210,29 @@ def test_zorder_shards_partition():
     # spatial locality: shard bounding boxes are much smaller than the scene's
     vol = [(xyz[s].max(0).values - xyz[s].min(0).values).prod().item() for s in sh]
     assert max(vol) < 0.8
+
+
+def test_division_positions_round_like_torch():
+    """The numpy split equals the torch formulation (float32 cumsum
+    accumulated in double, float32 share and thresholds, searchsorted) on
+    random and tied heuristics."""
+    import numpy as np
+    import torch
+    from blitzgs_b200 import distributed as D
+
+    def torch_split(h, ws, right):
+        prefix = torch.cumsum(h, dim=0)
+        per = prefix[-1] / ws
+        th = torch.arange(1, ws, dtype=prefix.dtype) * per
+        return [0] + torch.searchsorted(prefix, th, right=right).tolist() + [h.shape[0]]
+
+    g = np.random.default_rng(3)
+    for trial in range(300):
+        n = int(g.integers(8, 600))
+        ws = int(g.integers(2, 9))
+        h = (g.random(n) * g.choice([1.0, 1e3, 1e-3])).astype(np.float32)
+        if trial % 3 == 0:
+            h[:] = 1.0  # ties on the thresholds
+        t = torch.from_numpy(h)
+        for right in (False, True):
+            assert D.division_pos_heuristic(t, n, ws, right=right) == torch_split(t, ws, right)
