@@ -62,57 +62,80 @@ __global__ void __launch_bounds__(256) loss_fwd_kernel(LossParams p, Win win, do
     s_y[r][q] = yv;
   }
   __syncthreads();
-  // horizontal pass over all 42 input rows, 32 output columns
-  for (int k = tid; k < kIn * kLT; k += blockDim.x) {
-    const int r = k / kLT, q = k % kLT;
-    float a = 0.f, b = 0.f, aa = 0.f, bb = 0.f, ab = 0.f;
+  // horizontal pass over all 42 input rows, 32 output columns; a thread
+  // computes 4 neighbouring outputs of a row from 14 inputs held in
+  // registers (each output sums its 11 taps in the same order as a
+  // one-output loop, so the result is unchanged)
+  for (int k = tid; k < kIn * (kLT / 4); k += blockDim.x) {
+    const int r = k / (kLT / 4), q0 = (k % (kLT / 4)) * 4;
+    float xs[14], ys[14];
 #pragma unroll
-    for (int t = 0; t < 11; ++t) {
-      const float xv = s_x[r][q + t], yv = s_y[r][q + t], w = win.w[t];
-      a += w * xv;
-      b += w * yv;
-      aa += w * (xv * xv);
-      bb += w * (yv * yv);
-      ab += w * (xv * yv);
+    for (int u = 0; u < 14; ++u) {
+      xs[u] = s_x[r][q0 + u];
+      ys[u] = s_y[r][q0 + u];
     }
-    h[0][r][q] = a;
-    h[1][r][q] = b;
-    h[2][r][q] = aa;
-    h[3][r][q] = bb;
-    h[4][r][q] = ab;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float a = 0.f, b = 0.f, aa = 0.f, bb = 0.f, ab = 0.f;
+#pragma unroll
+      for (int t = 0; t < 11; ++t) {
+        const float xv = xs[j + t], yv = ys[j + t], w = win.w[t];
+        a += w * xv;
+        b += w * yv;
+        aa += w * (xv * xv);
+        bb += w * (yv * yv);
+        ab += w * (xv * yv);
+      }
+      h[0][r][q0 + j] = a;
+      h[1][r][q0 + j] = b;
+      h[2][r][q0 + j] = aa;
+      h[3][r][q0 + j] = bb;
+      h[4][r][q0 + j] = ab;
+    }
   }
   __syncthreads();
   double l1 = 0.0, ss = 0.0;
-  for (int k = tid; k < kLT * kLT; k += blockDim.x) {
-    const int r = k / kLT, q = k % kLT;
-    const int gy = y0 + r, gx = x0 + q;
-    if (gy >= p.Hb || gx >= p.W) continue;
-    float mu1 = 0.f, mu2 = 0.f, e11 = 0.f, e22 = 0.f, e12 = 0.f;
+  // vertical pass and SSIM: a thread takes 4 vertically neighbouring outputs
+  // of one column (consecutive threads: consecutive columns)
+  for (int k = tid; k < (kLT / 4) * kLT; k += blockDim.x) {
+    const int r0 = (k / kLT) * 4, q = k % kLT;
+    float m[5][4];
 #pragma unroll
-    for (int t = 0; t < 11; ++t) {
-      const float w = win.w[t];
-      mu1 += w * h[0][r + t][q];
-      mu2 += w * h[1][r + t][q];
-      e11 += w * h[2][r + t][q];
-      e22 += w * h[3][r + t][q];
-      e12 += w * h[4][r + t][q];
+    for (int c5 = 0; c5 < 5; ++c5) {
+      float v[14];
+#pragma unroll
+      for (int u = 0; u < 14; ++u) v[u] = h[c5][r0 + u][q];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float acc = 0.f;
+#pragma unroll
+        for (int t = 0; t < 11; ++t) acc += win.w[t] * v[j + t];
+        m[c5][j] = acc;
+      }
     }
-    const float mu1_sq = mu1 * mu1, mu2_sq = mu2 * mu2, mu12 = mu1 * mu2;
-    const float s11 = e11 - mu1_sq, s22 = e22 - mu2_sq, s12 = e12 - mu12;
-    const float A1 = 2.f * mu12 + kC1, A2 = 2.f * s12 + kC2;
-    const float B1 = mu1_sq + mu2_sq + kC1, B2 = s11 + s22 + kC2;
-    const float D = B1 * B2;
-    const float S = (A1 * A2) / D;
-    const float dmu1 = (2.f * mu2 * (A2 - A1) - S * 2.f * mu1 * (B2 - B1)) / D;
-    const float de11 = -S / B2;
-    const float de12 = 2.f * A1 / D;
-    const float xv = s_x[r + kHalo][q + kHalo], yv = s_y[r + kHalo][q + kHalo];
-    l1 += fabsf(xv - yv);
-    ss += S;
-    float* pp = p.partials + 3 * (c * plane + (int64_t)gy * p.W + gx);
-    pp[0] = dmu1;
-    pp[1] = de11;
-    pp[2] = de12;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int r = r0 + j;
+      const int gy = y0 + r, gx = x0 + q;
+      if (gy >= p.Hb || gx >= p.W) continue;
+      const float mu1 = m[0][j], mu2 = m[1][j], e11 = m[2][j], e22 = m[3][j], e12 = m[4][j];
+      const float mu1_sq = mu1 * mu1, mu2_sq = mu2 * mu2, mu12 = mu1 * mu2;
+      const float s11 = e11 - mu1_sq, s22 = e22 - mu2_sq, s12 = e12 - mu12;
+      const float A1 = 2.f * mu12 + kC1, A2 = 2.f * s12 + kC2;
+      const float B1 = mu1_sq + mu2_sq + kC1, B2 = s11 + s22 + kC2;
+      const float D = B1 * B2;
+      const float S = (A1 * A2) / D;
+      const float dmu1 = (2.f * mu2 * (A2 - A1) - S * 2.f * mu1 * (B2 - B1)) / D;
+      const float de11 = -S / B2;
+      const float de12 = 2.f * A1 / D;
+      const float xv = s_x[r + kHalo][q + kHalo], yv = s_y[r + kHalo][q + kHalo];
+      l1 += fabsf(xv - yv);
+      ss += S;
+      float* pp = p.partials + 3 * (c * plane + (int64_t)gy * p.W + gx);
+      pp[0] = dmu1;
+      pp[1] = de11;
+      pp[2] = de12;
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -158,40 +181,54 @@ __global__ void __launch_bounds__(256) loss_bwd_kernel(LossBwdParams bp, Win win
     s_p[2][r][q] = d;
   }
   __syncthreads();
-  for (int k = tid; k < kIn * kLT; k += blockDim.x) {
-    const int r = k / kLT, q = k % kLT;
-    float a = 0.f, b = 0.f, d = 0.f;
+  // horizontal pass: 4 neighbouring outputs of a row per thread, from 14
+  // inputs in registers (per output the same tap order as a one-output loop)
+  for (int k = tid; k < kIn * (kLT / 4); k += blockDim.x) {
+    const int r = k / (kLT / 4), q0 = (k % (kLT / 4)) * 4;
 #pragma unroll
-    for (int t = 0; t < 11; ++t) {
-      const float w = win.w[t];
-      a += w * s_p[0][r][q + t];
-      b += w * s_p[1][r][q + t];
-      d += w * s_p[2][r][q + t];
+    for (int m = 0; m < 3; ++m) {
+      float v[14];
+#pragma unroll
+      for (int u = 0; u < 14; ++u) v[u] = s_p[m][r][q0 + u];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float acc = 0.f;
+#pragma unroll
+        for (int t = 0; t < 11; ++t) acc += win.w[t] * v[j + t];
+        h[m][r][q0 + j] = acc;
+      }
     }
-    h[0][r][q] = a;
-    h[1][r][q] = b;
-    h[2][r][q] = d;
   }
   __syncthreads();
   const float s_l1 = bp.scale[0], s_ss = bp.scale[1];
-  for (int k = tid; k < kLT * kLT; k += blockDim.x) {
-    const int r = k / kLT, q = k % kLT;
-    const int gy = y0 + r, gx = x0 + q;
-    if (gy >= p.Hb || gx >= p.W) continue;
-    float q1 = 0.f, q2 = 0.f, q3 = 0.f;
+  // vertical pass: 4 vertically neighbouring outputs of a column per thread
+  for (int k = tid; k < (kLT / 4) * kLT; k += blockDim.x) {
+    const int r0 = (k / kLT) * 4, q = k % kLT;
+    float qs[3][4];
 #pragma unroll
-    for (int t = 0; t < 11; ++t) {
-      const float w = win.w[t];
-      q1 += w * h[0][r + t][q];
-      q2 += w * h[1][r + t][q];
-      q3 += w * h[2][r + t][q];
+    for (int m = 0; m < 3; ++m) {
+      float v[14];
+#pragma unroll
+      for (int u = 0; u < 14; ++u) v[u] = h[m][r0 + u][q];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float acc = 0.f;
+#pragma unroll
+        for (int t = 0; t < 11; ++t) acc += win.w[t] * v[j + t];
+        qs[m][j] = acc;
+      }
     }
-    const int64_t idx = c * plane + (int64_t)gy * p.W + gx;
-    const float xv = p.img[idx];
-    const float yv = load_gt(p, idx);
-    const float diff = xv - yv;
-    const float sg = diff > 0.f ? 1.f : (diff < 0.f ? -1.f : 0.f);
-    bp.dL_dimg[idx] = s_l1 * sg + s_ss * (q1 + 2.f * xv * q2 + yv * q3);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int gy = y0 + r0 + j, gx = x0 + q;
+      if (gy >= p.Hb || gx >= p.W) continue;
+      const int64_t idx = c * plane + (int64_t)gy * p.W + gx;
+      const float xv = p.img[idx];
+      const float yv = load_gt(p, idx);
+      const float diff = xv - yv;
+      const float sg = diff > 0.f ? 1.f : (diff < 0.f ? -1.f : 0.f);
+      bp.dL_dimg[idx] = s_l1 * sg + s_ss * (qs[0][j] + 2.f * xv * qs[1][j] + yv * qs[2][j]);
+    }
   }
 }
 
