@@ -49,7 +49,7 @@
 //
 // Backward follows the reference back-to-front replay (backward.cu:324-530)
 // but replaces the 11 global atomics per (pixel, Gaussian) pair with a
-// warp-level transpose reduction (16 shuffles for 11 values) and one
+// warp-level transpose reduction (13 shuffles for the 11 values) and one
 // 11-lane RED instruction per (warp, Gaussian) -- or, when at most
 // kDirectLanes pixels of the warp contribute, their own REDs.  T is
 // recovered with one reciprocal of (1 - alpha) (fast division, 1 - alpha in
@@ -261,11 +261,11 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
       ++n2l;
       act_bits |= 1u << j;
       const float4 cth = s_c[warp][j];
-      C0 += cth.x * alpha * T;
-      C1 += cth.y * alpha * T;
-      C2 += cth.z * alpha * T;
+      const float w = alpha * T;  // blending weight
+      C0 += cth.x * w;
+      C1 += cth.y * w;
+      C2 += cth.z * w;
       if (STATS) {
-        const float w = alpha * T;
         if (w_max < w) {
           w_max = w;
           id_max = s_id[warp][j];
@@ -337,48 +337,65 @@ __global__ void __launch_bounds__(kTilePix) blend_fwd_kernel(BlendFwdParams p) {
 // record: [m.x m.y 0 0 | a.x a.y 0 0 | c00 c01 c11 op | r g b 0].
 __constant__ int kSlot[11] = {0, 1, 4, 5, 8, 9, 10, 11, 12, 13, 14};
 
-// Sum 16 per-lane values over the warp; returns in every lane the total of
-// value index (lane >> 1).  16 shuffles instead of 80.
-__device__ __forceinline__ float warp_transpose_reduce16(float v[16]) {
+// Sum 11 per-lane values over the warp in 13 shuffles.  Each step halves the
+// values a lane keeps, swapping half with the partner lane (an odd one out is
+// summed by both partners), so lane L ends with the warp total of value
+// reduce11_value(L).  Step xor 16: values 0-4 | 5-9, value 10 by both;
+// xor 8: the first three of the five (with 10) | the last two and 10;
+// xor 4: first | second, the third by both; xor 2: the pair | the third;
+// xor 1: both.
+__device__ __forceinline__ float warp_transpose_reduce11(const float v[11]) {
   const int lane = threadIdx.x & 31;
-  float a[8];
+  float a[6];
   {
     const bool b = lane & 16;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float send = b ? v[i] : v[8 + i];
-      const float keep = b ? v[8 + i] : v[i];
+    for (int i = 0; i < 5; ++i) {
+      const float send = b ? v[i] : v[5 + i];
+      const float keep = b ? v[5 + i] : v[i];
       a[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
     }
+    a[5] = v[10] + __shfl_xor_sync(0xffffffffu, v[10], 16);
   }
-  float c[4];
+  float c[3];
   {
     const bool b = lane & 8;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float send = b ? a[i] : a[4 + i];
-      const float keep = b ? a[4 + i] : a[i];
+    for (int i = 0; i < 3; ++i) {
+      const float send = b ? a[i] : a[3 + i];
+      const float keep = b ? a[3 + i] : a[i];
       c[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
     }
   }
-  float e[2];
+  float e0, e1;
   {
     const bool b = lane & 4;
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const float send = b ? c[i] : c[2 + i];
-      const float keep = b ? c[2 + i] : c[i];
-      e[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-    }
+    const float send = b ? c[0] : c[1];
+    const float keep = b ? c[1] : c[0];
+    e0 = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    e1 = c[2] + __shfl_xor_sync(0xffffffffu, c[2], 4);
   }
   float g;
   {
     const bool b = lane & 2;
-    const float send = b ? e[0] : e[1];
-    const float keep = b ? e[1] : e[0];
+    const float send = b ? e0 : e1;
+    const float keep = b ? e1 : e0;
     g = keep + __shfl_xor_sync(0xffffffffu, send, 2);
   }
   return g + __shfl_xor_sync(0xffffffffu, g, 1);
+}
+
+// The value whose total lane L holds after warp_transpose_reduce11, or -1
+// where another lane holds the same total (one writer per value).
+__device__ __forceinline__ int reduce11_value(int lane) {
+  if (lane & 1) return -1;
+  const int half = 5 * ((lane >> 4) & 1), hi = (lane >> 3) & 1, odd = (lane >> 2) & 1;
+  if (lane & 2) {
+    if (odd) return -1;
+    if (hi) return half ? -1 : 10;
+    return half + 2;
+  }
+  return half + 3 * hi + odd;
 }
 
 // Backward, one warp per CTA: CTA tile * kStrips + s replays strip s of the
@@ -427,11 +444,27 @@ __device__ __forceinline__ void blend_bwd_strip(const BlendBwdParams& p, int gst
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) n_eff = max(n_eff, __shfl_xor_sync(0xffffffffu, n_eff, o));
 
+  // The pair loop sums the gradient values without their constant factors;
+  // each total is scaled once: d(pixel)/d(ndc) = W/2, H/2 and the signs of
+  // the mean gradients, -1/2 of the conic gradients.
   const float ddelx_dx = 0.5 * p.W;
   const float ddely_dy = 0.5 * p.H;
-  float accum[3] = {0.f, 0.f, 0.f};
+  const float kScale[11] = {-ddelx_dx, -ddely_dy, ddelx_dx, ddely_dy, -0.5f, -0.5f, -0.5f, 1.f, 1.f, 1.f, 1.f};
+  // record slot and scale of the total this lane writes after the warp
+  // reduction (slot -1: none)
+  const int red_value = reduce11_value(lane);
+  const int red_slot = red_value >= 0 ? kSlot[red_value] : -1;
+  float red_scale = 1.f;
+#pragma unroll
+  for (int m = 0; m < 11; ++m) red_scale = red_value == m ? kScale[m] : red_scale;
+  // The reference keeps the colour accumulated behind the current Gaussian
+  // per channel and forms sum_ch (colour - accum) * dL/dpix; only the dot
+  // product with dL/dpix is used, so it is carried as one scalar
+  // (acc_d = sum_ch accum_ch * dL/dpix_ch, same linear recurrence).
+  float acc_d = 0.f;
   float last_alpha = 0.f;
-  float last_color[3] = {0.f, 0.f, 0.f};
+  float last_cd = 0.f;
+  const float neg_bg = -T_final * bg_dot;  // background term of dL/dalpha, times 1/(1 - alpha)
 
   // software pipeline: list entries two batches ahead, Gaussian data one
   // batch ahead.  Walk mode: entries of the tile list from the strip's
@@ -499,7 +532,7 @@ __device__ __forceinline__ void blend_bwd_strip(const BlendBwdParams& p, int gst
     for (int j = 0; j < kept; ++j) {
       const float4 gb = s_b[j];
       const int pos = __float_as_int(gb.w);
-      float g[16];
+      float g[11];
       bool contrib = false;
       if (pos < last_contributor) {
         const float4 ga = s_a[j];
@@ -515,31 +548,25 @@ __device__ __forceinline__ void blend_bwd_strip(const BlendBwdParams& p, int gst
             const float inv1ma = __fdividef(1.0f, 1.f - alpha);  // 1 - alpha in [0.01, 1)
             T = T * inv1ma;
             const float dchannel_dcolor = alpha * T;
-            float dL_dalpha = 0.0f;
-            const float c[3] = {cth.x, cth.y, cth.z};
-#pragma unroll
-            for (int ch = 0; ch < 3; ++ch) {
-              accum[ch] = last_alpha * last_color[ch] + (1.f - last_alpha) * accum[ch];
-              last_color[ch] = c[ch];
-              dL_dalpha += (c[ch] - accum[ch]) * dpx[ch];
-              g[11 + ch] = dchannel_dcolor * dpx[ch];
-            }
-            dL_dalpha *= T;
+            const float cd = cth.x * dpx[0] + cth.y * dpx[1] + cth.z * dpx[2];
+            acc_d = fmaf(last_alpha, last_cd - acc_d, acc_d);
             last_alpha = alpha;
-            dL_dalpha += (-T_final * inv1ma) * bg_dot;
+            last_cd = cd;
+            const float dL_dalpha = (cd - acc_d) * T + neg_bg * inv1ma;
             const float dL_dG = con_o.w * dL_dalpha;
             const float gdx = G * d.x;
             const float gdy = G * d.y;
-            const float dG_ddelx = -gdx * con_o.x - gdy * con_o.y;
-            const float dG_ddely = -gdy * con_o.z - gdx * con_o.y;
-            g[0] = dL_dG * dG_ddelx * ddelx_dx;
-            g[1] = dL_dG * dG_ddely * ddely_dy;
+            g[0] = dL_dG * (gdx * con_o.x + gdy * con_o.y);  // x -W/2
+            g[1] = dL_dG * (gdy * con_o.z + gdx * con_o.y);  // x -H/2
             g[2] = fabsf(g[0]);
             g[3] = fabsf(g[1]);
-            g[4] = -0.5f * gdx * d.x * dL_dG;
-            g[5] = -0.5f * gdx * d.y * dL_dG;
-            g[6] = -0.5f * gdy * d.y * dL_dG;
+            const float gdx_dG = gdx * dL_dG;
+            g[4] = gdx_dG * d.x;  // x -1/2
+            g[5] = gdx_dG * d.y;
+            g[6] = gdy * dL_dG * d.y;
             g[7] = G * dL_dalpha;
+#pragma unroll
+            for (int ch = 0; ch < 3; ++ch) g[8 + ch] = dchannel_dcolor * dpx[ch];
           }
         }
       }
@@ -550,34 +577,18 @@ __device__ __forceinline__ void blend_bwd_strip(const BlendBwdParams& p, int gst
         // than the warp-wide transpose reduction
         if (contrib) {
           float* dst = p.grad_accum + 16 * (int64_t)s_id[j];
-          atomicAdd(dst + 0, g[0]);
-          atomicAdd(dst + 1, g[1]);
-          atomicAdd(dst + 4, g[2]);
-          atomicAdd(dst + 5, g[3]);
-          atomicAdd(dst + 8, g[4]);
-          atomicAdd(dst + 9, g[5]);
-          atomicAdd(dst + 10, g[6]);
-          atomicAdd(dst + 11, g[7]);
-          atomicAdd(dst + 12, g[11]);
-          atomicAdd(dst + 13, g[12]);
-          atomicAdd(dst + 14, g[13]);
+#pragma unroll
+          for (int m = 0; m < 11; ++m) atomicAdd(dst + kSlot[m], g[m] * kScale[m]);
         }
         continue;
       }
       if (!contrib) {
 #pragma unroll
-        for (int m = 0; m < 14; ++m) g[m] = 0.f;
+        for (int m = 0; m < 11; ++m) g[m] = 0.f;
       }
-      // value order for the reduction: m.x m.y a.x a.y c00 c01 c11 op r g b
-      float v[16];
-      v[0] = g[0]; v[1] = g[1]; v[2] = g[2]; v[3] = g[3];
-      v[4] = g[4]; v[5] = g[5]; v[6] = g[6]; v[7] = g[7];
-      v[8] = g[11]; v[9] = g[12]; v[10] = g[13];
-      v[11] = v[12] = v[13] = v[14] = v[15] = 0.f;
-      const float tot = warp_transpose_reduce16(v);
-      const int m = lane >> 1;
-      if ((lane & 1) == 0 && m < 11 && tot != 0.f)
-        atomicAdd(p.grad_accum + 16 * (int64_t)s_id[j] + kSlot[m], tot);
+      // value order for the reduction: m.x m.y |m.x| |m.y| c00 c01 c11 op r g b
+      const float tot = warp_transpose_reduce11(g) * red_scale;
+      if (red_slot >= 0 && tot != 0.f) atomicAdd(p.grad_accum + 16 * (int64_t)s_id[j] + red_slot, tot);
     }
   }
 }
@@ -586,7 +597,7 @@ __device__ __forceinline__ void blend_bwd_strip(const BlendBwdParams& p, int gst
 // one-warp CTAs looping over the strips, with static or ticketed strip
 // assignment, measured 45-55% slower on the city workload.)
 template <bool LISTS>
-__global__ void __launch_bounds__(32, 28) blend_bwd_kernel(BlendBwdParams p, int n_strips) {
+__global__ void __launch_bounds__(32, 32) blend_bwd_kernel(BlendBwdParams p, int n_strips) {
   __shared__ float4 s_a[32];
   __shared__ float4 s_b[32];
   __shared__ float4 s_c[32];

@@ -25,6 +25,7 @@ namespace {
 constexpr int kLT = 32;              // output tile edge
 constexpr int kHalo = 5;             // window radius
 constexpr int kIn = kLT + 2 * kHalo; // 42
+constexpr int kLossThreads = 256;
 constexpr float kC1 = 0.01f * 0.01f;
 constexpr float kC2 = 0.03f * 0.03f;
 
@@ -37,7 +38,7 @@ __device__ __forceinline__ float load_gt(const LossParams& p, int64_t idx) {
   return p.gt_f32[idx];
 }
 
-__global__ void __launch_bounds__(256) loss_fwd_kernel(LossParams p, Win win, double* sums) {
+__global__ void __launch_bounds__(kLossThreads) loss_fwd_kernel(LossParams p, Win win, double* sums) {
   __shared__ float s_x[kIn][kIn + 1];
   __shared__ float s_y[kIn][kIn + 1];
   __shared__ float h[5][kIn][kLT + 1];
@@ -49,7 +50,7 @@ __global__ void __launch_bounds__(256) loss_fwd_kernel(LossParams p, Win win, do
   const float* img = p.img + c * plane;
   const int tid = threadIdx.x;
 
-  for (int k = tid; k < kIn * kIn; k += blockDim.x) {
+  for (int k = tid; k < kIn * kIn; k += kLossThreads) {
     const int r = k / kIn, q = k % kIn;
     const int gy = y0 - kHalo + r, gx = x0 - kHalo + q;
     float xv = 0.f, yv = 0.f;
@@ -66,7 +67,7 @@ __global__ void __launch_bounds__(256) loss_fwd_kernel(LossParams p, Win win, do
   // computes 4 neighbouring outputs of a row from 14 inputs held in
   // registers (each output sums its 11 taps in the same order as a
   // one-output loop, so the result is unchanged)
-  for (int k = tid; k < kIn * (kLT / 4); k += blockDim.x) {
+  for (int k = tid; k < kIn * (kLT / 4); k += kLossThreads) {
     const int r = k / (kLT / 4), q0 = (k % (kLT / 4)) * 4;
     float xs[14], ys[14];
 #pragma unroll
@@ -97,7 +98,7 @@ __global__ void __launch_bounds__(256) loss_fwd_kernel(LossParams p, Win win, do
   double l1 = 0.0, ss = 0.0;
   // vertical pass and SSIM: a thread takes 4 vertically neighbouring outputs
   // of one column (consecutive threads: consecutive columns)
-  for (int k = tid; k < (kLT / 4) * kLT; k += blockDim.x) {
+  for (int k = tid; k < (kLT / 4) * kLT; k += kLossThreads) {
     const int r0 = (k / kLT) * 4, q = k % kLT;
     float m[5][4];
 #pragma unroll
@@ -123,11 +124,13 @@ __global__ void __launch_bounds__(256) loss_fwd_kernel(LossParams p, Win win, do
       const float s11 = e11 - mu1_sq, s22 = e22 - mu2_sq, s12 = e12 - mu12;
       const float A1 = 2.f * mu12 + kC1, A2 = 2.f * s12 + kC2;
       const float B1 = mu1_sq + mu2_sq + kC1, B2 = s11 + s22 + kC2;
-      const float D = B1 * B2;
-      const float S = (A1 * A2) / D;
-      const float dmu1 = (2.f * mu2 * (A2 - A1) - S * 2.f * mu1 * (B2 - B1)) / D;
-      const float de11 = -S / B2;
-      const float de12 = 2.f * A1 / D;
+      // one rounded reciprocal of D = B1 B2 serves the four quotients
+      // (1 / B2 = B1 / D)
+      const float inv_D = __frcp_rn(B1 * B2);
+      const float S = (A1 * A2) * inv_D;
+      const float dmu1 = (2.f * mu2 * (A2 - A1) - S * 2.f * mu1 * (B2 - B1)) * inv_D;
+      const float de11 = -S * (B1 * inv_D);
+      const float de12 = 2.f * A1 * inv_D;
       const float xv = s_x[r + kHalo][q + kHalo], yv = s_y[r + kHalo][q + kHalo];
       l1 += fabsf(xv - yv);
       ss += S;
@@ -149,7 +152,7 @@ __global__ void __launch_bounds__(256) loss_fwd_kernel(LossParams p, Win win, do
   __syncthreads();
   if (tid == 0) {
     double a = 0.0, b = 0.0;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+    for (int w = 0; w < kLossThreads / 32; ++w) {
       a += s_red[0][w];
       b += s_red[1][w];
     }
@@ -158,7 +161,7 @@ __global__ void __launch_bounds__(256) loss_fwd_kernel(LossParams p, Win win, do
   }
 }
 
-__global__ void __launch_bounds__(256) loss_bwd_kernel(LossBwdParams bp, Win win) {
+__global__ void __launch_bounds__(kLossThreads) loss_bwd_kernel(LossBwdParams bp, Win win) {
   const LossParams& p = bp.f;
   __shared__ float s_p[3][kIn][kIn + 1];
   __shared__ float h[3][kLT + 2 * kHalo][kLT + 1];
@@ -166,7 +169,7 @@ __global__ void __launch_bounds__(256) loss_bwd_kernel(LossBwdParams bp, Win win
   const int x0 = blockIdx.x * kLT, y0 = blockIdx.y * kLT;
   const int64_t plane = (int64_t)p.Hb * p.W;
   const int tid = threadIdx.x;
-  for (int k = tid; k < kIn * kIn; k += blockDim.x) {
+  for (int k = tid; k < kIn * kIn; k += kLossThreads) {
     const int r = k / kIn, q = k % kIn;
     const int gy = y0 - kHalo + r, gx = x0 - kHalo + q;
     float a = 0.f, b = 0.f, d = 0.f;
@@ -183,7 +186,7 @@ __global__ void __launch_bounds__(256) loss_bwd_kernel(LossBwdParams bp, Win win
   __syncthreads();
   // horizontal pass: 4 neighbouring outputs of a row per thread, from 14
   // inputs in registers (per output the same tap order as a one-output loop)
-  for (int k = tid; k < kIn * (kLT / 4); k += blockDim.x) {
+  for (int k = tid; k < kIn * (kLT / 4); k += kLossThreads) {
     const int r = k / (kLT / 4), q0 = (k % (kLT / 4)) * 4;
 #pragma unroll
     for (int m = 0; m < 3; ++m) {
@@ -202,7 +205,7 @@ __global__ void __launch_bounds__(256) loss_bwd_kernel(LossBwdParams bp, Win win
   __syncthreads();
   const float s_l1 = bp.scale[0], s_ss = bp.scale[1];
   // vertical pass: 4 vertically neighbouring outputs of a column per thread
-  for (int k = tid; k < (kLT / 4) * kLT; k += blockDim.x) {
+  for (int k = tid; k < (kLT / 4) * kLT; k += kLossThreads) {
     const int r0 = (k / kLT) * 4, q = k % kLT;
     float qs[3][4];
 #pragma unroll
@@ -296,7 +299,7 @@ int launch_loss_fwd(const LossParams& p, const float* window11, double* sums, cu
   Win w;
   for (int i = 0; i < 11; ++i) w.w[i] = window11[i];
   dim3 grid((p.W + kLT - 1) / kLT, (p.Hb + kLT - 1) / kLT, p.C);
-  loss_fwd_kernel<<<grid, 256, 0, st>>>(p, w, sums);
+  loss_fwd_kernel<<<grid, kLossThreads, 0, st>>>(p, w, sums);
   return (int)cudaGetLastError();
 }
 
@@ -305,7 +308,7 @@ int launch_loss_bwd(const LossBwdParams& p, const float* window11, cudaStream_t 
   Win w;
   for (int i = 0; i < 11; ++i) w.w[i] = window11[i];
   dim3 grid((p.f.W + kLT - 1) / kLT, (p.f.Hb + kLT - 1) / kLT, p.f.C);
-  loss_bwd_kernel<<<grid, 256, 0, st>>>(p, w);
+  loss_bwd_kernel<<<grid, kLossThreads, 0, st>>>(p, w);
   return (int)cudaGetLastError();
 }
 
