@@ -45,7 +45,9 @@
 // a tile-wide staging round shared by the 8 warps (23% slower forward, 35%
 // slower backward than 8x4 strips); two pixels per
 // thread (fewer instructions, but the occupancy loss cost more), a per-warp
-// box test inside the pair loop, and a guarded __expf in the backward.
+// box test inside the pair loop, a guarded __expf in the backward, and a
+// forward register cap for five CTAs per SM (48 registers, with small
+// spills: 2-4% slower than four CTAs at 61).
 //
 // Backward follows the reference back-to-front replay (backward.cu:324-530)
 // but replaces the 11 global atomics per (pixel, Gaussian) pair with a
