@@ -7,7 +7,10 @@ global id, so its per-tile Gaussian lists, tile ranges, per-pixel
 contributor counts and image are bit-identical to the single-GPU render of
 the same band.  Gradients are gathered by global Gaussian id and compared
 with the single-GPU result of the same band layout (tolerance: 1e-4
-relative, normwise, per parameter tensor)."""
+relative, normwise, per parameter tensor).  With densification statistics
+(``batch_loss(densify=...)``) and every camera rendered whole by one rank,
+the gathered max_radii2D and denom equal those of the single-GPU step
+exactly and the accumulated viewspace-gradient norms agree within 1e-4."""
 import os
 import socket
 
@@ -60,7 +63,24 @@ def _single_gpu_reference(sc, cam_ids, bands, dev):
     return float(total.item()), [p.grad.detach().cpu() for p in model]
 
 
-def _worker(rank, port, cam_ids, q):
+def _single_gpu_densify(sc, cam_ids, dev):
+    """Densification statistics of the single-GPU step over whole views."""
+    from blitzgs_b200 import densify as DZ, scene as S, step as ST
+    model = [t.to(dev).requires_grad_(True) for t in (sc.xyz, sc.scaling, sc.rotation, sc.opacity,
+                                                      sc.features_dc, sc.features_rest)]
+    stats = DZ.DensificationStats(sc.P, dev)
+    total = 0
+    for c in cam_ids:
+        cam = sc.cameras[c].to(dev)
+        gt = S.target_image(c, cam.image_height, cam.image_width).to(dev)
+        rs = S.raster_settings(cam, device=dev)
+        loss, *_ = ST.view_loss(model, rs, gt, scale_reg_weight=0.0, densify=stats)
+        total = total + loss
+    total.backward()
+    return [t.detach().cpu() for t in (stats.max_radii2D, stats.xyz_gradient_accum, stats.denom)]
+
+
+def _worker(rank, port, cam_ids, q, densify=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import datetime
     import torch.distributed as dist
@@ -69,7 +89,7 @@ def _worker(rank, port, cam_ids, q):
     dist.init_process_group("nccl", rank=rank, world_size=WS, timeout=datetime.timedelta(seconds=120),
                             device_id=dev)
     try:
-        from blitzgs_b200 import distributed as D, dist_step as DS, ops, scene as S
+        from blitzgs_b200 import densify as DZ, distributed as D, dist_step as DS, ops, scene as S
         captured = []
         real_render = ops.render_forward
 
@@ -99,7 +119,8 @@ def _worker(rank, port, cam_ids, q):
                 continue
             g = S.target_image(c, H, W).to(dev)
             gts.append(g[:, rr[0] * 16: min(H, rr[1] * 16)])
-        loss = DS.batch_loss(model, rasters, gts, strategies, reg_w=0.0)
+        stats = DZ.DensificationStats(len(shard), dev) if densify else None
+        loss = DS.batch_loss(model, rasters, gts, strategies, reg_w=0.0, densify=stats)
         loss.backward()
         lt = loss.detach().reshape(1)
         dist.all_reduce(lt)
@@ -109,27 +130,33 @@ def _worker(rank, port, cam_ids, q):
             full[shard.to(dev)] = p.grad
             dist.all_reduce(full)
             grads.append(full.cpu())
+        dz = None
+        if stats is not None:
+            # shards are disjoint id ranges: the sum of the zero-padded rows is the whole
+            dz = []
+            for t in (stats.max_radii2D, stats.xyz_gradient_accum, stats.denom):
+                full = torch.zeros((sc.P,) + tuple(t.shape[1:]), device=dev)
+                full[shard.to(dev)] = t
+                dist.all_reduce(full)
+                dz.append(full.cpu())
         bands = [[tuple(st.division_pos[i:i + 2]) for i in range(st.world_size)] for st in strategies]
         mine = [(k, strategies[k].row_range(rank)) for k in range(len(cam_ids)) if rank in strategies[k].gpu_ids]
-        q.put(("renders", rank, list(zip(mine, captured)), None))
+        q.put(("renders", rank, list(zip(mine, captured)), None, None))
         if rank == 0:
-            q.put(("ok", float(lt.item()), grads, bands))
+            q.put(("ok", float(lt.item()), grads, bands, dz))
         dist.barrier()
     except BaseException as ex:
-        q.put(("err", repr(ex), None, None))
+        q.put(("err", repr(ex), None, None, None))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("cam_ids", [[0, 1], [0]], ids=["whole-views", "split-view"])
-def test_two_rank_step_matches_single_gpu(cam_ids):
-    if torch.cuda.device_count() < WS:
-        pytest.skip("needs 2 GPUs")
+def _run(cam_ids, densify=False):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, port, cam_ids, q)) for r in range(WS)]
+    procs = [ctx.Process(target=_worker, args=(r, port, cam_ids, q, densify)) for r in range(WS)]
     for p in procs:
         p.start()
     renders, result = [], None
@@ -144,8 +171,15 @@ def test_two_rank_step_matches_single_gpu(cam_ids):
             result = item
     for p in procs:
         p.join(timeout=120)
-    status, loss, grads, bands = result
-    assert status == "ok", loss
+    assert result[0] == "ok", result[1]
+    return renders, result
+
+
+@pytest.mark.parametrize("cam_ids", [[0, 1], [0]], ids=["whole-views", "split-view"])
+def test_two_rank_step_matches_single_gpu(cam_ids):
+    if torch.cuda.device_count() < WS:
+        pytest.skip("needs 2 GPUs")
+    renders, (_, loss, grads, bands, _) = _run(cam_ids)
     sc = _scene()
     _check_renders_bit_identical(sc, cam_ids, renders)
     ref_loss, ref_grads = _single_gpu_reference(sc, cam_ids, bands, torch.device("cuda", 0))
@@ -153,6 +187,27 @@ def test_two_rank_step_matches_single_gpu(cam_ids):
     from tests.helpers import assert_grad_close
     for n, a, b in zip(["xyz", "scaling", "rotation", "opacity", "dc", "rest"], grads, ref_grads):
         assert_grad_close(a, b, 1e-4, n)
+
+
+def test_two_rank_densification_stats_match_single_gpu():
+    """batch_loss(densify=...) on two ranks: every camera of the batch is
+    rendered whole by one rank, so each owner's statistics (max radius, the
+    norm of the viewspace gradient summed over the receivers, the count) are
+    those of the single-GPU step over the same whole views."""
+    if torch.cuda.device_count() < WS:
+        pytest.skip("needs 2 GPUs")
+    cam_ids = [0, 1]
+    _, (_, _, _, bands, dz) = _run(cam_ids, densify=True)
+    sc = _scene()
+    gy = (sc.cameras[0].image_height + 15) // 16
+    for k, b in enumerate(bands):
+        nonempty = [(r0, r1) for r0, r1 in b if r1 > r0]
+        assert nonempty == [(0, gy)], f"camera {k} is not rendered whole by one rank: {b}"
+    ref = _single_gpu_densify(sc, cam_ids, torch.device("cuda", 0))
+    assert torch.equal(dz[0], ref[0]), "max_radii2D differs"
+    assert torch.equal(dz[2], ref[2]), "denom differs"
+    from tests.helpers import assert_grad_close
+    assert_grad_close(dz[1], ref[1], 1e-4, "xyz_gradient_accum")
 
 
 def _check_renders_bit_identical(sc, cam_ids, renders):
