@@ -19,9 +19,11 @@
 //     BLITZ_NOALLOC_SCRATCH_BYTES (64 MiB); larger requests are rejected with
 //     BLITZ_ESCRATCH and a message, before anything is launched;
 //   * the array is shared by every call in the process on a given device and
-//     keeps whatever the last call left in it; no part of it has to start at
-//     zero (each call writes every buffer in it before reading it, and the
-//     sort library initialises its own temporaries), so nothing is cleared;
+//     keeps whatever the last call left in it; the parts that must start at
+//     zero (the per-tile counters and the small block of totals and error
+//     word) are cleared by the binning itself on the call's stream, with
+//     cudaMemsetAsync, before its first kernel; every other buffer in it is
+//     written before it is read;
 //   * two calls whose work overlaps on the GPU (different streams, or host
 //     threads without ordering) race on the array: order them;
 //   * the first call on each device looks up the array's device address
