@@ -24,7 +24,9 @@ def _free_port():
 
 
 N_CAMS = 3
-SHARD = [40, 47, 33]  # Gaussians per rank (contiguous z-order shards: global id = shard offset + local index)
+# Gaussians per rank (contiguous z-order shards: global id = shard offset +
+# local index); rank 3 holds an empty shard
+SHARD = [40, 47, 33, 0, 29, 51, 18, 36]
 
 
 def _rank_data(rank, ws):
@@ -46,7 +48,7 @@ def _rank_data(rank, ws):
         rec[:, 3:] = torch.rand(L, 9, generator=g)
         mask = torch.zeros(L, dtype=torch.int64)
         for j in range(ws):
-            m = torch.rand(L, generator=g) < (0.3 + 0.2 * j)
+            m = torch.rand(L, generator=g) < (0.2 + 0.1 * (j % 7))
             if k == 2 and j == 1:
                 m[:] = False  # a camera sends nothing to rank 1
             mask |= m.to(torch.int64) << j
@@ -125,7 +127,7 @@ def _worker(rank, ws, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("ws", [2, 3])
+@pytest.mark.parametrize("ws", [2, 3, 4, 8])
 def test_exchange_layout_round_trip_gloo(ws):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
