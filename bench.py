@@ -522,6 +522,103 @@ def stage_bytes(name, metas):
     return tot
 
 
+# Fused L1 + SSIM, algorithmic work per output pixel and channel (the
+# separable 11-tap window; halo rows and recomputed products not counted):
+#   forward: the five moments' horizontal and vertical passes 2 x 5 x 11 x 2
+#   = 220, the three products x^2, y^2, xy, the SSIM value and its three
+#   partial derivatives 31, |x - y| and the two running sums 4 -> 258 FLOP;
+#   reads the image (4 B) and the target (1 B as uint8, 4 as float32) and
+#   writes the three partials (12 B).
+#   backward: the three partials' two passes 2 x 3 x 11 x 2 = 132 and the
+#   pixel gradient 10 -> 142 FLOP; reads image, target and partials and
+#   writes the pixel gradient (4 B).
+LOSS_FWD_FLOP_PER_PX = 258
+LOSS_BWD_FLOP_PER_PX = 142
+
+
+def _ints(v):
+    return [int(x) for x in (v.tolist() if hasattr(v, "tolist") else v)]
+
+
+def stage_work(name, metas):
+    """(FLOP, DRAM bytes) of all launches of one native stage, from the stage
+    timer's per-launch metadata; None where the stage has no model in that
+    form.  FLOP: the blend stages' per-pair model (forward 10 per evaluated
+    and 13 per contributing pair, backward 70 per replayed pair, pairs from
+    the kernels' own counters) and the loss's per-pixel counts above.  Bytes:
+    stage_bytes for the preprocess stages (only where the launch reports its
+    list length L); the binning's 4 P (tile counts read) + 4 V (visible list
+    written) + 20 R (each instance's 8-byte key written and read back, its
+    4-byte index written), with V and R the view's own totals (not the
+    buffer capacities a launch may have been issued with); the tile
+    count pass's 16 P (screen mean 8 and radius 4 read, count 4 written);
+    the loss's image, target and partial bytes above.  The blend stages'
+    DRAM bytes are left out: their per-Gaussian reads are L2 hits shared by
+    a tile's strips (ncu: 20-70 MB per city launch against about 8 TFLOP)."""
+    flop = byts = None
+    if name in ("blend_fwd", "blend_bwd") and all("pairs" in m for m in metas):
+        flop = 0.0
+        for m in metas:
+            pr = _ints(m["pairs"])
+            flop += (10.0 * pr[0] + 13.0 * pr[1]) if name == "blend_fwd" else 70.0 * pr[0]
+    elif name in ("loss_fwd", "loss_bwd") and all("pixels" in m for m in metas):
+        px = sum(int(m["pixels"]) for m in metas)
+        gtb = sum(int(m["pixels"]) * int(m.get("gt_bytes", 4)) for m in metas)
+        if name == "loss_fwd":
+            flop, byts = LOSS_FWD_FLOP_PER_PX * px, 16.0 * px + gtb
+        else:
+            flop, byts = LOSS_BWD_FLOP_PER_PX * px, 20.0 * px + gtb
+    elif name == "binning":
+        # "totals" where the launch was sized by capacities; else R / n_vis are exact
+        if all("totals" in m or ("R" in m and "n_vis" in m) for m in metas):
+            byts = 0.0
+            for m in metas:
+                R, V = _ints(m["totals"])[:2] if "totals" in m else (int(m["R"]), int(m["n_vis"]))
+                byts += 4.0 * m.get("P", 0) + 4.0 * V + 20.0 * R
+    elif name == "bin_count":
+        byts = sum(16.0 * m.get("P", 0) for m in metas)
+    elif name in ("preprocess_fwd", "preprocess_bwd"):
+        if all("n_list" in m and (name == "preprocess_bwd" or m.get("fused_count")) for m in metas):
+            byts = stage_bytes(name, metas)
+    return flop, byts
+
+
+def stage_rooflines(stages, peaks, peak_kind, fp32_peak):
+    """Every native stage against its roofline: the lower bound on its time is
+    max(FLOP / FP32 peak, bytes / copy bandwidth) over its modelled work, and
+    ``frac`` = that bound / the event-timed duration (1.0 = at the roofline).
+    ``bound`` names the larger term; ``achieved`` is that resource's rate."""
+    hbm = peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"])
+    out = {}
+    for name, (calls, ms, metas) in stages.items():
+        flop, byts = stage_work(name, metas)
+        if (flop is None and byts is None) or ms <= 0 or calls <= 0:
+            out[name] = {"model": None, "ms_per_launch": round(ms / max(calls, 1), 4)}
+            continue
+        t = ms / 1e3
+        t_f = flop / (fp32_peak * 1e12) if flop is not None and fp32_peak else 0.0
+        t_b = byts / (hbm * 1e9) if byts is not None else 0.0
+        if flop is not None and not fp32_peak and t_b == 0.0:
+            out[name] = {"model": "fp32", "frac": None, "ms_per_launch": round(ms / calls, 4),
+                         "flop_per_launch": round(flop / calls)}
+            continue
+        e = {"bound": "fp32" if t_f >= t_b else "hbm", "ms_per_launch": round(ms / calls, 4),
+             "frac": round(max(t_f, t_b) / t, 4)}
+        if e["bound"] == "fp32":
+            e.update(achieved=round(flop / t / 1e12, 3), peak=round(fp32_peak, 2), unit="TFLOP/s")
+        else:
+            e.update(achieved=round(byts / t / 1e9, 1), peak=hbm, unit="GB/s")
+        if flop is not None:
+            e["flop_per_launch"] = round(flop / calls)
+        if byts is not None:
+            e["bytes_per_launch"] = round(byts / calls)
+        out[name] = e
+    out["peaks"] = {"fp32_tflops": round(fp32_peak, 2) if fp32_peak else None,
+                    "fp32_source": "measured in this run (FP32 FMA probe, blitz_fp32_probe)",
+                    "hbm_gbs": hbm, "hbm_source": peak_kind}
+    return out
+
+
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of each
 # stage's kernels, summed over the stage's kernels, measured by ncu on this
 # bench's city workload (one-pass capture of the full workload).
@@ -928,6 +1025,10 @@ def main():
         if t is not None:
             rf["traffic"] = t
             rf["traffic_source"] = NCU_TRAFFIC_SOURCE
+    try:
+        stage_roof = stage_rooflines(r["stages"], peaks, pk, fp32)
+    except Exception as ex:  # the per-stage table must not sink the bench line
+        stage_roof = {"error": repr(ex)}
     cb = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         try:
@@ -939,6 +1040,7 @@ def main():
             "warmup": getattr(args, "warmup_done", args.warmup), "ms_per_step": round(r["ms"] / args.steps, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
             "clocks": r["clocks"], "roofline": roof, "roofline_hbm": roof_hbm, "stages_ms": stage_table,
+            "stages_roofline": stage_roof,
             "cpu_baseline": cb,
             "e2e": {"value": round(e2e, 4), "unit": UNIT, "h2d_bytes_per_step": r["h2d"],
                     "d2h_bytes_per_step": r["d2h"],

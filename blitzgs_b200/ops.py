@@ -590,7 +590,9 @@ def render_forward(means2D, depths, radii, conic_opacity, rgb, bg, compute_local
         tok = TIMER.begin("binning")
         _lib.call("blitz_render_bin", P, n_vis, R, H, W, ptr(means2D), ptr(depths), ptr(radii), ptr(cl), ptr(counts),
                   ptr(scratch), scratch.numel(), ptr(point_list), ptr(ranges), st)
-        TIMER.end(tok, P=P, R=R, n_vis=n_vis)
+        # R / n_vis are the buffer capacities; "totals" (device {R, n_vis}) the view's own
+        TIMER.end(tok, P=P, R=R, n_vis=n_vis,
+                  lazy=(lambda: {"totals": totals.reshape(-1)[:2].clone()}) if totals is not None else None)
         tok = TIMER.begin("blend_fwd")
         _lib.call("blitz_render_blend", P, H, W, ptr(means2D), ptr(conic_opacity), ptr(rgb), ptr(bg), ptr(cl),
                   ptr(point_list), ptr(ranges), ptr(final_T), ptr(n_contrib), ptr(color), ptr(n_render),
@@ -789,7 +791,7 @@ def loss_forward(img, gt):
     tok = TIMER.begin("loss_fwd")
     _lib.call("blitz_loss_forward", C, Hb, W, ptr(img), ptr(gt_u8), ptr(gt_f), win, ptr(partials),
               ptr(sums), _lib.stream_ptr())
-    TIMER.end(tok, pixels=C * Hb * W)
+    TIMER.end(tok, pixels=C * Hb * W, gt_bytes=1 if gt_u8 is not None else 4)
     return sums, partials
 
 
@@ -804,7 +806,7 @@ def loss_backward(img, gt, partials, scale):
     tok = TIMER.begin("loss_bwd")
     _lib.call("blitz_loss_backward", C, Hb, W, ptr(img), ptr(gt_u8), ptr(gt_f), win, ptr(partials),
               ptr(_f32c(scale)), ptr(out), _lib.stream_ptr())
-    TIMER.end(tok, pixels=C * Hb * W)
+    TIMER.end(tok, pixels=C * Hb * W, gt_bytes=1 if gt_u8 is not None else 4)
     return out
 
 

@@ -47,3 +47,53 @@ def test_launch_accounting(bench):
     # one single-GPU view: the 14 native kernels of the ncu launch list
     assert bench.LAUNCHES_PER_VIEW == 14
     assert bench.DIST_LAUNCHES_PER_BAND == 14 and bench.DIST_LAUNCHES_PER_CAMERA == 4
+
+
+def test_stage_rooflines_bound_and_fraction(bench):
+    """Each stage's lower time bound is max(FLOP / FP32 peak, bytes / copy
+    bandwidth) of its modelled work; frac = bound / event-timed time."""
+    px = 3 * 864 * 1152
+    stages = {
+        # 2 launches of 1e8 replayed pairs in 1.0 ms: 1.4e10 FLOP / 1e-3 s = 14 TFLOP/s of 70
+        "blend_bwd": (2, 1.0, [{"pairs": (100_000_000,)}] * 2),
+        # the view's own totals (R, V), not the capacities in R / n_vis
+        "binning": (1, 0.1, [{"P": 1_000_000, "R": 999_999, "n_vis": 999_999, "totals": (500_000, 100_000)}]),
+        "loss_fwd": (1, 0.05, [{"pixels": px, "gt_bytes": 1}]),
+        "loss_bwd": (1, 0.05, [{"pixels": px, "gt_bytes": 1}]),
+        "preprocess_bwd": (1, 0.05, [{"P": 8_000_000, "n_list": 250_000}]),
+        # the batched form reports no list length: no model
+        "preprocess_fwd": (1, 0.2, [{"P": 16_000_000}]),
+    }
+    t = bench.stage_rooflines(stages, {"hbm_gbs": 6500.0}, "measured", 70.0)
+    b = t["blend_bwd"]
+    assert b["bound"] == "fp32" and b["unit"] == "TFLOP/s"
+    assert b["achieved"] == pytest.approx(14.0) and b["frac"] == pytest.approx(0.2)
+    assert b["flop_per_launch"] == 7_000_000_000
+    g = t["binning"]
+    byts = 4 * 1_000_000 + 4 * 100_000 + 20 * 500_000
+    assert g["bound"] == "hbm" and g["bytes_per_launch"] == byts
+    assert g["frac"] == pytest.approx(byts / 6500e9 / 1e-4, abs=1e-4)  # rounded to 4 places
+    lf = t["loss_fwd"]
+    t_f, t_b = 258 * px / 70e12, 17 * px / 6500e9
+    assert lf["bound"] == ("fp32" if t_f >= t_b else "hbm")
+    assert lf["frac"] == pytest.approx(max(t_f, t_b) / 5e-5, abs=1e-4)
+    assert lf["flop_per_launch"] == 258 * px and lf["bytes_per_launch"] == 17 * px
+    assert t["loss_bwd"]["bytes_per_launch"] == 21 * px
+    assert t["preprocess_bwd"]["bytes_per_launch"] == 508 * 250_000
+    assert t["preprocess_fwd"]["model"] is None
+    assert t["peaks"]["hbm_gbs"] == 6500.0 and t["peaks"]["fp32_tflops"] == 70.0
+    # without an FP32 peak the FLOP-only stages report no fraction
+    t2 = bench.stage_rooflines({"blend_fwd": (1, 0.2, [{"pairs": (10, 5)}])}, {"hbm_gbs": 6500.0}, "measured", None)
+    assert t2["blend_fwd"]["frac"] is None and t2["blend_fwd"]["flop_per_launch"] == 165
+
+
+def test_stage_rooflines_without_model_metadata(bench):
+    """A launch without the metadata a model needs (the full rasterizer's
+    statistics blend has no pair counters) gets no fraction rather than an
+    error; a binning launch sized by its exact totals needs no "totals"."""
+    stages = {"blend_fwd": (2, 0.4, [{"pairs": (10, 5)}, {"P": 7}]),
+              "binning": (1, 0.1, [{"P": 100, "R": 50, "n_vis": 10}]),
+              "adam": (1, 0.1, [{}])}
+    t = bench.stage_rooflines(stages, {"hbm_gbs": 6500.0}, "measured", 70.0)
+    assert t["blend_fwd"]["model"] is None and t["adam"]["model"] is None
+    assert t["binning"]["bytes_per_launch"] == 4 * 100 + 4 * 10 + 20 * 50
