@@ -787,14 +787,25 @@ def run_reference(args):
             loss = loss + 10.0 * torch.sort(scales[vis], dim=-1)[0][..., 0].mean()
         return loss
 
-    def one_step(it, e2e):
+    bsz = args.bsz
+
+    def batch_ids(it):
+        """Cameras of step ``it``: the repo arm's sequence on one GPU."""
+        return [(it * bsz + k) % len(cams) for k in range(bsz)]
+
+    def one_step(it, e2e, gts_in=None):
+        """``e2e``: False (device-resident ground truth), or a 1-element
+        pinned host tensor: upload the ground truth from pinned memory (or
+        take ``gts_in``, this step's views already uploaded by GTPrefetch)
+        and copy the loss into it."""
         upload = e2e is not False
         for p in model:
             p.grad = None
         total = None
-        for k in range(args.bsz):
-            ci = (it * args.bsz + k) % len(cams)
-            if upload:
+        for k, ci in enumerate(batch_ids(it)):
+            if gts_in is not None:
+                gt = gts_in[k]
+            elif upload:
                 gt = torch.empty((3, H, W), dtype=torch.uint8, device=dev)
                 gt.copy_(gts_pin[ci], non_blocking=True)
             else:
@@ -827,19 +838,15 @@ def run_reference(args):
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     loss_host = torch.empty((args.steps,), dtype=torch.float32, pin_memory=True)
-    pf = GTPrefetch(dev, [[gts_pin[c] for c in batch_ids(args.warmup + it)] for it in range(args.steps)], H, W, bsz) \
-        if ws == 1 else None
+    # the same one-step-ahead ground-truth upload as the repo arm on one GPU
+    pf = GTPrefetch(dev, [[gts_pin[c] for c in batch_ids(args.warmup + it)] for it in range(args.steps)], H, W, bsz)
     e0.record()
-    if pf is not None:
-        pf.issue(0)
+    pf.issue(0)
     for it in range(args.steps):
-        if pf is not None:
-            if it + 1 < args.steps:
-                pf.issue(it + 1)  # the next step's upload overlaps this step
-            one_step(args.warmup + it, loss_host[it:it + 1], gts_in=pf.take(it))
-            pf.release(it)
-        else:
-            one_step(args.warmup + it, loss_host[it:it + 1])
+        if it + 1 < args.steps:
+            pf.issue(it + 1)  # the next step's upload overlaps this step
+        one_step(args.warmup + it, loss_host[it:it + 1], gts_in=pf.take(it))
+        pf.release(it)
     e1.record()
     torch.cuda.synchronize()
     clk = clocks.stop()

@@ -97,3 +97,32 @@ def test_stage_rooflines_without_model_metadata(bench):
     t = bench.stage_rooflines(stages, {"hbm_gbs": 6500.0}, "measured", 70.0)
     assert t["blend_fwd"]["model"] is None and t["adam"]["model"] is None
     assert t["binning"]["bytes_per_launch"] == 4 * 100 + 4 * 10 + 20 * 50
+
+
+def test_bench_functions_name_only_defined_globals():
+    """Every global name a function of bench.py reads is defined at module
+    level or is a builtin: the reference arm and the GPU-only paths cannot
+    run here, so an undefined name there would only surface on a GPU box."""
+    import ast
+    import builtins
+    import symtable
+    path = os.path.join(ROOT, "bench.py")
+    src = open(path).read()
+    defined = set(dir(builtins)) | {"__file__", "__name__"}
+    for node in ast.walk(ast.parse(src)):
+        if isinstance(node, (ast.Import, ast.ImportFrom)):
+            defined |= {(a.asname or a.name).split(".")[0] for a in node.names}
+    top = symtable.symtable(src, path, "exec")
+    defined |= {s.get_name() for s in top.get_symbols() if s.is_assigned() or s.is_imported()}
+    missing = []
+
+    def walk(t):
+        for s in t.get_symbols():
+            if s.is_global() and s.is_referenced() and s.get_name() not in defined:
+                missing.append((t.get_name(), t.get_lineno(), s.get_name()))
+        for c in t.get_children():
+            walk(c)
+
+    for c in top.get_children():
+        walk(c)
+    assert not missing, missing
