@@ -973,7 +973,15 @@ def main():
     if args.ops_case:
         return run_ops_case(args)
 
-    ws, rank, local = dist_setup(args.gpus)
+    if args.impl == "reference":
+        # The reference arm runs in rank 0 alone, on one GPU: no process group
+        # is formed, so the other ranks leave at once with nothing to wait on.
+        ws, rank, local = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0
+        if rank != 0:
+            return 0
+        torch.cuda.set_device(local)
+    else:
+        ws, rank, local = dist_setup(args.gpus)
     cfg = {"workload": f"{args.config} (BASELINE config 3: 8M clustered Gaussians, 1152x864 aerial views)"
            if args.config == "city" else args.config,
            "gaussians": None, "image": None, "views_per_gpu_per_step": args.bsz,
@@ -984,8 +992,6 @@ def main():
            "operator API (GaussianRasterizer.preprocess_gaussians / render_gaussians per camera, torch activations)"}
 
     if args.impl == "reference":
-        if rank != 0:
-            return 0
         if not reference_available():
             cb = cpu_baseline_sample()
             line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": 0,
