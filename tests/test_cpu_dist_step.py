@@ -1,7 +1,7 @@
 """The multi-GPU step's orchestration on gloo ranks (CPU): blitzgs_b200.dist_step
 forward and backward, the workload division, the exchange layout and both
-all-to-alls, the scatter-back and the in-place gradient buffers, at world
-sizes 1-8.
+all-to-alls, the scatter-back, the in-place gradient buffers and the
+densification statistics, at world sizes 1-8.
 
 The native kernels are replaced by CPU stand-ins with a simple model of
 their contracts (one 12-float record per listed Gaussian and destination,
@@ -225,6 +225,8 @@ def _worker(rank, ws, n_cams, reg_w, port, q):
         g = torch.Generator().manual_seed(11)
         gt_full = [torch.randint(0, 4, (3, H, W), generator=g, dtype=torch.uint8) for _ in range(n_cams)]
         history = D.DivisionStrategyHistoryFinal(cams, ws, rank)
+        from blitzgs_b200.densify import DensificationStats
+        stats = DensificationStats(hi - lo, "cpu")
         results = []
         for step in range(3):
             strategies, _ = D.start_strategy_final(cams, history)
@@ -236,12 +238,13 @@ def _worker(rank, ws, n_cams, reg_w, port, q):
                 for p in model:
                     p.grad = None  # fresh buffers in step 0, reused (earlier rows zeroed) in step 1
             # step 2 accumulates into the gradients of step 1
-            loss = DS.batch_loss(model, rasters, gts, strategies, reg_w=reg_w)
+            loss = DS.batch_loss(model, rasters, gts, strategies, reg_w=reg_w, densify=stats)
             loss.backward()
             # numpy copies: they travel through the queue by value (a shared
             # tensor would vanish with this process)
             results.append((float(loss.detach()), [p.grad.numpy().copy() for p in model]))
-        q.put((rank, "ok", lo, hi, results))
+        dens = [t.numpy().copy() for t in (stats.max_radii2D, stats.xyz_gradient_accum, stats.denom)]
+        q.put((rank, "ok", lo, hi, (results, dens)))
     except BaseException as ex:  # report to the parent
         import traceback
         q.put((rank, repr(ex) + traceback.format_exc(), 0, 0, None))
@@ -261,16 +264,21 @@ def _run(ws, n_cams, reg_w):
         p.join(timeout=60)
     for r in res:
         assert r[1] == "ok", r[1]
-    # per step: total loss over ranks, each gradient tensor assembled over the shards
+    # per step: total loss over ranks, each gradient tensor assembled over the
+    # shards; and the densification statistics assembled likewise
     steps = []
     for s in range(3):
-        loss = sum(r[4][s][0] for r in res)
+        loss = sum(r[4][0][s][0] for r in res)
         grads = [torch.zeros_like(t) for t in _scene()]
         for r in res:
-            for gt, g in zip(grads, r[4][s][1]):
+            for gt, g in zip(grads, r[4][0][s][1]):
                 gt[r[2]:r[3]] = torch.from_numpy(g)
         steps.append((loss, grads))
-    return steps
+    dens = [torch.zeros(P_TOTAL), torch.zeros(P_TOTAL, 1), torch.zeros(P_TOTAL, 1)]
+    for r in res:
+        for d, v in zip(dens, r[4][1]):
+            d[r[2]:r[3]] = torch.from_numpy(v)
+    return steps, dens
 
 
 _SINGLE = {}
@@ -287,8 +295,8 @@ def test_multi_rank_step_equals_one_rank(ws, n_cams, reg_w):
     key = (n_cams, reg_w)
     if key not in _SINGLE:
         _SINGLE[key] = _run(1, n_cams, reg_w)
-    want = _SINGLE[key]
-    got = _run(ws, n_cams, reg_w)
+    want, want_dens = _SINGLE[key]
+    got, got_dens = _run(ws, n_cams, reg_w)
     for s in range(3):
         assert got[s][0] == pytest.approx(want[s][0], rel=1e-6), (s, got[s][0], want[s][0])
         for name, a, b in zip(("xyz", "scaling", "rotation", "opacity", "dc", "rest"), got[s][1], want[s][1]):
@@ -296,3 +304,10 @@ def test_multi_rank_step_equals_one_rank(ws, n_cams, reg_w):
     # the step saw work: gradients reach the colours and positions, and step 2 accumulated
     assert float(want[0][1][4].abs().sum()) > 0 and float(want[0][1][0].abs().sum()) > 0
     assert torch.allclose(want[2][1][4], 2 * want[1][1][4])
+    # densification statistics over the three steps: max_radii2D, the summed
+    # norm of each Gaussian's viewspace gradient (on N ranks the owner's sum
+    # over the receivers) and the visibility count
+    for name, a, b in zip(("max_radii2D", "xyz_gradient_accum", "denom"), got_dens, want_dens):
+        assert torch.allclose(a, b, rtol=1e-6, atol=1e-6), (name, (a - b).abs().max())
+    assert 0 < float(want_dens[2].max()) <= 3 * n_cams  # at most once per camera and step
+    assert float(want_dens[1].sum()) > 0
