@@ -126,3 +126,22 @@ def test_bench_functions_name_only_defined_globals():
     for c in top.get_children():
         walk(c)
     assert not missing, missing
+
+
+def test_clock_sampler_summary(bench):
+    """Clock samples count only inside the marked timed regions; a region
+    shorter than the sampling period takes its nearest sample; throttle
+    reason bits are named."""
+    cs = bench.ClockSampler(0)
+    ms = 1_000_000  # ns per ms
+    # (t_ns, sm_mhz, max_mhz, reason bits): 1965 inside region 1, a capped sample outside
+    cs.samples = [(0 * ms, 900.0, 1965.0, 0x8), (100 * ms, 1965.0, 1965.0, 0), (150 * ms, 1965.0, 1965.0, 0),
+                  (200 * ms, 1950.0, 1965.0, 0x4), (400 * ms, 1800.0, 1965.0, 0)]
+    cs.windows = [[90 * ms, 210 * ms], [395 * ms, 396 * ms]]
+    out = cs.stop()
+    assert out["samples"] == 4  # three inside region 1, region 2 takes its nearest (400 ms)
+    assert out["sm_mhz"] == 1965.0 and out["sm_max_mhz"] == 1965.0
+    assert out["reasons"] == ["sw_power_cap"]  # the hw_slowdown sample at 0 ms lies outside both regions
+    empty = bench.ClockSampler(0)
+    empty.windows = [[0, 1]]
+    assert empty.stop() is None
