@@ -187,3 +187,63 @@ def test_compat_import_names():
         sys.path.remove(compat)
         for n in ("diff_gaussian_rasterization_f", "diff_gaussian_rasterization_r"):
             sys.modules.pop(n, None)
+
+
+# The reference's public wrapper API that its renderer glue, model and trainer
+# call (diff_gaussian_rasterization_f/_r __init__.py): method and function
+# parameter names in order.  A drop-in must accept the same names.
+_REF_API = {
+    ("f", "GaussianRasterizer", "__init__"): ["self", "raster_settings"],
+    ("f", "GaussianRasterizer", "markVisible"): ["self", "positions"],
+    ("f", "GaussianRasterizer", "preprocess_gaussians"): ["self", "means3D", "scales", "rotations", "shs",
+                                                          "opacities", "cuda_args"],
+    ("f", "GaussianRasterizer", "render_gaussians"): ["self", "means2D", "means2D_abs", "conic_opacity", "rgb",
+                                                      "all_map", "depths", "radii", "compute_locally",
+                                                      "extended_compute_locally", "cuda_args"],
+    ("f", "GaussianRasterizer", "forward"): ["self", "means3D", "means2D", "opacities", "culling", "dc", "shs",
+                                             "colors_precomp", "scales", "rotations", "cov3D_precomp",
+                                             "flag_max_count"],
+    ("f", "GaussianRasterizer", "render_simp"): ["self", "means3D", "means2D", "opacities", "culling", "dc", "shs",
+                                                 "colors_precomp", "scales", "rotations", "cov3D_precomp"],
+    ("f", "GaussianRasterizer", "render_depth"): ["self", "means3D", "means2D", "opacities", "culling", "dc", "shs",
+                                                  "colors_precomp", "scales", "rotations", "cov3D_precomp"],
+    ("f", "SparseGaussianAdam", "__init__"): ["self", "params", "lr", "eps"],
+    ("f", None, "preprocess_gaussians"): ["means3D", "scales", "rotations", "sh", "opacities", "raster_settings",
+                                          "cuda_args"],
+    ("f", None, "render_gaussians"): ["means2D", "means2D_abs", "conic_opacity", "rgb", "all_map", "depths", "radii",
+                                      "compute_locally", "extended_compute_locally", "raster_settings", "cuda_args"],
+    ("f", None, "rasterize_gaussians"): ["means3D", "means2D", "dc", "sh", "colors_precomp", "opacities", "scales",
+                                         "rotations", "cov3Ds_precomp", "flag_max_count", "culling",
+                                         "raster_settings"],
+    ("r", "GaussianRasterizer", "preprocess_gaussians"): ["self", "means3D", "scales", "rotations", "shs",
+                                                          "opacities", "cuda_args"],
+    ("r", "GaussianRasterizer", "render_gaussians"): ["self", "means2D", "means2D_abs", "conic_opacity", "rgb",
+                                                      "all_map", "depths", "radii", "compute_locally",
+                                                      "extended_compute_locally", "cuda_args"],
+}
+
+
+def test_compat_signatures_match_the_reference_api():
+    import importlib
+    import inspect
+    import sys
+    compat = os.path.join(ROOT, "blitzgs_b200", "compat")
+    sys.path.insert(0, compat)
+    try:
+        mods = {k: importlib.import_module(f"diff_gaussian_rasterization_{k}") for k in ("f", "r")}
+        for (m, cls, name), params in _REF_API.items():
+            obj = getattr(mods[m], cls) if cls else mods[m]
+            got = list(inspect.signature(getattr(obj, name)).parameters)
+            assert got[:len(params)] == params, (m, cls, name, got)
+            # anything added after the reference's parameters must be optional
+            extra = list(inspect.signature(getattr(obj, name)).parameters.values())[len(params):]
+            assert all(p.default is not inspect.Parameter.empty for p in extra), (m, cls, name, extra)
+        # SparseGaussianAdam.step(visibility, N) as the trainer calls it (train_internal.py:517-545)
+        step = list(inspect.signature(mods["f"].SparseGaussianAdam.step).parameters)
+        assert step[:3] == ["self", "visibility", "N"]
+        for op in ("get_local2j_ids_bool", "get_local2j_ids_bool_adjust_mode6", "adamUpdate"):
+            assert callable(getattr(mods["f"]._C, op))
+    finally:
+        sys.path.remove(compat)
+        for n in ("diff_gaussian_rasterization_f", "diff_gaussian_rasterization_r"):
+            sys.modules.pop(n, None)
